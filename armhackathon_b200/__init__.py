@@ -1,0 +1,45 @@
+"""armhackathon_b200 -- a B200-native selective-scan engine with the op
+surface of the reference ``arm_scan`` package (AdityaP9116/ARMHackathon).
+
+    import armhackathon_b200 as arm_scan
+    arm_scan.patch()                       # HF transformers Mamba uses the GPU scan
+    arm_scan.selective_scan(u, delta, A, B, C, D=..., z=...)
+    arm_scan.bidirectional_scan(...) / ss2d_scan(...)
+    arm_scan.mamba3_scan(...) / mamba3_scan_pair(...) / mamba3_mimo_scan(...)
+    arm_scan.ss2d_scan_mamba3(...) / noncausal_scan(...) / ss2d_noncausal_mamba3(...)
+    arm_scan.selective_scan_numpy(...)     # numpy in, numpy out (no torch)
+
+Every scan runs as sm_100a CUDA kernels in libb200scan.so, reached through
+its C ABI (include/b200scan.h).  There is no CPU implementation.
+"""
+
+from ._ffi import lib_path
+from .numpy_api import selective_scan_numpy
+
+__all__ = [
+    "selective_scan_numpy", "lib_path", "selective_scan", "selective_scan_bidirectional",
+    "bidirectional_scan", "ss2d_scan", "use_arm_scan", "mamba3_scan", "mamba3_scan_pair",
+    "mamba3_mimo_scan", "ss2d_scan_mamba3", "noncausal_scan", "noncausal_scan_dense",
+    "ss2d_noncausal_mamba3", "angles_to_cos_sin", "patch", "unpatch", "stats", "kernel_calls",
+]
+
+_LAZY = {
+    "selective_scan": ".op", "selective_scan_bidirectional": ".op", "kernel_calls": ".op",
+    "bidirectional_scan": ".bidirectional",
+    "ss2d_scan": ".ss2d", "use_arm_scan": ".ss2d",
+    "mamba3_scan": ".mamba3", "mamba3_scan_pair": ".mamba3", "mamba3_mimo_scan": ".mamba3",
+    "angles_to_cos_sin": ".mamba3",
+    "ss2d_scan_mamba3": ".ss2d_mamba3",
+    "noncausal_scan": ".mamba3_noncausal", "noncausal_scan_dense": ".mamba3_noncausal",
+    "ss2d_noncausal_mamba3": ".mamba3_noncausal",
+    "patch": ".patch", "unpatch": ".patch", "stats": ".patch",
+}
+
+
+def __getattr__(name):
+    # torch-dependent modules load on first use, so numpy-only callers never
+    # import torch
+    import importlib
+    if name in _LAZY:
+        return getattr(importlib.import_module(_LAZY[name], __name__), name)
+    raise AttributeError(f"module 'armhackathon_b200' has no attribute '{name}'")

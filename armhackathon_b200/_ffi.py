@@ -1,0 +1,183 @@
+"""ctypes binding of libb200scan.so (the C ABI in include/b200scan.h).
+
+Mirrors the reference loader python/arm_scan/_ffi.py: the library is looked up
+via the ``ARM_SCAN_LIB`` environment variable first, then next to this
+package; its ABI version is checked before any entry point is bound.  Pointers
+are passed as integer addresses (0 = null).
+
+Two call families:
+* ``*_raw``       -- the synchronous v7-shaped entry points.  Every buffer must
+  be host memory (the library stages it through the GPU) or every buffer
+  device memory; the call returns once the results are in place.
+* ``*_async_raw`` -- device pointers, enqueued on a CUDA stream handle.
+
+There is no CPU implementation behind any of these: if the library or a GPU
+is missing, the call raises.
+"""
+
+import ctypes
+import os
+import sys
+from pathlib import Path
+
+ABI_VERSION = 8
+
+_LIB_NAMES = ["libb200scan.so"]
+
+ERROR_NAMES = {
+    0: "ok",
+    1: "null pointer",
+    2: "invalid dims/shapes",
+    3: "backend unavailable",
+    4: "bad backend/threading enum",
+    5: "panic inside kernel",
+    6: "CUDA error",
+    7: "timeout",
+}
+
+BACKENDS = {"auto": 0, "scalar": 1, "sequential": 1, "neon": 2}
+THREADING = {"auto": 0, "sequential": 1, "seq": 1, "rayon": 2}
+
+
+class ArmScanDims(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_size_t) for n in ("batch", "dim", "len", "state", "groups")]
+
+
+class ArmMamba3Dims(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_size_t) for n in ("batch", "heads", "dv", "dqk", "len", "rank")]
+
+
+def _candidate_paths():
+    env = os.environ.get("ARM_SCAN_LIB")
+    if env:
+        yield Path(env)
+    here = Path(__file__).resolve().parent
+    for name in _LIB_NAMES:
+        yield here / name
+
+
+_lib = None
+_lib_path = None
+
+_VP = ctypes.c_void_p
+_I = ctypes.c_int
+
+
+def _bind(lib):
+    lib.arm_scan_abi_version.restype = ctypes.c_uint32
+    lib.arm_scan_last_error.restype = ctypes.c_char_p
+    m1 = [ctypes.POINTER(ArmScanDims), *([_VP] * 8), _I, _I, _I, _I, _VP, _VP, _VP]
+    lib.arm_scan_selective_scan_f32.argtypes = m1
+    lib.arm_scan_selective_scan_f32_async.argtypes = m1 + [_VP]
+    bi = [ctypes.POINTER(ArmScanDims), *([_VP] * 8), _I, _I, _I, _VP, _VP, _VP, _VP]
+    lib.arm_scan_selective_scan_bidirectional_f32.argtypes = bi
+    lib.arm_scan_selective_scan_bidirectional_f32_async.argtypes = bi + [_VP]
+    m3 = [ctypes.POINTER(ArmMamba3Dims), *([_VP] * 15), _I, _I, _I, _VP, _VP, _VP]
+    lib.arm_scan_mamba3_scan_f32.argtypes = m3
+    lib.arm_scan_mamba3_scan_f32_async.argtypes = m3 + [_VP]
+    for f in ("arm_scan_selective_scan_f32", "arm_scan_selective_scan_f32_async",
+              "arm_scan_selective_scan_bidirectional_f32",
+              "arm_scan_selective_scan_bidirectional_f32_async",
+              "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async"):
+        getattr(lib, f).restype = ctypes.c_int
+
+
+def load():
+    """Load (once) and return the ctypes library handle."""
+    global _lib, _lib_path
+    if _lib is not None:
+        return _lib
+    tried = []
+    for path in _candidate_paths():
+        tried.append(str(path))
+        if path.is_file():
+            lib = ctypes.CDLL(str(path))
+            version = lib.arm_scan_abi_version()
+            if version != ABI_VERSION:
+                raise RuntimeError(
+                    f"{path} has ABI version {version}, this package needs {ABI_VERSION}; "
+                    f"rebuild with `python -m armhackathon_b200.build`")
+            _bind(lib)
+            _lib, _lib_path = lib, path
+            return lib
+    raise OSError("libb200scan.so not found; build it with `python -m armhackathon_b200.build` "
+                  "(searched: " + ", ".join(tried) + ")")
+
+
+def lib_path():
+    load()
+    return _lib_path
+
+
+def _check(code, what):
+    if code != 0:
+        msg = load().arm_scan_last_error()
+        msg = msg.decode() if msg else ""
+        raise RuntimeError(f"{what} failed with code {code} ({ERROR_NAMES.get(code, 'unknown')})"
+                           + (f": {msg}" if msg else ""))
+
+
+def _n(p):
+    return p or None
+
+
+def scan_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_d_skip, ptr_z,
+             ptr_delta_bias, delta_softplus, backend, threading, ptr_out,
+             ptr_last, ptr_h0=0, *, reverse=False, stream=None):
+    """Mamba-1 scan.  ``stream`` None -> synchronous entry point (host or
+    device pointers); an integer stream handle -> the _async entry point."""
+    lib = load()
+    args = (ctypes.byref(dims), ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, _n(ptr_d_skip), _n(ptr_z),
+            _n(ptr_delta_bias), int(bool(delta_softplus)), int(bool(reverse)),
+            BACKENDS[backend], THREADING[threading], ptr_out, _n(ptr_last), _n(ptr_h0))
+    if stream is None:
+        _check(lib.arm_scan_selective_scan_f32(*args), "arm_scan_selective_scan_f32")
+    else:
+        _check(lib.arm_scan_selective_scan_f32_async(*args, _n(stream)),
+               "arm_scan_selective_scan_f32_async")
+
+
+def scan_bidir_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_d_skip, ptr_z,
+                   ptr_delta_bias, delta_softplus, backend, threading, ptr_out_fwd,
+                   ptr_out_bwd, ptr_last_fwd=0, ptr_last_bwd=0, *, stream=None):
+    """Fused bidirectional Mamba-1 scan (forward + reverse of the same inputs)."""
+    lib = load()
+    args = (ctypes.byref(dims), ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, _n(ptr_d_skip), _n(ptr_z),
+            _n(ptr_delta_bias), int(bool(delta_softplus)), BACKENDS[backend],
+            THREADING[threading], ptr_out_fwd, ptr_out_bwd, _n(ptr_last_fwd), _n(ptr_last_bwd))
+    if stream is None:
+        _check(lib.arm_scan_selective_scan_bidirectional_f32(*args),
+               "arm_scan_selective_scan_bidirectional_f32")
+    else:
+        _check(lib.arm_scan_selective_scan_bidirectional_f32_async(*args, _n(stream)),
+               "arm_scan_selective_scan_bidirectional_f32_async")
+
+
+def mamba3_raw(dims, ptrs, reverse, backend, threading, ptr_out, ptr_last_state,
+               ptr_last_bx, *, stream=None):
+    """Mamba-3 scan.  ``ptrs`` are the 15 input addresses in signature order:
+    q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, d_skip, z, psi, zeta, phi
+    (d_skip, z and the three MIMO projections may be 0)."""
+    lib = load()
+    if len(ptrs) != 15:
+        raise ValueError(f"expected 15 input pointers, got {len(ptrs)}")
+    args = (ctypes.byref(dims), *[_n(p) for p in ptrs], int(reverse), int(backend),
+            int(threading), ptr_out, _n(ptr_last_state), _n(ptr_last_bx))
+    if stream is None:
+        _check(lib.arm_scan_mamba3_scan_f32(*args), "arm_scan_mamba3_scan_f32")
+    else:
+        _check(lib.arm_scan_mamba3_scan_f32_async(*args, _n(stream)),
+               "arm_scan_mamba3_scan_f32_async")
+
+
+def exported_symbols():
+    """Names of every entry point include/b200scan.h declares."""
+    return ["arm_scan_abi_version", "arm_scan_last_error",
+            "arm_scan_selective_scan_f32", "arm_scan_selective_scan_f32_async",
+            "arm_scan_selective_scan_bidirectional_f32",
+            "arm_scan_selective_scan_bidirectional_f32_async",
+            "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async"]
+
+
+if __name__ == "__main__":  # pragma: no cover
+    print(lib_path(), load().arm_scan_abi_version(), file=sys.stderr)

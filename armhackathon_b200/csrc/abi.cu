@@ -1,0 +1,521 @@
+// The C ABI (include/b200scan.h): validation, host/device buffer handling and
+// dispatch to the sm_100a kernels.
+//
+// Validation follows the reference's C boundary, kernel/arm-scan-ffi/src/
+// lib.rs: null checks first (code 1), then enum decoding (code 4), then
+// overflow-checked element counts and shape rules (code 2), mirroring
+// arm-scan-core's validate() (lib.rs:181-249) and mamba3/mod.rs:213-335.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/b200scan.h"
+#include "m1_scan.h"
+#include "m3_scan.h"
+
+using namespace b200scan;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+    return fail(ARM_SCAN_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+bool mul_ok(size_t a, size_t b, size_t* out) {
+    if (a != 0 && b > SIZE_MAX / a) return false;
+    *out = a * b;
+    return true;
+}
+
+bool mul3(size_t a, size_t b, size_t c, size_t* out) {
+    size_t t;
+    return mul_ok(a, b, &t) && mul_ok(t, c, out);
+}
+
+bool mul4(size_t a, size_t b, size_t c, size_t d, size_t* out) {
+    size_t t;
+    return mul3(a, b, c, &t) && mul_ok(t, d, out);
+}
+
+int check_enums(int backend, int threading) {
+    if (backend < 0 || backend > 2 || threading < 0 || threading > 2)
+        return fail(ARM_SCAN_ERR_BAD_ENUM, "backend %d / threading %d out of range", backend,
+                    threading);
+    if (backend == 2)
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE, "the NEON backend does not exist on a GPU");
+    return ARM_SCAN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Buffers of one call: where they live and how many bytes each spans.
+struct Buf {
+    const void* ptr;
+    size_t bytes;
+    bool output;
+};
+
+enum class Where { Host, Device, Mixed };
+
+Where classify(const std::vector<Buf>& bufs, int* device) {
+    int n_host = 0, n_dev = 0;
+    *device = -1;
+    for (const Buf& b : bufs) {
+        if (!b.ptr) continue;
+        cudaPointerAttributes at;
+        if (cudaPointerGetAttributes(&at, b.ptr) != cudaSuccess) {
+            cudaGetLastError();
+            ++n_host;
+            continue;
+        }
+        if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) {
+            ++n_dev;
+            if (*device < 0) *device = at.device;
+        } else {
+            ++n_host;
+        }
+    }
+    if (n_dev && n_host) return Where::Mixed;
+    return n_dev ? Where::Device : Where::Host;
+}
+
+// Device staging area for host-pointer calls: one per device, grown on
+// demand and kept for the life of the process.
+struct Staging {
+    std::mutex mu;
+    void* base = nullptr;
+    size_t cap = 0;
+    cudaStream_t stream = nullptr;
+};
+Staging g_staging[64];
+
+class DeviceGuard {
+  public:
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&old_);
+        if (dev >= 0 && dev != old_) {
+            cudaSetDevice(dev);
+            switched_ = true;
+        }
+    }
+    ~DeviceGuard() {
+        if (switched_) cudaSetDevice(old_);
+    }
+
+  private:
+    int old_ = 0;
+    bool switched_ = false;
+};
+
+size_t round_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Runs `run(device_ptrs, stream)` either directly on device buffers (then
+// synchronizes) or after staging host buffers through device memory.
+template <class Run>
+int run_sync(std::vector<Buf>& bufs, Run&& run) {
+    int dev = -1;
+    const Where w = classify(bufs, &dev);
+    if (w == Where::Mixed)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS,
+                    "buffers mix host and device memory; pass all host or all device pointers");
+    std::vector<void*> dptr(bufs.size(), nullptr);
+    if (w == Where::Device) {
+        DeviceGuard g(dev);
+        for (size_t i = 0; i < bufs.size(); ++i) dptr[i] = const_cast<void*>(bufs[i].ptr);
+        int rc = run(dptr, static_cast<cudaStream_t>(nullptr));
+        if (rc != ARM_SCAN_OK) return rc;
+        cudaError_t e = cudaStreamSynchronize(nullptr);
+        return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "kernel");
+    }
+    int cur = 0;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur < 0 || cur >= 64) return fail(ARM_SCAN_ERR_CUDA, "device ordinal %d unsupported", cur);
+    Staging& st = g_staging[cur];
+    std::lock_guard<std::mutex> lock(st.mu);
+    size_t total = 0;
+    for (const Buf& b : bufs)
+        if (b.ptr) total += round_up(b.bytes);
+    if (total > st.cap) {
+        if (st.base) cudaFree(st.base);
+        st.base = nullptr;
+        st.cap = 0;
+        e = cudaMalloc(&st.base, total);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
+        st.cap = total;
+    }
+    if (!st.stream) {
+        e = cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+    }
+    char* p = static_cast<char*>(st.base);
+    for (size_t i = 0; i < bufs.size(); ++i) {
+        if (!bufs[i].ptr) continue;
+        dptr[i] = p;
+        p += round_up(bufs[i].bytes);
+        if (!bufs[i].output) {
+            e = cudaMemcpyAsync(dptr[i], bufs[i].ptr, bufs[i].bytes, cudaMemcpyHostToDevice,
+                                st.stream);
+            if (e != cudaSuccess) return cuda_fail(e, "copy to device");
+        }
+    }
+    int rc = run(dptr, st.stream);
+    if (rc != ARM_SCAN_OK) {
+        cudaStreamSynchronize(st.stream);
+        return rc;
+    }
+    for (size_t i = 0; i < bufs.size(); ++i) {
+        if (!bufs[i].ptr || !bufs[i].output) continue;
+        e = cudaMemcpyAsync(const_cast<void*>(bufs[i].ptr), dptr[i], bufs[i].bytes,
+                            cudaMemcpyDeviceToHost, st.stream);
+        if (e != cudaSuccess) return cuda_fail(e, "copy to host");
+    }
+    e = cudaStreamSynchronize(st.stream);
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Mamba-1
+struct M1Counts {
+    size_t bdl, bgnl, dn, bdn;
+};
+
+int m1_validate(const ArmScanDims* d, M1Counts* c) {
+    const size_t v[5] = {d->batch, d->dim, d->len, d->state, d->groups};
+    const char* names[5] = {"batch", "dim", "len", "state", "groups"};
+    for (int i = 0; i < 5; ++i)
+        if (v[i] == 0) return fail(ARM_SCAN_ERR_INVALID_DIMS, "dimension `%s` is zero", names[i]);
+    if (d->dim % d->groups)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "groups (%zu) does not divide dim (%zu)", d->groups,
+                    d->dim);
+    if (d->state > static_cast<size_t>(kMaxState))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "state %zu exceeds the supported maximum %lld",
+                    d->state, static_cast<long long>(kMaxState));
+    if (!mul3(d->batch, d->dim, d->len, &c->bdl) ||
+        !mul4(d->batch, d->groups, d->state, d->len, &c->bgnl) ||
+        !mul_ok(d->dim, d->state, &c->dn) || !mul3(d->batch, d->dim, d->state, &c->bdn))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "element counts overflow");
+    // every byte offset must fit in int64 for the kernels
+    if (c->bdl > (SIZE_MAX >> 3) / 4 || c->bgnl > (SIZE_MAX >> 3) / 4)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "tensors too large");
+    return ARM_SCAN_OK;
+}
+
+M1Params m1_params(const ArmScanDims* d, const std::vector<void*>& p, int softplus, int reverse) {
+    M1Params m{};
+    m.u = static_cast<const float*>(p[0]);
+    m.delta = static_cast<const float*>(p[1]);
+    m.A = static_cast<const float*>(p[2]);
+    m.B = static_cast<const float*>(p[3]);
+    m.C = static_cast<const float*>(p[4]);
+    m.d_skip = static_cast<const float*>(p[5]);
+    m.z = static_cast<const float*>(p[6]);
+    m.delta_bias = static_cast<const float*>(p[7]);
+    m.batch = static_cast<int64_t>(d->batch);
+    m.dim = static_cast<int64_t>(d->dim);
+    m.len = static_cast<int64_t>(d->len);
+    m.state = static_cast<int64_t>(d->state);
+    m.groups = static_cast<int64_t>(d->groups);
+    m.delta_softplus = softplus != 0;
+    m.reverse = reverse != 0;
+    return m;
+}
+
+int m1_run(const M1Params& m, int backend, cudaStream_t s) {
+    cudaError_t e = m1_scan_launch(m, backend, s);
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "selective_scan launch");
+}
+
+std::vector<Buf> m1_bufs(const M1Counts& c, const float* u, const float* delta, const float* a,
+                         const float* b, const float* cc, const float* d_skip, const float* z,
+                         const float* delta_bias, size_t dim) {
+    return {{u, c.bdl * 4, false},        {delta, c.bdl * 4, false}, {a, c.dn * 4, false},
+            {b, c.bgnl * 4, false},       {cc, c.bgnl * 4, false},   {d_skip, dim * 4, false},
+            {z, c.bdl * 4, false},        {delta_bias, dim * 4, false}};
+}
+
+// ---------------------------------------------------------------------------
+// Mamba-3
+struct M3Counts {
+    size_t blqk, bhl, hqk, hrv, blhv, blhr, bhvq, bhq;
+};
+
+int m3_validate(const ArmMamba3Dims* d, bool mimo, const void* last_state, const void* last_bx,
+                M3Counts* c) {
+    const size_t v[6] = {d->batch, d->heads, d->dv, d->dqk, d->len, d->rank};
+    const char* names[6] = {"batch", "heads", "dv", "dqk", "len", "rank"};
+    for (int i = 0; i < 6; ++i)
+        if (v[i] == 0) return fail(ARM_SCAN_ERR_INVALID_DIMS, "dimension `%s` is zero", names[i]);
+    if (d->dqk % 2)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "dqk (%zu) must be even for RoPE lane pairs", d->dqk);
+    if (d->rank > 1 && !mimo)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "rank > 1 requires the MIMO projections");
+    if (mimo && last_bx)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS,
+                    "MIMO defines no last_bx carry (one k per step is SISO-only)");
+    if (!m3_shape_supported(static_cast<int64_t>(d->dv), static_cast<int64_t>(d->dqk),
+                            static_cast<int64_t>(d->rank)))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS,
+                    "head dims dv=%zu dqk=%zu rank=%zu are outside the supported set "
+                    "(dv, dqk <= 256, rank <= 8)",
+                    d->dv, d->dqk, d->rank);
+    bool ok = mul4(d->batch, d->len, d->rank, d->dqk, &c->blqk) &&
+              mul3(d->batch, d->heads, d->len, &c->bhl) &&
+              mul3(d->heads, d->rank, d->dqk, &c->hqk) && mul3(d->heads, d->rank, d->dv, &c->hrv) &&
+              mul4(d->batch, d->len, d->heads, d->dv, &c->blhv) &&
+              mul4(d->batch, d->len, d->heads, d->dqk / 2, &c->blhr) &&
+              mul4(d->batch, d->heads, d->dv, d->dqk, &c->bhvq) &&
+              mul3(d->batch, d->heads, d->dqk, &c->bhq);
+    if (!ok) return fail(ARM_SCAN_ERR_INVALID_DIMS, "element counts overflow");
+    (void)last_state;
+    return ARM_SCAN_OK;
+}
+
+int m3_check_ptrs(const void* const* req, int n_req, const void* last_state, const void* last_bx,
+                  const void* psi, const void* zeta, const void* phi, bool* mimo) {
+    for (int i = 0; i < n_req; ++i)
+        if (!req[i]) return fail(ARM_SCAN_ERR_NULL_POINTER, "required pointer #%d is null", i);
+    const int n_mimo = (psi != nullptr) + (zeta != nullptr) + (phi != nullptr);
+    if (n_mimo != 0 && n_mimo != 3)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "psi/zeta/phi must be all null or all given");
+    *mimo = n_mimo == 3;
+    if (!*mimo && ((last_state == nullptr) != (last_bx == nullptr)))
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "last_state and last_bx must be given together");
+    return ARM_SCAN_OK;
+}
+
+M3Params m3_params(const ArmMamba3Dims* d, const std::vector<void*>& p, int reverse) {
+    M3Params m{};
+    m.q = static_cast<const float*>(p[0]);
+    m.k = static_cast<const float*>(p[1]);
+    m.v = static_cast<const float*>(p[2]);
+    m.adt = static_cast<const float*>(p[3]);
+    m.dt = static_cast<const float*>(p[4]);
+    m.trap = static_cast<const float*>(p[5]);
+    m.q_bias = static_cast<const float*>(p[6]);
+    m.k_bias = static_cast<const float*>(p[7]);
+    m.cos = static_cast<const float*>(p[8]);
+    m.sin = static_cast<const float*>(p[9]);
+    m.d_skip = static_cast<const float*>(p[10]);
+    m.z = static_cast<const float*>(p[11]);
+    m.psi = static_cast<const float*>(p[12]);
+    m.zeta = static_cast<const float*>(p[13]);
+    m.phi = static_cast<const float*>(p[14]);
+    m.out = static_cast<float*>(p[15]);
+    m.last_state = static_cast<float*>(p[16]);
+    m.last_bx = static_cast<float*>(p[17]);
+    m.batch = static_cast<int64_t>(d->batch);
+    m.heads = static_cast<int64_t>(d->heads);
+    m.dv = static_cast<int64_t>(d->dv);
+    m.dqk = static_cast<int64_t>(d->dqk);
+    m.len = static_cast<int64_t>(d->len);
+    m.rank = static_cast<int64_t>(d->rank);
+    m.reverse = reverse != 0;
+    return m;
+}
+
+std::vector<Buf> m3_bufs(const M3Counts& c, const ArmMamba3Dims* d, const float* q, const float* k,
+                         const float* v, const float* adt, const float* dt, const float* trap,
+                         const float* q_bias, const float* k_bias, const float* cos,
+                         const float* sin, const float* d_skip, const float* z, const float* psi,
+                         const float* zeta, const float* phi, float* out, float* last_state,
+                         float* last_bx) {
+    return {{q, c.blqk * 4, false},      {k, c.blqk * 4, false},       {v, c.blhv * 4, false},
+            {adt, c.bhl * 4, false},     {dt, c.bhl * 4, false},       {trap, c.bhl * 4, false},
+            {q_bias, c.hqk * 4, false},  {k_bias, c.hqk * 4, false},   {cos, c.blhr * 4, false},
+            {sin, c.blhr * 4, false},    {d_skip, d->heads * 4, false}, {z, c.blhv * 4, false},
+            {psi, c.hrv * 4, false},     {zeta, c.hrv * 4, false},     {phi, c.hrv * 4, false},
+            {out, c.blhv * 4, true},     {last_state, c.bhvq * 4, true}, {last_bx, c.bhq * 4, true}};
+}
+
+int m3_run(const M3Params& m, int backend, cudaStream_t s) {
+    cudaError_t e = m3_scan_launch(m, backend, s);
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "mamba3_scan launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+uint32_t arm_scan_abi_version(void) { return ARM_SCAN_ABI_VERSION; }
+
+const char* arm_scan_last_error(void) { return g_last_error.c_str(); }
+
+int arm_scan_selective_scan_f32(const ArmScanDims* dims, const float* u, const float* delta,
+                                const float* a, const float* b, const float* c,
+                                const float* d_skip, const float* z, const float* delta_bias,
+                                int delta_softplus, int reverse, int backend, int threading,
+                                float* out, float* last_state, const float* h0) {
+    if (!dims || !u || !delta || !a || !b || !c || !out)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    int rc = check_enums(backend, threading);
+    if (rc) return rc;
+    M1Counts cnt;
+    if ((rc = m1_validate(dims, &cnt))) return rc;
+    std::vector<Buf> bufs = m1_bufs(cnt, u, delta, a, b, c, d_skip, z, delta_bias, dims->dim);
+    bufs.push_back({h0, cnt.bdn * 4, false});
+    bufs.push_back({out, cnt.bdl * 4, true});
+    bufs.push_back({last_state, cnt.bdn * 4, true});
+    return run_sync(bufs, [&](const std::vector<void*>& p, cudaStream_t s) {
+        M1Params m = m1_params(dims, p, delta_softplus, reverse);
+        m.h0 = static_cast<const float*>(p[8]);
+        m.out = static_cast<float*>(p[9]);
+        m.last_state = static_cast<float*>(p[10]);
+        return m1_run(m, backend, s);
+    });
+}
+
+int arm_scan_selective_scan_f32_async(const ArmScanDims* dims, const float* u, const float* delta,
+                                      const float* a, const float* b, const float* c,
+                                      const float* d_skip, const float* z,
+                                      const float* delta_bias, int delta_softplus, int reverse,
+                                      int backend, int threading, float* out, float* last_state,
+                                      const float* h0, void* stream) {
+    if (!dims || !u || !delta || !a || !b || !c || !out)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    int rc = check_enums(backend, threading);
+    if (rc) return rc;
+    M1Counts cnt;
+    if ((rc = m1_validate(dims, &cnt))) return rc;
+    std::vector<void*> p = {const_cast<float*>(u),     const_cast<float*>(delta),
+                            const_cast<float*>(a),     const_cast<float*>(b),
+                            const_cast<float*>(c),     const_cast<float*>(d_skip),
+                            const_cast<float*>(z),     const_cast<float*>(delta_bias)};
+    M1Params m = m1_params(dims, p, delta_softplus, reverse);
+    m.h0 = h0;
+    m.out = out;
+    m.last_state = last_state;
+    return m1_run(m, backend, static_cast<cudaStream_t>(stream));
+}
+
+static int bidir_common(const ArmScanDims* dims, const float* u, const float* delta,
+                        const float* a, const float* b, const float* c, const float* d_skip,
+                        const float* z, const float* delta_bias, int backend, int threading,
+                        float* out_fwd, float* out_bwd, float* last_fwd, float* last_bwd,
+                        M1Counts* cnt) {
+    if (!dims || !u || !delta || !a || !b || !c || !out_fwd || !out_bwd)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    int rc = check_enums(backend, threading);
+    if (rc) return rc;
+    if ((rc = m1_validate(dims, cnt))) return rc;
+    if ((last_fwd == nullptr) != (last_bwd == nullptr))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "last_fwd and last_bwd must be given together");
+    return ARM_SCAN_OK;
+}
+
+static int bidir_run(const M1Params& base, float* out_fwd, float* out_bwd, float* last_fwd,
+                     float* last_bwd, int backend, cudaStream_t s) {
+    M1Params f = base, r = base;
+    f.reverse = 0;
+    f.out = out_fwd;
+    f.last_state = last_fwd;
+    r.reverse = 1;
+    r.out = out_bwd;
+    r.last_state = last_bwd;
+    cudaError_t e = m1_bidir_launch(f, r, backend, s);
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "bidirectional launch");
+}
+
+int arm_scan_selective_scan_bidirectional_f32(const ArmScanDims* dims, const float* u,
+                                              const float* delta, const float* a, const float* b,
+                                              const float* c, const float* d_skip, const float* z,
+                                              const float* delta_bias, int delta_softplus,
+                                              int backend, int threading, float* out_fwd,
+                                              float* out_bwd, float* last_fwd, float* last_bwd) {
+    M1Counts cnt;
+    int rc = bidir_common(dims, u, delta, a, b, c, d_skip, z, delta_bias, backend, threading,
+                          out_fwd, out_bwd, last_fwd, last_bwd, &cnt);
+    if (rc) return rc;
+    std::vector<Buf> bufs = m1_bufs(cnt, u, delta, a, b, c, d_skip, z, delta_bias, dims->dim);
+    bufs.push_back({out_fwd, cnt.bdl * 4, true});
+    bufs.push_back({out_bwd, cnt.bdl * 4, true});
+    bufs.push_back({last_fwd, cnt.bdn * 4, true});
+    bufs.push_back({last_bwd, cnt.bdn * 4, true});
+    return run_sync(bufs, [&](const std::vector<void*>& p, cudaStream_t s) {
+        M1Params m = m1_params(dims, p, delta_softplus, 0);
+        return bidir_run(m, static_cast<float*>(p[8]), static_cast<float*>(p[9]),
+                         static_cast<float*>(p[10]), static_cast<float*>(p[11]), backend, s);
+    });
+}
+
+int arm_scan_selective_scan_bidirectional_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
+    const float* c, const float* d_skip, const float* z, const float* delta_bias,
+    int delta_softplus, int backend, int threading, float* out_fwd, float* out_bwd,
+    float* last_fwd, float* last_bwd, void* stream) {
+    M1Counts cnt;
+    int rc = bidir_common(dims, u, delta, a, b, c, d_skip, z, delta_bias, backend, threading,
+                          out_fwd, out_bwd, last_fwd, last_bwd, &cnt);
+    if (rc) return rc;
+    std::vector<void*> p = {const_cast<float*>(u),     const_cast<float*>(delta),
+                            const_cast<float*>(a),     const_cast<float*>(b),
+                            const_cast<float*>(c),     const_cast<float*>(d_skip),
+                            const_cast<float*>(z),     const_cast<float*>(delta_bias)};
+    M1Params m = m1_params(dims, p, delta_softplus, 0);
+    return bidir_run(m, out_fwd, out_bwd, last_fwd, last_bwd, backend,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const float* k,
+                             const float* v, const float* adt, const float* dt, const float* trap,
+                             const float* q_bias, const float* k_bias, const float* cos,
+                             const float* sin, const float* d_skip, const float* z,
+                             const float* mimo_psi, const float* mimo_zeta, const float* mimo_phi,
+                             int reverse, int backend, int threading, float* out,
+                             float* last_state, float* last_bx) {
+    const void* req[] = {dims, q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, out};
+    bool mimo = false;
+    int rc = m3_check_ptrs(req, 12, last_state, last_bx, mimo_psi, mimo_zeta, mimo_phi, &mimo);
+    if (rc) return rc;
+    if ((rc = check_enums(backend, threading))) return rc;
+    M3Counts cnt;
+    if ((rc = m3_validate(dims, mimo, last_state, last_bx, &cnt))) return rc;
+    std::vector<Buf> bufs = m3_bufs(cnt, dims, q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin,
+                                    d_skip, z, mimo_psi, mimo_zeta, mimo_phi, out, last_state,
+                                    last_bx);
+    return run_sync(bufs, [&](const std::vector<void*>& p, cudaStream_t s) {
+        return m3_run(m3_params(dims, p, reverse), backend, s);
+    });
+}
+
+int arm_scan_mamba3_scan_f32_async(const ArmMamba3Dims* dims, const float* q, const float* k,
+                                   const float* v, const float* adt, const float* dt,
+                                   const float* trap, const float* q_bias, const float* k_bias,
+                                   const float* cos, const float* sin, const float* d_skip,
+                                   const float* z, const float* mimo_psi, const float* mimo_zeta,
+                                   const float* mimo_phi, int reverse, int backend, int threading,
+                                   float* out, float* last_state, float* last_bx, void* stream) {
+    const void* req[] = {dims, q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, out};
+    bool mimo = false;
+    int rc = m3_check_ptrs(req, 12, last_state, last_bx, mimo_psi, mimo_zeta, mimo_phi, &mimo);
+    if (rc) return rc;
+    if ((rc = check_enums(backend, threading))) return rc;
+    M3Counts cnt;
+    if ((rc = m3_validate(dims, mimo, last_state, last_bx, &cnt))) return rc;
+    std::vector<void*> p = {
+        const_cast<float*>(q),      const_cast<float*>(k),         const_cast<float*>(v),
+        const_cast<float*>(adt),    const_cast<float*>(dt),        const_cast<float*>(trap),
+        const_cast<float*>(q_bias), const_cast<float*>(k_bias),    const_cast<float*>(cos),
+        const_cast<float*>(sin),    const_cast<float*>(d_skip),    const_cast<float*>(z),
+        const_cast<float*>(mimo_psi), const_cast<float*>(mimo_zeta), const_cast<float*>(mimo_phi),
+        out,                        last_state,                    last_bx};
+    return m3_run(m3_params(dims, p, reverse), backend, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

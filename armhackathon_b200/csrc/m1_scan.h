@@ -1,0 +1,38 @@
+// Internal launch interface of the Mamba-1 kernels (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b200scan {
+
+constexpr int kBackendAuto = 0;
+constexpr int kBackendSequential = 1;  // the ABI's "scalar" backend value
+constexpr int64_t kMaxState = 256;
+
+// Device pointers, layouts as reference kernel/arm-scan-core/src/lib.rs:9-16.
+struct M1Params {
+    const float* u;
+    const float* delta;
+    const float* A;
+    const float* B;
+    const float* C;
+    const float* d_skip;      // nullable
+    const float* z;           // nullable
+    const float* delta_bias;  // nullable
+    const float* h0;          // nullable
+    float* out;
+    float* last_state;        // nullable
+    int64_t batch, dim, len, state, groups;
+    int delta_softplus;
+    int reverse;
+};
+
+bool m1_pointers_aligned16(const M1Params& p);
+int m1_pick_channels_per_cta(int64_t rows);
+cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream);
+// Forward and reverse scans of the same inputs (fused bidirectional entry).
+cudaError_t m1_bidir_launch(const M1Params& fwd, const M1Params& bwd, int backend,
+                            cudaStream_t stream);
+
+}  // namespace b200scan

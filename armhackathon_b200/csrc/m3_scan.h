@@ -1,0 +1,37 @@
+// Internal launch interface of the Mamba-3 kernels (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b200scan {
+
+// Device pointers, layouts as reference kernel/arm-scan-core/src/mamba3/
+// mod.rs:44-56 (with rank: q, k (b, l, rank, dqk); biases (h, rank, dqk)).
+struct M3Params {
+    const float* q;
+    const float* k;
+    const float* v;
+    const float* adt;
+    const float* dt;
+    const float* trap;
+    const float* q_bias;
+    const float* k_bias;
+    const float* cos;
+    const float* sin;
+    const float* d_skip;  // nullable
+    const float* z;       // nullable
+    const float* psi;     // MIMO only (all three or none)
+    const float* zeta;
+    const float* phi;
+    float* out;           // (b, h, l, dv) head-major
+    float* last_state;    // nullable, (b, h, dv, dqk)
+    float* last_bx;       // nullable, (b, h, dqk), SISO only
+    int64_t batch, heads, dv, dqk, len, rank;
+    int reverse;
+};
+
+bool m3_shape_supported(int64_t dv, int64_t dqk, int64_t rank);
+cudaError_t m3_scan_launch(const M3Params& p, int backend, cudaStream_t stream);
+
+}  // namespace b200scan

@@ -1,0 +1,243 @@
+"""PyTorch front-end of the Mamba-3 scans (SISO and rank-r MIMO).
+
+Same surface as the reference's python/arm_scan/mamba3.py: the custom op
+``arm_scan::mamba3_scan`` (with a fake kernel), ``angles_to_cos_sin`` (the RoPE
+angle pre-pass), ``mamba3_scan``, ``mamba3_scan_pair`` and
+``mamba3_mimo_scan``, with the reference's argument names, layouts and shape
+checks.  Extension: ``return_last_state=True`` also returns the final state
+(batch, heads, dv, dqk), which the reference's op never exposes.
+
+Contracts kept from the reference:
+* ``trap`` is PRE-sigmoid; the kernel applies the sigmoid.
+* angles arrive raw and ``angles_to_cos_sin`` accumulates
+  theta = cumsum(tanh(angle) * pi * dt) along the traversal-order time axis;
+  fewer angle pairs than dqk/2 are padded with the identity rotation.
+* SISO rotates interleaved lane pairs, MIMO rotates split halves.
+* the kernel writes head-major (b, h, l, dv); the op returns time-major
+  (b, l, h, dv).
+All tensors of a call live on one device; CPU tensors are computed on the
+current CUDA device through the synchronous entry point.
+"""
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _ffi
+from .op import _CALLS, _on_device, _prep, _ptr, _stream
+from .op import kernel_calls  # noqa: F401  (re-export, like the reference)
+
+
+def angles_to_cos_sin(angles: torch.Tensor, dt: torch.Tensor,
+                      half: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """RoPE angle pre-pass: theta = cumsum(tanh(angle) * pi * dt) over time.
+
+    angles (b, l, h, r) raw, dt (b, h, l) post-softplus, half = dqk // 2;
+    returns cos, sin (b, l, h, half), computed at the angles' precision
+    floored at float32; pairs r..half-1 get cos = 1, sin = 0.
+    """
+    if angles.dim() != 4:
+        raise ValueError(f"angles must be (b, l, h, r), got {tuple(angles.shape)}")
+    r = angles.shape[-1]
+    if r > half:
+        raise ValueError(f"angles has {r} rotation pairs but the head dim allows {half}")
+    dtype = torch.promote_types(angles.dtype, torch.float32)
+    dt_blh = dt.permute(0, 2, 1).unsqueeze(-1).to(dtype)
+    theta = torch.cumsum(torch.tanh(angles.to(dtype)) * math.pi * dt_blh, dim=1)
+    cos, sin = torch.cos(theta), torch.sin(theta)
+    if r < half:
+        pad = (*theta.shape[:-1], half - r)
+        cos = torch.cat([cos, torch.ones(pad, dtype=cos.dtype, device=cos.device)], dim=-1)
+        sin = torch.cat([sin, torch.zeros(pad, dtype=sin.dtype, device=sin.device)], dim=-1)
+    return cos, sin
+
+
+@torch.library.custom_op("arm_scan::mamba3_scan", mutates_args=())
+def _mamba3_scan_op(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    adt: torch.Tensor,
+    dt: torch.Tensor,
+    trap: torch.Tensor,
+    q_bias: torch.Tensor,
+    k_bias: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    d_skip: Optional[torch.Tensor],
+    z: Optional[torch.Tensor],
+    reverse: bool,
+    psi: Optional[torch.Tensor] = None,
+    zeta: Optional[torch.Tensor] = None,
+    phi: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    # q is (b, l, 1, dqk) for SISO (axis 2 = the single B/C group) and
+    # (b, l, rank, dqk) for MIMO (axis 2 = rank); the projections decide.
+    b, length, rank, dqk = q.shape
+    h, dv = v.shape[2], v.shape[3]
+    mimo = psi is not None
+    dims = _ffi.ArmMamba3Dims(b, h, dv, dqk, length, rank)
+    out_hm = v.new_empty((b, h, length, dv))
+    last_state = v.new_empty((b, h, dv, dqk))
+    last_bx = None if mimo else v.new_empty((b, h, dqk))
+    with _on_device(v):
+        _ffi.mamba3_raw(
+            dims,
+            [q.data_ptr(), k.data_ptr(), v.data_ptr(), adt.data_ptr(), dt.data_ptr(),
+             trap.data_ptr(), q_bias.data_ptr(), k_bias.data_ptr(), cos.data_ptr(),
+             sin.data_ptr(), _ptr(d_skip), _ptr(z), _ptr(psi), _ptr(zeta), _ptr(phi)],
+            1 if reverse else 0, _ffi.BACKENDS["auto"], _ffi.THREADING["auto"],
+            out_hm.data_ptr(), last_state.data_ptr(), _ptr(last_bx), stream=_stream(v))
+    _CALLS["n"] += 1
+    return out_hm.permute(0, 2, 1, 3).contiguous(), last_state
+
+
+@_mamba3_scan_op.register_fake
+def _(q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, d_skip, z, reverse,
+      psi=None, zeta=None, phi=None):
+    b, length, _, dqk = q.shape
+    h, dv = v.shape[2], v.shape[3]
+    return v.new_empty((b, length, h, dv)), v.new_empty((b, h, dv, dqk))
+
+
+def _check_shapes(q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, D, z):
+    """Every tensor against the SISO layout contract.  The C entry point is
+    told how many elements to read, so a short buffer would be an
+    out-of-bounds read rather than an error: shapes are owned here."""
+    b, length, groups, dqk = q.shape
+    if groups != 1:
+        raise ValueError(f"SISO expects one B/C group, got {groups}")
+    if dqk % 2:
+        raise ValueError(f"dqk must be even (RoPE lane pairs), got {dqk}")
+    if v.dim() != 4:
+        raise ValueError(f"v must be (b, l, h, dv), got {tuple(v.shape)}")
+    h, dv = v.shape[2], v.shape[3]
+    half = dqk // 2
+    want = {
+        "q": (b, length, 1, dqk), "k": (b, length, 1, dqk), "v": (b, length, h, dv),
+        "adt": (b, h, length), "dt": (b, h, length), "trap": (b, h, length),
+        "q_bias": (h, dqk), "k_bias": (h, dqk),
+        "cos": (b, length, h, half), "sin": (b, length, h, half),
+    }
+    got = dict(q=q, k=k, v=v, adt=adt, dt=dt, trap=trap, q_bias=q_bias, k_bias=k_bias,
+               cos=cos, sin=sin)
+    if D is not None:
+        want["D"], got["D"] = (h,), D
+    if z is not None:
+        want["z"], got["z"] = (b, length, h, dv), z
+    for name, shape in want.items():
+        actual = tuple(got[name].shape)
+        if actual != shape:
+            raise ValueError(f"{name} must be {shape}, got {actual}")
+
+
+def mamba3_scan(q, k, v, adt, dt, trap, q_bias, k_bias, angles=None,
+                D=None, z=None, reverse=False, cos=None, sin=None,
+                return_last_state=False):
+    """Mamba-3 SISO selective scan.
+
+    q, k : (b, l, 1, dqk) or (b, l, dqk);  v, z : (b, l, h, dv)
+    adt, dt : (b, h, l) (adt = A*dt <= 0, dt post-softplus);  trap : (b, h, l)
+    angles : (b, l, h, r) raw (the pre-pass runs here), or pass cos/sin
+    q_bias, k_bias : (h, dqk);  D : (h,)
+    returns (b, l, h, dv) [, last_state (b, h, dv, dqk)]
+    """
+    if q.dim() == 3:
+        q = q.unsqueeze(2)
+    if k.dim() == 3:
+        k = k.unsqueeze(2)
+    if (cos is None) != (sin is None):
+        raise ValueError("pass cos and sin together, or neither")
+    half = q.shape[-1] // 2
+    if cos is None:
+        if angles is None:
+            raise ValueError("pass either `angles` or both `cos` and `sin`")
+        cos, sin = angles_to_cos_sin(angles, dt, half)
+    _check_shapes(q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, D, z)
+    dev = v.device
+    opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
+    out, last = _mamba3_scan_op(
+        _prep(q, dev), _prep(k, dev), _prep(v, dev), _prep(adt, dev), _prep(dt, dev),
+        _prep(trap, dev), _prep(q_bias, dev), _prep(k_bias, dev), _prep(cos, dev),
+        _prep(sin, dev), opt(D), opt(z), bool(reverse))
+    return (out, last) if return_last_state else out
+
+
+def mamba3_scan_pair(q, k, v, adt, dt, trap, q_bias, k_bias, angles=None,
+                     D=None, z=None, cos=None, sin=None):
+    """Both traversal directions of the same inputs -> (fwd, bwd).
+
+    The angle pre-pass runs once and is shared: a reverse traversal walks the
+    same tokens backward, each keeping its own position's rotation.
+    """
+    if cos is None:
+        if angles is None:
+            raise ValueError("pass either `angles` or both `cos` and `sin`")
+        cos, sin = angles_to_cos_sin(angles, dt, q.shape[-1] // 2)
+    common = dict(q_bias=q_bias, k_bias=k_bias, D=D, z=z, cos=cos, sin=sin)
+    fwd = mamba3_scan(q, k, v, adt, dt, trap, reverse=False, **common)
+    bwd = mamba3_scan(q, k, v, adt, dt, trap, reverse=True, **common)
+    return fwd, bwd
+
+
+def mamba3_mimo_scan(q, k, v, adt, dt, trap, q_bias, k_bias, psi, zeta, phi,
+                     angles=None, D=None, z=None, reverse=False, cos=None, sin=None,
+                     return_last_state=False):
+    """Mamba-3 MIMO (rank-r) selective scan.
+
+    q, k : (b, l, r, 1, dqk) or (b, l, r, dqk);  v, z : (b, l, h, dv)
+    adt, dt, trap : (b, h, l);  q_bias, k_bias : (h, r, dqk)
+    psi, zeta, phi : (h, r, dv) input / gate / output projections
+    angles : (b, l, h, a) raw;  D : (h,)
+    returns (b, l, h, dv) [, last_state (b, h, dv, dqk)]
+
+    Not a SISO call at r = 1: MIMO rotates split halves (i, i + dqk/2).
+    """
+    if q.dim() == 5:
+        if q.shape[3] != 1:
+            raise ValueError(f"MIMO expects one B/C group, got {q.shape[3]}")
+        q = q[:, :, :, 0, :]
+    if k.dim() == 5:
+        k = k[:, :, :, 0, :]
+    if q.dim() != 4 or k.dim() != 4:
+        raise ValueError(f"q/k must be (b, l, r, dqk) after squeezing the group axis; got "
+                         f"{tuple(q.shape)} and {tuple(k.shape)}")
+    rank, dqk = q.shape[2], q.shape[3]
+    h, dv = v.shape[2], v.shape[3]
+    if (cos is None) != (sin is None):
+        raise ValueError("pass cos and sin together, or neither")
+    if cos is None:
+        if angles is None:
+            raise ValueError("pass either `angles` or both `cos` and `sin`")
+        cos, sin = angles_to_cos_sin(angles, dt, dqk // 2)
+    for name, t, want in (
+        ("q", q, (q.shape[0], q.shape[1], rank, dqk)),
+        ("k", k, (q.shape[0], q.shape[1], rank, dqk)),
+        ("q_bias", q_bias, (h, rank, dqk)),
+        ("k_bias", k_bias, (h, rank, dqk)),
+        ("psi", psi, (h, rank, dv)),
+        ("zeta", zeta, (h, rank, dv)),
+        ("phi", phi, (h, rank, dv)),
+    ):
+        if tuple(t.shape) != want:
+            raise ValueError(f"{name} must be {want}, got {tuple(t.shape)}")
+    if z is not None and tuple(z.shape) != tuple(v.shape):
+        raise ValueError(f"z must match v {tuple(v.shape)}, got {tuple(z.shape)}")
+    b, length = q.shape[0], q.shape[1]
+    half = dqk // 2
+    for name, t, want in (("adt", adt, (b, h, length)), ("dt", dt, (b, h, length)),
+                          ("trap", trap, (b, h, length)), ("cos", cos, (b, length, h, half)),
+                          ("sin", sin, (b, length, h, half))):
+        if tuple(t.shape) != want:
+            raise ValueError(f"{name} must be {want}, got {tuple(t.shape)}")
+    if D is not None and tuple(D.shape) != (h,):
+        raise ValueError(f"D must be ({h},), got {tuple(D.shape)}")
+    dev = v.device
+    opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
+    out, last = _mamba3_scan_op(
+        _prep(q, dev), _prep(k, dev), _prep(v, dev), _prep(adt, dev), _prep(dt, dev),
+        _prep(trap, dev), _prep(q_bias, dev), _prep(k_bias, dev), _prep(cos, dev),
+        _prep(sin, dev), opt(D), opt(z), bool(reverse), _prep(psi, dev), _prep(zeta, dev),
+        _prep(phi, dev))
+    return (out, last) if return_last_state else out

@@ -1,0 +1,181 @@
+"""PyTorch front-end of the Mamba-1 selective scan.
+
+Same surface as the reference's python/arm_scan/op.py: custom ops
+``arm_scan::selective_scan`` and ``arm_scan::selective_scan_bidirectional``
+with fake (meta) kernels, so they trace under ``torch.compile`` without a graph
+break, and the Python wrappers ``selective_scan`` /
+``selective_scan_bidirectional`` with the reference's argument names and
+defaults.
+
+Where the computation runs: always on the GPU, through libb200scan.so.
+* CUDA tensors are passed as device pointers to the ``_async`` entry points on
+  the current torch stream (no host synchronization).
+* CPU tensors (what reference callers pass) go through the synchronous entry
+  points, which copy them to the current CUDA device, run the kernel and copy
+  the results back -- the reference's blocking contract.  Pinned host tensors
+  make those copies faster.
+There is no CPU implementation: without a GPU the call raises.
+
+Inference only: no autograd formula is registered (as in the reference).
+"""
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import _ffi
+
+_CALLS = {"n": 0}
+
+
+def _prep(t: torch.Tensor, device) -> torch.Tensor:
+    return t.to(device=device, dtype=torch.float32).contiguous()
+
+
+def _ptr(t: Optional[torch.Tensor]) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor):
+    """Stream handle for a CUDA tensor's device, None for host tensors."""
+    if t.device.type == "cuda":
+        return torch.cuda.current_stream(t.device).cuda_stream
+    return None
+
+
+class _on_device:
+    """Make ``t``'s CUDA device current for the duration of a call."""
+
+    def __init__(self, t):
+        self.ctx = torch.cuda.device(t.device) if t.device.type == "cuda" else None
+
+    def __enter__(self):
+        if self.ctx is not None:
+            self.ctx.__enter__()
+
+    def __exit__(self, *exc):
+        if self.ctx is not None:
+            self.ctx.__exit__(*exc)
+
+
+@torch.library.custom_op("arm_scan::selective_scan", mutates_args=())
+def _selective_scan_op(
+    u: torch.Tensor,
+    delta: torch.Tensor,
+    a: torch.Tensor,
+    b: torch.Tensor,
+    c: torch.Tensor,
+    d_skip: Optional[torch.Tensor],
+    z: Optional[torch.Tensor],
+    delta_bias: Optional[torch.Tensor],
+    h0: Optional[torch.Tensor],
+    delta_softplus: bool,
+    reverse: bool,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    batch, dim, length = u.shape
+    state = a.shape[1]
+    groups = b.shape[1] if b.dim() == 4 else 1
+    out = torch.empty_like(u)
+    last_state = u.new_empty((batch, dim, state))
+    dims = _ffi.ArmScanDims(batch, dim, length, state, groups)
+    with _on_device(u):
+        _ffi.scan_raw(
+            dims, u.data_ptr(), delta.data_ptr(), a.data_ptr(), b.data_ptr(), c.data_ptr(),
+            _ptr(d_skip), _ptr(z), _ptr(delta_bias), delta_softplus, "auto", "auto",
+            out.data_ptr(), last_state.data_ptr(), ptr_h0=_ptr(h0), reverse=reverse,
+            stream=_stream(u))
+    _CALLS["n"] += 1
+    return out, last_state
+
+
+@_selective_scan_op.register_fake
+def _(u, delta, a, b, c, d_skip, z, delta_bias, h0, delta_softplus, reverse):
+    return torch.empty_like(u), u.new_empty((u.shape[0], u.shape[1], a.shape[1]))
+
+
+def _bc4(t, batch, state, length):
+    return t.reshape(batch, 1, state, length) if t.dim() == 3 else t
+
+
+def selective_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None,
+                   delta_softplus=False, return_last_state=False,
+                   initial_state=None, reverse=False):
+    """Mamba-1 selective scan.
+
+    u, delta, z : (batch, dim, len);  A : (dim, state)
+    B, C        : (batch, state, len) or (batch, groups, state, len)
+    D, delta_bias : (dim,);  initial_state : (batch, dim, state) or None
+    Returns out (batch, dim, len) [, last_state (batch, dim, state)], on u's
+    device.  Inputs are converted to contiguous float32 on u's device, so
+    transposed views and other devices' tensors are accepted.
+
+    ``reverse`` walks the sequence backward: output index t is still step t,
+    it equals flipping u/delta/B/C/z in time, scanning forward and flipping
+    the result; ``last_state`` is then the state after consuming t = 0.
+    """
+    batch, dim, length = u.shape
+    state = A.shape[1]
+    dev = u.device
+    B = _bc4(B, batch, state, length)
+    C = _bc4(C, batch, state, length)
+    opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
+    out, last_state = _selective_scan_op(
+        _prep(u, dev), _prep(delta, dev), _prep(A, dev), _prep(B, dev), _prep(C, dev),
+        opt(D), opt(z), opt(delta_bias), opt(initial_state), bool(delta_softplus),
+        bool(reverse))
+    return (out, last_state) if return_last_state else out
+
+
+@torch.library.custom_op("arm_scan::selective_scan_bidirectional", mutates_args=())
+def _selective_scan_bidir_op(
+    u: torch.Tensor,
+    delta: torch.Tensor,
+    a: torch.Tensor,
+    b: torch.Tensor,
+    c: torch.Tensor,
+    d_skip: Optional[torch.Tensor],
+    z: Optional[torch.Tensor],
+    delta_bias: Optional[torch.Tensor],
+    delta_softplus: bool,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    batch, dim, length = u.shape
+    state = a.shape[1]
+    out_fwd = torch.empty_like(u)
+    out_bwd = torch.empty_like(u)
+    dims = _ffi.ArmScanDims(batch, dim, length, state, b.shape[1] if b.dim() == 4 else 1)
+    with _on_device(u):
+        _ffi.scan_bidir_raw(
+            dims, u.data_ptr(), delta.data_ptr(), a.data_ptr(), b.data_ptr(), c.data_ptr(),
+            _ptr(d_skip), _ptr(z), _ptr(delta_bias), delta_softplus, "auto", "auto",
+            out_fwd.data_ptr(), out_bwd.data_ptr(), stream=_stream(u))
+    _CALLS["n"] += 1
+    return out_fwd, out_bwd
+
+
+@_selective_scan_bidir_op.register_fake
+def _(u, delta, a, b, c, d_skip, z, delta_bias, delta_softplus):
+    return torch.empty_like(u), torch.empty_like(u)
+
+
+def selective_scan_bidirectional(u, delta, A, B, C, D=None, z=None,
+                                 delta_bias=None, delta_softplus=False):
+    """Forward and backward scans of the same inputs in one call.
+
+    Layouts as ``selective_scan``; returns (out_fwd, out_bwd).  Equal to
+    ``selective_scan`` plus ``selective_scan(..., reverse=True)``; merging
+    the two directions is the caller's job (``bidirectional_scan``).
+    """
+    batch, dim, length = u.shape
+    state = A.shape[1]
+    dev = u.device
+    B = _bc4(B, batch, state, length)
+    C = _bc4(C, batch, state, length)
+    opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
+    return _selective_scan_bidir_op(
+        _prep(u, dev), _prep(delta, dev), _prep(A, dev), _prep(B, dev), _prep(C, dev),
+        opt(D), opt(z), opt(delta_bias), bool(delta_softplus))
+
+
+def kernel_calls() -> int:
+    """How many times a native scan entry point has been invoked."""
+    return _CALLS["n"]

@@ -1,0 +1,337 @@
+"""Benchmark of the selective-scan hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload prefill_scan|cfg0]
+
+A step is one Mamba-1 ``selective_scan`` call over one batch of synthetic
+input (fp32, seed 0).  Default workload ``prefill_scan``: the per-layer scan
+of BASELINE config 1 (HF Mamba-1 130M architecture prefill, batch 8 x
+L 2048, d_inner 1536, d_state 16, softplus + delta_bias + D skip + z gate,
+final state returned); 405.5 MB of algorithmic traffic per step, larger than
+the 126 MB L2, so no flush is needed between steps.  ``cfg0`` is BASELINE
+config 0 (batch 1) with an L2 flush between steps.
+
+value      -- algorithmic GB/s of the whole job (all ranks), inputs resident
+              in HBM, CUDA-event timed, max over ranks.
+e2e        -- the same metric through the reference-facing synchronous C
+              entry point with pinned HOST buffers (H2D + kernel + D2H inside
+              the timed region).
+roofline   -- the scan kernel's achieved algorithmic bandwidth against the
+              measured HBM copy bandwidth.
+cpu_baseline -- the oracle port of the reference's x86 CPU path (scalar
+              recurrence, rows spread over all host threads), rank 0 only.
+
+Multi-GPU: one process per GPU (torchrun); each rank scans its own batch
+(weak scaling over batch rows, no collective on the data path).
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "scan GB/s & elems/s vs HBM roofline at 1/2/4/8 B200; Mamba-1 prefill tok/s"
+
+WORKLOADS = {
+    "prefill_scan": dict(batch=8, dim=1536, len=2048, state=16, flush=False,
+                         desc="Mamba-1 selective_scan at the 130M prefill shape (BASELINE "
+                              "config 1's per-layer scan): batch 8 x L 2048, d_inner 1536, "
+                              "d_state 16, fp32"),
+    "cfg0": dict(batch=1, dim=1536, len=2048, state=16, flush=True,
+                 desc="BASELINE config 0: Mamba-1 selective_scan B1 D1536 L2048 N16 fp32"),
+}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def algorithmic_bytes(w):
+    B, D, L, N = w["batch"], w["dim"], w["len"], w["state"]
+    return 4 * (4 * B * D * L + 2 * B * N * L + D * N + 2 * D + B * D * N)
+
+
+def make_inputs(w, device, seed=0):
+    """Synthetic inputs with BASELINE config 0's distributions."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, D, L, N = w["batch"], w["dim"], w["len"], w["state"]
+    rn = lambda *s: torch.randn(*s, generator=g, device=device)  # noqa: E731
+    dt = torch.exp(torch.empty(D, device=device).uniform_(np.log(1e-3), np.log(1e-1),
+                                                           generator=g))
+    return dict(u=rn(B, D, L), delta=rn(B, D, L), z=rn(B, D, L),
+                A=-torch.arange(1, N + 1, device=device, dtype=torch.float32).repeat(D, 1),
+                B=rn(B, N, L), C=rn(B, N, L), D=torch.ones(D, device=device),
+                delta_bias=torch.log(torch.expm1(dt)))
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def run_reference(args, w):
+    """--impl reference: the reference's CPU path (scalar recurrence over rows
+    on all host threads; oracle port, the Rust crate has no toolchain here)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    nthreads = oracle.hw_threads()
+    rng = np.random.default_rng(0)
+    B, D, L, N = w["batch"], w["dim"], w["len"], w["state"]
+    f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    dt = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), D))
+    inp = dict(u=f(B, D, L), delta=f(B, D, L), z=f(B, D, L),
+               A=-np.tile(np.arange(1, N + 1, dtype=np.float32), (D, 1)), B=f(B, N, L),
+               C=f(B, N, L), D=np.ones(D, np.float32),
+               delta_bias=np.log(np.expm1(dt)).astype(np.float32))
+    for _ in range(args.warmup):
+        oracle.m1_scan(**inp, delta_softplus=True, dtype=np.float32, nthreads=nthreads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.m1_scan(**inp, delta_softplus=True, dtype=np.float32, nthreads=nthreads)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    gbs = algorithmic_bytes(w) / t / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": 0,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seed 0, BASELINE config 0 distributions)",
+            "config": {"workload": args.workload, "desc": w["desc"], "batch": B, "dim": D,
+                       "len": L, "state": N},
+            "elems_per_s": B * D * L / t,
+            "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": nthreads, "kind": "port",
+                             "sample": f"the full step workload ({B}x{D}x{L}, N={N}) per step"},
+            "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(w):
+    """Oracle port of the reference's CPU path on a bounded sample: all host
+    threads, batch row 0 only (1/batch of the workload)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    nthreads = oracle.hw_threads()
+    rng = np.random.default_rng(0)
+    D, L, N = w["dim"], w["len"], w["state"]
+    f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    dt = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), D))
+    inp = dict(u=f(1, D, L), delta=f(1, D, L), z=f(1, D, L),
+               A=-np.tile(np.arange(1, N + 1, dtype=np.float32), (D, 1)), B=f(1, N, L),
+               C=f(1, N, L), D=np.ones(D, np.float32),
+               delta_bias=np.log(np.expm1(dt)).astype(np.float32))
+    oracle.m1_scan(**inp, delta_softplus=True, dtype=np.float32, nthreads=nthreads)
+    reps, t_total = 0, 0.0
+    while t_total < 3.0 and reps < 50:
+        t0 = time.perf_counter()
+        oracle.m1_scan(**inp, delta_softplus=True, dtype=np.float32, nthreads=nthreads)
+        t_total += time.perf_counter() - t0
+        reps += 1
+    t = t_total / reps
+    sample = dict(w, batch=1)
+    return {"value": algorithmic_bytes(sample) / t / 1e9, "unit": "GB/s", "cores": nthreads,
+            "kind": "port",
+            "sample": f"batch row 0 of the workload (1x{D}x{L}, N={N}), {reps} reps"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="prefill_scan", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w)
+        return
+
+    import torch
+    import torch.distributed as dist
+    import armhackathon_b200 as arm
+    from armhackathon_b200 import _ffi
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    x = make_inputs(w, dev, seed=rank)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if w["flush"] else None
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return arm.selective_scan(x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"], z=x["z"],
+                                  delta_bias=x["delta_bias"], delta_softplus=True,
+                                  return_last_state=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_begin = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    launches_before = arm.kernel_calls()
+    with ClockSampler(local) as clk:
+        t_begin.record(stream)
+        for i in range(args.steps):
+            if flush is not None:
+                flush.fill_(i & 0xFF)
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    launches = arm.kernel_calls() - launches_before
+    if world > 1:
+        dist.barrier()
+    kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    step_ms = sum(kernel_ms) / len(kernel_ms) if flush is not None else \
+        t_begin.elapsed_time(t_end) / args.steps
+    t = torch.tensor([step_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms = float(t.item())
+    nbytes = algorithmic_bytes(w)
+    value = world * nbytes / (step_ms * 1e-3) / 1e9
+    elems = world * w["batch"] * w["dim"] * w["len"]
+
+    # e2e: the reference-facing synchronous C entry point with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        host = {k: v.cpu().pin_memory() for k, v in x.items()}
+        B, D, L, N = w["batch"], w["dim"], w["len"], w["state"]
+        out_h = torch.empty((B, D, L)).pin_memory()
+        last_h = torch.empty((B, D, N)).pin_memory()
+        dims = _ffi.ArmScanDims(B, D, L, N, 1)
+
+        def e2e_step():
+            _ffi.scan_raw(dims, host["u"].data_ptr(), host["delta"].data_ptr(),
+                          host["A"].data_ptr(), host["B"].data_ptr(), host["C"].data_ptr(),
+                          host["D"].data_ptr(), host["z"].data_ptr(),
+                          host["delta_bias"].data_ptr(), True, "auto", "auto",
+                          out_h.data_ptr(), last_h.data_ptr())
+        for _ in range(2):
+            e2e_step()
+        if world > 1:
+            dist.barrier()
+        e_steps = max(3, min(args.steps, 10))
+        t0 = time.perf_counter()
+        for _ in range(e_steps):
+            e2e_step()
+        e_ms = (time.perf_counter() - t0) * 1e3 / e_steps
+        te = torch.tensor([e_ms], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e_ms = float(te.item())
+        h2d = sum(v.numel() * 4 for v in host.values())
+        d2h = (out_h.numel() + last_h.numel()) * 4
+        e2e = {"value": world * nbytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
+               "path": "arm_scan_selective_scan_f32 (synchronous C entry, pinned host buffers)"}
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        k_ms = statistics.mean(kernel_ms)
+        achieved = nbytes / (k_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seed = rank, BASELINE config 0 distributions)",
+            "config": {"workload": args.workload, "desc": w["desc"], "batch_per_gpu": w["batch"],
+                       "dim": w["dim"], "len": w["len"], "state": w["state"],
+                       "parallelism": f"dp{world} (batch rows per rank, no collective)",
+                       "l2": "inputs larger than L2" if not w["flush"] else
+                             "256 MB L2 flush between steps (outside the kernel events)"},
+            "elems_per_s": elems / (step_ms * 1e-3),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_kind,
+                         "traffic": None, "bytes_per_launch": nbytes,
+                         "kernel_ms": k_ms},
+            "gpu_launches": launches,
+            "e2e": e2e,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(w)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,150 @@
+/*
+ * b200scan -- C ABI of the B200 selective-scan engine (libb200scan.so).
+ *
+ * Drop-in replacement for the reference's Rust cdylib
+ * kernel/arm-scan-ffi/src/lib.rs (ABI v7).  Entry points, structs, enum values
+ * and return codes 0-5 keep the reference's names, argument order and meaning
+ * so an existing ctypes/cgo binding only changes the library path and the
+ * expected version number (v8).  v8 adds:
+ *   - device-pointer, stream-ordered variants (suffix _async) that take a
+ *     cudaStream_t as `void* stream` and never synchronize;
+ *   - a final-state output for the Mamba-3 SISO and MIMO scans;
+ *   - return codes 6 (CUDA error) and 7 (timeout of a bounded wait);
+ *   - arm_scan_last_error(), a per-thread message for the last failure.
+ *
+ * Memory.  The synchronous v7-shaped entry points accept either HOST pointers
+ * (every buffer in host memory: inputs are copied to the current CUDA device,
+ * the scan runs, outputs are copied back, and the call returns when the
+ * results are in the caller's buffers -- the reference's blocking contract) or
+ * DEVICE pointers (every buffer on the current device: the scan runs on the
+ * default stream and the call returns after it completes).  Mixing host and
+ * device buffers in one call is rejected with code 2.  The _async variants
+ * require device pointers and return as soon as the work is enqueued.
+ *
+ * Layouts are the reference's (row-major, contiguous, fp32):
+ *   Mamba-1  u, delta, z, out (batch, dim, len); a (dim, state);
+ *            b, c (batch, groups, state, len); d_skip, delta_bias (dim);
+ *            h0, last_state (batch, dim, state)
+ *   Mamba-3  q, k (batch, len, rank, dqk); v, z (batch, len, heads, dv);
+ *            adt, dt, trap (batch, heads, len); cos, sin (batch, len, heads,
+ *            dqk/2); q_bias, k_bias (heads, rank, dqk); d_skip (heads);
+ *            psi, zeta, phi (heads, rank, dv);
+ *            out (batch, heads, len, dv) -- HEAD-major;
+ *            last_state (batch, heads, dv, dqk); last_bx (batch, heads, dqk)
+ * state (Mamba-1 d_state) must be <= 256.
+ */
+#ifndef B200SCAN_H
+#define B200SCAN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ARM_SCAN_ABI_VERSION 8u
+
+/* Return codes (0-5: reference arm-scan-ffi/src/lib.rs:53-58). */
+#define ARM_SCAN_OK 0
+#define ARM_SCAN_ERR_NULL_POINTER 1
+#define ARM_SCAN_ERR_INVALID_DIMS 2
+#define ARM_SCAN_ERR_BACKEND_UNAVAILABLE 3
+#define ARM_SCAN_ERR_BAD_ENUM 4
+#define ARM_SCAN_ERR_PANIC 5
+#define ARM_SCAN_ERR_CUDA 6
+#define ARM_SCAN_ERR_TIMEOUT 7
+
+/* backend: 0 = auto (chunked sm_100a kernels), 1 = scalar (a sequential
+ * on-device restatement of the reference's scalar loop, for cross-checks),
+ * 2 = neon (not available here: code 3).  threading: 0/1/2 are accepted
+ * (auto/sequential/rayon in the reference) and have no effect on a GPU. */
+
+/* Replaces ArmScanDims, arm-scan-ffi/src/lib.rs:44-50. */
+typedef struct ArmScanDims {
+    size_t batch;
+    size_t dim;
+    size_t len;
+    size_t state;
+    size_t groups;
+} ArmScanDims;
+
+/* Replaces ArmMamba3Dims, arm-scan-ffi/src/lib.rs:363-373. */
+typedef struct ArmMamba3Dims {
+    size_t batch;
+    size_t heads;
+    size_t dv;
+    size_t dqk;
+    size_t len;
+    size_t rank;
+} ArmMamba3Dims;
+
+/* Replaces arm_scan_abi_version, arm-scan-ffi/src/lib.rs:37-40. Returns 8. */
+uint32_t arm_scan_abi_version(void);
+
+/* Message describing the calling thread's most recent non-zero return. */
+const char* arm_scan_last_error(void);
+
+/* Replaces arm_scan_selective_scan_f32, arm-scan-ffi/src/lib.rs:97-116.
+ * Nullable: d_skip, z, delta_bias, last_state, h0. */
+int arm_scan_selective_scan_f32(const ArmScanDims* dims, const float* u,
+                                const float* delta, const float* a,
+                                const float* b, const float* c,
+                                const float* d_skip, const float* z,
+                                const float* delta_bias, int delta_softplus,
+                                int reverse, int backend, int threading,
+                                float* out, float* last_state, const float* h0);
+
+/* Replaces arm_scan_selective_scan_bidirectional_f32,
+ * arm-scan-ffi/src/lib.rs:233-252.  last_fwd/last_bwd both or neither. */
+int arm_scan_selective_scan_bidirectional_f32(
+    const ArmScanDims* dims, const float* u, const float* delta,
+    const float* a, const float* b, const float* c, const float* d_skip,
+    const float* z, const float* delta_bias, int delta_softplus, int backend,
+    int threading, float* out_fwd, float* out_bwd, float* last_fwd,
+    float* last_bwd);
+
+/* Replaces arm_scan_mamba3_scan_f32, arm-scan-ffi/src/lib.rs:417-445.
+ * SISO when psi/zeta/phi are all null (rank must be 1), MIMO when all three
+ * are given; a partial set is code 1.  last_state/last_bx both or neither
+ * (code 1).  For MIMO, last_bx must be null and last_state may be given
+ * (v8 extension: the reference rejects any carry for MIMO). */
+int arm_scan_mamba3_scan_f32(
+    const ArmMamba3Dims* dims, const float* q, const float* k, const float* v,
+    const float* adt, const float* dt, const float* trap, const float* q_bias,
+    const float* k_bias, const float* cos, const float* sin,
+    const float* d_skip, const float* z, const float* mimo_psi,
+    const float* mimo_zeta, const float* mimo_phi, int reverse, int backend,
+    int threading, float* out, float* last_state, float* last_bx);
+
+/* v8: device pointers, enqueued on `stream` (a cudaStream_t; NULL = the
+ * legacy default stream).  Same arguments and codes as the synchronous forms;
+ * a CUDA error raised by the enqueue is code 6. */
+int arm_scan_selective_scan_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta,
+    const float* a, const float* b, const float* c, const float* d_skip,
+    const float* z, const float* delta_bias, int delta_softplus, int reverse,
+    int backend, int threading, float* out, float* last_state,
+    const float* h0, void* stream);
+
+int arm_scan_selective_scan_bidirectional_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta,
+    const float* a, const float* b, const float* c, const float* d_skip,
+    const float* z, const float* delta_bias, int delta_softplus, int backend,
+    int threading, float* out_fwd, float* out_bwd, float* last_fwd,
+    float* last_bwd, void* stream);
+
+int arm_scan_mamba3_scan_f32_async(
+    const ArmMamba3Dims* dims, const float* q, const float* k, const float* v,
+    const float* adt, const float* dt, const float* trap, const float* q_bias,
+    const float* k_bias, const float* cos, const float* sin,
+    const float* d_skip, const float* z, const float* mimo_psi,
+    const float* mimo_zeta, const float* mimo_phi, int reverse, int backend,
+    int threading, float* out, float* last_state, float* last_bx,
+    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200SCAN_H */

@@ -1,0 +1,105 @@
+"""C-ABI library checks that need no GPU: it loads, reports ABI v8, exports
+every entry point include/b200scan.h declares, and rejects bad arguments with
+the reference's codes before touching a device (reference
+kernel/arm-scan-ffi/src/lib.rs:53-58 and its FFI unit tests)."""
+
+import ctypes
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+from armhackathon_b200 import _ffi
+
+HEADER = ROOT / "include" / "b200scan.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(arm_scan_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_with_abi_v8():
+    lib = _ffi.load()
+    assert lib.arm_scan_abi_version() == 8
+    assert _ffi.lib_path().name == "libb200scan.so"
+
+
+def test_every_declared_symbol_is_exported():
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_ffi.lib_path())],
+                         capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\sT\s(\w+)", out))
+    declared = declared_functions()
+    assert declared, "header parse found nothing"
+    missing = [f for f in declared if f not in exported]
+    assert not missing, missing
+    assert set(_ffi.exported_symbols()) <= set(declared)
+
+
+def _m1_call(dims, ptrs=None, backend=0, threading=0, out=True):
+    lib = _ffi.load()
+    buf = (ctypes.c_float * 8)()
+    p = ctypes.cast(buf, ctypes.c_void_p).value
+    args = ptrs if ptrs is not None else [p] * 5
+    return lib.arm_scan_selective_scan_f32(
+        ctypes.byref(dims) if dims is not None else None, *args, None, None, None,
+        1, 0, backend, threading, p if out else None, None, None)
+
+
+def test_null_pointer_rejected():
+    dims = _ffi.ArmScanDims(1, 1, 1, 1, 1)
+    assert _m1_call(dims, out=False) == 1
+    assert _m1_call(None) == 1
+    assert "null" in _ffi.load().arm_scan_last_error().decode()
+
+
+def test_bad_enum_and_neon_backend():
+    dims = _ffi.ArmScanDims(1, 1, 1, 1, 1)
+    assert _m1_call(dims, backend=7) == 4
+    assert _m1_call(dims, threading=-1) == 4
+    assert _m1_call(dims, backend=2) == 3
+
+
+@pytest.mark.parametrize("bad", [(0, 1, 1, 1, 1), (1, 0, 1, 1, 1), (1, 1, 0, 1, 1),
+                                 (1, 1, 1, 0, 1), (1, 1, 1, 1, 0), (1, 3, 4, 16, 2),
+                                 (1, 4, 4, 257, 1)])
+def test_invalid_dims_rejected(bad):
+    assert _m1_call(_ffi.ArmScanDims(*bad)) == 2
+
+
+def test_overflowing_dims_rejected():
+    big = (1 << 63) + 1
+    assert _m1_call(_ffi.ArmScanDims(big, 4, 4, 4, 1)) == 2
+
+
+def test_bidir_half_carry_rejected():
+    lib = _ffi.load()
+    buf = (ctypes.c_float * 8)()
+    p = ctypes.cast(buf, ctypes.c_void_p).value
+    dims = _ffi.ArmScanDims(1, 1, 1, 1, 1)
+    rc = lib.arm_scan_selective_scan_bidirectional_f32(
+        ctypes.byref(dims), p, p, p, p, p, None, None, None, 1, 0, 0, p, p, p, None)
+    assert rc == 2
+
+
+def _m3(dims, mimo=0, last_state=False, last_bx=False, reverse=0):
+    lib = _ffi.load()
+    buf = (ctypes.c_float * 8)()
+    p = ctypes.cast(buf, ctypes.c_void_p).value
+    proj = [p if i < mimo else None for i in range(3)]
+    return lib.arm_scan_mamba3_scan_f32(
+        ctypes.byref(dims), p, p, p, p, p, p, p, p, p, p, None, None, *proj, reverse, 0, 0, p,
+        p if last_state else None, p if last_bx else None)
+
+
+def test_mamba3_argument_rules():
+    siso = _ffi.ArmMamba3Dims(1, 1, 4, 4, 1, 1)
+    assert _m3(siso, mimo=2) == 1                          # partial projections
+    assert _m3(siso, last_state=True) == 1                 # half a carry
+    assert _m3(_ffi.ArmMamba3Dims(1, 1, 4, 5, 1, 1)) == 2  # odd dqk
+    assert _m3(_ffi.ArmMamba3Dims(1, 1, 4, 4, 1, 2)) == 2  # rank>1 without projections
+    assert _m3(_ffi.ArmMamba3Dims(1, 1, 4, 4, 1, 2), mimo=3, last_state=True,
+               last_bx=True) == 2                          # MIMO has no last_bx
+    assert _m3(_ffi.ArmMamba3Dims(0, 1, 4, 4, 1, 1)) == 2  # zero dim

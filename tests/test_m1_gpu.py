@@ -1,0 +1,201 @@
+"""Mamba-1 parity on the GPU: the CUDA kernels (through libb200scan.so's C ABI)
+against the reference's golden vectors and the CPU oracle.
+
+Tolerances: the reference's own gate for fp32 outputs against f64 ground
+truth -- max |out - out_f64| < 1e-4 and < max(50 x the upstream f32 floor,
+1e-6); last_state relative error < 1e-4 (reference tests/check_ffi.py:30-31,
+82-83) -- plus the build's fp32 bar: max relative error <= 1e-4 against the
+oracle, relative to the output's scale.
+"""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+M1_CASES = json.loads((GOLDEN / "index.json").read_text())["m1"]
+REL_TOL = 1e-4
+
+
+def arm():
+    import armhackathon_b200 as a
+    return a
+
+
+def load(name):
+    d = np.load(GOLDEN / "m1" / f"{name}.npz")
+    get = lambda k: d[k] if k in d.files else None  # noqa: E731
+    inputs = dict(u=d["u"], delta=d["delta"], A=d["A"], B=d["B"], C=d["C"], D=get("D_skip"),
+                  z=get("z"), delta_bias=get("delta_bias"),
+                  delta_softplus=bool(d["delta_softplus"]))
+    return inputs, d["out_f64"], d["last_state_f64"], float(d["f32_max_abs_err"])
+
+
+def cuda(inputs):
+    return {k: (torch.from_numpy(np.ascontiguousarray(v)).cuda() if isinstance(v, np.ndarray)
+                else v) for k, v in inputs.items()}
+
+
+def rel_err(got, want):
+    want = np.asarray(want, np.float64)
+    return float(np.abs(np.asarray(got, np.float64) - want).max()
+                 / max(np.abs(want).max(), 1e-30))
+
+
+def gate(out, last, out64, last64, floor):
+    err = np.abs(out.astype(np.float64) - out64).max()
+    assert err < 1e-4 and err < max(50 * floor, 1e-6), err
+    lrel = np.abs(last.astype(np.float64) - last64).max() / max(1.0, np.abs(last64).max())
+    assert lrel < 1e-4, lrel
+
+
+@pytest.mark.parametrize("name", M1_CASES)
+def test_golden_cuda_tensors(name):
+    inputs, out64, last64, floor = load(name)
+    out, last = arm().selective_scan(**cuda(inputs), return_last_state=True)
+    torch.cuda.synchronize()
+    gate(out.cpu().numpy(), last.cpu().numpy(), out64, last64, floor)
+
+
+@pytest.mark.parametrize("name", ["tiny", "medium", "grouped_BC", "hf_mixer_layer0"])
+def test_golden_host_buffers_numpy_api(name):
+    """Host arrays through the synchronous C entry point (library-side staging)."""
+    inputs, out64, last64, floor = load(name)
+    out, last = arm().selective_scan_numpy(**inputs, return_last_state=True)
+    gate(out, last, out64, last64, floor)
+
+
+@pytest.mark.parametrize("name", ["small", "long_seq", "grouped_BC", "edge_L1"])
+def test_sequential_backend_matches(name):
+    inputs, out64, last64, floor = load(name)
+    out, last = arm().selective_scan_numpy(**inputs, return_last_state=True, backend="scalar")
+    gate(out, last, out64, last64, floor)
+
+
+@pytest.mark.parametrize("name", ["small", "medium", "grouped_BC", "state13_neon_tail",
+                                  "extreme_delta", "edge_L1", "no_z"])
+def test_reverse_matches_oracle(name):
+    inputs, *_ = load(name)
+    want, want_last = oracle.m1_scan(**inputs, reverse=True)
+    out, last = arm().selective_scan(**cuda(inputs), reverse=True, return_last_state=True)
+    assert rel_err(out.cpu().numpy(), want) <= REL_TOL
+    assert rel_err(last.cpu().numpy(), want_last) <= REL_TOL
+
+
+def random_case(B, D, L, N, G=1, seed=0, z=True, dskip=True, bias=True):
+    rng = np.random.default_rng(seed)
+    f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    bc = (B, G, N, L) if G > 1 else (B, N, L)
+    return dict(u=f(B, D, L), delta=(f(B, D, L) * 0.5).astype(np.float32),
+                A=(-np.exp(rng.uniform(np.log(0.5), np.log(16), (D, N)))).astype(np.float32),
+                B=f(*bc), C=f(*bc), D=f(D) if dskip else None, z=f(B, D, L) if z else None,
+                delta_bias=rng.uniform(-6, -3, D).astype(np.float32) if bias else None,
+                delta_softplus=True)
+
+
+@pytest.mark.parametrize("shape", [(1, 7, 1001, 16, 1), (3, 40, 515, 13, 4), (2, 33, 4096, 16, 1),
+                                   (1, 1536, 130, 16, 1), (2, 24, 3, 1, 2), (1, 5, 777, 64, 1)])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_ragged_shapes_vs_oracle(shape, reverse):
+    """Lengths off the vector width and the macro-chunk, odd channel counts,
+    grouped B/C and unusual state sizes, forward and reverse."""
+    B, D, L, N, G = shape
+    inputs = random_case(B, D, L, N, G, seed=L)
+    want, want_last = oracle.m1_scan(**inputs, reverse=reverse, nthreads=8)
+    out, last = arm().selective_scan(**cuda(inputs), reverse=reverse, return_last_state=True)
+    assert rel_err(out.cpu().numpy(), want) <= REL_TOL
+    assert rel_err(last.cpu().numpy(), want_last) <= REL_TOL
+
+
+def test_h0_streaming_resume():
+    """Split scan resumed from last_state equals the one-shot scan."""
+    inputs = random_case(2, 96, 1000, 16, seed=3)
+    a = arm()
+    full, last_full = a.selective_scan(**cuda(inputs), return_last_state=True)
+    split = 333
+    tv = ("u", "delta", "B", "C", "z")
+    first = {k: (v[..., :split] if k in tv else v) for k, v in inputs.items()}
+    second = {k: (v[..., split:] if k in tv else v) for k, v in inputs.items()}
+    o1, s1 = a.selective_scan(**cuda(first), return_last_state=True)
+    o2, s2 = a.selective_scan(**cuda(second), return_last_state=True, initial_state=s1)
+    full = full.cpu().numpy()
+    assert rel_err(torch.cat([o1, o2], -1).cpu().numpy(), full) <= REL_TOL
+    assert rel_err(s2.cpu().numpy(), last_full.cpu().numpy()) <= REL_TOL
+
+
+def test_bidirectional_fused_and_merges():
+    inputs = random_case(2, 64, 777, 16, seed=5)
+    a = arm()
+    of, ob = a.selective_scan_bidirectional(**cuda(inputs))
+    wf, wb, _, _ = oracle.m1_scan_bidir(**inputs, nthreads=8)
+    assert rel_err(of.cpu().numpy(), wf) <= REL_TOL
+    assert rel_err(ob.cpu().numpy(), wb) <= REL_TOL
+    s = a.bidirectional_scan(**cuda(inputs), merge="sum")
+    assert rel_err(s.cpu().numpy(), wf + wb) <= REL_TOL
+    c = a.bidirectional_scan(**cuda(inputs), merge="concat")
+    assert tuple(c.shape) == (2, 128, 777)
+    (f2, lf), (b2, lb) = a.bidirectional_scan(**cuda(inputs), merge="none", return_last_state=True)
+    assert rel_err(f2.cpu().numpy(), wf) <= REL_TOL and rel_err(b2.cpu().numpy(), wb) <= REL_TOL
+
+
+def test_ss2d_golden_planes():
+    a = arm()
+    for name in json.loads((GOLDEN / "index.json").read_text())["m1_2d"]:
+        d = np.load(GOLDEN / "m1_2d" / f"{name}.npz")
+        t = lambda k: torch.from_numpy(d[k]).cuda()  # noqa: E731
+        planes = a.ss2d_scan(t("u"), t("delta"), t("A"), t("B"), t("C"), D=t("D"),
+                             delta_bias=t("delta_bias"), merge="none")
+        for key, got in zip(("out_row_fwd", "out_row_bwd", "out_col_fwd", "out_col_bwd"), planes):
+            err = np.abs(got.cpu().numpy().astype(np.float64) - d[key]).max()
+            assert err < 1e-4, (name, key, err)
+
+
+def test_config0_full_size_properties():
+    """BASELINE config 0 at full size (B1 D1536 L2048 N16): against the
+    oracle, and reverse == flip-forward-flip."""
+    rng = np.random.default_rng(0)
+    D, L, N = 1536, 2048, 16
+    dt = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), D))
+    inputs = dict(u=rng.standard_normal((1, D, L)).astype(np.float32),
+                  delta=rng.standard_normal((1, D, L)).astype(np.float32),
+                  A=np.tile(-np.arange(1, N + 1, dtype=np.float32), (D, 1)),
+                  B=rng.standard_normal((1, N, L)).astype(np.float32),
+                  C=rng.standard_normal((1, N, L)).astype(np.float32),
+                  D=np.ones(D, np.float32), z=rng.standard_normal((1, D, L)).astype(np.float32),
+                  delta_bias=np.log(np.expm1(dt)).astype(np.float32), delta_softplus=True)
+    want, want_last = oracle.m1_scan(**inputs, dtype=np.float64, nthreads=8)
+    out, last = arm().selective_scan(**cuda(inputs), return_last_state=True)
+    assert rel_err(out.cpu().numpy(), want) <= REL_TOL
+    assert rel_err(last.cpu().numpy(), want_last) <= REL_TOL
+    fl = {k: (np.ascontiguousarray(np.flip(v, -1)) if k in ("u", "delta", "B", "C", "z") else v)
+          for k, v in inputs.items()}
+    rev = arm().selective_scan(**cuda(inputs), reverse=True)
+    fwd_of_flip = arm().selective_scan(**cuda(fl))
+    assert rel_err(torch.flip(rev, [-1]).cpu().numpy(), fwd_of_flip.cpu().numpy()) <= REL_TOL
+
+
+def test_cpu_tensors_run_on_gpu_and_come_back():
+    inputs, out64, last64, floor = load("medium")
+    t = {k: (torch.from_numpy(v) if isinstance(v, np.ndarray) else v) for k, v in inputs.items()}
+    out, last = arm().selective_scan(**t, return_last_state=True)
+    assert out.device.type == "cpu"
+    gate(out.numpy(), last.numpy(), out64, last64, floor)
+
+
+def test_mixed_host_device_rejected():
+    import ctypes
+    from armhackathon_b200 import _ffi
+    x = torch.zeros(1, 1, 4, device="cuda")
+    h = torch.zeros(1, 1, 4)
+    dims = _ffi.ArmScanDims(1, 1, 4, 1, 1)
+    lib = _ffi.load()
+    rc = lib.arm_scan_selective_scan_f32(ctypes.byref(dims), x.data_ptr(), h.data_ptr(),
+                                         x.data_ptr(), x.data_ptr(), x.data_ptr(), None, None,
+                                         None, 1, 0, 0, 0, x.data_ptr(), None, None)
+    assert rc == 2

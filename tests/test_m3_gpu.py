@@ -1,0 +1,153 @@
+"""Mamba-3 parity on the GPU: CUDA kernels through the C ABI against the
+official-kernel captures (<= 8 / 12 bf16 ULPs at tensor scale, the reference's
+gates in tests/verify_golden_mamba3.py and verify_golden_mamba3_mimo.py), the
+reference's f64 oracle outputs stored in the fixtures (fp32 inputs: relative
+error <= 1e-4), and the CPU oracle for reverse traversal, final states, pairs,
+non-causal and 2D compositions."""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+IDX = json.loads((GOLDEN / "index.json").read_text())
+REL_TOL = 1e-4
+
+
+def arm():
+    import armhackathon_b200 as a
+    return a
+
+
+def rel_err(got, want):
+    want = np.asarray(want, np.float64)
+    return float(np.abs(np.asarray(got, np.float64) - want).max()
+                 / max(np.abs(want).max(), 1e-30))
+
+
+def load(family, name):
+    d = np.load(GOLDEN / family / f"{name}.npz")
+    kw = {k[3:]: torch.from_numpy(d[k]).cuda() for k in d.files if k.startswith("kw_")}
+    return kw, d
+
+
+def siso(kw, reverse=False, state=False):
+    return arm().mamba3_scan(kw["Q"], kw["K"], kw["V"], kw["ADT"], kw["DT"], kw["Trap"],
+                             kw["Q_bias"], kw["K_bias"], angles=kw["Angles"], D=kw["D"],
+                             z=kw["Z"], reverse=reverse, return_last_state=state)
+
+
+@pytest.mark.parametrize("name", IDX["m3_siso"])
+def test_siso_golden(name):
+    kw, d = load("m3_siso", name)
+    out, st = siso(kw, state=True)
+    rev, rst = siso(kw, reverse=True, state=True)
+    out, rev = out.cpu().numpy(), rev.cpu().numpy()
+    assert oracle.bf16_ulps_at_scale(out, d["out"]) <= 8.0
+    assert rel_err(out, d["ref_f64"]) <= REL_TOL
+    assert rel_err(rev, d["ref_rev_f64"]) <= REL_TOL
+    if "ref_state_f64" in d.files:
+        assert rel_err(st.cpu().numpy(), d["ref_state_f64"]) <= REL_TOL
+        assert rel_err(rst.cpu().numpy(), d["ref_rev_state_f64"]) <= REL_TOL
+
+
+@pytest.mark.parametrize("name", IDX["m3_mimo"])
+def test_mimo_golden(name):
+    kw, d = load("m3_mimo", name)
+    out = arm().mamba3_mimo_scan(kw["Q"], kw["K"], kw["V"], kw["ADT"], kw["DT"], kw["Trap"],
+                                 kw["Q_bias"], kw["K_bias"], kw["MIMO_V"], kw["MIMO_Z"],
+                                 kw["MIMO_Out"], angles=kw["Angles"], D=kw["D"], z=kw["Z"])
+    out = out.cpu().numpy()
+    assert oracle.bf16_ulps_at_scale(out, d["out"]) <= 12.0
+    assert rel_err(out, d["ref_f64"]) <= REL_TOL
+
+
+def random_siso(b, l, h, dv, dqk, r, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    f = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    dt = torch.nn.functional.softplus(f(b, h, l) - 4)
+    A = -torch.exp(torch.rand(h, generator=g) * np.log(16))
+    return dict(q=f(b, l, 1, dqk) / dqk ** 0.5, k=f(b, l, 1, dqk) / dqk ** 0.5, v=f(b, l, h, dv),
+                adt=A.view(1, h, 1) * dt, dt=dt, trap=f(b, h, l), q_bias=0.1 * f(h, dqk),
+                k_bias=0.1 * f(h, dqk), angles=f(b, l, h, r), D=1 + 0.1 * f(h), z=f(b, l, h, dv))
+
+
+@pytest.mark.parametrize("shape", [(2, 300, 3, 64, 128, 64), (1, 1, 2, 32, 64, 16),
+                                   (3, 129, 5, 48, 32, 8), (1, 257, 4, 64, 64, 32)])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_siso_random_vs_oracle(shape, reverse):
+    b, l, h, dv, dqk, r = shape
+    x = random_siso(b, l, h, dv, dqk, r, seed=l)
+    cos, sin = oracle.angles_to_cos_sin(x["angles"].numpy(), x["dt"].numpy(), dqk // 2)
+    want, wst, wbx = oracle.m3_siso(x["q"], x["k"], x["v"], x["adt"], x["dt"], x["trap"],
+                                    x["q_bias"], x["k_bias"], cos, sin, D=x["D"], z=x["z"],
+                                    reverse=reverse, want_state=True, nthreads=8)
+    xc = {k: v.cuda() for k, v in x.items()}
+    out, st = arm().mamba3_scan(**xc, reverse=reverse, return_last_state=True)
+    assert rel_err(out.cpu().numpy(), want) <= REL_TOL
+    assert rel_err(st.cpu().numpy(), wst) <= REL_TOL
+
+
+def test_pair_and_noncausal():
+    x = {k: v.cuda() for k, v in random_siso(2, 96, 3, 32, 64, 32, seed=11).items()}
+    a = arm()
+    fwd, bwd = a.mamba3_scan_pair(**x)
+    assert torch.allclose(fwd, a.mamba3_scan(**x), atol=0, rtol=0)
+    assert torch.allclose(bwd, a.mamba3_scan(**x, reverse=True), atol=0, rtol=0)
+    nc = a.noncausal_scan(**x)
+    dense = a.noncausal_scan_dense(**{k: v.double() for k, v in x.items()})
+    assert rel_err(nc.cpu().numpy(), dense.cpu().numpy()) <= REL_TOL
+    causal = a.noncausal_scan_dense(**{k: v.double() for k, v in x.items()}, causal=True)
+    assert rel_err(fwd.cpu().numpy(), causal.cpu().numpy()) <= REL_TOL
+
+
+def test_ss2d_mamba3_directions_vs_oracle():
+    g = torch.Generator().manual_seed(4)
+    b, H, W, h, dv, dqk, r = 2, 6, 9, 2, 32, 64, 16
+    f = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    dt = torch.nn.functional.softplus(f(b, h, H, W) - 4)
+    x = dict(q=f(b, H, W, 1, dqk) / 8, k=f(b, H, W, 1, dqk) / 8, v=f(b, H, W, h, dv),
+             adt=-dt * 2.0, dt=dt, trap=f(b, h, H, W), q_bias=0.1 * f(h, dqk),
+             k_bias=0.1 * f(h, dqk), angles=f(b, H, W, h, r), D=torch.ones(h), z=f(b, H, W, h, dv))
+    a = arm()
+    planes = a.ss2d_scan_mamba3(**{k: v.cuda() for k, v in x.items()}, merge="none")
+    from armhackathon_b200.ss2d import grid_to_views
+    from armhackathon_b200.ss2d_mamba3 import grid_to_views_time_major, views_to_grid_time_major
+    tv = {k: grid_to_views_time_major(x[k]) for k in ("q", "k", "v", "angles", "z")}
+    hv = {k: grid_to_views(x[k]) for k in ("adt", "dt", "trap")}
+    cos, sin = oracle.angles_to_cos_sin(tv["angles"].numpy(), hv["dt"].numpy(), dqk // 2)
+    outs = [oracle.m3_siso(tv["q"], tv["k"], tv["v"], hv["adt"], hv["dt"], hv["trap"],
+                           x["q_bias"], x["k_bias"], cos, sin, D=x["D"], z=tv["z"], reverse=rv)
+            for rv in (False, True)]
+    rf, cf = views_to_grid_time_major(torch.from_numpy(outs[0][:b]), torch.from_numpy(outs[0][b:]), H, W)
+    rb, cb = views_to_grid_time_major(torch.from_numpy(outs[1][:b]), torch.from_numpy(outs[1][b:]), H, W)
+    for got, want in zip(planes, (rf, rb, cf, cb)):
+        assert rel_err(got.cpu().numpy(), want.numpy()) <= REL_TOL
+    nc_rows, nc_cols = a.ss2d_noncausal_mamba3(**{k: v.cuda() for k, v in x.items()}, merge="none")
+    assert nc_rows.shape == (b, H, W, h, dv) and nc_cols.shape == (b, H, W, h, dv)
+
+
+def test_mimo_random_state_and_reverse():
+    g = torch.Generator().manual_seed(9)
+    b, l, h, dv, dqk, R = 2, 70, 3, 32, 64, 4
+    f = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    dt = torch.nn.functional.softplus(f(b, h, l) - 4)
+    x = dict(q=f(b, l, R, dqk) / 8, k=f(b, l, R, dqk) / 8, v=f(b, l, h, dv), adt=-dt, dt=dt,
+             trap=f(b, h, l), q_bias=0.1 * f(h, R, dqk), k_bias=0.1 * f(h, R, dqk),
+             psi=f(h, R, dv), zeta=f(h, R, dv), phi=f(h, R, dv), angles=f(b, l, h, dqk // 4),
+             D=torch.ones(h), z=f(b, l, h, dv))
+    cos, sin = oracle.angles_to_cos_sin(x["angles"].numpy(), x["dt"].numpy(), dqk // 2)
+    for rv in (False, True):
+        want, wst = oracle.m3_mimo(x["q"], x["k"], x["v"], x["adt"], x["dt"], x["trap"],
+                                   x["q_bias"], x["k_bias"], cos, sin, x["psi"], x["zeta"],
+                                   x["phi"], D=x["D"], z=x["z"], reverse=rv, want_state=True)
+        out, st = arm().mamba3_mimo_scan(**{k: v.cuda() for k, v in x.items()}, reverse=rv,
+                                         return_last_state=True)
+        assert rel_err(out.cpu().numpy(), want) <= REL_TOL
+        assert rel_err(st.cpu().numpy(), wst) <= REL_TOL
