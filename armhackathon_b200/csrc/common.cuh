@@ -37,26 +37,73 @@ __device__ __forceinline__ float sigmoid_f(float x) {
     return e / (1.f + e);
 }
 
+__device__ __forceinline__ float lg2_approx(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Fast softplus for the hot kernels (same threshold contract as softplus_f).
+// y = e^x by ex2.approx (relative error ~2^-22); softplus = log1p(y):
+//   y < 0.1  : the alternating series y - y^2/2 + y^3/3 - y^4/4 + y^5/5,
+//              truncation error < y^6/6 <= 1.7e-7 of the result;
+//   y >= 0.1 : ln2 * lg2.approx(1 + y), absolute error ~2^-22 on a result
+//              >= 0.095, i.e. relative error < 3e-6.
+__device__ __forceinline__ float softplus_fast(float x) {
+    if (x > 20.f) return x;
+    const float y = ex2_approx(x * kLog2e);
+    float ser = fmaf(y, 0.2f, -0.25f);
+    ser = fmaf(y, ser, 1.f / 3.f);
+    ser = fmaf(y, ser, -0.5f);
+    ser = fmaf(y, ser, 1.f);
+    ser *= y;
+    const float lg = lg2_approx(1.f + y) * 0.6931471805599453f;
+    return y < 0.1f ? ser : lg;
+}
+
+// Fast silu: x * 1/(1 + e^-x) with ex2.approx and rcp.approx (each ~1 ulp);
+// for x < -87 the exponential overflows to +inf and the result is -0, the
+// correctly rounded limit.
+__device__ __forceinline__ float silu_fast(float x) {
+    return x * rcp_approx(1.f + ex2_approx(-x * kLog2e));
+}
+
 // Packed fp32x2 arithmetic (PTX ISA 8.6, sm_100a): one instruction computes
 // two independent IEEE fp32 results with round-to-nearest, identical to two
 // scalar FFMA/FMUL.  Halves the FMA-pipe issue count of the scan's inner loop.
-__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
-    return (static_cast<unsigned long long>(__float_as_uint(v.y)) << 32) |
-           __float_as_uint(v.x);
-}
-__device__ __forceinline__ float2 f2_from(unsigned long long r) {
-    return make_float2(__uint_as_float(static_cast<unsigned>(r)),
-                       __uint_as_float(static_cast<unsigned>(r >> 32)));
-}
+// Operands are packed into 64-bit register pairs inside the asm (mov.b64
+// {lo, hi}), which ptxas resolves by register allocation, not arithmetic.
+#ifdef B200SCAN_SCALAR_PAIRS
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-    unsigned long long r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
-    return f2_from(r);
+    return make_float2(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y));
 }
 __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
-    unsigned long long r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-    return f2_from(r);
+    return make_float2(a.x * b.x, a.y * b.y);
 }
+#else
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 r;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(r.x), "=f"(r.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return r;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    float2 r;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(r.x), "=f"(r.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+#endif
 
 }  // namespace b200scan

@@ -25,6 +25,9 @@
 // time axis (each thread touches whole 32-byte sectors); B and C rows are
 // shared by all rows of a batch and stay L2-resident.  Rows of a CTA may span
 // two batches or two B/C groups: every thread resolves its own B/C row.
+#include <cstdint>
+#include <cstdlib>
+
 #include "common.cuh"
 #include "m1_scan.h"
 
@@ -332,6 +335,19 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
         m1_sequential_kernel<<<grid, 32 * warps_per_block, 0, stream>>>(p);
         return cudaGetLastError();
     }
+    // d_state <= 16 (every Mamba-1 model): the pipelined row-tile kernel,
+    // the fastest measured for both short-wide and batched problems.
+    // B200SCAN_M1_VARIANT overrides for tuning sweeps: 1-4 tile shapes,
+    // 5/6/7 row-sequential with 4/2/1 lanes per row, 0 the block-chunked
+    // kernel (also the path for d_state > 16).
+    int variant = -1;
+    if (const char* v = getenv("B200SCAN_M1_VARIANT")) variant = atoi(v);
+    const int64_t rows = p.batch * p.dim;
+    (void)rows;
+    if ((variant == 5 || variant == 6 || variant == 7) && m1_rowseq_applicable(p))
+        return m1_rowseq_launch(p, variant == 6 ? 2 : variant == 7 ? 1 : 4, stream);
+    const bool tile_ok = p.state <= 16 && p.len <= (INT32_MAX / 4) && p.state * p.len <= INT32_MAX;
+    if (tile_ok && variant != 0) return m1_tile_launch(p, variant < 1 || variant > 4 ? 1 : variant, stream);
     switch (m1_pick_channels_per_cta(p.batch * p.dim)) {
         case 32: return launch_chunked<32, 16>(p, stream);
         case 16: return launch_chunked<16, 16>(p, stream);

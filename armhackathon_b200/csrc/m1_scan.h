@@ -31,6 +31,11 @@ struct M1Params {
 bool m1_pointers_aligned16(const M1Params& p);
 int m1_pick_channels_per_cta(int64_t rows);
 cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream);
+// Pipelined row-tile kernel (m1_tile.cu); requires state <= 16.
+cudaError_t m1_tile_launch(const M1Params& p, int variant, cudaStream_t stream);
+// Row-sequential kernel (m1_rowseq.cu) and its applicability test.
+bool m1_rowseq_applicable(const M1Params& p);
+cudaError_t m1_rowseq_launch(const M1Params& p, int lanes_per_row, cudaStream_t stream);
 // Forward and reverse scans of the same inputs (fused bidirectional entry).
 cudaError_t m1_bidir_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                             cudaStream_t stream);

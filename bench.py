@@ -89,11 +89,15 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        import tempfile
+        self.path = tempfile.mktemp(suffix=".csv")
         try:
+            # -f: nvidia-smi writes (and flushes) each sample to the file
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "--format=csv,noheader,nounits", "-lms", "100", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
         except OSError:
             self.proc = None
         return self
@@ -101,13 +105,18 @@ class ClockSampler:
     def __exit__(self, *exc):
         self.lines = []
         if self.proc is not None:
+            time.sleep(0.25)
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            try:
+                with open(self.path) as f:
+                    self.lines = [ln for ln in f.read().splitlines() if ln.strip()]
+                os.unlink(self.path)
+            except OSError:
+                pass
 
     def summary(self):
         sm, mx, reasons = [], None, set()

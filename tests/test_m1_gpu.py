@@ -199,3 +199,20 @@ def test_mixed_host_device_rejected():
                                          x.data_ptr(), x.data_ptr(), x.data_ptr(), None, None,
                                          None, 1, 0, 0, 0, x.data_ptr(), None, None)
     assert rc == 2
+
+
+@pytest.mark.parametrize("variant", ["0", "1", "2", "3", "4", "5", "6", "7"])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_every_kernel_variant_vs_oracle(variant, reverse, monkeypatch):
+    """Each Mamba-1 kernel shape the library can dispatch to (selected with
+    B200SCAN_M1_VARIANT, read at every launch) against the oracle, on a
+    grouped, h0-seeded case with a ragged row count."""
+    monkeypatch.setenv("B200SCAN_M1_VARIANT", variant)
+    inputs = random_case(3, 40, 1028, 16, 2, seed=7)
+    rng = np.random.default_rng(1)
+    h0 = rng.standard_normal((3, 40, 16)).astype(np.float32)
+    want, want_last = oracle.m1_scan(**inputs, reverse=reverse, h0=h0, nthreads=8)
+    out, last = arm().selective_scan(**cuda(inputs), reverse=reverse, return_last_state=True,
+                                     initial_state=torch.from_numpy(h0).cuda())
+    assert rel_err(out.cpu().numpy(), want) <= REL_TOL
+    assert rel_err(last.cpu().numpy(), want_last) <= REL_TOL
