@@ -1,7 +1,7 @@
 """Benchmark of the selective-scan hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload prefill_scan|cfg0]
+                    [--workload prefill_scan|cfg0|cfg2|cfg3|cfg4a|cfg4b]
 
 A step is one Mamba-1 ``selective_scan`` call over one batch of synthetic
 input (fp32, seed 0).  Default workload ``prefill_scan``: the per-layer scan
@@ -49,6 +49,100 @@ WORKLOADS = {
     "cfg0": dict(batch=1, dim=1536, len=2048, state=16, flush=True,
                  desc="BASELINE config 0: Mamba-1 selective_scan B1 D1536 L2048 N16 fp32"),
 }
+
+
+M3_WORKLOADS = {
+    "cfg2": dict(kind="siso", batch=4, heads=24, dv=64, dqk=128, len=4096, rank=1, pairs=64,
+                 desc="BASELINE config 2: Mamba-3 SISO B4 H24 P64 N128 L4096 (fp32 on the C "
+                      "ABI; the config's bf16 inputs are exactly representable)"),
+    "cfg3": dict(kind="mimo", batch=8, heads=24, dv=64, dqk=128, len=8192, rank=4, pairs=64,
+                 desc="BASELINE config 3 shape: Mamba-3 MIMO r4 B8 H24 P64 N128 L8192 through the "
+                      "reference op formulation (psi/zeta/phi projections)"),
+    "cfg4a": dict(kind="ss2d", batch=8, heads=6, dv=64, dqk=64, len=128 * 128, rank=1, pairs=32,
+                  grid=128, desc="BASELINE config 4a: SS2D Mamba-3 SISO 128x128 grid B8 H6 P64 "
+                                 "N64 fp32, 4 directions summed"),
+    "cfg4b": dict(kind="bidir", batch=1, dim=1536, len=262144, state=16,
+                  desc="BASELINE config 4b: Mamba-1 bidirectional D1536 N16 L262144 fp32, summed"),
+}
+
+
+def m3_inputs(w, device, seed=0):
+    """Synthetic Mamba-3 inputs with BASELINE config 2's distributions."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, H, P, N, L, R = w["batch"], w["heads"], w["dv"], w["dqk"], w["len"], w["rank"]
+    rn = lambda *s: torch.randn(*s, generator=g, device=device)  # noqa: E731
+    dt = torch.nn.functional.softplus(rn(B, H, L) - 4)
+    A = -torch.exp(torch.rand(H, generator=g, device=device) * np.log(16))
+    # per-step rotation tanh(angle) * pi ~ U[0, pi): angle = atanh(U[0, 1))
+    ang = torch.atanh(torch.rand(B, L, H, w["pairs"], generator=g, device=device) * 0.999)
+    x = dict(v=rn(B, L, H, P), adt=A.view(1, H, 1) * dt, dt=dt, trap=rn(B, H, L),
+             D=1 + 0.1 * rn(H), angles=ang)
+    if w["kind"] == "mimo":
+        x.update(q=rn(B, L, R, N) / np.sqrt(N * R), k=rn(B, L, R, N) / np.sqrt(N * R),
+                 q_bias=torch.zeros(H, R, N, device=device),
+                 k_bias=torch.zeros(H, R, N, device=device),
+                 psi=rn(H, R, P), zeta=rn(H, R, P), phi=rn(H, R, P), z=rn(B, L, H, P))
+    else:
+        x.update(q=rn(B, L, 1, N) / np.sqrt(N), k=rn(B, L, 1, N) / np.sqrt(N),
+                 q_bias=torch.zeros(H, N, device=device), k_bias=torch.zeros(H, N, device=device))
+    return x
+
+
+def m3_bytes(w):
+    B, H, P, N, L, R = w["batch"], w["heads"], w["dv"], w["dqk"], w["len"], w["rank"]
+    # q, k, v, y, dt/adt/trap, angles (+ final state for SISO, z for MIMO)
+    b = 2 * B * L * R * N + 2 * B * L * H * P + 3 * B * H * L + B * L * H * w["pairs"]
+    if w["kind"] == "mimo":
+        b += B * L * H * P
+    if w["kind"] == "siso":
+        b += B * H * P * N
+    return 4 * b
+
+
+def run_m3(args, w):
+    """Time a Mamba-3 or bidirectional workload (recorded for the configs;
+    the headline line is the Mamba-1 prefill scan)."""
+    import torch
+    import armhackathon_b200 as arm
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if w["kind"] == "bidir":
+        x = make_inputs(dict(batch=1, dim=w["dim"], len=w["len"], state=w["state"]), dev)
+        step = lambda: arm.bidirectional_scan(  # noqa: E731
+            x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"], z=x["z"],
+            delta_bias=x["delta_bias"], delta_softplus=True, merge="sum")
+        nbytes = 4 * (4 * w["dim"] * w["len"] + 2 * w["state"] * w["len"])
+    else:
+        x = m3_inputs(w, dev)
+        nbytes = m3_bytes(w)
+        if w["kind"] == "mimo":
+            step = lambda: arm.mamba3_mimo_scan(**x)  # noqa: E731
+        elif w["kind"] == "siso":
+            step = lambda: arm.mamba3_scan(**x, return_last_state=True)  # noqa: E731
+        else:
+            B, H, g = w["batch"], w["heads"], w["grid"]
+            grid = lambda t: t.reshape(B, g, g, *t.shape[2:])  # noqa: E731
+            hm = lambda t: t.reshape(B, H, g, g)  # noqa: E731
+            xs = dict(q=grid(x["q"]), k=grid(x["k"]), v=grid(x["v"]), angles=grid(x["angles"]),
+                      adt=hm(x["adt"]), dt=hm(x["dt"]), trap=hm(x["trap"]),
+                      q_bias=x["q_bias"], k_bias=x["k_bias"], D=x["D"])
+            step = lambda: arm.ss2d_scan_mamba3(**xs)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    print(json.dumps({"metric": METRIC, "workload": args.workload, "desc": w["desc"],
+                      "ms_per_step": ms, "value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+                      "bytes_per_step": nbytes,
+                      "note": "whole op incl. the torch angle pre-pass and output permute"}),
+          flush=True)
 
 
 def peaks():
@@ -211,11 +305,20 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="prefill_scan", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="prefill_scan",
+                    choices=sorted(WORKLOADS) + sorted(M3_WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload in M3_WORKLOADS:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "workload": args.workload,
+                              "unavailable": "reference arm is implemented for the Mamba-1 "
+                                             "workloads only"}))
+            return
+        run_m3(args, M3_WORKLOADS[args.workload])
+        return
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, w)
