@@ -1,0 +1,350 @@
+// Mamba-3 SISO / MIMO scan in chunked (dual) form, fp32 on CUDA cores.
+//
+// One CTA per (batch, head) walks the sequence in chunks of QR = 64 rows,
+// where a row is a (step, rank) pair: 64 steps for SISO, 64/R steps of R
+// ranks for MIMO (R in {1, 2, 4}).  With l_t the within-chunk inclusive
+// cumulative sum of adt (traversal order), w_s = exp(l_last - l_s) * scale_s,
+// and S the (dv x dqk) state entering the chunk, the recurrence of
+// mamba3/scalar.rs:50-196 and mimo.rs:98-284 unrolls to
+//
+//   W[i][j] = (q_i . k_j) * ( exp(l_ti - l_tj) * scale_tj   if t_j < t_i
+//                             gamma_ti                      if t_j = t_i
+//                             0                             otherwise )
+//   Y[i]    = sum_j W[i][j] x_j  +  exp(l_ti) * (q_i . S^T)  +  D * x_i
+//   S      <- exp(l_last) * S  +  sum_j w_tj * x_j (x) k_j
+//
+// (alpha_t * exp(l_{t-1}) = exp(l_t) folds the per-step decay of the
+// sequential form into the chunk's cumulative decay; the diagonal of W is
+// the trapezoid's current-step term gamma_t (q.k) x, including MIMO's
+// rank-by-rank Gram).  SISO output is Y * silu(z); MIMO output sums the R
+// rows of a step: sum_r phi_r * silu(z * zeta_r) * Y[(t, r)].
+//
+// Shared memory holds q^T, k^T (dqk-major, for the Gram and q.S^T), w*k
+// row-major (for the state update; its last valid row is scale_T * k_T, the
+// SISO last_bx), x row-major, W^T and S^T (dqk-major).  Every product is a
+// register-tiled loop with 16-byte shared loads; four barriers per chunk.
+// Requires dv % 4 == 0, dqk % 8 == 0, dv <= 128, dqk <= 128.
+#include <cstdint>
+
+#include "common.cuh"
+#include "m3_scan.h"
+
+namespace b200scan {
+
+namespace {
+
+constexpr int kCkThreads = 256;
+constexpr int kQR = 64;  // rows (step, rank) per chunk
+
+struct CkLayout {
+    int N, P, NP4, PP4, QP4;  // dims and padded strides
+    int qT, kT, kw, x, WT, ST, gate;  // float offsets
+    int total;
+    __host__ __device__ CkLayout(int dqk, int dv) {
+        N = dqk;
+        P = dv;
+        QP4 = kQR + 4;
+        NP4 = N + 4;
+        PP4 = P + 4;
+        qT = 0;
+        kT = qT + N * QP4;
+        kw = kT + N * QP4;
+        x = kw + kQR * NP4;
+        WT = x + kQR * PP4;
+        ST = WT + kQR * QP4;
+        gate = ST + N * PP4;
+        total = gate + 4 * kQR + 8;  // lcum, scale, gamma, w  + eQ
+    }
+};
+
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+template <int R>
+__global__ void __launch_bounds__(kCkThreads, 1) m3_chunk_kernel(M3Params p) {
+    constexpr int QS = kQR / R;  // steps per chunk
+    extern __shared__ float4 smem4[];
+    float* sm = reinterpret_cast<float*>(smem4);
+    const CkLayout ly(static_cast<int>(p.dqk), static_cast<int>(p.dv));
+    const int N = ly.N, P = ly.P, half = N / 2;
+    float* qT = sm + ly.qT;
+    float* kT = sm + ly.kT;
+    float* kw = sm + ly.kw;
+    float* xs = sm + ly.x;
+    float* WT = sm + ly.WT;
+    float* ST = sm + ly.ST;
+    float* lcum = sm + ly.gate;
+    float* scl = lcum + kQR;
+    float* gam = scl + kQR;
+    float* wdec = gam + kQR;
+    float* eQ = wdec + kQR;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t bh = blockIdx.x;
+    const int64_t H = p.heads, L = p.len;
+    const int64_t bi = bh / H, h = bh % H;
+    const bool mimo = R > 1 || p.psi != nullptr;
+    const float dsk = p.d_skip ? p.d_skip[h] : 0.f;
+    const int64_t gate_base = (bi * H + h) * L;
+    const int n_chunks = static_cast<int>((L + QS - 1) / QS);
+
+    for (int i = tid; i < N * ly.PP4; i += kCkThreads) ST[i] = 0.f;
+
+    for (int ch = 0; ch < n_chunks; ++ch) {
+        const int64_t it0 = static_cast<int64_t>(ch) * QS;  // first traversal index
+        // ---- A1. gates of the chunk's steps (warp 0), cumulative log-decay
+        if (warp == 0) {
+            float lv[2], sc[2], gm[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int j = lane + 32 * e;
+                const int64_t it = it0 + j;
+                lv[e] = 0.f;
+                sc[e] = 0.f;
+                gm[e] = 0.f;
+                if (j < QS && it < L) {
+                    const int64_t t = p.reverse ? L - 1 - it : it;
+                    const int64_t g = gate_base + t;
+                    const float gamma = p.dt[g] * sigmoid_f(p.trap[g]);
+                    float shifted = 0.f;
+                    if (it + 1 < L) {
+                        const int64_t nx = p.reverse ? g - 1 : g + 1;
+                        shifted = p.dt[nx] * (1.f - sigmoid_f(p.trap[nx]));
+                    }
+                    lv[e] = p.adt[g];
+                    sc[e] = gamma + shifted;
+                    gm[e] = gamma;
+                }
+            }
+            // inclusive prefix sum over the 64 slots (lane, lane + 32)
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float v = __shfl_up_sync(0xffffffffu, lv[e], o);
+                    if (lane >= o) lv[e] += v;
+                }
+            lv[1] += __shfl_sync(0xffffffffu, lv[0], 31);
+            const float last = QS > 32 ? __shfl_sync(0xffffffffu, lv[1], 31)
+                                       : __shfl_sync(0xffffffffu, lv[0], QS - 1);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int j = lane + 32 * e;
+                if (j < QS) {
+                    lcum[j] = lv[e];
+                    scl[j] = sc[e];
+                    gam[j] = gm[e];
+                    wdec[j] = expf(last - lv[e]) * sc[e];
+                }
+            }
+            if (lane == 0) eQ[0] = expf(last);
+        }
+        __syncthreads();
+        // ---- A2. rotated q, k (q^T, k^T, w*k rows) and x rows
+        for (int idx = tid; idx < kQR * half; idx += kCkThreads) {
+            const int i = idx / half, pi = idx - (idx / half) * half;
+            const int j = i / R, r = i - (i / R) * R;  // step, rank
+            const int64_t it = it0 + j;
+            float q0 = 0.f, q1 = 0.f, k0 = 0.f, k1 = 0.f;
+            const int i0 = mimo ? pi : 2 * pi, i1 = mimo ? pi + half : 2 * pi + 1;
+            if (j < QS && it < L) {
+                const int64_t t = p.reverse ? L - 1 - it : it;
+                const int64_t qk_off = (bi * L + t) * (mimo ? R : 1) * N + r * N;
+                const float* qb = p.q_bias + (h * (mimo ? R : 1) + r) * N;
+                const float* kb = p.k_bias + (h * (mimo ? R : 1) + r) * N;
+                const int64_t cs = ((bi * L + t) * H + h) * half + pi;
+                const float c = p.cos[cs], s = p.sin[cs];
+                float a0 = p.q[qk_off + i0] + qb[i0], a1 = p.q[qk_off + i1] + qb[i1];
+                q0 = a0 * c - a1 * s;
+                q1 = a0 * s + a1 * c;
+                a0 = p.k[qk_off + i0] + kb[i0];
+                a1 = p.k[qk_off + i1] + kb[i1];
+                k0 = a0 * c - a1 * s;
+                k1 = a0 * s + a1 * c;
+            }
+            qT[i0 * ly.QP4 + i] = q0;
+            qT[i1 * ly.QP4 + i] = q1;
+            kT[i0 * ly.QP4 + i] = k0;
+            kT[i1 * ly.QP4 + i] = k1;
+            const float w = j < QS ? wdec[j] : 0.f;
+            kw[i * ly.NP4 + i0] = w * k0;
+            kw[i * ly.NP4 + i1] = w * k1;
+        }
+        for (int idx = tid; idx < kQR * P; idx += kCkThreads) {
+            const int i = idx / P, pp = idx - (idx / P) * P;
+            const int j = i / R, r = i - (i / R) * R;
+            const int64_t it = it0 + j;
+            float v = 0.f;
+            if (j < QS && it < L) {
+                const int64_t t = p.reverse ? L - 1 - it : it;
+                v = p.v[((bi * L + t) * H + h) * P + pp];
+                if (mimo) v *= p.psi[(h * R + r) * P + pp];
+            }
+            xs[i * ly.PP4 + pp] = v;
+        }
+        __syncthreads();
+        // ---- B. W^T[j][i] = mask(t_i, t_j) * (q_i . k_j); 4x4 tiles
+        {
+            const int ti = tid / 16, tj = tid % 16;  // 16 x 16 tiles of 4 x 4
+            const int i0 = ti * 4, j0 = tj * 4;
+            float acc[4][4] = {};
+            if (j0 / R <= (i0 + 3) / R) {
+                for (int n = 0; n < N; ++n) {
+                    const float4 a = ld4(qT + n * ly.QP4 + i0);
+                    const float4 b = ld4(kT + n * ly.QP4 + j0);
+                    const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(av[u], bv[v], acc[u][v]);
+                }
+            }
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                float out[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int si = (i0 + u) / R, sj = (j0 + v) / R;
+                    float m = 0.f;
+                    if (sj < si) m = expf(lcum[si] - lcum[sj]) * scl[sj];
+                    else if (sj == si) m = gam[si];
+                    out[u] = (si < QS) ? m * acc[u][v] : 0.f;
+                }
+                *reinterpret_cast<float4*>(WT + (j0 + v) * ly.QP4 + i0) =
+                    make_float4(out[0], out[1], out[2], out[3]);
+            }
+        }
+        __syncthreads();
+        // ---- C. Y = W x + exp(l) q S^T + D x; gate and store
+        for (int tile = tid; tile < (kQR / 4) * (P / 4); tile += kCkThreads) {
+            const int i0 = (tile / (P / 4)) * 4, p0 = (tile % (P / 4)) * 4;
+            float acc[4][4] = {}, inter[4][4] = {};
+            for (int j = 0; j < kQR; ++j) {
+                const float4 a = ld4(WT + j * ly.QP4 + i0);
+                const float4 b = ld4(xs + j * ly.PP4 + p0);
+                const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(av[u], bv[v], acc[u][v]);
+            }
+            if (ch > 0) {
+                for (int n = 0; n < N; ++n) {
+                    const float4 a = ld4(qT + n * ly.QP4 + i0);
+                    const float4 b = ld4(ST + n * ly.PP4 + p0);
+                    const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) inter[u][v] = fmaf(av[u], bv[v], inter[u][v]);
+                }
+            }
+            float y[4][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int si = (i0 + u) / R;
+                const float el = si < QS ? expf(lcum[si]) : 0.f;
+                const float4 xv = ld4(xs + (i0 + u) * ly.PP4 + p0);
+                const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int v = 0; v < 4; ++v) y[u][v] = acc[u][v] + el * inter[u][v] + dsk * xa[v];
+            }
+            // rows i0..i0+3 are steps i0/R .. (i0+3)/R; reduce ranks per step
+#pragma unroll
+            for (int u0 = 0; u0 < 4; u0 += R) {
+                const int step = (i0 + u0) / R;
+                const int64_t it = it0 + step;
+                if (step >= QS || it >= L) continue;
+                const int64_t t = p.reverse ? L - 1 - it : it;
+                const int64_t voff = ((bi * L + t) * H + h) * P + p0;
+                float o[4] = {0.f, 0.f, 0.f, 0.f};
+                float zv[4] = {0.f, 0.f, 0.f, 0.f};
+                if (p.z) {
+                    const float4 z4 = *reinterpret_cast<const float4*>(p.z + voff);
+                    zv[0] = z4.x; zv[1] = z4.y; zv[2] = z4.z; zv[3] = z4.w;
+                }
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        const float yy = y[u0 + r][v];
+                        if (mimo) {
+                            const int64_t po = (h * R + r) * P + p0 + v;
+                            const float g = p.z ? silu_f(zv[v] * p.zeta[po]) : 1.f;
+                            o[v] += p.phi[po] * g * yy;
+                        } else {
+                            o[v] = p.z ? yy * silu_f(zv[v]) : yy;
+                        }
+                    }
+                }
+                *reinterpret_cast<float4*>(p.out + ((bi * H + h) * L + t) * P + p0) =
+                    make_float4(o[0], o[1], o[2], o[3]);
+            }
+        }
+        __syncthreads();
+        // ---- D. S^T[n][p] = eQ * S^T + sum_j kw[j][n] x[j][p]; 8(n) x 4(p) tiles
+        {
+            const float e = eQ[0];
+            for (int tile = tid; tile < (N / 8) * (P / 4); tile += kCkThreads) {
+                const int n0 = (tile / (P / 4)) * 8, p0 = (tile % (P / 4)) * 4;
+                float acc[8][4] = {};
+                for (int j = 0; j < kQR; ++j) {
+                    const float4 k0 = ld4(kw + j * ly.NP4 + n0);
+                    const float4 k1 = ld4(kw + j * ly.NP4 + n0 + 4);
+                    const float4 b = ld4(xs + j * ly.PP4 + p0);
+                    const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+                    const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(kv[u], bv[v], acc[u][v]);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    float* s = ST + (n0 + u) * ly.PP4 + p0;
+                    const float4 old = ld4(s);
+                    *reinterpret_cast<float4*>(s) =
+                        make_float4(fmaf(e, old.x, acc[u][0]), fmaf(e, old.y, acc[u][1]),
+                                    fmaf(e, old.z, acc[u][2]), fmaf(e, old.w, acc[u][3]));
+                }
+            }
+        }
+        // SISO last_bx: scale_T * k_T, the last valid row of w*k in the final chunk
+        if (!mimo && p.last_bx && ch == n_chunks - 1) {
+            const int lastrow = static_cast<int>(L - 1 - it0);
+            for (int n = tid; n < N; n += kCkThreads) p.last_bx[bh * N + n] = kw[lastrow * ly.NP4 + n];
+        }
+        __syncthreads();
+    }
+    if (p.last_state) {
+        for (int idx = tid; idx < P * N; idx += kCkThreads) {
+            const int pp = idx / N, n = idx - (idx / N) * N;
+            p.last_state[(bh * P + pp) * N + n] = ST[n * ly.PP4 + pp];
+        }
+    }
+}
+
+}  // namespace
+
+bool m3_chunk_applicable(const M3Params& p) {
+    const int R = p.psi ? static_cast<int>(p.rank) : 1;
+    if (!(R == 1 || R == 2 || R == 4)) return false;
+    if (p.dv % 4 || p.dqk % 8 || p.dv > 128 || p.dqk > 128) return false;
+    const CkLayout ly(static_cast<int>(p.dqk), static_cast<int>(p.dv));
+    if (static_cast<size_t>(ly.total) * sizeof(float) > 227 * 1024) return false;
+    auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    return al(p.v) && al(p.z) && al(p.out);
+}
+
+cudaError_t m3_chunk_launch(const M3Params& p, cudaStream_t stream) {
+    const int R = p.psi ? static_cast<int>(p.rank) : 1;
+    const CkLayout ly(static_cast<int>(p.dqk), static_cast<int>(p.dv));
+    const size_t smem = static_cast<size_t>(ly.total) * sizeof(float);
+    auto kern = R == 4 ? m3_chunk_kernel<4> : R == 2 ? m3_chunk_kernel<2> : m3_chunk_kernel<1>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    kern<<<dim3(static_cast<unsigned>(p.batch * p.heads)), kCkThreads, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace b200scan

@@ -33,5 +33,8 @@ struct M3Params {
 
 bool m3_shape_supported(int64_t dv, int64_t dqk, int64_t rank);
 cudaError_t m3_scan_launch(const M3Params& p, int backend, cudaStream_t stream);
+// Chunked dual-form kernel (m3_chunk.cu): the default when applicable.
+bool m3_chunk_applicable(const M3Params& p);
+cudaError_t m3_chunk_launch(const M3Params& p, cudaStream_t stream);
 
 }  // namespace b200scan

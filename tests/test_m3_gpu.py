@@ -151,3 +151,33 @@ def test_mimo_random_state_and_reverse():
                                          return_last_state=True)
         assert rel_err(out.cpu().numpy(), want) <= REL_TOL
         assert rel_err(st.cpu().numpy(), wst) <= REL_TOL
+
+
+@pytest.mark.parametrize("mimo", [False, True])
+def test_sequential_backend_matches_oracle(mimo):
+    """backend=1 selects the sequential-in-time kernel (the on-device
+    restatement of the scalar loop); it must agree with the oracle too."""
+    from armhackathon_b200 import _ffi
+    g = torch.Generator().manual_seed(21)
+    b, l, h, dv, dqk, R = 2, 77, 3, 32, 64, (2 if mimo else 1)
+    f = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    dt = torch.nn.functional.softplus(f(b, h, l) - 4)
+    q, k = f(b, l, R, dqk) / 8, f(b, l, R, dqk) / 8
+    v, z, trap = f(b, l, h, dv), f(b, l, h, dv), f(b, h, l)
+    qb, kb = 0.1 * f(h, R, dqk), 0.1 * f(h, R, dqk)
+    proj = [f(h, R, dv) for _ in range(3)] if mimo else [None] * 3
+    cos, sin = oracle.angles_to_cos_sin(f(b, l, h, dqk // 4).numpy(), dt.numpy(), dqk // 2)
+    D = torch.ones(h)
+    if mimo:
+        want = oracle.m3_mimo(q, k, v, -dt, dt, trap, qb, kb, cos, sin, *proj, D=D, z=z)
+    else:
+        want = oracle.m3_siso(q, k, v, -dt, dt, trap, qb[:, 0], kb[:, 0], cos, sin, D=D, z=z)
+    dev = lambda t: None if t is None else t.float().contiguous().cuda()  # noqa: E731
+    ins = [dev(x) for x in (q, k, v, -dt, dt, trap, qb, kb, torch.from_numpy(cos),
+                            torch.from_numpy(sin), D, z, *proj)]
+    out = torch.empty(b, h, l, dv, device="cuda")
+    dims = _ffi.ArmMamba3Dims(b, h, dv, dqk, l, R)
+    _ffi.mamba3_raw(dims, [0 if t is None else t.data_ptr() for t in ins], 0, 1, 0,
+                    out.data_ptr(), 0, 0)
+    got = out.permute(0, 2, 1, 3).cpu().numpy()
+    assert rel_err(got, want) <= REL_TOL
