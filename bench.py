@@ -153,6 +153,18 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def profiled_traffic(workload):
+    """DRAM bytes per launch of the scan kernel from the committed ncu summary
+    (profiles/m1_tile_<workload>.md, line 'traffic_bytes_per_launch: N'), or
+    None when no capture of this workload is committed."""
+    import re
+    f = ROOT / "profiles" / f"m1_tile_{workload}.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", f.read_text())
+    return int(m.group(1)) if m else None
+
+
 def algorithmic_bytes(w):
     B, D, L, N = w["batch"], w["dim"], w["len"], w["state"]
     return 4 * (4 * B * D * L + 2 * B * N * L + D * N + 2 * D + B * D * N)
@@ -432,7 +444,10 @@ def main():
             "elems_per_s": elems / (step_ms * 1e-3),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
-                         "traffic": None, "bytes_per_launch": nbytes,
+                         "traffic": profiled_traffic(args.workload),
+                         "traffic_source": "ncu dram__bytes_read+write, one launch "
+                                           "(profiles/m1_tile_<workload>.md)",
+                         "bytes_per_launch": nbytes,
                          "kernel_ms": k_ms},
             "gpu_launches": launches,
             "e2e": e2e,
