@@ -344,6 +344,7 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
     if (const char* v = getenv("B200SCAN_M1_VARIANT")) variant = atoi(v);
     const int64_t rows = p.batch * p.dim;
     (void)rows;
+    if (variant == 8 && m1_twopass_applicable(p)) return m1_twopass_launch(p, stream);
     if ((variant == 5 || variant == 6 || variant == 7) && m1_rowseq_applicable(p))
         return m1_rowseq_launch(p, variant == 6 ? 2 : variant == 7 ? 1 : 4, stream);
     const bool tile_ok = p.state <= 16 && p.len <= (INT32_MAX / 4) && p.state * p.len <= INT32_MAX;

@@ -36,6 +36,9 @@ cudaError_t m1_tile_launch(const M1Params& p, int variant, cudaStream_t stream);
 // Row-sequential kernel (m1_rowseq.cu) and its applicability test.
 bool m1_rowseq_applicable(const M1Params& p);
 cudaError_t m1_rowseq_launch(const M1Params& p, int lanes_per_row, cudaStream_t stream);
+// Two-pass kernel (m1_twopass.cu) and its applicability test.
+bool m1_twopass_applicable(const M1Params& p);
+cudaError_t m1_twopass_launch(const M1Params& p, cudaStream_t stream);
 // Forward and reverse scans of the same inputs (fused bidirectional entry).
 cudaError_t m1_bidir_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                             cudaStream_t stream);
