@@ -75,6 +75,13 @@ def _bind(lib):
     m3 = [ctypes.POINTER(ArmMamba3Dims), *([_VP] * 15), _I, _I, _I, _VP, _VP, _VP]
     lib.arm_scan_mamba3_scan_f32.argtypes = m3
     lib.arm_scan_mamba3_scan_f32_async.argtypes = m3 + [_VP]
+    lib.arm_scan_mamba3_angles_workspace_bytes.restype = ctypes.c_size_t
+    lib.arm_scan_mamba3_angles_workspace_bytes.argtypes = [ctypes.POINTER(ArmMamba3Dims),
+                                                           ctypes.c_size_t]
+    lib.arm_scan_mamba3_angles_f32_async.restype = ctypes.c_int
+    lib.arm_scan_mamba3_angles_f32_async.argtypes = [
+        ctypes.POINTER(ArmMamba3Dims), _VP, ctypes.c_size_t, _VP, _VP, _VP, _VP,
+        ctypes.c_size_t, _VP]
     for f in ("arm_scan_selective_scan_f32", "arm_scan_selective_scan_f32_async",
               "arm_scan_selective_scan_bidirectional_f32",
               "arm_scan_selective_scan_bidirectional_f32_async",
@@ -170,13 +177,26 @@ def mamba3_raw(dims, ptrs, reverse, backend, threading, ptr_out, ptr_last_state,
                "arm_scan_mamba3_scan_f32_async")
 
 
+def angles_workspace_bytes(dims, n_angles):
+    return int(load().arm_scan_mamba3_angles_workspace_bytes(ctypes.byref(dims), n_angles))
+
+
+def angles_async_raw(dims, ptr_angles, n_angles, ptr_dt, ptr_cos, ptr_sin, ptr_ws, ws_bytes,
+                     stream):
+    """Mamba-3 angle pre-pass (device pointers, stream-ordered)."""
+    _check(load().arm_scan_mamba3_angles_f32_async(
+        ctypes.byref(dims), ptr_angles, n_angles, ptr_dt, ptr_cos, ptr_sin, ptr_ws, ws_bytes,
+        _n(stream)), "arm_scan_mamba3_angles_f32_async")
+
+
 def exported_symbols():
     """Names of every entry point include/b200scan.h declares."""
     return ["arm_scan_abi_version", "arm_scan_last_error",
             "arm_scan_selective_scan_f32", "arm_scan_selective_scan_f32_async",
             "arm_scan_selective_scan_bidirectional_f32",
             "arm_scan_selective_scan_bidirectional_f32_async",
-            "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async"]
+            "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
+            "arm_scan_mamba3_angles_workspace_bytes", "arm_scan_mamba3_angles_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

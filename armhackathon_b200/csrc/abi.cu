@@ -16,6 +16,7 @@
 
 #include "../../include/b200scan.h"
 #include "m1_scan.h"
+#include "m3_angles.h"
 #include "m3_scan.h"
 
 using namespace b200scan;
@@ -516,6 +517,38 @@ int arm_scan_mamba3_scan_f32_async(const ArmMamba3Dims* dims, const float* q, co
         const_cast<float*>(mimo_psi), const_cast<float*>(mimo_zeta), const_cast<float*>(mimo_phi),
         out,                        last_state,                    last_bx};
     return m3_run(m3_params(dims, p, reverse), backend, static_cast<cudaStream_t>(stream));
+}
+
+size_t arm_scan_mamba3_angles_workspace_bytes(const ArmMamba3Dims* dims, size_t n_angles) {
+    if (!dims) return 0;
+    return angle_workspace_bytes(static_cast<int64_t>(dims->batch),
+                                 static_cast<int64_t>(dims->heads),
+                                 static_cast<int64_t>(dims->len), static_cast<int64_t>(n_angles));
+}
+
+int arm_scan_mamba3_angles_f32_async(const ArmMamba3Dims* dims, const float* angles,
+                                     size_t n_angles, const float* dt, float* cos, float* sin,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+    if (!dims || !angles || !dt || !cos || !sin || !workspace)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    if (!dims->batch || !dims->heads || !dims->len || !dims->dqk || !n_angles)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "a dimension is zero");
+    if (dims->dqk % 2 || n_angles > dims->dqk / 2 || dims->dqk > 256)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS,
+                    "n_angles (%zu) must be <= dqk/2 with dqk (%zu) even and <= 256", n_angles,
+                    dims->dqk);
+    if (dims->batch * dims->heads > 65535)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "batch*heads above 65535");
+    const size_t need = arm_scan_mamba3_angles_workspace_bytes(dims, n_angles);
+    if (workspace_bytes < need)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "workspace of %zu bytes, %zu needed",
+                    workspace_bytes, need);
+    AngleParams a{angles, dt, cos, sin, static_cast<int64_t>(dims->batch),
+                  static_cast<int64_t>(dims->heads), static_cast<int64_t>(dims->len),
+                  static_cast<int64_t>(n_angles), static_cast<int64_t>(dims->dqk / 2)};
+    cudaError_t e = angle_launch(a, static_cast<float*>(workspace),
+                                 static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "angle pre-pass launch");
 }
 
 }  // extern "C"

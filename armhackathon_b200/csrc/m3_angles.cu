@@ -1,0 +1,89 @@
+// Mamba-3 RoPE angle pre-pass on the GPU.
+//
+// theta[b, t, h, p] = sum_{s <= t} tanh(angle[b, s, h, p]) * pi * dt[b, h, s]
+// cos/sin[b, t, h, p] = cos/sin(theta) for p < n_angles, and (1, 0) -- the
+// identity rotation -- for n_angles <= p < dqk/2.  Same contract as the
+// reference's python/arm_scan/mamba3.py:41-89 (angles_to_cos_sin), whose
+// prefix sum runs in torch; here it is a two-phase chunked scan:
+//   phase 1: per (batch*head, chunk of kAgChunk steps, pair) the chunk's sum
+//            of increments -> workspace;
+//   phase 2: each (batch*head, chunk, pair) adds the sums of the earlier
+//            chunks, then walks its chunk writing cos/sin.
+// Reads of angles are coalesced over pairs (the innermost axis).
+#include <cstdint>
+
+#include "common.cuh"
+#include "m3_angles.h"
+
+namespace b200scan {
+
+namespace {
+
+constexpr int kAgChunk = 128;
+constexpr float kPi = 3.14159265358979323846f;
+
+__global__ void angle_chunk_sums(AngleParams a, float* ws) {
+    const int64_t bh = blockIdx.y;
+    const int c = blockIdx.x;
+    const int p = threadIdx.x;
+    if (p >= a.n_angles) return;
+    const int64_t b = bh / a.heads, h = bh % a.heads;
+    const int64_t t0 = static_cast<int64_t>(c) * kAgChunk;
+    const int64_t t1 = t0 + kAgChunk < a.len ? t0 + kAgChunk : a.len;
+    float s = 0.f;
+    for (int64_t t = t0; t < t1; ++t) {
+        const float ang = a.angles[((b * a.len + t) * a.heads + h) * a.n_angles + p];
+        s = fmaf(tanhf(ang) * kPi, a.dt[(b * a.heads + h) * a.len + t], s);
+    }
+    ws[(bh * gridDim.x + c) * a.n_angles + p] = s;
+}
+
+__global__ void angle_chunk_write(AngleParams a, const float* ws) {
+    const int64_t bh = blockIdx.y;
+    const int c = blockIdx.x;
+    const int p = threadIdx.x;
+    if (p >= a.half) return;
+    const int64_t b = bh / a.heads, h = bh % a.heads;
+    const int64_t t0 = static_cast<int64_t>(c) * kAgChunk;
+    const int64_t t1 = t0 + kAgChunk < a.len ? t0 + kAgChunk : a.len;
+    if (p >= a.n_angles) {
+        for (int64_t t = t0; t < t1; ++t) {
+            const int64_t o = ((b * a.len + t) * a.heads + h) * a.half + p;
+            a.cos[o] = 1.f;
+            a.sin[o] = 0.f;
+        }
+        return;
+    }
+    float theta = 0.f;
+    for (int j = 0; j < c; ++j) theta += ws[(bh * gridDim.x + j) * a.n_angles + p];
+    for (int64_t t = t0; t < t1; ++t) {
+        const float ang = a.angles[((b * a.len + t) * a.heads + h) * a.n_angles + p];
+        theta = fmaf(tanhf(ang) * kPi, a.dt[(b * a.heads + h) * a.len + t], theta);
+        float sn, cs;
+        sincosf(theta, &sn, &cs);
+        const int64_t o = ((b * a.len + t) * a.heads + h) * a.half + p;
+        a.cos[o] = cs;
+        a.sin[o] = sn;
+    }
+}
+
+}  // namespace
+
+size_t angle_workspace_bytes(int64_t batch, int64_t heads, int64_t len, int64_t n_angles) {
+    const int64_t chunks = (len + kAgChunk - 1) / kAgChunk;
+    return static_cast<size_t>(batch * heads * chunks * n_angles) * sizeof(float);
+}
+
+cudaError_t angle_launch(const AngleParams& a, float* ws, cudaStream_t stream) {
+    const int64_t chunks = (a.len + kAgChunk - 1) / kAgChunk;
+    const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(a.batch * a.heads));
+    const int t1 = static_cast<int>((a.n_angles + 31) / 32 * 32);
+    const int t2 = static_cast<int>((a.half + 31) / 32 * 32);
+    angle_chunk_sums<<<grid, t1, 0, stream>>>(a, ws);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    angle_chunk_write<<<grid, t2, 0, stream>>>(a, ws);
+    return cudaGetLastError();
+}
+
+}  // namespace b200scan

@@ -43,13 +43,39 @@ def angles_to_cos_sin(angles: torch.Tensor, dt: torch.Tensor,
     if r > half:
         raise ValueError(f"angles has {r} rotation pairs but the head dim allows {half}")
     dtype = torch.promote_types(angles.dtype, torch.float32)
-    dt_blh = dt.permute(0, 2, 1).unsqueeze(-1).to(dtype)
-    theta = torch.cumsum(torch.tanh(angles.to(dtype)) * math.pi * dt_blh, dim=1)
-    cos, sin = torch.cos(theta), torch.sin(theta)
-    if r < half:
-        pad = (*theta.shape[:-1], half - r)
-        cos = torch.cat([cos, torch.ones(pad, dtype=cos.dtype, device=cos.device)], dim=-1)
-        sin = torch.cat([sin, torch.zeros(pad, dtype=sin.dtype, device=sin.device)], dim=-1)
+    if dtype == torch.float64:
+        # f64 analysis path (the dense non-causal check): plain torch, at the
+        # caller's precision, exactly as the reference computes it
+        dt_blh = dt.permute(0, 2, 1).unsqueeze(-1).to(dtype)
+        theta = torch.cumsum(torch.tanh(angles.to(dtype)) * math.pi * dt_blh, dim=1)
+        cos, sin = torch.cos(theta), torch.sin(theta)
+        if r < half:
+            pad = (*theta.shape[:-1], half - r)
+            cos = torch.cat([cos, torch.ones(pad, dtype=cos.dtype, device=cos.device)], dim=-1)
+            sin = torch.cat([sin, torch.zeros(pad, dtype=sin.dtype, device=sin.device)], dim=-1)
+        return cos, sin
+    return _angles_gpu(angles, dt, half)
+
+
+def _angles_gpu(angles, dt, half):
+    """fp32 pre-pass through the library's CUDA kernel; CPU inputs are
+    computed on the current CUDA device and returned on the CPU."""
+    home = angles.device
+    dev = home if home.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
+    a = angles.to(device=dev, dtype=torch.float32).contiguous()
+    d = dt.to(device=dev, dtype=torch.float32).contiguous()
+    b, length, h, r = a.shape
+    cos = torch.empty((b, length, h, half), device=dev)
+    sin = torch.empty_like(cos)
+    dims = _ffi.ArmMamba3Dims(b, h, 0, 2 * half, length, 1)
+    nbytes = _ffi.angles_workspace_bytes(dims, r)
+    ws = torch.empty(max(nbytes, 4), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _ffi.angles_async_raw(dims, a.data_ptr(), r, d.data_ptr(), cos.data_ptr(),
+                              sin.data_ptr(), ws.data_ptr(), nbytes,
+                              torch.cuda.current_stream(dev).cuda_stream)
+    if home.type != "cuda":
+        cos, sin = cos.to(home), sin.to(home)
     return cos, sin
 
 

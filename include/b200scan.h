@@ -143,6 +143,22 @@ int arm_scan_mamba3_scan_f32_async(
     int threading, float* out, float* last_state, float* last_bx,
     void* stream);
 
+/* v8: the Mamba-3 RoPE angle pre-pass on the GPU (device pointers), replacing
+ * the torch computation of the reference's angles_to_cos_sin
+ * (python/arm_scan/mamba3.py:41-89):
+ *   theta[b,t,h,p] = sum_{s<=t} tanh(angles[b,s,h,p]) * pi * dt[b,h,s]
+ *   cos/sin (batch, len, heads, dqk/2) = cos/sin(theta) for p < n_angles,
+ *   1/0 for n_angles <= p < dqk/2.
+ * angles (batch, len, heads, n_angles), dt (batch, heads, len); uses
+ * dims->batch, heads, len, dqk (rank and dv are ignored).  `workspace` must
+ * hold arm_scan_mamba3_angles_workspace_bytes(...) bytes of device memory,
+ * used only during the call's stream-ordered execution. */
+size_t arm_scan_mamba3_angles_workspace_bytes(const ArmMamba3Dims* dims, size_t n_angles);
+int arm_scan_mamba3_angles_f32_async(const ArmMamba3Dims* dims, const float* angles,
+                                     size_t n_angles, const float* dt, float* cos,
+                                     float* sin, void* workspace, size_t workspace_bytes,
+                                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

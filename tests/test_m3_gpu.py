@@ -181,3 +181,22 @@ def test_sequential_backend_matches_oracle(mimo):
                     out.data_ptr(), 0, 0)
     got = out.permute(0, 2, 1, 3).cpu().numpy()
     assert rel_err(got, want) <= REL_TOL
+
+
+@pytest.mark.parametrize("shape", [(2, 5000, 3, 64, 20), (1, 1, 2, 128, 64), (3, 129, 4, 16, 8)])
+def test_angle_prepass_kernel_vs_oracle(shape):
+    """The CUDA angle pre-pass (theta = cumsum(tanh(angle) * pi * dt), cos/sin
+    padded with the identity) against the f64 oracle restatement of the
+    reference's angles_to_cos_sin; pairs beyond n_angles must be exactly
+    (1, 0).  Tolerance 1e-4 absolute on cos/sin (the prefix sum is fp32, as
+    in the reference's torch path)."""
+    b, length, h, dqk, r = shape
+    g = torch.Generator().manual_seed(length)
+    ang = torch.randn(b, length, h, r, generator=g)
+    dt = torch.nn.functional.softplus(torch.randn(b, h, length, generator=g) - 4)
+    cos, sin = arm().angles_to_cos_sin(ang.cuda(), dt.cuda(), dqk // 2)
+    wc, ws = oracle.angles_to_cos_sin(ang.numpy(), dt.numpy(), dqk // 2)
+    assert np.abs(cos.cpu().numpy() - wc).max() < 1e-4
+    assert np.abs(sin.cpu().numpy() - ws).max() < 1e-4
+    if r < dqk // 2:
+        assert torch.all(cos[..., r:] == 1) and torch.all(sin[..., r:] == 0)
