@@ -82,6 +82,9 @@ def _bind(lib):
     lib.arm_scan_mamba3_angles_f32_async.argtypes = [
         ctypes.POINTER(ArmMamba3Dims), _VP, ctypes.c_size_t, _VP, _VP, _VP, _VP,
         ctypes.c_size_t, _VP]
+    lib.arm_scan_mamba3_angles_f32_noalloc.restype = ctypes.c_int
+    lib.arm_scan_mamba3_angles_f32_noalloc.argtypes = [
+        ctypes.POINTER(ArmMamba3Dims), _VP, ctypes.c_size_t, _VP, _VP, _VP, _VP]
     for f in ("arm_scan_selective_scan_f32", "arm_scan_selective_scan_f32_async",
               "arm_scan_selective_scan_bidirectional_f32",
               "arm_scan_selective_scan_bidirectional_f32_async",
@@ -196,7 +199,8 @@ def exported_symbols():
             "arm_scan_selective_scan_bidirectional_f32",
             "arm_scan_selective_scan_bidirectional_f32_async",
             "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
-            "arm_scan_mamba3_angles_workspace_bytes", "arm_scan_mamba3_angles_f32_async"]
+            "arm_scan_mamba3_angles_workspace_bytes", "arm_scan_mamba3_angles_f32_async",
+            "arm_scan_mamba3_angles_f32_noalloc"]
 
 
 if __name__ == "__main__":  # pragma: no cover

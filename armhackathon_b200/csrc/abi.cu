@@ -551,4 +551,31 @@ int arm_scan_mamba3_angles_f32_async(const ArmMamba3Dims* dims, const float* ang
     return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "angle pre-pass launch");
 }
 
+int arm_scan_mamba3_angles_f32_noalloc(const ArmMamba3Dims* dims, const float* angles,
+                                       size_t n_angles, const float* dt, float* cos, float* sin,
+                                       void* stream) {
+    if (!dims || !angles || !dt || !cos || !sin)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    if (!dims->batch || !dims->heads || !dims->len || !dims->dqk || !n_angles)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "a dimension is zero");
+    if (dims->dqk % 2 || n_angles > dims->dqk / 2 || dims->dqk > 256)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS,
+                    "n_angles (%zu) must be <= dqk/2 with dqk (%zu) even and <= 256", n_angles,
+                    dims->dqk);
+    if (dims->batch * dims->heads > 65535)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "batch*heads above 65535");
+    AngleParams a{angles, dt, cos, sin, static_cast<int64_t>(dims->batch),
+                  static_cast<int64_t>(dims->heads), static_cast<int64_t>(dims->len),
+                  static_cast<int64_t>(n_angles), static_cast<int64_t>(dims->dqk / 2)};
+    bool too_big = false;
+    cudaError_t e = angle_noalloc_launch(a, static_cast<cudaStream_t>(stream), &too_big);
+    if (too_big)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS,
+                    "problem needs %zu bytes of scratch; the built-in scratch holds %lld bytes "
+                    "(use arm_scan_mamba3_angles_f32_async with a workspace)",
+                    arm_scan_mamba3_angles_workspace_bytes(dims, n_angles),
+                    static_cast<long long>(kAngleNoAllocMaxFloats * 4));
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "allocation-free angle pre-pass");
+}
+
 }  // extern "C"

@@ -17,4 +17,10 @@ struct AngleParams {
 size_t angle_workspace_bytes(int64_t batch, int64_t heads, int64_t len, int64_t n_angles);
 cudaError_t angle_launch(const AngleParams& a, float* workspace, cudaStream_t stream);
 
+// Allocation-free variant: chunk sums in a fixed device array of this many
+// floats (4 MiB); sets *too_big (and launches nothing) when the problem needs
+// more.  The first call on a device looks up the array's device address.
+constexpr int64_t kAngleNoAllocMaxFloats = int64_t(1) << 20;
+cudaError_t angle_noalloc_launch(const AngleParams& a, cudaStream_t stream, bool* too_big);
+
 }  // namespace b200scan

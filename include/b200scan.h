@@ -159,6 +159,24 @@ int arm_scan_mamba3_angles_f32_async(const ArmMamba3Dims* dims, const float* ang
                                      float* sin, void* workspace, size_t workspace_bytes,
                                      void* stream);
 
+/* No counterpart in the reference.  The same angle pre-pass for callers that
+ * cannot allocate device memory at call time: a host framework or inference
+ * server whose device memory is owned by its own allocator (an extra
+ * cudaMalloc from a plugin can fail or fragment its pool), or a real-time
+ * caller that forbids allocation once it is running.  It calls no cudaMalloc
+ * or cudaFree; its scratch is a fixed 4 MiB device array inside the library
+ * (held by every GPU that loads the library until the process exits), so a
+ * problem needing more than 4 MiB of chunk sums
+ * (batch*heads*ceil(len/128)*n_angles*4 bytes) is rejected with code 2.
+ * The first call on each device looks up the array's device address; make
+ * that first call before any stream capture.  All calls share the one array:
+ * calls whose executions overlap on the GPU (different streams, or different
+ * host threads) race on it and must be serialized by the caller.  Arguments
+ * and results are those of arm_scan_mamba3_angles_f32_async. */
+int arm_scan_mamba3_angles_f32_noalloc(const ArmMamba3Dims* dims, const float* angles,
+                                       size_t n_angles, const float* dt, float* cos,
+                                       float* sin, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
