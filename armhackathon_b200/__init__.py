@@ -32,7 +32,7 @@ _LAZY = {
     "ss2d_scan_mamba3": ".ss2d_mamba3",
     "noncausal_scan": ".mamba3_noncausal", "noncausal_scan_dense": ".mamba3_noncausal",
     "ss2d_noncausal_mamba3": ".mamba3_noncausal",
-    "patch": ".patch", "unpatch": ".patch", "stats": ".patch",
+    "patch": ".hf_patch", "unpatch": ".hf_patch", "stats": ".hf_patch",
 }
 
 
@@ -41,5 +41,9 @@ def __getattr__(name):
     # import torch
     import importlib
     if name in _LAZY:
-        return getattr(importlib.import_module(_LAZY[name], __name__), name)
+        # importing a submodule binds it as a package attribute (``patch`` is
+        # both a module and its function): rebind the function afterwards
+        obj = getattr(importlib.import_module(_LAZY[name], __name__), name)
+        globals()[name] = obj
+        return obj
     raise AttributeError(f"module 'armhackathon_b200' has no attribute '{name}'")

@@ -243,6 +243,53 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def prefill_tok_s(dev, batch, length, steps=3, warmup=2):
+    """random-init Mamba-1 130M architecture (24 layers,
+    d_model 768, expand 2, d_state 16, d_conv 4, dt_rank 48, vocab 50280,
+    weights N(0, 0.02), A_log = log(1..16), dt bias as config 0), fp32, HF
+    transformers MambaForCausalLM with patch() routing the scan to this
+    library; a full forward (logits included) over random token ids.  Returns
+    tokens/s (CUDA events, median of `steps`)."""
+    import torch
+    from transformers import MambaConfig, MambaForCausalLM
+    import armhackathon_b200 as arm
+    cfg = MambaConfig(vocab_size=50280, hidden_size=768, state_size=16, num_hidden_layers=24,
+                      expand=2, conv_kernel=4, time_step_rank=48, initializer_range=0.02,
+                      use_cache=False)
+    torch.manual_seed(0)
+    model = MambaForCausalLM(cfg).to(dev).eval()
+    with torch.no_grad():
+        g = torch.Generator(device="cpu").manual_seed(0)
+        for layer in model.backbone.layers:
+            mx = layer.mixer
+            mx.A_log.copy_(torch.log(torch.arange(1, 17, dtype=torch.float32)).repeat(
+                mx.A_log.shape[0], 1))
+            dt = torch.exp(torch.empty(mx.dt_proj.bias.shape).uniform_(
+                np.log(1e-3), np.log(1e-1), generator=g))
+            mx.dt_proj.bias.copy_(torch.log(torch.expm1(dt)))
+    ids = torch.randint(0, 50280, (batch, length), device=dev)
+    arm.patch()
+    try:
+        times = []
+        with torch.no_grad():
+            for i in range(warmup + steps):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                model(ids)
+                b.record()
+                torch.cuda.synchronize()
+                if i >= warmup:
+                    times.append(a.elapsed_time(b))
+        engaged = arm.stats()["fast_calls"] > 0
+    finally:
+        arm.unpatch()
+    del model
+    torch.cuda.empty_cache()
+    ms = statistics.median(times)
+    return {"tok_s": batch * length / (ms * 1e-3), "ms": ms, "batch": batch, "len": length,
+            "kernel_engaged": engaged}
+
+
 def run_reference(args, w):
     """--impl reference: the reference's CPU path (scalar recurrence over rows
     on all host threads; oracle port, the Rust crate has no toolchain here)."""
@@ -321,6 +368,8 @@ def main():
                     choices=sorted(WORKLOADS) + sorted(M3_WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the config-1 HF prefill tok/s measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload in M3_WORKLOADS:
@@ -455,6 +504,10 @@ def main():
         }
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w)
+        if not args.no_prefill:
+            line["prefill"] = {
+                "metric": "Mamba-1 prefill tok/s (BASELINE config 1, fp32, patched HF, 1 GPU)",
+                "runs": [prefill_tok_s(dev, 8, 2048), prefill_tok_s(dev, 1, 32768)]}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

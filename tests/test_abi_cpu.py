@@ -103,3 +103,12 @@ def test_mamba3_argument_rules():
     assert _m3(_ffi.ArmMamba3Dims(1, 1, 4, 4, 1, 2), mimo=3, last_state=True,
                last_bx=True) == 2                          # MIMO has no last_bx
     assert _m3(_ffi.ArmMamba3Dims(0, 1, 4, 4, 1, 1)) == 2  # zero dim
+
+
+def test_lazy_exports_are_functions_after_submodule_import():
+    import importlib
+    import armhackathon_b200 as arm
+    importlib.import_module("armhackathon_b200.hf_patch")
+    for name in ("patch", "unpatch", "stats", "selective_scan", "mamba3_scan", "ss2d_scan"):
+        assert callable(getattr(arm, name)) and not hasattr(getattr(arm, name), "__path__")
+    assert type(arm.patch).__name__ == "function"
