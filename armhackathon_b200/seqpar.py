@@ -1,0 +1,86 @@
+"""Sequence-parallel bidirectional Mamba-1 scan across ranks (one GPU each).
+
+A long single sequence is split into contiguous segments, segment r on rank r
+(rank order = time order).  The recurrence h_t = a_t * h_{t-1} + b_t is linear
+in h, and the decay across a whole segment factorises per state:
+prod_t exp(dt_t * A_n) = exp(A_n * sum_t dt_t).  So a segment is summarised by
+(h_end from a zero start, sum dt) per (batch, channel): about
+batch*dim*(state+1)*4 bytes per direction (~100 KB at dim 1536, state 16).
+
+Per call:
+  1. each rank scans its segment forward and backward from zero, keeping the
+     final states and sum(dt) per row;
+  2. one all_gather of those summaries (the only collective);
+  3. rank r folds the summaries of ranks < r (forward) and > r (backward)
+     into its incoming states;
+  4. rank r rescans its segment from those states (ranks at the sequence ends
+     keep the pass-1 output of the direction that starts at them).
+The fold is exact algebra, so the result equals the unsplit bidirectional
+scan up to fp32 rounding.  No rank waits on another except inside the
+all_gather, whose timeout is the process group's.
+"""
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+
+def _segment_dt_sum(delta, delta_bias, delta_softplus):
+    dt = delta.float()
+    if delta_bias is not None:
+        dt = dt + delta_bias.float()[:, None]
+    if delta_softplus:
+        dt = F.softplus(dt)  # threshold 20, the kernel's contract
+    return dt.sum(-1)
+
+
+def fold_carries(h_ends, dt_sums, A, rank, reverse):
+    """Incoming state of segment ``rank`` from the other segments' summaries.
+
+    h_ends[j] (B, D, N): segment j's state after its traversal from zero;
+    dt_sums[j] (B, D); A (D, N).  Forward folds segments 0..rank-1 in order,
+    reverse folds segments W-1..rank+1."""
+    order = range(rank) if not reverse else range(len(h_ends) - 1, rank, -1)
+    h = torch.zeros_like(h_ends[0])
+    Af = A.float()[None]
+    for j in order:
+        h = torch.exp(Af * dt_sums[j][..., None]) * h + h_ends[j]
+    return h
+
+
+def bidirectional_scan_seqpar(u, delta, A, B, C, D=None, z=None, delta_bias=None,
+                              delta_softplus=False, merge="sum", group=None, scan_fn=None):
+    """Bidirectional scan of one sequence split over the ranks of ``group``.
+
+    Every rank passes its own segment (same layouts as ``selective_scan``:
+    u, delta, z (batch, dim, L_rank); B, C (batch, [groups,] state, L_rank);
+    A (dim, state); D, delta_bias (dim,)).  Returns this rank's segment of the
+    merged output ("sum") or (fwd, bwd) ("none").  ``scan_fn`` defaults to
+    this package's ``selective_scan``; tests substitute a CPU reference.
+    """
+    if merge not in ("sum", "none"):
+        raise ValueError(f"merge must be 'sum' or 'none', got {merge!r}")
+    if scan_fn is None:
+        from .op import selective_scan as scan_fn
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    kw = dict(D=D, z=z, delta_bias=delta_bias, delta_softplus=delta_softplus,
+              return_last_state=True)
+    yf, hf = scan_fn(u, delta, A, B, C, **kw)
+    yb, hb = scan_fn(u, delta, A, B, C, reverse=True, **kw)
+    sdt = _segment_dt_sum(delta, delta_bias, delta_softplus).to(hf.dtype)
+    packed = torch.cat([hf, hb, sdt[..., None]], dim=-1).contiguous()
+    parts = [torch.empty_like(packed) for _ in range(world)]
+    dist.all_gather(parts, packed, group=group)
+    N = hf.shape[-1]
+    h_f = [p[..., :N] for p in parts]
+    h_b = [p[..., N:2 * N] for p in parts]
+    sums = [p[..., 2 * N] for p in parts]
+    kw.pop("return_last_state")
+    if rank > 0:
+        yf = scan_fn(u, delta, A, B, C, initial_state=fold_carries(h_f, sums, A, rank, False),
+                     **kw)
+    if rank < world - 1:
+        yb = scan_fn(u, delta, A, B, C, reverse=True,
+                     initial_state=fold_carries(h_b, sums, A, rank, True), **kw)
+    return yf + yb if merge == "sum" else (yf, yb)

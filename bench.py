@@ -108,11 +108,50 @@ def run_m3(args, w):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     if w["kind"] == "bidir":
-        x = make_inputs(dict(batch=1, dim=w["dim"], len=w["len"], state=w["state"]), dev)
-        step = lambda: arm.bidirectional_scan(  # noqa: E731
-            x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"], z=x["z"],
-            delta_bias=x["delta_bias"], delta_softplus=True, merge="sum")
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        seg = w["len"] // world  # strong scaling: one sequence split over the ranks
+        x = make_inputs(dict(batch=1, dim=w["dim"], len=seg, state=w["state"]), dev, seed=rank)
+        if world > 1:
+            import torch.distributed as dist
+            from armhackathon_b200.seqpar import bidirectional_scan_seqpar
+            dist.init_process_group("nccl", device_id=dev)
+            step = lambda: bidirectional_scan_seqpar(  # noqa: E731
+                x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"], z=x["z"],
+                delta_bias=x["delta_bias"], delta_softplus=True)
+        else:
+            step = lambda: arm.bidirectional_scan(  # noqa: E731
+                x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"], z=x["z"],
+                delta_bias=x["delta_bias"], delta_softplus=True, merge="sum")
         nbytes = 4 * (4 * w["dim"] * w["len"] + 2 * w["state"] * w["len"])
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "workload": args.workload, "desc": w["desc"],
+                              "n_gpus": world, "scaling": "strong",
+                              "ms_per_step": float(ms.item()),
+                              "value": nbytes / (float(ms.item()) * 1e-3) / 1e9, "unit": "GB/s",
+                              "bytes_per_step": nbytes,
+                              "parallelism": f"sequence-parallel over {world} ranks, one "
+                                             "all_gather of segment carries per call"}),
+                  flush=True)
+        return
     else:
         x = m3_inputs(w, dev)
         nbytes = m3_bytes(w)
