@@ -348,7 +348,8 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
     if ((variant == 5 || variant == 6 || variant == 7) && m1_rowseq_applicable(p))
         return m1_rowseq_launch(p, variant == 6 ? 2 : variant == 7 ? 1 : 4, stream);
     const bool tile_ok = p.state <= 16 && p.len <= (INT32_MAX / 4) && p.state * p.len <= INT32_MAX;
-    if (tile_ok && variant != 0) return m1_tile_launch(p, variant < 1 || variant > 4 ? 1 : variant, stream);
+    if (tile_ok && variant != 0) return m1_tile_launch(
+        p, (variant >= 1 && variant <= 4) || variant == 9 || variant == 10 ? variant : 1, stream);
     switch (m1_pick_channels_per_cta(p.batch * p.dim)) {
         case 32: return launch_chunked<32, 16>(p, stream);
         case 16: return launch_chunked<16, 16>(p, stream);

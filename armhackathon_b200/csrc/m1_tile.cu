@@ -68,7 +68,7 @@ struct TileInfo {
     int n_rows;     // rows of the tile that exist (<= DC)
 };
 
-template <int DC, int K, bool VEC, bool REV>
+template <int DC, int K, bool VEC, bool REV, int POLY>
 __global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, int tiles_per_group,
                                                                   int n_tiles) {
     using LY = TileLayout<DC, K>;
@@ -228,8 +228,12 @@ __global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, in
                     const float2 dt2 = make_float2(dt[k], dt[k]);
                     const float2 du2 = make_float2(dtu[k], dtu[k]);
                     const float2 x01 = fmul2(dt2, al01), x23 = fmul2(dt2, al23);
+                    // POLY 1: states 2,3 of odd steps on the FMA pipe (25% of
+                    // the exps); POLY 2: states 2,3 of every step (50%)
                     const float2 a01 = make_float2(ex2_approx(x01.x), ex2_approx(x01.y));
-                    const float2 a23 = make_float2(ex2_approx(x23.x), ex2_approx(x23.y));
+                    const float2 a23 = (POLY == 2 || (POLY == 1 && (k & 1)))
+                                           ? exp2_poly2(x23)
+                                           : make_float2(ex2_approx(x23.x), ex2_approx(x23.y));
                     const float2 c01 = make_float2(cv.x, cv.y), c23 = make_float2(cv.z, cv.w);
                     h01 = ffma2(a01, h01, fmul2(du2, make_float2(bv.x, bv.y)));
                     h23 = ffma2(a23, h23, fmul2(du2, make_float2(bv.z, bv.w)));
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, in
     cp_async_wait_all();
 }
 
-template <int DC, int K>
+template <int DC, int K, int POLY = 0>
 cudaError_t launch_tile(const M1Params& p, cudaStream_t stream) {
     using LY = TileLayout<DC, K>;
     const int64_t gsz = p.dim / p.groups;
@@ -335,9 +339,11 @@ cudaError_t launch_tile(const M1Params& p, cudaStream_t stream) {
     const bool vec = (p.len % 4 == 0) && m1_pointers_aligned16(p);
     void (*kern)(M1Params, int, int);
     if (vec)
-        kern = p.reverse ? m1_tile_kernel<DC, K, true, true> : m1_tile_kernel<DC, K, true, false>;
+        kern = p.reverse ? m1_tile_kernel<DC, K, true, true, POLY>
+                         : m1_tile_kernel<DC, K, true, false, POLY>;
     else
-        kern = p.reverse ? m1_tile_kernel<DC, K, false, true> : m1_tile_kernel<DC, K, false, false>;
+        kern = p.reverse ? m1_tile_kernel<DC, K, false, true, POLY>
+                         : m1_tile_kernel<DC, K, false, false, POLY>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
@@ -361,6 +367,8 @@ cudaError_t m1_tile_launch(const M1Params& p, int variant, cudaStream_t stream) 
         case 2: return launch_tile<8, 8>(p, stream);
         case 3: return launch_tile<32, 8>(p, stream);
         case 4: return launch_tile<16, 4>(p, stream);
+        case 9: return launch_tile<16, 8, 1>(p, stream);
+        case 10: return launch_tile<16, 8, 2>(p, stream);
         default: return launch_tile<16, 8>(p, stream);
     }
 }

@@ -201,7 +201,7 @@ def test_mixed_host_device_rejected():
     assert rc == 2
 
 
-@pytest.mark.parametrize("variant", ["0", "1", "2", "3", "4", "5", "6", "7", "8"])
+@pytest.mark.parametrize("variant", ["0", "1", "2", "3", "4", "5", "6", "7", "8", "9", "10"])
 @pytest.mark.parametrize("reverse", [False, True])
 def test_every_kernel_variant_vs_oracle(variant, reverse, monkeypatch):
     """Each Mamba-1 kernel shape the library can dispatch to (selected with
