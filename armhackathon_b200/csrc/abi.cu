@@ -55,7 +55,8 @@ bool mul4(size_t a, size_t b, size_t c, size_t d, size_t* out) {
     return mul3(a, b, c, &t) && mul_ok(t, d, out);
 }
 
-int check_enums(int backend, int threading) {
+int check_enums(int backend, int threading, bool allow_tensor = false) {
+    if (allow_tensor && backend == 3 && threading >= 0 && threading <= 2) return ARM_SCAN_OK;
     if (backend < 0 || backend > 2 || threading < 0 || threading > 2)
         return fail(ARM_SCAN_ERR_BAD_ENUM, "backend %d / threading %d out of range", backend,
                     threading);
@@ -346,6 +347,9 @@ std::vector<Buf> m3_bufs(const M3Counts& c, const ArmMamba3Dims* d, const float*
 }
 
 int m3_run(const M3Params& m, int backend, cudaStream_t s) {
+    if (backend == 3 && !m3_tc_applicable(m))
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE,
+                    "the tensor backend covers SISO with dqk 128, dv 64 and 16-byte aligned v/z/out");
     cudaError_t e = m3_scan_launch(m, backend, s);
     return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "mamba3_scan launch");
 }
@@ -484,7 +488,7 @@ int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const fl
     bool mimo = false;
     int rc = m3_check_ptrs(req, 12, last_state, last_bx, mimo_psi, mimo_zeta, mimo_phi, &mimo);
     if (rc) return rc;
-    if ((rc = check_enums(backend, threading))) return rc;
+    if ((rc = check_enums(backend, threading, true))) return rc;
     M3Counts cnt;
     if ((rc = m3_validate(dims, mimo, last_state, last_bx, &cnt))) return rc;
     std::vector<Buf> bufs = m3_bufs(cnt, dims, q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin,
@@ -506,7 +510,7 @@ int arm_scan_mamba3_scan_f32_async(const ArmMamba3Dims* dims, const float* q, co
     bool mimo = false;
     int rc = m3_check_ptrs(req, 12, last_state, last_bx, mimo_psi, mimo_zeta, mimo_phi, &mimo);
     if (rc) return rc;
-    if ((rc = check_enums(backend, threading))) return rc;
+    if ((rc = check_enums(backend, threading, true))) return rc;
     M3Counts cnt;
     if ((rc = m3_validate(dims, mimo, last_state, last_bx, &cnt))) return rc;
     std::vector<void*> p = {

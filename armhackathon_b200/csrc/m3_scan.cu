@@ -202,6 +202,10 @@ bool m3_shape_supported(int64_t dv, int64_t dqk, int64_t rank) {
 cudaError_t m3_scan_launch(const M3Params& p, int backend, cudaStream_t stream) {
     // backend 1 ("scalar") and shapes the chunked kernel does not cover run
     // the sequential kernel; everything else the chunked dual form.
+    if (backend == 3) {
+        if (!m3_tc_applicable(p)) return cudaErrorNotSupported;
+        return m3_tc_launch(p, stream);
+    }
     if (backend != 1 && m3_chunk_applicable(p)) return m3_chunk_launch(p, stream);
     const bool mimo = p.psi != nullptr;
     const int R = mimo ? static_cast<int>(p.rank) : 1;

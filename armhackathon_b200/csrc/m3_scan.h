@@ -36,5 +36,9 @@ cudaError_t m3_scan_launch(const M3Params& p, int backend, cudaStream_t stream);
 // Chunked dual-form kernel (m3_chunk.cu): the default when applicable.
 bool m3_chunk_applicable(const M3Params& p);
 cudaError_t m3_chunk_launch(const M3Params& p, cudaStream_t stream);
+// Tensor-core kernel (m3_tc.cu): bf16 operands, fp32 accumulation; backend 3.
+bool m3_tc_applicable(const M3Params& p);
+cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream);
+int m3_tc_status_and_clear();  // 1 if a bounded wait expired since the last call
 
 }  // namespace b200scan

@@ -97,6 +97,7 @@ def _mamba3_scan_op(
     psi: Optional[torch.Tensor] = None,
     zeta: Optional[torch.Tensor] = None,
     phi: Optional[torch.Tensor] = None,
+    backend: int = 0,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     # q is (b, l, 1, dqk) for SISO (axis 2 = the single B/C group) and
     # (b, l, rank, dqk) for MIMO (axis 2 = rank); the projections decide.
@@ -113,7 +114,7 @@ def _mamba3_scan_op(
             [q.data_ptr(), k.data_ptr(), v.data_ptr(), adt.data_ptr(), dt.data_ptr(),
              trap.data_ptr(), q_bias.data_ptr(), k_bias.data_ptr(), cos.data_ptr(),
              sin.data_ptr(), _ptr(d_skip), _ptr(z), _ptr(psi), _ptr(zeta), _ptr(phi)],
-            1 if reverse else 0, _ffi.BACKENDS["auto"], _ffi.THREADING["auto"],
+            1 if reverse else 0, backend, _ffi.THREADING["auto"],
             out_hm.data_ptr(), last_state.data_ptr(), _ptr(last_bx), stream=_stream(v))
     _CALLS["n"] += 1
     return out_hm.permute(0, 2, 1, 3).contiguous(), last_state
@@ -121,7 +122,7 @@ def _mamba3_scan_op(
 
 @_mamba3_scan_op.register_fake
 def _(q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, d_skip, z, reverse,
-      psi=None, zeta=None, phi=None):
+      psi=None, zeta=None, phi=None, backend=0):
     b, length, _, dqk = q.shape
     h, dv = v.shape[2], v.shape[3]
     return v.new_empty((b, length, h, dv)), v.new_empty((b, h, dv, dqk))
@@ -158,9 +159,12 @@ def _check_shapes(q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, D, z):
             raise ValueError(f"{name} must be {shape}, got {actual}")
 
 
+_PRECISION = {"fp32": 0, "bf16": 3}
+
+
 def mamba3_scan(q, k, v, adt, dt, trap, q_bias, k_bias, angles=None,
                 D=None, z=None, reverse=False, cos=None, sin=None,
-                return_last_state=False):
+                return_last_state=False, precision="fp32"):
     """Mamba-3 SISO selective scan.
 
     q, k : (b, l, 1, dqk) or (b, l, dqk);  v, z : (b, l, h, dv)
@@ -168,7 +172,13 @@ def mamba3_scan(q, k, v, adt, dt, trap, q_bias, k_bias, angles=None,
     angles : (b, l, h, r) raw (the pre-pass runs here), or pass cos/sin
     q_bias, k_bias : (h, dqk);  D : (h,)
     returns (b, l, h, dv) [, last_state (b, h, dv, dqk)]
+
+    precision "fp32" (default): fp32 arithmetic throughout.  "bf16": the
+    tensor-core kernel -- q/k/v/W operands rounded to bf16, fp32
+    accumulation and fp32 state (for bf16 models; covers dqk 128, dv 64).
     """
+    if precision not in _PRECISION:
+        raise ValueError(f"precision must be one of {sorted(_PRECISION)}, got {precision!r}")
     if q.dim() == 3:
         q = q.unsqueeze(2)
     if k.dim() == 3:
@@ -186,7 +196,7 @@ def mamba3_scan(q, k, v, adt, dt, trap, q_bias, k_bias, angles=None,
     out, last = _mamba3_scan_op(
         _prep(q, dev), _prep(k, dev), _prep(v, dev), _prep(adt, dev), _prep(dt, dev),
         _prep(trap, dev), _prep(q_bias, dev), _prep(k_bias, dev), _prep(cos, dev),
-        _prep(sin, dev), opt(D), opt(z), bool(reverse))
+        _prep(sin, dev), opt(D), opt(z), bool(reverse), backend=_PRECISION[precision])
     return (out, last) if return_last_state else out
 
 

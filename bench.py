@@ -158,7 +158,9 @@ def run_m3(args, w):
         if w["kind"] == "mimo":
             step = lambda: arm.mamba3_mimo_scan(**x)  # noqa: E731
         elif w["kind"] == "siso":
-            step = lambda: arm.mamba3_scan(**x, return_last_state=True)  # noqa: E731
+            prec = "bf16" if args.m3_bf16 else "fp32"
+            step = lambda: arm.mamba3_scan(**x, return_last_state=True,  # noqa: E731
+                                           precision=prec)
         else:
             B, H, g = w["batch"], w["heads"], w["grid"]
             grid = lambda t: t.reshape(B, g, g, *t.shape[2:])  # noqa: E731
@@ -407,6 +409,8 @@ def main():
                     choices=sorted(WORKLOADS) + sorted(M3_WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--m3-bf16", action="store_true",
+                    help="Mamba-3 SISO workloads on the tensor-core (bf16 operand) kernel")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the config-1 HF prefill tok/s measurement")
     args = ap.parse_args()

@@ -200,3 +200,34 @@ def test_angle_prepass_kernel_vs_oracle(shape):
     assert np.abs(sin.cpu().numpy() - ws).max() < 1e-4
     if r < dqk // 2:
         assert torch.all(cos[..., r:] == 1) and torch.all(sin[..., r:] == 0)
+
+
+BF16_TOL = 2e-2  # bf16 operands, fp32 accumulation and state (north_star bf16 bar)
+
+
+@pytest.mark.parametrize("shape", [(1, 300, 2), (2, 128, 3), (1, 1, 1), (3, 517, 4)])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_tensor_core_siso_vs_oracle(shape, reverse):
+    """tcgen05 kernel (precision="bf16") against the f64 oracle: outputs and
+    final states within the bf16 bar, including partial last chunks."""
+    b, l, h = shape
+    x = random_siso(b, l, h, 64, 128, 64, seed=l + 1)
+    cos, sin = oracle.angles_to_cos_sin(x["angles"].numpy(), x["dt"].numpy(), 64)
+    want, wst, _ = oracle.m3_siso(x["q"], x["k"], x["v"], x["adt"], x["dt"], x["trap"],
+                                  x["q_bias"], x["k_bias"], cos, sin, D=x["D"], z=x["z"],
+                                  reverse=reverse, want_state=True, nthreads=8)
+    out, st = arm().mamba3_scan(**{k: v.cuda() for k, v in x.items()}, reverse=reverse,
+                                return_last_state=True, precision="bf16")
+    assert rel_err(out.cpu().numpy(), want) <= BF16_TOL
+    assert rel_err(st.cpu().numpy(), wst) <= BF16_TOL
+
+
+@pytest.mark.parametrize("name", [n for n in IDX["m3_siso"] if n.endswith(("00", "01", "02", "03"))])
+def test_tensor_core_siso_official_goldens(name):
+    """The 24-head x 64 x 128 captures from the official (bf16) kernel, within
+    the reference's 8 bf16-ULP gate."""
+    kw, d = load("m3_siso", name)
+    out = arm().mamba3_scan(kw["Q"], kw["K"], kw["V"], kw["ADT"], kw["DT"], kw["Trap"],
+                            kw["Q_bias"], kw["K_bias"], angles=kw["Angles"], D=kw["D"],
+                            z=kw["Z"], precision="bf16")
+    assert oracle.bf16_ulps_at_scale(out.cpu().numpy(), d["out"]) <= 8.0
