@@ -2,23 +2,40 @@
 // operands with fp32 accumulation in tensor memory; selected with backend 3.
 //
 // Same chunked dual form as m3_chunk.cu (see its header for the algebra),
-// with chunks of QC = 128 steps so every product is an M = 128 UMMA:
-//   G     = Qr Kr^T                 M=128 (i) N=128 (j) K=dqk     -> TMEM cols [0,128)
-//   W     = mask(l, scale, gamma) o G, rounded to bf16, back to shared memory
-//   Y     = W X + (e^l o Qr) S^T     M=128 (i) N=dv    K=128, dqk -> TMEM cols [128,192)
-//   dS^T  = (w o Kr)^T X             M=128 (n) N=dv    K=128      -> TMEM cols [192,256)
-// One CTA of 4 warps per (batch, head); warp w owns TMEM lanes 32w..32w+31,
-// i.e. rows i (for G, Y) and state rows n (for dS^T) of those lanes.  The
-// state S^T (dqk x dv) stays fp32 in registers (thread n holds row n) and is
-// rounded to bf16 only as the next chunk's MMA operand.  Operands use the
-// canonical no-swizzle layouts: 8-row x 16-byte core matrices.
+// with chunks of QC = 128 steps so every product is an M = 128 UMMA, split
+// into three launches so every chunk of every (batch, head) runs in parallel:
+//
+//  1. m3_tc_intra, one CTA per (batch*head, chunk), independent:
+//       G    = Qr Kr^T            M=128 (i) N=128 (j) K=dqk -> TMEM cols [0,128)
+//       W    = mask(l, scale, gamma) o G -> bf16, over Qr in shared memory
+//       Y    = W X                M=128 (i) N=dv  K=128     -> TMEM cols [0,64)
+//       dS^T = Kr^T (w o X)       M=128 (n) N=dv  K=128     -> TMEM cols [64,128)
+//     (Kr's K-major core matrices for G are byte for byte the MN-major A
+//     operand of dS^T; only the descriptor strides differ, so one copy
+//     serves both)
+//     writes y_intra + D x to out (gated by silu(z) already for chunk 0,
+//     whose entering state is zero), dS^T (fp32) and e^l o Qr (bf16, in
+//     its shared-memory operand image) to the workspace, and the chunk's
+//     total decay e^{l_last}.
+//  2. m3_tc_state: per (batch*head, slice of the state), walks the chunks
+//     S_in(c+1) = e^{l_last(c)} S_in(c) + dS(c) in fp32, overwriting dS(c)
+//     with S_in(c); the final state is last_state.
+//  3. m3_tc_inter, one CTA per (batch*head, chunk >= 1):
+//       Y   += (e^l o Qr) S_in^T  M=128 (i) N=dv  K=dqk      -> TMEM cols [0,64)
+//     then silu(z) gating and the final store.
+// Operands use the canonical no-swizzle layouts (8-row x 16-byte core
+// matrices); every operand is staged with 16-byte stores that fill whole
+// 128-byte rows of banks.  The state stays fp32 end to end; only MMA
+// operands are rounded to bf16.
 //
 // Every wait on an mbarrier is bounded; on expiry the kernel records a
-// timeout in g_tc_status, skips the remaining work and frees its tensor
-// memory.  Requires dqk == 128, dv == 64, rank 1, len % 8 == 0 is NOT needed.
+// timeout in g_tc_status, skips the remaining work, waits (bounded) for the
+// MMAs in flight and frees its tensor memory.  Requires dqk == 128,
+// dv == 64, rank 1 and 16-byte aligned tensors.
 #include <cuda_bf16.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "common.cuh"
 #include "m3_scan.h"
@@ -32,8 +49,6 @@ namespace {
 constexpr int kTcQ = 128;   // steps per chunk
 constexpr int kTcN = 128;   // dqk
 constexpr int kTcP = 64;    // dv
-constexpr int kTcThreads = 128;
-constexpr uint32_t kTmemCols = 256;
 
 // ---- shared-memory operand layouts (bf16 elements, byte offsets) ----------
 // K-major (rows r, K index k): core matrix (r/8, k/8) of 8x8 elements is 128
@@ -136,298 +151,503 @@ __device__ __forceinline__ uint16_t bf16_bits(float x) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 
-// shared memory map (bytes)
-constexpr uint32_t kOffQ = 0;                         // Qr  K-major 128x128
-constexpr uint32_t kOffQs = kOffQ + 128 * 128 * 2;    // e^l Qr K-major
-constexpr uint32_t kOffK = kOffQs + 128 * 128 * 2;    // Kr  K-major (B of G)
-constexpr uint32_t kOffKw = kOffK + 128 * 128 * 2;    // w Kr MN-major (A of dS^T: m=n, k=j)
-constexpr uint32_t kOffW = kOffKw + 128 * 128 * 2;    // W   K-major (A of Y: r=i, k=j)
-constexpr uint32_t kOffX = kOffW + 128 * 128 * 2;     // X   MN-major (B: m=p, k=j)
-constexpr uint32_t kOffS = kOffX + 64 * 128 * 2;      // S^T MN-major (B: m=p, k=n)
-constexpr uint32_t kOffGate = kOffS + 64 * 128 * 2;   // lcum, scale, gamma, w (fp32 x 128)
-constexpr uint32_t kOffMisc = kOffGate + 4 * 128 * 4; // eQ, mbarrier, tmem base
-constexpr uint32_t kTcSmem = kOffMisc + 64;
 
-__global__ void __launch_bounds__(kTcThreads, 1) m3_tc_kernel(M3Params p) {
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    return static_cast<uint32_t>(bf16_bits(lo)) | (static_cast<uint32_t>(bf16_bits(hi)) << 16);
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+    return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                      pack_bf16x2(f[6], f[7]));
+}
+__device__ __forceinline__ void ld8(const float* g, float (&f)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(g);
+    const float4 b = *reinterpret_cast<const float4*>(g + 4);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+__device__ __forceinline__ void ldg8(const float* g, float (&f)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(g));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(g + 4));
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(slot));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s), "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t tmem, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols));
+}
+
+// CTA-uniform bounded wait; false (and the status flag set) on expiry
+__device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity) {
+    const bool expired = __syncthreads_or(!mbar_wait(bar, parity));
+    if (expired && threadIdx.x == 0) atomicExch(&g_tc_status, 1);
+    return !expired;
+}
+
+constexpr int kTcThreads2 = 256;
+constexpr uint32_t kChunkImg = 128 * 128 * 2;  // bytes of one 128 x 128 bf16 operand
+constexpr uint32_t kChunkSt = 128 * 64 * 4;    // bytes of one fp32 dqk x dv state
+
+// workspace of one launch: e^l Qr images, dS/S_in states, chunk decays
+struct TcWs {
+    uint8_t* qs;    // [bh][chunk] kChunkImg
+    float* st;      // [bh][chunk] dqk x dv, row n, column p
+    float* decay;   // [bh][chunk]
+};
+
+// ---- phase 1 shared memory (bytes) ----
+constexpr uint32_t k1Q = 0;                      // Qr K-major (A of G); then W (A of Y)
+constexpr uint32_t k1K = k1Q + kChunkImg;        // Kr K-major (B of G; A of dS^T as MN-major)
+constexpr uint32_t k1X = k1K + kChunkImg;        // X MN-major (B of Y: m=p, k=j)
+constexpr uint32_t k1Xw = k1X + 128 * 64 * 2;    // w o X MN-major (B of dS^T)
+constexpr uint32_t k1Gate = k1Xw + 128 * 64 * 2; // lcum, scale, gamma, w (fp32 x 128)
+constexpr uint32_t k1Misc = k1Gate + 4 * 128 * 4;
+constexpr uint32_t k1Smem = k1Misc + 64;
+
+__global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs ws, int n_chunks) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    float* lcum = reinterpret_cast<float*>(smem + kOffGate);
+    float* lcum = reinterpret_cast<float*>(smem + k1Gate);
     float* scl = lcum + kTcQ;
     float* gam = scl + kTcQ;
     float* wdec = gam + kTcQ;
-    float* eQ = reinterpret_cast<float*>(smem + kOffMisc);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffMisc + 16);
-    uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc + 32);
+    float* eQ = reinterpret_cast<float*>(smem + k1Misc);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + k1Misc + 16);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + k1Misc + 32);
     const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t bh = blockIdx.x;
     const int64_t H = p.heads, L = p.len;
+    const int64_t bh = blockIdx.x % (p.batch * H);
+    const int ch = static_cast<int>(blockIdx.x / (p.batch * H));
     const int64_t bi = bh / H, h = bh % H;
-    const float dsk = p.d_skip ? p.d_skip[h] : 0.f;
-    const int64_t gate_base = (bi * H + h) * L;
-    const int n_chunks = static_cast<int>((L + kTcQ - 1) / kTcQ);
-    constexpr int half = kTcN / 2;
+    const int64_t bhc = bh * n_chunks + ch;
+    const int64_t gate_base = bh * L;
+    const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
 
-    if (warp == 0) {
-        const uint32_t slot = static_cast<uint32_t>(__cvta_generic_to_shared(tmem_base_slot));
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot),
-                     "r"(kTmemCols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
+    if (warp == 0) tmem_alloc(tmem_slot, 128);
     if (tid == 0) {
         mbar_init(bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+
+    // X items: step j, 8 consecutive channels (one 16-byte chunk of the
+    // MN-major operand); loads issued before the gate pass, stored after
+    constexpr int kXItems = 128 * 8 / kTcThreads2;
+    float xv[kXItems][8];
+#pragma unroll
+    for (int r = 0; r < kXItems; ++r) {
+        const int item = tid + r * kTcThreads2;
+        const int hi = item >> 5;
+        const int j = (hi >> 1) * 8 + (item & 7);
+        const int pc = ((item >> 3) & 3) + 4 * (hi & 1);
+        const int64_t it = it0 + j;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xv[r][e] = 0.f;
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            ldg8(p.v + ((bi * L + t) * H + h) * kTcP + pc * 8, xv[r]);
+        }
+    }
+    if (warp == 0) {
+        // gates: cumulative log decay, trapezoid weights, state weights
+        float lv[4], sc[4], gm[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int64_t it = it0 + lane * 4 + e;
+            lv[e] = sc[e] = gm[e] = 0.f;
+            if (it < L) {
+                const int64_t t = p.reverse ? L - 1 - it : it;
+                const int64_t g = gate_base + t;
+                const float gamma = p.dt[g] * sigmoid_f(p.trap[g]);
+                float shifted = 0.f;
+                if (it + 1 < L) {
+                    const int64_t nx = p.reverse ? g - 1 : g + 1;
+                    shifted = p.dt[nx] * (1.f - sigmoid_f(p.trap[nx]));
+                }
+                lv[e] = p.adt[g];
+                sc[e] = gamma + shifted;
+                gm[e] = gamma;
+            }
+        }
+        lv[1] += lv[0];
+        lv[2] += lv[1];
+        lv[3] += lv[2];
+        float run = lv[3];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float v = __shfl_up_sync(0xffffffffu, run, o);
+            if (lane >= o) run += v;
+        }
+        const float before = run - lv[3];
+        const float last = __shfl_sync(0xffffffffu, run, 31);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int j = lane * 4 + e;
+            const float l = before + lv[e];
+            lcum[j] = l;
+            scl[j] = sc[e];
+            gam[j] = gm[e];
+            wdec[j] = expf(last - l) * sc[e];
+        }
+        if (lane == 0) {
+            eQ[0] = expf(last);
+            ws.decay[bhc] = expf(last);
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < kXItems; ++r) {
+        const int item = tid + r * kTcThreads2;
+        const int hi = item >> 5;
+        const int j = (hi >> 1) * 8 + (item & 7);
+        const int pc = ((item >> 3) & 3) + 4 * (hi & 1);
+        const float w = wdec[j];
+        float xw[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xw[e] = w * xv[r][e];
+        const uint32_t o = mnmaj_off(pc * 8, j, kTcP);
+        *reinterpret_cast<uint4*>(smem + k1X + o) = pack8(xv[r]);
+        *reinterpret_cast<uint4*>(smem + k1Xw + o) = pack8(xw);
+    }
+    // Qr, Kr to shared memory; e^l o Qr to the workspace.  One item
+    // = step j, 8 consecutive dims (4 rotation pairs); a warp covers 8 steps
+    // x 4 dim-chunks, i.e. 128 contiguous bytes of each of 8 input rows.
+    {
+        uint8_t* qs_img = ws.qs + bhc * kChunkImg;
+        const float* qb = p.q_bias + h * kTcN;
+        const float* kb = p.k_bias + h * kTcN;
+        // items r = 2m, 2m+1 share their dim chunk; both are loaded before
+        // either is stored, so each pair costs one memory round trip
+        for (int m = 0; m < 128 * 16 / kTcThreads2 / 2; ++m) {
+            float qa[2][8], ka[2][8], cc[2][4], ss[2][4];
+            int jj[2];
+            int kc = 0;
+            bool live[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int item = tid + (2 * m + u) * kTcThreads2;
+                const int hi = item >> 5;
+                jj[u] = (hi & 15) * 8 + (item & 7);
+                kc = ((item >> 3) & 3) + 4 * (hi >> 4);
+                const int64_t it = it0 + jj[u];
+                live[u] = it < L;
+                const int64_t t = live[u] ? (p.reverse ? L - 1 - it : it) : 0;
+                const int64_t qk = (bi * L + t) * kTcN + kc * 8;
+                const int64_t cs = ((bi * L + t) * H + h) * (kTcN / 2) + kc * 4;
+                ldg8(p.q + qk, qa[u]);
+                ldg8(p.k + qk, ka[u]);
+                const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cos + cs));
+                const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sin + cs));
+                cc[u][0] = c4.x; cc[u][1] = c4.y; cc[u][2] = c4.z; cc[u][3] = c4.w;
+                ss[u][0] = s4.x; ss[u][1] = s4.y; ss[u][2] = s4.z; ss[u][3] = s4.w;
+            }
+            float qbb[8], kbb[8];
+            ldg8(qb + kc * 8, qbb);
+            ldg8(kb + kc * 8, kbb);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int j = jj[u];
+                float qr[8], kr[8], qs[8];
+                const float el = live[u] ? expf(lcum[j]) : 0.f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float a0 = qa[u][2 * e] + qbb[2 * e], a1 = qa[u][2 * e + 1] + qbb[2 * e + 1];
+                    qr[2 * e] = a0 * cc[u][e] - a1 * ss[u][e];
+                    qr[2 * e + 1] = a0 * ss[u][e] + a1 * cc[u][e];
+                    a0 = ka[u][2 * e] + kbb[2 * e];
+                    a1 = ka[u][2 * e + 1] + kbb[2 * e + 1];
+                    kr[2 * e] = a0 * cc[u][e] - a1 * ss[u][e];
+                    kr[2 * e + 1] = a0 * ss[u][e] + a1 * cc[u][e];
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    if (!live[u]) qr[e] = kr[e] = 0.f;
+                    qs[e] = el * qr[e];
+                }
+                const uint32_t ko = kmaj_off(j, kc * 8, 128);
+                *reinterpret_cast<uint4*>(smem + k1Q + ko) = pack8(qr);
+                *reinterpret_cast<uint4*>(smem + k1K + ko) = pack8(kr);
+                *reinterpret_cast<uint4*>(qs_img + ko) = pack8(qs);
+            }
+        }
+    }
+    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_base_slot;
-    const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tG = tmem, tY = tmem + 128, tS = tmem + 192;
-
-    // fp32 state row n = tid of S^T (dqk x dv)
-    float S[kTcP];
-#pragma unroll
-    for (int q = 0; q < kTcP; ++q) S[q] = 0.f;
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int hc = warp >> 2;  // column half of this warp
+    const uint32_t tG = tmem, tY = tmem, tS = tmem + 64;
     uint32_t phase = 0;
-    bool ok_run = true;
+    bool ok = true;
 
-    const uint32_t id_G = instr_desc(128, 128, false, false);
-    const uint32_t id_Y = instr_desc(128, kTcP, false, true);
-    const uint32_t id_S = instr_desc(128, kTcP, true, true);
-
-    for (int ch = 0; ch < n_chunks; ++ch) {
-        const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
-        // ---- gates (warp 0): cumulative log decay, trapezoid weights
-        if (warp == 0) {
-            float lv[4], sc[4], gm[4];
+    if (tid == 0) {
+        const uint32_t id_G = instr_desc(128, 128, false, false);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int j = lane * 4 + e;  // contiguous steps per lane
-                const int64_t it = it0 + j;
-                lv[e] = sc[e] = gm[e] = 0.f;
-                if (it < L) {
-                    const int64_t t = p.reverse ? L - 1 - it : it;
-                    const int64_t g = gate_base + t;
-                    const float gamma = p.dt[g] * sigmoid_f(p.trap[g]);
-                    float shifted = 0.f;
-                    if (it + 1 < L) {
-                        const int64_t nx = p.reverse ? g - 1 : g + 1;
-                        shifted = p.dt[nx] * (1.f - sigmoid_f(p.trap[nx]));
-                    }
-                    lv[e] = p.adt[g];
-                    sc[e] = gamma + shifted;
-                    gm[e] = gamma;
-                }
-            }
-            lv[1] += lv[0];
-            lv[2] += lv[1];
-            lv[3] += lv[2];
-            float run = lv[3];
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const float v = __shfl_up_sync(0xffffffffu, run, o);
-                if (lane >= o) run += v;
-            }
-            const float before = run - lv[3];
-            const float last = __shfl_sync(0xffffffffu, run, 31);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int j = lane * 4 + e;
-                const float l = before + lv[e];
-                lcum[j] = l;
-                scl[j] = sc[e];
-                gam[j] = gm[e];
-                wdec[j] = expf(last - l) * sc[e];
-            }
-            if (lane == 0) eQ[0] = expf(last);
+        for (int kb = 0; kb < kTcN / 16; ++kb) {
+            const uint64_t a = smem_desc(sbase + k1Q + kb * 2 * 16 * 128, 16 * 128, 128);
+            const uint64_t b = smem_desc(sbase + k1K + kb * 2 * 16 * 128, 16 * 128, 128);
+            umma(tG, a, b, id_G, kb > 0);
         }
-        __syncthreads();
-        // ---- operands: rotated q/k rows, e^l q, w k, x (all bf16)
-        for (int idx = tid; idx < kTcQ * half; idx += kTcThreads) {
-            const int j = idx / half, pi = idx % half;
-            const int64_t it = it0 + j;
-            float q0 = 0.f, q1 = 0.f, k0 = 0.f, k1 = 0.f;
-            if (it < L) {
-                const int64_t t = p.reverse ? L - 1 - it : it;
-                const int64_t qk = (bi * L + t) * kTcN;
-                const float* qb = p.q_bias + h * kTcN;
-                const float* kb = p.k_bias + h * kTcN;
-                const int64_t cs = ((bi * L + t) * H + h) * half + pi;
-                const float c = p.cos[cs], s = p.sin[cs];
-                float a0 = p.q[qk + 2 * pi] + qb[2 * pi], a1 = p.q[qk + 2 * pi + 1] + qb[2 * pi + 1];
-                q0 = a0 * c - a1 * s;
-                q1 = a0 * s + a1 * c;
-                a0 = p.k[qk + 2 * pi] + kb[2 * pi];
-                a1 = p.k[qk + 2 * pi + 1] + kb[2 * pi + 1];
-                k0 = a0 * c - a1 * s;
-                k1 = a0 * s + a1 * c;
-            }
-            const float el = it < L ? expf(lcum[j]) : 0.f;
-            const float w = wdec[j];
-            const int n0 = 2 * pi, n1 = 2 * pi + 1;
-            *reinterpret_cast<uint16_t*>(smem + kOffQ + kmaj_off(j, n0, 128)) = bf16_bits(q0);
-            *reinterpret_cast<uint16_t*>(smem + kOffQ + kmaj_off(j, n1, 128)) = bf16_bits(q1);
-            *reinterpret_cast<uint16_t*>(smem + kOffQs + kmaj_off(j, n0, 128)) = bf16_bits(el * q0);
-            *reinterpret_cast<uint16_t*>(smem + kOffQs + kmaj_off(j, n1, 128)) = bf16_bits(el * q1);
-            *reinterpret_cast<uint16_t*>(smem + kOffK + kmaj_off(j, n0, 128)) = bf16_bits(k0);
-            *reinterpret_cast<uint16_t*>(smem + kOffK + kmaj_off(j, n1, 128)) = bf16_bits(k1);
-            *reinterpret_cast<uint16_t*>(smem + kOffKw + mnmaj_off(n0, j, 128)) = bf16_bits(w * k0);
-            *reinterpret_cast<uint16_t*>(smem + kOffKw + mnmaj_off(n1, j, 128)) = bf16_bits(w * k1);
-        }
-        for (int idx = tid; idx < kTcQ * kTcP; idx += kTcThreads) {
-            const int j = idx / kTcP, pp = idx % kTcP;
-            const int64_t it = it0 + j;
-            float v = 0.f;
-            if (it < L) {
-                const int64_t t = p.reverse ? L - 1 - it : it;
-                v = p.v[((bi * L + t) * H + h) * kTcP + pp];
-            }
-            *reinterpret_cast<uint16_t*>(smem + kOffX + mnmaj_off(pp, j, kTcP)) = bf16_bits(v);
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
+        umma_commit(bar);
+    }
+    ok = cta_wait(bar, phase);
+    phase ^= 1;
+    if (ok) {
         tc_fence_after();
-        // ---- G = Qr Kr^T
-        if (tid == 0) {
+        // W = mask o G (row i, columns of this warp's half) over Qr
+        const int i = (warp & 3) * 32 + lane;
+        const float li = lcum[i], gi = gam[i];
 #pragma unroll
-            for (int kb = 0; kb < kTcN / 16; ++kb) {
-                const uint64_t a = smem_desc(sbase + kOffQ + kb * 2 * (128 / 8) * 128, (128 / 8) * 128, 128);
-                const uint64_t b = smem_desc(sbase + kOffK + kb * 2 * (128 / 8) * 128, (128 / 8) * 128, 128);
-                umma(tG, a, b, id_G, kb > 0);
-            }
-            umma_commit(bar);
-        }
-        if (__syncthreads_or(!mbar_wait(bar, phase))) {
-            ok_run = false;
-            if (tid == 0) atomicExch(&g_tc_status, 1);
-            break;
-        }
-        phase ^= 1;
-        tc_fence_after();
-        // ---- W = mask o G -> bf16, row i = tid
-        {
-            const int i = tid;
-            const float li = lcum[i], gi = gam[i];
+        for (int cb = 0; cb < 2; ++cb) {
+            float g[32];
+            tmem_ld32(tG + t_lane + hc * 64 + cb * 32, g);
 #pragma unroll
-            for (int cb = 0; cb < 4; ++cb) {
-                float g[32];
-                tmem_ld32(tG + t_lane + cb * 32, g);
+            for (int c8 = 0; c8 < 4; ++c8) {
+                float wv[8];
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const int j = cb * 32 + c;
+                for (int c = 0; c < 8; ++c) {
+                    const int j = hc * 64 + cb * 32 + c8 * 8 + c;
                     float m = 0.f;
                     if (j < i) m = expf(li - lcum[j]) * scl[j];
                     else if (j == i) m = gi;
-                    *reinterpret_cast<uint16_t*>(smem + kOffW + kmaj_off(i, j, 128)) =
-                        bf16_bits(m * g[c]);
+                    wv[c] = m * g[c8 * 8 + c];
                 }
+                *reinterpret_cast<uint4*>(smem + k1Q + kmaj_off(i, hc * 64 + cb * 32 + c8 * 8, 128)) =
+                    pack8(wv);
             }
         }
-        // S^T (bf16) for Y's inter-chunk term, row n = tid
-#pragma unroll
-        for (int q = 0; q < kTcP; ++q)
-            *reinterpret_cast<uint16_t*>(smem + kOffS + mnmaj_off(q, tid, kTcP)) = bf16_bits(S[q]);
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
-        // ---- Y = W X + (e^l Qr) S^T ; dS^T = (w Kr)^T X
         if (tid == 0) {
+            const uint32_t id_Y = instr_desc(128, kTcP, false, true);
+            const uint32_t id_S = instr_desc(128, kTcP, true, true);
             for (int kb = 0; kb < kTcQ / 16; ++kb) {
-                const uint64_t a = smem_desc(sbase + kOffW + kb * 2 * (128 / 8) * 128, (128 / 8) * 128, 128);
-                const uint64_t b = smem_desc(sbase + kOffX + kb * 2 * (kTcP / 8) * 128, (kTcP / 8) * 128, 128);
+                const uint64_t a = smem_desc(sbase + k1Q + kb * 2 * 16 * 128, 16 * 128, 128);
+                const uint64_t b = smem_desc(sbase + k1X + kb * 2 * 8 * 128, 8 * 128, 128);
                 umma(tY, a, b, id_Y, kb > 0);
             }
-            if (ch > 0) {
-                for (int kb = 0; kb < kTcN / 16; ++kb) {
-                    const uint64_t a = smem_desc(sbase + kOffQs + kb * 2 * (128 / 8) * 128, (128 / 8) * 128, 128);
-                    const uint64_t b = smem_desc(sbase + kOffS + kb * 2 * (kTcP / 8) * 128, (kTcP / 8) * 128, 128);
-                    umma(tY, a, b, id_Y, 1);
-                }
-            }
+            // A = Kr viewed MN-major (m = n, k = j): next 8 n = 2048 B (SBO),
+            // next 8 j = 128 B (LBO); 16 steps of j = 256 B
             for (int kb = 0; kb < kTcQ / 16; ++kb) {
-                const uint64_t a = smem_desc(sbase + kOffKw + kb * 2 * (128 / 8) * 128, (128 / 8) * 128, 128);
-                const uint64_t b = smem_desc(sbase + kOffX + kb * 2 * (kTcP / 8) * 128, (kTcP / 8) * 128, 128);
+                const uint64_t a = smem_desc(sbase + k1K + kb * 2 * 128, 128, 16 * 128);
+                const uint64_t b = smem_desc(sbase + k1Xw + kb * 2 * 8 * 128, 8 * 128, 128);
                 umma(tS, a, b, id_S, kb > 0);
             }
             umma_commit(bar);
         }
-        if (__syncthreads_or(!mbar_wait(bar, phase))) {
-            ok_run = false;
-            if (tid == 0) atomicExch(&g_tc_status, 1);
-            break;
-        }
+        ok = cta_wait(bar, phase);
         phase ^= 1;
+    }
+    if (ok) {
         tc_fence_after();
-        // ---- epilogue: y row i = tid; state row n = tid
+        const int r = (warp & 3) * 32 + lane;  // output row i / state row n
         {
-            const int i = tid;
-            const int64_t it = it0 + i;
-            float y[64];
-            tmem_ld32(tY + t_lane, *reinterpret_cast<float(*)[32]>(y));
-            tmem_ld32(tY + t_lane + 32, *reinterpret_cast<float(*)[32]>(y + 32));
+            float y[32];
+            tmem_ld32(tY + t_lane + hc * 32, y);
+            const int64_t it = it0 + r;
             if (it < L) {
+                const float dsk = p.d_skip ? p.d_skip[h] : 0.f;
                 const int64_t t = p.reverse ? L - 1 - it : it;
-                const int64_t voff = ((bi * L + t) * H + h) * kTcP;
-                float* o = p.out + ((bi * H + h) * L + t) * kTcP;
+                const int64_t voff = ((bi * L + t) * H + h) * kTcP + hc * 32;
+                float* o = p.out + (bh * L + t) * kTcP + hc * 32;
+                const bool gate = p.z && ch == 0;
+                float4 vv[8], zz[8];
 #pragma unroll
-                for (int q = 0; q < kTcP; q += 4) {
-                    const float4 vv = *reinterpret_cast<const float4*>(p.v + voff + q);
-                    float r4[4] = {fmaf(dsk, vv.x, y[q]), fmaf(dsk, vv.y, y[q + 1]),
-                                   fmaf(dsk, vv.z, y[q + 2]), fmaf(dsk, vv.w, y[q + 3])};
-                    if (p.z) {
-                        const float4 zz = *reinterpret_cast<const float4*>(p.z + voff + q);
-                        r4[0] *= silu_f(zz.x);
-                        r4[1] *= silu_f(zz.y);
-                        r4[2] *= silu_f(zz.z);
-                        r4[3] *= silu_f(zz.w);
-                    }
-                    *reinterpret_cast<float4*>(o + q) = make_float4(r4[0], r4[1], r4[2], r4[3]);
+                for (int q = 0; q < 8; ++q) {
+                    vv[q] = __ldg(reinterpret_cast<const float4*>(p.v + voff) + q);
+                    zz[q] = gate ? __ldg(reinterpret_cast<const float4*>(p.z + voff) + q)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-            }
-            float ds[64];
-            tmem_ld32(tS + t_lane, *reinterpret_cast<float(*)[32]>(ds));
-            tmem_ld32(tS + t_lane + 32, *reinterpret_cast<float(*)[32]>(ds + 32));
-            const float e = eQ[0];
 #pragma unroll
-            for (int q = 0; q < kTcP; ++q) S[q] = fmaf(e, S[q], ds[q]);
-            if (p.last_bx && ch == n_chunks - 1) {
-                // scale_T * k_T: rotated k of the final step, fp32 (recomputed)
-                const int jl = static_cast<int>(L - 1 - it0);
-                if (tid < half) {
-                    const int64_t itl = it0 + jl;
-                    const int64_t t = p.reverse ? L - 1 - itl : itl;
-                    const int64_t qk = (bi * L + t) * kTcN;
-                    const float* kb = p.k_bias + h * kTcN;
-                    const int64_t cs = ((bi * L + t) * H + h) * half + tid;
-                    const float c = p.cos[cs], s = p.sin[cs];
-                    const float a0 = p.k[qk + 2 * tid] + kb[2 * tid];
-                    const float a1 = p.k[qk + 2 * tid + 1] + kb[2 * tid + 1];
-                    p.last_bx[bh * kTcN + 2 * tid] = scl[jl] * (a0 * c - a1 * s);
-                    p.last_bx[bh * kTcN + 2 * tid + 1] = scl[jl] * (a0 * s + a1 * c);
+                for (int q = 0; q < 8; ++q) {
+                    float r4[4] = {fmaf(dsk, vv[q].x, y[4 * q]), fmaf(dsk, vv[q].y, y[4 * q + 1]),
+                                   fmaf(dsk, vv[q].z, y[4 * q + 2]), fmaf(dsk, vv[q].w, y[4 * q + 3])};
+                    if (gate) {
+                        r4[0] *= silu_f(zz[q].x);
+                        r4[1] *= silu_f(zz[q].y);
+                        r4[2] *= silu_f(zz[q].z);
+                        r4[3] *= silu_f(zz[q].w);
+                    }
+                    *reinterpret_cast<float4*>(o + 4 * q) = make_float4(r4[0], r4[1], r4[2], r4[3]);
                 }
             }
         }
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-    }
-    if (!ok_run) {
-        // a wait expired: give the MMAs in flight a second bounded wait
-        // before the tensor memory they write is released
-        mbar_wait(bar, phase);
-    } else if (p.last_state) {
+        {
+            float ds[32];
+            tmem_ld32(tS + t_lane + hc * 32, ds);
+            float* st = ws.st + bhc * (kTcN * kTcP) + r * kTcP + hc * 32;
 #pragma unroll
-        for (int q = 0; q < kTcP; ++q) p.last_state[(bh * kTcP + q) * kTcN + tid] = S[q];
+            for (int q = 0; q < 32; q += 4)
+                *reinterpret_cast<float4*>(st + q) = make_float4(ds[q], ds[q + 1], ds[q + 2], ds[q + 3]);
+        }
+        if (p.last_bx && ch == n_chunks - 1 && tid < kTcN / 2) {
+            // scale_T * k_T: rotated k of the final step, fp32
+            const int jl = static_cast<int>(L - 1 - it0);
+            const int64_t t = p.reverse ? 0 : L - 1;
+            const int64_t qk = (bi * L + t) * kTcN;
+            const float* kb = p.k_bias + h * kTcN;
+            const int64_t cs = ((bi * L + t) * H + h) * (kTcN / 2) + tid;
+            const float c = p.cos[cs], s = p.sin[cs];
+            const float a0 = p.k[qk + 2 * tid] + kb[2 * tid];
+            const float a1 = p.k[qk + 2 * tid + 1] + kb[2 * tid + 1];
+            p.last_bx[bh * kTcN + 2 * tid] = scl[jl] * (a0 * c - a1 * s);
+            p.last_bx[bh * kTcN + 2 * tid + 1] = scl[jl] * (a0 * s + a1 * c);
+        }
+    } else {
+        mbar_wait(bar, phase ^ 1);  // MMAs still in flight: bounded second wait
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(kTmemCols));
+        tmem_dealloc(tmem, 128);
+    }
+}
+
+// S_in(0) = 0; S_in(c+1) = decay(c) S_in(c) + dS(c).  Thread owns 4
+// consecutive state entries; slices of 1024 entries per CTA.
+constexpr int kStSlices = (kTcN * kTcP) / (kTcThreads2 * 4);
+
+__global__ void __launch_bounds__(kTcThreads2) m3_tc_state(M3Params p, TcWs ws, int n_chunks) {
+    const int64_t bh = blockIdx.x;
+    const int e0 = (blockIdx.y * kTcThreads2 + threadIdx.x) * 4;
+    float4 S = make_float4(0.f, 0.f, 0.f, 0.f);
+    float* base = ws.st + bh * n_chunks * (kTcN * kTcP) + e0;
+    const float* dec = ws.decay + bh * n_chunks;
+    float4 nd = *reinterpret_cast<const float4*>(base);
+    float nq = dec[0];
+    for (int c = 0; c < n_chunks; ++c) {
+        const float4 d = nd;
+        const float q = nq;
+        if (c + 1 < n_chunks) {
+            nd = *reinterpret_cast<const float4*>(base + static_cast<int64_t>(c + 1) * (kTcN * kTcP));
+            nq = dec[c + 1];
+        }
+        *reinterpret_cast<float4*>(base + static_cast<int64_t>(c) * (kTcN * kTcP)) = S;
+        S.x = fmaf(q, S.x, d.x);
+        S.y = fmaf(q, S.y, d.y);
+        S.z = fmaf(q, S.z, d.z);
+        S.w = fmaf(q, S.w, d.w);
+    }
+    if (p.last_state) {
+        // state entries are (n, p) row-major; last_state is (p, n)
+        const float sv[4] = {S.x, S.y, S.z, S.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int n = (e0 + e) / kTcP, pp = (e0 + e) % kTcP;
+            p.last_state[(bh * kTcP + pp) * kTcN + n] = sv[e];
+        }
+    }
+}
+
+// ---- phase 3 shared memory ----
+constexpr uint32_t k3Qs = 0;                  // e^l Qr K-major (A)
+constexpr uint32_t k3S = kChunkImg;           // S_in^T MN-major (B: m=p, k=n)
+constexpr uint32_t k3Misc = k3S + 128 * 64 * 2;
+constexpr uint32_t k3Smem = k3Misc + 64;
+
+__global__ void __launch_bounds__(kTcThreads2, 4) m3_tc_inter(M3Params p, TcWs ws, int n_chunks) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + k3Misc);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + k3Misc + 16);
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t H = p.heads, L = p.len;
+    const int64_t bh = blockIdx.x % (p.batch * H);
+    const int ch = 1 + static_cast<int>(blockIdx.x / (p.batch * H));
+    const int64_t bi = bh / H, h = bh % H;
+    const int64_t bhc = bh * n_chunks + ch;
+    const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
+
+    if (warp == 0) tmem_alloc(tmem_slot, 64);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(ws.qs + bhc * kChunkImg);
+        uint4* dst = reinterpret_cast<uint4*>(smem + k3Qs);
+#pragma unroll 4
+        for (int i = tid; i < static_cast<int>(kChunkImg / 16); i += kTcThreads2) dst[i] = __ldg(src + i);
+        // S_in^T: 16-byte chunk = state row n, 8 consecutive p
+        const float* st = ws.st + bhc * (kTcN * kTcP);
+#pragma unroll 4
+        for (int item = tid; item < 128 * 8; item += kTcThreads2) {
+            const int hi = item >> 5;
+            const int n = (hi >> 1) * 8 + (item & 7);
+            const int pc = ((item >> 3) & 3) + 4 * (hi & 1);
+            float f[8];
+            ldg8(st + n * kTcP + pc * 8, f);
+            *reinterpret_cast<uint4*>(smem + k3S + mnmaj_off(pc * 8, n, kTcP)) = pack8(f);
+        }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (tid == 0) {
+        const uint32_t id_Y = instr_desc(128, kTcP, false, true);
+#pragma unroll
+        for (int kb = 0; kb < kTcN / 16; ++kb) {
+            const uint64_t a = smem_desc(sbase + k3Qs + kb * 2 * 16 * 128, 16 * 128, 128);
+            const uint64_t b = smem_desc(sbase + k3S + kb * 2 * 8 * 128, 8 * 128, 128);
+            umma(tmem, a, b, id_Y, kb > 0);
+        }
+        umma_commit(bar);
+    }
+    if (cta_wait(bar, 0)) {
+        tc_fence_after();
+        const int i = (warp & 3) * 32 + lane;
+        const int hc = warp >> 2;
+        float y[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + hc * 32, y);
+        const int64_t it = it0 + i;
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            float* o = p.out + (bh * L + t) * kTcP + hc * 32;
+            const float* zr = p.z ? p.z + ((bi * L + t) * H + h) * kTcP + hc * 32 : nullptr;
+#pragma unroll
+            for (int qq = 0; qq < 32; qq += 8) {
+                float4 oo[2], zz[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    oo[u] = *reinterpret_cast<const float4*>(o + qq + 4 * u);
+                    zz[u] = zr ? __ldg(reinterpret_cast<const float4*>(zr + qq + 4 * u))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int q = qq + 4 * u;
+                    float r4[4] = {oo[u].x + y[q], oo[u].y + y[q + 1], oo[u].z + y[q + 2],
+                                   oo[u].w + y[q + 3]};
+                    if (zr) {
+                        r4[0] *= silu_f(zz[u].x);
+                        r4[1] *= silu_f(zz[u].y);
+                        r4[2] *= silu_f(zz[u].z);
+                        r4[3] *= silu_f(zz[u].w);
+                    }
+                    *reinterpret_cast<float4*>(o + q) = make_float4(r4[0], r4[1], r4[2], r4[3]);
+                }
+            }
+        }
+    } else {
+        mbar_wait(bar, 0);  // the MMA still in flight: bounded second wait
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 64);
     }
 }
 
@@ -435,16 +655,89 @@ __global__ void __launch_bounds__(kTcThreads, 1) m3_tc_kernel(M3Params p) {
 
 bool m3_tc_applicable(const M3Params& p) {
     auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
-    return p.psi == nullptr && p.rank == 1 && p.dqk == kTcN && p.dv == kTcP && al(p.v) &&
-           al(p.z) && al(p.out);
+    return p.psi == nullptr && p.rank == 1 && p.dqk == kTcN && p.dv == kTcP && al(p.q) &&
+           al(p.k) && al(p.v) && al(p.z) && al(p.out) && al(p.q_bias) && al(p.k_bias) &&
+           al(p.cos) && al(p.sin) && p.len > 0;
 }
 
-cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
-    cudaError_t e = cudaFuncSetAttribute(m3_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kTcSmem));
+size_t m3_tc_workspace_bytes(const M3Params& p) {
+    const int64_t nc = (p.len + kTcQ - 1) / kTcQ;
+    return static_cast<size_t>(p.batch * p.heads * nc) * (kChunkImg + kChunkSt + 16);
+}
+
+// Per-device memory pool for the workspace.  It keeps what it has reserved
+// (release threshold = max), so repeated calls reuse the same pages instead
+// of mapping fresh ones on every call, as the default pool (threshold 0)
+// does after each synchronization.
+namespace {
+constexpr int kMaxPoolDevices = 64;
+std::mutex g_pool_mu;
+cudaMemPool_t g_pool[kMaxPoolDevices] = {};
+
+cudaError_t workspace_pool(cudaMemPool_t* out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    m3_tc_kernel<<<dim3(static_cast<unsigned>(p.batch * p.heads)), kTcThreads, kTcSmem, stream>>>(p);
-    return cudaGetLastError();
+    if (dev < 0 || dev >= kMaxPoolDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_pool_mu);
+    if (!g_pool[dev]) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.handleTypes = cudaMemHandleTypeNone;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool = nullptr;
+        e = cudaMemPoolCreate(&pool, &props);
+        if (e != cudaSuccess) return e;
+        uint64_t keep = ~0ull;
+        e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        if (e != cudaSuccess) {
+            cudaMemPoolDestroy(pool);
+            return e;
+        }
+        g_pool[dev] = pool;
+    }
+    *out = g_pool[dev];
+    return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
+    const int64_t bh = p.batch * p.heads;
+    const int n_chunks = static_cast<int>((p.len + kTcQ - 1) / kTcQ);
+    cudaError_t e = cudaFuncSetAttribute(m3_tc_intra, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(k1Smem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(m3_tc_intra, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(m3_tc_inter, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(k3Smem));
+    if (e != cudaSuccess) return e;
+    // stream-ordered workspace: valid under stream capture, freed after use
+    void* raw = nullptr;
+    cudaMemPool_t pool = nullptr;
+    e = workspace_pool(&pool);
+    if (e != cudaSuccess) return e;
+    e = cudaMallocFromPoolAsync(&raw, m3_tc_workspace_bytes(p), pool, stream);
+    if (e != cudaSuccess) return e;
+    const size_t units = static_cast<size_t>(bh) * n_chunks;
+    TcWs ws;
+    ws.qs = static_cast<uint8_t*>(raw);
+    ws.st = reinterpret_cast<float*>(ws.qs + units * kChunkImg);
+    ws.decay = ws.st + units * (kTcN * kTcP);
+    m3_tc_intra<<<static_cast<unsigned>(units), kTcThreads2, k1Smem, stream>>>(p, ws, n_chunks);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) {
+        m3_tc_state<<<dim3(static_cast<unsigned>(bh), kStSlices), kTcThreads2, 0, stream>>>(p, ws, n_chunks);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess && n_chunks > 1) {
+        m3_tc_inter<<<static_cast<unsigned>(bh * (n_chunks - 1)), kTcThreads2, k3Smem, stream>>>(
+            p, ws, n_chunks);
+        e = cudaGetLastError();
+    }
+    const cudaError_t ef = cudaFreeAsync(raw, stream);
+    return e != cudaSuccess ? e : ef;
 }
 
 int m3_tc_status_and_clear() {
