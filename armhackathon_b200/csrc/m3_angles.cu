@@ -23,6 +23,11 @@ namespace {
 constexpr int kAgChunk = 128;
 constexpr float kPi = 3.14159265358979323846f;
 
+// Loads of a group of kAgUnroll steps are all issued before any of its
+// arithmetic (and, in phase 2, before its stores), so each group costs one
+// memory round trip.
+constexpr int kAgUnroll = 8;
+
 __global__ void angle_chunk_sums(AngleParams a, float* ws) {
     const int64_t bh = blockIdx.y;
     const int c = blockIdx.x;
@@ -31,10 +36,20 @@ __global__ void angle_chunk_sums(AngleParams a, float* ws) {
     const int64_t b = bh / a.heads, h = bh % a.heads;
     const int64_t t0 = static_cast<int64_t>(c) * kAgChunk;
     const int64_t t1 = t0 + kAgChunk < a.len ? t0 + kAgChunk : a.len;
+    const float* ang = a.angles + ((b * a.len) * a.heads + h) * a.n_angles + p;
+    const int64_t ang_step = a.heads * a.n_angles;
+    const float* dt = a.dt + (b * a.heads + h) * a.len;
     float s = 0.f;
-    for (int64_t t = t0; t < t1; ++t) {
-        const float ang = a.angles[((b * a.len + t) * a.heads + h) * a.n_angles + p];
-        s = fmaf(tanhf(ang) * kPi, a.dt[(b * a.heads + h) * a.len + t], s);
+    for (int64_t t = t0; t < t1; t += kAgUnroll) {
+        float av[kAgUnroll], dv[kAgUnroll];
+#pragma unroll
+        for (int u = 0; u < kAgUnroll; ++u) {
+            const bool in = t + u < t1;
+            av[u] = in ? __ldg(ang + (t + u) * ang_step) : 0.f;
+            dv[u] = in ? __ldg(dt + t + u) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kAgUnroll; ++u) s = fmaf(tanhf(av[u]) * kPi, dv[u], s);
     }
     ws[(bh * gridDim.x + c) * a.n_angles + p] = s;
 }
@@ -47,24 +62,38 @@ __global__ void angle_chunk_write(AngleParams a, const float* ws) {
     const int64_t b = bh / a.heads, h = bh % a.heads;
     const int64_t t0 = static_cast<int64_t>(c) * kAgChunk;
     const int64_t t1 = t0 + kAgChunk < a.len ? t0 + kAgChunk : a.len;
+    const int64_t out_step = a.heads * a.half;
+    float* cs_out = a.cos + ((b * a.len) * a.heads + h) * a.half + p;
+    float* sn_out = a.sin + ((b * a.len) * a.heads + h) * a.half + p;
     if (p >= a.n_angles) {
         for (int64_t t = t0; t < t1; ++t) {
-            const int64_t o = ((b * a.len + t) * a.heads + h) * a.half + p;
-            a.cos[o] = 1.f;
-            a.sin[o] = 0.f;
+            cs_out[t * out_step] = 1.f;
+            sn_out[t * out_step] = 0.f;
         }
         return;
     }
     float theta = 0.f;
-    for (int j = 0; j < c; ++j) theta += ws[(bh * gridDim.x + j) * a.n_angles + p];
-    for (int64_t t = t0; t < t1; ++t) {
-        const float ang = a.angles[((b * a.len + t) * a.heads + h) * a.n_angles + p];
-        theta = fmaf(tanhf(ang) * kPi, a.dt[(b * a.heads + h) * a.len + t], theta);
-        float sn, cs;
-        sincosf(theta, &sn, &cs);
-        const int64_t o = ((b * a.len + t) * a.heads + h) * a.half + p;
-        a.cos[o] = cs;
-        a.sin[o] = sn;
+    for (int j = 0; j < c; ++j) theta += __ldg(ws + (bh * gridDim.x + j) * a.n_angles + p);
+    const float* ang = a.angles + ((b * a.len) * a.heads + h) * a.n_angles + p;
+    const int64_t ang_step = a.heads * a.n_angles;
+    const float* dt = a.dt + (b * a.heads + h) * a.len;
+    for (int64_t t = t0; t < t1; t += kAgUnroll) {
+        float av[kAgUnroll], dv[kAgUnroll];
+#pragma unroll
+        for (int u = 0; u < kAgUnroll; ++u) {
+            const bool in = t + u < t1;
+            av[u] = in ? __ldg(ang + (t + u) * ang_step) : 0.f;
+            dv[u] = in ? __ldg(dt + t + u) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kAgUnroll; ++u) {
+            if (t + u >= t1) break;
+            theta = fmaf(tanhf(av[u]) * kPi, dv[u], theta);
+            float sn, cs;
+            sincosf(theta, &sn, &cs);
+            cs_out[(t + u) * out_step] = cs;
+            sn_out[(t + u) * out_step] = sn;
+        }
     }
 }
 

@@ -152,8 +152,10 @@ __device__ __forceinline__ uint16_t bf16_bits(float x) {
 }
 
 
+// one cvt.rn.bf16x2.f32 (round to nearest even, as bf16_bits)
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    return static_cast<uint32_t>(bf16_bits(lo)) | (static_cast<uint32_t>(bf16_bits(hi)) << 16);
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
 }
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
     return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
@@ -173,6 +175,11 @@ __device__ __forceinline__ void ldg8(const float* g, float (&f)[8]) {
     f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
 
+// bulk prefetch of [g, g + bytes) into L2 (16-byte aligned, multiple of 16)
+__device__ __forceinline__ void prefetch_l2(const void* g, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(g), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
     const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(slot));
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s), "r"(cols));
@@ -182,9 +189,11 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t tmem, uint32_t cols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols));
 }
 
-// CTA-uniform bounded wait; false (and the status flag set) on expiry
+// CTA-uniform bounded wait; false (and the status flag set) on expiry.
+// Thread 0 polls; the others wait at the barrier without taking issue slots.
 __device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity) {
-    const bool expired = __syncthreads_or(!mbar_wait(bar, parity));
+    const bool mine = threadIdx.x == 0 ? !mbar_wait(bar, parity) : false;
+    const bool expired = __syncthreads_or(mine);
     if (expired && threadIdx.x == 0) atomicExch(&g_tc_status, 1);
     return !expired;
 }
@@ -209,174 +218,58 @@ constexpr uint32_t k1Gate = k1Xw + 128 * 64 * 2; // lcum, scale, gamma, w (fp32 
 constexpr uint32_t k1Misc = k1Gate + 4 * 128 * 4;
 constexpr uint32_t k1Smem = k1Misc + 64;
 
+// Requests every row tile `tile` will read from DRAM into L2 (each row is a
+// separate 256- or 512-byte piece), so that its loads, issued one tile
+// later, hit L2.
+__device__ __forceinline__ void intra_prefetch(const M3Params& p, int64_t tile, int n_chunks) {
+    const int64_t BH = p.batch * p.heads, H = p.heads, L = p.len;
+    const int64_t bh = tile % BH;
+    const int64_t bi = bh / H, h = bh % H;
+    const int ch = static_cast<int>(tile / BH);
+    const int tid = threadIdx.x, j = tid & 127;
+    const int64_t it = static_cast<int64_t>(ch) * kTcQ + j;
+    if (it >= L) return;
+    const int64_t t = p.reverse ? L - 1 - it : it;
+    const int64_t row = (bi * L + t) * H + h;
+    if (tid < 128) {
+        prefetch_l2(p.v + row * kTcP, kTcP * 4);
+        prefetch_l2(p.cos + row * (kTcN / 2), kTcN * 2);
+        prefetch_l2(p.sin + row * (kTcN / 2), kTcN * 2);
+    } else {
+        if (h == 0) {  // q, k rows are shared by all heads
+            prefetch_l2(p.q + (bi * L + t) * kTcN, kTcN * 4);
+            prefetch_l2(p.k + (bi * L + t) * kTcN, kTcN * 4);
+        }
+        if (p.z && ch == 0) prefetch_l2(p.z + row * kTcP, kTcP * 4);
+    }
+    (void)n_chunks;
+}
+
+// Persistent: CTA b handles tiles b, b + gridDim.x, ... (tile = chunk *
+// batch*heads + batch*head), prefetching each next tile while it works on
+// the current one.  Gates are kept in log2 units (l2 = l * log2 e) so every
+// decay factor is one ex2.
 __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs ws, int n_chunks) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    float* lcum = reinterpret_cast<float*>(smem + k1Gate);
+    float* lcum = reinterpret_cast<float*>(smem + k1Gate);  // log2 units
     float* scl = lcum + kTcQ;
     float* gam = scl + kTcQ;
     float* wdec = gam + kTcQ;
-    float* eQ = reinterpret_cast<float*>(smem + k1Misc);
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + k1Misc + 16);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + k1Misc + 32);
     const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    constexpr float kLog2eF = 1.4426950408889634f;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t H = p.heads, L = p.len;
-    const int64_t bh = blockIdx.x % (p.batch * H);
-    const int ch = static_cast<int>(blockIdx.x / (p.batch * H));
-    const int64_t bi = bh / H, h = bh % H;
-    const int64_t bhc = bh * n_chunks + ch;
-    const int64_t gate_base = bh * L;
-    const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
+    const int64_t H = p.heads, L = p.len, BH = p.batch * p.heads;
+    const int64_t n_tiles = BH * n_chunks;
 
     if (warp == 0) tmem_alloc(tmem_slot, 128);
     if (tid == 0) {
         mbar_init(bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-
-    // X items: step j, 8 consecutive channels (one 16-byte chunk of the
-    // MN-major operand); loads issued before the gate pass, stored after
-    constexpr int kXItems = 128 * 8 / kTcThreads2;
-    float xv[kXItems][8];
-#pragma unroll
-    for (int r = 0; r < kXItems; ++r) {
-        const int item = tid + r * kTcThreads2;
-        const int hi = item >> 5;
-        const int j = (hi >> 1) * 8 + (item & 7);
-        const int pc = ((item >> 3) & 3) + 4 * (hi & 1);
-        const int64_t it = it0 + j;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) xv[r][e] = 0.f;
-        if (it < L) {
-            const int64_t t = p.reverse ? L - 1 - it : it;
-            ldg8(p.v + ((bi * L + t) * H + h) * kTcP + pc * 8, xv[r]);
-        }
-    }
-    if (warp == 0) {
-        // gates: cumulative log decay, trapezoid weights, state weights
-        float lv[4], sc[4], gm[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int64_t it = it0 + lane * 4 + e;
-            lv[e] = sc[e] = gm[e] = 0.f;
-            if (it < L) {
-                const int64_t t = p.reverse ? L - 1 - it : it;
-                const int64_t g = gate_base + t;
-                const float gamma = p.dt[g] * sigmoid_f(p.trap[g]);
-                float shifted = 0.f;
-                if (it + 1 < L) {
-                    const int64_t nx = p.reverse ? g - 1 : g + 1;
-                    shifted = p.dt[nx] * (1.f - sigmoid_f(p.trap[nx]));
-                }
-                lv[e] = p.adt[g];
-                sc[e] = gamma + shifted;
-                gm[e] = gamma;
-            }
-        }
-        lv[1] += lv[0];
-        lv[2] += lv[1];
-        lv[3] += lv[2];
-        float run = lv[3];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float v = __shfl_up_sync(0xffffffffu, run, o);
-            if (lane >= o) run += v;
-        }
-        const float before = run - lv[3];
-        const float last = __shfl_sync(0xffffffffu, run, 31);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int j = lane * 4 + e;
-            const float l = before + lv[e];
-            lcum[j] = l;
-            scl[j] = sc[e];
-            gam[j] = gm[e];
-            wdec[j] = expf(last - l) * sc[e];
-        }
-        if (lane == 0) {
-            eQ[0] = expf(last);
-            ws.decay[bhc] = expf(last);
-        }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < kXItems; ++r) {
-        const int item = tid + r * kTcThreads2;
-        const int hi = item >> 5;
-        const int j = (hi >> 1) * 8 + (item & 7);
-        const int pc = ((item >> 3) & 3) + 4 * (hi & 1);
-        const float w = wdec[j];
-        float xw[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) xw[e] = w * xv[r][e];
-        const uint32_t o = mnmaj_off(pc * 8, j, kTcP);
-        *reinterpret_cast<uint4*>(smem + k1X + o) = pack8(xv[r]);
-        *reinterpret_cast<uint4*>(smem + k1Xw + o) = pack8(xw);
-    }
-    // Qr, Kr to shared memory; e^l o Qr to the workspace.  One item
-    // = step j, 8 consecutive dims (4 rotation pairs); a warp covers 8 steps
-    // x 4 dim-chunks, i.e. 128 contiguous bytes of each of 8 input rows.
-    {
-        uint8_t* qs_img = ws.qs + bhc * kChunkImg;
-        const float* qb = p.q_bias + h * kTcN;
-        const float* kb = p.k_bias + h * kTcN;
-        // items r = 2m, 2m+1 share their dim chunk; both are loaded before
-        // either is stored, so each pair costs one memory round trip
-        for (int m = 0; m < 128 * 16 / kTcThreads2 / 2; ++m) {
-            float qa[2][8], ka[2][8], cc[2][4], ss[2][4];
-            int jj[2];
-            int kc = 0;
-            bool live[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int item = tid + (2 * m + u) * kTcThreads2;
-                const int hi = item >> 5;
-                jj[u] = (hi & 15) * 8 + (item & 7);
-                kc = ((item >> 3) & 3) + 4 * (hi >> 4);
-                const int64_t it = it0 + jj[u];
-                live[u] = it < L;
-                const int64_t t = live[u] ? (p.reverse ? L - 1 - it : it) : 0;
-                const int64_t qk = (bi * L + t) * kTcN + kc * 8;
-                const int64_t cs = ((bi * L + t) * H + h) * (kTcN / 2) + kc * 4;
-                ldg8(p.q + qk, qa[u]);
-                ldg8(p.k + qk, ka[u]);
-                const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cos + cs));
-                const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sin + cs));
-                cc[u][0] = c4.x; cc[u][1] = c4.y; cc[u][2] = c4.z; cc[u][3] = c4.w;
-                ss[u][0] = s4.x; ss[u][1] = s4.y; ss[u][2] = s4.z; ss[u][3] = s4.w;
-            }
-            float qbb[8], kbb[8];
-            ldg8(qb + kc * 8, qbb);
-            ldg8(kb + kc * 8, kbb);
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int j = jj[u];
-                float qr[8], kr[8], qs[8];
-                const float el = live[u] ? expf(lcum[j]) : 0.f;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    float a0 = qa[u][2 * e] + qbb[2 * e], a1 = qa[u][2 * e + 1] + qbb[2 * e + 1];
-                    qr[2 * e] = a0 * cc[u][e] - a1 * ss[u][e];
-                    qr[2 * e + 1] = a0 * ss[u][e] + a1 * cc[u][e];
-                    a0 = ka[u][2 * e] + kbb[2 * e];
-                    a1 = ka[u][2 * e + 1] + kbb[2 * e + 1];
-                    kr[2 * e] = a0 * cc[u][e] - a1 * ss[u][e];
-                    kr[2 * e + 1] = a0 * ss[u][e] + a1 * cc[u][e];
-                }
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    if (!live[u]) qr[e] = kr[e] = 0.f;
-                    qs[e] = el * qr[e];
-                }
-                const uint32_t ko = kmaj_off(j, kc * 8, 128);
-                *reinterpret_cast<uint4*>(smem + k1Q + ko) = pack8(qr);
-                *reinterpret_cast<uint4*>(smem + k1K + ko) = pack8(kr);
-                *reinterpret_cast<uint4*>(qs_img + ko) = pack8(qs);
-            }
-        }
-    }
-    fence_async_smem();
+    if (blockIdx.x < n_tiles) intra_prefetch(p, blockIdx.x, n_chunks);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -387,40 +280,199 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs w
     uint32_t phase = 0;
     bool ok = true;
 
-    if (tid == 0) {
-        const uint32_t id_G = instr_desc(128, 128, false, false);
+    for (int64_t tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+        if (tile + gridDim.x < n_tiles) intra_prefetch(p, tile + gridDim.x, n_chunks);
+        const int64_t bh = tile % BH;
+        const int ch = static_cast<int>(tile / BH);
+        const int64_t bi = bh / H, h = bh % H;
+        const int64_t bhc = bh * n_chunks + ch;
+        const int64_t gate_base = bh * L;
+        const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
+
+        // X items: step j, 8 consecutive channels (one 16-byte chunk of the
+        // MN-major operand); loads issued before the gate pass, stored after
+        constexpr int kXItems = 128 * 8 / kTcThreads2;
+        float xv[kXItems][8];
 #pragma unroll
-        for (int kb = 0; kb < kTcN / 16; ++kb) {
-            const uint64_t a = smem_desc(sbase + k1Q + kb * 2 * 16 * 128, 16 * 128, 128);
-            const uint64_t b = smem_desc(sbase + k1K + kb * 2 * 16 * 128, 16 * 128, 128);
-            umma(tG, a, b, id_G, kb > 0);
+        for (int r = 0; r < kXItems; ++r) {
+            const int item = tid + r * kTcThreads2;
+            const int hi = item >> 5;
+            const int j = (hi >> 1) * 8 + (item & 7);
+            const int pc = ((item >> 3) & 3) + 4 * (hi & 1);
+            const int64_t it = it0 + j;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xv[r][e] = 0.f;
+            if (it < L) {
+                const int64_t t = p.reverse ? L - 1 - it : it;
+                ldg8(p.v + ((bi * L + t) * H + h) * kTcP + pc * 8, xv[r]);
+            }
         }
-        umma_commit(bar);
-    }
-    ok = cta_wait(bar, phase);
-    phase ^= 1;
-    if (ok) {
-        tc_fence_after();
-        // W = mask o G (row i, columns of this warp's half) over Qr
-        const int i = (warp & 3) * 32 + lane;
-        const float li = lcum[i], gi = gam[i];
+        if (warp == 0) {
+            // gates: cumulative log2 decay, trapezoid weights, state weights
+            float lv[4], sc[4], gm[4];
 #pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {
-            float g[32];
-            tmem_ld32(tG + t_lane + hc * 64 + cb * 32, g);
-#pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
-                float wv[8];
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const int j = hc * 64 + cb * 32 + c8 * 8 + c;
-                    float m = 0.f;
-                    if (j < i) m = expf(li - lcum[j]) * scl[j];
-                    else if (j == i) m = gi;
-                    wv[c] = m * g[c8 * 8 + c];
+            for (int e = 0; e < 4; ++e) {
+                const int64_t it = it0 + lane * 4 + e;
+                lv[e] = sc[e] = gm[e] = 0.f;
+                if (it < L) {
+                    const int64_t t = p.reverse ? L - 1 - it : it;
+                    const int64_t g = gate_base + t;
+                    const float gamma = __ldg(p.dt + g) * sigmoid_f(__ldg(p.trap + g));
+                    float shifted = 0.f;
+                    if (it + 1 < L) {
+                        const int64_t nx = p.reverse ? g - 1 : g + 1;
+                        shifted = __ldg(p.dt + nx) * (1.f - sigmoid_f(__ldg(p.trap + nx)));
+                    }
+                    lv[e] = __ldg(p.adt + g) * kLog2eF;
+                    sc[e] = gamma + shifted;
+                    gm[e] = gamma;
                 }
-                *reinterpret_cast<uint4*>(smem + k1Q + kmaj_off(i, hc * 64 + cb * 32 + c8 * 8, 128)) =
-                    pack8(wv);
+            }
+            lv[1] += lv[0];
+            lv[2] += lv[1];
+            lv[3] += lv[2];
+            float run = lv[3];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float v = __shfl_up_sync(0xffffffffu, run, o);
+                if (lane >= o) run += v;
+            }
+            const float before = run - lv[3];
+            const float last = __shfl_sync(0xffffffffu, run, 31);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = lane * 4 + e;
+                const float l = before + lv[e];
+                lcum[j] = l;
+                scl[j] = sc[e];
+                gam[j] = gm[e];
+                wdec[j] = ex2_approx(last - l) * sc[e];
+            }
+            if (lane == 0) ws.decay[bhc] = ex2_approx(last);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < kXItems; ++r) {
+            const int item = tid + r * kTcThreads2;
+            const int hi = item >> 5;
+            const int j = (hi >> 1) * 8 + (item & 7);
+            const int pc = ((item >> 3) & 3) + 4 * (hi & 1);
+            const float w = wdec[j];
+            float xw[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xw[e] = w * xv[r][e];
+            const uint32_t o = mnmaj_off(pc * 8, j, kTcP);
+            *reinterpret_cast<uint4*>(smem + k1X + o) = pack8(xv[r]);
+            *reinterpret_cast<uint4*>(smem + k1Xw + o) = pack8(xw);
+        }
+        // Qr, Kr to shared memory; e^l o Qr to the workspace.  One item =
+        // step j, 8 consecutive dims (4 rotation pairs); a warp covers 8
+        // steps x 4 dim-chunks, i.e. 128 contiguous bytes of each input row.
+        {
+            uint8_t* qs_img = ws.qs + bhc * kChunkImg;
+            const float* qb = p.q_bias + h * kTcN;
+            const float* kb = p.k_bias + h * kTcN;
+            // items r = 2m, 2m+1 share their dim chunk; both are loaded
+            // before either is stored: one memory round trip per pair
+            for (int m = 0; m < 128 * 16 / kTcThreads2 / 2; ++m) {
+                float qa[2][8], ka[2][8], cc[2][4], ss[2][4];
+                int jj[2];
+                int kc = 0;
+                bool live[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int item = tid + (2 * m + u) * kTcThreads2;
+                    const int hi = item >> 5;
+                    jj[u] = (hi & 15) * 8 + (item & 7);
+                    kc = ((item >> 3) & 3) + 4 * (hi >> 4);
+                    const int64_t it = it0 + jj[u];
+                    live[u] = it < L;
+                    const int64_t t = live[u] ? (p.reverse ? L - 1 - it : it) : 0;
+                    const int64_t qk = (bi * L + t) * kTcN + kc * 8;
+                    const int64_t cs = ((bi * L + t) * H + h) * (kTcN / 2) + kc * 4;
+                    ldg8(p.q + qk, qa[u]);
+                    ldg8(p.k + qk, ka[u]);
+                    const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cos + cs));
+                    const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sin + cs));
+                    cc[u][0] = c4.x; cc[u][1] = c4.y; cc[u][2] = c4.z; cc[u][3] = c4.w;
+                    ss[u][0] = s4.x; ss[u][1] = s4.y; ss[u][2] = s4.z; ss[u][3] = s4.w;
+                }
+                float qbb[8], kbb[8];
+                ldg8(qb + kc * 8, qbb);
+                ldg8(kb + kc * 8, kbb);
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int j = jj[u];
+                    float qr[8], kr[8], qs[8];
+                    const float el = live[u] ? ex2_approx(lcum[j]) : 0.f;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        float a0 = qa[u][2 * e] + qbb[2 * e], a1 = qa[u][2 * e + 1] + qbb[2 * e + 1];
+                        qr[2 * e] = a0 * cc[u][e] - a1 * ss[u][e];
+                        qr[2 * e + 1] = a0 * ss[u][e] + a1 * cc[u][e];
+                        a0 = ka[u][2 * e] + kbb[2 * e];
+                        a1 = ka[u][2 * e + 1] + kbb[2 * e + 1];
+                        kr[2 * e] = a0 * cc[u][e] - a1 * ss[u][e];
+                        kr[2 * e + 1] = a0 * ss[u][e] + a1 * cc[u][e];
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        if (!live[u]) qr[e] = kr[e] = 0.f;
+                        qs[e] = el * qr[e];
+                    }
+                    const uint32_t ko = kmaj_off(j, kc * 8, 128);
+                    *reinterpret_cast<uint4*>(smem + k1Q + ko) = pack8(qr);
+                    *reinterpret_cast<uint4*>(smem + k1K + ko) = pack8(kr);
+                    *reinterpret_cast<uint4*>(qs_img + ko) = pack8(qs);
+                }
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+
+        if (tid == 0) {
+            const uint32_t id_G = instr_desc(128, 128, false, false);
+#pragma unroll
+            for (int kb = 0; kb < kTcN / 16; ++kb) {
+                const uint64_t a = smem_desc(sbase + k1Q + kb * 2 * 16 * 128, 16 * 128, 128);
+                const uint64_t b = smem_desc(sbase + k1K + kb * 2 * 16 * 128, 16 * 128, 128);
+                umma(tG, a, b, id_G, kb > 0);
+            }
+            umma_commit(bar);
+        }
+        ok = cta_wait(bar, phase);
+        phase ^= 1;
+        if (!ok) break;
+        tc_fence_after();
+        {
+            // W = mask o G (row i, columns of this warp's half) over Qr
+            const int i = (warp & 3) * 32 + lane;
+            const float li = lcum[i], gi = gam[i];
+#pragma unroll
+            for (int cb = 0; cb < 2; ++cb) {
+                float g[32];
+                tmem_ld32(tG + t_lane + hc * 64 + cb * 32, g);
+#pragma unroll
+                for (int c8 = 0; c8 < 4; ++c8) {
+                    const int j0 = hc * 64 + cb * 32 + c8 * 8;
+                    const float4 la = *reinterpret_cast<const float4*>(lcum + j0);
+                    const float4 lb = *reinterpret_cast<const float4*>(lcum + j0 + 4);
+                    const float4 sa = *reinterpret_cast<const float4*>(scl + j0);
+                    const float4 sb = *reinterpret_cast<const float4*>(scl + j0 + 4);
+                    const float lj[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+                    const float sj[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+                    float wv[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const int j = j0 + c;
+                        // lcum is non-increasing, so li - lj <= 0 for j < i
+                        const float m = j < i ? ex2_approx(li - lj[c]) * sj[c] : (j == i ? gi : 0.f);
+                        wv[c] = m * g[c8 * 8 + c];
+                    }
+                    *reinterpret_cast<uint4*>(smem + k1Q + kmaj_off(i, j0, 128)) = pack8(wv);
+                }
             }
         }
         fence_async_smem();
@@ -446,8 +498,7 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs w
         }
         ok = cta_wait(bar, phase);
         phase ^= 1;
-    }
-    if (ok) {
+        if (!ok) break;
         tc_fence_after();
         const int r = (warp & 3) * 32 + lane;  // output row i / state row n
         {
@@ -502,9 +553,12 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs w
             p.last_bx[bh * kTcN + 2 * tid] = scl[jl] * (a0 * c - a1 * s);
             p.last_bx[bh * kTcN + 2 * tid + 1] = scl[jl] * (a0 * s + a1 * c);
         }
-    } else {
-        mbar_wait(bar, phase ^ 1);  // MMAs still in flight: bounded second wait
+        // the next tile overwrites shared memory and tensor memory
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
     }
+    if (!ok) mbar_wait(bar, phase ^ 1);  // MMAs still in flight: bounded second wait
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -568,6 +622,21 @@ __global__ void __launch_bounds__(kTcThreads2, 4) m3_tc_inter(M3Params p, TcWs w
     const int64_t bhc = bh * n_chunks + ch;
     const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
 
+    {
+        const int j = tid & 127;
+        const int64_t it = it0 + j;
+        if (tid < 128) {
+            if (it < L) {
+                const int64_t t = p.reverse ? L - 1 - it : it;
+                prefetch_l2(p.out + (bh * L + t) * kTcP, kTcP * 4);
+                if (p.z) prefetch_l2(p.z + ((bi * L + t) * H + h) * kTcP, kTcP * 4);
+            }
+        } else if (tid < 136) {
+            const int q = tid - 128;  // 8 pieces of 4 KB of each image
+            prefetch_l2(ws.qs + bhc * kChunkImg + q * 4096, 4096);
+            prefetch_l2(reinterpret_cast<const uint8_t*>(ws.st + bhc * (kTcN * kTcP)) + q * 4096, 4096);
+        }
+    }
     if (warp == 0) tmem_alloc(tmem_slot, 64);
     if (tid == 0) {
         mbar_init(bar, 1);
@@ -725,7 +794,11 @@ cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
     ws.qs = static_cast<uint8_t*>(raw);
     ws.st = reinterpret_cast<float*>(ws.qs + units * kChunkImg);
     ws.decay = ws.st + units * (kTcN * kTcP);
-    m3_tc_intra<<<static_cast<unsigned>(units), kTcThreads2, k1Smem, stream>>>(p, ws, n_chunks);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const size_t grid1 = units < static_cast<size_t>(2 * sms) ? units : static_cast<size_t>(2 * sms);
+    m3_tc_intra<<<static_cast<unsigned>(grid1), kTcThreads2, k1Smem, stream>>>(p, ws, n_chunks);
     e = cudaGetLastError();
     if (e == cudaSuccess) {
         m3_tc_state<<<dim3(static_cast<unsigned>(bh), kStSlices), kTcThreads2, 0, stream>>>(p, ws, n_chunks);
