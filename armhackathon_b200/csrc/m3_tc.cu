@@ -2,27 +2,23 @@
 // operands with fp32 accumulation in tensor memory; selected with backend 3.
 //
 // Same chunked dual form as m3_chunk.cu (see its header for the algebra),
-// with chunks of QC = 128 steps so every product is an M = 128 UMMA, split
-// into three launches so every chunk of every (batch, head) runs in parallel:
+// with chunks of QC = 128 steps so every product is an M = 128 UMMA, in
+// three launches so every chunk of every (batch, head) runs in parallel:
 //
-//  1. m3_tc_intra, one CTA per (batch*head, chunk), independent:
-//       G    = Qr Kr^T            M=128 (i) N=128 (j) K=dqk -> TMEM cols [0,128)
-//       W    = mask(l, scale, gamma) o G -> bf16, over Qr in shared memory
-//       Y    = W X                M=128 (i) N=dv  K=128     -> TMEM cols [0,64)
-//       dS^T = Kr^T (w o X)       M=128 (n) N=dv  K=128     -> TMEM cols [64,128)
-//     (Kr's K-major core matrices for G are byte for byte the MN-major A
-//     operand of dS^T; only the descriptor strides differ, so one copy
-//     serves both)
-//     writes y_intra + D x to out (gated by silu(z) already for chunk 0,
-//     whose entering state is zero), dS^T (fp32) and e^l o Qr (bf16, in
-//     its shared-memory operand image) to the workspace, and the chunk's
-//     total decay e^{l_last}.
-//  2. m3_tc_state: per (batch*head, slice of the state), walks the chunks
-//     S_in(c+1) = e^{l_last(c)} S_in(c) + dS(c) in fp32, overwriting dS(c)
-//     with S_in(c); the final state is last_state.
-//  3. m3_tc_inter, one CTA per (batch*head, chunk >= 1):
-//       Y   += (e^l o Qr) S_in^T  M=128 (i) N=dv  K=dqk      -> TMEM cols [0,64)
-//     then silu(z) gating and the final store.
+//  A. m3_tc_dstate, one CTA per (batch*head, chunk):
+//       dS^T = Kr^T (w o X)      M=128 (n) N=dv K=128 (steps) -> TMEM
+//     to the workspace in fp32, with the chunk's total decay 2^{l2_last}.
+//     (Kr's K-major core matrices are byte for byte the MN-major A operand
+//     of dS^T; only the descriptor strides differ.)
+//  B. m3_tc_state: per (batch*head, slice of the state), walks the chunks
+//     S_in(c+1) = 2^{l2_last(c)} S_in(c) + dS(c) in fp32 and writes S_in(c)
+//     as chunk c's bf16 operand image; the final state is last_state.
+//  C. m3_tc_out, persistent, per (batch*head, chunk):
+//       G = Qr Kr^T              M=128 (i) N=128 (j) K=dqk
+//       Z = Qr S_in^T            M=128 (i) N=dv      K=dqk   (chunk > 0)
+//       W = mask(l, scale, gamma) o G -> bf16, over Qr in shared memory
+//       Y = W X                  M=128 (i) N=dv      K=128
+//       y = (Y + 2^{l2_i} Z + D x) * silu(z)
 // Operands use the canonical no-swizzle layouts (8-row x 16-byte core
 // matrices); every operand is staged with 16-byte stores that fill whole
 // 128-byte rows of banks.  The state stays fp32 end to end; only MMA
@@ -200,233 +196,366 @@ __device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity) {
 
 constexpr int kTcThreads2 = 256;
 constexpr uint32_t kChunkImg = 128 * 128 * 2;  // bytes of one 128 x 128 bf16 operand
+constexpr uint32_t kStImg = 128 * 64 * 2;      // bytes of one dqk x dv bf16 operand
 constexpr uint32_t kChunkSt = 128 * 64 * 4;    // bytes of one fp32 dqk x dv state
 
-// workspace of one launch: e^l Qr images, dS/S_in states, chunk decays
+// workspace of one launch
 struct TcWs {
-    uint8_t* qs;    // [bh][chunk] kChunkImg
-    float* st;      // [bh][chunk] dqk x dv, row n, column p
-    float* decay;   // [bh][chunk]
+    float* st;        // [bh][chunk] dS^T, fp32, row n, column p
+    uint8_t* simg;    // [bh][chunk] S_in^T, bf16 MN-major operand image (m = p, k = n)
+    float* decay;     // [bh][chunk] e^{l_last}
 };
 
-// ---- phase 1 shared memory (bytes) ----
-constexpr uint32_t k1Q = 0;                      // Qr K-major (A of G); then W (A of Y)
-constexpr uint32_t k1K = k1Q + kChunkImg;        // Kr K-major (B of G; A of dS^T as MN-major)
-constexpr uint32_t k1X = k1K + kChunkImg;        // X MN-major (B of Y: m=p, k=j)
-constexpr uint32_t k1Xw = k1X + 128 * 64 * 2;    // w o X MN-major (B of dS^T)
-constexpr uint32_t k1Gate = k1Xw + 128 * 64 * 2; // lcum, scale, gamma, w (fp32 x 128)
-constexpr uint32_t k1Misc = k1Gate + 4 * 128 * 4;
-constexpr uint32_t k1Smem = k1Misc + 64;
-
-// Requests every row tile `tile` will read from DRAM into L2 (each row is a
-// separate 256- or 512-byte piece), so that its loads, issued one tile
-// later, hit L2.
-__device__ __forceinline__ void intra_prefetch(const M3Params& p, int64_t tile, int n_chunks) {
-    const int64_t BH = p.batch * p.heads, H = p.heads, L = p.len;
-    const int64_t bh = tile % BH;
-    const int64_t bi = bh / H, h = bh % H;
-    const int ch = static_cast<int>(tile / BH);
-    const int tid = threadIdx.x, j = tid & 127;
-    const int64_t it = static_cast<int64_t>(ch) * kTcQ + j;
-    if (it >= L) return;
-    const int64_t t = p.reverse ? L - 1 - it : it;
-    const int64_t row = (bi * L + t) * H + h;
-    if (tid < 128) {
-        prefetch_l2(p.v + row * kTcP, kTcP * 4);
-        prefetch_l2(p.cos + row * (kTcN / 2), kTcN * 2);
-        prefetch_l2(p.sin + row * (kTcN / 2), kTcN * 2);
-    } else {
-        if (h == 0) {  // q, k rows are shared by all heads
-            prefetch_l2(p.q + (bi * L + t) * kTcN, kTcN * 4);
-            prefetch_l2(p.k + (bi * L + t) * kTcN, kTcN * 4);
+// Gates of one chunk (warp 0): cumulative log2 decay l2 (lcum), trapezoid
+// scale, gamma, state weight w_j = 2^(l2_last - l2_j) * scale_j, and
+// (lane 0) the chunk's total decay.
+__device__ __forceinline__ void tile_gates(const M3Params& p, int64_t bh, int64_t it0, float* lcum,
+                                           float* scl, float* gam, float* wdec, float* decay) {
+    constexpr float kLog2eF = 1.4426950408889634f;
+    const int lane = threadIdx.x & 31;
+    const int64_t L = p.len, gate_base = bh * L;
+    float lv[4], sc[4], gm[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int64_t it = it0 + lane * 4 + e;
+        lv[e] = sc[e] = gm[e] = 0.f;
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            const int64_t g = gate_base + t;
+            const float gamma = __ldg(p.dt + g) * sigmoid_f(__ldg(p.trap + g));
+            float shifted = 0.f;
+            if (it + 1 < L) {
+                const int64_t nx = p.reverse ? g - 1 : g + 1;
+                shifted = __ldg(p.dt + nx) * (1.f - sigmoid_f(__ldg(p.trap + nx)));
+            }
+            lv[e] = __ldg(p.adt + g) * kLog2eF;
+            sc[e] = gamma + shifted;
+            gm[e] = gamma;
         }
-        if (p.z && ch == 0) prefetch_l2(p.z + row * kTcP, kTcP * 4);
     }
-    (void)n_chunks;
+    lv[1] += lv[0];
+    lv[2] += lv[1];
+    lv[3] += lv[2];
+    float run = lv[3];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(0xffffffffu, run, o);
+        if (lane >= o) run += v;
+    }
+    const float before = run - lv[3];
+    const float last = __shfl_sync(0xffffffffu, run, 31);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int j = lane * 4 + e;
+        const float l = before + lv[e];
+        lcum[j] = l;
+        scl[j] = sc[e];
+        gam[j] = gm[e];
+        wdec[j] = ex2_approx(last - l) * sc[e];
+    }
+    if (decay && lane == 0) *decay = ex2_approx(last);
 }
 
-// Persistent: CTA b handles tiles b, b + gridDim.x, ... (tile = chunk *
-// batch*heads + batch*head), prefetching each next tile while it works on
-// the current one.  Gates are kept in log2 units (l2 = l * log2 e) so every
-// decay factor is one ex2.
-__global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs ws, int n_chunks) {
+// X items: step j, 8 consecutive channels = one 16-byte chunk of an
+// MN-major (m = p, k = j) operand.  Item r of this thread:
+__device__ __forceinline__ void x_item(int r, int& j, int& pc) {
+    const int item = threadIdx.x + r * kTcThreads2;
+    const int hi = item >> 5;
+    j = (hi >> 1) * 8 + (item & 7);
+    pc = ((item >> 3) & 3) + 4 * (hi & 1);
+}
+constexpr int kXItems = 128 * 8 / kTcThreads2;
+
+__device__ __forceinline__ void load_x(const M3Params& p, int64_t bi, int64_t h, int64_t it0,
+                                       float (&xv)[kXItems][8]) {
+    const int64_t L = p.len, H = p.heads;
+#pragma unroll
+    for (int r = 0; r < kXItems; ++r) {
+        int j, pc;
+        x_item(r, j, pc);
+        const int64_t it = it0 + j;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xv[r][e] = 0.f;
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            ldg8(p.v + ((bi * L + t) * H + h) * kTcP + pc * 8, xv[r]);
+        }
+    }
+}
+
+// Rotated k (and, with WITH_Q, rotated q) rows of one chunk into K-major
+// 128 x 128 operand images.  One item = step j, 8 consecutive dims (4
+// rotation pairs); a warp covers 8 steps x 4 dim-chunks, i.e. 128
+// contiguous bytes of each input row.  Items 2m and 2m+1 share their dim
+// chunk and are both loaded before either is stored.
+template <bool WITH_Q>
+__device__ __forceinline__ void stage_qk(const M3Params& p, int64_t bi, int64_t h, int64_t it0,
+                                         uint8_t* img_q, uint8_t* img_k) {
+    const int64_t L = p.len, H = p.heads;
+    const int tid = threadIdx.x;
+    const float* qb = p.q_bias + h * kTcN;
+    const float* kb = p.k_bias + h * kTcN;
+    for (int m = 0; m < 128 * 16 / kTcThreads2 / 2; ++m) {
+        float qa[2][8], ka[2][8], cc[2][4], ss[2][4];
+        int jj[2];
+        int kc = 0;
+        bool live[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int item = tid + (2 * m + u) * kTcThreads2;
+            const int hi = item >> 5;
+            jj[u] = (hi & 15) * 8 + (item & 7);
+            kc = ((item >> 3) & 3) + 4 * (hi >> 4);
+            const int64_t it = it0 + jj[u];
+            live[u] = it < L;
+            const int64_t t = live[u] ? (p.reverse ? L - 1 - it : it) : 0;
+            const int64_t qk = (bi * L + t) * kTcN + kc * 8;
+            const int64_t cs = ((bi * L + t) * H + h) * (kTcN / 2) + kc * 4;
+            if (WITH_Q) ldg8(p.q + qk, qa[u]);
+            ldg8(p.k + qk, ka[u]);
+            const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cos + cs));
+            const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sin + cs));
+            cc[u][0] = c4.x; cc[u][1] = c4.y; cc[u][2] = c4.z; cc[u][3] = c4.w;
+            ss[u][0] = s4.x; ss[u][1] = s4.y; ss[u][2] = s4.z; ss[u][3] = s4.w;
+        }
+        float qbb[8], kbb[8];
+        if (WITH_Q) ldg8(qb + kc * 8, qbb);
+        ldg8(kb + kc * 8, kbb);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            float qr[8], kr[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (WITH_Q) {
+                    const float a0 = qa[u][2 * e] + qbb[2 * e], a1 = qa[u][2 * e + 1] + qbb[2 * e + 1];
+                    qr[2 * e] = a0 * cc[u][e] - a1 * ss[u][e];
+                    qr[2 * e + 1] = a0 * ss[u][e] + a1 * cc[u][e];
+                }
+                const float a0 = ka[u][2 * e] + kbb[2 * e], a1 = ka[u][2 * e + 1] + kbb[2 * e + 1];
+                kr[2 * e] = a0 * cc[u][e] - a1 * ss[u][e];
+                kr[2 * e + 1] = a0 * ss[u][e] + a1 * cc[u][e];
+            }
+            if (!live[u]) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) qr[e] = kr[e] = 0.f;
+            }
+            const uint32_t ko = kmaj_off(jj[u], kc * 8, 128);
+            if (WITH_Q) *reinterpret_cast<uint4*>(img_q + ko) = pack8(qr);
+            *reinterpret_cast<uint4*>(img_k + ko) = pack8(kr);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel A: per (batch*head, chunk) the chunk's state contribution
+// dS^T = Kr^T (w o X) (fp32, to the workspace), its total decay, and for the
+// last chunk scale_T * k_T.
+constexpr uint32_t kAK = 0;                        // Kr K-major; A of dS^T as MN-major
+constexpr uint32_t kAXw = kAK + kChunkImg;         // w o X MN-major (B)
+constexpr uint32_t kAGate = kAXw + 128 * 64 * 2;   // lcum, scale, gamma, w
+constexpr uint32_t kAMisc = kAGate + 4 * 128 * 4;
+constexpr uint32_t kASmem = kAMisc + 64;
+
+__global__ void __launch_bounds__(kTcThreads2, 3) m3_tc_dstate(M3Params p, TcWs ws, int n_chunks) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    float* lcum = reinterpret_cast<float*>(smem + k1Gate);  // log2 units
+    float* lcum = reinterpret_cast<float*>(smem + kAGate);
     float* scl = lcum + kTcQ;
     float* gam = scl + kTcQ;
     float* wdec = gam + kTcQ;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + k1Misc + 16);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + k1Misc + 32);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kAMisc);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kAMisc + 16);
     const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    constexpr float kLog2eF = 1.4426950408889634f;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t H = p.heads, L = p.len, BH = p.batch * p.heads;
+    const int64_t bh = blockIdx.x % BH;
+    const int ch = static_cast<int>(blockIdx.x / BH);
+    const int64_t bi = bh / H, h = bh % H;
+    const int64_t bhc = bh * n_chunks + ch;
+    const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
+
+    if (warp == 0) tmem_alloc(tmem_slot, 64);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    float xv[kXItems][8];
+    load_x(p, bi, h, it0, xv);
+    if (warp == 0) tile_gates(p, bh, it0, lcum, scl, gam, wdec, ws.decay + bhc);
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < kXItems; ++r) {
+        int j, pc;
+        x_item(r, j, pc);
+        const float w = wdec[j];
+        float xw[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xw[e] = w * xv[r][e];
+        *reinterpret_cast<uint4*>(smem + kAXw + mnmaj_off(pc * 8, j, kTcP)) = pack8(xw);
+    }
+    stage_qk<false>(p, bi, h, it0, nullptr, smem + kAK);
+    if (p.last_bx && ch == n_chunks - 1 && tid < kTcN / 2) {
+        // scale_T * k_T: rotated k of the final step, fp32
+        const int jl = static_cast<int>(L - 1 - it0);
+        const int64_t t = p.reverse ? 0 : L - 1;
+        const int64_t qk = (bi * L + t) * kTcN;
+        const float* kb = p.k_bias + h * kTcN;
+        const int64_t cs = ((bi * L + t) * H + h) * (kTcN / 2) + tid;
+        const float c = p.cos[cs], s = p.sin[cs];
+        const float a0 = p.k[qk + 2 * tid] + kb[2 * tid];
+        const float a1 = p.k[qk + 2 * tid + 1] + kb[2 * tid + 1];
+        p.last_bx[bh * kTcN + 2 * tid] = scl[jl] * (a0 * c - a1 * s);
+        p.last_bx[bh * kTcN + 2 * tid + 1] = scl[jl] * (a0 * s + a1 * c);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (tid == 0) {
+        const uint32_t id_S = instr_desc(128, kTcP, true, true);
+        // A = Kr viewed MN-major (m = n, k = j): next 8 n = 2048 B (SBO),
+        // next 8 j = 128 B (LBO); 16 steps of j = 256 B
+        for (int kb = 0; kb < kTcQ / 16; ++kb) {
+            const uint64_t a = smem_desc(sbase + kAK + kb * 2 * 128, 128, 16 * 128);
+            const uint64_t b = smem_desc(sbase + kAXw + kb * 2 * 8 * 128, 8 * 128, 128);
+            umma(tmem, a, b, id_S, kb > 0);
+        }
+        umma_commit(bar);
+    }
+    if (cta_wait(bar, 0)) {
+        tc_fence_after();
+        const int n = (warp & 3) * 32 + lane, hc = warp >> 2;
+        float ds[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + hc * 32, ds);
+        float* st = ws.st + bhc * (kTcN * kTcP) + n * kTcP + hc * 32;
+#pragma unroll
+        for (int q = 0; q < 32; q += 4)
+            *reinterpret_cast<float4*>(st + q) = make_float4(ds[q], ds[q + 1], ds[q + 2], ds[q + 3]);
+    } else {
+        mbar_wait(bar, 0);  // the MMA still in flight: bounded second wait
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 64);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel B: S_in(0) = 0; S_in(c+1) = decay(c) S_in(c) + dS(c) in fp32.
+// S_in(c) is written as chunk c's bf16 MN-major operand image; the final
+// state goes to last_state.  A thread owns 4 consecutive (n, p) entries;
+// slices of 1024 entries per CTA.
+constexpr int kStSlices = (kTcN * kTcP) / (kTcThreads2 * 4);
+
+__global__ void __launch_bounds__(kTcThreads2) m3_tc_state(M3Params p, TcWs ws, int n_chunks) {
+    const int64_t bh = blockIdx.x;
+    const int e0 = (blockIdx.y * kTcThreads2 + threadIdx.x) * 4;
+    const int n = e0 / kTcP, p0 = e0 % kTcP;
+    const uint32_t img_off = mnmaj_off(p0, n, kTcP);  // 4 consecutive p: 8 bytes
+    float4 S = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* base = ws.st + bh * n_chunks * (kTcN * kTcP) + e0;
+    uint8_t* img = ws.simg + bh * n_chunks * kStImg + img_off;
+    const float* dec = ws.decay + bh * n_chunks;
+    float4 nd = __ldg(reinterpret_cast<const float4*>(base));
+    float nq = __ldg(dec);
+    for (int c = 0; c < n_chunks; ++c) {
+        const float4 d = nd;
+        const float q = nq;
+        if (c + 1 < n_chunks) {
+            nd = __ldg(reinterpret_cast<const float4*>(base + static_cast<int64_t>(c + 1) * (kTcN * kTcP)));
+            nq = __ldg(dec + c + 1);
+        }
+        if (c > 0)
+            *reinterpret_cast<uint2*>(img + static_cast<int64_t>(c) * kStImg) =
+                make_uint2(pack_bf16x2(S.x, S.y), pack_bf16x2(S.z, S.w));
+        S.x = fmaf(q, S.x, d.x);
+        S.y = fmaf(q, S.y, d.y);
+        S.z = fmaf(q, S.z, d.z);
+        S.w = fmaf(q, S.w, d.w);
+    }
+    if (p.last_state) {
+        // state entries are (n, p) row-major; last_state is (p, n)
+        const float sv[4] = {S.x, S.y, S.z, S.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) p.last_state[(bh * kTcP + p0 + e) * kTcN + n] = sv[e];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel C, persistent (CTA b takes tiles b, b + gridDim.x, ...; tile =
+// chunk * batch*heads + batch*head): the chunk's output
+//   G = Qr Kr^T -> TMEM [0,128);  Z = Qr S_in^T -> TMEM [128,192) (chunk > 0)
+//   W = mask o G -> bf16 over Qr;  Y = W X -> TMEM [0,64)
+//   y = (Y + 2^{l2_i} Z + D x) * silu(z)
+constexpr uint32_t kCQ = 0;                        // Qr K-major (A of G, Z); then W (A of Y)
+constexpr uint32_t kCK = kCQ + kChunkImg;          // Kr K-major (B of G)
+constexpr uint32_t kCX = kCK + kChunkImg;          // X MN-major (B of Y)
+constexpr uint32_t kCS = kCX + 128 * 64 * 2;       // S_in^T MN-major (B of Z)
+constexpr uint32_t kCGate = kCS + kStImg;          // lcum, scale, gamma, w
+constexpr uint32_t kCMisc = kCGate + 4 * 128 * 4;
+constexpr uint32_t kCSmem = kCMisc + 64;
+
+__global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_out(M3Params p, TcWs ws, int n_chunks) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    float* lcum = reinterpret_cast<float*>(smem + kCGate);  // log2 units
+    float* scl = lcum + kTcQ;
+    float* gam = scl + kTcQ;
+    float* wdec = gam + kTcQ;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kCMisc);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kCMisc + 16);
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t H = p.heads, L = p.len, BH = p.batch * p.heads;
     const int64_t n_tiles = BH * n_chunks;
 
-    if (warp == 0) tmem_alloc(tmem_slot, 128);
+    if (warp == 0) tmem_alloc(tmem_slot, 256);
     if (tid == 0) {
         mbar_init(bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (blockIdx.x < n_tiles) intra_prefetch(p, blockIdx.x, n_chunks);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int hc = warp >> 2;  // column half of this warp
-    const uint32_t tG = tmem, tY = tmem, tS = tmem + 64;
+    const uint32_t tG = tmem, tY = tmem, tZ = tmem + 128;
     uint32_t phase = 0;
     bool ok = true;
 
     for (int64_t tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-        if (tile + gridDim.x < n_tiles) intra_prefetch(p, tile + gridDim.x, n_chunks);
         const int64_t bh = tile % BH;
         const int ch = static_cast<int>(tile / BH);
         const int64_t bi = bh / H, h = bh % H;
         const int64_t bhc = bh * n_chunks + ch;
-        const int64_t gate_base = bh * L;
         const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
 
-        // X items: step j, 8 consecutive channels (one 16-byte chunk of the
-        // MN-major operand); loads issued before the gate pass, stored after
-        constexpr int kXItems = 128 * 8 / kTcThreads2;
         float xv[kXItems][8];
+        load_x(p, bi, h, it0, xv);
+        uint4 sv[kStImg / 16 / kTcThreads2];
+        if (ch > 0) {
+            const uint4* src = reinterpret_cast<const uint4*>(ws.simg + bhc * kStImg);
+#pragma unroll
+            for (int r = 0; r < static_cast<int>(kStImg / 16 / kTcThreads2); ++r)
+                sv[r] = __ldg(src + tid + r * kTcThreads2);
+        }
+        if (warp == 0) tile_gates(p, bh, it0, lcum, scl, gam, wdec, nullptr);
 #pragma unroll
         for (int r = 0; r < kXItems; ++r) {
-            const int item = tid + r * kTcThreads2;
-            const int hi = item >> 5;
-            const int j = (hi >> 1) * 8 + (item & 7);
-            const int pc = ((item >> 3) & 3) + 4 * (hi & 1);
-            const int64_t it = it0 + j;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) xv[r][e] = 0.f;
-            if (it < L) {
-                const int64_t t = p.reverse ? L - 1 - it : it;
-                ldg8(p.v + ((bi * L + t) * H + h) * kTcP + pc * 8, xv[r]);
-            }
+            int j, pc;
+            x_item(r, j, pc);
+            *reinterpret_cast<uint4*>(smem + kCX + mnmaj_off(pc * 8, j, kTcP)) = pack8(xv[r]);
         }
-        if (warp == 0) {
-            // gates: cumulative log2 decay, trapezoid weights, state weights
-            float lv[4], sc[4], gm[4];
+        if (ch > 0) {
+            uint4* dst = reinterpret_cast<uint4*>(smem + kCS);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int64_t it = it0 + lane * 4 + e;
-                lv[e] = sc[e] = gm[e] = 0.f;
-                if (it < L) {
-                    const int64_t t = p.reverse ? L - 1 - it : it;
-                    const int64_t g = gate_base + t;
-                    const float gamma = __ldg(p.dt + g) * sigmoid_f(__ldg(p.trap + g));
-                    float shifted = 0.f;
-                    if (it + 1 < L) {
-                        const int64_t nx = p.reverse ? g - 1 : g + 1;
-                        shifted = __ldg(p.dt + nx) * (1.f - sigmoid_f(__ldg(p.trap + nx)));
-                    }
-                    lv[e] = __ldg(p.adt + g) * kLog2eF;
-                    sc[e] = gamma + shifted;
-                    gm[e] = gamma;
-                }
-            }
-            lv[1] += lv[0];
-            lv[2] += lv[1];
-            lv[3] += lv[2];
-            float run = lv[3];
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const float v = __shfl_up_sync(0xffffffffu, run, o);
-                if (lane >= o) run += v;
-            }
-            const float before = run - lv[3];
-            const float last = __shfl_sync(0xffffffffu, run, 31);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int j = lane * 4 + e;
-                const float l = before + lv[e];
-                lcum[j] = l;
-                scl[j] = sc[e];
-                gam[j] = gm[e];
-                wdec[j] = ex2_approx(last - l) * sc[e];
-            }
-            if (lane == 0) ws.decay[bhc] = ex2_approx(last);
+            for (int r = 0; r < static_cast<int>(kStImg / 16 / kTcThreads2); ++r)
+                dst[tid + r * kTcThreads2] = sv[r];
         }
-        __syncthreads();
-#pragma unroll
-        for (int r = 0; r < kXItems; ++r) {
-            const int item = tid + r * kTcThreads2;
-            const int hi = item >> 5;
-            const int j = (hi >> 1) * 8 + (item & 7);
-            const int pc = ((item >> 3) & 3) + 4 * (hi & 1);
-            const float w = wdec[j];
-            float xw[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) xw[e] = w * xv[r][e];
-            const uint32_t o = mnmaj_off(pc * 8, j, kTcP);
-            *reinterpret_cast<uint4*>(smem + k1X + o) = pack8(xv[r]);
-            *reinterpret_cast<uint4*>(smem + k1Xw + o) = pack8(xw);
-        }
-        // Qr, Kr to shared memory; e^l o Qr to the workspace.  One item =
-        // step j, 8 consecutive dims (4 rotation pairs); a warp covers 8
-        // steps x 4 dim-chunks, i.e. 128 contiguous bytes of each input row.
-        {
-            uint8_t* qs_img = ws.qs + bhc * kChunkImg;
-            const float* qb = p.q_bias + h * kTcN;
-            const float* kb = p.k_bias + h * kTcN;
-            // items r = 2m, 2m+1 share their dim chunk; both are loaded
-            // before either is stored: one memory round trip per pair
-            for (int m = 0; m < 128 * 16 / kTcThreads2 / 2; ++m) {
-                float qa[2][8], ka[2][8], cc[2][4], ss[2][4];
-                int jj[2];
-                int kc = 0;
-                bool live[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int item = tid + (2 * m + u) * kTcThreads2;
-                    const int hi = item >> 5;
-                    jj[u] = (hi & 15) * 8 + (item & 7);
-                    kc = ((item >> 3) & 3) + 4 * (hi >> 4);
-                    const int64_t it = it0 + jj[u];
-                    live[u] = it < L;
-                    const int64_t t = live[u] ? (p.reverse ? L - 1 - it : it) : 0;
-                    const int64_t qk = (bi * L + t) * kTcN + kc * 8;
-                    const int64_t cs = ((bi * L + t) * H + h) * (kTcN / 2) + kc * 4;
-                    ldg8(p.q + qk, qa[u]);
-                    ldg8(p.k + qk, ka[u]);
-                    const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cos + cs));
-                    const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sin + cs));
-                    cc[u][0] = c4.x; cc[u][1] = c4.y; cc[u][2] = c4.z; cc[u][3] = c4.w;
-                    ss[u][0] = s4.x; ss[u][1] = s4.y; ss[u][2] = s4.z; ss[u][3] = s4.w;
-                }
-                float qbb[8], kbb[8];
-                ldg8(qb + kc * 8, qbb);
-                ldg8(kb + kc * 8, kbb);
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int j = jj[u];
-                    float qr[8], kr[8], qs[8];
-                    const float el = live[u] ? ex2_approx(lcum[j]) : 0.f;
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        float a0 = qa[u][2 * e] + qbb[2 * e], a1 = qa[u][2 * e + 1] + qbb[2 * e + 1];
-                        qr[2 * e] = a0 * cc[u][e] - a1 * ss[u][e];
-                        qr[2 * e + 1] = a0 * ss[u][e] + a1 * cc[u][e];
-                        a0 = ka[u][2 * e] + kbb[2 * e];
-                        a1 = ka[u][2 * e + 1] + kbb[2 * e + 1];
-                        kr[2 * e] = a0 * cc[u][e] - a1 * ss[u][e];
-                        kr[2 * e + 1] = a0 * ss[u][e] + a1 * cc[u][e];
-                    }
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        if (!live[u]) qr[e] = kr[e] = 0.f;
-                        qs[e] = el * qr[e];
-                    }
-                    const uint32_t ko = kmaj_off(j, kc * 8, 128);
-                    *reinterpret_cast<uint4*>(smem + k1Q + ko) = pack8(qr);
-                    *reinterpret_cast<uint4*>(smem + k1K + ko) = pack8(kr);
-                    *reinterpret_cast<uint4*>(qs_img + ko) = pack8(qs);
-                }
-            }
-        }
+        stage_qk<true>(p, bi, h, it0, smem + kCQ, smem + kCK);
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
@@ -436,9 +565,18 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs w
             const uint32_t id_G = instr_desc(128, 128, false, false);
 #pragma unroll
             for (int kb = 0; kb < kTcN / 16; ++kb) {
-                const uint64_t a = smem_desc(sbase + k1Q + kb * 2 * 16 * 128, 16 * 128, 128);
-                const uint64_t b = smem_desc(sbase + k1K + kb * 2 * 16 * 128, 16 * 128, 128);
+                const uint64_t a = smem_desc(sbase + kCQ + kb * 2 * 16 * 128, 16 * 128, 128);
+                const uint64_t b = smem_desc(sbase + kCK + kb * 2 * 16 * 128, 16 * 128, 128);
                 umma(tG, a, b, id_G, kb > 0);
+            }
+            if (ch > 0) {
+                const uint32_t id_Z = instr_desc(128, kTcP, false, true);
+#pragma unroll
+                for (int kb = 0; kb < kTcN / 16; ++kb) {
+                    const uint64_t a = smem_desc(sbase + kCQ + kb * 2 * 16 * 128, 16 * 128, 128);
+                    const uint64_t b = smem_desc(sbase + kCS + kb * 2 * 8 * 128, 8 * 128, 128);
+                    umma(tZ, a, b, id_Z, kb > 0);
+                }
             }
             umma_commit(bar);
         }
@@ -471,7 +609,7 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs w
                         const float m = j < i ? ex2_approx(li - lj[c]) * sj[c] : (j == i ? gi : 0.f);
                         wv[c] = m * g[c8 * 8 + c];
                     }
-                    *reinterpret_cast<uint4*>(smem + k1Q + kmaj_off(i, j0, 128)) = pack8(wv);
+                    *reinterpret_cast<uint4*>(smem + kCQ + kmaj_off(i, j0, 128)) = pack8(wv);
                 }
             }
         }
@@ -481,18 +619,10 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs w
         tc_fence_after();
         if (tid == 0) {
             const uint32_t id_Y = instr_desc(128, kTcP, false, true);
-            const uint32_t id_S = instr_desc(128, kTcP, true, true);
             for (int kb = 0; kb < kTcQ / 16; ++kb) {
-                const uint64_t a = smem_desc(sbase + k1Q + kb * 2 * 16 * 128, 16 * 128, 128);
-                const uint64_t b = smem_desc(sbase + k1X + kb * 2 * 8 * 128, 8 * 128, 128);
+                const uint64_t a = smem_desc(sbase + kCQ + kb * 2 * 16 * 128, 16 * 128, 128);
+                const uint64_t b = smem_desc(sbase + kCX + kb * 2 * 8 * 128, 8 * 128, 128);
                 umma(tY, a, b, id_Y, kb > 0);
-            }
-            // A = Kr viewed MN-major (m = n, k = j): next 8 n = 2048 B (SBO),
-            // next 8 j = 128 B (LBO); 16 steps of j = 256 B
-            for (int kb = 0; kb < kTcQ / 16; ++kb) {
-                const uint64_t a = smem_desc(sbase + k1K + kb * 2 * 128, 128, 16 * 128);
-                const uint64_t b = smem_desc(sbase + k1Xw + kb * 2 * 8 * 128, 8 * 128, 128);
-                umma(tS, a, b, id_S, kb > 0);
             }
             umma_commit(bar);
         }
@@ -500,29 +630,35 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs w
         phase ^= 1;
         if (!ok) break;
         tc_fence_after();
-        const int r = (warp & 3) * 32 + lane;  // output row i / state row n
         {
+            const int i = (warp & 3) * 32 + lane;
             float y[32];
             tmem_ld32(tY + t_lane + hc * 32, y);
-            const int64_t it = it0 + r;
+            if (ch > 0) {
+                float zt[32];
+                tmem_ld32(tZ + t_lane + hc * 32, zt);
+                const float el = ex2_approx(lcum[i]);
+#pragma unroll
+                for (int q = 0; q < 32; ++q) y[q] = fmaf(el, zt[q], y[q]);
+            }
+            const int64_t it = it0 + i;
             if (it < L) {
                 const float dsk = p.d_skip ? p.d_skip[h] : 0.f;
                 const int64_t t = p.reverse ? L - 1 - it : it;
                 const int64_t voff = ((bi * L + t) * H + h) * kTcP + hc * 32;
                 float* o = p.out + (bh * L + t) * kTcP + hc * 32;
-                const bool gate = p.z && ch == 0;
                 float4 vv[8], zz[8];
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
                     vv[q] = __ldg(reinterpret_cast<const float4*>(p.v + voff) + q);
-                    zz[q] = gate ? __ldg(reinterpret_cast<const float4*>(p.z + voff) + q)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                    zz[q] = p.z ? __ldg(reinterpret_cast<const float4*>(p.z + voff) + q)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
                     float r4[4] = {fmaf(dsk, vv[q].x, y[4 * q]), fmaf(dsk, vv[q].y, y[4 * q + 1]),
                                    fmaf(dsk, vv[q].z, y[4 * q + 2]), fmaf(dsk, vv[q].w, y[4 * q + 3])};
-                    if (gate) {
+                    if (p.z) {
                         r4[0] *= silu_f(zz[q].x);
                         r4[1] *= silu_f(zz[q].y);
                         r4[2] *= silu_f(zz[q].z);
@@ -531,27 +667,6 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs w
                     *reinterpret_cast<float4*>(o + 4 * q) = make_float4(r4[0], r4[1], r4[2], r4[3]);
                 }
             }
-        }
-        {
-            float ds[32];
-            tmem_ld32(tS + t_lane + hc * 32, ds);
-            float* st = ws.st + bhc * (kTcN * kTcP) + r * kTcP + hc * 32;
-#pragma unroll
-            for (int q = 0; q < 32; q += 4)
-                *reinterpret_cast<float4*>(st + q) = make_float4(ds[q], ds[q + 1], ds[q + 2], ds[q + 3]);
-        }
-        if (p.last_bx && ch == n_chunks - 1 && tid < kTcN / 2) {
-            // scale_T * k_T: rotated k of the final step, fp32
-            const int jl = static_cast<int>(L - 1 - it0);
-            const int64_t t = p.reverse ? 0 : L - 1;
-            const int64_t qk = (bi * L + t) * kTcN;
-            const float* kb = p.k_bias + h * kTcN;
-            const int64_t cs = ((bi * L + t) * H + h) * (kTcN / 2) + tid;
-            const float c = p.cos[cs], s = p.sin[cs];
-            const float a0 = p.k[qk + 2 * tid] + kb[2 * tid];
-            const float a1 = p.k[qk + 2 * tid + 1] + kb[2 * tid + 1];
-            p.last_bx[bh * kTcN + 2 * tid] = scl[jl] * (a0 * c - a1 * s);
-            p.last_bx[bh * kTcN + 2 * tid + 1] = scl[jl] * (a0 * s + a1 * c);
         }
         // the next tile overwrites shared memory and tensor memory
         tc_fence_before();
@@ -563,160 +678,7 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_intra(M3Params p, TcWs w
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, 128);
-    }
-}
-
-// S_in(0) = 0; S_in(c+1) = decay(c) S_in(c) + dS(c).  Thread owns 4
-// consecutive state entries; slices of 1024 entries per CTA.
-constexpr int kStSlices = (kTcN * kTcP) / (kTcThreads2 * 4);
-
-__global__ void __launch_bounds__(kTcThreads2) m3_tc_state(M3Params p, TcWs ws, int n_chunks) {
-    const int64_t bh = blockIdx.x;
-    const int e0 = (blockIdx.y * kTcThreads2 + threadIdx.x) * 4;
-    float4 S = make_float4(0.f, 0.f, 0.f, 0.f);
-    float* base = ws.st + bh * n_chunks * (kTcN * kTcP) + e0;
-    const float* dec = ws.decay + bh * n_chunks;
-    float4 nd = *reinterpret_cast<const float4*>(base);
-    float nq = dec[0];
-    for (int c = 0; c < n_chunks; ++c) {
-        const float4 d = nd;
-        const float q = nq;
-        if (c + 1 < n_chunks) {
-            nd = *reinterpret_cast<const float4*>(base + static_cast<int64_t>(c + 1) * (kTcN * kTcP));
-            nq = dec[c + 1];
-        }
-        *reinterpret_cast<float4*>(base + static_cast<int64_t>(c) * (kTcN * kTcP)) = S;
-        S.x = fmaf(q, S.x, d.x);
-        S.y = fmaf(q, S.y, d.y);
-        S.z = fmaf(q, S.z, d.z);
-        S.w = fmaf(q, S.w, d.w);
-    }
-    if (p.last_state) {
-        // state entries are (n, p) row-major; last_state is (p, n)
-        const float sv[4] = {S.x, S.y, S.z, S.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int n = (e0 + e) / kTcP, pp = (e0 + e) % kTcP;
-            p.last_state[(bh * kTcP + pp) * kTcN + n] = sv[e];
-        }
-    }
-}
-
-// ---- phase 3 shared memory ----
-constexpr uint32_t k3Qs = 0;                  // e^l Qr K-major (A)
-constexpr uint32_t k3S = kChunkImg;           // S_in^T MN-major (B: m=p, k=n)
-constexpr uint32_t k3Misc = k3S + 128 * 64 * 2;
-constexpr uint32_t k3Smem = k3Misc + 64;
-
-__global__ void __launch_bounds__(kTcThreads2, 4) m3_tc_inter(M3Params p, TcWs ws, int n_chunks) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + k3Misc);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + k3Misc + 16);
-    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t H = p.heads, L = p.len;
-    const int64_t bh = blockIdx.x % (p.batch * H);
-    const int ch = 1 + static_cast<int>(blockIdx.x / (p.batch * H));
-    const int64_t bi = bh / H, h = bh % H;
-    const int64_t bhc = bh * n_chunks + ch;
-    const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
-
-    {
-        const int j = tid & 127;
-        const int64_t it = it0 + j;
-        if (tid < 128) {
-            if (it < L) {
-                const int64_t t = p.reverse ? L - 1 - it : it;
-                prefetch_l2(p.out + (bh * L + t) * kTcP, kTcP * 4);
-                if (p.z) prefetch_l2(p.z + ((bi * L + t) * H + h) * kTcP, kTcP * 4);
-            }
-        } else if (tid < 136) {
-            const int q = tid - 128;  // 8 pieces of 4 KB of each image
-            prefetch_l2(ws.qs + bhc * kChunkImg + q * 4096, 4096);
-            prefetch_l2(reinterpret_cast<const uint8_t*>(ws.st + bhc * (kTcN * kTcP)) + q * 4096, 4096);
-        }
-    }
-    if (warp == 0) tmem_alloc(tmem_slot, 64);
-    if (tid == 0) {
-        mbar_init(bar, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    {
-        const uint4* src = reinterpret_cast<const uint4*>(ws.qs + bhc * kChunkImg);
-        uint4* dst = reinterpret_cast<uint4*>(smem + k3Qs);
-#pragma unroll 4
-        for (int i = tid; i < static_cast<int>(kChunkImg / 16); i += kTcThreads2) dst[i] = __ldg(src + i);
-        // S_in^T: 16-byte chunk = state row n, 8 consecutive p
-        const float* st = ws.st + bhc * (kTcN * kTcP);
-#pragma unroll 4
-        for (int item = tid; item < 128 * 8; item += kTcThreads2) {
-            const int hi = item >> 5;
-            const int n = (hi >> 1) * 8 + (item & 7);
-            const int pc = ((item >> 3) & 3) + 4 * (hi & 1);
-            float f[8];
-            ldg8(st + n * kTcP + pc * 8, f);
-            *reinterpret_cast<uint4*>(smem + k3S + mnmaj_off(pc * 8, n, kTcP)) = pack8(f);
-        }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    if (tid == 0) {
-        const uint32_t id_Y = instr_desc(128, kTcP, false, true);
-#pragma unroll
-        for (int kb = 0; kb < kTcN / 16; ++kb) {
-            const uint64_t a = smem_desc(sbase + k3Qs + kb * 2 * 16 * 128, 16 * 128, 128);
-            const uint64_t b = smem_desc(sbase + k3S + kb * 2 * 8 * 128, 8 * 128, 128);
-            umma(tmem, a, b, id_Y, kb > 0);
-        }
-        umma_commit(bar);
-    }
-    if (cta_wait(bar, 0)) {
-        tc_fence_after();
-        const int i = (warp & 3) * 32 + lane;
-        const int hc = warp >> 2;
-        float y[32];
-        tmem_ld32(tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + hc * 32, y);
-        const int64_t it = it0 + i;
-        if (it < L) {
-            const int64_t t = p.reverse ? L - 1 - it : it;
-            float* o = p.out + (bh * L + t) * kTcP + hc * 32;
-            const float* zr = p.z ? p.z + ((bi * L + t) * H + h) * kTcP + hc * 32 : nullptr;
-#pragma unroll
-            for (int qq = 0; qq < 32; qq += 8) {
-                float4 oo[2], zz[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    oo[u] = *reinterpret_cast<const float4*>(o + qq + 4 * u);
-                    zz[u] = zr ? __ldg(reinterpret_cast<const float4*>(zr + qq + 4 * u))
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int q = qq + 4 * u;
-                    float r4[4] = {oo[u].x + y[q], oo[u].y + y[q + 1], oo[u].z + y[q + 2],
-                                   oo[u].w + y[q + 3]};
-                    if (zr) {
-                        r4[0] *= silu_f(zz[u].x);
-                        r4[1] *= silu_f(zz[u].y);
-                        r4[2] *= silu_f(zz[u].z);
-                        r4[3] *= silu_f(zz[u].w);
-                    }
-                    *reinterpret_cast<float4*>(o + q) = make_float4(r4[0], r4[1], r4[2], r4[3]);
-                }
-            }
-        }
-    } else {
-        mbar_wait(bar, 0);  // the MMA still in flight: bounded second wait
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-        tc_fence_after();
-        tmem_dealloc(tmem, 64);
+        tmem_dealloc(tmem, 256);
     }
 }
 
@@ -731,7 +693,7 @@ bool m3_tc_applicable(const M3Params& p) {
 
 size_t m3_tc_workspace_bytes(const M3Params& p) {
     const int64_t nc = (p.len + kTcQ - 1) / kTcQ;
-    return static_cast<size_t>(p.batch * p.heads * nc) * (kChunkImg + kChunkSt + 16);
+    return static_cast<size_t>(p.batch * p.heads * nc) * (kChunkSt + kStImg + 16);
 }
 
 // Per-device memory pool for the workspace.  It keeps what it has reserved
@@ -774,13 +736,15 @@ cudaError_t workspace_pool(cudaMemPool_t* out) {
 cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
     const int64_t bh = p.batch * p.heads;
     const int n_chunks = static_cast<int>((p.len + kTcQ - 1) / kTcQ);
-    cudaError_t e = cudaFuncSetAttribute(m3_tc_intra, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(k1Smem));
+    cudaError_t e = cudaFuncSetAttribute(m3_tc_out, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kCSmem));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(m3_tc_intra, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        e = cudaFuncSetAttribute(m3_tc_out, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(m3_tc_inter, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(k3Smem));
+        e = cudaFuncSetAttribute(m3_tc_dstate, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kASmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(m3_tc_dstate, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     // stream-ordered workspace: valid under stream capture, freed after use
     void* raw = nullptr;
@@ -791,22 +755,21 @@ cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     const size_t units = static_cast<size_t>(bh) * n_chunks;
     TcWs ws;
-    ws.qs = static_cast<uint8_t*>(raw);
-    ws.st = reinterpret_cast<float*>(ws.qs + units * kChunkImg);
-    ws.decay = ws.st + units * (kTcN * kTcP);
+    ws.st = static_cast<float*>(raw);
+    ws.simg = reinterpret_cast<uint8_t*>(ws.st + units * (kTcN * kTcP));
+    ws.decay = reinterpret_cast<float*>(ws.simg + units * kStImg);
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const size_t grid1 = units < static_cast<size_t>(2 * sms) ? units : static_cast<size_t>(2 * sms);
-    m3_tc_intra<<<static_cast<unsigned>(grid1), kTcThreads2, k1Smem, stream>>>(p, ws, n_chunks);
+    m3_tc_dstate<<<static_cast<unsigned>(units), kTcThreads2, kASmem, stream>>>(p, ws, n_chunks);
     e = cudaGetLastError();
     if (e == cudaSuccess) {
         m3_tc_state<<<dim3(static_cast<unsigned>(bh), kStSlices), kTcThreads2, 0, stream>>>(p, ws, n_chunks);
         e = cudaGetLastError();
     }
-    if (e == cudaSuccess && n_chunks > 1) {
-        m3_tc_inter<<<static_cast<unsigned>(bh * (n_chunks - 1)), kTcThreads2, k3Smem, stream>>>(
-            p, ws, n_chunks);
+    if (e == cudaSuccess) {
+        const size_t grid = units < static_cast<size_t>(2 * sms) ? units : static_cast<size_t>(2 * sms);
+        m3_tc_out<<<static_cast<unsigned>(grid), kTcThreads2, kCSmem, stream>>>(p, ws, n_chunks);
         e = cudaGetLastError();
     }
     const cudaError_t ef = cudaFreeAsync(raw, stream);
