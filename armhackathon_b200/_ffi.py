@@ -20,7 +20,7 @@ import os
 import sys
 from pathlib import Path
 
-ABI_VERSION = 8
+ABI_VERSION = 9
 
 _LIB_NAMES = ["libb200scan.so"]
 
@@ -88,7 +88,8 @@ def _bind(lib):
     for f in ("arm_scan_selective_scan_f32", "arm_scan_selective_scan_f32_async",
               "arm_scan_selective_scan_bidirectional_f32",
               "arm_scan_selective_scan_bidirectional_f32_async",
-              "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async"):
+              "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
+              "arm_scan_tensor_status"):
         getattr(lib, f).restype = ctypes.c_int
 
 
@@ -192,6 +193,12 @@ def angles_async_raw(dims, ptr_angles, n_angles, ptr_dt, ptr_cos, ptr_sin, ptr_w
         _n(stream)), "arm_scan_mamba3_angles_f32_async")
 
 
+def tensor_status():
+    """Raise if a tensor-core kernel's bounded wait expired since the last
+    check (call after synchronizing the stream of an async launch)."""
+    _check(load().arm_scan_tensor_status(), "arm_scan_tensor_status")
+
+
 def exported_symbols():
     """Names of every entry point include/b200scan.h declares."""
     return ["arm_scan_abi_version", "arm_scan_last_error",
@@ -200,7 +207,7 @@ def exported_symbols():
             "arm_scan_selective_scan_bidirectional_f32_async",
             "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
             "arm_scan_mamba3_angles_workspace_bytes", "arm_scan_mamba3_angles_f32_async",
-            "arm_scan_mamba3_angles_f32_noalloc"]
+            "arm_scan_mamba3_angles_f32_noalloc", "arm_scan_tensor_status"]
 
 
 if __name__ == "__main__":  # pragma: no cover

@@ -129,8 +129,16 @@ size_t round_up(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Runs `run(device_ptrs, stream)` either directly on device buffers (then
 // synchronizes) or after staging host buffers through device memory.
+int tensor_status_code() {
+    return m3_tc_status_and_clear()
+               ? fail(ARM_SCAN_ERR_TIMEOUT, "a tensor-core MMA completion wait expired")
+               : ARM_SCAN_OK;
+}
+
+// post (optional) runs after a successful synchronization and may turn the
+// result into an error (device-side status flags).
 template <class Run>
-int run_sync(std::vector<Buf>& bufs, Run&& run) {
+int run_sync(std::vector<Buf>& bufs, Run&& run, int (*post)() = nullptr) {
     int dev = -1;
     const Where w = classify(bufs, &dev);
     if (w == Where::Mixed)
@@ -143,7 +151,8 @@ int run_sync(std::vector<Buf>& bufs, Run&& run) {
         int rc = run(dptr, static_cast<cudaStream_t>(nullptr));
         if (rc != ARM_SCAN_OK) return rc;
         cudaError_t e = cudaStreamSynchronize(nullptr);
-        return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "kernel");
+        if (e != cudaSuccess) return cuda_fail(e, "kernel");
+        return post ? post() : ARM_SCAN_OK;
     }
     int cur = 0;
     cudaError_t e = cudaGetDevice(&cur);
@@ -189,7 +198,8 @@ int run_sync(std::vector<Buf>& bufs, Run&& run) {
         if (e != cudaSuccess) return cuda_fail(e, "copy to host");
     }
     e = cudaStreamSynchronize(st.stream);
-    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "kernel");
+    if (e != cudaSuccess) return cuda_fail(e, "kernel");
+    return post ? post() : ARM_SCAN_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -494,10 +504,15 @@ int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const fl
     std::vector<Buf> bufs = m3_bufs(cnt, dims, q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin,
                                     d_skip, z, mimo_psi, mimo_zeta, mimo_phi, out, last_state,
                                     last_bx);
-    return run_sync(bufs, [&](const std::vector<void*>& p, cudaStream_t s) {
-        return m3_run(m3_params(dims, p, reverse), backend, s);
-    });
+    return run_sync(
+        bufs,
+        [&](const std::vector<void*>& p, cudaStream_t s) {
+            return m3_run(m3_params(dims, p, reverse), backend, s);
+        },
+        backend == 3 ? tensor_status_code : nullptr);
 }
+
+int arm_scan_tensor_status(void) { return tensor_status_code(); }
 
 int arm_scan_mamba3_scan_f32_async(const ArmMamba3Dims* dims, const float* q, const float* k,
                                    const float* v, const float* adt, const float* dt,

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define ARM_SCAN_ABI_VERSION 8u
+#define ARM_SCAN_ABI_VERSION 9u
 
 /* Return codes (0-5: reference arm-scan-ffi/src/lib.rs:53-58). */
 #define ARM_SCAN_OK 0
@@ -55,10 +55,14 @@ extern "C" {
 #define ARM_SCAN_ERR_CUDA 6
 #define ARM_SCAN_ERR_TIMEOUT 7
 
-/* backend: 0 = auto (chunked sm_100a kernels), 1 = scalar (a sequential
- * on-device restatement of the reference's scalar loop, for cross-checks),
- * 2 = neon (not available here: code 3).  threading: 0/1/2 are accepted
- * (auto/sequential/rayon in the reference) and have no effect on a GPU. */
+/* backend: 0 = auto (chunked sm_100a kernels, fp32 arithmetic), 1 = scalar
+ * (a sequential on-device restatement of the reference's scalar loop, for
+ * cross-checks), 2 = neon (not available here: code 3), 3 = tensor
+ * (extension, Mamba-3 entry points only: tcgen05 tensor-core kernels with
+ * bf16 matrix operands, fp32 accumulation and fp32 state, for bf16 models;
+ * SISO with dqk 128, dv 64 and 16-byte aligned tensors, otherwise code 3).
+ * threading: 0/1/2 are accepted (auto/sequential/rayon in the reference)
+ * and have no effect on a GPU. */
 
 /* Replaces ArmScanDims, arm-scan-ffi/src/lib.rs:44-50. */
 typedef struct ArmScanDims {
@@ -79,7 +83,7 @@ typedef struct ArmMamba3Dims {
     size_t rank;
 } ArmMamba3Dims;
 
-/* Replaces arm_scan_abi_version, arm-scan-ffi/src/lib.rs:37-40. Returns 8. */
+/* Replaces arm_scan_abi_version, arm-scan-ffi/src/lib.rs:37-40. Returns 9. */
 uint32_t arm_scan_abi_version(void);
 
 /* Message describing the calling thread's most recent non-zero return. */
@@ -176,6 +180,15 @@ int arm_scan_mamba3_angles_f32_async(const ArmMamba3Dims* dims, const float* ang
 int arm_scan_mamba3_angles_f32_noalloc(const ArmMamba3Dims* dims, const float* angles,
                                        size_t n_angles, const float* dt, float* cos,
                                        float* sin, void* stream);
+
+/* Extension (no counterpart in the reference): status of the tensor-core
+ * kernels (backend 3).  Their waits on their own MMA completions are
+ * bounded; an expired wait abandons the remaining tiles and sets a device
+ * flag.  The synchronous entry points check it themselves (code 7); after
+ * an _async call, synchronize the stream and call this: returns 0, or 7
+ * (message in arm_scan_last_error) if a wait expired since the last check,
+ * and clears the flag. */
+int arm_scan_tensor_status(void);
 
 #ifdef __cplusplus
 }

@@ -23,7 +23,7 @@ def declared_functions():
 
 def test_library_loads_with_abi_v8():
     lib = _ffi.load()
-    assert lib.arm_scan_abi_version() == 8
+    assert lib.arm_scan_abi_version() == 9
     assert _ffi.lib_path().name == "libb200scan.so"
 
 

@@ -218,6 +218,9 @@ def test_tensor_core_siso_vs_oracle(shape, reverse):
                                   reverse=reverse, want_state=True, nthreads=8)
     out, st = arm().mamba3_scan(**{k: v.cuda() for k, v in x.items()}, reverse=reverse,
                                 return_last_state=True, precision="bf16")
+    torch.cuda.synchronize()
+    from armhackathon_b200 import _ffi
+    _ffi.tensor_status()  # no bounded MMA wait expired
     assert rel_err(out.cpu().numpy(), want) <= BF16_TOL
     assert rel_err(st.cpu().numpy(), wst) <= BF16_TOL
 
