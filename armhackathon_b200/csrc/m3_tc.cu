@@ -31,6 +31,7 @@
 #include <cuda_bf16.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -682,6 +683,317 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_out(M3Params p, TcWs ws,
     }
 }
 
+// ---------------------------------------------------------------------------
+// Fused single-launch variant (default).  Persistent CTAs take tiles from an
+// atomic counter in chunk-major order (tile = chunk * batch*heads + bh), so a
+// tile's predecessor chunk (same bh) was always taken earlier by a running
+// CTA.  Per tile:
+//   1. G = Qr Kr^T and dS^T = Kr^T (w o X) in one MMA group;
+//   2. W = mask o G over Kr (free once group 1 completed), Y = W X issued;
+//   3. the chain: wait for the predecessor's outgoing state (flag per bh,
+//      acquire), S_out = 2^{l2_last} S_in + dS in fp32, publish it (release)
+//      to the bh's other slot, then build the bf16 S_in^T operand;
+//   4. Z = Qr S_in^T;  y = (Y + 2^{l2_i} Z + D x) * silu(z).
+// The outgoing states live in two fp32 slots per bh (chunk c reads slot
+// (c+1)&1, writes slot c&1): 64 KB per bh, resident in L2.
+// The wait for a predecessor is bounded (with nanosleep backoff); on expiry
+// the tile sets the status flag, and the CTA stops after its MMAs drain.
+constexpr uint32_t kFQ = 0;                        // Qr K-major (A of G, Z)
+constexpr uint32_t kFK = kFQ + kChunkImg;          // Kr K-major (B of G, A of dS^T); then W
+constexpr uint32_t kFX = kFK + kChunkImg;          // X MN-major (B of Y)
+constexpr uint32_t kFXw = kFX + 128 * 64 * 2;      // w o X MN-major (B of dS^T)
+// S_in^T MN-major (B of Z) reuses w o X: it is written in the chain step,
+// after group 1 (the only reader of w o X) has completed
+constexpr uint32_t kFS = kFXw;
+constexpr uint32_t kFGate = kFXw + 128 * 64 * 2;   // lcum, scale, gamma, w
+constexpr uint32_t kFMisc = kFGate + 4 * 128 * 4;
+constexpr uint32_t kFSmem = kFMisc + 64;
+
+struct ChainWs {
+    float* slots;            // [bh][2][dqk][dv] fp32 outgoing states
+    unsigned int* flags;     // [bh] chunks published (zeroed per launch)
+    unsigned int* counter;   // tile counter (zeroed per launch)
+};
+
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// bounded wait until *flag >= want; false on expiry (about a second)
+__device__ __forceinline__ bool wait_flag(const unsigned int* flag, unsigned int want) {
+    for (uint32_t it = 0; it < (1u << 22); ++it) {
+        if (ld_acquire(flag) >= want) return true;
+        __nanosleep(256);
+    }
+    return false;
+}
+
+__global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainWs cw, int n_chunks) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    float* lcum = reinterpret_cast<float*>(smem + kFGate);  // log2 units
+    float* scl = lcum + kTcQ;
+    float* gam = scl + kTcQ;
+    float* wdec = gam + kTcQ;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kFMisc);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kFMisc + 16);
+    int* tile_slot = reinterpret_cast<int*>(smem + kFMisc + 24);
+    float* last_decay = reinterpret_cast<float*>(smem + kFMisc + 28);
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    constexpr int kSt = kTcN * kTcP;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t H = p.heads, L = p.len, BH = p.batch * p.heads;
+    const int64_t n_tiles = BH * n_chunks;
+
+    if (warp == 0) tmem_alloc(tmem_slot, 256);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int hc = warp >> 2;                 // column half of this warp
+    const int r = (warp & 3) * 32 + lane;     // TMEM lane: row i (G, Y, Z) / state row n (dS)
+    const uint32_t tG = tmem, tY = tmem, tZ = tmem + 64, tS = tmem + 128;
+    uint32_t phase = 0;
+    bool ok = true;
+
+    while (ok) {
+        if (tid == 0) *tile_slot = static_cast<int>(atomicAdd(cw.counter, 1u));
+        __syncthreads();
+        const int64_t tile = *tile_slot;
+        if (tile >= n_tiles) break;
+        const int64_t bh = tile % BH;
+        const int ch = static_cast<int>(tile / BH);
+        const int64_t bi = bh / H, h = bh % H;
+        const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
+
+        float xv[kXItems][8];
+        load_x(p, bi, h, it0, xv);
+        if (warp == 0) tile_gates(p, bh, it0, lcum, scl, gam, wdec, last_decay);
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < kXItems; ++q) {
+            int j, pc;
+            x_item(q, j, pc);
+            const float w = wdec[j];
+            float xw[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xw[e] = w * xv[q][e];
+            const uint32_t o = mnmaj_off(pc * 8, j, kTcP);
+            *reinterpret_cast<uint4*>(smem + kFX + o) = pack8(xv[q]);
+            *reinterpret_cast<uint4*>(smem + kFXw + o) = pack8(xw);
+        }
+        stage_qk<true>(p, bi, h, it0, smem + kFQ, smem + kFK);
+        if (p.last_bx && ch == n_chunks - 1 && tid < kTcN / 2) {
+            const int jl = static_cast<int>(L - 1 - it0);
+            const int64_t t = p.reverse ? 0 : L - 1;
+            const int64_t qk = (bi * L + t) * kTcN;
+            const float* kb = p.k_bias + h * kTcN;
+            const int64_t cs = ((bi * L + t) * H + h) * (kTcN / 2) + tid;
+            const float c = p.cos[cs], s = p.sin[cs];
+            const float a0 = p.k[qk + 2 * tid] + kb[2 * tid];
+            const float a1 = p.k[qk + 2 * tid + 1] + kb[2 * tid + 1];
+            p.last_bx[bh * kTcN + 2 * tid] = scl[jl] * (a0 * c - a1 * s);
+            p.last_bx[bh * kTcN + 2 * tid + 1] = scl[jl] * (a0 * s + a1 * c);
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        // ---- group 1: G = Qr Kr^T; dS^T = Kr^T (w o X)
+        if (tid == 0) {
+            const uint32_t id_G = instr_desc(128, 128, false, false);
+            const uint32_t id_S = instr_desc(128, kTcP, true, true);
+#pragma unroll
+            for (int kb = 0; kb < kTcN / 16; ++kb) {
+                const uint64_t a = smem_desc(sbase + kFQ + kb * 2 * 16 * 128, 16 * 128, 128);
+                const uint64_t b = smem_desc(sbase + kFK + kb * 2 * 16 * 128, 16 * 128, 128);
+                umma(tG, a, b, id_G, kb > 0);
+            }
+            for (int kb = 0; kb < kTcQ / 16; ++kb) {
+                const uint64_t a = smem_desc(sbase + kFK + kb * 2 * 128, 128, 16 * 128);
+                const uint64_t b = smem_desc(sbase + kFXw + kb * 2 * 8 * 128, 8 * 128, 128);
+                umma(tS, a, b, id_S, kb > 0);
+            }
+            umma_commit(bar);
+        }
+        ok = cta_wait(bar, phase);
+        phase ^= 1;
+        if (!ok) break;
+        tc_fence_after();
+        {
+            // W = mask o G (row i = r, this warp's column half) over Kr
+            const float li = lcum[r], gi = gam[r];
+#pragma unroll
+            for (int cb = 0; cb < 2; ++cb) {
+                float g[32];
+                tmem_ld32(tG + t_lane + hc * 64 + cb * 32, g);
+#pragma unroll
+                for (int c8 = 0; c8 < 4; ++c8) {
+                    const int j0 = hc * 64 + cb * 32 + c8 * 8;
+                    const float4 la = *reinterpret_cast<const float4*>(lcum + j0);
+                    const float4 lb = *reinterpret_cast<const float4*>(lcum + j0 + 4);
+                    const float4 sa = *reinterpret_cast<const float4*>(scl + j0);
+                    const float4 sb = *reinterpret_cast<const float4*>(scl + j0 + 4);
+                    const float lj[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+                    const float sj[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+                    float wv[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const int j = j0 + c;
+                        const float m = j < r ? ex2_approx(li - lj[c]) * sj[c] : (j == r ? gi : 0.f);
+                        wv[c] = m * g[c8 * 8 + c];
+                    }
+                    *reinterpret_cast<uint4*>(smem + kFK + kmaj_off(r, j0, 128)) = pack8(wv);
+                }
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (tid == 0) {
+            const uint32_t id_Y = instr_desc(128, kTcP, false, true);
+            for (int kb = 0; kb < kTcQ / 16; ++kb) {
+                const uint64_t a = smem_desc(sbase + kFK + kb * 2 * 16 * 128, 16 * 128, 128);
+                const uint64_t b = smem_desc(sbase + kFX + kb * 2 * 8 * 128, 8 * 128, 128);
+                umma(tY, a, b, id_Y, kb > 0);
+            }
+            // no commit yet: Z joins this group after the chain step
+        }
+        // ---- chain: S_in from the predecessor chunk, S_out published
+        {
+            bool got = true;
+            if (tid == 0 && ch > 0) got = wait_flag(cw.flags + bh, static_cast<unsigned>(ch));
+            if (__syncthreads_or(!got)) {
+                if (tid == 0) atomicExch(&g_tc_status, 1);
+                ok = false;
+                if (tid == 0) umma_commit(bar);  // drain the issued Y before leaving
+                mbar_wait(bar, phase);
+                break;
+            }
+            float sin_[32], ds[32];
+            float* slot_in = cw.slots + (bh * 2 + ((ch + 1) & 1)) * kSt + r * kTcP + hc * 32;
+            float* slot_out = cw.slots + (bh * 2 + (ch & 1)) * kSt + r * kTcP + hc * 32;
+            if (ch > 0) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 v4 = __ldcg(reinterpret_cast<const float4*>(slot_in) + q);
+                    sin_[4 * q] = v4.x; sin_[4 * q + 1] = v4.y; sin_[4 * q + 2] = v4.z; sin_[4 * q + 3] = v4.w;
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 32; ++q) sin_[q] = 0.f;
+            }
+            tmem_ld32(tS + t_lane + hc * 32, ds);
+            const float dec = *last_decay;
+            float so[32];
+#pragma unroll
+            for (int q = 0; q < 32; ++q) so[q] = fmaf(dec, sin_[q], ds[q]);
+            if (ch + 1 < n_chunks) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    __stcg(reinterpret_cast<float4*>(slot_out) + q,
+                           make_float4(so[4 * q], so[4 * q + 1], so[4 * q + 2], so[4 * q + 3]));
+                __threadfence();
+            } else if (p.last_state) {
+                // final state, (p, n) layout
+#pragma unroll
+                for (int q = 0; q < 32; ++q) p.last_state[(bh * kTcP + hc * 32 + q) * kTcN + r] = so[q];
+            }
+            // S_in^T operand image (m = p, k = n): 4 chunks of 8 p at state row r
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = sin_[c8 * 8 + e];
+                *reinterpret_cast<uint4*>(smem + kFS + mnmaj_off(hc * 32 + c8 * 8, r, kTcP)) = pack8(f);
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();  // every thread's S_out stores precede the release below
+            tc_fence_after();
+            if (tid == 0 && ch + 1 < n_chunks) {
+                __threadfence();
+                st_release(cw.flags + bh, static_cast<unsigned>(ch + 1));
+            }
+        }
+        if (tid == 0) {
+            if (ch > 0) {
+                const uint32_t id_Z = instr_desc(128, kTcP, false, true);
+#pragma unroll
+                for (int kb = 0; kb < kTcN / 16; ++kb) {
+                    const uint64_t a = smem_desc(sbase + kFQ + kb * 2 * 16 * 128, 16 * 128, 128);
+                    const uint64_t b = smem_desc(sbase + kFS + kb * 2 * 8 * 128, 8 * 128, 128);
+                    umma(tZ, a, b, id_Z, kb > 0);
+                }
+            }
+            umma_commit(bar);
+        }
+        ok = cta_wait(bar, phase);
+        phase ^= 1;
+        if (!ok) break;
+        tc_fence_after();
+        {
+            float y[32];
+            tmem_ld32(tY + t_lane + hc * 32, y);
+            if (ch > 0) {
+                float zt[32];
+                tmem_ld32(tZ + t_lane + hc * 32, zt);
+                const float el = ex2_approx(lcum[r]);
+#pragma unroll
+                for (int q = 0; q < 32; ++q) y[q] = fmaf(el, zt[q], y[q]);
+            }
+            const int64_t it = it0 + r;
+            if (it < L) {
+                const float dsk = p.d_skip ? p.d_skip[h] : 0.f;
+                const int64_t t = p.reverse ? L - 1 - it : it;
+                const int64_t voff = ((bi * L + t) * H + h) * kTcP + hc * 32;
+                float* o = p.out + (bh * L + t) * kTcP + hc * 32;
+                float4 vv[8], zz[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    vv[q] = __ldg(reinterpret_cast<const float4*>(p.v + voff) + q);
+                    zz[q] = p.z ? __ldg(reinterpret_cast<const float4*>(p.z + voff) + q)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    float r4[4] = {fmaf(dsk, vv[q].x, y[4 * q]), fmaf(dsk, vv[q].y, y[4 * q + 1]),
+                                   fmaf(dsk, vv[q].z, y[4 * q + 2]), fmaf(dsk, vv[q].w, y[4 * q + 3])};
+                    if (p.z) {
+                        r4[0] *= silu_f(zz[q].x);
+                        r4[1] *= silu_f(zz[q].y);
+                        r4[2] *= silu_f(zz[q].z);
+                        r4[3] *= silu_f(zz[q].w);
+                    }
+                    *reinterpret_cast<float4*>(o + 4 * q) = make_float4(r4[0], r4[1], r4[2], r4[3]);
+                }
+            }
+        }
+        // the next tile overwrites shared memory and tensor memory
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    if (!ok) mbar_wait(bar, phase ^ 1);  // MMAs still in flight: bounded second wait
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
 }  // namespace
 
 bool m3_tc_applicable(const M3Params& p) {
@@ -733,7 +1045,8 @@ cudaError_t workspace_pool(cudaMemPool_t* out) {
 }
 }  // namespace
 
-cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
+// Three-launch form (kernels A, B, C): selected with B200SCAN_M3_TC_SPLIT=1.
+cudaError_t m3_tc_launch_split(const M3Params& p, cudaStream_t stream) {
     const int64_t bh = p.batch * p.heads;
     const int n_chunks = static_cast<int>((p.len + kTcQ - 1) / kTcQ);
     cudaError_t e = cudaFuncSetAttribute(m3_tc_out, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -774,6 +1087,46 @@ cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
     }
     const cudaError_t ef = cudaFreeAsync(raw, stream);
     return e != cudaSuccess ? e : ef;
+}
+
+
+cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
+    const int64_t bh = p.batch * p.heads;
+    const int n_chunks = static_cast<int>((p.len + kTcQ - 1) / kTcQ);
+    cudaError_t e = cudaFuncSetAttribute(m3_tc_fused, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kFSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(m3_tc_fused, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    cudaMemPool_t pool = nullptr;
+    e = workspace_pool(&pool);
+    if (e != cudaSuccess) return e;
+    const size_t slot_bytes = static_cast<size_t>(bh) * 2 * kChunkSt;
+    const size_t flag_bytes = static_cast<size_t>(bh + 1) * sizeof(unsigned int);
+    void* raw = nullptr;
+    e = cudaMallocFromPoolAsync(&raw, slot_bytes + flag_bytes, pool, stream);
+    if (e != cudaSuccess) return e;
+    ChainWs cw;
+    cw.slots = static_cast<float*>(raw);
+    cw.flags = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(raw) + slot_bytes);
+    cw.counter = cw.flags + bh;
+    e = cudaMemsetAsync(cw.flags, 0, flag_bytes, stream);
+    if (e == cudaSuccess) {
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int64_t units = bh * n_chunks;
+        const int64_t grid = units < 2 * sms ? units : 2 * sms;
+        m3_tc_fused<<<static_cast<unsigned>(grid), kTcThreads2, kFSmem, stream>>>(p, cw, n_chunks);
+        e = cudaGetLastError();
+    }
+    const cudaError_t ef = cudaFreeAsync(raw, stream);
+    return e != cudaSuccess ? e : ef;
+}
+
+cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
+    const char* v = std::getenv("B200SCAN_M3_TC_SPLIT");
+    return (v && v[0] == '1') ? m3_tc_launch_split(p, stream) : m3_tc_launch_fused(p, stream);
 }
 
 int m3_tc_status_and_clear() {
