@@ -47,6 +47,15 @@ class ArmMamba3Dims(ctypes.Structure):
     _fields_ = [(n, ctypes.c_size_t) for n in ("batch", "heads", "dv", "dqk", "len", "rank")]
 
 
+class ArmMamba3TcOptions(ctypes.Structure):
+    _fields_ = [("in_dtype", ctypes.c_int), ("out_dtype", ctypes.c_int),
+                ("out_layout", ctypes.c_int), ("angles_shared", ctypes.c_int),
+                ("n_angles", ctypes.c_size_t)]
+
+
+DTYPE_F32, DTYPE_BF16 = 0, 1
+
+
 def _candidate_paths():
     env = os.environ.get("ARM_SCAN_LIB")
     if env:
@@ -91,6 +100,10 @@ def _bind(lib):
               "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
               "arm_scan_tensor_status"):
         getattr(lib, f).restype = ctypes.c_int
+    lib.arm_scan_mamba3_siso_tc_async.restype = ctypes.c_int
+    lib.arm_scan_mamba3_siso_tc_async.argtypes = [
+        ctypes.POINTER(ArmMamba3Dims), ctypes.POINTER(ArmMamba3TcOptions), *([_VP] * 11),
+        ctypes.c_int, _VP, _VP, _VP, _VP]
 
 
 def load():
@@ -181,6 +194,17 @@ def mamba3_raw(dims, ptrs, reverse, backend, threading, ptr_out, ptr_last_state,
                "arm_scan_mamba3_scan_f32_async")
 
 
+def mamba3_tc_raw(dims, opts, ptrs, reverse, ptr_out, ptr_last_state, ptr_last_bx, stream):
+    """Tensor-core Mamba-3 SISO with the angle pre-pass fused in.  ``ptrs``:
+    q, k, v, adt, dt, trap, q_bias, k_bias, angles, d_skip, z (the last two
+    may be 0).  Device pointers, stream-ordered."""
+    if len(ptrs) != 11:
+        raise ValueError(f"expected 11 input pointers, got {len(ptrs)}")
+    _check(load().arm_scan_mamba3_siso_tc_async(
+        ctypes.byref(dims), ctypes.byref(opts), *[_n(p) for p in ptrs], int(reverse), ptr_out,
+        _n(ptr_last_state), _n(ptr_last_bx), _n(stream)), "arm_scan_mamba3_siso_tc_async")
+
+
 def angles_workspace_bytes(dims, n_angles):
     return int(load().arm_scan_mamba3_angles_workspace_bytes(ctypes.byref(dims), n_angles))
 
@@ -207,7 +231,8 @@ def exported_symbols():
             "arm_scan_selective_scan_bidirectional_f32_async",
             "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
             "arm_scan_mamba3_angles_workspace_bytes", "arm_scan_mamba3_angles_f32_async",
-            "arm_scan_mamba3_angles_f32_noalloc", "arm_scan_tensor_status"]
+            "arm_scan_mamba3_angles_f32_noalloc", "arm_scan_tensor_status",
+            "arm_scan_mamba3_siso_tc_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

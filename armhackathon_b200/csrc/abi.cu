@@ -514,6 +514,55 @@ int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const fl
 
 int arm_scan_tensor_status(void) { return tensor_status_code(); }
 
+int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOptions* opts,
+                                  const void* q, const void* k, const void* v, const float* adt,
+                                  const float* dt, const float* trap, const float* q_bias,
+                                  const float* k_bias, const void* angles, const float* d_skip,
+                                  const void* z, int reverse, void* out, float* last_state,
+                                  float* last_bx, void* stream) {
+    if (!opts) return fail(ARM_SCAN_ERR_NULL_POINTER, "opts is null");
+    const void* req[] = {dims, q, k, v, adt, dt, trap, q_bias, k_bias, out};
+    bool mimo = false;
+    int rc = m3_check_ptrs(req, 10, last_state, last_bx, nullptr, nullptr, nullptr, &mimo);
+    if (rc) return rc;
+    if (opts->n_angles > 0 && !angles)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "angles is null with n_angles > 0");
+    auto is_dtype = [](int d) { return d == ARM_SCAN_DTYPE_F32 || d == ARM_SCAN_DTYPE_BF16; };
+    if (!is_dtype(opts->in_dtype) || !is_dtype(opts->out_dtype))
+        return fail(ARM_SCAN_ERR_BAD_ENUM, "dtype must be ARM_SCAN_DTYPE_F32 (0) or _BF16 (1)");
+    if (opts->out_layout != 0 && opts->out_layout != 1)
+        return fail(ARM_SCAN_ERR_BAD_ENUM, "out_layout must be 0 or 1, got %d", opts->out_layout);
+    if (opts->angles_shared != 0 && opts->angles_shared != 1)
+        return fail(ARM_SCAN_ERR_BAD_ENUM, "angles_shared must be 0 or 1, got %d", opts->angles_shared);
+    M3Counts cnt;
+    if ((rc = m3_validate(dims, false, last_state, last_bx, &cnt))) return rc;
+    if (dims->rank != 1)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "the tensor-core entry is SISO (rank 1)");
+    if (opts->n_angles > dims->dqk / 2)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "n_angles (%zu) exceeds dqk/2 (%zu)", opts->n_angles,
+                    dims->dqk / 2);
+    std::vector<void*> p = {
+        const_cast<void*>(q),        const_cast<void*>(k),        const_cast<void*>(v),
+        const_cast<float*>(adt),     const_cast<float*>(dt),      const_cast<float*>(trap),
+        const_cast<float*>(q_bias),  const_cast<float*>(k_bias),  nullptr,
+        nullptr,                     const_cast<float*>(d_skip),  const_cast<void*>(z),
+        nullptr,                     nullptr,                     nullptr,
+        out,                         last_state,                  last_bx};
+    M3Params m = m3_params(dims, p, reverse);
+    m.angles = angles;
+    m.n_angles = static_cast<int64_t>(opts->n_angles);
+    m.angles_shared = opts->angles_shared;
+    m.in_bf16 = opts->in_dtype == ARM_SCAN_DTYPE_BF16;
+    m.out_bf16 = opts->out_dtype == ARM_SCAN_DTYPE_BF16;
+    m.out_blh = opts->out_layout;
+    if (!m3_tc_angles_applicable(m))
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE,
+                    "the tensor-core entry covers dqk 128, dv 64 with 16-byte aligned q/k/v/z/out "
+                    "and biases");
+    cudaError_t e = m3_tc_launch(m, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "mamba3_siso_tc launch");
+}
+
 int arm_scan_mamba3_scan_f32_async(const ArmMamba3Dims* dims, const float* q, const float* k,
                                    const float* v, const float* adt, const float* dt,
                                    const float* trap, const float* q_bias, const float* k_bias,

@@ -29,6 +29,13 @@ struct M3Params {
     float* last_bx;       // nullable, (b, h, dqk), SISO only
     int64_t batch, heads, dv, dqk, len, rank;
     int reverse;
+    // tensor-core extension (arm_scan_mamba3_siso_tc_async); zero otherwise
+    const void* angles;     // raw RoPE angles, (b, l, n_angles) shared or (b, l, h, n_angles)
+    int64_t n_angles;       // rotated pairs; pairs >= n_angles are unrotated
+    int angles_shared;      // 1: one angle row per (b, l) for all heads
+    int in_bf16;            // q, k, v, z, angles are bf16 (else fp32)
+    int out_bf16;           // out is bf16 (else fp32)
+    int out_blh;            // out is (b, l, h, dv) (else head-major (b, h, l, dv))
 };
 
 bool m3_shape_supported(int64_t dv, int64_t dqk, int64_t rank);
@@ -40,5 +47,7 @@ cudaError_t m3_chunk_launch(const M3Params& p, cudaStream_t stream);
 bool m3_tc_applicable(const M3Params& p);
 cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream);
 int m3_tc_status_and_clear();  // 1 if a bounded wait expired since the last call
+// true if p (with angles set) is a shape the extension entry covers
+bool m3_tc_angles_applicable(const M3Params& p);
 
 }  // namespace b200scan

@@ -706,7 +706,8 @@ constexpr uint32_t kFXw = kFX + 128 * 64 * 2;      // w o X MN-major (B of dS^T)
 // after group 1 (the only reader of w o X) has completed
 constexpr uint32_t kFS = kFXw;
 constexpr uint32_t kFGate = kFXw + 128 * 64 * 2;   // lcum, scale, gamma, w
-constexpr uint32_t kFMisc = kFGate + 4 * 128 * 4;
+constexpr uint32_t kFQtot = kFGate + 4 * 128 * 4;  // angles mode: [4 quadrants][64 pairs], theta0[64]
+constexpr uint32_t kFMisc = kFQtot + 5 * 64 * 4;
 constexpr uint32_t kFSmem = kFMisc + 64;
 
 struct ChainWs {
@@ -733,7 +734,271 @@ __device__ __forceinline__ bool wait_flag(const unsigned int* flag, unsigned int
     return false;
 }
 
-__global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainWs cw, int n_chunks) {
+// ---- typed input helpers (fp32 or bf16 rows of 8) ------------------------
+__device__ __forceinline__ float bf16_to_f(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+
+template <bool IN16>
+__device__ __forceinline__ void ld8_in(const void* base, int64_t idx, float (&f)[8]) {
+    if (IN16) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + idx));
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            f[2 * e] = bf16_to_f(w[e] & 0xFFFFu);
+            f[2 * e + 1] = bf16_to_f(w[e] >> 16);
+        }
+    } else {
+        ldg8(static_cast<const float*>(base) + idx, f);
+    }
+}
+
+template <bool IN16>
+__device__ __forceinline__ float ld1_in(const void* base, int64_t idx) {
+    if (IN16) return bf16_to_f(__ldg(static_cast<const uint16_t*>(base) + idx));
+    return __ldg(static_cast<const float*>(base) + idx);
+}
+
+template <bool IN16>
+__device__ __forceinline__ void load_x_t(const M3Params& p, int64_t bi, int64_t h, int64_t it0,
+                                         float (&xv)[kXItems][8]) {
+    const int64_t L = p.len, H = p.heads;
+#pragma unroll
+    for (int r = 0; r < kXItems; ++r) {
+        int j, pc;
+        x_item(r, j, pc);
+        const int64_t it = it0 + j;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xv[r][e] = 0.f;
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            ld8_in<IN16>(p.v, ((bi * L + t) * H + h) * kTcP + pc * 8, xv[r]);
+        }
+    }
+}
+
+// ---- angle pre-pass (angles mode) ----------------------------------------
+// Natural-time range [lo, hi) of traversal chunk c.
+__device__ __forceinline__ void chunk_range(int64_t L, int c, int reverse, int64_t& lo, int64_t& hi) {
+    if (!reverse) {
+        lo = static_cast<int64_t>(c) * kTcQ;
+        hi = lo + kTcQ < L ? lo + kTcQ : L;
+    } else {
+        hi = L - static_cast<int64_t>(c) * kTcQ;
+        lo = hi - kTcQ > 0 ? hi - kTcQ : 0;
+    }
+}
+
+// Per (traversal chunk, bh, pair): sum of tanh(angle) * pi * dt over the
+// chunk's steps -> theta0[bh][c][pair]; also the table ta = tanh(angle) * pi
+// (written once per angle row: by head 0 when angles are shared).  256
+// threads: pair = tid % 64, quarter = tid / 64 takes 32 of the 128 steps.
+template <bool IN16>
+__global__ void __launch_bounds__(256) m3_tc_angle_sums(M3Params p, float* ta, float* theta0,
+                                                       int n_chunks) {
+    __shared__ float part[4][64];
+    const int c = blockIdx.x;
+    const int64_t bh = blockIdx.y;
+    const int pr = threadIdx.x & 63, qr = threadIdx.x >> 6;
+    const int64_t H = p.heads, L = p.len, NA = p.n_angles;
+    const int64_t bi = bh / H, h = bh % H;
+    int64_t lo, hi;
+    chunk_range(L, c, p.reverse, lo, hi);
+    const int64_t qlo = lo + 32 * qr < hi ? lo + 32 * qr : hi;
+    const int64_t qhi = qlo + 32 < hi ? qlo + 32 : hi;
+    const bool writer = !p.angles_shared || h == 0;
+    const float* dt = p.dt + bh * L;
+    constexpr float kPiF = 3.14159265358979323846f;
+    float s = 0.f;
+    if (pr < NA) {
+        for (int64_t t = qlo; t < qhi; t += 8) {
+            float a[8], d[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const bool in = t + u < qhi;
+                const int64_t row = p.angles_shared ? (bi * L + t + u) : ((bi * L + t + u) * H + h);
+                a[u] = in ? ld1_in<IN16>(p.angles, row * NA + pr) : 0.f;
+                d[u] = in ? __ldg(dt + t + u) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (t + u >= qhi) break;
+                const float tv = tanhf(a[u]) * kPiF;
+                s = fmaf(tv, d[u], s);
+                if (writer) {
+                    const int64_t row = p.angles_shared ? (bi * L + t + u) : ((bi * L + t + u) * H + h);
+                    ta[row * NA + pr] = tv;
+                }
+            }
+        }
+    }
+    part[qr][pr] = s;
+    __syncthreads();
+    if (qr == 0 && pr < NA)
+        theta0[(bh * n_chunks + c) * 64 + pr] = ((part[0][pr] + part[1][pr]) + part[2][pr]) + part[3][pr];
+}
+
+// Exclusive prefix of the chunk sums in natural-time order, in place.
+__global__ void m3_tc_angle_prefix(M3Params p, float* theta0, int n_chunks) {
+    const int64_t bh = blockIdx.x;
+    const int pr = threadIdx.x;
+    if (pr >= p.n_angles) return;
+    float acc = 0.f;
+    for (int i = 0; i < n_chunks; ++i) {
+        const int c = p.reverse ? n_chunks - 1 - i : i;
+        float* cell = theta0 + (bh * n_chunks + c) * 64 + pr;
+        const float v = *cell;
+        *cell = acc;
+        acc += v;
+    }
+}
+
+// Rotated q, k rows of one chunk from raw angles, in two parts around the
+// gate pass's barrier.  Lane = step within the warp's quadrant
+// (j = 32 * (warp & 3) + lane); the warp pair (w, w + 4) splits the 16 dim
+// chunks (kc = 2 i + (warp >> 2)).  theta(step, pair) = theta0(chunk) +
+// prefix over the chunk's steps, in natural time order, of ta * dt: a warp
+// scan over lanes plus the totals of the quadrants before.
+//
+// Part A (before the barrier): increments, warp scans, quadrant totals and
+// the chunk's theta0 row into shared memory.
+__device__ __forceinline__ void ang_part_a(const M3Params& p, const float* ta, const float* theta0,
+                                           int64_t bi, int64_t h, int64_t bh, int ch,
+                                           int n_chunks, int64_t it0, float (&th)[8][4],
+                                           float* qtot, float* th0s) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int qd = warp & 3, sub = warp >> 2;
+    const int64_t L = p.len, H = p.heads, NA = p.n_angles;
+    const int j = qd * 32 + lane;
+    const int64_t it = it0 + j;
+    const bool live = it < L;
+    const bool rev = p.reverse != 0;
+    const int64_t t = live ? (rev ? L - 1 - it : it) : 0;
+    if (tid < NA) th0s[tid] = __ldg(theta0 + (bh * n_chunks + ch) * 64 + tid);
+    const float dtv = live ? __ldg(p.dt + bh * L + t) : 0.f;
+    const int64_t arow = p.angles_shared ? (bi * L + t) : ((bi * L + t) * H + h);
+    const float* tr = ta + arow * NA;
+    if ((NA & 3) == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int kc = 2 * i + sub;
+            float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (live && 4 * kc < NA) v4 = __ldg(reinterpret_cast<const float4*>(tr) + kc);
+            th[i][0] = v4.x * dtv;
+            th[i][1] = v4.y * dtv;
+            th[i][2] = v4.z * dtv;
+            th[i][3] = v4.w * dtv;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int pr = 4 * (2 * i + sub) + e;
+                th[i][e] = (live && pr < NA) ? __ldg(tr + pr) * dtv : 0.f;
+            }
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float v = rev ? __shfl_down_sync(0xffffffffu, th[i][e], o)
+                                    : __shfl_up_sync(0xffffffffu, th[i][e], o);
+                if (rev ? lane + o < 32 : lane >= o) th[i][e] += v;
+            }
+    }
+    if (lane == (rev ? 0 : 31)) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) qtot[qd * 64 + 4 * (2 * i + sub) + e] = th[i][e];
+    }
+}
+
+// Part B (after the barrier): quadrant offsets, then q, k loads (two items
+// per round trip), rotation, bf16 operand images, and the fp32 carry k.
+template <bool IN16>
+__device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_t h, int64_t bh,
+                                           int64_t it0, float (&th)[8][4], const float* qtot,
+                                           const float* th0s, uint8_t* img_q, uint8_t* img_k,
+                                           const float* scl) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int qd = warp & 3, sub = warp >> 2;
+    const int64_t L = p.len, NA = p.n_angles;
+    const int j = qd * 32 + lane;
+    const int64_t it = it0 + j;
+    const bool live = it < L;
+    const bool rev = p.reverse != 0;
+    const int64_t t = live ? (rev ? L - 1 - it : it) : 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int pr = 4 * (2 * i + sub) + e;
+            if (pr >= NA) continue;
+            float off = th0s[pr];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (rev ? q > qd : q < qd) off += qtot[q * 64 + pr];
+            th[i][e] += off;
+        }
+    const float* qb = p.q_bias + h * kTcN;
+    const float* kb = p.k_bias + h * kTcN;
+    const bool want_bx = p.last_bx && live && it == L - 1;
+    const int64_t qrow = (bi * L + t) * kTcN;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        float qa[2][8], ka[2][8];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int kc = 2 * (2 * m + u) + sub;
+            if (live) {
+                ld8_in<IN16>(p.q, qrow + kc * 8, qa[u]);
+                ld8_in<IN16>(p.k, qrow + kc * 8, ka[u]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) qa[u][e] = ka[u][e] = 0.f;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int i = 2 * m + u;
+            const int kc = 2 * i + sub;
+            float qbb[8], kbb[8], qr[8], kr[8];
+            ldg8(qb + kc * 8, qbb);
+            ldg8(kb + kc * 8, kbb);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float sn = 0.f, cs = 1.f;
+                if (4 * kc + e < NA) __sincosf(th[i][e], &sn, &cs);
+                float a0 = qa[u][2 * e] + qbb[2 * e], a1 = qa[u][2 * e + 1] + qbb[2 * e + 1];
+                qr[2 * e] = a0 * cs - a1 * sn;
+                qr[2 * e + 1] = a0 * sn + a1 * cs;
+                a0 = ka[u][2 * e] + kbb[2 * e];
+                a1 = ka[u][2 * e + 1] + kbb[2 * e + 1];
+                kr[2 * e] = a0 * cs - a1 * sn;
+                kr[2 * e + 1] = a0 * sn + a1 * cs;
+            }
+            if (!live) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) qr[e] = kr[e] = 0.f;
+            }
+            if (want_bx) {
+                // scale_T * k_T for the carry: rotated k of the final step, fp32
+#pragma unroll
+                for (int e = 0; e < 8; ++e) p.last_bx[bh * kTcN + kc * 8 + e] = scl[j] * kr[e];
+            }
+            const uint32_t ko = kmaj_off(j, kc * 8, 128);
+            *reinterpret_cast<uint4*>(img_q + ko) = pack8(qr);
+            *reinterpret_cast<uint4*>(img_k + ko) = pack8(kr);
+        }
+    }
+}
+
+template <bool ANG, bool IN16, bool OUT16>
+__global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainWs cw, int n_chunks,
+                                                             const float* ta, const float* theta0) {
     extern __shared__ __align__(1024) uint8_t smem[];
     float* lcum = reinterpret_cast<float*>(smem + kFGate);  // log2 units
     float* scl = lcum + kTcQ;
@@ -743,6 +1008,8 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kFMisc + 16);
     int* tile_slot = reinterpret_cast<int*>(smem + kFMisc + 24);
     float* last_decay = reinterpret_cast<float*>(smem + kFMisc + 28);
+    float* qtot = reinterpret_cast<float*>(smem + kFQtot);  // angles mode: quadrant totals
+    float* th0s = qtot + 4 * 64;                            // angles mode: chunk's theta0
     const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
     constexpr int kSt = kTcN * kTcP;
 
@@ -777,7 +1044,9 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
 
         float xv[kXItems][8];
-        load_x(p, bi, h, it0, xv);
+        load_x_t<IN16>(p, bi, h, it0, xv);
+        float th[8][4];
+        if (ANG) ang_part_a(p, ta, theta0, bi, h, bh, ch, n_chunks, it0, th, qtot, th0s);
         if (warp == 0) tile_gates(p, bh, it0, lcum, scl, gam, wdec, last_decay);
         __syncthreads();
 #pragma unroll
@@ -792,8 +1061,11 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
             *reinterpret_cast<uint4*>(smem + kFX + o) = pack8(xv[q]);
             *reinterpret_cast<uint4*>(smem + kFXw + o) = pack8(xw);
         }
-        stage_qk<true>(p, bi, h, it0, smem + kFQ, smem + kFK);
-        if (p.last_bx && ch == n_chunks - 1 && tid < kTcN / 2) {
+        if (ANG)
+            ang_part_b<IN16>(p, bi, h, bh, it0, th, qtot, th0s, smem + kFQ, smem + kFK, scl);
+        else
+            stage_qk<true>(p, bi, h, it0, smem + kFQ, smem + kFK);
+        if (!ANG && p.last_bx && ch == n_chunks - 1 && tid < kTcN / 2) {
             const int jl = static_cast<int>(L - 1 - it0);
             const int64_t t = p.reverse ? 0 : L - 1;
             const int64_t qk = (bi * L + t) * kTcN;
@@ -958,25 +1230,28 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
                 const float dsk = p.d_skip ? p.d_skip[h] : 0.f;
                 const int64_t t = p.reverse ? L - 1 - it : it;
                 const int64_t voff = ((bi * L + t) * H + h) * kTcP + hc * 32;
-                float* o = p.out + (bh * L + t) * kTcP + hc * 32;
-                float4 vv[8], zz[8];
+                const int64_t ooff = (p.out_blh ? ((bi * L + t) * H + h) : (bh * L + t)) * kTcP + hc * 32;
+                float vv[4][8], zz[4][8];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    vv[q] = __ldg(reinterpret_cast<const float4*>(p.v + voff) + q);
-                    zz[q] = p.z ? __ldg(reinterpret_cast<const float4*>(p.z + voff) + q)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int q = 0; q < 4; ++q) {
+                    ld8_in<IN16>(p.v, voff + 8 * q, vv[q]);
+                    if (p.z) ld8_in<IN16>(p.z, voff + 8 * q, zz[q]);
                 }
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    float r4[4] = {fmaf(dsk, vv[q].x, y[4 * q]), fmaf(dsk, vv[q].y, y[4 * q + 1]),
-                                   fmaf(dsk, vv[q].z, y[4 * q + 2]), fmaf(dsk, vv[q].w, y[4 * q + 3])};
-                    if (p.z) {
-                        r4[0] *= silu_f(zz[q].x);
-                        r4[1] *= silu_f(zz[q].y);
-                        r4[2] *= silu_f(zz[q].z);
-                        r4[3] *= silu_f(zz[q].w);
+                for (int q = 0; q < 4; ++q) {
+                    float r8[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        r8[e] = fmaf(dsk, vv[q][e], y[8 * q + e]);
+                        if (p.z) r8[e] *= silu_f(zz[q][e]);
                     }
-                    *reinterpret_cast<float4*>(o + 4 * q) = make_float4(r4[0], r4[1], r4[2], r4[3]);
+                    if (OUT16) {
+                        *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + ooff + 8 * q) = pack8(r8);
+                    } else {
+                        float4* o4 = reinterpret_cast<float4*>(p.out + ooff + 8 * q);
+                        o4[0] = make_float4(r8[0], r8[1], r8[2], r8[3]);
+                        o4[1] = make_float4(r8[4], r8[5], r8[6], r8[7]);
+                    }
                 }
             }
         }
@@ -1001,6 +1276,13 @@ bool m3_tc_applicable(const M3Params& p) {
     return p.psi == nullptr && p.rank == 1 && p.dqk == kTcN && p.dv == kTcP && al(p.q) &&
            al(p.k) && al(p.v) && al(p.z) && al(p.out) && al(p.q_bias) && al(p.k_bias) &&
            al(p.cos) && al(p.sin) && p.len > 0;
+}
+
+bool m3_tc_angles_applicable(const M3Params& p) {
+    auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    return p.psi == nullptr && p.rank == 1 && p.dqk == kTcN && p.dv == kTcP && p.len > 0 &&
+           p.n_angles >= 0 && p.n_angles <= kTcN / 2 && al(p.q) && al(p.k) && al(p.v) &&
+           al(p.z) && al(p.out) && al(p.q_bias) && al(p.k_bias);
 }
 
 size_t m3_tc_workspace_bytes(const M3Params& p) {
@@ -1090,41 +1372,77 @@ cudaError_t m3_tc_launch_split(const M3Params& p, cudaStream_t stream) {
 }
 
 
+template <bool ANG, bool IN16, bool OUT16>
+cudaError_t launch_fused_kernel(const M3Params& p, const ChainWs& cw, int n_chunks, const float* ta,
+                                const float* theta0, cudaStream_t stream) {
+    auto kern = m3_tc_fused<ANG, IN16, OUT16>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kFSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t units = p.batch * p.heads * n_chunks;
+    const int64_t grid = units < 2 * sms ? units : 2 * sms;
+    kern<<<static_cast<unsigned>(grid), kTcThreads2, kFSmem, stream>>>(p, cw, n_chunks, ta, theta0);
+    return cudaGetLastError();
+}
+
 cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
     const int64_t bh = p.batch * p.heads;
     const int n_chunks = static_cast<int>((p.len + kTcQ - 1) / kTcQ);
-    cudaError_t e = cudaFuncSetAttribute(m3_tc_fused, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kFSmem));
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(m3_tc_fused, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (e != cudaSuccess) return e;
+    const bool ang = p.angles != nullptr;
     cudaMemPool_t pool = nullptr;
-    e = workspace_pool(&pool);
+    cudaError_t e = workspace_pool(&pool);
     if (e != cudaSuccess) return e;
     const size_t slot_bytes = static_cast<size_t>(bh) * 2 * kChunkSt;
-    const size_t flag_bytes = static_cast<size_t>(bh + 1) * sizeof(unsigned int);
+    const size_t flag_bytes = (static_cast<size_t>(bh + 1) * sizeof(unsigned int) + 255) / 256 * 256;
+    const size_t ta_floats =
+        ang ? static_cast<size_t>(p.batch * p.len * (p.angles_shared ? 1 : p.heads) * p.n_angles) : 0;
+    const size_t th_floats = ang ? static_cast<size_t>(bh) * n_chunks * 64 : 0;
     void* raw = nullptr;
-    e = cudaMallocFromPoolAsync(&raw, slot_bytes + flag_bytes, pool, stream);
+    e = cudaMallocFromPoolAsync(&raw, slot_bytes + flag_bytes + (ta_floats + th_floats) * 4 + 16,
+                                pool, stream);
     if (e != cudaSuccess) return e;
     ChainWs cw;
     cw.slots = static_cast<float*>(raw);
     cw.flags = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(raw) + slot_bytes);
     cw.counter = cw.flags + bh;
+    float* theta0 = reinterpret_cast<float*>(static_cast<uint8_t*>(raw) + slot_bytes + flag_bytes);
+    float* ta = theta0 + th_floats;
     e = cudaMemsetAsync(cw.flags, 0, flag_bytes, stream);
-    if (e == cudaSuccess) {
-        int dev = 0, sms = 148;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        const int64_t units = bh * n_chunks;
-        const int64_t grid = units < 2 * sms ? units : 2 * sms;
-        m3_tc_fused<<<static_cast<unsigned>(grid), kTcThreads2, kFSmem, stream>>>(p, cw, n_chunks);
+    if (e == cudaSuccess && ang && p.n_angles > 0) {
+        const dim3 g(static_cast<unsigned>(n_chunks), static_cast<unsigned>(bh));
+        if (p.in_bf16)
+            m3_tc_angle_sums<true><<<g, 256, 0, stream>>>(p, ta, theta0, n_chunks);
+        else
+            m3_tc_angle_sums<false><<<g, 256, 0, stream>>>(p, ta, theta0, n_chunks);
         e = cudaGetLastError();
+        if (e == cudaSuccess) {
+            m3_tc_angle_prefix<<<static_cast<unsigned>(bh), 64, 0, stream>>>(p, theta0, n_chunks);
+            e = cudaGetLastError();
+        }
+    }
+    if (e == cudaSuccess) {
+        if (!ang)
+            e = launch_fused_kernel<false, false, false>(p, cw, n_chunks, nullptr, nullptr, stream);
+        else if (p.in_bf16 && p.out_bf16)
+            e = launch_fused_kernel<true, true, true>(p, cw, n_chunks, ta, theta0, stream);
+        else if (p.in_bf16)
+            e = launch_fused_kernel<true, true, false>(p, cw, n_chunks, ta, theta0, stream);
+        else if (p.out_bf16)
+            e = launch_fused_kernel<true, false, true>(p, cw, n_chunks, ta, theta0, stream);
+        else
+            e = launch_fused_kernel<true, false, false>(p, cw, n_chunks, ta, theta0, stream);
     }
     const cudaError_t ef = cudaFreeAsync(raw, stream);
     return e != cudaSuccess ? e : ef;
 }
 
 cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
+    if (p.angles) return m3_tc_launch_fused(p, stream);
     const char* v = std::getenv("B200SCAN_M3_TC_SPLIT");
     return (v && v[0] == '1') ? m3_tc_launch_split(p, stream) : m3_tc_launch_fused(p, stream);
 }

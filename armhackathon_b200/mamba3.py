@@ -128,6 +128,75 @@ def _(q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, d_skip, z, reverse,
     return v.new_empty((b, length, h, dv)), v.new_empty((b, h, dv, dqk))
 
 
+@torch.library.custom_op("arm_scan::mamba3_scan_tc", mutates_args=())
+def _mamba3_scan_tc_op(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    adt: torch.Tensor,
+    dt: torch.Tensor,
+    trap: torch.Tensor,
+    q_bias: torch.Tensor,
+    k_bias: torch.Tensor,
+    angles: torch.Tensor,
+    d_skip: Optional[torch.Tensor],
+    z: Optional[torch.Tensor],
+    reverse: bool,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    # q, k, v, z, angles share one dtype (fp32 or bf16); out has it too and
+    # is written directly in (b, l, h, dv)
+    b, length, _, dqk = q.shape
+    h, dv = v.shape[2], v.shape[3]
+    dims = _ffi.ArmMamba3Dims(b, h, dv, dqk, length, 1)
+    bf16 = q.dtype == torch.bfloat16
+    dtype = _ffi.DTYPE_BF16 if bf16 else _ffi.DTYPE_F32
+    opts = _ffi.ArmMamba3TcOptions(dtype, dtype, 1, 1 if angles.shape[2] == 1 else 0,
+                                   angles.shape[3])
+    out = v.new_empty((b, length, h, dv))
+    last_state = v.new_empty((b, h, dv, dqk), dtype=torch.float32)
+    last_bx = v.new_empty((b, h, dqk), dtype=torch.float32)
+    with _on_device(v):
+        _ffi.mamba3_tc_raw(
+            dims, opts,
+            [q.data_ptr(), k.data_ptr(), v.data_ptr(), adt.data_ptr(), dt.data_ptr(),
+             trap.data_ptr(), q_bias.data_ptr(), k_bias.data_ptr(), angles.data_ptr(),
+             _ptr(d_skip), _ptr(z)],
+            1 if reverse else 0, out.data_ptr(), last_state.data_ptr(), last_bx.data_ptr(),
+            _stream(v))
+    _CALLS["n"] += 1
+    return out, last_state
+
+
+@_mamba3_scan_tc_op.register_fake
+def _(q, k, v, adt, dt, trap, q_bias, k_bias, angles, d_skip, z, reverse):
+    b, length, _, dqk = q.shape
+    h, dv = v.shape[2], v.shape[3]
+    return v.new_empty((b, length, h, dv)), v.new_empty((b, h, dv, dqk), dtype=torch.float32)
+
+
+def _mamba3_tc_angles(q, k, v, adt, dt, trap, q_bias, k_bias, angles, D, z, reverse):
+    """precision="bf16" with raw angles: one tensor-core call with the angle
+    pre-pass fused in.  q, k, v, z, angles run in bf16 when q is bf16 (else
+    fp32); the output has that dtype."""
+    b, length, _, dqk = q.shape
+    h = v.shape[2]
+    if angles.dim() != 4 or angles.shape[:2] != (b, length) or angles.shape[2] not in (1, h):
+        raise ValueError(f"angles must be (b, l, h, r) or (b, l, 1, r), got {tuple(angles.shape)}")
+    if angles.shape[3] > dqk // 2:
+        raise ValueError(f"angles has {angles.shape[3]} pairs, more than dqk/2 = {dqk // 2}")
+    home = v.device
+    dev = home if home.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
+    io = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
+    big = lambda t: t.to(device=dev, dtype=io).contiguous()  # noqa: E731
+    f32 = lambda t: None if t is None else t.to(device=dev, dtype=torch.float32).contiguous()  # noqa: E731
+    out, last = _mamba3_scan_tc_op(
+        big(q), big(k), big(v), f32(adt), f32(dt), f32(trap), f32(q_bias), f32(k_bias),
+        big(angles), f32(D), None if z is None else big(z), bool(reverse))
+    if home.type != "cuda":
+        out, last = out.to(home), last.to(home)
+    return out, last
+
+
 def _check_shapes(q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, D, z):
     """Every tensor against the SISO layout contract.  The C entry point is
     told how many elements to read, so a short buffer would be an
@@ -176,6 +245,9 @@ def mamba3_scan(q, k, v, adt, dt, trap, q_bias, k_bias, angles=None,
     precision "fp32" (default): fp32 arithmetic throughout.  "bf16": the
     tensor-core kernel -- q/k/v/W operands rounded to bf16, fp32
     accumulation and fp32 state (for bf16 models; covers dqk 128, dv 64).
+    With raw ``angles`` it also fuses the angle pre-pass, accepts bf16 (or
+    fp32) q/k/v/z/angles, returns the output in that dtype, and takes angles
+    (b, l, 1, r) shared by all heads.
     """
     if precision not in _PRECISION:
         raise ValueError(f"precision must be one of {sorted(_PRECISION)}, got {precision!r}")
@@ -186,6 +258,12 @@ def mamba3_scan(q, k, v, adt, dt, trap, q_bias, k_bias, angles=None,
     if (cos is None) != (sin is None):
         raise ValueError("pass cos and sin together, or neither")
     half = q.shape[-1] // 2
+    if precision == "bf16" and cos is None and angles is not None:
+        if q.shape[2] != 1:
+            raise ValueError(f"SISO expects one B/C group, got {q.shape[2]}")
+        out, last = _mamba3_tc_angles(q, k, v, adt, dt, trap, q_bias, k_bias, angles, D, z,
+                                      reverse)
+        return (out, last) if return_last_state else out
     if cos is None:
         if angles is None:
             raise ValueError("pass either `angles` or both `cos` and `sin`")

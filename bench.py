@@ -100,6 +100,14 @@ def m3_bytes(w):
     return 4 * b
 
 
+def m3_bytes_bf16(w):
+    """Config 2 as specified: q, k, v, y and angles (shared by the heads) in
+    bf16; dt, adt, trap and the final state in fp32."""
+    B, H, P, N, L = w["batch"], w["heads"], w["dv"], w["dqk"], w["len"]
+    return (2 * (2 * B * L * N + 2 * B * L * H * P + B * L * w["pairs"])
+            + 4 * (3 * B * H * L + B * H * P * N))
+
+
 def run_m3(args, w):
     """Time a Mamba-3 or bidirectional workload (recorded for the configs;
     the headline line is the Mamba-1 prefill scan)."""
@@ -157,10 +165,17 @@ def run_m3(args, w):
         nbytes = m3_bytes(w)
         if w["kind"] == "mimo":
             step = lambda: arm.mamba3_mimo_scan(**x)  # noqa: E731
+        elif w["kind"] == "siso" and args.m3_bf16:
+            # bf16 model inputs, angles shared by all heads; the tensor-core
+            # entry with the angle pre-pass fused in, output (b, l, h, dv) bf16
+            bf = torch.bfloat16
+            xb = dict(x, q=x["q"].to(bf), k=x["k"].to(bf), v=x["v"].to(bf),
+                      angles=x["angles"][:, :, :1, :].to(bf).contiguous())
+            nbytes = m3_bytes_bf16(w)
+            step = lambda: arm.mamba3_scan(**xb, return_last_state=True,  # noqa: E731
+                                           precision="bf16")
         elif w["kind"] == "siso":
-            prec = "bf16" if args.m3_bf16 else "fp32"
-            step = lambda: arm.mamba3_scan(**x, return_last_state=True,  # noqa: E731
-                                           precision=prec)
+            step = lambda: arm.mamba3_scan(**x, return_last_state=True)  # noqa: E731
         else:
             B, H, g = w["batch"], w["heads"], w["grid"]
             grid = lambda t: t.reshape(B, g, g, *t.shape[2:])  # noqa: E731

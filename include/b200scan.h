@@ -181,6 +181,36 @@ int arm_scan_mamba3_angles_f32_noalloc(const ArmMamba3Dims* dims, const float* a
                                        size_t n_angles, const float* dt, float* cos,
                                        float* sin, void* stream);
 
+/* Extension (no counterpart in the reference): Mamba-3 SISO on the tensor
+ * cores for bf16 models, with the RoPE angle pre-pass fused in.  Options: */
+#define ARM_SCAN_DTYPE_F32 0
+#define ARM_SCAN_DTYPE_BF16 1
+typedef struct ArmMamba3TcOptions {
+    int in_dtype;      /* q, k, v, z and angles: ARM_SCAN_DTYPE_F32 or _BF16 */
+    int out_dtype;     /* out: ARM_SCAN_DTYPE_F32 or _BF16 */
+    int out_layout;    /* 0: (batch, heads, len, dv) as arm_scan_mamba3_scan_f32;
+                          1: (batch, len, heads, dv), the Python op's layout */
+    int angles_shared; /* 1: angles (batch, len, n_angles), one row for all heads;
+                          0: angles (batch, len, heads, n_angles) */
+    size_t n_angles;   /* rotated pairs per step, <= dqk / 2; pairs beyond it are unrotated */
+} ArmMamba3TcOptions;
+
+/* Same recurrence and arguments as arm_scan_mamba3_scan_f32_async with
+ * rank 1, except: raw angles replace cos/sin (theta = forward cumsum over
+ * time of tanh(angle) * pi * dt, computed on the device, as
+ * arm_scan_mamba3_angles_f32_async does), the dtypes and output layout come
+ * from opts, and MIMO projections do not exist.  adt, dt, trap, q_bias,
+ * k_bias, d_skip, last_state, last_bx stay fp32; the state is fp32; matrix
+ * operands are rounded to bf16 (the tensor backend).  Device pointers only,
+ * 16-byte aligned; dqk must be 128 and dv 64 (else code 3).  Stream-ordered;
+ * an expired internal wait is reported by arm_scan_tensor_status. */
+int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOptions* opts,
+                                  const void* q, const void* k, const void* v, const float* adt,
+                                  const float* dt, const float* trap, const float* q_bias,
+                                  const float* k_bias, const void* angles, const float* d_skip,
+                                  const void* z, int reverse, void* out, float* last_state,
+                                  float* last_bx, void* stream);
+
 /* Extension (no counterpart in the reference): status of the tensor-core
  * kernels (backend 3).  Their waits on their own MMA completions are
  * bounded; an expired wait abandons the remaining tiles and sets a device

@@ -21,7 +21,7 @@ def declared_functions():
     return sorted(set(re.findall(r"\b(arm_scan_[a-z0-9_]+)\s*\(", text)))
 
 
-def test_library_loads_with_abi_v8():
+def test_library_loads_with_abi_v9():
     lib = _ffi.load()
     assert lib.arm_scan_abi_version() == 9
     assert _ffi.lib_path().name == "libb200scan.so"
@@ -103,6 +103,35 @@ def test_mamba3_argument_rules():
     assert _m3(_ffi.ArmMamba3Dims(1, 1, 4, 4, 1, 2), mimo=3, last_state=True,
                last_bx=True) == 2                          # MIMO has no last_bx
     assert _m3(_ffi.ArmMamba3Dims(0, 1, 4, 4, 1, 1)) == 2  # zero dim
+
+
+def _tc(dims, opts, angles=True, null_q=False, last_state=False, last_bx=False):
+    """arm_scan_mamba3_siso_tc_async with dummy non-null pointers: every
+    case here is rejected by the host checks before any device work."""
+    lib = _ffi.load()
+    p = ctypes.c_void_p(16)
+    ptrs = [None if null_q else p] + [p] * 7 + [p if angles else None, None, None]
+    return lib.arm_scan_mamba3_siso_tc_async(
+        ctypes.byref(dims), opts if opts is None else ctypes.byref(opts), *ptrs, 0, p,
+        p if last_state else None, p if last_bx else None, None)
+
+
+def test_tensor_entry_argument_rules():
+    good = _ffi.ArmMamba3Dims(1, 1, 64, 128, 1, 1)
+    o = lambda i=0, out=0, lay=1, sh=1, n=64: _ffi.ArmMamba3TcOptions(i, out, lay, sh, n)  # noqa: E731
+    assert _tc(good, None) == 1                                     # null opts
+    assert _tc(good, o(), null_q=True) == 1                         # null q
+    assert _tc(good, o(), angles=False) == 1                        # angles needed for n_angles > 0
+    assert _tc(good, o(), last_state=True) == 1                     # half a carry
+    assert _tc(good, o(i=2)) == 4                                   # bad dtype
+    assert _tc(good, o(out=-1)) == 4
+    assert _tc(good, o(lay=2)) == 4                                 # bad layout
+    assert _tc(good, o(sh=3)) == 4
+    assert _tc(good, o(n=65)) == 2                                  # more pairs than dqk/2
+    assert _tc(_ffi.ArmMamba3Dims(1, 1, 64, 128, 1, 2), o()) == 2   # rank 2 (no projections)
+    assert _tc(_ffi.ArmMamba3Dims(1, 1, 64, 64, 1, 1), o(n=32)) == 3  # dqk 64: not covered
+    assert _tc(_ffi.ArmMamba3Dims(1, 1, 32, 128, 1, 1), o()) == 3   # dv 32: not covered
+    assert b"tensor" in _ffi.load().arm_scan_last_error()
 
 
 def test_lazy_exports_are_functions_after_submodule_import():

@@ -234,3 +234,108 @@ def test_tensor_core_siso_official_goldens(name):
                             kw["Q_bias"], kw["K_bias"], angles=kw["Angles"], D=kw["D"],
                             z=kw["Z"], precision="bf16")
     assert oracle.bf16_ulps_at_scale(out.cpu().numpy(), d["out"]) <= 8.0
+
+
+def _tc_case(b, l, h, r, seed, bf16, shared):
+    """Inputs for the fused-angle tensor entry and the f64 oracle's answer on
+    exactly those (bf16-rounded where bf16) values."""
+    x = random_siso(b, l, h, 64, 128, r, seed=seed)
+    if shared:
+        x["angles"] = x["angles"][:, :, :1, :].contiguous()
+    if bf16:
+        for key in ("q", "k", "v", "z", "angles"):
+            x[key] = x[key].to(torch.bfloat16)
+    xf = {key: val.float() for key, val in x.items()}
+    full = xf["angles"].expand(b, l, h, r).contiguous()
+    cos, sin = oracle.angles_to_cos_sin(full.numpy(), xf["dt"].numpy(), 64)
+    return x, xf, cos, sin
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("shared", [False, True])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_tensor_core_fused_angles_vs_oracle(bf16, shared, reverse):
+    """precision="bf16" with raw angles: angle pre-pass fused into the
+    tensor-core kernel, bf16 or fp32 q/k/v/z/angles, output in that dtype
+    and (b, l, h, dv) layout; against the f64 oracle within the bf16 bar."""
+    b, l, h, r = 2, 389, 3, 64
+    x, xf, cos, sin = _tc_case(b, l, h, r, 7 + l, bf16, shared)
+    want, wst, _ = oracle.m3_siso(xf["q"], xf["k"], xf["v"], xf["adt"], xf["dt"], xf["trap"],
+                                  xf["q_bias"], xf["k_bias"], cos, sin, D=xf["D"], z=xf["z"],
+                                  reverse=reverse, want_state=True, nthreads=8)
+    out, st = arm().mamba3_scan(**{k: v.cuda() for k, v in x.items()}, reverse=reverse,
+                                return_last_state=True, precision="bf16")
+    torch.cuda.synchronize()
+    from armhackathon_b200 import _ffi
+    _ffi.tensor_status()
+    assert out.dtype == (torch.bfloat16 if bf16 else torch.float32)
+    assert tuple(out.shape) == (b, l, h, 64) and out.is_contiguous()
+    assert rel_err(out.float().cpu().numpy(), want) <= BF16_TOL
+    assert rel_err(st.cpu().numpy(), wst) <= BF16_TOL
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1, 64), (1, 128, 2, 48), (2, 1000, 2, 8),
+                                   (3, 255, 2, 64)])
+def test_tensor_core_fused_angles_shapes_and_carry(shape):
+    """Ragged lengths, fewer rotated pairs than dqk/2, and the (last_state,
+    last_bx) carry through the C entry point with head-major output."""
+    import ctypes
+    from armhackathon_b200 import _ffi
+    b, l, h, r = shape
+    x, xf, cos, sin = _tc_case(b, l, h, r, 3 * l + r, True, False)
+    for reverse in (False, True):
+        want, wst, wbx = oracle.m3_siso(xf["q"], xf["k"], xf["v"], xf["adt"], xf["dt"],
+                                        xf["trap"], xf["q_bias"], xf["k_bias"], cos, sin,
+                                        D=xf["D"], z=xf["z"], reverse=reverse,
+                                        want_state=True, nthreads=8)
+        c = {k: v.cuda().contiguous() for k, v in x.items()}
+        out = torch.empty((b, h, l, 64), device="cuda")
+        st = torch.empty((b, h, 64, 128), device="cuda")
+        bx = torch.empty((b, h, 128), device="cuda")
+        dims = _ffi.ArmMamba3Dims(b, h, 64, 128, l, 1)
+        opts = _ffi.ArmMamba3TcOptions(_ffi.DTYPE_BF16, _ffi.DTYPE_F32, 0, 0, r)
+        _ffi.mamba3_tc_raw(dims, opts, [c["q"].data_ptr(), c["k"].data_ptr(), c["v"].data_ptr(),
+                                        c["adt"].data_ptr(), c["dt"].data_ptr(),
+                                        c["trap"].data_ptr(), c["q_bias"].data_ptr(),
+                                        c["k_bias"].data_ptr(), c["angles"].data_ptr(),
+                                        c["D"].data_ptr(), c["z"].data_ptr()],
+                           reverse, out.data_ptr(), st.data_ptr(), bx.data_ptr(),
+                           torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        _ffi.tensor_status()
+        got = out.permute(0, 2, 1, 3).cpu().numpy()
+        assert rel_err(got, want) <= BF16_TOL
+        assert rel_err(st.cpu().numpy(), wst) <= BF16_TOL
+        assert rel_err(bx.cpu().numpy(), wbx) <= 1e-4  # fp32 carry, not an MMA operand
+
+
+def test_tensor_core_fused_matches_cos_sin_entry():
+    """Same fp32 inputs through the fused-angle entry and the reference-layout
+    cos/sin entry (backend 3): both within the bf16 bar of each other."""
+    b, l, h, r = 2, 640, 4, 64
+    x = random_siso(b, l, h, 64, 128, r, seed=11)
+    c = {k: v.cuda() for k, v in x.items()}
+    a = arm().mamba3_scan(**c, precision="bf16")
+    cos, sin = arm().angles_to_cos_sin(c["angles"], c["dt"], 64)
+    c.pop("angles")
+    bb = arm().mamba3_scan(**c, cos=cos, sin=sin, precision="bf16")
+    assert rel_err(a.cpu().numpy(), bb.cpu().numpy()) <= BF16_TOL
+
+
+@pytest.mark.parametrize("split", ["0", "1"])
+def test_tensor_core_cos_sin_split_and_fused(split, monkeypatch):
+    """The reference-layout entry's two tensor-core forms (one persistent
+    launch; three launches with B200SCAN_M3_TC_SPLIT=1) against the oracle."""
+    monkeypatch.setenv("B200SCAN_M3_TC_SPLIT", split)
+    x = random_siso(2, 700, 3, 64, 128, 64, seed=5)
+    cos, sin = oracle.angles_to_cos_sin(x["angles"].numpy(), x["dt"].numpy(), 64)
+    want, wst, _ = oracle.m3_siso(x["q"], x["k"], x["v"], x["adt"], x["dt"], x["trap"],
+                                  x["q_bias"], x["k_bias"], cos, sin, D=x["D"], z=x["z"],
+                                  want_state=True, nthreads=8)
+    c = {k: v.cuda() for k, v in x.items()}
+    c.pop("angles")
+    out, st = arm().mamba3_scan(**c, cos=torch.from_numpy(cos).float().cuda(),
+                                sin=torch.from_numpy(sin).float().cuda(), return_last_state=True,
+                                precision="bf16")
+    assert rel_err(out.cpu().numpy(), want) <= BF16_TOL
+    assert rel_err(st.cpu().numpy(), wst) <= BF16_TOL
