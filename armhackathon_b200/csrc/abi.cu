@@ -359,7 +359,8 @@ std::vector<Buf> m3_bufs(const M3Counts& c, const ArmMamba3Dims* d, const float*
 int m3_run(const M3Params& m, int backend, cudaStream_t s) {
     if (backend == 3 && !m3_tc_applicable(m))
         return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE,
-                    "the tensor backend covers SISO with dqk 128, dv 64 and 16-byte aligned v/z/out");
+                    "the tensor backend covers SISO and MIMO rank 2/4 with dqk 128, dv 64 and "
+                    "16-byte aligned tensors");
     cudaError_t e = m3_scan_launch(m, backend, s);
     return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "mamba3_scan launch");
 }

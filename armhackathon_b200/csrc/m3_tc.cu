@@ -852,6 +852,141 @@ __global__ void m3_tc_angle_prefix(M3Params p, float* theta0, int n_chunks) {
     }
 }
 
+// ---- rank generalization: a tile holds 128 rows = (128 / R) steps x R ranks,
+// row i = step (i / R), rank (i % R).  R = 1 is SISO.
+
+// Gates of one tile's steps (warp 0), replicated into the R rows of each
+// step: cumulative log2 decay, trapezoid scale, gamma, state weight.
+template <int R>
+__device__ __forceinline__ void tile_gates_r(const M3Params& p, int64_t bh, int64_t s0, float* lcum,
+                                             float* scl, float* gam, float* wdec, float* decay) {
+    constexpr float kLog2eF = 1.4426950408889634f;
+    constexpr int SPL = kTcQ / R / 32;  // steps per lane
+    const int lane = threadIdx.x & 31;
+    const int64_t L = p.len, gate_base = bh * L;
+    float lv[SPL], sc[SPL], gm[SPL];
+#pragma unroll
+    for (int e = 0; e < SPL; ++e) {
+        const int64_t it = s0 + lane * SPL + e;
+        lv[e] = sc[e] = gm[e] = 0.f;
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            const int64_t g = gate_base + t;
+            const float gamma = __ldg(p.dt + g) * sigmoid_f(__ldg(p.trap + g));
+            float shifted = 0.f;
+            if (it + 1 < L) {
+                const int64_t nx = p.reverse ? g - 1 : g + 1;
+                shifted = __ldg(p.dt + nx) * (1.f - sigmoid_f(__ldg(p.trap + nx)));
+            }
+            lv[e] = __ldg(p.adt + g) * kLog2eF;
+            sc[e] = gamma + shifted;
+            gm[e] = gamma;
+        }
+    }
+#pragma unroll
+    for (int e = 1; e < SPL; ++e) lv[e] += lv[e - 1];
+    float run = lv[SPL - 1];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(0xffffffffu, run, o);
+        if (lane >= o) run += v;
+    }
+    const float before = run - lv[SPL - 1];
+    const float last = __shfl_sync(0xffffffffu, run, 31);
+#pragma unroll
+    for (int e = 0; e < SPL; ++e) {
+        const float l = before + lv[e];
+        const float w = ex2_approx(last - l) * sc[e];
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+            const int row = (lane * SPL + e) * R + rr;
+            lcum[row] = l;
+            scl[row] = sc[e];
+            gam[row] = gm[e];
+            wdec[row] = w;
+        }
+    }
+    if (decay && lane == 0) *decay = ex2_approx(last);
+}
+
+// X rows (fp32 inputs): SISO x = v; MIMO x_r = psi_r o v.
+template <int R>
+__device__ __forceinline__ void load_x_r(const M3Params& p, int64_t bi, int64_t h, int64_t s0,
+                                         float (&xv)[kXItems][8]) {
+    const int64_t L = p.len, H = p.heads;
+#pragma unroll
+    for (int q = 0; q < kXItems; ++q) {
+        int j, pc;
+        x_item(q, j, pc);
+        const int64_t it = s0 + j / R;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xv[q][e] = 0.f;
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            ldg8(p.v + ((bi * L + t) * H + h) * kTcP + pc * 8, xv[q]);
+            if (R > 1) {
+                float ps[8];
+                ldg8(p.psi + (h * R + j % R) * kTcP + pc * 8, ps);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) xv[q][e] *= ps[e];
+            }
+        }
+    }
+}
+
+// MIMO rotated q, k rows from cos/sin, split-halves RoPE: pair m rotates
+// dims (m, m + dqk/2).  One item = row j (step, rank) x low dim chunk kc
+// (dims 8kc..8kc+7) and its partner chunk kc + 8; 1024 items, 4 per thread.
+template <int R>
+__device__ __forceinline__ void stage_qk_mimo(const M3Params& p, int64_t bi, int64_t h,
+                                              int64_t s0, uint8_t* img_q, uint8_t* img_k) {
+    const int64_t L = p.len, H = p.heads;
+    constexpr int half = kTcN / 2;
+#pragma unroll
+    for (int m = 0; m < 128 * 8 / kTcThreads2; ++m) {
+        const int item = threadIdx.x + m * kTcThreads2;
+        const int j = (item >> 8) * 32 + (item & 31);   // a warp covers 32 rows of one chunk
+        const int kc = (item >> 5) & 7;
+        const int rk = j % R;
+        const int64_t it = s0 + j / R;
+        float qlo[8], qhi[8], klo[8], khi[8];
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            const int64_t qk = ((bi * L + t) * R + rk) * kTcN + kc * 8;
+            const int64_t bb = (h * R + rk) * kTcN + kc * 8;
+            const int64_t cs = ((bi * L + t) * H + h) * half + kc * 8;
+            float bq0[8], bq1[8], bk0[8], bk1[8], c[8], s[8];
+            ldg8(p.q + qk, qlo);
+            ldg8(p.q + qk + half, qhi);
+            ldg8(p.k + qk, klo);
+            ldg8(p.k + qk + half, khi);
+            ldg8(p.q_bias + bb, bq0);
+            ldg8(p.q_bias + bb + half, bq1);
+            ldg8(p.k_bias + bb, bk0);
+            ldg8(p.k_bias + bb + half, bk1);
+            ldg8(p.cos + cs, c);
+            ldg8(p.sin + cs, s);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                float a0 = qlo[e] + bq0[e], a1 = qhi[e] + bq1[e];
+                qlo[e] = a0 * c[e] - a1 * s[e];
+                qhi[e] = a0 * s[e] + a1 * c[e];
+                a0 = klo[e] + bk0[e];
+                a1 = khi[e] + bk1[e];
+                klo[e] = a0 * c[e] - a1 * s[e];
+                khi[e] = a0 * s[e] + a1 * c[e];
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qlo[e] = qhi[e] = klo[e] = khi[e] = 0.f;
+        }
+        *reinterpret_cast<uint4*>(img_q + kmaj_off(j, kc * 8, 128)) = pack8(qlo);
+        *reinterpret_cast<uint4*>(img_q + kmaj_off(j, kc * 8 + half, 128)) = pack8(qhi);
+        *reinterpret_cast<uint4*>(img_k + kmaj_off(j, kc * 8, 128)) = pack8(klo);
+        *reinterpret_cast<uint4*>(img_k + kmaj_off(j, kc * 8 + half, 128)) = pack8(khi);
+    }
+}
+
 // Rotated q, k rows of one chunk from raw angles, in two parts around the
 // gate pass's barrier.  Lane = step within the warp's quadrant
 // (j = 32 * (warp & 3) + lane); the warp pair (w, w + 4) splits the 16 dim
@@ -996,7 +1131,7 @@ __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_
     }
 }
 
-template <bool ANG, bool IN16, bool OUT16>
+template <bool ANG, bool IN16, bool OUT16, int R>
 __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainWs cw, int n_chunks,
                                                              const float* ta, const float* theta0) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -1041,13 +1176,16 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         const int64_t bh = tile % BH;
         const int ch = static_cast<int>(tile / BH);
         const int64_t bi = bh / H, h = bh % H;
-        const int64_t it0 = static_cast<int64_t>(ch) * kTcQ;
+        const int64_t it0 = static_cast<int64_t>(ch) * (kTcQ / R);  // first step of the tile
 
         float xv[kXItems][8];
-        load_x_t<IN16>(p, bi, h, it0, xv);
+        if (R > 1)
+            load_x_r<R>(p, bi, h, it0, xv);
+        else
+            load_x_t<IN16>(p, bi, h, it0, xv);
         float th[8][4];
         if (ANG) ang_part_a(p, ta, theta0, bi, h, bh, ch, n_chunks, it0, th, qtot, th0s);
-        if (warp == 0) tile_gates(p, bh, it0, lcum, scl, gam, wdec, last_decay);
+        if (warp == 0) tile_gates_r<R>(p, bh, it0, lcum, scl, gam, wdec, last_decay);
         __syncthreads();
 #pragma unroll
         for (int q = 0; q < kXItems; ++q) {
@@ -1063,9 +1201,11 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         }
         if (ANG)
             ang_part_b<IN16>(p, bi, h, bh, it0, th, qtot, th0s, smem + kFQ, smem + kFK, scl);
+        else if (R > 1)
+            stage_qk_mimo<R>(p, bi, h, it0, smem + kFQ, smem + kFK);
         else
             stage_qk<true>(p, bi, h, it0, smem + kFQ, smem + kFK);
-        if (!ANG && p.last_bx && ch == n_chunks - 1 && tid < kTcN / 2) {
+        if (!ANG && R == 1 && p.last_bx && ch == n_chunks - 1 && tid < kTcN / 2) {
             const int jl = static_cast<int>(L - 1 - it0);
             const int64_t t = p.reverse ? 0 : L - 1;
             const int64_t qk = (bi * L + t) * kTcN;
@@ -1121,8 +1261,9 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
                     float wv[8];
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
-                        const int j = j0 + c;
-                        const float m = j < r ? ex2_approx(li - lj[c]) * sj[c] : (j == r ? gi : 0.f);
+                        // steps of rows j and r: the mask couples every rank of a step
+                        const int sjr = (j0 + c) / R, sir = r / R;
+                        const float m = sjr < sir ? ex2_approx(li - lj[c]) * sj[c] : (sjr == sir ? gi : 0.f);
                         wv[c] = m * g[c8 * 8 + c];
                     }
                     *reinterpret_cast<uint4*>(smem + kFK + kmaj_off(r, j0, 128)) = pack8(wv);
@@ -1225,36 +1366,77 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
 #pragma unroll
                 for (int q = 0; q < 32; ++q) y[q] = fmaf(el, zt[q], y[q]);
             }
-            const int64_t it = it0 + r;
-            if (it < L) {
+            if (R > 1) {
+                // MIMO: out_t = sum_r phi_r o g_r o (y_(t,r) + D x_(t,r)),
+                // g_r = silu(z o zeta_r) (1 without z); the R rows of a step
+                // are R adjacent lanes of this warp
+                const int64_t it = it0 + r / R;
+                const int rk = r % R;
+                const bool live = it < L;
+                const int64_t t = live ? (p.reverse ? L - 1 - it : it) : 0;
                 const float dsk = p.d_skip ? p.d_skip[h] : 0.f;
-                const int64_t t = p.reverse ? L - 1 - it : it;
                 const int64_t voff = ((bi * L + t) * H + h) * kTcP + hc * 32;
-                const int64_t ooff = (p.out_blh ? ((bi * L + t) * H + h) : (bh * L + t)) * kTcP + hc * 32;
-                float vv[4][8], zz[4][8];
+                const int64_t poff = (h * R + rk) * kTcP + hc * 32;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    ld8_in<IN16>(p.v, voff + 8 * q, vv[q]);
-                    if (p.z) ld8_in<IN16>(p.z, voff + 8 * q, zz[q]);
-                }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float r8[8];
+                    float vv[8], ps[8], ph[8], zt[8], ze[8];
+                    if (live) {
+                        ldg8(p.v + voff + 8 * q, vv);
+                        ldg8(p.psi + poff + 8 * q, ps);
+                        ldg8(p.phi + poff + 8 * q, ph);
+                        if (p.z) {
+                            ldg8(p.z + voff + 8 * q, zt);
+                            ldg8(p.zeta + poff + 8 * q, ze);
+                        }
+                    }
+                    float o8[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
-                        r8[e] = fmaf(dsk, vv[q][e], y[8 * q + e]);
-                        if (p.z) r8[e] *= silu_f(zz[q][e]);
+                        float a = live ? fmaf(dsk, ps[e] * vv[e], y[8 * q + e]) * ph[e] : 0.f;
+                        if (live && p.z) a *= silu_f(zt[e] * ze[e]);
+#pragma unroll
+                        for (int o = 1; o < R; o <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                        o8[e] = a;
                     }
-                    if (OUT16) {
-                        *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + ooff + 8 * q) = pack8(r8);
-                    } else {
-                        float4* o4 = reinterpret_cast<float4*>(p.out + ooff + 8 * q);
-                        o4[0] = make_float4(r8[0], r8[1], r8[2], r8[3]);
-                        o4[1] = make_float4(r8[4], r8[5], r8[6], r8[7]);
+                    if (live && rk == 0) {
+                        float* o = p.out + (p.out_blh ? ((bi * L + t) * H + h) : (bh * L + t)) * kTcP +
+                                   hc * 32 + 8 * q;
+                        reinterpret_cast<float4*>(o)[0] = make_float4(o8[0], o8[1], o8[2], o8[3]);
+                        reinterpret_cast<float4*>(o)[1] = make_float4(o8[4], o8[5], o8[6], o8[7]);
+                    }
+                }
+            } else {
+                const int64_t it = it0 + r;
+                if (it < L) {
+                    const float dsk = p.d_skip ? p.d_skip[h] : 0.f;
+                    const int64_t t = p.reverse ? L - 1 - it : it;
+                    const int64_t voff = ((bi * L + t) * H + h) * kTcP + hc * 32;
+                    const int64_t ooff = (p.out_blh ? ((bi * L + t) * H + h) : (bh * L + t)) * kTcP + hc * 32;
+                    float vv[4][8], zz[4][8];
+    #pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        ld8_in<IN16>(p.v, voff + 8 * q, vv[q]);
+                        if (p.z) ld8_in<IN16>(p.z, voff + 8 * q, zz[q]);
+                    }
+    #pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float r8[8];
+    #pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            r8[e] = fmaf(dsk, vv[q][e], y[8 * q + e]);
+                            if (p.z) r8[e] *= silu_f(zz[q][e]);
+                        }
+                        if (OUT16) {
+                            *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + ooff + 8 * q) = pack8(r8);
+                        } else {
+                            float4* o4 = reinterpret_cast<float4*>(p.out + ooff + 8 * q);
+                            o4[0] = make_float4(r8[0], r8[1], r8[2], r8[3]);
+                            o4[1] = make_float4(r8[4], r8[5], r8[6], r8[7]);
+                        }
                     }
                 }
             }
-        }
+            }
         // the next tile overwrites shared memory and tensor memory
         tc_fence_before();
         __syncthreads();
@@ -1273,9 +1455,12 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
 
 bool m3_tc_applicable(const M3Params& p) {
     auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
-    return p.psi == nullptr && p.rank == 1 && p.dqk == kTcN && p.dv == kTcP && al(p.q) &&
-           al(p.k) && al(p.v) && al(p.z) && al(p.out) && al(p.q_bias) && al(p.k_bias) &&
-           al(p.cos) && al(p.sin) && p.len > 0;
+    const bool siso = p.psi == nullptr && p.rank == 1;
+    const bool mimo = p.psi != nullptr && (p.rank == 2 || p.rank == 4) && al(p.psi) && al(p.zeta) &&
+                      al(p.phi);
+    return (siso || mimo) && p.dqk == kTcN && p.dv == kTcP && al(p.q) && al(p.k) && al(p.v) &&
+           al(p.z) && al(p.out) && al(p.q_bias) && al(p.k_bias) && al(p.cos) && al(p.sin) &&
+           p.len > 0;
 }
 
 bool m3_tc_angles_applicable(const M3Params& p) {
@@ -1372,10 +1557,10 @@ cudaError_t m3_tc_launch_split(const M3Params& p, cudaStream_t stream) {
 }
 
 
-template <bool ANG, bool IN16, bool OUT16>
+template <bool ANG, bool IN16, bool OUT16, int R = 1>
 cudaError_t launch_fused_kernel(const M3Params& p, const ChainWs& cw, int n_chunks, const float* ta,
                                 const float* theta0, cudaStream_t stream) {
-    auto kern = m3_tc_fused<ANG, IN16, OUT16>;
+    auto kern = m3_tc_fused<ANG, IN16, OUT16, R>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kFSmem));
     if (e == cudaSuccess)
@@ -1392,7 +1577,8 @@ cudaError_t launch_fused_kernel(const M3Params& p, const ChainWs& cw, int n_chun
 
 cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
     const int64_t bh = p.batch * p.heads;
-    const int n_chunks = static_cast<int>((p.len + kTcQ - 1) / kTcQ);
+    const int64_t steps = kTcQ / p.rank;  // steps per tile (128 rows = steps x rank)
+    const int n_chunks = static_cast<int>((p.len + steps - 1) / steps);
     const bool ang = p.angles != nullptr;
     cudaMemPool_t pool = nullptr;
     cudaError_t e = workspace_pool(&pool);
@@ -1426,7 +1612,11 @@ cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
         }
     }
     if (e == cudaSuccess) {
-        if (!ang)
+        if (p.rank == 4)
+            e = launch_fused_kernel<false, false, false, 4>(p, cw, n_chunks, nullptr, nullptr, stream);
+        else if (p.rank == 2)
+            e = launch_fused_kernel<false, false, false, 2>(p, cw, n_chunks, nullptr, nullptr, stream);
+        else if (!ang)
             e = launch_fused_kernel<false, false, false>(p, cw, n_chunks, nullptr, nullptr, stream);
         else if (p.in_bf16 && p.out_bf16)
             e = launch_fused_kernel<true, true, true>(p, cw, n_chunks, ta, theta0, stream);
@@ -1442,7 +1632,7 @@ cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
 }
 
 cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
-    if (p.angles) return m3_tc_launch_fused(p, stream);
+    if (p.angles || p.rank > 1) return m3_tc_launch_fused(p, stream);
     const char* v = std::getenv("B200SCAN_M3_TC_SPLIT");
     return (v && v[0] == '1') ? m3_tc_launch_split(p, stream) : m3_tc_launch_fused(p, stream);
 }

@@ -297,7 +297,7 @@ def mamba3_scan_pair(q, k, v, adt, dt, trap, q_bias, k_bias, angles=None,
 
 def mamba3_mimo_scan(q, k, v, adt, dt, trap, q_bias, k_bias, psi, zeta, phi,
                      angles=None, D=None, z=None, reverse=False, cos=None, sin=None,
-                     return_last_state=False):
+                     return_last_state=False, precision="fp32"):
     """Mamba-3 MIMO (rank-r) selective scan.
 
     q, k : (b, l, r, 1, dqk) or (b, l, r, dqk);  v, z : (b, l, h, dv)
@@ -307,7 +307,12 @@ def mamba3_mimo_scan(q, k, v, adt, dt, trap, q_bias, k_bias, psi, zeta, phi,
     returns (b, l, h, dv) [, last_state (b, h, dv, dqk)]
 
     Not a SISO call at r = 1: MIMO rotates split halves (i, i + dqk/2).
+
+    precision "bf16": the tensor-core kernel (ranks 2 and 4, dqk 128, dv 64):
+    q/k/x/W operands rounded to bf16, fp32 accumulation and fp32 state.
     """
+    if precision not in _PRECISION:
+        raise ValueError(f"precision must be one of {sorted(_PRECISION)}, got {precision!r}")
     if q.dim() == 5:
         if q.shape[3] != 1:
             raise ValueError(f"MIMO expects one B/C group, got {q.shape[3]}")
@@ -353,5 +358,5 @@ def mamba3_mimo_scan(q, k, v, adt, dt, trap, q_bias, k_bias, psi, zeta, phi,
         _prep(q, dev), _prep(k, dev), _prep(v, dev), _prep(adt, dev), _prep(dt, dev),
         _prep(trap, dev), _prep(q_bias, dev), _prep(k_bias, dev), _prep(cos, dev),
         _prep(sin, dev), opt(D), opt(z), bool(reverse), _prep(psi, dev), _prep(zeta, dev),
-        _prep(phi, dev))
+        _prep(phi, dev), backend=_PRECISION[precision])
     return (out, last) if return_last_state else out

@@ -164,7 +164,8 @@ def run_m3(args, w):
         x = m3_inputs(w, dev)
         nbytes = m3_bytes(w)
         if w["kind"] == "mimo":
-            step = lambda: arm.mamba3_mimo_scan(**x)  # noqa: E731
+            prec = "bf16" if args.m3_bf16 else "fp32"
+            step = lambda: arm.mamba3_mimo_scan(**x, precision=prec)  # noqa: E731
         elif w["kind"] == "siso" and args.m3_bf16:
             # bf16 model inputs, angles shared by all heads; the tensor-core
             # entry with the angle pre-pass fused in, output (b, l, h, dv) bf16
@@ -425,7 +426,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--m3-bf16", action="store_true",
-                    help="Mamba-3 SISO workloads on the tensor-core (bf16 operand) kernel")
+                    help="Mamba-3 SISO/MIMO workloads on the tensor-core (bf16 operand) kernels")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the config-1 HF prefill tok/s measurement")
     args = ap.parse_args()

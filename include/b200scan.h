@@ -60,7 +60,8 @@ extern "C" {
  * cross-checks), 2 = neon (not available here: code 3), 3 = tensor
  * (extension, Mamba-3 entry points only: tcgen05 tensor-core kernels with
  * bf16 matrix operands, fp32 accumulation and fp32 state, for bf16 models;
- * SISO with dqk 128, dv 64 and 16-byte aligned tensors, otherwise code 3).
+ * SISO, or MIMO of rank 2 or 4, with dqk 128, dv 64 and 16-byte aligned
+ * tensors, otherwise code 3).
  * threading: 0/1/2 are accepted (auto/sequential/rayon in the reference)
  * and have no effect on a GPU. */
 

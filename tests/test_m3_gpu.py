@@ -339,3 +339,33 @@ def test_tensor_core_cos_sin_split_and_fused(split, monkeypatch):
                                 precision="bf16")
     assert rel_err(out.cpu().numpy(), want) <= BF16_TOL
     assert rel_err(st.cpu().numpy(), wst) <= BF16_TOL
+
+
+@pytest.mark.parametrize("R", [2, 4])
+@pytest.mark.parametrize("shape", [(2, 300, 3), (1, 33, 2), (1, 1, 1)])
+def test_tensor_core_mimo_vs_oracle(R, shape):
+    """MIMO on the tensor cores (backend 3): rows = (step, rank), split-halves
+    RoPE, psi/zeta/phi projections, forward and reverse, ragged lengths."""
+    b, l, h = shape
+    dv, dqk = 64, 128
+    g = torch.Generator().manual_seed(17 * R + l)
+    f = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    dt = torch.nn.functional.softplus(f(b, h, l) - 4)
+    A = -torch.exp(torch.rand(h, generator=g) * np.log(16))
+    x = dict(q=f(b, l, R, dqk) / (dqk * R) ** 0.5, k=f(b, l, R, dqk) / (dqk * R) ** 0.5,
+             v=f(b, l, h, dv), adt=A.view(1, h, 1) * dt, dt=dt, trap=f(b, h, l),
+             q_bias=0.1 * f(h, R, dqk), k_bias=0.1 * f(h, R, dqk), psi=f(h, R, dv),
+             zeta=f(h, R, dv), phi=f(h, R, dv), angles=f(b, l, h, 64), D=1 + 0.1 * f(h),
+             z=f(b, l, h, dv))
+    cos, sin = oracle.angles_to_cos_sin(x["angles"].numpy(), x["dt"].numpy(), dqk // 2)
+    for rv in (False, True):
+        want, wst = oracle.m3_mimo(x["q"], x["k"], x["v"], x["adt"], x["dt"], x["trap"],
+                                   x["q_bias"], x["k_bias"], cos, sin, x["psi"], x["zeta"],
+                                   x["phi"], D=x["D"], z=x["z"], reverse=rv, want_state=True)
+        out, st = arm().mamba3_mimo_scan(**{k: v.cuda() for k, v in x.items()}, reverse=rv,
+                                         return_last_state=True, precision="bf16")
+        torch.cuda.synchronize()
+        from armhackathon_b200 import _ffi
+        _ffi.tensor_status()
+        assert rel_err(out.cpu().numpy(), want) <= BF16_TOL
+        assert rel_err(st.cpu().numpy(), wst) <= BF16_TOL
