@@ -327,6 +327,126 @@ int m1_pick_channels_per_cta(int64_t rows) {
     return 4;
 }
 
+// ---------------------------------------------------------------------------
+// Time-split scan for few rows and long sequences (one long sequence has only
+// batch*dim rows, too few tiles for the GPU).  The sequence is cut into S
+// equal segments, scanned as S times as many rows:
+//   1. state-only tile-kernel pass of every segment from a zero state -> h_end;
+//   2. per (row, segment) sum of dt over the segment (exact segment decay
+//      exp(A * sum dt) per state);
+//   3. fold, in traversal order: h_in(s) = exp(A sum dt(prev)) h_in(prev) +
+//      h_end(prev), seeded by h0; the final h is last_state;
+//   4. full tile-kernel pass of every segment from its h_in.
+namespace {
+
+__global__ void m1_seg_dtsum_kernel(M1Params p, int64_t S, int64_t Ls, float* dtsum) {
+    // one CTA per (row, segment); dtsum[(b * S + s) * D + d]
+    const int64_t bsd = blockIdx.x;  // logical row b' * D + d
+    const int64_t bb = bsd / p.dim, d = bsd % p.dim;
+    const int64_t b = bb / S, s = bb % S;
+    const float* dl = p.delta + (b * p.dim + d) * p.len + s * Ls;
+    const float bias = p.delta_bias ? p.delta_bias[d] : 0.f;
+    float acc = 0.f;
+    for (int64_t t = threadIdx.x; t < Ls; t += blockDim.x) {
+        float v = __ldg(dl + t) + bias;
+        if (p.delta_softplus) v = softplus_fast(v);  // as the tile kernel's per-step dt
+        acc += v;
+    }
+    __shared__ float red[32];
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) dtsum[bsd] = v;
+    }
+}
+
+__global__ void m1_seg_fold_kernel(M1Params p, int64_t S, const float* hend, const float* dtsum,
+                                   float* hin) {
+    // one thread per (b, d, n); segments in traversal order
+    const int64_t N = p.state, D = p.dim;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= p.batch * D * N) return;
+    const int64_t n = i % N, d = (i / N) % D, b = i / (N * D);
+    const float a = p.A[d * N + n];
+    float h = p.h0 ? p.h0[i] : 0.f;
+    for (int64_t k = 0; k < S; ++k) {
+        const int64_t s = p.reverse ? S - 1 - k : k;
+        const int64_t row = (b * S + s) * D + d;
+        hin[row * N + n] = h;
+        h = fmaf(expf(a * dtsum[row]), h, hend[row * N + n]);
+    }
+    if (p.last_state) p.last_state[i] = h;
+}
+
+}  // namespace
+
+int m1_timesplit_segments(const M1Params& p) {
+    if (const char* v = getenv("B200SCAN_M1_TIMESPLIT")) {
+        const int s = atoi(v);
+        if (s <= 1) return 1;
+        return (p.len % s == 0 && (p.len / s) % 4 == 0) ? s : 1;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t tiles = (p.batch * p.dim + 15) / 16;
+    // The split runs every exp twice (state pass + rescan), and the tile
+    // kernel's throughput per SM is the limit, so it pays only when fewer
+    // than half of the SMs would otherwise have a tile (measured: 96 tiles,
+    // i.e. one sequence of 1536 channels, gains nothing).
+    if (p.state > 16 || 2 * tiles >= sms || p.len < 16384) return 1;
+    // about three waves of the two-CTA-per-SM persistent grid
+    for (int s = 16; s >= 2; s >>= 1)
+        if (tiles * s <= 6 * sms && p.len % s == 0 && (p.len / s) % 4 == 0 && p.len / s >= 2048)
+            return s;
+    return 1;
+}
+
+cudaError_t m1_timesplit_launch(const M1Params& p, int S, cudaStream_t stream) {
+    const int64_t Ls = p.len / S, rows = p.batch * p.dim * S;
+    const size_t st_bytes = static_cast<size_t>(rows * p.state) * sizeof(float);
+    cudaMemPool_t pool = nullptr;
+    cudaError_t e = device_workspace_pool(&pool);
+    if (e != cudaSuccess) return e;
+    void* raw = nullptr;
+    e = cudaMallocFromPoolAsync(&raw, 2 * st_bytes + static_cast<size_t>(rows) * sizeof(float), pool,
+                                stream);
+    if (e != cudaSuccess) return e;
+    float* hend = static_cast<float*>(raw);
+    float* hin = hend + rows * p.state;
+    float* dtsum = hin + rows * p.state;
+    M1Params q = p;
+    q.batch = p.batch * S;
+    q.len = Ls;
+    q.seg_count = S;
+    q.len_full = p.len;
+    q.h0 = nullptr;
+    q.out = nullptr;  // state only
+    q.last_state = hend;
+    e = m1_tile_launch(q, 1, stream);
+    if (e == cudaSuccess) {
+        m1_seg_dtsum_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(p, S, Ls, dtsum);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        const int64_t n = p.batch * p.dim * p.state;
+        m1_seg_fold_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(p, S, hend,
+                                                                                     dtsum, hin);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        q.out = p.out;
+        q.h0 = hin;
+        q.last_state = nullptr;
+        e = m1_tile_launch(q, 1, stream);
+    }
+    const cudaError_t ef = cudaFreeAsync(raw, stream);
+    return e != cudaSuccess ? e : ef;
+}
+
 cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) {
     if (backend == kBackendSequential) {
         const int64_t BD = p.batch * p.dim;
@@ -348,6 +468,10 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
     if ((variant == 5 || variant == 6 || variant == 7) && m1_rowseq_applicable(p))
         return m1_rowseq_launch(p, variant == 6 ? 2 : variant == 7 ? 1 : 4, stream);
     const bool tile_ok = p.state <= 16 && p.len <= (INT32_MAX / 4) && p.state * p.len <= INT32_MAX;
+    if (tile_ok && (variant == -1 || variant == 1)) {
+        const int S = m1_timesplit_segments(p);
+        if (S > 1) return m1_timesplit_launch(p, S, stream);
+    }
     if (tile_ok && variant != 0) return m1_tile_launch(
         p, (variant >= 1 && variant <= 4) || variant == 9 || variant == 10 ? variant : 1, stream);
     switch (m1_pick_channels_per_cta(p.batch * p.dim)) {

@@ -26,9 +26,21 @@ struct M1Params {
     int64_t batch, dim, len, state, groups;
     int delta_softplus;
     int reverse;
+    // Segmented view (time-split scans; tile kernel only): logical batch
+    // b' = b * seg_count + s is segment s (steps s*len .. s*len+len-1) of
+    // batch b of tensors whose rows are len_full long.  seg_count 0 or 1
+    // with len_full 0: the plain layout.  out == nullptr: state only.
+    int64_t seg_count = 1;
+    int64_t len_full = 0;
 };
 
 bool m1_pointers_aligned16(const M1Params& p);
+// Per-device stream-ordered memory pool for kernel workspaces; keeps what it
+// has reserved (defined in m3_tc.cu).
+cudaError_t device_workspace_pool(cudaMemPool_t* out);
+// Segments of a time-split Mamba-1 scan (1: no split) and its launcher.
+int m1_timesplit_segments(const M1Params& p);
+cudaError_t m1_timesplit_launch(const M1Params& p, int segments, cudaStream_t stream);
 int m1_pick_channels_per_cta(int64_t rows);
 cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream);
 // Pipelined row-tile kernel (m1_tile.cu); requires state <= 16.

@@ -87,6 +87,13 @@ __global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, in
 
     const int tid = threadIdx.x, c = tid % DC, s = tid / DC;
     const int L = static_cast<int>(p.len), N = static_cast<int>(p.state);
+    // element offsets of a logical row / (batch, group) under the segmented view
+    const int64_t SEG = p.seg_count > 1 ? p.seg_count : 1;
+    const int64_t LP = p.len_full > 0 ? p.len_full : p.len;
+    auto phys_row = [&](int64_t row) {
+        const int64_t bb = row / p.dim, d = row - bb * p.dim;
+        return ((bb / SEG) * p.dim + d) * LP + (bb % SEG) * L;
+    };
     const int n_groups = (N + 3) / 4;
     const int gsz = static_cast<int>(p.dim / p.groups);
     const int n_macro = (L + T - 1) / T;
@@ -95,7 +102,10 @@ __global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, in
         TileInfo ti;
         const int bg = tile / tiles_per_group, jt = tile - bg * tiles_per_group;
         ti.row0 = static_cast<int64_t>(bg) * gsz + static_cast<int64_t>(jt) * DC;
-        ti.bc0 = static_cast<int64_t>(bg) * N * L;
+        {
+            const int64_t bb = bg / p.groups, g = bg - bb * p.groups;
+            ti.bc0 = ((bb / SEG) * p.groups + g) * N * LP + (bb % SEG) * L;
+        }
         const int rem = gsz - jt * DC;
         ti.n_rows = rem < DC ? rem : DC;
         return ti;
@@ -107,7 +117,8 @@ __global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, in
             const bool act = c < ti.n_rows;
             const int64_t row = ti.row0 + (act ? c : 0);
             const int i0 = mc * T + s * K;
-            const float* srcs[2] = {p.delta + row * L, p.u + row * L};
+            const int64_t base = phys_row(row);
+            const float* srcs[2] = {p.delta + base, p.u + base};
 #pragma unroll
             for (int a = 0; a < 2; ++a) {
                 float* dst = xs + ((buf * 2 + a) * kTileThreads + tid) * XS;
@@ -137,7 +148,7 @@ __global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, in
                 const int n = idx / T, j = idx - (idx / T) * T;
                 const int it = mc * T + j;
                 const bool ok = it < L && n < N;
-                const int off = ok ? n * L + (REV ? L - 1 - it : it) : 0;
+                const int64_t off = ok ? n * LP + (REV ? L - 1 - it : it) : 0;
                 const int w = LY::row(j) + n;
                 cp_async4(db + w, Bg + off, ok);
                 cp_async4(dc + w, Cg + off, ok);
@@ -184,8 +195,8 @@ __global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, in
 
             // z for the epilogue, straight from global (consumed at the end)
             float zv[K];
-            if (p.z) {
-                const float* zr = p.z + row * L;
+            if (p.z && p.out) {
+                const float* zr = p.z + phys_row(row);
 #pragma unroll
                 for (int k = 0; k < K; ++k) {
                     const int it = i0 + k;
@@ -302,8 +313,8 @@ __global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, in
                 }
             }
 
-            if (active) {
-                float* orow = p.out + row * L;
+            if (active && p.out) {
+                float* orow = p.out + phys_row(row);
 #pragma unroll
                 for (int k = 0; k < K; ++k) {
                     const int it = i0 + k;
@@ -333,10 +344,11 @@ cudaError_t launch_tile(const M1Params& p, cudaStream_t stream) {
     const int64_t gsz = p.dim / p.groups;
     const int64_t tiles_per_group = (gsz + DC - 1) / DC;
     const int64_t n_tiles = p.batch * p.groups * tiles_per_group;
-    if (n_tiles > INT32_MAX || p.len > (INT32_MAX / 4) || p.state * p.len > INT32_MAX)
+    const int64_t pitch = p.len_full > 0 ? p.len_full : p.len;
+    if (n_tiles > INT32_MAX || p.len > (INT32_MAX / 4) || p.state * pitch > INT32_MAX)
         return cudaErrorInvalidValue;
     const size_t smem = LY::bytes();
-    const bool vec = (p.len % 4 == 0) && m1_pointers_aligned16(p);
+    const bool vec = (p.len % 4 == 0) && (pitch % 4 == 0) && m1_pointers_aligned16(p);
     void (*kern)(M1Params, int, int);
     if (vec)
         kern = p.reverse ? m1_tile_kernel<DC, K, true, true, POLY>

@@ -35,6 +35,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "m1_scan.h"
 #include "m3_scan.h"
 
 namespace b200scan {
@@ -1484,7 +1485,9 @@ constexpr int kMaxPoolDevices = 64;
 std::mutex g_pool_mu;
 cudaMemPool_t g_pool[kMaxPoolDevices] = {};
 
-cudaError_t workspace_pool(cudaMemPool_t* out) {
+}  // namespace
+
+cudaError_t device_workspace_pool(cudaMemPool_t* out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -1510,7 +1513,7 @@ cudaError_t workspace_pool(cudaMemPool_t* out) {
     *out = g_pool[dev];
     return cudaSuccess;
 }
-}  // namespace
+
 
 // Three-launch form (kernels A, B, C): selected with B200SCAN_M3_TC_SPLIT=1.
 cudaError_t m3_tc_launch_split(const M3Params& p, cudaStream_t stream) {
@@ -1529,7 +1532,7 @@ cudaError_t m3_tc_launch_split(const M3Params& p, cudaStream_t stream) {
     // stream-ordered workspace: valid under stream capture, freed after use
     void* raw = nullptr;
     cudaMemPool_t pool = nullptr;
-    e = workspace_pool(&pool);
+    e = device_workspace_pool(&pool);
     if (e != cudaSuccess) return e;
     e = cudaMallocFromPoolAsync(&raw, m3_tc_workspace_bytes(p), pool, stream);
     if (e != cudaSuccess) return e;
@@ -1581,7 +1584,7 @@ cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
     const int n_chunks = static_cast<int>((p.len + steps - 1) / steps);
     const bool ang = p.angles != nullptr;
     cudaMemPool_t pool = nullptr;
-    cudaError_t e = workspace_pool(&pool);
+    cudaError_t e = device_workspace_pool(&pool);
     if (e != cudaSuccess) return e;
     const size_t slot_bytes = static_cast<size_t>(bh) * 2 * kChunkSt;
     const size_t flag_bytes = (static_cast<size_t>(bh + 1) * sizeof(unsigned int) + 255) / 256 * 256;

@@ -216,3 +216,42 @@ def test_every_kernel_variant_vs_oracle(variant, reverse, monkeypatch):
                                      initial_state=torch.from_numpy(h0).cuda())
     assert rel_err(out.cpu().numpy(), want) <= REL_TOL
     assert rel_err(last.cpu().numpy(), want_last) <= REL_TOL
+
+
+def _slow_decay_case(B, D, L, N, seed):
+    """Inputs whose state survives across thousands of steps (tiny dt, small
+    |A|), so the time-split's carries between segments matter."""
+    x = random_case(B, D, L, N, seed=seed)
+    rng = np.random.default_rng(seed + 1)
+    x["A"] = (-rng.uniform(0.05, 1.0, (D, N))).astype(np.float32)
+    x["delta_bias"] = rng.uniform(-9, -7, D).astype(np.float32)
+    return x
+
+
+@pytest.mark.parametrize("segments", ["4", "8"])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_time_split_vs_oracle(segments, reverse, monkeypatch):
+    """Few rows, long sequence, split in time (state-only pass, segment-decay
+    fold, rescan from the carries): output, h0 resume and last_state."""
+    monkeypatch.setenv("B200SCAN_M1_TIMESPLIT", segments)
+    B, D, L, N = 2, 24, 8192, 16
+    x = _slow_decay_case(B, D, L, N, seed=int(segments))
+    h0 = np.random.default_rng(3).standard_normal((B, D, N)).astype(np.float32)
+    want, want_last = oracle.m1_scan(**x, reverse=reverse, h0=h0, nthreads=8)
+    out, last = arm().selective_scan(**cuda(x), reverse=reverse, return_last_state=True,
+                                     initial_state=torch.from_numpy(h0).cuda())
+    assert rel_err(out.cpu().numpy(), want) <= REL_TOL
+    assert rel_err(last.cpu().numpy(), want_last) <= REL_TOL
+
+
+def test_time_split_chosen_automatically_and_bidirectional():
+    """A one-sequence, few-channel, long problem takes the time split by
+    itself; the fused bidirectional entry goes through it in both directions."""
+    B, D, L, N = 1, 64, 32768, 16
+    x = _slow_decay_case(B, D, L, N, seed=21)
+    fwd, _ = oracle.m1_scan(**x, nthreads=8)
+    bwd, _ = oracle.m1_scan(**x, reverse=True, nthreads=8)
+    out = arm().selective_scan(**cuda(x))
+    assert rel_err(out.cpu().numpy(), fwd) <= REL_TOL
+    both = arm().bidirectional_scan(**cuda(x), merge="sum")
+    assert rel_err(both.cpu().numpy(), fwd + bwd) <= REL_TOL
