@@ -1132,6 +1132,56 @@ __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_
     }
 }
 
+// Requests every row tile `tile` will read into L2 (one 16-byte-aligned bulk
+// prefetch per row), so that its loads, issued a tile later, hit L2.
+template <bool ANG, bool IN16, int R>
+__device__ __forceinline__ void prefetch_tile(const M3Params& p, const float* ta,
+                                              const float* theta0, int64_t tile, int n_chunks) {
+    const int64_t BH = p.batch * p.heads, H = p.heads, L = p.len;
+    const int64_t bh = tile % BH, bi = bh / H, h = bh % H;
+    const int ch = static_cast<int>(tile / BH);
+    constexpr int TS = kTcQ / R;
+    const int64_t s0 = static_cast<int64_t>(ch) * TS;
+    const int tid = threadIdx.x;
+    const uint32_t es = IN16 ? 2 : 4;  // bytes per element of q, k, v, z
+    if (tid < TS) {
+        const int64_t it = s0 + tid;
+        if (it >= L) return;
+        const int64_t t = p.reverse ? L - 1 - it : it;
+        const int64_t row = (bi * L + t) * H + h;
+        const uint8_t* q = static_cast<const uint8_t*>(static_cast<const void*>(p.q));
+        const uint8_t* k = static_cast<const uint8_t*>(static_cast<const void*>(p.k));
+        const uint8_t* v = static_cast<const uint8_t*>(static_cast<const void*>(p.v));
+        if (h == 0) {  // q, k rows are shared by all heads
+            prefetch_l2(q + (bi * L + t) * R * kTcN * es, R * kTcN * es);
+            prefetch_l2(k + (bi * L + t) * R * kTcN * es, R * kTcN * es);
+        }
+        prefetch_l2(v + row * kTcP * es, kTcP * es);
+        if (p.z) prefetch_l2(static_cast<const uint8_t*>(static_cast<const void*>(p.z)) + row * kTcP * es,
+                             kTcP * es);
+        if (ANG) {
+            const int64_t arow = p.angles_shared ? (bi * L + t) : row;
+            if ((p.n_angles & 3) == 0 && p.n_angles > 0 && (!p.angles_shared || h == 0))
+                prefetch_l2(ta + arow * p.n_angles, static_cast<uint32_t>(p.n_angles * 4));
+        } else {
+            prefetch_l2(p.cos + row * (kTcN / 2), kTcN * 2);
+            prefetch_l2(p.sin + row * (kTcN / 2), kTcN * 2);
+        }
+    } else if (tid < TS + 3) {
+        // gate rows: TS steps (+1 for the trapezoid's next step), 16-byte aligned span
+        const float* g = tid == TS ? p.dt : tid == TS + 1 ? p.trap : p.adt;
+        if (reinterpret_cast<uintptr_t>(g) & 15u) return;  // bulk prefetch needs 16-byte alignment
+        int64_t lo = p.reverse ? L - (s0 + TS) - 1 : s0;
+        int64_t hi = p.reverse ? L - s0 : s0 + TS + 1;
+        lo = lo < 0 ? 0 : lo;
+        hi = hi > L ? L : hi;
+        const int64_t a = (bh * L + lo) & ~int64_t(3), b = ((bh * L + hi) + 3) & ~int64_t(3);
+        if (b > a) prefetch_l2(g + a, static_cast<uint32_t>((b - a) * 4));
+    } else if (ANG && tid == TS + 3 && p.n_angles > 0) {
+        prefetch_l2(theta0 + (bh * n_chunks + ch) * 64, 256);
+    }
+}
+
 template <bool ANG, bool IN16, bool OUT16, int R>
 __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainWs cw, int n_chunks,
                                                              const float* ta, const float* theta0) {
@@ -1142,7 +1192,8 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
     float* wdec = gam + kTcQ;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kFMisc);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kFMisc + 16);
-    int* tile_slot = reinterpret_cast<int*>(smem + kFMisc + 24);
+    int* tile_slot = reinterpret_cast<int*>(smem + kFMisc + 24);  // the next tile
+
     float* last_decay = reinterpret_cast<float*>(smem + kFMisc + 28);
     float* qtot = reinterpret_cast<float*>(smem + kFQtot);  // angles mode: quadrant totals
     float* th0s = qtot + 4 * 64;                            // angles mode: chunk's theta0
@@ -1169,11 +1220,17 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
     uint32_t phase = 0;
     bool ok = true;
 
-    while (ok) {
+    // Thread 0 takes the next tile when the current one starts; the CTA
+    // prefetches it into L2 during the current one.  Tiles still come from
+    // the counter in order: the lowest tile any CTA is working on always has
+    // a finished predecessor, so the chain cannot stall.
+    if (tid == 0) *tile_slot = static_cast<int>(atomicAdd(cw.counter, 1u));
+    __syncthreads();
+    int64_t tile = *tile_slot;
+    if (tile < n_tiles) prefetch_tile<ANG, IN16, R>(p, ta, theta0, tile, n_chunks);
+    while (ok && tile < n_tiles) {
+        __syncthreads();  // every thread has read the slot
         if (tid == 0) *tile_slot = static_cast<int>(atomicAdd(cw.counter, 1u));
-        __syncthreads();
-        const int64_t tile = *tile_slot;
-        if (tile >= n_tiles) break;
         const int64_t bh = tile % BH;
         const int ch = static_cast<int>(tile / BH);
         const int64_t bi = bh / H, h = bh % H;
@@ -1188,6 +1245,8 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         if (ANG) ang_part_a(p, ta, theta0, bi, h, bh, ch, n_chunks, it0, th, qtot, th0s);
         if (warp == 0) tile_gates_r<R>(p, bh, it0, lcum, scl, gam, wdec, last_decay);
         __syncthreads();
+        const int64_t next_tile = *tile_slot;
+        if (next_tile < n_tiles) prefetch_tile<ANG, IN16, R>(p, ta, theta0, next_tile, n_chunks);
 #pragma unroll
         for (int q = 0; q < kXItems; ++q) {
             int j, pc;
@@ -1318,7 +1377,6 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
                 for (int q = 0; q < 8; ++q)
                     __stcg(reinterpret_cast<float4*>(slot_out) + q,
                            make_float4(so[4 * q], so[4 * q + 1], so[4 * q + 2], so[4 * q + 3]));
-                __threadfence();
             } else if (p.last_state) {
                 // final state, (p, n) layout
 #pragma unroll
@@ -1442,6 +1500,7 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
+        tile = next_tile;
     }
     if (!ok) mbar_wait(bar, phase ^ 1);  // MMAs still in flight: bounded second wait
     tc_fence_before();
