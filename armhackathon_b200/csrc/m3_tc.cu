@@ -292,11 +292,10 @@ __device__ __forceinline__ void load_x(const M3Params& p, int64_t bi, int64_t h,
 // chunk and are both loaded before either is stored.
 template <bool WITH_Q>
 __device__ __forceinline__ void stage_qk(const M3Params& p, int64_t bi, int64_t h, int64_t it0,
-                                         uint8_t* img_q, uint8_t* img_k) {
+                                         uint8_t* img_q, uint8_t* img_k, const float* qb,
+                                         const float* kb) {
     const int64_t L = p.len, H = p.heads;
     const int tid = threadIdx.x;
-    const float* qb = p.q_bias + h * kTcN;
-    const float* kb = p.k_bias + h * kTcN;
     for (int m = 0; m < 128 * 16 / kTcThreads2 / 2; ++m) {
         float qa[2][8], ka[2][8], cc[2][4], ss[2][4];
         int jj[2];
@@ -321,8 +320,8 @@ __device__ __forceinline__ void stage_qk(const M3Params& p, int64_t bi, int64_t 
             ss[u][0] = s4.x; ss[u][1] = s4.y; ss[u][2] = s4.z; ss[u][3] = s4.w;
         }
         float qbb[8], kbb[8];
-        if (WITH_Q) ldg8(qb + kc * 8, qbb);
-        ldg8(kb + kc * 8, kbb);
+        if (WITH_Q) ld8(qb + kc * 8, qbb);
+        ld8(kb + kc * 8, kbb);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             float qr[8], kr[8];
@@ -394,7 +393,7 @@ __global__ void __launch_bounds__(kTcThreads2, 3) m3_tc_dstate(M3Params p, TcWs 
         for (int e = 0; e < 8; ++e) xw[e] = w * xv[r][e];
         *reinterpret_cast<uint4*>(smem + kAXw + mnmaj_off(pc * 8, j, kTcP)) = pack8(xw);
     }
-    stage_qk<false>(p, bi, h, it0, nullptr, smem + kAK);
+    stage_qk<false>(p, bi, h, it0, nullptr, smem + kAK, p.q_bias + h * kTcN, p.k_bias + h * kTcN);
     if (p.last_bx && ch == n_chunks - 1 && tid < kTcN / 2) {
         // scale_T * k_T: rotated k of the final step, fp32
         const int jl = static_cast<int>(L - 1 - it0);
@@ -557,7 +556,7 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_out(M3Params p, TcWs ws,
             for (int r = 0; r < static_cast<int>(kStImg / 16 / kTcThreads2); ++r)
                 dst[tid + r * kTcThreads2] = sv[r];
         }
-        stage_qk<true>(p, bi, h, it0, smem + kCQ, smem + kCK);
+        stage_qk<true>(p, bi, h, it0, smem + kCQ, smem + kCK, p.q_bias + h * kTcN, p.k_bias + h * kTcN);
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
@@ -708,7 +707,8 @@ constexpr uint32_t kFXw = kFX + 128 * 64 * 2;      // w o X MN-major (B of dS^T)
 constexpr uint32_t kFS = kFXw;
 constexpr uint32_t kFGate = kFXw + 128 * 64 * 2;   // lcum, scale, gamma, w
 constexpr uint32_t kFQtot = kFGate + 4 * 128 * 4;  // angles mode: [4 quadrants][64 pairs], theta0[64]
-constexpr uint32_t kFMisc = kFQtot + 5 * 64 * 4;
+constexpr uint32_t kFBias = kFQtot + 5 * 64 * 4;   // this head's q, k biases: [2][rank <= 4][dqk]
+constexpr uint32_t kFMisc = kFBias + 2 * 4 * 128 * 4;
 constexpr uint32_t kFSmem = kFMisc + 64;
 
 struct ChainWs {
@@ -940,7 +940,8 @@ __device__ __forceinline__ void load_x_r(const M3Params& p, int64_t bi, int64_t 
 // (dims 8kc..8kc+7) and its partner chunk kc + 8; 1024 items, 4 per thread.
 template <int R>
 __device__ __forceinline__ void stage_qk_mimo(const M3Params& p, int64_t bi, int64_t h,
-                                              int64_t s0, uint8_t* img_q, uint8_t* img_k) {
+                                              int64_t s0, uint8_t* img_q, uint8_t* img_k,
+                                              const float* qbs, const float* kbs) {
     const int64_t L = p.len, H = p.heads;
     constexpr int half = kTcN / 2;
 #pragma unroll
@@ -954,17 +955,17 @@ __device__ __forceinline__ void stage_qk_mimo(const M3Params& p, int64_t bi, int
         if (it < L) {
             const int64_t t = p.reverse ? L - 1 - it : it;
             const int64_t qk = ((bi * L + t) * R + rk) * kTcN + kc * 8;
-            const int64_t bb = (h * R + rk) * kTcN + kc * 8;
+            const int bb = rk * kTcN + kc * 8;  // this head's bias block [R][dqk]
             const int64_t cs = ((bi * L + t) * H + h) * half + kc * 8;
             float bq0[8], bq1[8], bk0[8], bk1[8], c[8], s[8];
             ldg8(p.q + qk, qlo);
             ldg8(p.q + qk + half, qhi);
             ldg8(p.k + qk, klo);
             ldg8(p.k + qk + half, khi);
-            ldg8(p.q_bias + bb, bq0);
-            ldg8(p.q_bias + bb + half, bq1);
-            ldg8(p.k_bias + bb, bk0);
-            ldg8(p.k_bias + bb + half, bk1);
+            ld8(qbs + bb, bq0);
+            ld8(qbs + bb + half, bq1);
+            ld8(kbs + bb, bk0);
+            ld8(kbs + bb + half, bk1);
             ldg8(p.cos + cs, c);
             ldg8(p.sin + cs, s);
 #pragma unroll
@@ -1058,7 +1059,7 @@ template <bool IN16>
 __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_t h, int64_t bh,
                                            int64_t it0, float (&th)[8][4], const float* qtot,
                                            const float* th0s, uint8_t* img_q, uint8_t* img_k,
-                                           const float* scl) {
+                                           const float* scl, const float* qb, const float* kb) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int qd = warp & 3, sub = warp >> 2;
     const int64_t L = p.len, NA = p.n_angles;
@@ -1079,8 +1080,6 @@ __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_
                 if (rev ? q > qd : q < qd) off += qtot[q * 64 + pr];
             th[i][e] += off;
         }
-    const float* qb = p.q_bias + h * kTcN;
-    const float* kb = p.k_bias + h * kTcN;
     const bool want_bx = p.last_bx && live && it == L - 1;
     const int64_t qrow = (bi * L + t) * kTcN;
 #pragma unroll
@@ -1102,8 +1101,8 @@ __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_
             const int i = 2 * m + u;
             const int kc = 2 * i + sub;
             float qbb[8], kbb[8], qr[8], kr[8];
-            ldg8(qb + kc * 8, qbb);
-            ldg8(kb + kc * 8, kbb);
+            ld8(qb + kc * 8, qbb);
+            ld8(kb + kc * 8, kbb);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 float sn = 0.f, cs = 1.f;
@@ -1197,6 +1196,8 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
     float* last_decay = reinterpret_cast<float*>(smem + kFMisc + 28);
     float* qtot = reinterpret_cast<float*>(smem + kFQtot);  // angles mode: quadrant totals
     float* th0s = qtot + 4 * 64;                            // angles mode: chunk's theta0
+    float* qbs = reinterpret_cast<float*>(smem + kFBias);   // [R][dqk]
+    float* kbs = qbs + R * kTcN;
     const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
     constexpr int kSt = kTcN * kTcP;
 
@@ -1243,6 +1244,10 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
             load_x_t<IN16>(p, bi, h, it0, xv);
         float th[8][4];
         if (ANG) ang_part_a(p, ta, theta0, bi, h, bh, ch, n_chunks, it0, th, qtot, th0s);
+        for (int i = tid; i < R * kTcN; i += kTcThreads2) {
+            qbs[i] = __ldg(p.q_bias + h * R * kTcN + i);
+            kbs[i] = __ldg(p.k_bias + h * R * kTcN + i);
+        }
         if (warp == 0) tile_gates_r<R>(p, bh, it0, lcum, scl, gam, wdec, last_decay);
         __syncthreads();
         const int64_t next_tile = *tile_slot;
@@ -1260,11 +1265,12 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
             *reinterpret_cast<uint4*>(smem + kFXw + o) = pack8(xw);
         }
         if (ANG)
-            ang_part_b<IN16>(p, bi, h, bh, it0, th, qtot, th0s, smem + kFQ, smem + kFK, scl);
+            ang_part_b<IN16>(p, bi, h, bh, it0, th, qtot, th0s, smem + kFQ, smem + kFK, scl, qbs,
+                             kbs);
         else if (R > 1)
-            stage_qk_mimo<R>(p, bi, h, it0, smem + kFQ, smem + kFK);
+            stage_qk_mimo<R>(p, bi, h, it0, smem + kFQ, smem + kFK, qbs, kbs);
         else
-            stage_qk<true>(p, bi, h, it0, smem + kFQ, smem + kFK);
+            stage_qk<true>(p, bi, h, it0, smem + kFQ, smem + kFK, qbs, kbs);
         if (!ANG && R == 1 && p.last_bx && ch == n_chunks - 1 && tid < kTcN / 2) {
             const int jl = static_cast<int>(L - 1 - it0);
             const int64_t t = p.reverse ? 0 : L - 1;
