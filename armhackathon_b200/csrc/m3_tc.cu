@@ -753,6 +753,18 @@ __device__ __forceinline__ void ld8_in(const void* base, int64_t idx, float (&f)
     }
 }
 
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        f[2 * e] = bf16_to_f(w[e] & 0xFFFFu);
+        f[2 * e + 1] = bf16_to_f(w[e] >> 16);
+    }
+}
+__device__ __forceinline__ uint4 ld8_raw16(const void* base, int64_t idx) {
+    return __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + idx));
+}
+
 template <bool IN16>
 __device__ __forceinline__ float ld1_in(const void* base, int64_t idx) {
     if (IN16) return bf16_to_f(__ldg(static_cast<const uint16_t*>(base) + idx));
@@ -1082,23 +1094,34 @@ __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_
         }
     const bool want_bx = p.last_bx && live && it == L - 1;
     const int64_t qrow = (bi * L + t) * kTcN;
+    // two rounds of four items: every q, k load of a round is in flight
+    // before any of them is used (bf16 rows stay packed until then)
+    constexpr int kPer = 4;
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        float qa[2][8], ka[2][8];
+    for (int m = 0; m < 8 / kPer; ++m) {
+        uint4 qraw[kPer], kraw[kPer];
+        float qa[kPer][8], ka[kPer][8];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int kc = 2 * (2 * m + u) + sub;
-            if (live) {
-                ld8_in<IN16>(p.q, qrow + kc * 8, qa[u]);
-                ld8_in<IN16>(p.k, qrow + kc * 8, ka[u]);
+        for (int u = 0; u < kPer; ++u) {
+            const int kc = 2 * (kPer * m + u) + sub;
+            if (IN16) {
+                qraw[u] = live ? ld8_raw16(p.q, qrow + kc * 8) : make_uint4(0u, 0u, 0u, 0u);
+                kraw[u] = live ? ld8_raw16(p.k, qrow + kc * 8) : make_uint4(0u, 0u, 0u, 0u);
+            } else if (live) {
+                ld8_in<false>(p.q, qrow + kc * 8, qa[u]);
+                ld8_in<false>(p.k, qrow + kc * 8, ka[u]);
             } else {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) qa[u][e] = ka[u][e] = 0.f;
             }
         }
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int i = 2 * m + u;
+        for (int u = 0; u < kPer; ++u) {
+            if (IN16) {
+                unpack8(qraw[u], qa[u]);
+                unpack8(kraw[u], ka[u]);
+            }
+            const int i = kPer * m + u;
             const int kc = 2 * i + sub;
             float qbb[8], kbb[8], qr[8], kr[8];
             ld8(qb + kc * 8, qbb);
@@ -1229,8 +1252,10 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
     __syncthreads();
     int64_t tile = *tile_slot;
     if (tile < n_tiles) prefetch_tile<ANG, IN16, R>(p, ta, theta0, tile, n_chunks);
+    __syncthreads();  // every thread has read the first tile
     while (ok && tile < n_tiles) {
-        __syncthreads();  // every thread has read the slot
+        // every thread read the slot (the next tile) before the previous
+        // tile's closing barrier, so thread 0 may refill it now
         if (tid == 0) *tile_slot = static_cast<int>(atomicAdd(cw.counter, 1u));
         const int64_t bh = tile % BH;
         const int ch = static_cast<int>(tile / BH);
@@ -1238,10 +1263,24 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         const int64_t it0 = static_cast<int64_t>(ch) * (kTcQ / R);  // first step of the tile
 
         float xv[kXItems][8];
-        if (R > 1)
+        uint4 xraw[kXItems];  // bf16 inputs: v stays packed until after the gate barrier
+        if (R > 1) {
             load_x_r<R>(p, bi, h, it0, xv);
-        else
-            load_x_t<IN16>(p, bi, h, it0, xv);
+        } else if (IN16) {
+#pragma unroll
+            for (int q = 0; q < kXItems; ++q) {
+                int j, pc;
+                x_item(q, j, pc);
+                const int64_t itx = it0 + j;
+                xraw[q] = make_uint4(0u, 0u, 0u, 0u);
+                if (itx < L) {
+                    const int64_t t = p.reverse ? L - 1 - itx : itx;
+                    xraw[q] = ld8_raw16(p.v, ((bi * L + t) * H + h) * kTcP + pc * 8);
+                }
+            }
+        } else {
+            load_x_t<false>(p, bi, h, it0, xv);
+        }
         float th[8][4];
         if (ANG) ang_part_a(p, ta, theta0, bi, h, bh, ch, n_chunks, it0, th, qtot, th0s);
         for (int i = tid; i < R * kTcN; i += kTcThreads2) {
@@ -1250,6 +1289,10 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         }
         if (warp == 0) tile_gates_r<R>(p, bh, it0, lcum, scl, gam, wdec, last_decay);
         __syncthreads();
+        if (IN16 && R == 1) {
+#pragma unroll
+            for (int q = 0; q < kXItems; ++q) unpack8(xraw[q], xv[q]);
+        }
         const int64_t next_tile = *tile_slot;
         if (next_tile < n_tiles) prefetch_tile<ANG, IN16, R>(p, ta, theta0, next_tile, n_chunks);
 #pragma unroll
@@ -1417,6 +1460,19 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
             }
             umma_commit(bar);
         }
+        // bf16 SISO: this row's v and z for the epilogue, requested before
+        // waiting for the last MMAs
+        uint4 vraw[4], zraw[4];
+        if (IN16 && R == 1) {
+            const int64_t ite = it0 + r;
+            const int64_t te = ite < L ? (p.reverse ? L - 1 - ite : ite) : 0;
+            const int64_t voff = ((bi * L + te) * H + h) * kTcP + hc * 32;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                vraw[q] = ite < L ? ld8_raw16(p.v, voff + 8 * q) : make_uint4(0u, 0u, 0u, 0u);
+                zraw[q] = (ite < L && p.z) ? ld8_raw16(p.z, voff + 8 * q) : make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
         ok = cta_wait(bar, phase);
         phase ^= 1;
         if (!ok) break;
@@ -1480,8 +1536,13 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
                     float vv[4][8], zz[4][8];
     #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        ld8_in<IN16>(p.v, voff + 8 * q, vv[q]);
-                        if (p.z) ld8_in<IN16>(p.z, voff + 8 * q, zz[q]);
+                        if (IN16) {
+                            unpack8(vraw[q], vv[q]);
+                            unpack8(zraw[q], zz[q]);
+                        } else {
+                            ld8_in<IN16>(p.v, voff + 8 * q, vv[q]);
+                            if (p.z) ld8_in<IN16>(p.z, voff + 8 * q, zz[q]);
+                        }
                     }
     #pragma unroll
                     for (int q = 0; q < 4; ++q) {
