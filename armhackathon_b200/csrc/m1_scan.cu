@@ -473,7 +473,7 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
         if (S > 1) return m1_timesplit_launch(p, S, stream);
     }
     if (tile_ok && variant != 0) return m1_tile_launch(
-        p, (variant >= 1 && variant <= 4) || variant == 9 || variant == 10 ? variant : 1, stream);
+        p, (variant >= 1 && variant <= 4) || (variant >= 9 && variant <= 11) ? variant : 1, stream);
     switch (m1_pick_channels_per_cta(p.batch * p.dim)) {
         case 32: return launch_chunked<32, 16>(p, stream);
         case 16: return launch_chunked<16, 16>(p, stream);

@@ -68,9 +68,9 @@ struct TileInfo {
     int n_rows;     // rows of the tile that exist (<= DC)
 };
 
-template <int DC, int K, bool VEC, bool REV, int POLY>
-__global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, int tiles_per_group,
-                                                                  int n_tiles) {
+template <int DC, int K, bool VEC, bool REV, int POLY, int MINB = 2>
+__global__ void __launch_bounds__(kTileThreads, MINB) m1_tile_kernel(M1Params p, int tiles_per_group,
+                                                                     int n_tiles) {
     using LY = TileLayout<DC, K>;
     constexpr int S = LY::S, T = LY::T, XS = LY::XS;
     constexpr int AGG_STRIDE = 4 * DC + 4;  // floats per segment in aggP/aggH
@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(kTileThreads, 2) m1_tile_kernel(M1Params p, in
     cp_async_wait_all();
 }
 
-template <int DC, int K, int POLY = 0>
+template <int DC, int K, int POLY = 0, int MINB = 2>
 cudaError_t launch_tile(const M1Params& p, cudaStream_t stream) {
     using LY = TileLayout<DC, K>;
     const int64_t gsz = p.dim / p.groups;
@@ -351,11 +351,11 @@ cudaError_t launch_tile(const M1Params& p, cudaStream_t stream) {
     const bool vec = (p.len % 4 == 0) && (pitch % 4 == 0) && m1_pointers_aligned16(p);
     void (*kern)(M1Params, int, int);
     if (vec)
-        kern = p.reverse ? m1_tile_kernel<DC, K, true, true, POLY>
-                         : m1_tile_kernel<DC, K, true, false, POLY>;
+        kern = p.reverse ? m1_tile_kernel<DC, K, true, true, POLY, MINB>
+                         : m1_tile_kernel<DC, K, true, false, POLY, MINB>;
     else
-        kern = p.reverse ? m1_tile_kernel<DC, K, false, true, POLY>
-                         : m1_tile_kernel<DC, K, false, false, POLY>;
+        kern = p.reverse ? m1_tile_kernel<DC, K, false, true, POLY, MINB>
+                         : m1_tile_kernel<DC, K, false, false, POLY, MINB>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
@@ -381,6 +381,7 @@ cudaError_t m1_tile_launch(const M1Params& p, int variant, cudaStream_t stream) 
         case 4: return launch_tile<16, 4>(p, stream);
         case 9: return launch_tile<16, 8, 1>(p, stream);
         case 10: return launch_tile<16, 8, 2>(p, stream);
+        case 11: return launch_tile<16, 4, 0, 3>(p, stream);  // three CTAs per SM
         default: return launch_tile<16, 8>(p, stream);
     }
 }
