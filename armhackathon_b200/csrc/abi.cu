@@ -373,6 +373,115 @@ uint32_t arm_scan_abi_version(void) { return ARM_SCAN_ABI_VERSION; }
 
 const char* arm_scan_last_error(void) { return g_last_error.c_str(); }
 
+// Host buffers with batch >= 2: a per-batch pipeline over two streams, so
+// that batch b+1's upload overlaps batch b's scan and download (separate
+// copy engines; rows of different batches never interact).  Buffers in the
+// order of the synchronous entry: u, delta, A, B, C, D, z, delta_bias, h0,
+// out, last_state; A, D, delta_bias are shared by the batches.
+struct Pipe {
+    std::mutex mu;
+    void* base = nullptr;
+    size_t cap = 0;
+    cudaStream_t s[2] = {nullptr, nullptr};
+    cudaEvent_t shared_ready = nullptr;
+};
+Pipe g_pipe[64];
+
+bool m1_pipeline_worthwhile(const ArmScanDims* d, const std::vector<Buf>& bufs) {
+    size_t total = 0;
+    for (const Buf& b : bufs) total += b.ptr ? b.bytes : 0;
+    return d->batch >= 2 && total >= (size_t(16) << 20);
+}
+
+int m1_host_pipelined(const ArmScanDims* d, const std::vector<Buf>& bufs, int softplus, int reverse,
+                      int backend) {
+    constexpr int kSliced[] = {0, 1, 3, 4, 6, 8, 9, 10};
+    constexpr int kShared[] = {2, 5, 7};
+    const size_t nb = d->batch;
+    int cur = 0;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur < 0 || cur >= 64) return fail(ARM_SCAN_ERR_CUDA, "device ordinal %d unsupported", cur);
+    Pipe& pp = g_pipe[cur];
+    std::lock_guard<std::mutex> lock(pp.mu);
+    size_t off[11] = {}, slot_bytes = 0, shared_bytes = 0;
+    for (int i : kShared) {
+        off[i] = shared_bytes;
+        shared_bytes += bufs[i].ptr ? round_up(bufs[i].bytes) : 0;
+    }
+    for (int i : kSliced) {
+        off[i] = slot_bytes;
+        slot_bytes += bufs[i].ptr ? round_up(bufs[i].bytes / nb) : 0;
+    }
+    const size_t need = shared_bytes + 2 * slot_bytes;
+    if (need > pp.cap) {
+        if (pp.base) {
+            cudaDeviceSynchronize();
+            cudaFree(pp.base);
+        }
+        pp.base = nullptr;
+        pp.cap = 0;
+        e = cudaMalloc(&pp.base, need);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(pipeline staging)");
+        pp.cap = need;
+    }
+    for (auto& st : pp.s)
+        if (!st && (e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking)) != cudaSuccess)
+            return cuda_fail(e, "cudaStreamCreate");
+    if (!pp.shared_ready &&
+        (e = cudaEventCreateWithFlags(&pp.shared_ready, cudaEventDisableTiming)) != cudaSuccess)
+        return cuda_fail(e, "cudaEventCreate");
+    char* base = static_cast<char*>(pp.base);
+    std::vector<void*> dptr(11, nullptr);
+    for (int i : kShared) {
+        if (!bufs[i].ptr) continue;
+        dptr[i] = base + off[i];
+        e = cudaMemcpyAsync(dptr[i], bufs[i].ptr, bufs[i].bytes, cudaMemcpyHostToDevice, pp.s[0]);
+        if (e != cudaSuccess) return cuda_fail(e, "copy to device");
+    }
+    if ((e = cudaEventRecord(pp.shared_ready, pp.s[0])) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(pp.s[1], pp.shared_ready, 0)) != cudaSuccess)
+        return cuda_fail(e, "pipeline event");
+    ArmScanDims one = *d;
+    one.batch = 1;
+    for (size_t b = 0; b < nb; ++b) {
+        cudaStream_t st = pp.s[b & 1];
+        char* slot = base + shared_bytes + (b & 1) * slot_bytes;
+        for (int i : kSliced) {
+            if (!bufs[i].ptr) continue;
+            const size_t sl = bufs[i].bytes / nb;
+            dptr[i] = slot + off[i];
+            if (!bufs[i].output) {
+                e = cudaMemcpyAsync(dptr[i], static_cast<const char*>(bufs[i].ptr) + b * sl, sl,
+                                    cudaMemcpyHostToDevice, st);
+                if (e != cudaSuccess) return cuda_fail(e, "copy to device");
+            }
+        }
+        M1Params m = m1_params(&one, dptr, softplus, reverse);
+        m.h0 = static_cast<const float*>(dptr[8]);
+        m.out = static_cast<float*>(dptr[9]);
+        m.last_state = static_cast<float*>(dptr[10]);
+        const int rc = m1_run(m, backend, st);
+        if (rc != ARM_SCAN_OK) {
+            cudaStreamSynchronize(pp.s[0]);
+            cudaStreamSynchronize(pp.s[1]);
+            return rc;
+        }
+        for (int i : {9, 10}) {
+            if (!bufs[i].ptr) continue;
+            const size_t sl = bufs[i].bytes / nb;
+            e = cudaMemcpyAsync(const_cast<char*>(static_cast<const char*>(bufs[i].ptr)) + b * sl,
+                                dptr[i], sl, cudaMemcpyDeviceToHost, st);
+            if (e != cudaSuccess) return cuda_fail(e, "copy to host");
+        }
+    }
+    const cudaError_t e0 = cudaStreamSynchronize(pp.s[0]);
+    const cudaError_t e1 = cudaStreamSynchronize(pp.s[1]);
+    if (e0 != cudaSuccess) return cuda_fail(e0, "kernel");
+    if (e1 != cudaSuccess) return cuda_fail(e1, "kernel");
+    return ARM_SCAN_OK;
+}
+
 int arm_scan_selective_scan_f32(const ArmScanDims* dims, const float* u, const float* delta,
                                 const float* a, const float* b, const float* c,
                                 const float* d_skip, const float* z, const float* delta_bias,
@@ -388,6 +497,9 @@ int arm_scan_selective_scan_f32(const ArmScanDims* dims, const float* u, const f
     bufs.push_back({h0, cnt.bdn * 4, false});
     bufs.push_back({out, cnt.bdl * 4, true});
     bufs.push_back({last_state, cnt.bdn * 4, true});
+    int dev = -1;
+    if (classify(bufs, &dev) == Where::Host && m1_pipeline_worthwhile(dims, bufs))
+        return m1_host_pipelined(dims, bufs, delta_softplus, reverse, backend);
     return run_sync(bufs, [&](const std::vector<void*>& p, cudaStream_t s) {
         M1Params m = m1_params(dims, p, delta_softplus, reverse);
         m.h0 = static_cast<const float*>(p[8]);

@@ -145,12 +145,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ uint16_t bf16_bits(float x) {
-    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
-}
 
 
-// one cvt.rn.bf16x2.f32 (round to nearest even, as bf16_bits)
+// one cvt.rn.bf16x2.f32 (round to nearest even)
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&v);
