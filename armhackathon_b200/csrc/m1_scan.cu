@@ -455,8 +455,7 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
         m1_sequential_kernel<<<grid, 32 * warps_per_block, 0, stream>>>(p);
         return cudaGetLastError();
     }
-    // d_state <= 16 (every Mamba-1 model): the pipelined row-tile kernel,
-    // the fastest measured for both short-wide and batched problems.
+    // Otherwise, d_state <= 16: the pipelined row-tile kernel.
     // B200SCAN_M1_VARIANT overrides for tuning sweeps: 1-4 tile shapes,
     // 5/6/7 row-sequential with 4/2/1 lanes per row, 0 the block-chunked
     // kernel (also the path for d_state > 16).
@@ -465,6 +464,12 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
     const int64_t rows = p.batch * p.dim;
     (void)rows;
     if (variant == 8 && m1_twopass_applicable(p)) return m1_twopass_launch(p, stream);
+    // default: the fold-free two-pass kernel where it applies (length a
+    // multiple of 64, 16-byte aligned, d_state <= 16); variant 12 forces it
+    if (variant == -1 || variant == 12) {
+        const int S = m1_seg2_segments(p);
+        if (S > 0) return m1_seg2_launch(p, S, stream);
+    }
     if ((variant == 5 || variant == 6 || variant == 7) && m1_rowseq_applicable(p))
         return m1_rowseq_launch(p, variant == 6 ? 2 : variant == 7 ? 1 : 4, stream);
     const bool tile_ok = p.state <= 16 && p.len <= (INT32_MAX / 4) && p.state * p.len <= INT32_MAX;

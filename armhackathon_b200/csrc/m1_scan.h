@@ -38,6 +38,10 @@ bool m1_pointers_aligned16(const M1Params& p);
 // Per-device stream-ordered memory pool for kernel workspaces; keeps what it
 // has reserved (defined in m3_tc.cu).
 cudaError_t device_workspace_pool(cudaMemPool_t* out);
+// Fold-free two-pass segmented kernel (m1_seg2.cu): segment count (0: not
+// applicable) and launcher.
+int m1_seg2_segments(const M1Params& p);
+cudaError_t m1_seg2_launch(const M1Params& p, int segments, cudaStream_t stream);
 // Segments of a time-split Mamba-1 scan (1: no split) and its launcher.
 int m1_timesplit_segments(const M1Params& p);
 cudaError_t m1_timesplit_launch(const M1Params& p, int segments, cudaStream_t stream);

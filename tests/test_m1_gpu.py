@@ -201,7 +201,8 @@ def test_mixed_host_device_rejected():
     assert rc == 2
 
 
-@pytest.mark.parametrize("variant", ["0", "1", "2", "3", "4", "5", "6", "7", "8", "9", "10"])
+@pytest.mark.parametrize("variant", ["0", "1", "2", "3", "4", "5", "6", "7", "8", "9", "10",
+                                     "11", "12"])
 @pytest.mark.parametrize("reverse", [False, True])
 def test_every_kernel_variant_vs_oracle(variant, reverse, monkeypatch):
     """Each Mamba-1 kernel shape the library can dispatch to (selected with
@@ -273,3 +274,27 @@ def test_host_entry_pipelined_matches_device(shape):
         return_last_state=True)
     assert np.array_equal(out_h, out_d.cpu().numpy())
     assert np.array_equal(last_h, last_d.cpu().numpy())
+
+
+@pytest.mark.parametrize("shape", [(2, 40, 2048, 16, 2), (3, 130, 1024, 13, 1), (1, 8, 4096, 16, 1)])
+@pytest.mark.parametrize("segments", ["1", "4", "16"])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_fold_free_two_pass_vs_oracle(shape, segments, reverse, monkeypatch):
+    """Variant 12 (fold-free two-pass: segment end states, exact segment-decay
+    carries, rescan) on lengths it covers, with grouped B/C, ragged channel
+    counts, d_state 13, h0 and slowly decaying states that carry across
+    segments."""
+    monkeypatch.setenv("B200SCAN_M1_VARIANT", "12")
+    monkeypatch.setenv("B200SCAN_M1_SEG2_S", segments)
+    B, D, L, N, G = shape
+    x = _slow_decay_case(B, D, L, N, seed=L + N)
+    if G > 1:
+        rng = np.random.default_rng(5)
+        x["B"] = rng.standard_normal((B, G, N, L)).astype(np.float32)
+        x["C"] = rng.standard_normal((B, G, N, L)).astype(np.float32)
+    h0 = np.random.default_rng(2).standard_normal((B, D, N)).astype(np.float32)
+    want, want_last = oracle.m1_scan(**x, reverse=reverse, h0=h0, nthreads=8)
+    out, last = arm().selective_scan(**cuda(x), reverse=reverse, return_last_state=True,
+                                     initial_state=torch.from_numpy(h0).cuda())
+    assert rel_err(out.cpu().numpy(), want) <= REL_TOL
+    assert rel_err(last.cpu().numpy(), want_last) <= REL_TOL
