@@ -100,6 +100,8 @@ def _bind(lib):
               "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
               "arm_scan_tensor_status"):
         getattr(lib, f).restype = ctypes.c_int
+    lib.arm_scan_kernel_launches.restype = ctypes.c_ulonglong
+    lib.arm_scan_kernel_launches.argtypes = []
     lib.arm_scan_mamba3_siso_tc_async.restype = ctypes.c_int
     lib.arm_scan_mamba3_siso_tc_async.argtypes = [
         ctypes.POINTER(ArmMamba3Dims), ctypes.POINTER(ArmMamba3TcOptions), *([_VP] * 11),
@@ -217,6 +219,11 @@ def angles_async_raw(dims, ptr_angles, n_angles, ptr_dt, ptr_cos, ptr_sin, ptr_w
         _n(stream)), "arm_scan_mamba3_angles_f32_async")
 
 
+def kernel_launches():
+    """GPU kernels the library has launched in this process so far."""
+    return int(load().arm_scan_kernel_launches())
+
+
 def tensor_status():
     """Raise if a tensor-core kernel's bounded wait expired since the last
     check (call after synchronizing the stream of an async launch)."""
@@ -232,7 +239,7 @@ def exported_symbols():
             "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
             "arm_scan_mamba3_angles_workspace_bytes", "arm_scan_mamba3_angles_f32_async",
             "arm_scan_mamba3_angles_f32_noalloc", "arm_scan_tensor_status",
-            "arm_scan_mamba3_siso_tc_async"]
+            "arm_scan_mamba3_siso_tc_async", "arm_scan_kernel_launches"]
 
 
 if __name__ == "__main__":  # pragma: no cover

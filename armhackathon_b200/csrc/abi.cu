@@ -7,6 +7,7 @@
 // arm-scan-core's validate() (lib.rs:181-249) and mamba3/mod.rs:213-335.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -367,6 +368,11 @@ int m3_run(const M3Params& m, int backend, cudaStream_t s) {
 
 }  // namespace
 
+namespace b200scan {
+std::atomic<unsigned long long> g_kernel_launches{0};
+void note_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace b200scan
+
 extern "C" {
 
 uint32_t arm_scan_abi_version(void) { return ARM_SCAN_ABI_VERSION; }
@@ -626,6 +632,8 @@ int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const fl
 }
 
 int arm_scan_tensor_status(void) { return tensor_status_code(); }
+
+unsigned long long arm_scan_kernel_launches(void) { return b200scan::g_kernel_launches.load(); }
 
 int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOptions* opts,
                                   const void* q, const void* k, const void* v, const float* adt,

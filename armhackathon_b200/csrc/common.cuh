@@ -15,6 +15,12 @@
 
 namespace b200scan {
 
+// Counts kernel launches made by this library (host side, all threads);
+// read through arm_scan_kernel_launches().  Every launcher calls it once per
+// kernel it starts.
+void note_launch();
+
+
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ float ex2_approx(float x) {

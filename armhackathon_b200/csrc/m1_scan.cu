@@ -306,6 +306,7 @@ cudaError_t launch_chunked(const M1Params& p, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
     }
     kern<<<grid, kThreads, smem, stream>>>(p);
+    note_launch();
     return cudaGetLastError();
 }
 
@@ -429,12 +430,14 @@ cudaError_t m1_timesplit_launch(const M1Params& p, int S, cudaStream_t stream) {
     e = m1_tile_launch(q, 1, stream);
     if (e == cudaSuccess) {
         m1_seg_dtsum_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(p, S, Ls, dtsum);
+        note_launch();
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
         const int64_t n = p.batch * p.dim * p.state;
         m1_seg_fold_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(p, S, hend,
                                                                                      dtsum, hin);
+        note_launch();
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
@@ -453,6 +456,7 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
         const int warps_per_block = 4;
         const dim3 grid(static_cast<unsigned>((BD + warps_per_block - 1) / warps_per_block));
         m1_sequential_kernel<<<grid, 32 * warps_per_block, 0, stream>>>(p);
+        note_launch();
         return cudaGetLastError();
     }
     // Otherwise, d_state <= 16: the pipelined row-tile kernel.

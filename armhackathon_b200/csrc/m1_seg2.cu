@@ -30,6 +30,11 @@ namespace {
 
 constexpr int kS2Rows = 128;   // threads (rows) per CTA
 constexpr int kS2Chunk = 64;   // steps of B/C per staged chunk
+// default share of exps on the FMA pipe (see m1_seg2_kernel): pass 2 (kSeg2Poly)
+// and pass 1 (kSeg2Poly1, the MUFU-bound one); the two passes' decays then
+// differ by the approximations' error (~1e-7 relative), not by design
+constexpr int kSeg2Poly = 0;
+constexpr int kSeg2Poly1 = 0;
 constexpr int kS2Stride = 20;  // floats per staged step (16 states + pad: fewer bank conflicts)
 
 __device__ __forceinline__ void cpa4(float* smem, const float* gmem, bool pred) {
@@ -55,7 +60,9 @@ __device__ __forceinline__ float4 ld_steps(const float* row, int64_t L, int64_t 
     return make_float4(v.w, v.z, v.y, v.x);
 }
 
-template <bool FULL, bool REV>
+// POLY: 0 every exp on MUFU; 1 states 12-15 (25%), 2 states 8-15 (50%) on the
+// FMA pipe (exp2_poly2).
+template <bool FULL, bool REV, int POLY>
 __global__ void __launch_bounds__(kS2Rows) m1_seg2_kernel(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
     __shared__ __align__(16) float sb[2][2][kS2Chunk * kS2Stride];  // [buf][B, C][step][state]
     const int N = static_cast<int>(p.state);
@@ -153,8 +160,9 @@ __global__ void __launch_bounds__(kS2Rows) m1_seg2_kernel(M1Params p, Seg2Ws ws,
                 for (int q4 = 0; q4 < 4; ++q4) {
                     const float4 bb = *reinterpret_cast<const float4*>(bk + 4 * q4);
                     const float2 x0 = fmul2(dt2, a2[2 * q4]), x1 = fmul2(dt2, a2[2 * q4 + 1]);
-                    const float2 e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-                    const float2 e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+                    const bool poly = (POLY == 1 && q4 == 3) || (POLY == 2 && q4 >= 2);
+                    const float2 e0 = poly ? exp2_poly2(x0) : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+                    const float2 e1 = poly ? exp2_poly2(x1) : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
                     h[2 * q4] = ffma2(e0, h[2 * q4], fmul2(du2, make_float2(bb.x, bb.y)));
                     h[2 * q4 + 1] = ffma2(e1, h[2 * q4 + 1], fmul2(du2, make_float2(bb.z, bb.w)));
                     if (FULL) {
@@ -199,8 +207,9 @@ __global__ void m1_seg2_carry_kernel(M1Params p, Seg2Ws ws, int S) {
     float h = p.h0 ? p.h0[i] : 0.f;
     for (int k = 0; k < S; ++k) {  // segments are already in traversal order
         const int64_t sr = static_cast<int64_t>(k) * rows_all + row;
+        const float ds = __ldg(ws.dtsum + sr), he = __ldg(ws.hend + sr * 16 + n);
         ws.hin[sr * 16 + n] = h;
-        h = fmaf(ex2_approx(a * ws.dtsum[sr]), h, ws.hend[sr * 16 + n]);
+        h = fmaf(ex2_approx(a * ds), h, he);
     }
     if (p.last_state) p.last_state[i] = h;
 }
@@ -241,21 +250,27 @@ cudaError_t m1_seg2_launch(const M1Params& p, int S, cudaStream_t stream) {
     const int64_t gsz = p.dim / p.groups;
     const dim3 grid(static_cast<unsigned>(((gsz + kS2Rows - 1) / kS2Rows) * p.batch * p.groups),
                     static_cast<unsigned>(S));
-    if (p.reverse)
-        m1_seg2_kernel<false, true><<<grid, kS2Rows, 0, stream>>>(p, ws, S, Ls);
-    else
-        m1_seg2_kernel<false, false><<<grid, kS2Rows, 0, stream>>>(p, ws, S, Ls);
+    int poly = kSeg2Poly, poly1 = kSeg2Poly1;
+    if (const char* v = getenv("B200SCAN_M1_SEG2_POLY")) poly = atoi(v);
+    if (const char* v = getenv("B200SCAN_M1_SEG2_POLY1")) poly1 = atoi(v);
+    auto k1 = poly1 == 2 ? (p.reverse ? m1_seg2_kernel<false, true, 2> : m1_seg2_kernel<false, false, 2>)
+            : poly1 == 1 ? (p.reverse ? m1_seg2_kernel<false, true, 1> : m1_seg2_kernel<false, false, 1>)
+                         : (p.reverse ? m1_seg2_kernel<false, true, 0> : m1_seg2_kernel<false, false, 0>);
+    auto k2 = poly == 2 ? (p.reverse ? m1_seg2_kernel<true, true, 2> : m1_seg2_kernel<true, false, 2>)
+            : poly == 1 ? (p.reverse ? m1_seg2_kernel<true, true, 1> : m1_seg2_kernel<true, false, 1>)
+                        : (p.reverse ? m1_seg2_kernel<true, true, 0> : m1_seg2_kernel<true, false, 0>);
+    k1<<<grid, kS2Rows, 0, stream>>>(p, ws, S, Ls);
+    note_launch();
     e = cudaGetLastError();
     if (e == cudaSuccess) {
         const int64_t n = rows * p.state;
         m1_seg2_carry_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(p, ws, S);
+        note_launch();
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
-        if (p.reverse)
-            m1_seg2_kernel<true, true><<<grid, kS2Rows, 0, stream>>>(p, ws, S, Ls);
-        else
-            m1_seg2_kernel<true, false><<<grid, kS2Rows, 0, stream>>>(p, ws, S, Ls);
+        k2<<<grid, kS2Rows, 0, stream>>>(p, ws, S, Ls);
+        note_launch();
         e = cudaGetLastError();
     }
     const cudaError_t ef = cudaFreeAsync(raw, stream);

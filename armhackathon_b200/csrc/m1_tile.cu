@@ -368,6 +368,7 @@ cudaError_t launch_tile(const M1Params& p, cudaStream_t stream) {
     const int64_t grid = n_tiles < cap ? n_tiles : cap;
     kern<<<dim3(static_cast<unsigned>(grid)), kTileThreads, smem, stream>>>(
         p, static_cast<int>(tiles_per_group), static_cast<int>(n_tiles));
+    note_launch();
     return cudaGetLastError();
 }
 

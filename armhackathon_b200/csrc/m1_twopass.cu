@@ -277,6 +277,7 @@ cudaError_t m1_twopass_launch(const M1Params& p, cudaStream_t stream) {
     const int64_t cap = static_cast<int64_t>(sms) * per_sm;
     kern<<<dim3(static_cast<unsigned>(n_tiles < cap ? n_tiles : cap)), kTpWarps * 32, smem,
            stream>>>(p, static_cast<int>(tiles_per_group), static_cast<int>(n_tiles));
+    note_launch();
     return cudaGetLastError();
 }
 

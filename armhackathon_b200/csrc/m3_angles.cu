@@ -110,9 +110,11 @@ cudaError_t angle_launch(const AngleParams& a, float* ws, cudaStream_t stream) {
     const int t1 = static_cast<int>((a.n_angles + 31) / 32 * 32);
     const int t2 = static_cast<int>((a.half + 31) / 32 * 32);
     angle_chunk_sums<<<grid, t1, 0, stream>>>(a, ws);
+    note_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     angle_chunk_write<<<grid, t2, 0, stream>>>(a, ws);
+    note_launch();
     return cudaGetLastError();
 }
 

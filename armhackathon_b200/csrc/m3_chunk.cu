@@ -530,15 +530,18 @@ cudaError_t m3_chunk_launch_split(const M3Params& p, cudaStream_t stream) {
     ws.decay = ws.st + units * np;
     const dim3 grid(static_cast<unsigned>(n_chunks), static_cast<unsigned>(bh));
     m3_chunk_ds_kernel<R><<<grid, kCkThreads, smem_ds, stream>>>(p, ws, n_chunks);
+    note_launch();
     e = cudaGetLastError();
     if (e == cudaSuccess) {
         const unsigned slices = static_cast<unsigned>((np / 4 + kCkThreads - 1) / kCkThreads);
         m3_chunk_state_kernel<<<dim3(static_cast<unsigned>(bh), slices), kCkThreads, 0, stream>>>(
             p, ws, n_chunks);
+        note_launch();
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
         m3_chunk_out_kernel<R><<<grid, kCkThreads, smem_out, stream>>>(p, ws, n_chunks);
+        note_launch();
         e = cudaGetLastError();
     }
     const cudaError_t ef = cudaFreeAsync(raw, stream);
@@ -569,6 +572,7 @@ cudaError_t m3_chunk_launch(const M3Params& p, cudaStream_t stream) {
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     kern<<<dim3(static_cast<unsigned>(p.batch * p.heads)), kCkThreads, smem, stream>>>(p);
+    note_launch();
     return cudaGetLastError();
 }
 

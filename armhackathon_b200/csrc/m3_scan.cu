@@ -219,6 +219,7 @@ cudaError_t m3_scan_launch(const M3Params& p, int backend, cudaStream_t stream) 
     }
     const dim3 grid(static_cast<unsigned>(p.batch * p.heads));
     kern<<<grid, kM3Threads, smem, stream>>>(p);
+    note_launch();
     return cudaGetLastError();
 }
 

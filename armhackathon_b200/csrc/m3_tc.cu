@@ -1668,14 +1668,17 @@ cudaError_t m3_tc_launch_split(const M3Params& p, cudaStream_t stream) {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     m3_tc_dstate<<<static_cast<unsigned>(units), kTcThreads2, kASmem, stream>>>(p, ws, n_chunks);
+    note_launch();
     e = cudaGetLastError();
     if (e == cudaSuccess) {
         m3_tc_state<<<dim3(static_cast<unsigned>(bh), kStSlices), kTcThreads2, 0, stream>>>(p, ws, n_chunks);
+        note_launch();
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
         const size_t grid = units < static_cast<size_t>(2 * sms) ? units : static_cast<size_t>(2 * sms);
         m3_tc_out<<<static_cast<unsigned>(grid), kTcThreads2, kCSmem, stream>>>(p, ws, n_chunks);
+        note_launch();
         e = cudaGetLastError();
     }
     const cudaError_t ef = cudaFreeAsync(raw, stream);
@@ -1698,6 +1701,7 @@ cudaError_t launch_fused_kernel(const M3Params& p, const ChainWs& cw, int n_chun
     const int64_t units = p.batch * p.heads * n_chunks;
     const int64_t grid = units < 2 * sms ? units : 2 * sms;
     kern<<<static_cast<unsigned>(grid), kTcThreads2, kFSmem, stream>>>(p, cw, n_chunks, ta, theta0);
+    note_launch();
     return cudaGetLastError();
 }
 
@@ -1727,13 +1731,17 @@ cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
     e = cudaMemsetAsync(cw.flags, 0, flag_bytes, stream);
     if (e == cudaSuccess && ang && p.n_angles > 0) {
         const dim3 g(static_cast<unsigned>(n_chunks), static_cast<unsigned>(bh));
-        if (p.in_bf16)
+        if (p.in_bf16) {
             m3_tc_angle_sums<true><<<g, 256, 0, stream>>>(p, ta, theta0, n_chunks);
-        else
+            note_launch();
+        } else {
             m3_tc_angle_sums<false><<<g, 256, 0, stream>>>(p, ta, theta0, n_chunks);
+            note_launch();
+        }
         e = cudaGetLastError();
         if (e == cudaSuccess) {
             m3_tc_angle_prefix<<<static_cast<unsigned>(bh), 64, 0, stream>>>(p, theta0, n_chunks);
+            note_launch();
             e = cudaGetLastError();
         }
     }

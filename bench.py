@@ -211,11 +211,11 @@ def peaks():
 
 
 def profiled_traffic(workload):
-    """DRAM bytes per launch of the scan kernel from the committed ncu summary
-    (profiles/m1_tile_<workload>.md, line 'traffic_bytes_per_launch: N'), or
-    None when no capture of this workload is committed."""
+    """DRAM bytes of one scan op (all of its kernels) from the committed ncu
+    summary (profiles/m1_seg2_<workload>.md, line 'traffic_bytes_per_launch:
+    N'), or None when no capture of this workload is committed."""
     import re
-    f = ROOT / "profiles" / f"m1_tile_{workload}.md"
+    f = ROOT / "profiles" / f"m1_seg2_{workload}.md"
     if not f.exists():
         return None
     m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", f.read_text())
@@ -476,7 +476,8 @@ def main():
     torch.cuda.synchronize()
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    launches_before = arm.kernel_calls()
+    from armhackathon_b200 import _ffi
+    launches_before = _ffi.kernel_launches()
     with ClockSampler(local) as clk:
         t_begin.record(stream)
         for i in range(args.steps):
@@ -487,7 +488,7 @@ def main():
             ends[i].record(stream)
         t_end.record(stream)
         torch.cuda.synchronize()
-    launches = arm.kernel_calls() - launches_before
+    launches = _ffi.kernel_launches() - launches_before  # GPU kernels, counted by the library
     if world > 1:
         dist.barrier()
     kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
@@ -553,8 +554,8 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
                          "traffic": profiled_traffic(args.workload),
-                         "traffic_source": "ncu dram__bytes_read+write, one launch "
-                                           "(profiles/m1_tile_<workload>.md)",
+                         "traffic_source": "ncu dram__bytes_read+write summed over the op's "
+                                           "kernels (profiles/m1_seg2_<workload>.md)",
                          "bytes_per_launch": nbytes,
                          "kernel_ms": k_ms},
             "gpu_launches": launches,

@@ -221,6 +221,11 @@ int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOp
  * and clears the flag. */
 int arm_scan_tensor_status(void);
 
+/* Extension (diagnostics, no counterpart in the reference): number of GPU
+ * kernels this library has launched in the process so far (all devices,
+ * all threads); the difference around a call is that call's launch count. */
+unsigned long long arm_scan_kernel_launches(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -298,3 +298,16 @@ def test_fold_free_two_pass_vs_oracle(shape, segments, reverse, monkeypatch):
                                      initial_state=torch.from_numpy(h0).cuda())
     assert rel_err(out.cpu().numpy(), want) <= REL_TOL
     assert rel_err(last.cpu().numpy(), want_last) <= REL_TOL
+
+
+def test_library_counts_its_kernel_launches():
+    """arm_scan_kernel_launches() advances by the kernels a call starts: three
+    for the default fold-free form (pass 1, carries, pass 2)."""
+    from armhackathon_b200 import _ffi
+    x = cuda(random_case(2, 64, 2048, 16, seed=3))
+    arm().selective_scan(**x)
+    torch.cuda.synchronize()
+    before = _ffi.kernel_launches()
+    arm().selective_scan(**x)
+    torch.cuda.synchronize()
+    assert _ffi.kernel_launches() - before == 3
