@@ -8,6 +8,7 @@ surface of the reference ``arm_scan`` package (AdityaP9116/ARMHackathon).
     arm_scan.mamba3_scan(...) / mamba3_scan_pair(...) / mamba3_mimo_scan(...)
     arm_scan.ss2d_scan_mamba3(...) / noncausal_scan(...) / ss2d_noncausal_mamba3(...)
     arm_scan.selective_scan_numpy(...)     # numpy in, numpy out (no torch)
+    arm_scan.selective_state_update(state, x, dt, A, B, C, ...)  # one decode step
 
 Every scan runs as sm_100a CUDA kernels in libb200scan.so, reached through
 its C ABI (include/b200scan.h).  There is no CPU implementation.
@@ -21,10 +22,12 @@ __all__ = [
     "bidirectional_scan", "ss2d_scan", "use_arm_scan", "mamba3_scan", "mamba3_scan_pair",
     "mamba3_mimo_scan", "ss2d_scan_mamba3", "noncausal_scan", "noncausal_scan_dense",
     "ss2d_noncausal_mamba3", "angles_to_cos_sin", "patch", "unpatch", "stats", "kernel_calls",
+    "selective_state_update",
 ]
 
 _LAZY = {
     "selective_scan": ".op", "selective_scan_bidirectional": ".op", "kernel_calls": ".op",
+    "selective_state_update": ".op",
     "bidirectional_scan": ".bidirectional",
     "ss2d_scan": ".ss2d", "use_arm_scan": ".ss2d",
     "mamba3_scan": ".mamba3", "mamba3_scan_pair": ".mamba3", "mamba3_mimo_scan": ".mamba3",

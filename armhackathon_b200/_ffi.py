@@ -100,6 +100,9 @@ def _bind(lib):
               "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
               "arm_scan_tensor_status"):
         getattr(lib, f).restype = ctypes.c_int
+    lib.arm_scan_selective_state_update_f32_async.restype = ctypes.c_int
+    lib.arm_scan_selective_state_update_f32_async.argtypes = [
+        ctypes.POINTER(ArmScanDims), *([_VP] * 9), ctypes.c_int, _VP, _VP]
     lib.arm_scan_kernel_launches.restype = ctypes.c_ulonglong
     lib.arm_scan_kernel_launches.argtypes = []
     lib.arm_scan_mamba3_siso_tc_async.restype = ctypes.c_int
@@ -219,6 +222,15 @@ def angles_async_raw(dims, ptr_angles, n_angles, ptr_dt, ptr_cos, ptr_sin, ptr_w
         _n(stream)), "arm_scan_mamba3_angles_f32_async")
 
 
+def state_update_raw(dims, ptr_state, ptr_x, ptr_dt, ptr_a, ptr_b, ptr_c, ptr_d_skip, ptr_z,
+                     ptr_dt_bias, dt_softplus, ptr_out, stream):
+    """One Mamba-1 decode step (device pointers, stream-ordered)."""
+    _check(load().arm_scan_selective_state_update_f32_async(
+        ctypes.byref(dims), ptr_state, ptr_x, ptr_dt, ptr_a, ptr_b, ptr_c, _n(ptr_d_skip),
+        _n(ptr_z), _n(ptr_dt_bias), int(dt_softplus), ptr_out, _n(stream)),
+        "arm_scan_selective_state_update_f32_async")
+
+
 def kernel_launches():
     """GPU kernels the library has launched in this process so far."""
     return int(load().arm_scan_kernel_launches())
@@ -239,7 +251,8 @@ def exported_symbols():
             "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
             "arm_scan_mamba3_angles_workspace_bytes", "arm_scan_mamba3_angles_f32_async",
             "arm_scan_mamba3_angles_f32_noalloc", "arm_scan_tensor_status",
-            "arm_scan_mamba3_siso_tc_async", "arm_scan_kernel_launches"]
+            "arm_scan_mamba3_siso_tc_async", "arm_scan_kernel_launches",
+            "arm_scan_selective_state_update_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

@@ -633,6 +633,42 @@ int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const fl
 
 int arm_scan_tensor_status(void) { return tensor_status_code(); }
 
+int arm_scan_selective_state_update_f32_async(const ArmScanDims* dims, float* state,
+                                              const float* x, const float* dt, const float* a,
+                                              const float* b, const float* c,
+                                              const float* d_skip, const float* z,
+                                              const float* dt_bias, int dt_softplus, float* out,
+                                              void* stream) {
+    if (!dims || !state || !x || !dt || !a || !b || !c || !out)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    if (!dims->batch || !dims->dim || !dims->state || !dims->groups)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "batch, dim, state and groups must be non-zero");
+    if (dims->dim % dims->groups)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "dim (%zu) must be a multiple of groups (%zu)",
+                    dims->dim, dims->groups);
+    size_t bd = 0, bdn = 0;
+    if (!mul3(dims->batch, dims->dim, 1, &bd) || !mul3(dims->batch, dims->dim, dims->state, &bdn))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "element counts overflow");
+    M1Params m{};
+    m.u = x;
+    m.delta = dt;
+    m.A = a;
+    m.B = b;
+    m.C = c;
+    m.d_skip = d_skip;
+    m.z = z;
+    m.delta_bias = dt_bias;
+    m.out = out;
+    m.batch = static_cast<int64_t>(dims->batch);
+    m.dim = static_cast<int64_t>(dims->dim);
+    m.len = 1;
+    m.state = static_cast<int64_t>(dims->state);
+    m.groups = static_cast<int64_t>(dims->groups);
+    m.delta_softplus = dt_softplus != 0;
+    cudaError_t e = m1_decode_launch(m, state, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "selective_state_update launch");
+}
+
 unsigned long long arm_scan_kernel_launches(void) { return b200scan::g_kernel_launches.load(); }
 
 int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOptions* opts,

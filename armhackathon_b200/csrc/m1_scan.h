@@ -38,6 +38,10 @@ bool m1_pointers_aligned16(const M1Params& p);
 // Per-device stream-ordered memory pool for kernel workspaces; keeps what it
 // has reserved (defined in m3_tc.cu).
 cudaError_t device_workspace_pool(cudaMemPool_t* out);
+// Single-token state update (m1_decode.cu): p.u = x (batch, dim), p.delta =
+// dt (batch, dim), p.B/p.C (batch, groups, state), p.out (batch, dim);
+// state (batch, dim, state) is read and updated in place.
+cudaError_t m1_decode_launch(const M1Params& p, float* state, cudaStream_t stream);
 // Fold-free two-pass segmented kernel (m1_seg2.cu): segment count (0: not
 // applicable) and launcher.
 int m1_seg2_segments(const M1Params& p);

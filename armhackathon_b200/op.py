@@ -179,3 +179,57 @@ def selective_scan_bidirectional(u, delta, A, B, C, D=None, z=None,
 def kernel_calls() -> int:
     """How many times a native scan entry point has been invoked."""
     return _CALLS["n"]
+
+
+@torch.library.custom_op("arm_scan::selective_state_update", mutates_args=("state",))
+def _state_update_op(state: torch.Tensor, x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor,
+                     B: torch.Tensor, C: torch.Tensor, D: Optional[torch.Tensor],
+                     z: Optional[torch.Tensor], dt_bias: Optional[torch.Tensor],
+                     dt_softplus: bool) -> torch.Tensor:
+    batch, dim, n = state.shape
+    groups = B.shape[1]
+    dims = _ffi.ArmScanDims(batch, dim, 1, n, groups)
+    out = x.new_empty((batch, dim))
+    with _on_device(state):
+        _ffi.state_update_raw(dims, state.data_ptr(), x.data_ptr(), dt.data_ptr(), A.data_ptr(),
+                              B.data_ptr(), C.data_ptr(), _ptr(D), _ptr(z), _ptr(dt_bias),
+                              dt_softplus, out.data_ptr(), _stream(state))
+    _CALLS["n"] += 1
+    return out
+
+
+@_state_update_op.register_fake
+def _(state, x, dt, A, B, C, D, z, dt_bias, dt_softplus):
+    return x.new_empty((state.shape[0], state.shape[1]))
+
+
+def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None,
+                           dt_softplus=False):
+    """One decode step of the Mamba-1 recurrence (mamba_ssm's
+    ``selective_state_update``): updates ``state`` (batch, dim, d_state), a
+    contiguous fp32 CUDA tensor, in place and returns y (batch, dim).
+
+    x, dt, z : (batch, dim);  A : (dim, d_state);  B, C : (batch, d_state) or
+    (batch, groups, d_state);  D, dt_bias : (dim,).  Equivalent to
+    ``selective_scan`` over one step with ``initial_state=state`` and
+    ``return_last_state=True``, without the scan's staging.
+    """
+    if state.device.type != "cuda" or state.dtype != torch.float32 or not state.is_contiguous():
+        raise ValueError("state must be a contiguous float32 CUDA tensor (updated in place)")
+    batch, dim, n = state.shape
+    dev = state.device
+    if B.dim() == 2:
+        B, C = B.unsqueeze(1), C.unsqueeze(1)
+    groups = B.shape[1]
+    for name, t, want in (("x", x, (batch, dim)), ("dt", dt, (batch, dim)), ("A", A, (dim, n)),
+                          ("B", B, (batch, groups, n)), ("C", C, (batch, groups, n))):
+        if tuple(t.shape) != want:
+            raise ValueError(f"{name} must be {want}, got {tuple(t.shape)}")
+    if dim % groups:
+        raise ValueError(f"dim ({dim}) must be a multiple of groups ({groups})")
+    for name, t, want in (("D", D, (dim,)), ("dt_bias", dt_bias, (dim,)), ("z", z, (batch, dim))):
+        if t is not None and tuple(t.shape) != want:
+            raise ValueError(f"{name} must be {want}, got {tuple(t.shape)}")
+    opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
+    return _state_update_op(state, _prep(x, dev), _prep(dt, dev), _prep(A, dev), _prep(B, dev),
+                            _prep(C, dev), opt(D), opt(z), opt(dt_bias), bool(dt_softplus))

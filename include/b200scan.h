@@ -212,6 +212,20 @@ int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOp
                                   const void* z, int reverse, void* out, float* last_state,
                                   float* last_bx, void* stream);
 
+/* Extension (no counterpart in the reference; mamba_ssm's
+ * selective_state_update): one decode step of the Mamba-1 recurrence for
+ * every (batch, channel), updating `state` (batch, dim, state) in place:
+ * dt' = softplus(dt + dt_bias) if dt_softplus, h = exp(dt' A) h + dt' x B,
+ * out = C.h + D x, times silu(z).  x, dt, z, out are (batch, dim); B, C are
+ * (batch, groups, state); A (dim, state); D, dt_bias (dim,).  dims->len is
+ * ignored.  Device pointers, stream-ordered; nullable: d_skip, z, dt_bias. */
+int arm_scan_selective_state_update_f32_async(const ArmScanDims* dims, float* state,
+                                              const float* x, const float* dt, const float* a,
+                                              const float* b, const float* c,
+                                              const float* d_skip, const float* z,
+                                              const float* dt_bias, int dt_softplus, float* out,
+                                              void* stream);
+
 /* Extension (no counterpart in the reference): status of the tensor-core
  * kernels (backend 3).  Their waits on their own MMA completions are
  * bounded; an expired wait abandons the remaining tiles and sets a device

@@ -141,3 +141,18 @@ def test_lazy_exports_are_functions_after_submodule_import():
     for name in ("patch", "unpatch", "stats", "selective_scan", "mamba3_scan", "ss2d_scan"):
         assert callable(getattr(arm, name)) and not hasattr(getattr(arm, name), "__path__")
     assert type(arm.patch).__name__ == "function"
+
+
+def test_state_update_argument_rules():
+    """arm_scan_selective_state_update_f32_async: host checks before any
+    device work (dummy pointers never dereferenced)."""
+    lib = _ffi.load()
+    p = ctypes.c_void_p(16)
+
+    def call(dims, null_state=False):
+        return lib.arm_scan_selective_state_update_f32_async(
+            ctypes.byref(dims), None if null_state else p, p, p, p, p, p, None, None, None, 1, p,
+            None)
+    assert call(_ffi.ArmScanDims(1, 4, 1, 4, 1), null_state=True) == 1
+    assert call(_ffi.ArmScanDims(0, 4, 1, 4, 1)) == 2
+    assert call(_ffi.ArmScanDims(1, 6, 1, 4, 4)) == 2   # dim not a multiple of groups

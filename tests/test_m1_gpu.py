@@ -311,3 +311,26 @@ def test_library_counts_its_kernel_launches():
     arm().selective_scan(**x)
     torch.cuda.synchronize()
     assert _ffi.kernel_launches() - before == 3
+
+
+@pytest.mark.parametrize("groups", [1, 2])
+def test_decode_steps_equal_the_scan(groups):
+    """T chained selective_state_update steps from h0 reproduce the scan of
+    the same T steps (outputs and final state), and one step matches the
+    oracle."""
+    B, D, T, N = 3, 40, 9, 16
+    x = random_case(B, D, T, N, groups, seed=11)
+    h0 = np.random.default_rng(4).standard_normal((B, D, N)).astype(np.float32)
+    want, want_last = oracle.m1_scan(**x, h0=h0, nthreads=8)
+    c = cuda(x)
+    state = torch.from_numpy(h0).cuda().contiguous()
+    ys = []
+    for t in range(T):
+        Bt = c["B"][..., t] if groups > 1 else c["B"][:, :, t]
+        Ct = c["C"][..., t] if groups > 1 else c["C"][:, :, t]
+        ys.append(arm().selective_state_update(
+            state, c["u"][:, :, t], c["delta"][:, :, t], c["A"], Bt, Ct, D=c["D"],
+            z=c["z"][:, :, t], dt_bias=c["delta_bias"], dt_softplus=True))
+    y = torch.stack(ys, dim=-1)
+    assert rel_err(y.cpu().numpy(), want) <= REL_TOL
+    assert rel_err(state.cpu().numpy(), want_last) <= REL_TOL
