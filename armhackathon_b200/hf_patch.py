@@ -22,9 +22,11 @@ For releases without slow_forward but with a module-level
 ``mamba_selective_scan`` that function is wrapped instead.
 
 The kernel handles cache-less forwards and the cached prefill of
-``generate()`` (zero initial state).  Decode steps, mamba.py training mode and
-any call that needs autograd (the op has no backward) fall back to the
-original.
+``generate()`` (zero initial state).  With the "has_previous_state" API the
+decode steps of ``generate()`` also run on the GPU (one
+``selective_state_update`` per layer and token; an extension: the reference
+falls back for them).  Other decode steps, mamba.py training mode and any
+call that needs autograd (the op has no backward) fall back to the original.
 """
 
 import inspect
@@ -32,10 +34,10 @@ import inspect
 import torch
 import torch.nn.functional as F
 
-from .op import kernel_calls, selective_scan
+from .op import kernel_calls, selective_scan, selective_state_update
 
 _STATE = {"orig": None, "api": None, "arg_names": (), "target": None,
-          "fast_calls": 0, "fallback_calls": 0}
+          "fast_calls": 0, "fallback_calls": 0, "decode_calls": 0}
 
 
 def _detect_api(orig):
@@ -85,6 +87,35 @@ def _mixer_scan_forward(self, input_states, cache_params, cache_position, attent
         else:
             cache_params.update_recurrent_state(last_state.to(dtype), self.layer_idx)
     return self.out_proj(scan_output.transpose(1, 2).to(dtype))
+
+
+def _mixer_decode_forward(self, input_states, cache_params, attention_mask):
+    """MambaMixer.slow_forward's decode branch ("has_previous_state" API, one
+    token) with the state update on the GPU kernel."""
+    # shapes and mask handling exactly as the original's decode branch
+    dtype = input_states.dtype
+    projected_states = self.in_proj(input_states).transpose(1, 2)
+    hidden_states, gate = projected_states.chunk(2, dim=1)
+    if attention_mask is not None:
+        hidden_states = hidden_states * attention_mask.unsqueeze(1)
+    state = cache_params.layers[self.layer_idx].recurrent_states.to(torch.float32).contiguous()
+    conv_state = cache_params.update_conv_state(hidden_states, self.layer_idx)
+    conv_state = conv_state.to(self.conv1d.weight.device)
+    hidden_states = torch.sum(conv_state * self.conv1d.weight[:, 0, :], dim=-1)
+    if self.use_conv_bias:
+        hidden_states = hidden_states + self.conv1d.bias
+    hidden_states = self.act(hidden_states).to(dtype).unsqueeze(-1)  # [batch, intermediate_size, 1]
+    if attention_mask is not None:
+        hidden_states = hidden_states * attention_mask.unsqueeze(1)
+    hidden_states = hidden_states[:, :, -1]
+    ssm_parameters = self.x_proj(hidden_states)
+    time_step, B, C = torch.split(
+        ssm_parameters, [self.time_step_rank, self.ssm_state_size, self.ssm_state_size], dim=-1)
+    A = -torch.exp(self.A_log.float())
+    y = selective_state_update(state, hidden_states, self.dt_proj(time_step), A, B, C, D=self.D,
+                               z=gate[:, :, -1], dt_softplus=True)
+    cache_params.update_recurrent_state(state.to(dtype), self.layer_idx)
+    return self.out_proj(y.unsqueeze(1).to(dtype))
 
 
 def _patch_scan_fn(modeling_mamba):
@@ -151,6 +182,11 @@ def patch():
         else:
             is_prefill = cache_params is None or not cache_params.has_previous_state(
                 self.layer_idx)
+        if (not is_prefill and api == "has_previous_state" and input_states.shape[1] == 1
+                and input_states.device.type == "cuda" and not self.training
+                and not _needs_grad(self, input_states)):
+            _STATE["decode_calls"] += 1
+            return _mixer_decode_forward(self, input_states, cache_params, attention_mask)
         if (use_mambapy and self.training) or not is_prefill or _needs_grad(self, input_states):
             _STATE["fallback_calls"] += 1
             return orig(self, input_states, *args, **kwargs)
@@ -179,5 +215,6 @@ def unpatch():
 def stats():
     """Engagement counters."""
     return {"fast_calls": _STATE["fast_calls"], "fallback_calls": _STATE["fallback_calls"],
+            "decode_calls": _STATE["decode_calls"],
             "kernel_calls": kernel_calls(), "patched": _STATE["orig"] is not None,
             "api": _STATE["api"]}

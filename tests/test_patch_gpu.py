@@ -30,10 +30,13 @@ def test_patched_logits_and_generation_match_unpatched():
     try:
         assert targets
         before = arm.stats()["fast_calls"]
+        dec_before = arm.stats()["decode_calls"]
         with torch.no_grad():
             got = model(ids).logits
             got_gen = model.generate(ids[:1, :20], max_new_tokens=8, do_sample=False)
         assert arm.stats()["fast_calls"] - before >= 3 * 2  # every layer, both calls
+        # generate's 7 single-token steps run through selective_state_update
+        assert arm.stats()["decode_calls"] - dec_before == 3 * 7
         rel = (got - want).abs().max() / want.abs().max()
         assert rel < 1e-4, rel
         assert torch.equal(got_gen, want_gen)
