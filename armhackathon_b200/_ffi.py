@@ -100,6 +100,9 @@ def _bind(lib):
               "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
               "arm_scan_tensor_status"):
         getattr(lib, f).restype = ctypes.c_int
+    lib.arm_scan_selective_scan_final_state_f32_async.restype = ctypes.c_int
+    lib.arm_scan_selective_scan_final_state_f32_async.argtypes = [
+        ctypes.POINTER(ArmScanDims), *([_VP] * 6), ctypes.c_int, ctypes.c_int, _VP, _VP, _VP]
     lib.arm_scan_selective_state_update_f32_async.restype = ctypes.c_int
     lib.arm_scan_selective_state_update_f32_async.argtypes = [
         ctypes.POINTER(ArmScanDims), *([_VP] * 9), ctypes.c_int, _VP, _VP]
@@ -222,6 +225,15 @@ def angles_async_raw(dims, ptr_angles, n_angles, ptr_dt, ptr_cos, ptr_sin, ptr_w
         _n(stream)), "arm_scan_mamba3_angles_f32_async")
 
 
+def final_state_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_delta_bias, softplus,
+                    reverse, ptr_h0, ptr_last, stream):
+    """Final state of a Mamba-1 scan without outputs (device pointers)."""
+    _check(load().arm_scan_selective_scan_final_state_f32_async(
+        ctypes.byref(dims), ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, _n(ptr_delta_bias),
+        int(softplus), int(reverse), _n(ptr_h0), ptr_last, _n(stream)),
+        "arm_scan_selective_scan_final_state_f32_async")
+
+
 def state_update_raw(dims, ptr_state, ptr_x, ptr_dt, ptr_a, ptr_b, ptr_c, ptr_d_skip, ptr_z,
                      ptr_dt_bias, dt_softplus, ptr_out, stream):
     """One Mamba-1 decode step (device pointers, stream-ordered)."""
@@ -252,7 +264,8 @@ def exported_symbols():
             "arm_scan_mamba3_angles_workspace_bytes", "arm_scan_mamba3_angles_f32_async",
             "arm_scan_mamba3_angles_f32_noalloc", "arm_scan_tensor_status",
             "arm_scan_mamba3_siso_tc_async", "arm_scan_kernel_launches",
-            "arm_scan_selective_state_update_f32_async"]
+            "arm_scan_selective_state_update_f32_async",
+            "arm_scan_selective_scan_final_state_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

@@ -633,6 +633,29 @@ int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const fl
 
 int arm_scan_tensor_status(void) { return tensor_status_code(); }
 
+int arm_scan_selective_scan_final_state_f32_async(const ArmScanDims* dims, const float* u,
+                                                  const float* delta, const float* a,
+                                                  const float* b, const float* c,
+                                                  const float* delta_bias, int delta_softplus,
+                                                  int reverse, const float* h0,
+                                                  float* last_state, void* stream) {
+    if (!dims || !u || !delta || !a || !b || !c || !last_state)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    M1Counts cnt;
+    int rc = m1_validate(dims, &cnt);
+    if (rc) return rc;
+    if (dims->state > 16)
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE, "the final-state entry covers d_state <= 16");
+    std::vector<void*> p = {const_cast<float*>(u), const_cast<float*>(delta), const_cast<float*>(a),
+                            const_cast<float*>(b), const_cast<float*>(c),     nullptr,
+                            nullptr,               const_cast<float*>(delta_bias)};
+    M1Params m = m1_params(dims, p, delta_softplus, reverse);
+    m.h0 = h0;
+    m.last_state = last_state;
+    cudaError_t e = m1_final_state_launch(m, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "final-state launch");
+}
+
 int arm_scan_selective_state_update_f32_async(const ArmScanDims* dims, float* state,
                                               const float* x, const float* dt, const float* a,
                                               const float* b, const float* c,

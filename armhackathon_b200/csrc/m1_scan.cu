@@ -450,6 +450,17 @@ cudaError_t m1_timesplit_launch(const M1Params& p, int S, cudaStream_t stream) {
     return e != cudaSuccess ? e : ef;
 }
 
+cudaError_t m1_final_state_launch(const M1Params& p, cudaStream_t stream) {
+    M1Params q = p;
+    q.out = nullptr;
+    q.z = nullptr;
+    q.d_skip = nullptr;
+    const int S = m1_seg2_segments(q);
+    if (S > 0) return m1_seg2_launch(q, S, stream);
+    const bool tile_ok = q.state <= 16 && q.len <= (INT32_MAX / 4) && q.state * q.len <= INT32_MAX;
+    return tile_ok ? m1_tile_launch(q, 1, stream) : cudaErrorNotSupported;
+}
+
 cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) {
     if (backend == kBackendSequential) {
         const int64_t BD = p.batch * p.dim;

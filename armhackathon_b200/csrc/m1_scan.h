@@ -38,6 +38,10 @@ bool m1_pointers_aligned16(const M1Params& p);
 // Per-device stream-ordered memory pool for kernel workspaces; keeps what it
 // has reserved (defined in m3_tc.cu).
 cudaError_t device_workspace_pool(cudaMemPool_t* out);
+// Final state only (no outputs): the two-pass kernel's first pass and
+// carries, or the tile kernel in its state-only mode.  cudaErrorNotSupported
+// for d_state > 16.
+cudaError_t m1_final_state_launch(const M1Params& p, cudaStream_t stream);
 // Single-token state update (m1_decode.cu): p.u = x (batch, dim), p.delta =
 // dt (batch, dim), p.B/p.C (batch, groups, state), p.out (batch, dim);
 // state (batch, dim, state) is read and updated in place.

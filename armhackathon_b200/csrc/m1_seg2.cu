@@ -268,7 +268,7 @@ cudaError_t m1_seg2_launch(const M1Params& p, int S, cudaStream_t stream) {
         note_launch();
         e = cudaGetLastError();
     }
-    if (e == cudaSuccess) {
+    if (e == cudaSuccess && p.out) {  // out == nullptr: final state only
         k2<<<grid, kS2Rows, 0, stream>>>(p, ws, S, Ls);
         note_launch();
         e = cudaGetLastError();

@@ -233,3 +233,43 @@ def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None,
     opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
     return _state_update_op(state, _prep(x, dev), _prep(dt, dev), _prep(A, dev), _prep(B, dev),
                             _prep(C, dev), opt(D), opt(z), opt(dt_bias), bool(dt_softplus))
+
+
+@torch.library.custom_op("arm_scan::selective_scan_final_state", mutates_args=())
+def _final_state_op(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
+                    C: torch.Tensor, delta_bias: Optional[torch.Tensor],
+                    initial_state: Optional[torch.Tensor], delta_softplus: bool,
+                    reverse: bool) -> torch.Tensor:
+    batch, dim, length = u.shape
+    state, groups = A.shape[1], B.shape[1]
+    dims = _ffi.ArmScanDims(batch, dim, length, state, groups)
+    last = u.new_empty((batch, dim, state))
+    with _on_device(u):
+        _ffi.final_state_raw(dims, u.data_ptr(), delta.data_ptr(), A.data_ptr(), B.data_ptr(),
+                             C.data_ptr(), _ptr(delta_bias), delta_softplus, reverse,
+                             _ptr(initial_state), last.data_ptr(), _stream(u))
+    _CALLS["n"] += 1
+    return last
+
+
+@_final_state_op.register_fake
+def _(u, delta, A, B, C, delta_bias, initial_state, delta_softplus, reverse):
+    return u.new_empty((u.shape[0], u.shape[1], A.shape[1]))
+
+
+def selective_scan_final_state(u, delta, A, B, C, delta_bias=None, delta_softplus=False,
+                               initial_state=None, reverse=False):
+    """The ``last_state`` of ``selective_scan`` with the same arguments,
+    without computing the outputs (d_state <= 16).  The first step of a
+    sequence-parallel scan; CUDA tensors only."""
+    if u.device.type != "cuda":
+        raise ValueError("selective_scan_final_state runs on CUDA tensors")
+    batch, dim, length = u.shape
+    state = A.shape[1]
+    dev = u.device
+    B = _bc4(B, batch, state, length)
+    C = _bc4(C, batch, state, length)
+    opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
+    return _final_state_op(_prep(u, dev), _prep(delta, dev), _prep(A, dev), _prep(B, dev),
+                           _prep(C, dev), opt(delta_bias), opt(initial_state),
+                           bool(delta_softplus), bool(reverse))

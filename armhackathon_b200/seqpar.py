@@ -8,13 +8,13 @@ prod_t exp(dt_t * A_n) = exp(A_n * sum_t dt_t).  So a segment is summarised by
 batch*dim*(state+1)*4 bytes per direction (~100 KB at dim 1536, state 16).
 
 Per call:
-  1. each rank scans its segment forward and backward from zero, keeping the
-     final states and sum(dt) per row;
+  1. each rank computes the final states of its segment, forward and
+     backward from zero, without outputs (selective_scan_final_state), and
+     sum(dt) per row;
   2. one all_gather of those summaries (the only collective);
   3. rank r folds the summaries of ranks < r (forward) and > r (backward)
      into its incoming states;
-  4. rank r rescans its segment from those states (ranks at the sequence ends
-     keep the pass-1 output of the direction that starts at them).
+  4. rank r scans its segment in both directions from those states.
 The fold is exact algebra, so the result equals the unsplit bidirectional
 scan up to fp32 rounding.  No rank waits on another except inside the
 all_gather, whose timeout is the process group's.
@@ -49,25 +49,28 @@ def fold_carries(h_ends, dt_sums, A, rank, reverse):
 
 
 def bidirectional_scan_seqpar(u, delta, A, B, C, D=None, z=None, delta_bias=None,
-                              delta_softplus=False, merge="sum", group=None, scan_fn=None):
+                              delta_softplus=False, merge="sum", group=None, scan_fn=None,
+                              state_fn=None):
     """Bidirectional scan of one sequence split over the ranks of ``group``.
 
     Every rank passes its own segment (same layouts as ``selective_scan``:
     u, delta, z (batch, dim, L_rank); B, C (batch, [groups,] state, L_rank);
     A (dim, state); D, delta_bias (dim,)).  Returns this rank's segment of the
-    merged output ("sum") or (fwd, bwd) ("none").  ``scan_fn`` defaults to
-    this package's ``selective_scan``; tests substitute a CPU reference.
+    merged output ("sum") or (fwd, bwd) ("none").  ``scan_fn`` and
+    ``state_fn`` default to this package's ``selective_scan`` and
+    ``selective_scan_final_state``; tests substitute CPU references.
     """
     if merge not in ("sum", "none"):
         raise ValueError(f"merge must be 'sum' or 'none', got {merge!r}")
     if scan_fn is None:
         from .op import selective_scan as scan_fn
+    if state_fn is None:
+        from .op import selective_scan_final_state as state_fn
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    kw = dict(D=D, z=z, delta_bias=delta_bias, delta_softplus=delta_softplus,
-              return_last_state=True)
-    yf, hf = scan_fn(u, delta, A, B, C, **kw)
-    yb, hb = scan_fn(u, delta, A, B, C, reverse=True, **kw)
+    skw = dict(delta_bias=delta_bias, delta_softplus=delta_softplus)
+    hf = state_fn(u, delta, A, B, C, **skw)
+    hb = state_fn(u, delta, A, B, C, reverse=True, **skw)
     sdt = _segment_dt_sum(delta, delta_bias, delta_softplus).to(hf.dtype)
     packed = torch.cat([hf, hb, sdt[..., None]], dim=-1).contiguous()
     parts = [torch.empty_like(packed) for _ in range(world)]
@@ -76,11 +79,9 @@ def bidirectional_scan_seqpar(u, delta, A, B, C, D=None, z=None, delta_bias=None
     h_f = [p[..., :N] for p in parts]
     h_b = [p[..., N:2 * N] for p in parts]
     sums = [p[..., 2 * N] for p in parts]
-    kw.pop("return_last_state")
-    if rank > 0:
-        yf = scan_fn(u, delta, A, B, C, initial_state=fold_carries(h_f, sums, A, rank, False),
-                     **kw)
-    if rank < world - 1:
-        yb = scan_fn(u, delta, A, B, C, reverse=True,
-                     initial_state=fold_carries(h_b, sums, A, rank, True), **kw)
+    kw = dict(D=D, z=z, **skw)
+    h_in_f = fold_carries(h_f, sums, A, rank, False) if rank > 0 else None
+    h_in_b = fold_carries(h_b, sums, A, rank, True) if rank < world - 1 else None
+    yf = scan_fn(u, delta, A, B, C, initial_state=h_in_f, **kw)
+    yb = scan_fn(u, delta, A, B, C, reverse=True, initial_state=h_in_b, **kw)
     return yf + yb if merge == "sum" else (yf, yb)

@@ -212,6 +212,19 @@ int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOp
                                   const void* z, int reverse, void* out, float* last_state,
                                   float* last_bx, void* stream);
 
+/* Extension (no counterpart in the reference): the final state of
+ * arm_scan_selective_scan_f32_async's recurrence without computing the
+ * outputs (D, z and out play no part): the first step of a sequence-parallel
+ * scan, whose ranks exchange end states before scanning from them.
+ * last_state (batch, dim, state) is required; h0 is nullable.  d_state must
+ * be <= 16 (else code 3).  Device pointers, stream-ordered. */
+int arm_scan_selective_scan_final_state_f32_async(const ArmScanDims* dims, const float* u,
+                                                  const float* delta, const float* a,
+                                                  const float* b, const float* c,
+                                                  const float* delta_bias, int delta_softplus,
+                                                  int reverse, const float* h0,
+                                                  float* last_state, void* stream);
+
 /* Extension (no counterpart in the reference; mamba_ssm's
  * selective_state_update): one decode step of the Mamba-1 recurrence for
  * every (batch, channel), updating `state` (batch, dim, state) in place:

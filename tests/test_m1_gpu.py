@@ -334,3 +334,21 @@ def test_decode_steps_equal_the_scan(groups):
     y = torch.stack(ys, dim=-1)
     assert rel_err(y.cpu().numpy(), want) <= REL_TOL
     assert rel_err(state.cpu().numpy(), want_last) <= REL_TOL
+
+
+@pytest.mark.parametrize("shape", [(2, 40, 2048, 16, 1), (1, 34, 1001, 13, 2)])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_final_state_entry_equals_scan_last_state(shape, reverse):
+    """selective_scan_final_state (no outputs: the two-pass kernel's first
+    pass and carries, or the tile kernel's state-only mode) returns the scan's
+    last_state."""
+    B, D, L, N, G = shape
+    x = random_case(B, D, L, N, G, seed=L)
+    h0 = torch.from_numpy(np.random.default_rng(3).standard_normal((B, D, N)).astype(np.float32))
+    c = cuda(x)
+    _, want = arm().selective_scan(**c, reverse=reverse, initial_state=h0.cuda(),
+                                   return_last_state=True)
+    got = arm().selective_scan_final_state(c["u"], c["delta"], c["A"], c["B"], c["C"],
+                                           delta_bias=c["delta_bias"], delta_softplus=True,
+                                           initial_state=h0.cuda(), reverse=reverse)
+    assert rel_err(got.cpu().numpy(), want.cpu().numpy()) <= 1e-5

@@ -24,6 +24,12 @@ def _oracle_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
     return (out, last) if return_last_state else out
 
 
+def _oracle_state(u, delta, A, B, C, delta_bias=None, delta_softplus=False, reverse=False,
+                  initial_state=None):
+    return _oracle_scan(u, delta, A, B, C, delta_bias=delta_bias, delta_softplus=delta_softplus,
+                        reverse=reverse, initial_state=initial_state, return_last_state=True)[1]
+
+
 def _case(L):
     rng = np.random.default_rng(0)
     Bsz, Dd, N = 2, 5, 16
@@ -47,7 +53,7 @@ def _worker(rank, world, port, L, q):
     sl = slice(cuts[rank], cuts[rank + 1])
     tv = ("u", "delta", "B", "C", "z")
     mine = {k: (v[..., sl].contiguous() if k in tv else v) for k, v in x.items()}
-    got = bidirectional_scan_seqpar(**mine, scan_fn=_oracle_scan)
+    got = bidirectional_scan_seqpar(**mine, scan_fn=_oracle_scan, state_fn=_oracle_state)
     full = _oracle_scan(**x) + _oracle_scan(**x, reverse=True)
     err = float((got - full[..., sl]).abs().max() / full.abs().max())
     q.put((rank, err))
