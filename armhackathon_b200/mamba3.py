@@ -184,6 +184,10 @@ def _mamba3_tc_angles(q, k, v, adt, dt, trap, q_bias, k_bias, angles, D, z, reve
         raise ValueError(f"angles must be (b, l, h, r) or (b, l, 1, r), got {tuple(angles.shape)}")
     if angles.shape[3] > dqk // 2:
         raise ValueError(f"angles has {angles.shape[3]} pairs, more than dqk/2 = {dqk // 2}")
+    if angles.shape[2] > 1 and angles.stride(2) == 0:
+        # a head-broadcast view (angles.expand over heads): pass the one row
+        # per (b, l) instead of materialising a copy per head
+        angles = angles[:, :, :1, :]
     home = v.device
     dev = home if home.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
     io = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32

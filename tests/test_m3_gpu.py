@@ -369,3 +369,18 @@ def test_tensor_core_mimo_vs_oracle(R, shape):
         _ffi.tensor_status()
         assert rel_err(out.cpu().numpy(), want) <= BF16_TOL
         assert rel_err(st.cpu().numpy(), wst) <= BF16_TOL
+
+
+def test_tensor_core_expanded_angles_view_is_shared():
+    """Angles given as a head-broadcast view (b, l, 1, r).expand(b, l, h, r),
+    as a Mamba-3 LM block passes them, give the same result as the explicit
+    per-head copy."""
+    b, l, h, r = 2, 300, 4, 64
+    x = random_siso(b, l, h, 64, 128, r, seed=21)
+    c = {k: v.cuda() for k, v in x.items()}
+    row = c["angles"][:, :, :1, :]
+    c["angles"] = row.expand(b, l, h, r)
+    got = arm().mamba3_scan(**c, precision="bf16")
+    c["angles"] = row.expand(b, l, h, r).contiguous()
+    want = arm().mamba3_scan(**c, precision="bf16")
+    assert torch.equal(got, want)
