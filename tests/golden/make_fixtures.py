@@ -35,6 +35,7 @@ Usage:  python tests/golden/make_fixtures.py [--ref /path/to/reference]
 
 import argparse
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -176,9 +177,11 @@ def make_m3(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference",
-                    help="reference checkout (read-only)")
+    ap.add_argument("--ref", default=os.environ.get("ARM_SCAN_REFERENCE"),
+                    help="reference checkout, read-only (default: $ARM_SCAN_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("pass --ref or set ARM_SCAN_REFERENCE to the reference checkout")
     ref = Path(args.ref)
     index = {
         "source": "AdityaP9116/ARMHackathon tests/golden (+ its Python oracles)",
