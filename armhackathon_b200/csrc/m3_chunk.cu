@@ -138,9 +138,9 @@ __device__ __forceinline__ void ck_gates(const M3Params& p, int64_t bh, int64_t 
 }
 
 // A2. rotated q (WITH_Q), k into q^T, k^T (WITH_QT) and w*k rows (WITH_KW),
-// and x rows.
+// and x rows.  Element-by-element form (any alignment).
 template <int R, bool WITH_QT, bool WITH_KW>
-__device__ __forceinline__ void ck_stage(const M3Params& p, const CkLayout& ly, int64_t bi,
+__device__ __forceinline__ void ck_stage_scalar(const M3Params& p, const CkLayout& ly, int64_t bi,
                                          int64_t h, int64_t it0, const CkSmem& s) {
     constexpr int QS = kQR / R;
     const int tid = threadIdx.x;
@@ -196,6 +196,115 @@ __device__ __forceinline__ void ck_stage(const M3Params& p, const CkLayout& ly, 
         }
         s.xs[i * ly.PP4 + pp] = v;
     }
+}
+
+__host__ __device__ inline bool ck_aligned16(const void* q) {
+    return (reinterpret_cast<uintptr_t>(q) & 15u) == 0;
+}
+// whether the vector form of A2 applies (dims and 16-byte alignment)
+__host__ __device__ inline bool ck_vec_ok(const M3Params& p) {
+    return p.dqk % 8 == 0 && p.dv % 4 == 0 && ck_aligned16(p.q) && ck_aligned16(p.k) &&
+           ck_aligned16(p.cos) && ck_aligned16(p.sin) && ck_aligned16(p.q_bias) &&
+           ck_aligned16(p.k_bias) && ck_aligned16(p.v) && (p.psi == nullptr || ck_aligned16(p.psi));
+}
+
+// A2, vector form (16-byte aligned q, k, cos, sin, biases, v): one item =
+// one row x 4 rotation pairs, read with 16-byte loads (interleaved SISO: 8
+// consecutive dims; MIMO split halves: 4 dims of each half).  Rows vary
+// fastest across threads, so the transposed q^T / k^T stores are
+// conflict-free and a warp's loads cover whole 32-byte sectors.
+template <int R, bool WITH_QT, bool WITH_KW>
+__device__ __forceinline__ void ck_stage_vec(const M3Params& p, const CkLayout& ly, int64_t bi,
+                                             int64_t h, int64_t it0, const CkSmem& s) {
+    constexpr int QS = kQR / R;
+    const int tid = threadIdx.x;
+    const int64_t H = p.heads, L = p.len;
+    const int N = ly.N, P = ly.P, half = N / 2;
+    const bool mimo = R > 1 || p.psi != nullptr;
+    const int n_chunks = half / 4;
+    for (int idx = tid; idx < kQR * n_chunks; idx += kCkThreads) {
+        const int i = idx % kQR, c = idx / kQR;
+        const int j = i / R, r = i - (i / R) * R;  // step, rank
+        const int64_t it = it0 + j;
+        // dims of the 4 pairs: lo[e] rotates with hi[e]
+        const int d_lo = mimo ? 4 * c : 8 * c;
+        float qlo[4] = {0.f, 0.f, 0.f, 0.f}, qhi[4] = {0.f, 0.f, 0.f, 0.f};
+        float klo[4] = {0.f, 0.f, 0.f, 0.f}, khi[4] = {0.f, 0.f, 0.f, 0.f};
+        if (j < QS && it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            const int64_t qk_off = (bi * L + t) * (mimo ? R : 1) * N + r * N;
+            const int64_t bo = (h * (mimo ? R : 1) + r) * N;
+            const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cos + ((bi * L + t) * H + h) * half + 4 * c));
+            const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sin + ((bi * L + t) * H + h) * half + 4 * c));
+            const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+            auto rot = [&](const float* src, const float* bias, float (&lo)[4], float (&hi)[4]) {
+                float a[4], b[4];
+                if (mimo) {
+                    const float4 x0 = __ldg(reinterpret_cast<const float4*>(src + d_lo));
+                    const float4 x1 = __ldg(reinterpret_cast<const float4*>(src + d_lo + half));
+                    const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + d_lo));
+                    const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + d_lo + half));
+                    a[0] = x0.x + b0.x; a[1] = x0.y + b0.y; a[2] = x0.z + b0.z; a[3] = x0.w + b0.w;
+                    b[0] = x1.x + b1.x; b[1] = x1.y + b1.y; b[2] = x1.z + b1.z; b[3] = x1.w + b1.w;
+                } else {
+                    const float4 x0 = __ldg(reinterpret_cast<const float4*>(src + d_lo));
+                    const float4 x1 = __ldg(reinterpret_cast<const float4*>(src + d_lo + 4));
+                    const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + d_lo));
+                    const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + d_lo + 4));
+                    a[0] = x0.x + b0.x; b[0] = x0.y + b0.y; a[1] = x0.z + b0.z; b[1] = x0.w + b0.w;
+                    a[2] = x1.x + b1.x; b[2] = x1.y + b1.y; a[3] = x1.z + b1.z; b[3] = x1.w + b1.w;
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    lo[e] = a[e] * cc[e] - b[e] * ss[e];
+                    hi[e] = a[e] * ss[e] + b[e] * cc[e];
+                }
+            };
+            if (WITH_QT) rot(p.q + qk_off, p.q_bias + bo, qlo, qhi);
+            rot(p.k + qk_off, p.k_bias + bo, klo, khi);
+        }
+        const float w = (WITH_KW && j < QS) ? s.wdec[j] : 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int i0 = mimo ? d_lo + e : d_lo + 2 * e;
+            const int i1 = mimo ? d_lo + e + half : d_lo + 2 * e + 1;
+            if (WITH_QT) {
+                s.qT[i0 * ly.QP4 + i] = qlo[e];
+                s.qT[i1 * ly.QP4 + i] = qhi[e];
+                s.kT[i0 * ly.QP4 + i] = klo[e];
+                s.kT[i1 * ly.QP4 + i] = khi[e];
+            }
+            if (WITH_KW) {
+                s.kw[i * ly.NP4 + i0] = w * klo[e];
+                s.kw[i * ly.NP4 + i1] = w * khi[e];
+            }
+        }
+    }
+    // x rows: 4 channels per item, rows fastest
+    for (int idx = tid; idx < kQR * (P / 4); idx += kCkThreads) {
+        const int i = idx % kQR, c = idx / kQR;
+        const int j = i / R, r = i - (i / R) * R;
+        const int64_t it = it0 + j;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < QS && it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            v = __ldg(reinterpret_cast<const float4*>(p.v + ((bi * L + t) * H + h) * P + 4 * c));
+            if (mimo) {
+                const float4 ps = __ldg(reinterpret_cast<const float4*>(p.psi + (h * R + r) * P + 4 * c));
+                v.x *= ps.x; v.y *= ps.y; v.z *= ps.z; v.w *= ps.w;
+            }
+        }
+        *reinterpret_cast<float4*>(s.xs + i * ly.PP4 + 4 * c) = v;
+    }
+}
+
+template <int R, bool WITH_QT, bool WITH_KW>
+__device__ __forceinline__ void ck_stage(const M3Params& p, const CkLayout& ly, int64_t bi,
+                                         int64_t h, int64_t it0, const CkSmem& s, bool vec) {
+    if (vec)
+        ck_stage_vec<R, WITH_QT, WITH_KW>(p, ly, bi, h, it0, s);
+    else
+        ck_stage_scalar<R, WITH_QT, WITH_KW>(p, ly, bi, h, it0, s);
 }
 
 // B. W^T[j][i] = mask(t_i, t_j) * (q_i . k_j); 4x4 tiles
@@ -341,6 +450,7 @@ __device__ __forceinline__ void ck_last_bx(const M3Params& p, const CkLayout& ly
 // memory.
 template <int R>
 __global__ void __launch_bounds__(kCkThreads, 1) m3_chunk_kernel(M3Params p) {
+    const bool vec = ck_vec_ok(p);
     constexpr int QS = kQR / R;
     extern __shared__ float4 smem4[];
     const CkLayout ly(static_cast<int>(p.dqk), static_cast<int>(p.dv));
@@ -356,7 +466,7 @@ __global__ void __launch_bounds__(kCkThreads, 1) m3_chunk_kernel(M3Params p) {
         const int64_t it0 = static_cast<int64_t>(ch) * QS;  // first traversal index
         if (warp == 0) ck_gates<R>(p, bh, it0, s);
         __syncthreads();
-        ck_stage<R, true, true>(p, ly, bi, h, it0, s);
+        ck_stage<R, true, true>(p, ly, bi, h, it0, s, vec);
         __syncthreads();
         ck_w<R>(ly, s);
         __syncthreads();
@@ -402,6 +512,7 @@ struct CkWs {
 
 template <int R>
 __global__ void __launch_bounds__(kCkThreads) m3_chunk_ds_kernel(M3Params p, CkWs ws, int n_chunks) {
+    const bool vec = ck_vec_ok(p);
     constexpr int QS = kQR / R;
     extern __shared__ float4 smem4[];
     const CkLayout ly(static_cast<int>(p.dqk), static_cast<int>(p.dv), kCkDs);
@@ -415,7 +526,7 @@ __global__ void __launch_bounds__(kCkThreads) m3_chunk_ds_kernel(M3Params p, CkW
     if (warp == 0) ck_gates<R>(p, bh, it0, s);
     __syncthreads();
     if (tid == 0) ws.decay[bh * n_chunks + ch] = s.eQ[0];
-    ck_stage<R, false, true>(p, ly, bi, h, it0, s);
+    ck_stage<R, false, true>(p, ly, bi, h, it0, s, vec);
     __syncthreads();
     float* out = ws.st + (bh * n_chunks + ch) * static_cast<int64_t>(N) * P;
     for (int tile = tid; tile < (N / 8) * (P / 4); tile += kCkThreads) {
@@ -466,6 +577,7 @@ __global__ void __launch_bounds__(kCkThreads) m3_chunk_state_kernel(M3Params p, 
 
 template <int R>
 __global__ void __launch_bounds__(kCkThreads) m3_chunk_out_kernel(M3Params p, CkWs ws, int n_chunks) {
+    const bool vec = ck_vec_ok(p);
     constexpr int QS = kQR / R;
     extern __shared__ float4 smem4[];
     const CkLayout ly(static_cast<int>(p.dqk), static_cast<int>(p.dv), kCkOut);
@@ -484,7 +596,7 @@ __global__ void __launch_bounds__(kCkThreads) m3_chunk_out_kernel(M3Params p, Ck
         }
     }
     __syncthreads();
-    ck_stage<R, true, false>(p, ly, bi, h, it0, s);
+    ck_stage<R, true, false>(p, ly, bi, h, it0, s, vec);
     __syncthreads();
     ck_w<R>(ly, s);
     __syncthreads();

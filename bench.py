@@ -222,6 +222,24 @@ def profiled_traffic(workload):
     return int(m.group(1)) if m else None
 
 
+def mufu_roofline(w, k_ms, clocks):
+    """The Mamba-1 scan's binding unit: one exp per (batch, channel, step,
+    state) is the algorithm's minimum (the reference computes exactly that);
+    the MUFU pipe issues 16 of them per clock per SM (nominal), taken at the
+    SM clock sampled during the timed region."""
+    import torch
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
+    exps = w["batch"] * w["dim"] * w["len"] * w["state"]
+    achieved = exps / (k_ms * 1e-3) / 1e9
+    peak = 16 * sms * mhz * 1e6 / 1e9
+    return {"bound": "mufu", "achieved": achieved, "peak": peak, "unit": "Gexp/s",
+            "frac": achieved / peak, "peak_source": "nominal 16/clk/SM x sampled SM clock",
+            "executed_per_algorithmic": 2.0,
+            "note": "the default two-pass kernel computes every exp twice (segment end states, "
+                    "then outputs), plus the softplus/silu exps per (row, step)"}
+
+
 def algorithmic_bytes(w):
     B, D, L, N = w["batch"], w["dim"], w["len"], w["state"]
     return 4 * (4 * B * D * L + 2 * B * N * L + D * N + 2 * D + B * D * N)
@@ -562,6 +580,7 @@ def main():
             "e2e": e2e,
             "clocks": clk.summary(),
         }
+        line["mufu"] = mufu_roofline(w, k_ms, line["clocks"])
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w)
         if not args.no_prefill:
