@@ -384,3 +384,22 @@ def test_tensor_core_expanded_angles_view_is_shared():
     c["angles"] = row.expand(b, l, h, r).contiguous()
     want = arm().mamba3_scan(**c, precision="bf16")
     assert torch.equal(got, want)
+
+
+def test_chunk_kernel_unaligned_q_k_take_scalar_staging():
+    """q, k that are not 16-byte aligned (a view one element into its
+    storage) run the chunk kernels' element-by-element staging; same result."""
+    x = random_siso(2, 300, 3, 64, 128, 64, seed=13)
+    cos, sin = oracle.angles_to_cos_sin(x["angles"].numpy(), x["dt"].numpy(), 64)
+    want = oracle.m3_siso(x["q"], x["k"], x["v"], x["adt"], x["dt"], x["trap"], x["q_bias"],
+                          x["k_bias"], cos, sin, D=x["D"], z=x["z"], nthreads=8)
+    c = {k: v.cuda() for k, v in x.items()}
+    for name in ("q", "k"):
+        t = c[name]
+        buf = torch.empty(t.numel() + 1, device="cuda")
+        shifted = buf[1:].view(t.shape)
+        shifted.copy_(t)
+        assert shifted.data_ptr() % 16 != 0
+        c[name] = shifted
+    out = arm().mamba3_scan(**c)
+    assert rel_err(out.cpu().numpy(), want) <= REL_TOL
