@@ -100,6 +100,10 @@ def _bind(lib):
               "arm_scan_mamba3_scan_f32", "arm_scan_mamba3_scan_f32_async",
               "arm_scan_tensor_status"):
         getattr(lib, f).restype = ctypes.c_int
+    lib.arm_scan_mamba3_ss2d_f32_async.restype = ctypes.c_int
+    lib.arm_scan_mamba3_ss2d_f32_async.argtypes = [
+        ctypes.POINTER(ArmMamba3Dims), ctypes.c_size_t, *([_VP] * 9), ctypes.c_size_t,
+        _VP, _VP, _VP, _VP]
     lib.arm_scan_selective_scan_final_state_f32_async.restype = ctypes.c_int
     lib.arm_scan_selective_scan_final_state_f32_async.argtypes = [
         ctypes.POINTER(ArmScanDims), *([_VP] * 6), ctypes.c_int, ctypes.c_int, _VP, _VP, _VP]
@@ -225,6 +229,14 @@ def angles_async_raw(dims, ptr_angles, n_angles, ptr_dt, ptr_cos, ptr_sin, ptr_w
         _n(stream)), "arm_scan_mamba3_angles_f32_async")
 
 
+def ss2d_mamba3_raw(dims, grid_w, ptrs, n_angles, ptr_d_skip, ptr_z, ptr_out, stream):
+    """Four-direction Mamba-3 SISO cross-scan of a row-major token grid.
+    ``ptrs``: q, k, v, adt, dt, trap, q_bias, k_bias, angles."""
+    _check(load().arm_scan_mamba3_ss2d_f32_async(
+        ctypes.byref(dims), int(grid_w), *[_n(p) for p in ptrs], int(n_angles),
+        _n(ptr_d_skip), _n(ptr_z), ptr_out, _n(stream)), "arm_scan_mamba3_ss2d_f32_async")
+
+
 def final_state_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_delta_bias, softplus,
                     reverse, ptr_h0, ptr_last, stream):
     """Final state of a Mamba-1 scan without outputs (device pointers)."""
@@ -265,7 +277,7 @@ def exported_symbols():
             "arm_scan_mamba3_angles_f32_noalloc", "arm_scan_tensor_status",
             "arm_scan_mamba3_siso_tc_async", "arm_scan_kernel_launches",
             "arm_scan_selective_state_update_f32_async",
-            "arm_scan_selective_scan_final_state_f32_async"]
+            "arm_scan_selective_scan_final_state_f32_async", "arm_scan_mamba3_ss2d_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

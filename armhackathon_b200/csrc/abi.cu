@@ -799,6 +799,75 @@ int arm_scan_mamba3_angles_f32_async(const ArmMamba3Dims* dims, const float* ang
     return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "angle pre-pass launch");
 }
 
+int arm_scan_mamba3_ss2d_f32_async(const ArmMamba3Dims* dims, size_t grid_w, const float* q,
+                                   const float* k, const float* v, const float* adt,
+                                   const float* dt, const float* trap, const float* q_bias,
+                                   const float* k_bias, const float* angles, size_t n_angles,
+                                   const float* d_skip, const float* z, float* out, void* stream) {
+    const void* req[] = {dims, q, k, v, adt, dt, trap, q_bias, k_bias, angles, out};
+    bool mimo = false;
+    int rc = m3_check_ptrs(req, 11, nullptr, nullptr, nullptr, nullptr, nullptr, &mimo);
+    if (rc) return rc;
+    M3Counts cnt;
+    if ((rc = m3_validate(dims, false, nullptr, nullptr, &cnt))) return rc;
+    if (dims->rank != 1) return fail(ARM_SCAN_ERR_INVALID_DIMS, "the SS2D entry is SISO (rank 1)");
+    if (!grid_w || dims->len % grid_w)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "len (%zu) must be a multiple of grid_w (%zu)",
+                    dims->len, grid_w);
+    if (!n_angles || n_angles > dims->dqk / 2)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "n_angles (%zu) must be in [1, dqk/2]", n_angles);
+    if (dims->batch * dims->heads > 65535)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "batch*heads above 65535");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    std::vector<void*> p = {const_cast<float*>(q),      const_cast<float*>(k),
+                            const_cast<float*>(v),      const_cast<float*>(adt),
+                            const_cast<float*>(dt),     const_cast<float*>(trap),
+                            const_cast<float*>(q_bias), const_cast<float*>(k_bias),
+                            nullptr,                    nullptr,
+                            const_cast<float*>(d_skip), const_cast<float*>(z),
+                            nullptr,                    nullptr,
+                            nullptr,                    out,
+                            nullptr,                    nullptr};
+    M3Params base = m3_params(dims, p, 0);
+    base.grid_w = static_cast<int64_t>(grid_w);
+    base.out_blh = 1;
+    base.out_acc = 1;
+    if (!m3_chunk_applicable(base))
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE,
+                    "the SS2D entry covers dv <= 128, dqk <= 128 with 16-byte aligned v, z, out");
+    const size_t cs = cnt.blhr;  // floats of one cos (or sin) array
+    const size_t ws_angle = arm_scan_mamba3_angles_workspace_bytes(dims, n_angles);
+    cudaMemPool_t pool = nullptr;
+    cudaError_t e = device_workspace_pool(&pool);
+    if (e != cudaSuccess) return cuda_fail(e, "workspace pool");
+    void* raw = nullptr;
+    e = cudaMallocFromPoolAsync(&raw, 4 * cs * sizeof(float) + ws_angle + 256, pool, s);
+    if (e != cudaSuccess) return cuda_fail(e, "workspace");
+    float* trig = static_cast<float*>(raw);  // [ordering][cos, sin]
+    float* angle_ws = trig + 4 * cs;
+    e = cudaMemsetAsync(out, 0, cnt.blhv * sizeof(float), s);
+    for (int col = 0; col < 2 && e == cudaSuccess; ++col) {
+        float* cosv = trig + (2 * col) * cs;
+        float* sinv = cosv + cs;
+        AngleParams a{angles, dt, cosv, sinv, static_cast<int64_t>(dims->batch),
+                      static_cast<int64_t>(dims->heads), static_cast<int64_t>(dims->len),
+                      static_cast<int64_t>(n_angles), static_cast<int64_t>(dims->dqk / 2),
+                      static_cast<int64_t>(grid_w), col};
+        e = angle_launch(a, angle_ws, s);
+        for (int rev = 0; rev < 2 && e == cudaSuccess; ++rev) {
+            M3Params m = base;
+            m.cos = cosv;
+            m.sin = sinv;
+            m.col_major = col;
+            m.reverse = rev;
+            e = m3_chunk_launch(m, s);
+        }
+    }
+    const cudaError_t ef = cudaFreeAsync(raw, s);
+    if (e == cudaSuccess) e = ef;
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "mamba3 ss2d launch");
+}
+
 int arm_scan_mamba3_angles_f32_noalloc(const ArmMamba3Dims* dims, const float* angles,
                                        size_t n_angles, const float* dt, float* cos, float* sin,
                                        void* stream) {

@@ -28,6 +28,12 @@ constexpr float kPi = 3.14159265358979323846f;
 // memory round trip.
 constexpr int kAgUnroll = 8;
 
+__device__ __forceinline__ int64_t angle_phys(const AngleParams& a, int64_t t) {
+    if (!a.col_major) return t;
+    const int64_t rows = a.len / a.grid_w;
+    return (t % rows) * a.grid_w + t / rows;
+}
+
 __global__ void angle_chunk_sums(AngleParams a, float* ws) {
     const int64_t bh = blockIdx.y;
     const int c = blockIdx.x;
@@ -45,8 +51,9 @@ __global__ void angle_chunk_sums(AngleParams a, float* ws) {
 #pragma unroll
         for (int u = 0; u < kAgUnroll; ++u) {
             const bool in = t + u < t1;
-            av[u] = in ? __ldg(ang + (t + u) * ang_step) : 0.f;
-            dv[u] = in ? __ldg(dt + t + u) : 0.f;
+            const int64_t pt = in ? angle_phys(a, t + u) : 0;
+            av[u] = in ? __ldg(ang + pt * ang_step) : 0.f;
+            dv[u] = in ? __ldg(dt + pt) : 0.f;
         }
 #pragma unroll
         for (int u = 0; u < kAgUnroll; ++u) s = fmaf(tanhf(av[u]) * kPi, dv[u], s);
@@ -82,8 +89,9 @@ __global__ void angle_chunk_write(AngleParams a, const float* ws) {
 #pragma unroll
         for (int u = 0; u < kAgUnroll; ++u) {
             const bool in = t + u < t1;
-            av[u] = in ? __ldg(ang + (t + u) * ang_step) : 0.f;
-            dv[u] = in ? __ldg(dt + t + u) : 0.f;
+            const int64_t pt = in ? angle_phys(a, t + u) : 0;
+            av[u] = in ? __ldg(ang + pt * ang_step) : 0.f;
+            dv[u] = in ? __ldg(dt + pt) : 0.f;
         }
 #pragma unroll
         for (int u = 0; u < kAgUnroll; ++u) {

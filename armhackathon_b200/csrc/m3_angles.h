@@ -12,6 +12,11 @@ struct AngleParams {
     float* cos;           // (batch, len, heads, half)
     float* sin;
     int64_t batch, heads, len, n_angles, half;
+    // traversal of a (len / grid_w) x grid_w grid stored row-major (SS2D):
+    // col_major 1 reads angles and dt at step t's grid position; cos/sin are
+    // written in traversal order
+    int64_t grid_w = 0;
+    int col_major = 0;
 };
 
 size_t angle_workspace_bytes(int64_t batch, int64_t heads, int64_t len, int64_t n_angles);

@@ -101,11 +101,11 @@ __device__ __forceinline__ void ck_gates(const M3Params& p, int64_t bh, int64_t 
         gm[e] = 0.f;
         if (j < QS && it < L) {
             const int64_t t = p.reverse ? L - 1 - it : it;
-            const int64_t g = gate_base + t;
+            const int64_t g = gate_base + m3_phys(p, t);
             const float gamma = p.dt[g] * sigmoid_f(p.trap[g]);
             float shifted = 0.f;
             if (it + 1 < L) {
-                const int64_t nx = p.reverse ? g - 1 : g + 1;
+                const int64_t nx = gate_base + m3_phys(p, p.reverse ? t - 1 : t + 1);
                 shifted = p.dt[nx] * (1.f - sigmoid_f(p.trap[nx]));
             }
             lv[e] = p.adt[g];
@@ -155,7 +155,8 @@ __device__ __forceinline__ void ck_stage_scalar(const M3Params& p, const CkLayou
         const int i0 = mimo ? pi : 2 * pi, i1 = mimo ? pi + half : 2 * pi + 1;
         if (j < QS && it < L) {
             const int64_t t = p.reverse ? L - 1 - it : it;
-            const int64_t qk_off = (bi * L + t) * (mimo ? R : 1) * N + r * N;
+            const int64_t pt = m3_phys(p, t);
+            const int64_t qk_off = (bi * L + pt) * (mimo ? R : 1) * N + r * N;
             const float* qb = p.q_bias + (h * (mimo ? R : 1) + r) * N;
             const float* kb = p.k_bias + (h * (mimo ? R : 1) + r) * N;
             const int64_t cs = ((bi * L + t) * H + h) * half + pi;
@@ -191,7 +192,7 @@ __device__ __forceinline__ void ck_stage_scalar(const M3Params& p, const CkLayou
         float v = 0.f;
         if (j < QS && it < L) {
             const int64_t t = p.reverse ? L - 1 - it : it;
-            v = p.v[((bi * L + t) * H + h) * P + pp];
+            v = p.v[((bi * L + m3_phys(p, t)) * H + h) * P + pp];
             if (mimo) v *= p.psi[(h * R + r) * P + pp];
         }
         s.xs[i * ly.PP4 + pp] = v;
@@ -232,7 +233,7 @@ __device__ __forceinline__ void ck_stage_vec(const M3Params& p, const CkLayout& 
         float klo[4] = {0.f, 0.f, 0.f, 0.f}, khi[4] = {0.f, 0.f, 0.f, 0.f};
         if (j < QS && it < L) {
             const int64_t t = p.reverse ? L - 1 - it : it;
-            const int64_t qk_off = (bi * L + t) * (mimo ? R : 1) * N + r * N;
+            const int64_t qk_off = (bi * L + m3_phys(p, t)) * (mimo ? R : 1) * N + r * N;
             const int64_t bo = (h * (mimo ? R : 1) + r) * N;
             const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cos + ((bi * L + t) * H + h) * half + 4 * c));
             const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sin + ((bi * L + t) * H + h) * half + 4 * c));
@@ -288,7 +289,7 @@ __device__ __forceinline__ void ck_stage_vec(const M3Params& p, const CkLayout& 
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (j < QS && it < L) {
             const int64_t t = p.reverse ? L - 1 - it : it;
-            v = __ldg(reinterpret_cast<const float4*>(p.v + ((bi * L + t) * H + h) * P + 4 * c));
+            v = __ldg(reinterpret_cast<const float4*>(p.v + ((bi * L + m3_phys(p, t)) * H + h) * P + 4 * c));
             if (mimo) {
                 const float4 ps = __ldg(reinterpret_cast<const float4*>(p.psi + (h * R + r) * P + 4 * c));
                 v.x *= ps.x; v.y *= ps.y; v.z *= ps.z; v.w *= ps.w;
@@ -391,7 +392,8 @@ __device__ __forceinline__ void ck_out(const M3Params& p, const CkLayout& ly, in
             const int64_t it = it0 + step;
             if (step >= QS || it >= L) continue;
             const int64_t t = p.reverse ? L - 1 - it : it;
-            const int64_t voff = ((bi * L + t) * H + h) * P + p0;
+            const int64_t pt = m3_phys(p, t);
+            const int64_t voff = ((bi * L + pt) * H + h) * P + p0;
             float o[4] = {0.f, 0.f, 0.f, 0.f};
             float zv[4] = {0.f, 0.f, 0.f, 0.f};
             if (p.z) {
@@ -412,8 +414,13 @@ __device__ __forceinline__ void ck_out(const M3Params& p, const CkLayout& ly, in
                     }
                 }
             }
-            *reinterpret_cast<float4*>(p.out + ((bi * H + h) * L + t) * P + p0) =
-                make_float4(o[0], o[1], o[2], o[3]);
+            float4* dst = reinterpret_cast<float4*>(
+                p.out + (p.out_blh ? (bi * L + pt) * H + h : (bi * H + h) * L + pt) * P + p0);
+            if (p.out_acc) {
+                const float4 prev = *dst;
+                o[0] += prev.x; o[1] += prev.y; o[2] += prev.z; o[3] += prev.w;
+            }
+            *dst = make_float4(o[0], o[1], o[2], o[3]);
         }
     }
 }

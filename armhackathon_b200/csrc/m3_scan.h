@@ -36,7 +36,21 @@ struct M3Params {
     int in_bf16;            // q, k, v, z, angles are bf16 (else fp32)
     int out_bf16;           // out is bf16 (else fp32)
     int out_blh;            // out is (b, l, h, dv) (else head-major (b, h, l, dv))
+    // traversal of a (len / grid_w) x grid_w token grid stored row-major:
+    // col_major 1 walks it column by column (SS2D); q, k, v, z, adt, dt, trap
+    // and out are read / written at the grid position of each step, cos/sin
+    // at the step (the angle pre-pass writes them in traversal order)
+    int64_t grid_w;
+    int col_major;
+    int out_acc;            // out += y (the four SS2D traversals sum in place)
 };
+
+// grid position of traversal step t
+__host__ __device__ inline int64_t m3_phys(const M3Params& p, int64_t t) {
+    if (!p.col_major) return t;
+    const int64_t rows = p.len / p.grid_w;
+    return (t % rows) * p.grid_w + t / rows;
+}
 
 bool m3_shape_supported(int64_t dv, int64_t dqk, int64_t rank);
 cudaError_t m3_scan_launch(const M3Params& p, int backend, cudaStream_t stream);

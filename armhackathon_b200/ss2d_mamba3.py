@@ -12,6 +12,8 @@ The angle pre-pass accumulates along the traversal order, so it runs on the
 views (each ordering gets its own theta), never on the grid.
 """
 
+from typing import Optional
+
 import torch
 
 from .ss2d import _MERGES, grid_to_views
@@ -54,6 +56,47 @@ def _check_grid(name, t, b, h, w, dim, head_major=False):
                          f"full shape {tuple(t.shape)}")
 
 
+@torch.library.custom_op("arm_scan::ss2d_mamba3_fused", mutates_args=())
+def _ss2d_fused_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, adt: torch.Tensor,
+                   dt: torch.Tensor, trap: torch.Tensor, q_bias: torch.Tensor, k_bias: torch.Tensor,
+                   angles: torch.Tensor, d_skip: Optional[torch.Tensor], z: Optional[torch.Tensor],
+                   grid_w: int) -> torch.Tensor:
+    from . import _ffi
+    from .op import _on_device, _ptr, _stream, _CALLS
+    b, length, _, dqk = q.shape
+    h, dv = v.shape[2], v.shape[3]
+    dims = _ffi.ArmMamba3Dims(b, h, dv, dqk, length, 1)
+    out = v.new_empty((b, length, h, dv))
+    with _on_device(v):
+        _ffi.ss2d_mamba3_raw(
+            dims, grid_w, [q.data_ptr(), k.data_ptr(), v.data_ptr(), adt.data_ptr(),
+                           dt.data_ptr(), trap.data_ptr(), q_bias.data_ptr(), k_bias.data_ptr(),
+                           angles.data_ptr()],
+            angles.shape[3], _ptr(d_skip), _ptr(z), out.data_ptr(), _stream(v))
+    _CALLS["n"] += 1
+    return out
+
+
+@_ss2d_fused_op.register_fake
+def _(q, k, v, adt, dt, trap, q_bias, k_bias, angles, d_skip, z, grid_w):
+    return v.new_empty((q.shape[0], q.shape[1], v.shape[2], v.shape[3]))
+
+
+def _ss2d_fused(q, k, v, adt, dt, trap, q_bias, k_bias, angles, D, z, h, w):
+    """All four traversals in one library call reading the grid in place;
+    returns the sum (b, H, W, heads, dv)."""
+    b = q.shape[0]
+    f = lambda t: t.to(torch.float32).contiguous()  # noqa: E731
+    L = h * w
+    out = _ss2d_fused_op(
+        f(q).reshape(b, L, 1, q.shape[-1]), f(k).reshape(b, L, 1, k.shape[-1]),
+        f(v).reshape(b, L, v.shape[3], v.shape[4]), f(adt).reshape(b, adt.shape[1], L),
+        f(dt).reshape(b, dt.shape[1], L), f(trap).reshape(b, trap.shape[1], L), f(q_bias),
+        f(k_bias), f(angles).reshape(b, L, angles.shape[3], angles.shape[4]),
+        None if D is None else f(D), None if z is None else f(z).reshape(b, L, *z.shape[3:]), w)
+    return out.reshape(b, h, w, v.shape[3], v.shape[4])
+
+
 def ss2d_scan_mamba3(q, k, v, adt, dt, trap, q_bias, k_bias, angles, D=None, z=None,
                      merge="sum", scan_pair=None):
     """Four-direction cross-scan over a token grid with Mamba-3 SISO.
@@ -73,6 +116,11 @@ def ss2d_scan_mamba3(q, k, v, adt, dt, trap, q_bias, k_bias, angles, D=None, z=N
         _check_grid(name, t, b, h, w, 4, head_major=True)
     if z is not None:
         _check_grid("z", z, b, h, w, 5)
+    if (scan_pair is None and merge in ("sum", "mean") and q.shape[3] == 1
+            and all(t.is_cuda for t in (q, k, v, adt, dt, trap, angles))
+            and 1 <= angles.shape[4] <= q.shape[4] // 2):
+        out = _ss2d_fused(q, k, v, adt, dt, trap, q_bias, k_bias, angles, D, z, h, w)
+        return out if merge == "sum" else out * 0.25
     if scan_pair is None:
         scan_pair = scan_pair_mamba3
     fwd, bwd = scan_pair(

@@ -212,6 +212,22 @@ int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOp
                                   const void* z, int reverse, void* out, float* last_state,
                                   float* last_bx, void* stream);
 
+/* Extension (no counterpart in the reference): the four-direction Mamba-3
+ * SISO cross-scan of a token grid in one call (the reference composes it in
+ * Python, python/arm_scan/ss2d_mamba3.py).  The grid is len / grid_w rows of
+ * grid_w tokens, stored row-major: q, k (batch, len, 1, dqk); v, z (batch,
+ * len, heads, dv); angles (batch, len, heads, n_angles); adt, dt, trap
+ * (batch, heads, len).  The scan runs row-major and column-major, each
+ * forward and backward, reading the grid in place (the angle pre-pass runs
+ * per ordering, in its traversal order), and the four outputs are summed
+ * into out (batch, len, heads, dv).  n_angles in [1, dqk/2]; d_skip and z
+ * nullable.  Device pointers, stream-ordered; fp32 chunk kernels. */
+int arm_scan_mamba3_ss2d_f32_async(const ArmMamba3Dims* dims, size_t grid_w, const float* q,
+                                   const float* k, const float* v, const float* adt,
+                                   const float* dt, const float* trap, const float* q_bias,
+                                   const float* k_bias, const float* angles, size_t n_angles,
+                                   const float* d_skip, const float* z, float* out, void* stream);
+
 /* Extension (no counterpart in the reference): the final state of
  * arm_scan_selective_scan_f32_async's recurrence without computing the
  * outputs (D, z and out play no part): the first step of a sequence-parallel
