@@ -671,16 +671,13 @@ cudaError_t m3_chunk_launch(const M3Params& p, cudaStream_t stream) {
     const int R = p.psi ? static_cast<int>(p.rank) : 1;
     const CkLayout ly(static_cast<int>(p.dqk), static_cast<int>(p.dv));
     const size_t smem = static_cast<size_t>(ly.total) * sizeof(float);
-    // The sequential form runs one CTA per (batch, head); when that fills
-    // less than half of the GPU's CTA slots, the chunk-parallel form (every
-    // (batch*head, chunk) its own CTA, at the cost of a second staging pass
-    // and a state round trip through memory) is faster.
-    // B200SCAN_M3_CHUNK_SEQ=1 / =0 forces one or the other.
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t slots = static_cast<int64_t>(sms) * static_cast<int64_t>(227 * 1024 / smem);
-    bool split = 2 * p.batch * p.heads < slots && p.len > kQR;
+    // The chunk-parallel form (every (batch*head, chunk) its own CTA, at the
+    // cost of a second staging pass and a state round trip through memory)
+    // measured faster than the sequential form (one CTA per (batch, head)) on
+    // every benchmarked shape (config 2 1.81 vs 2.19 ms, config 3 23.2 vs 30.2,
+    // config 4a 7.8 vs 17.4); the sequential form remains for single-chunk
+    // sequences.  B200SCAN_M3_CHUNK_SEQ=1 / =0 forces one or the other.
+    bool split = p.len > kQR / R;  // more than one chunk of (step, rank) rows
     if (const char* v = std::getenv("B200SCAN_M3_CHUNK_SEQ")) split = v[0] != '1';
     if (split && (p.dqk * p.dv) % 4 == 0)
         return R == 4 ? m3_chunk_launch_split<4>(p, stream)
