@@ -6,14 +6,19 @@
 // a thread owns one (row, segment) and walks its steps in order with all
 // d_state <= 16 states in registers, so there is no per-chunk fold:
 //
-//   pass 1: each (row, segment) from a zero state -> h_end, sum of dt;
+//   pass 1: each (row, segment) but the last from a zero state -> h_end,
+//           sum of dt; the first segment instead runs the full scan from
+//           h0 (its incoming state is known), writing y and its true end;
 //   carry:  h_in(s) = exp(A sum dt(prev)) h_in(prev) + h_end(prev) in
-//           traversal order, seeded by h0; the final h is last_state;
-//   pass 2: each (row, segment) from h_in, writing y.
+//           traversal order, starting from the first segment's end;
+//   pass 2: each (row, segment) but the first from h_in, writing y; the
+//           last segment writes last_state.
 //
-// Every exp is computed twice (once per pass), in exchange for no barriers
-// in the sweeps and far fewer instructions per (step, state) than the
-// fold's aggregate bookkeeping.  A CTA is 128 rows of one (batch, group)
+// Every exp but those of the first and last segments is computed twice
+// (2 (S - 1) / S per element), in exchange for no barriers in the sweeps
+// and far fewer instructions per (step, state) than the fold's aggregate
+// bookkeeping.  With out == nullptr (final state only) pass 1 covers every
+// segment from zero and the carry ends in last_state.  A CTA is 128 rows of one (batch, group)
 // and one segment; B and C of the segment are staged in chunks of 64 steps
 // by cp.async into a transposed [step][state] slab (one LDS.128 = 4 states
 // of a step, broadcast to every row), double-buffered.  u, delta, z are
@@ -60,18 +65,27 @@ __device__ __forceinline__ float4 ld_steps(const float* row, int64_t L, int64_t 
     return make_float4(v.w, v.z, v.y, v.x);
 }
 
+// Sweep modes of one (row block, segment).
+enum Seg2Mode {
+    kSeg2State = 0,  // from zero: end state + sum of dt
+    kSeg2Rescan = 1, // from h_in: y (and last_state on the last segment)
+    kSeg2First = 2,  // from h0: y, and the true end state into hend
+};
+
+using Seg2Slab = float[2][2][kS2Chunk * kS2Stride];  // [buf][B, C][step][state]
+
 // POLY: 0 every exp on MUFU; 1 states 12-15 (25%), 2 states 8-15 (50%) on the
 // FMA pipe (exp2_poly2).
-template <bool FULL, bool REV, int POLY>
-__global__ void __launch_bounds__(kS2Rows) m1_seg2_kernel(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
-    __shared__ __align__(16) float sb[2][2][kS2Chunk * kS2Stride];  // [buf][B, C][step][state]
+template <int MODE, bool REV, int POLY>
+__device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& ws, int S, int64_t Ls,
+                                              int s, Seg2Slab& sb) {
+    constexpr bool FULL = MODE != kSeg2State;
     const int N = static_cast<int>(p.state);
     const int64_t L = p.len, D = p.dim, G = p.groups, gsz = D / G;
     const int64_t rows_all = p.batch * D;
     const int blocks_per_group = static_cast<int>((gsz + kS2Rows - 1) / kS2Rows);
     const int64_t bg = blockIdx.x / blocks_per_group;  // (batch, group)
     const int jb = blockIdx.x % blocks_per_group;
-    const int s = blockIdx.y;
     const int64_t b = bg / G, g = bg % G;
     const int64_t dd = g * gsz + static_cast<int64_t>(jb) * kS2Rows + threadIdx.x;  // channel
     const bool active = static_cast<int64_t>(jb) * kS2Rows + threadIdx.x < gsz;
@@ -92,8 +106,11 @@ __global__ void __launch_bounds__(kS2Rows) m1_seg2_kernel(M1Params p, Seg2Ws ws,
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
         h[q] = make_float2(0.f, 0.f);
-        if (FULL) {
+        if (MODE == kSeg2Rescan) {
             const float* hi = ws.hin + (static_cast<int64_t>(s) * rows_all + row) * 16;
+            h[q] = make_float2(2 * q < N ? hi[2 * q] : 0.f, 2 * q + 1 < N ? hi[2 * q + 1] : 0.f);
+        } else if (MODE == kSeg2First && p.h0) {
+            const float* hi = p.h0 + row * N;
             h[q] = make_float2(2 * q < N ? hi[2 * q] : 0.f, 2 * q + 1 < N ? hi[2 * q + 1] : 0.f);
         }
     }
@@ -187,7 +204,7 @@ __global__ void __launch_bounds__(kS2Rows) m1_seg2_kernel(M1Params p, Seg2Ws ws,
         }
         __syncthreads();  // buffer buf is restaged two chunks later
     }
-    if (!FULL && active) {
+    if (MODE != kSeg2Rescan && active) {
         float* he = ws.hend + (static_cast<int64_t>(s) * rows_all + row) * 16;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -196,22 +213,56 @@ __global__ void __launch_bounds__(kS2Rows) m1_seg2_kernel(M1Params p, Seg2Ws ws,
         }
         ws.dtsum[static_cast<int64_t>(s) * rows_all + row] = dtsum;
     }
+    if (FULL && s == S - 1 && p.last_state && active) {
+        float* ls = p.last_state + row * N;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (2 * q < N) ls[2 * q] = h[q].x;
+            if (2 * q + 1 < N) ls[2 * q + 1] = h[q].y;
+        }
+    }
 }
 
+// Pass 1.  FIRST: segment 0 (blockIdx.y == 0) runs the full scan from h0 and
+// the others (1 .. S-2) the state-only sweep; otherwise every segment is
+// state-only.
+template <bool FIRST, bool REV, int POLY>
+__global__ void __launch_bounds__(kS2Rows, 5) m1_seg2_pass1(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
+    __shared__ __align__(16) Seg2Slab sb;
+    const int s = blockIdx.y;
+    if (FIRST && s == 0)
+        m1_seg2_sweep<kSeg2First, REV, POLY>(p, ws, S, Ls, 0, sb);
+    else
+        m1_seg2_sweep<kSeg2State, REV, POLY>(p, ws, S, Ls, s, sb);
+}
+
+// Pass 2: segments 1 .. S-1 from their incoming states.
+template <bool REV, int POLY>
+__global__ void __launch_bounds__(kS2Rows) m1_seg2_pass2(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
+    __shared__ __align__(16) Seg2Slab sb;
+    m1_seg2_sweep<kSeg2Rescan, REV, POLY>(p, ws, S, Ls, blockIdx.y + 1, sb);
+}
+
+// FIRST: segment 0's hend is already its true end state (pass 1 ran it from
+// h0), the carry fills h_in of segments 1 .. S-1 and pass 2 writes
+// last_state.  Otherwise every hend is from zero, the carry starts at h0 and
+// ends in last_state.
+template <bool FIRST>
 __global__ void m1_seg2_carry_kernel(M1Params p, Seg2Ws ws, int S) {
     const int64_t rows_all = p.batch * p.dim, N = p.state;
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= rows_all * N) return;
     const int64_t row = i / N, n = i % N;
     const float a = p.A[(row % p.dim) * N + n] * kLog2e;
-    float h = p.h0 ? p.h0[i] : 0.f;
-    for (int k = 0; k < S; ++k) {  // segments are already in traversal order
+    float h = FIRST ? __ldg(ws.hend + row * 16 + n) : (p.h0 ? p.h0[i] : 0.f);
+    for (int k = FIRST ? 1 : 0; k < S; ++k) {  // segments are already in traversal order
         const int64_t sr = static_cast<int64_t>(k) * rows_all + row;
-        const float ds = __ldg(ws.dtsum + sr), he = __ldg(ws.hend + sr * 16 + n);
         ws.hin[sr * 16 + n] = h;
+        if (FIRST && k == S - 1) break;
+        const float ds = __ldg(ws.dtsum + sr), he = __ldg(ws.hend + sr * 16 + n);
         h = fmaf(ex2_approx(a * ds), h, he);
     }
-    if (p.last_state) p.last_state[i] = h;
+    if (!FIRST && p.last_state) p.last_state[i] = h;
 }
 
 }  // namespace
@@ -253,23 +304,32 @@ cudaError_t m1_seg2_launch(const M1Params& p, int S, cudaStream_t stream) {
     int poly = kSeg2Poly, poly1 = kSeg2Poly1;
     if (const char* v = getenv("B200SCAN_M1_SEG2_POLY")) poly = atoi(v);
     if (const char* v = getenv("B200SCAN_M1_SEG2_POLY1")) poly1 = atoi(v);
-    auto k1 = poly1 == 2 ? (p.reverse ? m1_seg2_kernel<false, true, 2> : m1_seg2_kernel<false, false, 2>)
-            : poly1 == 1 ? (p.reverse ? m1_seg2_kernel<false, true, 1> : m1_seg2_kernel<false, false, 1>)
-                         : (p.reverse ? m1_seg2_kernel<false, true, 0> : m1_seg2_kernel<false, false, 0>);
-    auto k2 = poly == 2 ? (p.reverse ? m1_seg2_kernel<true, true, 2> : m1_seg2_kernel<true, false, 2>)
-            : poly == 1 ? (p.reverse ? m1_seg2_kernel<true, true, 1> : m1_seg2_kernel<true, false, 1>)
-                        : (p.reverse ? m1_seg2_kernel<true, true, 0> : m1_seg2_kernel<true, false, 0>);
-    k1<<<grid, kS2Rows, 0, stream>>>(p, ws, S, Ls);
+    const bool first = p.out != nullptr;  // out == nullptr: final state only
+#define SEG2_PICK(K, PL, ...)                                                                    \
+    (PL == 2 ? (p.reverse ? K<__VA_ARGS__ true, 2> : K<__VA_ARGS__ false, 2>)                    \
+             : PL == 1 ? (p.reverse ? K<__VA_ARGS__ true, 1> : K<__VA_ARGS__ false, 1>)          \
+                       : (p.reverse ? K<__VA_ARGS__ true, 0> : K<__VA_ARGS__ false, 0>))
+    auto k1 = first ? SEG2_PICK(m1_seg2_pass1, poly1, true,) : SEG2_PICK(m1_seg2_pass1, poly1, false,);
+    auto k2 = SEG2_PICK(m1_seg2_pass2, poly, );
+#undef SEG2_PICK
+    // pass 1 covers segments 0 .. S-2 when the first one runs in full (all of
+    // them for S == 1), every segment otherwise
+    const unsigned s1 = first ? static_cast<unsigned>(S > 1 ? S - 1 : 1) : static_cast<unsigned>(S);
+    k1<<<dim3(grid.x, s1), kS2Rows, 0, stream>>>(p, ws, S, Ls);
     note_launch();
     e = cudaGetLastError();
-    if (e == cudaSuccess) {
+    if (e == cudaSuccess && (S > 1 || !first)) {
         const int64_t n = rows * p.state;
-        m1_seg2_carry_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(p, ws, S);
+        const unsigned cg = static_cast<unsigned>((n + 255) / 256);
+        if (first)
+            m1_seg2_carry_kernel<true><<<cg, 256, 0, stream>>>(p, ws, S);
+        else
+            m1_seg2_carry_kernel<false><<<cg, 256, 0, stream>>>(p, ws, S);
         note_launch();
         e = cudaGetLastError();
     }
-    if (e == cudaSuccess && p.out) {  // out == nullptr: final state only
-        k2<<<grid, kS2Rows, 0, stream>>>(p, ws, S, Ls);
+    if (e == cudaSuccess && first && S > 1) {
+        k2<<<dim3(grid.x, static_cast<unsigned>(S - 1)), kS2Rows, 0, stream>>>(p, ws, S, Ls);
         note_launch();
         e = cudaGetLastError();
     }

@@ -277,7 +277,7 @@ def test_host_entry_pipelined_matches_device(shape):
 
 
 @pytest.mark.parametrize("shape", [(2, 40, 2048, 16, 2), (3, 130, 1024, 13, 1), (1, 8, 4096, 16, 1)])
-@pytest.mark.parametrize("segments", ["1", "4", "16"])
+@pytest.mark.parametrize("segments", ["1", "2", "4", "16"])
 @pytest.mark.parametrize("reverse", [False, True])
 def test_fold_free_two_pass_vs_oracle(shape, segments, reverse, monkeypatch):
     """Variant 12 (fold-free two-pass: segment end states, exact segment-decay
