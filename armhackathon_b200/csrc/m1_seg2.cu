@@ -33,8 +33,14 @@ namespace b200scan {
 
 namespace {
 
-constexpr int kS2Rows = 128;   // threads (rows) per CTA
+constexpr int kS2Rows = 128;   // rows per CTA
 constexpr int kS2Chunk = 64;   // steps of B/C per staged chunk
+// rows per thread: 2 (half the shared-memory loads per row, 64 threads and
+// ~165 registers) measured 13% slower at the prefill shape than 1
+#ifndef B200SCAN_SEG2_RPT
+#define B200SCAN_SEG2_RPT 1
+#endif
+constexpr int kS2Rpt = B200SCAN_SEG2_RPT;
 // default share of exps on the FMA pipe (see m1_seg2_kernel): pass 2 (kSeg2Poly)
 // and pass 1 (kSeg2Poly1, the MUFU-bound one); the two passes' decays then
 // differ by the approximations' error (~1e-7 relative), not by design
@@ -74,12 +80,17 @@ enum Seg2Mode {
 
 using Seg2Slab = float[2][2][kS2Chunk * kS2Stride];  // [buf][B, C][step][state]
 
+// One CTA sweeps kS2Rows rows of one (batch, group) over one segment with
+// kS2Rows / RPT threads: a thread owns RPT rows (threadIdx.x + r * threads),
+// so each shared-memory load of B/C (the same 4 states of a step for every
+// row) feeds RPT rows' updates.
 // POLY: 0 every exp on MUFU; 1 states 12-15 (25%), 2 states 8-15 (50%) on the
 // FMA pipe (exp2_poly2).
-template <int MODE, bool REV, int POLY>
+template <int MODE, bool REV, int POLY, int RPT>
 __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& ws, int S, int64_t Ls,
                                               int s, Seg2Slab& sb) {
     constexpr bool FULL = MODE != kSeg2State;
+    constexpr int T = kS2Rows / RPT;  // threads
     const int N = static_cast<int>(p.state);
     const int64_t L = p.len, D = p.dim, G = p.groups, gsz = D / G;
     const int64_t rows_all = p.batch * D;
@@ -87,39 +98,39 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
     const int64_t bg = blockIdx.x / blocks_per_group;  // (batch, group)
     const int jb = blockIdx.x % blocks_per_group;
     const int64_t b = bg / G, g = bg % G;
-    const int64_t dd = g * gsz + static_cast<int64_t>(jb) * kS2Rows + threadIdx.x;  // channel
-    const bool active = static_cast<int64_t>(jb) * kS2Rows + threadIdx.x < gsz;
-    const int64_t row = b * D + (active ? dd : g * gsz);
     const int64_t it0 = static_cast<int64_t>(s) * Ls;  // first traversal step of the segment
 
-    // this row's A * log2 e, bias, D
-    float2 a2[8];
+    int64_t row[RPT];
+    bool active[RPT];
+    float2 a2[RPT][8], h[RPT][8];  // this row's A * log2 e; state
+    float bias[RPT], dsk[RPT];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        const int n0 = 2 * q;
-        const float* A = p.A + (row % D) * N;
-        a2[q] = make_float2(n0 < N ? A[n0] * kLog2e : 0.f, n0 + 1 < N ? A[n0 + 1] * kLog2e : 0.f);
-    }
-    const float bias = p.delta_bias ? p.delta_bias[row % D] : 0.f;
-    const float dsk = p.d_skip ? p.d_skip[row % D] : 0.f;
-    float2 h[8];
+    for (int r = 0; r < RPT; ++r) {
+        const int64_t local = static_cast<int64_t>(jb) * kS2Rows + r * T + threadIdx.x;
+        active[r] = local < gsz;
+        row[r] = b * D + g * gsz + (active[r] ? local : 0);
+        const int64_t ch = row[r] % D;
+        const float* A = p.A + ch * N;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        h[q] = make_float2(0.f, 0.f);
-        if (MODE == kSeg2Rescan) {
-            const float* hi = ws.hin + (static_cast<int64_t>(s) * rows_all + row) * 16;
-            h[q] = make_float2(2 * q < N ? hi[2 * q] : 0.f, 2 * q + 1 < N ? hi[2 * q + 1] : 0.f);
-        } else if (MODE == kSeg2First && p.h0) {
-            const float* hi = p.h0 + row * N;
-            h[q] = make_float2(2 * q < N ? hi[2 * q] : 0.f, 2 * q + 1 < N ? hi[2 * q + 1] : 0.f);
-        }
+        for (int q = 0; q < 8; ++q)
+            a2[r][q] = make_float2(2 * q < N ? A[2 * q] * kLog2e : 0.f,
+                                   2 * q + 1 < N ? A[2 * q + 1] * kLog2e : 0.f);
+        bias[r] = p.delta_bias ? p.delta_bias[ch] : 0.f;
+        dsk[r] = p.d_skip ? p.d_skip[ch] : 0.f;
+        const float* hi = MODE == kSeg2Rescan ? ws.hin + (static_cast<int64_t>(s) * rows_all + row[r]) * 16
+                          : (MODE == kSeg2First && p.h0) ? p.h0 + row[r] * N
+                                                        : nullptr;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            h[r][q] = hi ? make_float2(2 * q < N ? hi[2 * q] : 0.f, 2 * q + 1 < N ? hi[2 * q + 1] : 0.f)
+                         : make_float2(0.f, 0.f);
     }
 
     const float* Bg = p.B + bg * N * L;
     const float* Cg = p.C + bg * N * L;
     // stage chunk c of the segment into buffer buf: element (step j, state n)
     auto stage = [&](int c, int buf) {
-        for (int idx = threadIdx.x; idx < kS2Chunk * 16; idx += kS2Rows) {
+        for (int idx = threadIdx.x; idx < kS2Chunk * 16; idx += T) {
             const int n = idx / kS2Chunk, j = idx % kS2Chunk;  // coalesced over steps
             const int64_t it = it0 + static_cast<int64_t>(c) * kS2Chunk + j;
             const bool ok = n < N && it < L;
@@ -130,16 +141,18 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
         cpa_commit();
     };
 
-    const float* drow = p.delta + row * L;
-    const float* urow = p.u + row * L;
-    const float* zrow = (FULL && p.z) ? p.z + row * L : nullptr;
-    float* orow = FULL ? p.out + row * L : nullptr;
+    const bool has_z = FULL && p.z;
     const int n_chunks = static_cast<int>((Ls + kS2Chunk - 1) / kS2Chunk);
-    float dtsum = 0.f;
-
+    float dtsum[RPT];
+    float4 nd[RPT], nu[RPT], nz[RPT];
     stage(0, 0);
-    float4 nd = ld_steps<REV>(drow, L, it0), nu = ld_steps<REV>(urow, L, it0);
-    float4 nz = zrow ? ld_steps<REV>(zrow, L, it0) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+        dtsum[r] = 0.f;
+        nd[r] = ld_steps<REV>(p.delta + row[r] * L, L, it0);
+        nu[r] = ld_steps<REV>(p.u + row[r] * L, L, it0);
+        nz[r] = has_z ? ld_steps<REV>(p.z + row[r] * L, L, it0) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     for (int c = 0; c < n_chunks; ++c) {
         const int buf = c & 1;
         if (c + 1 < n_chunks) {
@@ -154,71 +167,97 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
 #pragma unroll 1
         for (int j4 = 0; j4 < kS2Chunk; j4 += 4) {
             const int64_t it = it0 + static_cast<int64_t>(c) * kS2Chunk + j4;
-            const float4 d4 = nd, u4 = nu, z4 = nz;
-            if (j4 + 4 < kS2Chunk || c + 1 < n_chunks) {
-                nd = ld_steps<REV>(drow, L, it + 4);
-                nu = ld_steps<REV>(urow, L, it + 4);
-                if (zrow) nz = ld_steps<REV>(zrow, L, it + 4);
+            float dv[RPT][4], uv[RPT][4], zv[RPT][4], yv[RPT][4];
+            const bool more = j4 + 4 < kS2Chunk || c + 1 < n_chunks;
+#pragma unroll
+            for (int r = 0; r < RPT; ++r) {
+                dv[r][0] = nd[r].x, dv[r][1] = nd[r].y, dv[r][2] = nd[r].z, dv[r][3] = nd[r].w;
+                uv[r][0] = nu[r].x, uv[r][1] = nu[r].y, uv[r][2] = nu[r].z, uv[r][3] = nu[r].w;
+                zv[r][0] = nz[r].x, zv[r][1] = nz[r].y, zv[r][2] = nz[r].z, zv[r][3] = nz[r].w;
+                if (more) {
+                    nd[r] = ld_steps<REV>(p.delta + row[r] * L, L, it + 4);
+                    nu[r] = ld_steps<REV>(p.u + row[r] * L, L, it + 4);
+                    if (has_z) nz[r] = ld_steps<REV>(p.z + row[r] * L, L, it + 4);
+                }
             }
-            const float dv[4] = {d4.x, d4.y, d4.z, d4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
-            const float zv[4] = {z4.x, z4.y, z4.z, z4.w};
-            float yv[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                float dt = dv[k] + bias;
-                if (p.delta_softplus) dt = softplus_fast(dt);
-                dtsum += dt;
-                const float dtu = dt * uv[k];
-                const float2 dt2 = make_float2(dt, dt), du2 = make_float2(dtu, dtu);
+                float2 dt2[RPT], du2[RPT], y2[RPT];
+#pragma unroll
+                for (int r = 0; r < RPT; ++r) {
+                    float dt = dv[r][k] + bias[r];
+                    if (p.delta_softplus) dt = softplus_fast(dt);
+                    dtsum[r] += dt;
+                    const float dtu = dt * uv[r][k];
+                    dt2[r] = make_float2(dt, dt);
+                    du2[r] = make_float2(dtu, dtu);
+                    y2[r] = make_float2(0.f, 0.f);
+                }
                 const float* bk = sB + (j4 + k) * kS2Stride;
                 const float* ck = sC + (j4 + k) * kS2Stride;
-                float2 y2 = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int q4 = 0; q4 < 4; ++q4) {
                     const float4 bb = *reinterpret_cast<const float4*>(bk + 4 * q4);
-                    const float2 x0 = fmul2(dt2, a2[2 * q4]), x1 = fmul2(dt2, a2[2 * q4 + 1]);
+                    float4 cc;
+                    if (FULL) cc = *reinterpret_cast<const float4*>(ck + 4 * q4);
                     const bool poly = (POLY == 1 && q4 == 3) || (POLY == 2 && q4 >= 2);
-                    const float2 e0 = poly ? exp2_poly2(x0) : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-                    const float2 e1 = poly ? exp2_poly2(x1) : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
-                    h[2 * q4] = ffma2(e0, h[2 * q4], fmul2(du2, make_float2(bb.x, bb.y)));
-                    h[2 * q4 + 1] = ffma2(e1, h[2 * q4 + 1], fmul2(du2, make_float2(bb.z, bb.w)));
-                    if (FULL) {
-                        const float4 cc = *reinterpret_cast<const float4*>(ck + 4 * q4);
-                        y2 = ffma2(make_float2(cc.x, cc.y), h[2 * q4], y2);
-                        y2 = ffma2(make_float2(cc.z, cc.w), h[2 * q4 + 1], y2);
+#pragma unroll
+                    for (int r = 0; r < RPT; ++r) {
+                        const float2 x0 = fmul2(dt2[r], a2[r][2 * q4]), x1 = fmul2(dt2[r], a2[r][2 * q4 + 1]);
+                        const float2 e0 = poly ? exp2_poly2(x0) : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+                        const float2 e1 = poly ? exp2_poly2(x1) : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+                        h[r][2 * q4] = ffma2(e0, h[r][2 * q4], fmul2(du2[r], make_float2(bb.x, bb.y)));
+                        h[r][2 * q4 + 1] = ffma2(e1, h[r][2 * q4 + 1], fmul2(du2[r], make_float2(bb.z, bb.w)));
+                        if (FULL) {
+                            y2[r] = ffma2(make_float2(cc.x, cc.y), h[r][2 * q4], y2[r]);
+                            y2[r] = ffma2(make_float2(cc.z, cc.w), h[r][2 * q4 + 1], y2[r]);
+                        }
                     }
                 }
                 if (FULL) {
-                    float y = y2.x + y2.y + dsk * uv[k];
-                    if (zrow) y *= silu_fast(zv[k]);
-                    yv[k] = y;
+#pragma unroll
+                    for (int r = 0; r < RPT; ++r) {
+                        float y = y2[r].x + y2[r].y + dsk[r] * uv[r][k];
+                        if (has_z) y *= silu_fast(zv[r][k]);
+                        yv[r][k] = y;
+                    }
                 }
             }
-            if (FULL && active && it < L) {
-                if (!REV)
-                    __stcs(reinterpret_cast<float4*>(orow + it), make_float4(yv[0], yv[1], yv[2], yv[3]));
-                else
-                    __stcs(reinterpret_cast<float4*>(orow + (L - 4 - it)),
-                           make_float4(yv[3], yv[2], yv[1], yv[0]));
+            if (FULL && it < L) {
+#pragma unroll
+                for (int r = 0; r < RPT; ++r) {
+                    if (!active[r]) continue;
+                    float* orow = p.out + row[r] * L;
+                    if (!REV)
+                        __stcs(reinterpret_cast<float4*>(orow + it),
+                               make_float4(yv[r][0], yv[r][1], yv[r][2], yv[r][3]));
+                    else
+                        __stcs(reinterpret_cast<float4*>(orow + (L - 4 - it)),
+                               make_float4(yv[r][3], yv[r][2], yv[r][1], yv[r][0]));
+                }
             }
         }
         __syncthreads();  // buffer buf is restaged two chunks later
     }
-    if (MODE != kSeg2Rescan && active) {
-        float* he = ws.hend + (static_cast<int64_t>(s) * rows_all + row) * 16;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            he[2 * q] = h[q].x;
-            he[2 * q + 1] = h[q].y;
+    for (int r = 0; r < RPT; ++r) {
+        if (!active[r]) continue;
+        if (MODE != kSeg2Rescan) {
+            float* he = ws.hend + (static_cast<int64_t>(s) * rows_all + row[r]) * 16;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                he[2 * q] = h[r][q].x;
+                he[2 * q + 1] = h[r][q].y;
+            }
+            ws.dtsum[static_cast<int64_t>(s) * rows_all + row[r]] = dtsum[r];
         }
-        ws.dtsum[static_cast<int64_t>(s) * rows_all + row] = dtsum;
-    }
-    if (FULL && s == S - 1 && p.last_state && active) {
-        float* ls = p.last_state + row * N;
+        if (FULL && s == S - 1 && p.last_state) {
+            float* ls = p.last_state + row[r] * N;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            if (2 * q < N) ls[2 * q] = h[q].x;
-            if (2 * q + 1 < N) ls[2 * q + 1] = h[q].y;
+            for (int q = 0; q < 8; ++q) {
+                if (2 * q < N) ls[2 * q] = h[r][q].x;
+                if (2 * q + 1 < N) ls[2 * q + 1] = h[r][q].y;
+            }
         }
     }
 }
@@ -227,20 +266,20 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
 // the others (1 .. S-2) the state-only sweep; otherwise every segment is
 // state-only.
 template <bool FIRST, bool REV, int POLY>
-__global__ void __launch_bounds__(kS2Rows, 5) m1_seg2_pass1(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
+__global__ void __launch_bounds__(kS2Rows / kS2Rpt) m1_seg2_pass1(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
     __shared__ __align__(16) Seg2Slab sb;
     const int s = blockIdx.y;
     if (FIRST && s == 0)
-        m1_seg2_sweep<kSeg2First, REV, POLY>(p, ws, S, Ls, 0, sb);
+        m1_seg2_sweep<kSeg2First, REV, POLY, kS2Rpt>(p, ws, S, Ls, 0, sb);
     else
-        m1_seg2_sweep<kSeg2State, REV, POLY>(p, ws, S, Ls, s, sb);
+        m1_seg2_sweep<kSeg2State, REV, POLY, kS2Rpt>(p, ws, S, Ls, s, sb);
 }
 
 // Pass 2: segments 1 .. S-1 from their incoming states.
 template <bool REV, int POLY>
-__global__ void __launch_bounds__(kS2Rows) m1_seg2_pass2(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
+__global__ void __launch_bounds__(kS2Rows / kS2Rpt) m1_seg2_pass2(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
     __shared__ __align__(16) Seg2Slab sb;
-    m1_seg2_sweep<kSeg2Rescan, REV, POLY>(p, ws, S, Ls, blockIdx.y + 1, sb);
+    m1_seg2_sweep<kSeg2Rescan, REV, POLY, kS2Rpt>(p, ws, S, Ls, blockIdx.y + 1, sb);
 }
 
 // FIRST: segment 0's hend is already its true end state (pass 1 ran it from
@@ -315,7 +354,7 @@ cudaError_t m1_seg2_launch(const M1Params& p, int S, cudaStream_t stream) {
     // pass 1 covers segments 0 .. S-2 when the first one runs in full (all of
     // them for S == 1), every segment otherwise
     const unsigned s1 = first ? static_cast<unsigned>(S > 1 ? S - 1 : 1) : static_cast<unsigned>(S);
-    k1<<<dim3(grid.x, s1), kS2Rows, 0, stream>>>(p, ws, S, Ls);
+    k1<<<dim3(grid.x, s1), kS2Rows / kS2Rpt, 0, stream>>>(p, ws, S, Ls);
     note_launch();
     e = cudaGetLastError();
     if (e == cudaSuccess && (S > 1 || !first)) {
@@ -329,7 +368,7 @@ cudaError_t m1_seg2_launch(const M1Params& p, int S, cudaStream_t stream) {
         e = cudaGetLastError();
     }
     if (e == cudaSuccess && first && S > 1) {
-        k2<<<dim3(grid.x, static_cast<unsigned>(S - 1)), kS2Rows, 0, stream>>>(p, ws, S, Ls);
+        k2<<<dim3(grid.x, static_cast<unsigned>(S - 1)), kS2Rows / kS2Rpt, 0, stream>>>(p, ws, S, Ls);
         note_launch();
         e = cudaGetLastError();
     }

@@ -222,6 +222,16 @@ def profiled_traffic(workload):
     return int(m.group(1)) if m else None
 
 
+def seg2_segments(w):
+    """Segment count the default Mamba-1 kernel picks for this shape (the rule
+    of m1_seg2_segments in armhackathon_b200/csrc/m1_seg2.cu)."""
+    rows, L, S = w["batch"] * w["dim"], w["len"], 1
+    while rows * S < 148 * 1024 and L % (2 * S) == 0 and L // (2 * S) >= 128 \
+            and (L // (2 * S)) % 64 == 0:
+        S *= 2
+    return S
+
+
 def mufu_roofline(w, k_ms, clocks):
     """The Mamba-1 scan's binding unit: one exp per (batch, channel, step,
     state) is the algorithm's minimum (the reference computes exactly that);
@@ -231,13 +241,14 @@ def mufu_roofline(w, k_ms, clocks):
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
     exps = w["batch"] * w["dim"] * w["len"] * w["state"]
+    S = seg2_segments(w)
     achieved = exps / (k_ms * 1e-3) / 1e9
     peak = 16 * sms * mhz * 1e6 / 1e9
     return {"bound": "mufu", "achieved": achieved, "peak": peak, "unit": "Gexp/s",
             "frac": achieved / peak, "peak_source": "nominal 16/clk/SM x sampled SM clock",
-            "executed_per_algorithmic": 2.0,
-            "note": "the default two-pass kernel computes every exp twice (segment end states, "
-                    "then outputs), plus the softplus/silu exps per (row, step)"}
+            "executed_per_algorithmic": 2 * (S - 1) / S if S > 1 else 1.0, "segments": S,
+            "note": "the default two-pass kernel computes the exps of segments 1 .. S-2 twice "
+                    "(end states, then outputs), plus the softplus/silu exps per (row, step)"}
 
 
 def algorithmic_bytes(w):
