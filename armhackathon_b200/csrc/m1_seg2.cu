@@ -41,6 +41,16 @@ constexpr int kS2Chunk = 64;   // steps of B/C per staged chunk
 #define B200SCAN_SEG2_RPT 1
 #endif
 constexpr int kS2Rpt = B200SCAN_SEG2_RPT;
+// minimum resident CTAs per SM asked of the compiler: pass 1 at 5 (96
+// registers; its first-segment branch otherwise takes 100 and 4 CTAs) measured
+// 7% faster over the op; pass 2 at 6 (80 registers, spills) 8% slower
+#ifndef B200SCAN_SEG2_MINB1
+#define B200SCAN_SEG2_MINB1 5
+#endif
+#ifndef B200SCAN_SEG2_MINB2
+#define B200SCAN_SEG2_MINB2 1
+#endif
+constexpr int kS2MinBlocks1 = B200SCAN_SEG2_MINB1, kS2MinBlocks2 = B200SCAN_SEG2_MINB2;
 // default share of exps on the FMA pipe (see m1_seg2_kernel): pass 2 (kSeg2Poly)
 // and pass 1 (kSeg2Poly1, the MUFU-bound one); the two passes' decays then
 // differ by the approximations' error (~1e-7 relative), not by design
@@ -266,7 +276,7 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
 // the others (1 .. S-2) the state-only sweep; otherwise every segment is
 // state-only.
 template <bool FIRST, bool REV, int POLY>
-__global__ void __launch_bounds__(kS2Rows / kS2Rpt) m1_seg2_pass1(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
+__global__ void __launch_bounds__(kS2Rows / kS2Rpt, kS2MinBlocks1) m1_seg2_pass1(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
     __shared__ __align__(16) Seg2Slab sb;
     const int s = blockIdx.y;
     if (FIRST && s == 0)
@@ -277,7 +287,7 @@ __global__ void __launch_bounds__(kS2Rows / kS2Rpt) m1_seg2_pass1(M1Params p, Se
 
 // Pass 2: segments 1 .. S-1 from their incoming states.
 template <bool REV, int POLY>
-__global__ void __launch_bounds__(kS2Rows / kS2Rpt) m1_seg2_pass2(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
+__global__ void __launch_bounds__(kS2Rows / kS2Rpt, kS2MinBlocks2) m1_seg2_pass2(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
     __shared__ __align__(16) Seg2Slab sb;
     m1_seg2_sweep<kSeg2Rescan, REV, POLY, kS2Rpt>(p, ws, S, Ls, blockIdx.y + 1, sb);
 }
