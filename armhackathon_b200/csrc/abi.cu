@@ -371,6 +371,13 @@ int m3_run(const M3Params& m, int backend, cudaStream_t s) {
 namespace b200scan {
 std::atomic<unsigned long long> g_kernel_launches{0};
 void note_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("B200SCAN_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
 }  // namespace b200scan
 
 extern "C" {

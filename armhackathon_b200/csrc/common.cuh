@@ -141,4 +141,35 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
                        __uint_as_float(ty * 8388608u + __float_as_uint(p.y)));
 }
 
+// ---- programmatic dependent launch (sm_90+) --------------------------------
+// A kernel launched with launch_pdl may start while its stream predecessor is
+// still running; it calls griddep_wait() before touching anything the
+// predecessor writes (that returns once the predecessor grid has completed and
+// its memory is visible).  griddep_launch_dependents() lets the next
+// PDL-launched kernel be scheduled early.  Both are no-ops in a kernel that
+// was launched plainly.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// B200SCAN_PDL=0 turns the attribute off (plain stream-ordered launches).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 }  // namespace b200scan

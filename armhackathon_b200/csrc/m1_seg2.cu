@@ -41,16 +41,14 @@ constexpr int kS2Chunk = 64;   // steps of B/C per staged chunk
 #define B200SCAN_SEG2_RPT 1
 #endif
 constexpr int kS2Rpt = B200SCAN_SEG2_RPT;
-// minimum resident CTAs per SM asked of the compiler: pass 1 at 5 (96
-// registers; its first-segment branch otherwise takes 100 and 4 CTAs) measured
-// 7% faster over the op; pass 2 at 6 (80 registers, spills) 8% slower
+// pass 1 asks the compiler for 5 resident CTAs per SM (96 registers; its
+// first-segment branch otherwise takes 100 and 4 CTAs).  Pass 2 carries no
+// minimum: with an explicit minimum of 1 the compiler spends 196 registers
+// (2 CTAs per SM), without one 86.
 #ifndef B200SCAN_SEG2_MINB1
 #define B200SCAN_SEG2_MINB1 5
 #endif
-#ifndef B200SCAN_SEG2_MINB2
-#define B200SCAN_SEG2_MINB2 1
-#endif
-constexpr int kS2MinBlocks1 = B200SCAN_SEG2_MINB1, kS2MinBlocks2 = B200SCAN_SEG2_MINB2;
+constexpr int kS2MinBlocks1 = B200SCAN_SEG2_MINB1;
 // default share of exps on the FMA pipe (see m1_seg2_kernel): pass 2 (kSeg2Poly)
 // and pass 1 (kSeg2Poly1, the MUFU-bound one); the two passes' decays then
 // differ by the approximations' error (~1e-7 relative), not by design
@@ -127,6 +125,14 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
                                    2 * q + 1 < N ? A[2 * q + 1] * kLog2e : 0.f);
         bias[r] = p.delta_bias ? p.delta_bias[ch] : 0.f;
         dsk[r] = p.d_skip ? p.d_skip[ch] : 0.f;
+    }
+
+    // everything above reads only the op's inputs; under a programmatic
+    // dependent launch the incoming states are the first thing that needs
+    // the carry kernel finished (a no-op otherwise)
+    if (MODE == kSeg2Rescan) griddep_wait();
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
         const float* hi = MODE == kSeg2Rescan ? ws.hin + (static_cast<int64_t>(s) * rows_all + row[r]) * 16
                           : (MODE == kSeg2First && p.h0) ? p.h0 + row[r] * N
                                                         : nullptr;
@@ -278,6 +284,7 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
 template <bool FIRST, bool REV, int POLY>
 __global__ void __launch_bounds__(kS2Rows / kS2Rpt, kS2MinBlocks1) m1_seg2_pass1(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
     __shared__ __align__(16) Seg2Slab sb;
+    griddep_launch_dependents();  // the carry kernel may be scheduled into the tail wave
     const int s = blockIdx.y;
     if (FIRST && s == 0)
         m1_seg2_sweep<kSeg2First, REV, POLY, kS2Rpt>(p, ws, S, Ls, 0, sb);
@@ -287,7 +294,7 @@ __global__ void __launch_bounds__(kS2Rows / kS2Rpt, kS2MinBlocks1) m1_seg2_pass1
 
 // Pass 2: segments 1 .. S-1 from their incoming states.
 template <bool REV, int POLY>
-__global__ void __launch_bounds__(kS2Rows / kS2Rpt, kS2MinBlocks2) m1_seg2_pass2(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
+__global__ void __launch_bounds__(kS2Rows / kS2Rpt) m1_seg2_pass2(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
     __shared__ __align__(16) Seg2Slab sb;
     m1_seg2_sweep<kSeg2Rescan, REV, POLY, kS2Rpt>(p, ws, S, Ls, blockIdx.y + 1, sb);
 }
@@ -300,17 +307,31 @@ template <bool FIRST>
 __global__ void m1_seg2_carry_kernel(M1Params p, Seg2Ws ws, int S) {
     const int64_t rows_all = p.batch * p.dim, N = p.state;
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    griddep_launch_dependents();  // pass 2 may start its prologue
+    griddep_wait();               // pass 1's end states
     if (i >= rows_all * N) return;
     const int64_t row = i / N, n = i % N;
     const float a = p.A[(row % p.dim) * N + n] * kLog2e;
     float h = FIRST ? __ldg(ws.hend + row * 16 + n) : (p.h0 ? p.h0[i] : 0.f);
-    for (int k = FIRST ? 1 : 0; k < S; ++k) {  // segments are already in traversal order
-        const int64_t sr = static_cast<int64_t>(k) * rows_all + row;
-        ws.hin[sr * 16 + n] = h;
-        if (FIRST && k == S - 1) break;
-        const float ds = __ldg(ws.dtsum + sr), he = __ldg(ws.hend + sr * 16 + n);
-        h = fmaf(ex2_approx(a * ds), h, he);
+    // segments are already in traversal order; each group of 8 has all its
+    // loads in flight before the serial combine
+    const int k_end = FIRST ? S - 1 : S;  // segments whose (dtsum, hend) fold in
+    for (int k0 = FIRST ? 1 : 0; k0 < k_end; k0 += 8) {
+        float ds[8], he[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int64_t sr = static_cast<int64_t>(k0 + u) * rows_all + row;
+            ds[u] = k0 + u < k_end ? __ldg(ws.dtsum + sr) : 0.f;
+            he[u] = k0 + u < k_end ? __ldg(ws.hend + sr * 16 + n) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (k0 + u >= k_end) break;
+            ws.hin[(static_cast<int64_t>(k0 + u) * rows_all + row) * 16 + n] = h;
+            h = fmaf(ex2_approx(a * ds[u]), h, he[u]);
+        }
     }
+    if (FIRST && S > 1) ws.hin[(static_cast<int64_t>(S - 1) * rows_all + row) * 16 + n] = h;
     if (!FIRST && p.last_state) p.last_state[i] = h;
 }
 
@@ -370,17 +391,14 @@ cudaError_t m1_seg2_launch(const M1Params& p, int S, cudaStream_t stream) {
     if (e == cudaSuccess && (S > 1 || !first)) {
         const int64_t n = rows * p.state;
         const unsigned cg = static_cast<unsigned>((n + 255) / 256);
-        if (first)
-            m1_seg2_carry_kernel<true><<<cg, 256, 0, stream>>>(p, ws, S);
-        else
-            m1_seg2_carry_kernel<false><<<cg, 256, 0, stream>>>(p, ws, S);
+        e = first ? launch_pdl(m1_seg2_carry_kernel<true>, dim3(cg), dim3(256), stream, p, ws, S)
+                  : launch_pdl(m1_seg2_carry_kernel<false>, dim3(cg), dim3(256), stream, p, ws, S);
         note_launch();
-        e = cudaGetLastError();
     }
     if (e == cudaSuccess && first && S > 1) {
-        k2<<<dim3(grid.x, static_cast<unsigned>(S - 1)), kS2Rows / kS2Rpt, 0, stream>>>(p, ws, S, Ls);
+        e = launch_pdl(k2, dim3(grid.x, static_cast<unsigned>(S - 1)), dim3(kS2Rows / kS2Rpt), stream, p,
+                       ws, S, Ls);
         note_launch();
-        e = cudaGetLastError();
     }
     const cudaError_t ef = cudaFreeAsync(raw, stream);
     return e != cudaSuccess ? e : ef;
