@@ -9,6 +9,7 @@ surface of the reference ``arm_scan`` package (AdityaP9116/ARMHackathon).
     arm_scan.ss2d_scan_mamba3(...) / noncausal_scan(...) / ss2d_noncausal_mamba3(...)
     arm_scan.selective_scan_numpy(...)     # numpy in, numpy out (no torch)
     arm_scan.selective_state_update(state, x, dt, A, B, C, ...)  # one decode step
+    arm_scan.mamba3_mixer_prologue(proj, ...) / mamba3_mixer_scan(proj, ...)  # Mamba-3 mixer
 
 Every scan runs as sm_100a CUDA kernels in libb200scan.so, reached through
 its C ABI (include/b200scan.h).  There is no CPU implementation.
@@ -22,7 +23,8 @@ __all__ = [
     "bidirectional_scan", "ss2d_scan", "use_arm_scan", "mamba3_scan", "mamba3_scan_pair",
     "mamba3_mimo_scan", "ss2d_scan_mamba3", "noncausal_scan", "noncausal_scan_dense",
     "ss2d_noncausal_mamba3", "angles_to_cos_sin", "patch", "unpatch", "stats", "kernel_calls",
-    "selective_state_update", "selective_scan_final_state",
+    "selective_state_update", "selective_scan_final_state", "mamba3_mixer_prologue",
+    "mamba3_mixer_scan",
 ]
 
 _LAZY = {
@@ -35,6 +37,7 @@ _LAZY = {
     "ss2d_scan_mamba3": ".ss2d_mamba3",
     "noncausal_scan": ".mamba3_noncausal", "noncausal_scan_dense": ".mamba3_noncausal",
     "ss2d_noncausal_mamba3": ".mamba3_noncausal",
+    "mamba3_mixer_prologue": ".mamba3_mixer", "mamba3_mixer_scan": ".mamba3_mixer",
     "patch": ".hf_patch", "unpatch": ".hf_patch", "stats": ".hf_patch",
 }
 

@@ -20,7 +20,7 @@ import os
 import sys
 from pathlib import Path
 
-ABI_VERSION = 9
+ABI_VERSION = 10
 
 _LIB_NAMES = ["libb200scan.so"]
 
@@ -45,6 +45,11 @@ class ArmScanDims(ctypes.Structure):
 
 class ArmMamba3Dims(ctypes.Structure):
     _fields_ = [(n, ctypes.c_size_t) for n in ("batch", "heads", "dv", "dqk", "len", "rank")]
+
+
+class ArmMamba3MixerDims(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_size_t) for n in ("batch", "len", "heads", "headdim", "d_state",
+                                               "rank", "n_angles")]
 
 
 class ArmMamba3TcOptions(ctypes.Structure):
@@ -112,6 +117,10 @@ def _bind(lib):
         ctypes.POINTER(ArmScanDims), *([_VP] * 9), ctypes.c_int, _VP, _VP]
     lib.arm_scan_kernel_launches.restype = ctypes.c_ulonglong
     lib.arm_scan_kernel_launches.argtypes = []
+    lib.arm_scan_mamba3_mixer_prologue_f32_async.restype = ctypes.c_int
+    lib.arm_scan_mamba3_mixer_prologue_f32_async.argtypes = [
+        ctypes.POINTER(ArmMamba3MixerDims), *([_VP] * 4), ctypes.c_float, ctypes.c_float,
+        *([_VP] * 9)]
     lib.arm_scan_mamba3_siso_tc_async.restype = ctypes.c_int
     lib.arm_scan_mamba3_siso_tc_async.argtypes = [
         ctypes.POINTER(ArmMamba3Dims), ctypes.POINTER(ArmMamba3TcOptions), *([_VP] * 11),
@@ -255,6 +264,15 @@ def state_update_raw(dims, ptr_state, ptr_x, ptr_dt, ptr_a, ptr_b, ptr_c, ptr_d_
         "arm_scan_selective_state_update_f32_async")
 
 
+def mixer_prologue_raw(dims, ptr_proj, ptr_dt_bias, ptr_b_norm_w, ptr_c_norm_w, a_floor, eps,
+                       ptr_z, ptr_x, ptr_q, ptr_k, ptr_dt, ptr_adt, ptr_trap, ptr_angles, stream):
+    """Mamba-3 mixer prologue (device pointers, stream-ordered)."""
+    _check(load().arm_scan_mamba3_mixer_prologue_f32_async(
+        ctypes.byref(dims), ptr_proj, ptr_dt_bias, ptr_b_norm_w, ptr_c_norm_w, float(a_floor),
+        float(eps), ptr_z, ptr_x, ptr_q, ptr_k, ptr_dt, ptr_adt, ptr_trap, ptr_angles,
+        _n(stream)), "arm_scan_mamba3_mixer_prologue_f32_async")
+
+
 def kernel_launches():
     """GPU kernels the library has launched in this process so far."""
     return int(load().arm_scan_kernel_launches())
@@ -277,7 +295,8 @@ def exported_symbols():
             "arm_scan_mamba3_angles_f32_noalloc", "arm_scan_tensor_status",
             "arm_scan_mamba3_siso_tc_async", "arm_scan_kernel_launches",
             "arm_scan_selective_state_update_f32_async",
-            "arm_scan_selective_scan_final_state_f32_async", "arm_scan_mamba3_ss2d_f32_async"]
+            "arm_scan_selective_scan_final_state_f32_async", "arm_scan_mamba3_ss2d_f32_async",
+            "arm_scan_mamba3_mixer_prologue_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

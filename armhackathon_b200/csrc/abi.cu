@@ -17,6 +17,7 @@
 
 #include "../../include/b200scan.h"
 #include "m1_scan.h"
+#include "m3_mixer.h"
 #include "m3_angles.h"
 #include "m3_scan.h"
 
@@ -700,6 +701,54 @@ int arm_scan_selective_state_update_f32_async(const ArmScanDims* dims, float* st
 }
 
 unsigned long long arm_scan_kernel_launches(void) { return b200scan::g_kernel_launches.load(); }
+
+int arm_scan_mamba3_mixer_prologue_f32_async(const ArmMamba3MixerDims* dims, const float* proj,
+                                             const float* dt_bias, const float* b_norm_weight,
+                                             const float* c_norm_weight, float a_floor, float eps,
+                                             float* z, float* x, float* q, float* k, float* dt,
+                                             float* adt, float* trap, float* angles, void* stream) {
+    const void* req[] = {dims, proj, dt_bias, b_norm_weight, c_norm_weight, z, x, q, k, dt, adt,
+                         trap, angles};
+    for (const void* r : req)
+        if (!r) return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    if (!dims->heads || !dims->headdim || !dims->d_state || !dims->rank)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "heads, headdim, d_state and rank must be non-zero");
+    if (dims->n_angles > dims->d_state / 2)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "n_angles (%zu) exceeds d_state / 2 (%zu)",
+                    dims->n_angles, dims->d_state / 2);
+    size_t hp = 0, rn = 0, rows = 0;
+    if (!mul3(dims->heads, dims->headdim, 1, &hp) || !mul3(dims->rank, dims->d_state, 1, &rn) ||
+        !mul3(dims->batch, dims->len, 1, &rows))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "element counts overflow");
+    const size_t w = 2 * hp + 2 * rn + 3 * dims->heads + dims->n_angles;
+    size_t total = 0;
+    if (!mul3(rows, w, 1, &total) || total > (size_t(1) << 62))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "element counts overflow");
+    b200scan::MixerParams m{};
+    m.proj = proj;
+    m.dt_bias = dt_bias;
+    m.b_norm_w = b_norm_weight;
+    m.c_norm_w = c_norm_weight;
+    m.a_floor = a_floor;
+    m.eps = eps;
+    m.z = z;
+    m.x = x;
+    m.q = q;
+    m.k = k;
+    m.dt = dt;
+    m.adt = adt;
+    m.trap = trap;
+    m.angles = angles;
+    m.batch = static_cast<int64_t>(dims->batch);
+    m.len = static_cast<int64_t>(dims->len);
+    m.heads = static_cast<int64_t>(dims->heads);
+    m.headdim = static_cast<int64_t>(dims->headdim);
+    m.d_state = static_cast<int64_t>(dims->d_state);
+    m.rank = static_cast<int64_t>(dims->rank);
+    m.n_angles = static_cast<int64_t>(dims->n_angles);
+    const cudaError_t e = b200scan::m3_mixer_prologue_launch(m, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "mamba3 mixer prologue launch");
+}
 
 int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOptions* opts,
                                   const void* q, const void* k, const void* v, const float* adt,

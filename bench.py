@@ -61,6 +61,11 @@ M3_WORKLOADS = {
     "cfg4a": dict(kind="ss2d", batch=8, heads=6, dv=64, dqk=64, len=128 * 128, rank=1, pairs=32,
                   grid=128, desc="BASELINE config 4a: SS2D Mamba-3 SISO 128x128 grid B8 H6 P64 "
                                  "N64 fp32, 4 directions summed"),
+    "m3_mixer": dict(kind="mixer", batch=4, heads=24, dv=64, dqk=128, len=4096, rank=1,
+                     pairs=32, desc="Mamba-3 mixer prologue (in_proj output -> scan inputs: "
+                                    "split, softplus/heavy-tail gates, B/C RMSNorm, relayouts) "
+                                    "at config 2's shape with the checkpoint's 3432-wide in_proj "
+                                    "rows (rope_fraction 0.5: 32 angles), fp32"),
     "cfg4b": dict(kind="bidir", batch=1, dim=1536, len=262144, state=16,
                   desc="BASELINE config 4b: Mamba-1 bidirectional D1536 N16 L262144 fp32, summed"),
 }
@@ -106,6 +111,51 @@ def m3_bytes_bf16(w):
     B, H, P, N, L = w["batch"], w["heads"], w["dv"], w["dqk"], w["len"]
     return (2 * (2 * B * L * N + 2 * B * L * H * P + B * L * w["pairs"])
             + 4 * (3 * B * H * L + B * H * P * N))
+
+
+def mixer_inputs(w, device, seed=0):
+    """Synthetic in_proj output and mixer parameters for the prologue."""
+    import torch
+    from armhackathon_b200.mamba3_mixer import proj_width
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, H, P, N, L, R = w["batch"], w["heads"], w["dv"], w["dqk"], w["len"], w["rank"]
+    W = proj_width(H, P, N, R, w["pairs"])
+    rn = lambda *s: torch.randn(*s, generator=g, device=device)  # noqa: E731
+    return dict(proj=rn(B, L, W), nheads=H, headdim=P, d_state=N, n_angles=w["pairs"],
+                dt_bias=rn(H) - 2, B_norm_weight=1 + 0.1 * rn(N), C_norm_weight=1 + 0.1 * rn(N),
+                mimo_rank=R)
+
+
+def mixer_bytes(w):
+    """Read one in_proj row, write the same number of floats (z, x, q, k,
+    dt, adt, trap, angles), per (batch, step); parameters are negligible."""
+    from armhackathon_b200.mamba3_mixer import proj_width
+    W = proj_width(w["heads"], w["dv"], w["dqk"], w["rank"], w["pairs"])
+    return 2 * 4 * w["batch"] * w["len"] * W
+
+
+def torch_mixer_prologue(proj, nheads, headdim, d_state, n_angles, dt_bias, B_norm_weight,
+                         C_norm_weight, mimo_rank, A_floor=1e-4, eps=1e-5):
+    """The same prologue as separate torch ops on the GPU (how the reference's
+    mixer runs it), for comparison with the fused kernel."""
+    import torch
+    import torch.nn.functional as F
+    b, l, _ = proj.shape
+    hp, rn = nheads * headdim, mimo_rank * d_state
+    z, x, Bm, Cm, ddt, dda, trap, ang = torch.split(
+        proj, [hp, hp, rn, rn, nheads, nheads, nheads, n_angles], dim=-1)
+    a = -(dda.clamp_min(0) + torch.reciprocal(1 - dda.clamp_max(0)))
+    a = a.clamp_max(-A_floor)
+    dt = F.softplus(ddt + dt_bias)
+
+    def rms(t, wt):
+        t = t.reshape(b, l, mimo_rank, d_state)
+        return t * torch.rsqrt(t.square().mean(-1, keepdim=True) + eps) * wt
+    return (z.reshape(b, l, nheads, headdim).contiguous(),
+            x.reshape(b, l, nheads, headdim).contiguous(), rms(Cm, C_norm_weight),
+            rms(Bm, B_norm_weight), dt.permute(0, 2, 1).contiguous(),
+            (a * dt).permute(0, 2, 1).contiguous(), trap.permute(0, 2, 1).contiguous(),
+            ang.contiguous())
 
 
 def run_m3(args, w):
@@ -160,6 +210,8 @@ def run_m3(args, w):
                                              "all_gather of segment carries per call"}),
                   flush=True)
         return
+    elif w["kind"] == "mixer":
+        return run_mixer(args, w, dev)
     else:
         x = m3_inputs(w, dev)
         nbytes = m3_bytes(w)
@@ -200,6 +252,52 @@ def run_m3(args, w):
                       "bytes_per_step": nbytes,
                       "note": "whole op incl. the torch angle pre-pass and output permute"}),
           flush=True)
+
+
+def run_mixer(args, w, dev):
+    """The fused Mamba-3 mixer prologue: HBM roofline of the one kernel, the
+    same prologue as separate torch ops, and prologue + fp32 scan."""
+    import torch
+    import armhackathon_b200 as arm
+    from armhackathon_b200 import _ffi
+    x = mixer_inputs(w, dev)
+    nbytes = mixer_bytes(w)
+    H, N = w["heads"], w["dqk"]
+    scan_kw = dict(D=torch.ones(H, device=dev), B_bias=torch.zeros(H, 1, N, device=dev),
+                   C_bias=torch.zeros(H, 1, N, device=dev))
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / steps
+
+    n0 = _ffi.kernel_launches()
+    with ClockSampler(dev.index or 0) as clk:
+        ms = timed(lambda: arm.mamba3_mixer_prologue(**x), args.steps)
+    clocks = clk.summary()
+    per_call = (_ffi.kernel_launches() - n0) / (args.warmup + args.steps)
+    launches = int(round(per_call * args.steps))  # kernels in the timed region
+    torch_ms = timed(lambda: torch_mixer_prologue(**x), args.steps)
+    full_ms = timed(lambda: arm.mamba3_mixer_scan(**x, **scan_kw), max(1, args.steps // 5))
+    peak, peak_kind = peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": METRIC, "workload": args.workload, "desc": w["desc"], "ms_per_step": ms,
+        "value": gbs, "unit": "GB/s", "bytes_per_step": nbytes, "dtype": "f32",
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "peak_source": peak_kind},
+        "gpu_launches": launches, "clocks": clocks,
+        "torch_ops_ms": torch_ms, "prologue_plus_fp32_scan_ms": full_ms,
+        "l2": "inputs larger than L2",
+        "note": "the prologue alone (one kernel, CUDA events); torch_ops_ms = the same "
+                "prologue as separate torch ops on this GPU"}), flush=True)
 
 
 def peaks():

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define ARM_SCAN_ABI_VERSION 9u
+#define ARM_SCAN_ABI_VERSION 10u
 
 /* Return codes (0-5: reference arm-scan-ffi/src/lib.rs:53-58). */
 #define ARM_SCAN_OK 0
@@ -268,6 +268,38 @@ int arm_scan_tensor_status(void);
  * kernels this library has launched in the process so far (all devices,
  * all threads); the difference around a call is that call's launch count. */
 unsigned long long arm_scan_kernel_launches(void);
+
+/* Extension: shape of the Mamba-3 mixer whose prologue
+ * arm_scan_mamba3_mixer_prologue_f32_async runs (one B/C group; rank 1 for
+ * SISO).  The in_proj row is W = 2*heads*headdim + 2*rank*d_state + 3*heads
+ * + n_angles floats wide (apps/mamba3_lm/block.py:116-121). */
+typedef struct ArmMamba3MixerDims {
+    size_t batch;
+    size_t len;
+    size_t heads;
+    size_t headdim;
+    size_t d_state;
+    size_t rank;
+    size_t n_angles;
+} ArmMamba3MixerDims;
+
+/* Extension (reference apps/mamba3_lm/block.py:146-177, Mamba3Mixer.forward
+ * between in_proj and the scan, in torch there): one pass over the in_proj
+ * output proj (batch, len, W), fp32, writing the scan's inputs:
+ *   z, x       (batch, len, heads, headdim)  the first two slices, contiguous
+ *   q, k       (batch, len, rank, d_state)   RMSNorm(C) * c_norm_weight and
+ *              RMSNorm(B) * b_norm_weight, rstd = 1/sqrt(mean(v^2) + eps)
+ *   dt, adt    (batch, heads, len)           dt = softplus(dd_dt + dt_bias)
+ *              (threshold 20), adt = min(-heavy_tail(dd_A), -a_floor) * dt,
+ *              heavy_tail(v) = max(v, 0) + 1 / (1 - min(v, 0))
+ *   trap       (batch, heads, len)           the pre-sigmoid slice, transposed
+ *   angles     (batch, len, n_angles)        the last slice, contiguous
+ * Device pointers, stream-ordered; none nullable.  n_angles <= d_state / 2. */
+int arm_scan_mamba3_mixer_prologue_f32_async(const ArmMamba3MixerDims* dims, const float* proj,
+                                             const float* dt_bias, const float* b_norm_weight,
+                                             const float* c_norm_weight, float a_floor, float eps,
+                                             float* z, float* x, float* q, float* k, float* dt,
+                                             float* adt, float* trap, float* angles, void* stream);
 
 #ifdef __cplusplus
 }

@@ -133,6 +133,38 @@ def angles_to_cos_sin(angles, dt, half):
     return cos, sin
 
 
+def m3_mixer_prologue(proj, heads, headdim, d_state, rank, n_angles, dt_bias, B_norm_weight,
+                      C_norm_weight, A_floor, eps):
+    """Mamba-3 mixer prologue, apps/mamba3_lm/block.py:146-177, in float64.
+
+    proj (b, l, W), one B/C group, split as block.py:116-121 / 150-151;
+    heavy_tail (52-62), clamp (165), softplus (166, threshold 20), ADT (167),
+    (b, l, h) -> (b, h, l) transposes (158, 168-169), RMSNorm (78-82; eps
+    inside the sqrt) of B (-> k) and C (-> q).  Returns a dict of z, x
+    (b, l, h, p), q, k (b, l, r, n), dt, adt, trap (b, h, l), angles (b, l, a).
+    """
+    proj = np.asarray(proj, np.float64)
+    b, l, _ = proj.shape
+    hp, rn = heads * headdim, rank * d_state
+    cuts = np.cumsum([hp, hp, rn, rn, heads, heads, heads])
+    z, x, B, C, dd_dt, dd_A, trap, ang = np.split(proj, cuts, axis=-1)
+    neg, pos = np.minimum(dd_A, 0.0), np.maximum(dd_A, 0.0)
+    A = np.minimum(-(pos + 1.0 / (1.0 - neg)), -float(A_floor))
+    v = dd_dt + np.asarray(dt_bias, np.float64)
+    dt = np.where(v > 20.0, v, np.log1p(np.exp(np.minimum(v, 20.0))))
+    adt = A * dt
+
+    def rms(t, w):
+        t = t.reshape(b, l, rank, d_state)
+        rstd = 1.0 / np.sqrt(np.mean(t * t, axis=-1, keepdims=True) + float(eps))
+        return t * rstd * np.asarray(w, np.float64)
+
+    tr = lambda t: np.ascontiguousarray(np.transpose(t, (0, 2, 1)))  # noqa: E731
+    return dict(z=z.reshape(b, l, heads, headdim), x=x.reshape(b, l, heads, headdim),
+                q=rms(C, C_norm_weight), k=rms(B, B_norm_weight), dt=tr(dt), adt=tr(adt),
+                trap=tr(trap), angles=ang)
+
+
 def m3_siso(q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, D=None, z=None,
             reverse=False, dtype=np.float64, nthreads=1, want_state=False):
     """Mamba-3 SISO scan (kernel/arm-scan-core/src/mamba3/scalar.rs:50-196).

@@ -30,6 +30,14 @@ What is produced, per family:
   cut to ``MIMO_MAX_L`` tokens the same way, plus ``ref_f64`` from
   ``mamba3_mimo_ref`` (mamba3_ref.py:305).
 
+* ``m3_mixer/<case>.npz`` -- the Mamba-3 mixer's prologue (everything between
+  ``in_proj`` and the scan call, apps/mamba3_lm/block.py:146-177) run by the
+  reference's own ``Mamba3Mixer`` on seeded random weights and inputs: its
+  scan entry (``arm_scan.mamba3_scan`` / ``mamba3_mimo_scan``) is replaced by
+  a stub that records the arguments it receives.  Stored: the ``in_proj``
+  output ``proj``, the mixer's parameters, and the recorded q, k, v, z, adt,
+  dt, trap and (head 0 of the broadcast) angles.
+
 Usage:  python tests/golden/make_fixtures.py [--ref /path/to/reference]
 """
 
@@ -175,6 +183,65 @@ def make_m3(ref):
     return names
 
 
+MIXER_CASES = {
+    # name: (Mamba3Mixer kwargs, batch, len, seed)
+    "siso_rope_half": (dict(d_model=64, d_state=16, expand=2, headdim=16, rope_fraction=0.5), 2, 33, 1),
+    "siso_rope_full": (dict(d_model=48, d_state=32, expand=2, headdim=8, rope_fraction=1.0), 1, 70, 2),
+    "mimo_r2": (dict(d_model=64, d_state=16, expand=2, headdim=16, rope_fraction=0.5,
+                     is_mimo=True, mimo_rank=2), 2, 21, 3),
+    "mimo_r4": (dict(d_model=32, d_state=8, expand=2, headdim=8, rope_fraction=1.0,
+                     is_mimo=True, mimo_rank=4, A_floor=0.05), 1, 40, 4),
+}
+
+
+def make_mixer(ref):
+    import torch
+    sys.path.insert(0, str(ref / "python"))
+    sys.path.insert(0, str(ref))
+    from apps.mamba3_lm import block  # noqa: E402
+
+    seen = {}
+
+    def record(**kw):
+        seen.clear()
+        seen.update(kw)
+        return torch.zeros_like(kw["v"])
+
+    block.arm_scan.mamba3_scan = record
+    block.arm_scan.mamba3_mimo_scan = record
+    names = []
+    for name, (kw, b, l, seed) in MIXER_CASES.items():
+        torch.manual_seed(seed)
+        mix = block.Mamba3Mixer(**kw).float()
+        with torch.no_grad():
+            # the parameters' inits are constants; random values exercise them
+            for prm in (mix.dt_bias, mix.D, mix.B_bias, mix.C_bias, mix.B_norm.weight,
+                        mix.C_norm.weight):
+                prm.copy_(torch.randn_like(prm) * 0.5 + 1.0)
+            mix.in_proj.weight.mul_(3.0)  # dd_A on both sides of heavy_tail's kink
+            u = torch.randn(b, l, kw["d_model"])
+            proj = mix.in_proj(u)
+            mix(u)
+        r = mix.mimo_rank
+        q = seen["q"].reshape(b, l, r, -1) if r > 1 else seen["q"].reshape(b, l, -1)
+        k = seen["k"].reshape(b, l, r, -1) if r > 1 else seen["k"].reshape(b, l, -1)
+        arrays = dict(
+            proj=proj, dt_bias=mix.dt_bias, B_norm_weight=mix.B_norm.weight,
+            C_norm_weight=mix.C_norm.weight, A_floor=torch.tensor(mix.A_floor),
+            eps=torch.tensor(mix.B_norm.eps), heads=torch.tensor(mix.nheads),
+            headdim=torch.tensor(mix.headdim), d_state=torch.tensor(mix.d_state),
+            rank=torch.tensor(r), n_angles=torch.tensor(mix.num_rope_angles),
+            D=mix.D, q_bias=seen["q_bias"], k_bias=seen["k_bias"],
+            q=q, k=k, v=seen["v"], z=seen["z"], adt=seen["adt"], dt=seen["dt"],
+            trap=seen["trap"], angles=seen["angles"][:, :, 0, :])
+        if r > 1:
+            arrays.update(psi=seen["psi"], zeta=seen["zeta"], phi=seen["phi"])
+        _save(HERE / "m3_mixer" / f"{name}.npz",
+              **{k: np.ascontiguousarray(v.detach().float().numpy()) for k, v in arrays.items()})
+        names.append(name)
+    return names
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("ARM_SCAN_REFERENCE"),
@@ -191,6 +258,7 @@ def main():
         "m1_2d": make_m1_2d(ref),
     }
     index.update({f"m3_{k}": v for k, v in make_m3(ref).items()})
+    index["m3_mixer"] = make_mixer(ref)
     (HERE / "index.json").write_text(json.dumps(index, indent=1) + "\n")
     print(json.dumps({k: (len(v) if isinstance(v, list) else v)
                       for k, v in index.items()}))

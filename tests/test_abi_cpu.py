@@ -21,9 +21,9 @@ def declared_functions():
     return sorted(set(re.findall(r"\b(arm_scan_[a-z0-9_]+)\s*\(", text)))
 
 
-def test_library_loads_with_abi_v9():
+def test_library_loads_with_abi_v10():
     lib = _ffi.load()
-    assert lib.arm_scan_abi_version() == 9
+    assert lib.arm_scan_abi_version() == 10
     assert _ffi.lib_path().name == "libb200scan.so"
 
 
@@ -156,3 +156,19 @@ def test_state_update_argument_rules():
     assert call(_ffi.ArmScanDims(1, 4, 1, 4, 1), null_state=True) == 1
     assert call(_ffi.ArmScanDims(0, 4, 1, 4, 1)) == 2
     assert call(_ffi.ArmScanDims(1, 6, 1, 4, 4)) == 2   # dim not a multiple of groups
+
+
+def test_mixer_prologue_argument_rules():
+    """arm_scan_mamba3_mixer_prologue_f32_async: host checks before any
+    device work (dummy pointers never dereferenced)."""
+    lib = _ffi.load()
+    p = ctypes.c_void_p(16)
+
+    def call(dims, null_proj=False):
+        return lib.arm_scan_mamba3_mixer_prologue_f32_async(
+            ctypes.byref(dims), None if null_proj else p, p, p, p, ctypes.c_float(1e-4),
+            ctypes.c_float(1e-5), p, p, p, p, p, p, p, p, None)
+    assert call(_ffi.ArmMamba3MixerDims(1, 4, 2, 8, 16, 1, 4), null_proj=True) == 1
+    assert call(_ffi.ArmMamba3MixerDims(1, 4, 0, 8, 16, 1, 4)) == 2   # no heads
+    assert call(_ffi.ArmMamba3MixerDims(1, 4, 2, 8, 16, 1, 9)) == 2   # n_angles > d_state / 2
+    assert call(_ffi.ArmMamba3MixerDims(1, 1 << 62, 2, 8, 16, 1, 4)) == 2  # overflow

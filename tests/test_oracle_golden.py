@@ -11,6 +11,9 @@ Gates restate the reference's own:
   tests/verify_golden_mamba3.py:50-82, verify_golden_mamba3_mimo.py:129),
   and agreement with the reference's own f64 oracle outputs stored in the
   fixtures (forward, reverse and final state).
+* Mamba-3 mixer prologue: the scan arguments the reference's own
+  Mamba3Mixer.forward produced from a recorded in_proj output
+  (apps/mamba3_lm/block.py:146-199), to f32 rounding.
 """
 
 import json
@@ -26,6 +29,20 @@ M1_CASES = json.loads((GOLDEN / "index.json").read_text())["m1"]
 M1_2D = json.loads((GOLDEN / "index.json").read_text())["m1_2d"]
 SISO = json.loads((GOLDEN / "index.json").read_text())["m3_siso"]
 MIMO = json.loads((GOLDEN / "index.json").read_text())["m3_mimo"]
+MIXER = json.loads((GOLDEN / "index.json").read_text())["m3_mixer"]
+
+# oracle output name -> fixture name (the scan receives x as v)
+MIXER_KEYS = (("z", "z"), ("x", "v"), ("q", "q"), ("k", "k"), ("dt", "dt"), ("adt", "adt"),
+              ("trap", "trap"), ("angles", "angles"))
+
+
+def load_mixer(name):
+    d = np.load(GOLDEN / "m3_mixer" / f"{name}.npz")
+    i = lambda k: int(d[k].reshape(-1)[0])  # noqa: E731
+    dims = dict(heads=i("heads"), headdim=i("headdim"), d_state=i("d_state"), rank=i("rank"),
+                n_angles=i("n_angles"), A_floor=float(d["A_floor"].reshape(-1)[0]),
+                eps=float(d["eps"].reshape(-1)[0]))
+    return d, dims
 
 
 def load_m1(name):
@@ -196,3 +213,21 @@ def test_m3_siso_reverse_is_flip_forward_flip_with_shared_angles():
                          fl(kw["DT"], 2), fl(kw["Trap"], 2), kw["Q_bias"], kw["K_bias"],
                          fl(cos, 1), fl(sin, 1), D=kw["D"], z=fl(kw["Z"], 1))
     np.testing.assert_allclose(rev, np.flip(fwd, 1), rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("name", MIXER)
+def test_m3_mixer_prologue_oracle_vs_reference_block(name):
+    d, dims = load_mixer(name)
+    got = oracle.m3_mixer_prologue(d["proj"], dims["heads"], dims["headdim"], dims["d_state"],
+                                   dims["rank"], dims["n_angles"], d["dt_bias"],
+                                   d["B_norm_weight"], d["C_norm_weight"], dims["A_floor"],
+                                   dims["eps"])
+    for ok, fk in MIXER_KEYS:
+        want = d[fk]
+        g = got[ok].reshape(want.shape)
+        # copies are exact; the arithmetic outputs differ by f32 rounding only
+        assert np.abs(g - want).max() <= 1e-6 * max(1.0, np.abs(want).max()), ok
+    # both branches of heavy_tail and the A_floor clamp are exercised
+    w = 2 * dims["heads"] * dims["headdim"] + 2 * dims["rank"] * dims["d_state"] + dims["heads"]
+    dd_a = d["proj"][..., w:w + dims["heads"]]
+    assert (dd_a > 0).any() and (dd_a < 0).any()
