@@ -48,22 +48,43 @@ __global__ void __launch_bounds__(kMixThreads) m3_mixer_prologue_kernel(MixerPar
     const float* src = p.proj + (b * L + l0) * W;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-    // z, x: rows x 2HP floats, each row's two halves to their own tensors
+    // z, x: each row's first 2HP floats, halves to their own tensors; a
+    // row's columns are spread over the CTA, four loads in flight per thread
     if (VEC) {
-        const int64_t hp4 = HP / 4, n4 = static_cast<int64_t>(rows) * 2 * hp4;
-        for (int64_t i = tid; i < n4; i += kMixThreads) {
-            const int64_t r = i / (2 * hp4), c = i % (2 * hp4);
-            const float4 v = __ldcs(reinterpret_cast<const float4*>(src + r * W) + c);
-            float* dst = c < hp4 ? p.z : p.x;
-            __stcs(reinterpret_cast<float4*>(dst + (b * L + l0 + r) * HP) + (c < hp4 ? c : c - hp4), v);
+        const int hp4 = static_cast<int>(HP / 4);
+        for (int r = 0; r < rows; ++r) {
+            const float4* s4 = reinterpret_cast<const float4*>(src + r * W);
+            float4* z4 = reinterpret_cast<float4*>(p.z + (b * L + l0 + r) * HP);
+            float4* x4 = reinterpret_cast<float4*>(p.x + (b * L + l0 + r) * HP);
+            for (int c0 = tid; c0 < 2 * hp4; c0 += 4 * kMixThreads) {
+                float4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int c = c0 + u * kMixThreads;
+                    if (c < 2 * hp4) v[u] = __ldcs(s4 + c);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int c = c0 + u * kMixThreads;
+                    if (c < hp4)
+                        __stcs(z4 + c, v[u]);
+                    else if (c < 2 * hp4)
+                        __stcs(x4 + (c - hp4), v[u]);
+                }
+            }
         }
     } else {
-        const int64_t n = static_cast<int64_t>(rows) * 2 * HP;
-        for (int64_t i = tid; i < n; i += kMixThreads) {
-            const int64_t r = i / (2 * HP), c = i % (2 * HP);
-            const float v = __ldcs(src + r * W + c);
-            float* dst = c < HP ? p.z : p.x;
-            __stcs(dst + (b * L + l0 + r) * HP + (c < HP ? c : c - HP), v);
+        for (int r = 0; r < rows; ++r) {
+            const float* sr = src + r * W;
+            float* zr = p.z + (b * L + l0 + r) * HP;
+            float* xr = p.x + (b * L + l0 + r) * HP;
+            for (int64_t c = tid; c < 2 * HP; c += kMixThreads) {
+                const float v = __ldcs(sr + c);
+                if (c < HP)
+                    __stcs(zr + c, v);
+                else
+                    __stcs(xr + (c - HP), v);
+            }
         }
     }
 
