@@ -48,31 +48,28 @@ __global__ void __launch_bounds__(kMixThreads) m3_mixer_prologue_kernel(MixerPar
     const float* src = p.proj + (b * L + l0) * W;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-    // z, x: each row's first 2HP floats, halves to their own tensors; the
-    // (row, column) items of the CTA's rows are swept flat, eight loads in
-    // flight per thread before their stores
+    // z, x: each row's first 2HP floats, halves to their own tensors; a
+    // row's columns are spread over the CTA, four loads in flight per thread
     if (VEC) {
-        const int hp4 = static_cast<int>(HP / 4), w2 = 2 * hp4, n_items = rows * w2;
-        for (int i0 = tid; i0 < n_items; i0 += 8 * kMixThreads) {
-            float4 v[8];
+        const int hp4 = static_cast<int>(HP / 4);
+        for (int r = 0; r < rows; ++r) {
+            const float4* s4 = reinterpret_cast<const float4*>(src + r * W);
+            float4* z4 = reinterpret_cast<float4*>(p.z + (b * L + l0 + r) * HP);
+            float4* x4 = reinterpret_cast<float4*>(p.x + (b * L + l0 + r) * HP);
+            for (int c0 = tid; c0 < 2 * hp4; c0 += 4 * kMixThreads) {
+                float4 v[4];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int i = i0 + u * kMixThreads;
-                if (i < n_items) {
-                    const int r = i / w2, c = i - r * w2;
-                    v[u] = __ldcs(reinterpret_cast<const float4*>(src + r * W) + c);
+                for (int u = 0; u < 4; ++u) {
+                    const int c = c0 + u * kMixThreads;
+                    if (c < 2 * hp4) v[u] = __ldcs(s4 + c);
                 }
-            }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int i = i0 + u * kMixThreads;
-                if (i < n_items) {
-                    const int r = i / w2, c = i - r * w2;
-                    const int64_t row = b * L + l0 + r;
+                for (int u = 0; u < 4; ++u) {
+                    const int c = c0 + u * kMixThreads;
                     if (c < hp4)
-                        __stcs(reinterpret_cast<float4*>(p.z + row * HP) + c, v[u]);
-                    else
-                        __stcs(reinterpret_cast<float4*>(p.x + row * HP) + (c - hp4), v[u]);
+                        __stcs(z4 + c, v[u]);
+                    else if (c < 2 * hp4)
+                        __stcs(x4 + (c - hp4), v[u]);
                 }
             }
         }
