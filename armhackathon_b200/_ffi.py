@@ -20,7 +20,7 @@ import os
 import sys
 from pathlib import Path
 
-ABI_VERSION = 10
+ABI_VERSION = 11
 
 _LIB_NAMES = ["libb200scan.so"]
 
@@ -117,6 +117,9 @@ def _bind(lib):
         ctypes.POINTER(ArmScanDims), *([_VP] * 9), ctypes.c_int, _VP, _VP]
     lib.arm_scan_kernel_launches.restype = ctypes.c_ulonglong
     lib.arm_scan_kernel_launches.argtypes = []
+    lib.arm_scan_selective_scan_bidirectional_sum_f32_async.restype = ctypes.c_int
+    lib.arm_scan_selective_scan_bidirectional_sum_f32_async.argtypes = [
+        ctypes.POINTER(ArmScanDims), *([_VP] * 8), _I, _I, _I, _VP, _VP, _VP, _VP]
     lib.arm_scan_mamba3_mixer_prologue_f32_async.restype = ctypes.c_int
     lib.arm_scan_mamba3_mixer_prologue_f32_async.argtypes = [
         ctypes.POINTER(ArmMamba3MixerDims), *([_VP] * 4), ctypes.c_float, ctypes.c_float,
@@ -273,6 +276,17 @@ def mixer_prologue_raw(dims, ptr_proj, ptr_dt_bias, ptr_b_norm_w, ptr_c_norm_w, 
         _n(stream)), "arm_scan_mamba3_mixer_prologue_f32_async")
 
 
+def scan_bidir_sum_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_d_skip, ptr_z,
+                       ptr_delta_bias, delta_softplus, backend, ptr_out, ptr_last_fwd=0,
+                       ptr_last_bwd=0, *, stream):
+    """Bidirectional Mamba-1 scan summed into one output (device pointers)."""
+    _check(load().arm_scan_selective_scan_bidirectional_sum_f32_async(
+        ctypes.byref(dims), ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, _n(ptr_d_skip), _n(ptr_z),
+        _n(ptr_delta_bias), int(bool(delta_softplus)), BACKENDS[backend], THREADING["auto"],
+        ptr_out, _n(ptr_last_fwd), _n(ptr_last_bwd), _n(stream)),
+        "arm_scan_selective_scan_bidirectional_sum_f32_async")
+
+
 def kernel_launches():
     """GPU kernels the library has launched in this process so far."""
     return int(load().arm_scan_kernel_launches())
@@ -296,7 +310,8 @@ def exported_symbols():
             "arm_scan_mamba3_siso_tc_async", "arm_scan_kernel_launches",
             "arm_scan_selective_state_update_f32_async",
             "arm_scan_selective_scan_final_state_f32_async", "arm_scan_mamba3_ss2d_f32_async",
-            "arm_scan_mamba3_mixer_prologue_f32_async"]
+            "arm_scan_mamba3_mixer_prologue_f32_async",
+            "arm_scan_selective_scan_bidirectional_sum_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

@@ -14,7 +14,7 @@ which is what per-direction mixers do; pass D=None to add it once yourself.
 
 import torch
 
-from .op import selective_scan, selective_scan_bidirectional
+from .op import selective_scan, selective_scan_bidirectional, selective_scan_bidirectional_sum
 
 _MERGES = ("sum", "mean", "concat", "none")
 
@@ -31,6 +31,13 @@ def bidirectional_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None,
     """
     if merge not in _MERGES:
         raise ValueError(f"merge must be one of {_MERGES}, got {merge!r}")
+    if (reverse_params is None and not return_last_state and merge in ("sum", "mean")
+            and u.device.type == "cuda"):
+        # one library call: the traversals share their first pass and the
+        # reverse one sums into the output in place
+        out = selective_scan_bidirectional_sum(
+            u, delta, A, B, C, D=D, z=z, delta_bias=delta_bias, delta_softplus=delta_softplus)
+        return out if merge == "sum" else out.mul_(0.5)
     if reverse_params is None and not return_last_state:
         out_f, out_b = selective_scan_bidirectional(
             u, delta, A, B, C, D=D, z=z, delta_bias=delta_bias,

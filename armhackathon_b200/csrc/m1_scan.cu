@@ -502,11 +502,60 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
     }
 }
 
+// Whether a bidirectional call takes the shared-pass form of the two-pass
+// kernel (default where that kernel applies; B200SCAN_M1_BIDIR_SHARED=0 runs
+// the two traversals as independent scans).
+static int bidir_shared_segments(const M1Params& fwd, int backend) {
+    if (backend == kBackendSequential) return 0;
+    if (const char* v = getenv("B200SCAN_M1_VARIANT"))
+        if (atoi(v) != -1 && atoi(v) != 12) return 0;
+    if (const char* v = getenv("B200SCAN_M1_BIDIR_SHARED"))
+        if (v[0] == '0') return 0;
+    return m1_seg2_segments(fwd);
+}
+
 cudaError_t m1_bidir_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                             cudaStream_t stream) {
+    if (const int S = bidir_shared_segments(fwd, backend)) return m1_seg2_bidir_launch(fwd, bwd, S, stream);
     cudaError_t e = m1_scan_launch(fwd, backend, stream);
     if (e != cudaSuccess) return e;
     return m1_scan_launch(bwd, backend, stream);
+}
+
+namespace {
+__global__ void m1_add_kernel(float* __restrict__ out, const float* __restrict__ other, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] += other[i];
+}
+}  // namespace
+
+cudaError_t m1_bidir_sum_launch(const M1Params& fwd, const M1Params& bwd, int backend,
+                                cudaStream_t stream) {
+    // fwd.out receives the sum; bwd.out is ignored
+    if (const int S = bidir_shared_segments(fwd, backend)) {
+        M1Params r = bwd;
+        r.out = fwd.out;
+        r.out_acc = 1;
+        return m1_seg2_bidir_launch(fwd, r, S, stream);
+    }
+    const int64_t n = fwd.batch * fwd.dim * fwd.len;
+    cudaMemPool_t pool = nullptr;
+    cudaError_t e = device_workspace_pool(&pool);
+    if (e != cudaSuccess) return e;
+    void* tmp = nullptr;
+    e = cudaMallocFromPoolAsync(&tmp, static_cast<size_t>(n) * sizeof(float), pool, stream);
+    if (e != cudaSuccess) return e;
+    M1Params r = bwd;
+    r.out = static_cast<float*>(tmp);
+    e = m1_bidir_launch(fwd, r, backend, stream);
+    if (e == cudaSuccess) {
+        m1_add_kernel<<<148 * 8, 256, 0, stream>>>(fwd.out, r.out, n);
+        note_launch();
+        e = cudaGetLastError();
+    }
+    const cudaError_t ef = cudaFreeAsync(tmp, stream);
+    return e != cudaSuccess ? e : ef;
 }
 
 }  // namespace b200scan

@@ -32,6 +32,9 @@ struct M1Params {
     // with len_full 0: the plain layout.  out == nullptr: state only.
     int64_t seg_count = 1;
     int64_t len_full = 0;
+    // Two-pass kernel only: add y to what out already holds (the second
+    // traversal of a bidirectional scan summed in place).
+    int out_acc = 0;
 };
 
 bool m1_pointers_aligned16(const M1Params& p);
@@ -49,6 +52,14 @@ cudaError_t m1_decode_launch(const M1Params& p, float* state, cudaStream_t strea
 // Fold-free two-pass segmented kernel (m1_seg2.cu): segment count (0: not
 // applicable) and launcher.
 int m1_seg2_segments(const M1Params& p);
+// Both traversals of one bidirectional scan with the two-pass kernel (bwd is
+// fwd with reverse = 1 and its own out / last_state; bwd.out_acc sums into
+// fwd.out).
+// Bidirectional scan summed into fwd.out (bwd.out unused).
+cudaError_t m1_bidir_sum_launch(const M1Params& fwd, const M1Params& bwd, int backend,
+                                cudaStream_t stream);
+cudaError_t m1_seg2_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S,
+                                 cudaStream_t stream);
 cudaError_t m1_seg2_launch(const M1Params& p, int segments, cudaStream_t stream);
 // Segments of a time-split Mamba-1 scan (1: no split) and its launcher.
 int m1_timesplit_segments(const M1Params& p);

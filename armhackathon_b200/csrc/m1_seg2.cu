@@ -84,6 +84,9 @@ enum Seg2Mode {
     kSeg2State = 0,  // from zero: end state + sum of dt
     kSeg2Rescan = 1, // from h_in: y (and last_state on the last segment)
     kSeg2First = 2,  // from h0: y, and the true end state into hend
+    kSeg2Bidir = 3,  // from zero, walking forward: the end state and, for the
+                     // reverse traversal of the same inputs, the segment's
+                     // aggregate from zero (see m1_seg2_pass1_bidir)
 };
 
 using Seg2Slab = float[2][2][kS2Chunk * kS2Stride];  // [buf][B, C][step][state]
@@ -96,8 +99,9 @@ using Seg2Slab = float[2][2][kS2Chunk * kS2Stride];  // [buf][B, C][step][state]
 // FMA pipe (exp2_poly2).
 template <int MODE, bool REV, int POLY, int RPT>
 __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& ws, int S, int64_t Ls,
-                                              int s, Seg2Slab& sb) {
-    constexpr bool FULL = MODE != kSeg2State;
+                                              int s, Seg2Slab& sb, const Seg2Ws* wsb = nullptr) {
+    constexpr bool FULL = MODE != kSeg2State && MODE != kSeg2Bidir;
+    constexpr bool BID = MODE == kSeg2Bidir;
     constexpr int T = kS2Rows / RPT;  // threads
     const int N = static_cast<int>(p.state);
     const int64_t L = p.len, D = p.dim, G = p.groups, gsz = D / G;
@@ -111,6 +115,9 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
     int64_t row[RPT];
     bool active[RPT];
     float2 a2[RPT][8], h[RPT][8];  // this row's A * log2 e; state
+    // BID: running product of the decays since the segment start, and the
+    // reverse traversal's aggregate sum_t P_<t * dt_t u_t B_t
+    float2 pr[RPT][8], hb[RPT][8];
     float bias[RPT], dsk[RPT];
 #pragma unroll
     for (int r = 0; r < RPT; ++r) {
@@ -137,9 +144,12 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
                           : (MODE == kSeg2First && p.h0) ? p.h0 + row[r] * N
                                                         : nullptr;
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
+        for (int q = 0; q < 8; ++q) {
             h[r][q] = hi ? make_float2(2 * q < N ? hi[2 * q] : 0.f, 2 * q + 1 < N ? hi[2 * q + 1] : 0.f)
                          : make_float2(0.f, 0.f);
+            pr[r][q] = make_float2(1.f, 1.f);
+            hb[r][q] = make_float2(0.f, 0.f);
+        }
     }
 
     const float* Bg = p.B + bg * N * L;
@@ -222,8 +232,16 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
                         const float2 x0 = fmul2(dt2[r], a2[r][2 * q4]), x1 = fmul2(dt2[r], a2[r][2 * q4 + 1]);
                         const float2 e0 = poly ? exp2_poly2(x0) : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
                         const float2 e1 = poly ? exp2_poly2(x1) : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
-                        h[r][2 * q4] = ffma2(e0, h[r][2 * q4], fmul2(du2[r], make_float2(bb.x, bb.y)));
-                        h[r][2 * q4 + 1] = ffma2(e1, h[r][2 * q4 + 1], fmul2(du2[r], make_float2(bb.z, bb.w)));
+                        const float2 bu0 = fmul2(du2[r], make_float2(bb.x, bb.y));
+                        const float2 bu1 = fmul2(du2[r], make_float2(bb.z, bb.w));
+                        h[r][2 * q4] = ffma2(e0, h[r][2 * q4], bu0);
+                        h[r][2 * q4 + 1] = ffma2(e1, h[r][2 * q4 + 1], bu1);
+                        if (BID) {
+                            hb[r][2 * q4] = ffma2(pr[r][2 * q4], bu0, hb[r][2 * q4]);
+                            hb[r][2 * q4 + 1] = ffma2(pr[r][2 * q4 + 1], bu1, hb[r][2 * q4 + 1]);
+                            pr[r][2 * q4] = fmul2(pr[r][2 * q4], e0);
+                            pr[r][2 * q4 + 1] = fmul2(pr[r][2 * q4 + 1], e1);
+                        }
                         if (FULL) {
                             y2[r] = ffma2(make_float2(cc.x, cc.y), h[r][2 * q4], y2[r]);
                             y2[r] = ffma2(make_float2(cc.z, cc.w), h[r][2 * q4 + 1], y2[r]);
@@ -244,12 +262,14 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
                 for (int r = 0; r < RPT; ++r) {
                     if (!active[r]) continue;
                     float* orow = p.out + row[r] * L;
-                    if (!REV)
-                        __stcs(reinterpret_cast<float4*>(orow + it),
-                               make_float4(yv[r][0], yv[r][1], yv[r][2], yv[r][3]));
-                    else
-                        __stcs(reinterpret_cast<float4*>(orow + (L - 4 - it)),
-                               make_float4(yv[r][3], yv[r][2], yv[r][1], yv[r][0]));
+                    float4* o4 = reinterpret_cast<float4*>(orow + (REV ? L - 4 - it : it));
+                    float4 y4 = REV ? make_float4(yv[r][3], yv[r][2], yv[r][1], yv[r][0])
+                                    : make_float4(yv[r][0], yv[r][1], yv[r][2], yv[r][3]);
+                    if (p.out_acc) {  // summing into an earlier traversal's output
+                        const float4 o = __ldcs(o4);
+                        y4 = make_float4(o.x + y4.x, o.y + y4.y, o.z + y4.z, o.w + y4.w);
+                    }
+                    __stcs(o4, y4);
                 }
             }
         }
@@ -266,6 +286,17 @@ __device__ __forceinline__ void m1_seg2_sweep(const M1Params& p, const Seg2Ws& w
                 he[2 * q + 1] = h[r][q].y;
             }
             ws.dtsum[static_cast<int64_t>(s) * rows_all + row[r]] = dtsum[r];
+        }
+        if (BID) {
+            // the reverse traversal visits this segment as its (S - 1 - s)-th
+            const int64_t sr = static_cast<int64_t>(S - 1 - s) * rows_all + row[r];
+            float* he = wsb->hend + sr * 16;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                he[2 * q] = hb[r][q].x;
+                he[2 * q + 1] = hb[r][q].y;
+            }
+            wsb->dtsum[sr] = dtsum[r];
         }
         if (FULL && s == S - 1 && p.last_state) {
             float* ls = p.last_state + row[r] * N;
@@ -292,11 +323,26 @@ __global__ void __launch_bounds__(kS2Rows / kS2Rpt, kS2MinBlocks1) m1_seg2_pass1
         m1_seg2_sweep<kSeg2State, REV, POLY, kS2Rpt>(p, ws, S, Ls, s, sb);
 }
 
-// Pass 2: segments 1 .. S-1 from their incoming states.
-template <bool REV, int POLY>
-__global__ void __launch_bounds__(kS2Rows / kS2Rpt) m1_seg2_pass2(M1Params p, Seg2Ws ws, int S, int64_t Ls) {
+// Pass 1 of both traversals of the same inputs (bidirectional scan), one
+// forward walk per segment with every exp computed once: the forward end
+// state from zero as kSeg2State, and the reverse traversal's aggregate of the
+// segment from zero, sum_t (prod_{r<t} exp(dt_r A)) dt_t u_t B_t (the running
+// product needs multiplies only), written at the reverse traversal's segment
+// index into wsb.
+template <int POLY>
+__global__ void __launch_bounds__(kS2Rows / kS2Rpt, kS2MinBlocks1)
+    m1_seg2_pass1_bidir(M1Params p, Seg2Ws ws, Seg2Ws wsb, int S, int64_t Ls) {
     __shared__ __align__(16) Seg2Slab sb;
-    m1_seg2_sweep<kSeg2Rescan, REV, POLY, kS2Rpt>(p, ws, S, Ls, blockIdx.y + 1, sb);
+    griddep_launch_dependents();
+    m1_seg2_sweep<kSeg2Bidir, false, POLY, kS2Rpt>(p, ws, S, Ls, blockIdx.y, sb, &wsb);
+}
+
+// Pass 2: segments s_off .. S-1 from their incoming states.
+template <bool REV, int POLY>
+__global__ void __launch_bounds__(kS2Rows / kS2Rpt) m1_seg2_pass2(M1Params p, Seg2Ws ws, int S, int64_t Ls,
+                                                                  int s_off) {
+    __shared__ __align__(16) Seg2Slab sb;
+    m1_seg2_sweep<kSeg2Rescan, REV, POLY, kS2Rpt>(p, ws, S, Ls, blockIdx.y + s_off, sb);
 }
 
 // FIRST: segment 0's hend is already its true end state (pass 1 ran it from
@@ -397,9 +443,55 @@ cudaError_t m1_seg2_launch(const M1Params& p, int S, cudaStream_t stream) {
     }
     if (e == cudaSuccess && first && S > 1) {
         e = launch_pdl(k2, dim3(grid.x, static_cast<unsigned>(S - 1)), dim3(kS2Rows / kS2Rpt), stream, p,
-                       ws, S, Ls);
+                       ws, S, Ls, 1);
         note_launch();
     }
+    const cudaError_t ef = cudaFreeAsync(raw, stream);
+    return e != cudaSuccess ? e : ef;
+}
+
+// Both traversals of the same inputs: fwd (reverse 0) and bwd (reverse 1)
+// share every input but out / last_state (and out_acc).  One shared pass 1,
+// a carry per direction, a pass 2 per direction over every segment: three
+// exps per (step, state) instead of 2 x 2(S-1)/S.  bwd.out == fwd.out with
+// bwd.out_acc sums the two outputs in place (bwd's pass 2 runs after fwd's).
+cudaError_t m1_seg2_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S,
+                                 cudaStream_t stream) {
+    const int64_t rows = fwd.batch * fwd.dim, Ls = fwd.len / S;
+    cudaMemPool_t pool = nullptr;
+    cudaError_t e = device_workspace_pool(&pool);
+    if (e != cudaSuccess) return e;
+    const size_t st = static_cast<size_t>(S) * rows * 16, per = 2 * st + static_cast<size_t>(S) * rows;
+    void* raw = nullptr;
+    e = cudaMallocFromPoolAsync(&raw, 2 * per * sizeof(float), pool, stream);
+    if (e != cudaSuccess) return e;
+    Seg2Ws wf, wb;
+    wf.hend = static_cast<float*>(raw);
+    wf.hin = wf.hend + st;
+    wf.dtsum = wf.hin + st;
+    wb.hend = wf.hend + per;
+    wb.hin = wb.hend + st;
+    wb.dtsum = wb.hin + st;
+    const int64_t gsz = fwd.dim / fwd.groups;
+    const unsigned gx = static_cast<unsigned>(((gsz + kS2Rows - 1) / kS2Rows) * fwd.batch * fwd.groups);
+    const dim3 grid(gx, static_cast<unsigned>(S)), block(kS2Rows / kS2Rpt);
+    m1_seg2_pass1_bidir<0><<<grid, block, 0, stream>>>(fwd, wf, wb, S, Ls);
+    note_launch();
+    e = cudaGetLastError();
+    const int64_t n = rows * fwd.state;
+    const dim3 cg(static_cast<unsigned>((n + 255) / 256));
+    // the carries end in last_state; pass 2 leaves it alone
+    M1Params f2 = fwd, b2 = bwd;
+    f2.last_state = nullptr;
+    b2.last_state = nullptr;
+    if (e == cudaSuccess) e = launch_pdl(m1_seg2_carry_kernel<false>, cg, dim3(256), stream, fwd, wf, S);
+    if (e == cudaSuccess) note_launch();
+    if (e == cudaSuccess) e = launch_pdl(m1_seg2_carry_kernel<false>, cg, dim3(256), stream, bwd, wb, S);
+    if (e == cudaSuccess) note_launch();
+    if (e == cudaSuccess) e = launch_pdl(m1_seg2_pass2<false, 0>, grid, block, stream, f2, wf, S, Ls, 0);
+    if (e == cudaSuccess) note_launch();
+    if (e == cudaSuccess) e = launch_pdl(m1_seg2_pass2<true, 0>, grid, block, stream, b2, wb, S, Ls, 0);
+    if (e == cudaSuccess) note_launch();
     const cudaError_t ef = cudaFreeAsync(raw, stream);
     return e != cudaSuccess ? e : ef;
 }

@@ -157,6 +157,54 @@ def _(u, delta, a, b, c, d_skip, z, delta_bias, delta_softplus):
     return torch.empty_like(u), torch.empty_like(u)
 
 
+@torch.library.custom_op("arm_scan::selective_scan_bidirectional_sum", mutates_args=())
+def _selective_scan_bidir_sum_op(
+    u: torch.Tensor,
+    delta: torch.Tensor,
+    a: torch.Tensor,
+    b: torch.Tensor,
+    c: torch.Tensor,
+    d_skip: Optional[torch.Tensor],
+    z: Optional[torch.Tensor],
+    delta_bias: Optional[torch.Tensor],
+    delta_softplus: bool,
+) -> torch.Tensor:
+    batch, dim, length = u.shape
+    state = a.shape[1]
+    out = torch.empty_like(u)
+    dims = _ffi.ArmScanDims(batch, dim, length, state, b.shape[1] if b.dim() == 4 else 1)
+    with _on_device(u):
+        _ffi.scan_bidir_sum_raw(
+            dims, u.data_ptr(), delta.data_ptr(), a.data_ptr(), b.data_ptr(), c.data_ptr(),
+            _ptr(d_skip), _ptr(z), _ptr(delta_bias), delta_softplus, "auto", out.data_ptr(),
+            stream=_stream(u))
+    _CALLS["n"] += 1
+    return out
+
+
+@_selective_scan_bidir_sum_op.register_fake
+def _(u, delta, a, b, c, d_skip, z, delta_bias, delta_softplus):
+    return torch.empty_like(u)
+
+
+def selective_scan_bidirectional_sum(u, delta, A, B, C, D=None, z=None, delta_bias=None,
+                                     delta_softplus=False):
+    """out_fwd + out_bwd of ``selective_scan_bidirectional`` in one call, on
+    CUDA tensors: the two traversals share their first pass and the reverse
+    one adds into the output in place."""
+    if u.device.type != "cuda":
+        raise ValueError("selective_scan_bidirectional_sum needs CUDA tensors")
+    batch, dim, length = u.shape
+    state = A.shape[1]
+    dev = u.device
+    B = _bc4(B, batch, state, length)
+    C = _bc4(C, batch, state, length)
+    opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
+    return _selective_scan_bidir_sum_op(
+        _prep(u, dev), _prep(delta, dev), _prep(A, dev), _prep(B, dev), _prep(C, dev),
+        opt(D), opt(z), opt(delta_bias), bool(delta_softplus))
+
+
 def selective_scan_bidirectional(u, delta, A, B, C, D=None, z=None,
                                  delta_bias=None, delta_softplus=False):
     """Forward and backward scans of the same inputs in one call.

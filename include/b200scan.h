@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define ARM_SCAN_ABI_VERSION 10u
+#define ARM_SCAN_ABI_VERSION 11u
 
 /* Return codes (0-5: reference arm-scan-ffi/src/lib.rs:53-58). */
 #define ARM_SCAN_OK 0
@@ -268,6 +268,20 @@ int arm_scan_tensor_status(void);
  * kernels this library has launched in the process so far (all devices,
  * all threads); the difference around a call is that call's launch count. */
 unsigned long long arm_scan_kernel_launches(void);
+
+/* Extension: the bidirectional scan merged by sum, as the reference's
+ * bidirectional_scan(merge="sum") computes it from the two outputs of
+ * arm_scan_selective_scan_bidirectional_f32 (python/arm_scan/bidirectional.py:
+ * 98-175): out = out_fwd + out_bwd, (batch, dim, len).  Same inputs, dims and
+ * codes as the bidirectional entry (backend 0 or 1); last_fwd / last_bwd are
+ * both-or-neither.  Device pointers, stream-ordered.  Where the two-pass
+ * kernel applies, both traversals share their first pass (every exp of it
+ * computed once) and the reverse traversal adds into `out` in place. */
+int arm_scan_selective_scan_bidirectional_sum_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
+    const float* c, const float* d_skip, const float* z, const float* delta_bias,
+    int delta_softplus, int backend, int threading, float* out, float* last_fwd,
+    float* last_bwd, void* stream);
 
 /* Extension: shape of the Mamba-3 mixer whose prologue
  * arm_scan_mamba3_mixer_prologue_f32_async runs (one B/C group; rank 1 for

@@ -21,9 +21,9 @@ def declared_functions():
     return sorted(set(re.findall(r"\b(arm_scan_[a-z0-9_]+)\s*\(", text)))
 
 
-def test_library_loads_with_abi_v10():
+def test_library_loads_with_abi_v11():
     lib = _ffi.load()
-    assert lib.arm_scan_abi_version() == 10
+    assert lib.arm_scan_abi_version() == 11
     assert _ffi.lib_path().name == "libb200scan.so"
 
 

@@ -144,6 +144,61 @@ def test_bidirectional_fused_and_merges():
     assert rel_err(f2.cpu().numpy(), wf) <= REL_TOL and rel_err(b2.cpu().numpy(), wb) <= REL_TOL
 
 
+@pytest.mark.parametrize("segments", ["1", "2", "4", "16"])
+@pytest.mark.parametrize("shape", [(2, 70, 1024, 13, 2), (1, 64, 4096, 16, 1)])
+def test_bidirectional_shared_first_pass(segments, shape, monkeypatch):
+    """The bidirectional entries on lengths the two-pass kernel takes: one
+    forward walk per segment gives both traversals' segment aggregates (the
+    reverse one from running products of the decays), then a carry and a
+    rescan per direction; the sum entry adds the reverse traversal in place.
+    Slowly decaying states so the carries matter; grouped B/C, ragged
+    channel counts, d_state 13; final states through the C entry."""
+    from armhackathon_b200 import _ffi
+    monkeypatch.setenv("B200SCAN_M1_SEG2_S", segments)
+    B, D, L, N, G = shape
+    x = _slow_decay_case(B, D, L, N, seed=L + N)
+    if G > 1:
+        rng = np.random.default_rng(7)
+        x["B"] = rng.standard_normal((B, G, N, L)).astype(np.float32)
+        x["C"] = rng.standard_normal((B, G, N, L)).astype(np.float32)
+    wf, wb, wlf, wlb = oracle.m1_scan_bidir(**x, nthreads=8)
+    a = arm()
+    t = cuda(x)
+    of, ob = a.selective_scan_bidirectional(**t)
+    assert rel_err(of.cpu().numpy(), wf) <= REL_TOL
+    assert rel_err(ob.cpu().numpy(), wb) <= REL_TOL
+    s = a.bidirectional_scan(**t, merge="sum")
+    assert rel_err(s.cpu().numpy(), wf + wb) <= REL_TOL
+    m = a.bidirectional_scan(**t, merge="mean")
+    assert rel_err(m.cpu().numpy(), 0.5 * (wf + wb)) <= REL_TOL
+    lf = torch.empty(B, D, N, device="cuda")
+    lb = torch.empty(B, D, N, device="cuda")
+    out = torch.empty(B, D, L, device="cuda")
+    dims = _ffi.ArmScanDims(B, D, L, N, G)
+    _ffi.scan_bidir_sum_raw(dims, t["u"].data_ptr(), t["delta"].data_ptr(), t["A"].data_ptr(),
+                            t["B"].data_ptr(), t["C"].data_ptr(), t["D"].data_ptr(),
+                            t["z"].data_ptr(), t["delta_bias"].data_ptr(), True, "auto",
+                            out.data_ptr(), lf.data_ptr(), lb.data_ptr(),
+                            stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rel_err(out.cpu().numpy(), wf + wb) <= REL_TOL
+    assert rel_err(lf.cpu().numpy(), wlf) <= REL_TOL
+    assert rel_err(lb.cpu().numpy(), wlb) <= REL_TOL
+
+
+def test_bidirectional_sum_without_shared_pass(monkeypatch):
+    """The sum entry where the traversals run as independent scans (forced,
+    and on a length the two-pass kernel does not take): second output in
+    workspace, then an add kernel."""
+    a = arm()
+    for env, L in (("0", 1024), ("1", 777)):
+        monkeypatch.setenv("B200SCAN_M1_BIDIR_SHARED", env)
+        x = random_case(2, 64, L, 16, seed=9)
+        wf, wb, _, _ = oracle.m1_scan_bidir(**x, nthreads=8)
+        s = a.bidirectional_scan(**cuda(x), merge="sum")
+        assert rel_err(s.cpu().numpy(), wf + wb) <= REL_TOL
+
+
 def test_ss2d_golden_planes():
     a = arm()
     for name in json.loads((GOLDEN / "index.json").read_text())["m1_2d"]:
