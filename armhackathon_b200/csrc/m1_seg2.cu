@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(kS2Rows / kS2Rpt, kS2MinBlocks1) m1_seg2_pass1
 // product needs multiplies only), written at the reverse traversal's segment
 // index into wsb.
 template <int POLY>
-__global__ void __launch_bounds__(kS2Rows / kS2Rpt, kS2MinBlocks1)
+__global__ void __launch_bounds__(kS2Rows / kS2Rpt, 4)  // 32 more live registers: 4 CTAs
     m1_seg2_pass1_bidir(M1Params p, Seg2Ws ws, Seg2Ws wsb, int S, int64_t Ls) {
     __shared__ __align__(16) Seg2Slab sb;
     griddep_launch_dependents();
