@@ -71,6 +71,15 @@ def ss2d_scan(u, delta, A, B, C, D=None, delta_bias=None, delta_softplus=True,
             return v.reshape(2 * bb, g, n, hh * ww)
         return grid_to_views(t)
 
+    if scan_pair is scan_pair_arm and merge != "none" and u.device.type == "cuda":
+        # one library call sums each ordering's two traversals in place
+        from .op import selective_scan_bidirectional_sum
+        both = selective_scan_bidirectional_sum(
+            grid_to_views(u), grid_to_views(delta), A, _views(B), _views(C), D=D,
+            delta_bias=delta_bias, delta_softplus=delta_softplus)
+        row_s, col_s = views_to_grid(both[:b], both[b:], h, w)
+        out = row_s + col_s
+        return out if merge == "sum" else out * 0.25
     fwd, bwd = scan_pair(grid_to_views(u), grid_to_views(delta), A, _views(B), _views(C),
                          D=D, delta_bias=delta_bias, delta_softplus=delta_softplus)
     row_f, col_f = views_to_grid(fwd[:b], fwd[b:], h, w)

@@ -209,6 +209,12 @@ def test_ss2d_golden_planes():
         for key, got in zip(("out_row_fwd", "out_row_bwd", "out_col_fwd", "out_col_bwd"), planes):
             err = np.abs(got.cpu().numpy().astype(np.float64) - d[key]).max()
             assert err < 1e-4, (name, key, err)
+        want = sum(d[k] for k in ("out_row_fwd", "out_row_bwd", "out_col_fwd", "out_col_bwd"))
+        for merge, scale in (("sum", 1.0), ("mean", 0.25)):
+            got = a.ss2d_scan(t("u"), t("delta"), t("A"), t("B"), t("C"), D=t("D"),
+                              delta_bias=t("delta_bias"), merge=merge)
+            err = np.abs(got.cpu().numpy().astype(np.float64) - scale * want).max()
+            assert err < 4e-4, (name, merge, err)
 
 
 def test_config0_full_size_properties():
