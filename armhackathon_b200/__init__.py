@@ -24,7 +24,7 @@ __all__ = [
     "mamba3_mimo_scan", "ss2d_scan_mamba3", "noncausal_scan", "noncausal_scan_dense",
     "ss2d_noncausal_mamba3", "angles_to_cos_sin", "patch", "unpatch", "stats", "kernel_calls",
     "selective_state_update", "selective_scan_final_state", "mamba3_mixer_prologue",
-    "selective_scan_bidirectional_sum",
+    "selective_scan_bidirectional_sum", "selective_scan_bidirectional_final_states",
     "mamba3_mixer_scan",
 ]
 
@@ -32,6 +32,7 @@ _LAZY = {
     "selective_scan": ".op", "selective_scan_bidirectional": ".op", "kernel_calls": ".op",
     "selective_state_update": ".op", "selective_scan_final_state": ".op",
     "selective_scan_bidirectional_sum": ".op",
+    "selective_scan_bidirectional_final_states": ".op",
     "bidirectional_scan": ".bidirectional",
     "ss2d_scan": ".ss2d", "use_arm_scan": ".ss2d",
     "mamba3_scan": ".mamba3", "mamba3_scan_pair": ".mamba3", "mamba3_mimo_scan": ".mamba3",

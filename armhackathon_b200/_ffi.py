@@ -119,7 +119,10 @@ def _bind(lib):
     lib.arm_scan_kernel_launches.argtypes = []
     lib.arm_scan_selective_scan_bidirectional_sum_f32_async.restype = ctypes.c_int
     lib.arm_scan_selective_scan_bidirectional_sum_f32_async.argtypes = [
-        ctypes.POINTER(ArmScanDims), *([_VP] * 8), _I, _I, _I, _VP, _VP, _VP, _VP]
+        ctypes.POINTER(ArmScanDims), *([_VP] * 8), _I, _I, _I, _VP, _VP, _VP, _VP, _VP, _VP]
+    lib.arm_scan_selective_scan_bidirectional_final_states_f32_async.restype = ctypes.c_int
+    lib.arm_scan_selective_scan_bidirectional_final_states_f32_async.argtypes = [
+        ctypes.POINTER(ArmScanDims), *([_VP] * 6), _I, _I, _VP, _VP, _VP]
     lib.arm_scan_mamba3_mixer_prologue_f32_async.restype = ctypes.c_int
     lib.arm_scan_mamba3_mixer_prologue_f32_async.argtypes = [
         ctypes.POINTER(ArmMamba3MixerDims), *([_VP] * 4), ctypes.c_float, ctypes.c_float,
@@ -278,13 +281,22 @@ def mixer_prologue_raw(dims, ptr_proj, ptr_dt_bias, ptr_b_norm_w, ptr_c_norm_w, 
 
 def scan_bidir_sum_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_d_skip, ptr_z,
                        ptr_delta_bias, delta_softplus, backend, ptr_out, ptr_last_fwd=0,
-                       ptr_last_bwd=0, *, stream):
+                       ptr_last_bwd=0, ptr_h0_fwd=0, ptr_h0_bwd=0, *, stream):
     """Bidirectional Mamba-1 scan summed into one output (device pointers)."""
     _check(load().arm_scan_selective_scan_bidirectional_sum_f32_async(
         ctypes.byref(dims), ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, _n(ptr_d_skip), _n(ptr_z),
         _n(ptr_delta_bias), int(bool(delta_softplus)), BACKENDS[backend], THREADING["auto"],
-        ptr_out, _n(ptr_last_fwd), _n(ptr_last_bwd), _n(stream)),
-        "arm_scan_selective_scan_bidirectional_sum_f32_async")
+        ptr_out, _n(ptr_last_fwd), _n(ptr_last_bwd), _n(ptr_h0_fwd), _n(ptr_h0_bwd),
+        _n(stream)), "arm_scan_selective_scan_bidirectional_sum_f32_async")
+
+
+def bidir_states_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_delta_bias,
+                     delta_softplus, backend, ptr_last_fwd, ptr_last_bwd, *, stream):
+    """Final states of both traversals of a bidirectional scan (device pointers)."""
+    _check(load().arm_scan_selective_scan_bidirectional_final_states_f32_async(
+        ctypes.byref(dims), ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, _n(ptr_delta_bias),
+        int(bool(delta_softplus)), BACKENDS[backend], ptr_last_fwd, ptr_last_bwd, _n(stream)),
+        "arm_scan_selective_scan_bidirectional_final_states_f32_async")
 
 
 def kernel_launches():
@@ -311,7 +323,8 @@ def exported_symbols():
             "arm_scan_selective_state_update_f32_async",
             "arm_scan_selective_scan_final_state_f32_async", "arm_scan_mamba3_ss2d_f32_async",
             "arm_scan_mamba3_mixer_prologue_f32_async",
-            "arm_scan_selective_scan_bidirectional_sum_f32_async"]
+            "arm_scan_selective_scan_bidirectional_sum_f32_async",
+            "arm_scan_selective_scan_bidirectional_final_states_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

@@ -618,7 +618,7 @@ int arm_scan_selective_scan_bidirectional_sum_f32_async(
     const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
     const float* c, const float* d_skip, const float* z, const float* delta_bias,
     int delta_softplus, int backend, int threading, float* out, float* last_fwd,
-    float* last_bwd, void* stream) {
+    float* last_bwd, const float* h0_fwd, const float* h0_bwd, void* stream) {
     M1Counts cnt;
     int rc = bidir_common(dims, u, delta, a, b, c, d_skip, z, delta_bias, backend, threading,
                           out, out, last_fwd, last_bwd, &cnt);
@@ -631,11 +631,36 @@ int arm_scan_selective_scan_bidirectional_sum_f32_async(
     M1Params f = base, r = base;
     f.out = out;
     f.last_state = last_fwd;
+    f.h0 = h0_fwd;
     r.reverse = 1;
     r.out = nullptr;
     r.last_state = last_bwd;
+    r.h0 = h0_bwd;
     cudaError_t e = m1_bidir_sum_launch(f, r, backend, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "bidirectional sum launch");
+}
+
+int arm_scan_selective_scan_bidirectional_final_states_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
+    const float* c, const float* delta_bias, int delta_softplus, int backend, float* last_fwd,
+    float* last_bwd, void* stream) {
+    if (!last_fwd || !last_bwd)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "last_fwd and last_bwd are required");
+    M1Counts cnt;
+    int rc = bidir_common(dims, u, delta, a, b, c, nullptr, nullptr, delta_bias, backend, 0,
+                          last_fwd, last_bwd, last_fwd, last_bwd, &cnt);
+    if (rc) return rc;
+    std::vector<void*> p = {const_cast<float*>(u), const_cast<float*>(delta),
+                            const_cast<float*>(a), const_cast<float*>(b),
+                            const_cast<float*>(c), nullptr,
+                            nullptr,               const_cast<float*>(delta_bias)};
+    M1Params base = m1_params(dims, p, delta_softplus, 0);
+    M1Params f = base, r = base;
+    f.last_state = last_fwd;
+    r.reverse = 1;
+    r.last_state = last_bwd;
+    cudaError_t e = m1_bidir_states_launch(f, r, backend, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "bidirectional final states launch");
 }
 
 int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const float* k,

@@ -522,6 +522,17 @@ cudaError_t m1_bidir_launch(const M1Params& fwd, const M1Params& bwd, int backen
     return m1_scan_launch(bwd, backend, stream);
 }
 
+cudaError_t m1_bidir_states_launch(const M1Params& fwd, const M1Params& bwd, int backend,
+                                   cudaStream_t stream) {
+    M1Params f = fwd, r = bwd;
+    f.out = r.out = nullptr;
+    f.z = r.z = nullptr;
+    f.d_skip = r.d_skip = nullptr;
+    if (const int S = bidir_shared_segments(f, backend)) return m1_seg2_bidir_launch(f, r, S, stream);
+    const cudaError_t e = m1_final_state_launch(f, stream);
+    return e != cudaSuccess ? e : m1_final_state_launch(r, stream);
+}
+
 namespace {
 __global__ void m1_add_kernel(float* __restrict__ out, const float* __restrict__ other, int64_t n) {
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;

@@ -55,6 +55,9 @@ int m1_seg2_segments(const M1Params& p);
 // Both traversals of one bidirectional scan with the two-pass kernel (bwd is
 // fwd with reverse = 1 and its own out / last_state; bwd.out_acc sums into
 // fwd.out).
+// Final states of both traversals (no outputs); each from its own h0.
+cudaError_t m1_bidir_states_launch(const M1Params& fwd, const M1Params& bwd, int backend,
+                                   cudaStream_t stream);
 // Bidirectional scan summed into fwd.out (bwd.out unused).
 cudaError_t m1_bidir_sum_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                                 cudaStream_t stream);

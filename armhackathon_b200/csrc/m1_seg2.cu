@@ -455,6 +455,8 @@ cudaError_t m1_seg2_launch(const M1Params& p, int S, cudaStream_t stream) {
 // a carry per direction, a pass 2 per direction over every segment: three
 // exps per (step, state) instead of 2 x 2(S-1)/S.  bwd.out == fwd.out with
 // bwd.out_acc sums the two outputs in place (bwd's pass 2 runs after fwd's).
+// fwd.out == nullptr: final states only (pass 1 and the carries).  Each
+// direction's carry starts at its own h0.
 cudaError_t m1_seg2_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S,
                                  cudaStream_t stream) {
     const int64_t rows = fwd.batch * fwd.dim, Ls = fwd.len / S;
@@ -488,10 +490,12 @@ cudaError_t m1_seg2_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S
     if (e == cudaSuccess) note_launch();
     if (e == cudaSuccess) e = launch_pdl(m1_seg2_carry_kernel<false>, cg, dim3(256), stream, bwd, wb, S);
     if (e == cudaSuccess) note_launch();
-    if (e == cudaSuccess) e = launch_pdl(m1_seg2_pass2<false, 0>, grid, block, stream, f2, wf, S, Ls, 0);
-    if (e == cudaSuccess) note_launch();
-    if (e == cudaSuccess) e = launch_pdl(m1_seg2_pass2<true, 0>, grid, block, stream, b2, wb, S, Ls, 0);
-    if (e == cudaSuccess) note_launch();
+    if (fwd.out) {
+        if (e == cudaSuccess) e = launch_pdl(m1_seg2_pass2<false, 0>, grid, block, stream, f2, wf, S, Ls, 0);
+        if (e == cudaSuccess) note_launch();
+        if (e == cudaSuccess) e = launch_pdl(m1_seg2_pass2<true, 0>, grid, block, stream, b2, wb, S, Ls, 0);
+        if (e == cudaSuccess) note_launch();
+    }
     const cudaError_t ef = cudaFreeAsync(raw, stream);
     return e != cudaSuccess ? e : ef;
 }

@@ -168,6 +168,8 @@ def _selective_scan_bidir_sum_op(
     z: Optional[torch.Tensor],
     delta_bias: Optional[torch.Tensor],
     delta_softplus: bool,
+    h0_fwd: Optional[torch.Tensor] = None,
+    h0_bwd: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     batch, dim, length = u.shape
     state = a.shape[1]
@@ -177,21 +179,23 @@ def _selective_scan_bidir_sum_op(
         _ffi.scan_bidir_sum_raw(
             dims, u.data_ptr(), delta.data_ptr(), a.data_ptr(), b.data_ptr(), c.data_ptr(),
             _ptr(d_skip), _ptr(z), _ptr(delta_bias), delta_softplus, "auto", out.data_ptr(),
-            stream=_stream(u))
+            ptr_h0_fwd=_ptr(h0_fwd), ptr_h0_bwd=_ptr(h0_bwd), stream=_stream(u))
     _CALLS["n"] += 1
     return out
 
 
 @_selective_scan_bidir_sum_op.register_fake
-def _(u, delta, a, b, c, d_skip, z, delta_bias, delta_softplus):
+def _(u, delta, a, b, c, d_skip, z, delta_bias, delta_softplus, h0_fwd=None, h0_bwd=None):
     return torch.empty_like(u)
 
 
 def selective_scan_bidirectional_sum(u, delta, A, B, C, D=None, z=None, delta_bias=None,
-                                     delta_softplus=False):
+                                     delta_softplus=False, initial_states=None):
     """out_fwd + out_bwd of ``selective_scan_bidirectional`` in one call, on
     CUDA tensors: the two traversals share their first pass and the reverse
-    one adds into the output in place."""
+    one adds into the output in place.  ``initial_states`` = (h0_fwd,
+    h0_bwd), each (batch, dim, state) or None: the incoming state of each
+    traversal (the reverse one's enters at the last step)."""
     if u.device.type != "cuda":
         raise ValueError("selective_scan_bidirectional_sum needs CUDA tensors")
     batch, dim, length = u.shape
@@ -200,9 +204,53 @@ def selective_scan_bidirectional_sum(u, delta, A, B, C, D=None, z=None, delta_bi
     B = _bc4(B, batch, state, length)
     C = _bc4(C, batch, state, length)
     opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
+    h0f, h0b = initial_states if initial_states is not None else (None, None)
+    for t in (h0f, h0b):
+        if t is not None and tuple(t.shape) != (batch, dim, state):
+            raise ValueError(f"initial states must be {(batch, dim, state)}, got {tuple(t.shape)}")
     return _selective_scan_bidir_sum_op(
         _prep(u, dev), _prep(delta, dev), _prep(A, dev), _prep(B, dev), _prep(C, dev),
-        opt(D), opt(z), opt(delta_bias), bool(delta_softplus))
+        opt(D), opt(z), opt(delta_bias), bool(delta_softplus), opt(h0f), opt(h0b))
+
+
+@torch.library.custom_op("arm_scan::selective_scan_bidirectional_final_states", mutates_args=())
+def _bidir_states_op(u: torch.Tensor, delta: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
+                     c: torch.Tensor, delta_bias: Optional[torch.Tensor],
+                     delta_softplus: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+    batch, dim, length = u.shape
+    state = a.shape[1]
+    hf = u.new_empty((batch, dim, state))
+    hb = u.new_empty((batch, dim, state))
+    dims = _ffi.ArmScanDims(batch, dim, length, state, b.shape[1] if b.dim() == 4 else 1)
+    with _on_device(u):
+        _ffi.bidir_states_raw(dims, u.data_ptr(), delta.data_ptr(), a.data_ptr(), b.data_ptr(),
+                              c.data_ptr(), _ptr(delta_bias), delta_softplus, "auto",
+                              hf.data_ptr(), hb.data_ptr(), stream=_stream(u))
+    _CALLS["n"] += 1
+    return hf, hb
+
+
+@_bidir_states_op.register_fake
+def _(u, delta, a, b, c, delta_bias, delta_softplus):
+    s = (u.shape[0], u.shape[1], a.shape[1])
+    return u.new_empty(s), u.new_empty(s)
+
+
+def selective_scan_bidirectional_final_states(u, delta, A, B, C, delta_bias=None,
+                                              delta_softplus=False):
+    """(h_fwd, h_bwd): the states after the forward and the reverse traversal
+    from zero, without outputs, on CUDA tensors (one shared first pass where
+    the two-pass kernel applies)."""
+    if u.device.type != "cuda":
+        raise ValueError("selective_scan_bidirectional_final_states needs CUDA tensors")
+    batch, dim, length = u.shape
+    state = A.shape[1]
+    dev = u.device
+    B = _bc4(B, batch, state, length)
+    C = _bc4(C, batch, state, length)
+    return _bidir_states_op(_prep(u, dev), _prep(delta, dev), _prep(A, dev), _prep(B, dev),
+                            _prep(C, dev), None if delta_bias is None else _prep(delta_bias, dev),
+                            bool(delta_softplus))
 
 
 def selective_scan_bidirectional(u, delta, A, B, C, D=None, z=None,

@@ -15,6 +15,10 @@ Per call:
   3. rank r folds the summaries of ranks < r (forward) and > r (backward)
      into its incoming states;
   4. rank r scans its segment in both directions from those states.
+With the library's own functions on CUDA tensors and merge "sum", step 1 is
+one call (``selective_scan_bidirectional_final_states``: both directions from a
+shared first pass) and step 4 another (``selective_scan_bidirectional_sum``
+with both incoming states).
 The fold is exact algebra, so the result equals the unsplit bidirectional
 scan up to fp32 rounding.  No rank waits on another except inside the
 all_gather, whose timeout is the process group's.
@@ -69,8 +73,17 @@ def bidirectional_scan_seqpar(u, delta, A, B, C, D=None, z=None, delta_bias=None
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     skw = dict(delta_bias=delta_bias, delta_softplus=delta_softplus)
-    hf = state_fn(u, delta, A, B, C, **skw)
-    hb = state_fn(u, delta, A, B, C, reverse=True, **skw)
+    # the library's own functions on CUDA tensors: both directions' summaries
+    # from one shared first pass, and both outputs summed by one call
+    fused = merge == "sum" and u.device.type == "cuda" and getattr(
+        scan_fn, "__module__", "") == __package__ + ".op" and getattr(
+        state_fn, "__module__", "") == __package__ + ".op"
+    if fused:
+        from .op import selective_scan_bidirectional_final_states
+        hf, hb = selective_scan_bidirectional_final_states(u, delta, A, B, C, **skw)
+    else:
+        hf = state_fn(u, delta, A, B, C, **skw)
+        hb = state_fn(u, delta, A, B, C, reverse=True, **skw)
     sdt = _segment_dt_sum(delta, delta_bias, delta_softplus).to(hf.dtype)
     packed = torch.cat([hf, hb, sdt[..., None]], dim=-1).contiguous()
     parts = [torch.empty_like(packed) for _ in range(world)]
@@ -82,6 +95,10 @@ def bidirectional_scan_seqpar(u, delta, A, B, C, D=None, z=None, delta_bias=None
     kw = dict(D=D, z=z, **skw)
     h_in_f = fold_carries(h_f, sums, A, rank, False) if rank > 0 else None
     h_in_b = fold_carries(h_b, sums, A, rank, True) if rank < world - 1 else None
+    if fused:
+        from .op import selective_scan_bidirectional_sum
+        return selective_scan_bidirectional_sum(u, delta, A, B, C, initial_states=(h_in_f, h_in_b),
+                                                **kw)
     yf = scan_fn(u, delta, A, B, C, initial_state=h_in_f, **kw)
     yb = scan_fn(u, delta, A, B, C, reverse=True, initial_state=h_in_b, **kw)
     return yf + yb if merge == "sum" else (yf, yb)

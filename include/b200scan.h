@@ -276,11 +276,25 @@ unsigned long long arm_scan_kernel_launches(void);
  * codes as the bidirectional entry (backend 0 or 1); last_fwd / last_bwd are
  * both-or-neither.  Device pointers, stream-ordered.  Where the two-pass
  * kernel applies, both traversals share their first pass (every exp of it
- * computed once) and the reverse traversal adds into `out` in place. */
+ * computed once) and the reverse traversal adds into `out` in place.
+ * h0_fwd / h0_bwd (nullable, (batch, dim, state)): incoming state of each
+ * traversal (the reverse one's at t = len - 1). */
 int arm_scan_selective_scan_bidirectional_sum_f32_async(
     const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
     const float* c, const float* d_skip, const float* z, const float* delta_bias,
     int delta_softplus, int backend, int threading, float* out, float* last_fwd,
+    float* last_bwd, const float* h0_fwd, const float* h0_bwd, void* stream);
+
+/* Extension: final states of both traversals of a bidirectional scan, without
+ * outputs: last_fwd = the state after the forward traversal, last_bwd = after
+ * the reverse one (at t = 0), each (batch, dim, state) from a zero start.
+ * Inputs and codes as the bidirectional entry (no D or z: they do not reach
+ * the states).  Where the two-pass kernel applies both come from one shared
+ * first pass.  With the sum entry's h0_fwd / h0_bwd this gives a sequence
+ * split over devices its segment summaries and then its outputs. */
+int arm_scan_selective_scan_bidirectional_final_states_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
+    const float* c, const float* delta_bias, int delta_softplus, int backend, float* last_fwd,
     float* last_bwd, void* stream);
 
 /* Extension: shape of the Mamba-3 mixer whose prologue

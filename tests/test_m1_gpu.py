@@ -186,6 +186,33 @@ def test_bidirectional_shared_first_pass(segments, shape, monkeypatch):
     assert rel_err(lb.cpu().numpy(), wlb) <= REL_TOL
 
 
+@pytest.mark.parametrize("shared", ["1", "0"])
+def test_bidirectional_final_states_and_sum_with_h0(shared, monkeypatch):
+    """The two calls a sequence split over devices makes: both traversals'
+    final states from zero (one shared first pass), then both outputs summed
+    from given incoming states (forward one enters at t = 0, reverse one at
+    t = L - 1); with and without the shared pass."""
+    monkeypatch.setenv("B200SCAN_M1_BIDIR_SHARED", shared)
+    B, D, L, N = 2, 70, 1024, 13
+    x = _slow_decay_case(B, D, L, N, seed=11)
+    a = arm()
+    t = cuda(x)
+    hf, hb = a.selective_scan_bidirectional_final_states(
+        t["u"], t["delta"], t["A"], t["B"], t["C"], delta_bias=t["delta_bias"],
+        delta_softplus=True)
+    _, wlf = oracle.m1_scan(**x, nthreads=8)
+    _, wlb = oracle.m1_scan(**x, reverse=True, nthreads=8)
+    assert rel_err(hf.cpu().numpy(), wlf) <= REL_TOL
+    assert rel_err(hb.cpu().numpy(), wlb) <= REL_TOL
+    rng = np.random.default_rng(3)
+    h0f, h0b = (rng.standard_normal((B, D, N)).astype(np.float32) for _ in range(2))
+    out = a.selective_scan_bidirectional_sum(
+        **t, initial_states=(torch.from_numpy(h0f).cuda(), torch.from_numpy(h0b).cuda()))
+    wf, _ = oracle.m1_scan(**x, h0=h0f, nthreads=8)
+    wb, _ = oracle.m1_scan(**x, reverse=True, h0=h0b, nthreads=8)
+    assert rel_err(out.cpu().numpy(), wf + wb) <= REL_TOL
+
+
 def test_bidirectional_sum_without_shared_pass(monkeypatch):
     """The sum entry where the traversals run as independent scans (forced,
     and on a length the two-pass kernel does not take): second output in
