@@ -440,3 +440,44 @@ def test_final_state_entry_equals_scan_last_state(shape, reverse):
                                            delta_bias=c["delta_bias"], delta_softplus=True,
                                            initial_state=h0.cuda(), reverse=reverse)
     assert rel_err(got.cpu().numpy(), want.cpu().numpy()) <= 1e-5
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_seqpar_fused_path_one_device(world, monkeypatch):
+    """The sequence-parallel bidirectional scan on the library's own CUDA
+    functions (shared-pass final states, then the sum entry with incoming
+    states), every rank of a ``world``-way split run in this one process: the
+    all_gather is replaced by the ranks' summaries computed here, so the
+    result per segment must equal the unsplit bidirectional sum."""
+    import torch.distributed as dist
+    from armhackathon_b200 import seqpar
+    B, D, L, N = 1, 96, 192 * world * 4, 16
+    x = _slow_decay_case(B, D, L, N, seed=21)
+    t = cuda(x)
+    a = arm()
+    full = a.bidirectional_scan(**t, merge="sum")
+    seg = L // world
+    sl = lambda v, r: v[..., r * seg:(r + 1) * seg].contiguous()  # noqa: E731
+    summaries = []
+    for r in range(world):
+        hf, hb = a.selective_scan_bidirectional_final_states(
+            sl(t["u"], r), sl(t["delta"], r), t["A"], sl(t["B"], r), sl(t["C"], r),
+            delta_bias=t["delta_bias"], delta_softplus=True)
+        sdt = seqpar._segment_dt_sum(sl(t["delta"], r), t["delta_bias"], True)
+        summaries.append(torch.cat([hf, hb, sdt[..., None]], dim=-1))
+    rank = {"r": 0}
+
+    def fake_all_gather(parts, packed, group=None):
+        assert torch.allclose(packed, summaries[rank["r"]], rtol=1e-6, atol=1e-6)
+        for p, s in zip(parts, summaries):
+            p.copy_(s)
+
+    monkeypatch.setattr(dist, "get_world_size", lambda group=None: world)
+    monkeypatch.setattr(dist, "get_rank", lambda group=None: rank["r"])
+    monkeypatch.setattr(dist, "all_gather", fake_all_gather)
+    for r in range(world):
+        rank["r"] = r
+        y = seqpar.bidirectional_scan_seqpar(
+            sl(t["u"], r), sl(t["delta"], r), t["A"], sl(t["B"], r), sl(t["C"], r), D=t["D"],
+            z=sl(t["z"], r), delta_bias=t["delta_bias"], delta_softplus=True)
+        assert rel_err(y.cpu().numpy(), sl(full, r).cpu().numpy()) <= REL_TOL
