@@ -172,3 +172,27 @@ def test_mixer_prologue_argument_rules():
     assert call(_ffi.ArmMamba3MixerDims(1, 4, 0, 8, 16, 1, 4)) == 2   # no heads
     assert call(_ffi.ArmMamba3MixerDims(1, 4, 2, 8, 16, 1, 9)) == 2   # n_angles > d_state / 2
     assert call(_ffi.ArmMamba3MixerDims(1, 1 << 62, 2, 8, 16, 1, 4)) == 2  # overflow
+
+
+def test_bidirectional_sum_and_states_argument_rules():
+    """The bidirectional sum / final-states entries: host checks before any
+    device work (dummy pointers never dereferenced)."""
+    lib = _ffi.load()
+    p = ctypes.c_void_p(16)
+    dims = _ffi.ArmScanDims(1, 4, 64, 4, 1)
+
+    def sum_call(out=p, lf=None, lb=None, d=dims):
+        return lib.arm_scan_selective_scan_bidirectional_sum_f32_async(
+            ctypes.byref(d), p, p, p, p, p, None, None, None, 1, 0, 0, out, lf, lb, None, None,
+            None)
+
+    def states_call(lf=p, lb=p, backend=0, d=dims):
+        return lib.arm_scan_selective_scan_bidirectional_final_states_f32_async(
+            ctypes.byref(d), p, p, p, p, p, None, 1, backend, lf, lb, None)
+    assert sum_call(out=None) == 1
+    assert sum_call(lf=p) == 2                  # last states both-or-neither
+    assert sum_call(d=_ffi.ArmScanDims(0, 4, 64, 4, 1)) == 2
+    assert states_call(lb=None) == 1
+    assert states_call(backend=2) == 3          # neon backend unavailable
+    assert states_call(backend=9) == 4
+    assert states_call(d=_ffi.ArmScanDims(1, 6, 64, 4, 4)) == 2  # dim not a multiple of groups
