@@ -286,6 +286,8 @@ def run_mixer(args, w, dev):
     launches = int(round(per_call * args.steps))  # kernels in the timed region
     torch_ms = timed(lambda: torch_mixer_prologue(**x), args.steps)
     full_ms = timed(lambda: arm.mamba3_mixer_scan(**x, **scan_kw), max(1, args.steps // 5))
+    bf16_ms = timed(lambda: arm.mamba3_mixer_scan(**x, **scan_kw, precision="bf16"),
+                    max(1, args.steps // 5))
     peak, peak_kind = peaks()
     gbs = nbytes / (ms * 1e-3) / 1e9
     print(json.dumps({
@@ -295,6 +297,7 @@ def run_mixer(args, w, dev):
                      "frac": gbs / peak, "peak_source": peak_kind},
         "gpu_launches": launches, "clocks": clocks,
         "torch_ops_ms": torch_ms, "prologue_plus_fp32_scan_ms": full_ms,
+        "prologue_plus_bf16_tensor_scan_ms": bf16_ms,
         "l2": "inputs larger than L2",
         "note": "the prologue alone (one kernel, CUDA events); torch_ops_ms = the same "
                 "prologue as separate torch ops on this GPU"}), flush=True)

@@ -95,3 +95,22 @@ def test_mixer_prologue_rejects_host_tensor_and_wrong_width():
         prologue(d, dims, torch.from_numpy(d["proj"]))
     with pytest.raises(ValueError):
         prologue(d, dims, torch.from_numpy(d["proj"][..., :-1].copy()).cuda())
+
+
+def test_mixer_scan_bf16_tensor_path():
+    """A mixer at the tensor-core shape (d_state 128, headdim 64):
+    precision "bf16" routes the prologue's outputs, with the angles passed
+    broadcast over heads, to the tcgen05 scan; against the fp32 mixer scan at
+    the bf16 tolerance of the tensor-core tests."""
+    g = torch.Generator(device="cuda").manual_seed(4)
+    H, P, N, NA, b, l = 3, 64, 128, 32, 2, 300
+    from armhackathon_b200.mamba3_mixer import proj_width
+    W = proj_width(H, P, N, 1, NA)
+    proj = torch.randn(b, l, W, device="cuda", generator=g)
+    rn = lambda *s: torch.randn(*s, device="cuda", generator=g)  # noqa: E731
+    kw = dict(nheads=H, headdim=P, d_state=N, n_angles=NA, dt_bias=rn(H) - 2,
+              B_norm_weight=1 + 0.1 * rn(N), C_norm_weight=1 + 0.1 * rn(N), D=rn(H),
+              B_bias=0.1 * rn(H, 1, N), C_bias=0.1 * rn(H, 1, N))
+    want = arm().mamba3_mixer_scan(proj, **kw).cpu().numpy()
+    got = arm().mamba3_mixer_scan(proj, **kw, precision="bf16").float().cpu().numpy()
+    assert np.abs(got - want).max() / np.abs(want).max() <= 2e-2
