@@ -117,6 +117,8 @@ def _bind(lib):
         ctypes.POINTER(ArmScanDims), *([_VP] * 9), ctypes.c_int, _VP, _VP]
     lib.arm_scan_kernel_launches.restype = ctypes.c_ulonglong
     lib.arm_scan_kernel_launches.argtypes = []
+    lib.arm_scan_set_kernel_override.restype = ctypes.c_int
+    lib.arm_scan_set_kernel_override.argtypes = [_I, _I]
     lib.arm_scan_selective_scan_bidirectional_sum_f32_async.restype = ctypes.c_int
     lib.arm_scan_selective_scan_bidirectional_sum_f32_async.argtypes = [
         ctypes.POINTER(ArmScanDims), *([_VP] * 8), _I, _I, _I, _VP, _VP, _VP, _VP, _VP, _VP]
@@ -304,6 +306,35 @@ def kernel_launches():
     return int(load().arm_scan_kernel_launches())
 
 
+KNOBS = {"m1_kernel": 0, "m1_segments": 1, "m1_bidir_independent": 2, "m3_tc_split": 3,
+         "m3_chunk_form": 4, "pdl_off": 5}
+M1_KERNELS = {"auto": 0, "lane": 1, "tile": 2, "chunked": 3, "tile_timesplit": 4}
+
+
+def set_kernel_override(knob, value):
+    """Process-wide kernel-selection override (``KNOBS``; 0 = default)."""
+    _check(load().arm_scan_set_kernel_override(KNOBS[knob], int(value)),
+           "arm_scan_set_kernel_override")
+
+
+class kernel_override:
+    """Context manager: ``with kernel_override(m1_kernel=2, m1_segments=4): ...``
+    sets the given knobs and puts every one back to 0 on exit."""
+
+    def __init__(self, **knobs):
+        self.knobs = knobs
+
+    def __enter__(self):
+        for k, v in self.knobs.items():
+            set_kernel_override(k, v)
+        return self
+
+    def __exit__(self, *exc):
+        for k in self.knobs:
+            set_kernel_override(k, 0)
+        return False
+
+
 def tensor_status():
     """Raise if a tensor-core kernel's bounded wait expired since the last
     check (call after synchronizing the stream of an async launch)."""
@@ -324,7 +355,8 @@ def exported_symbols():
             "arm_scan_selective_scan_final_state_f32_async", "arm_scan_mamba3_ss2d_f32_async",
             "arm_scan_mamba3_mixer_prologue_f32_async",
             "arm_scan_selective_scan_bidirectional_sum_f32_async",
-            "arm_scan_selective_scan_bidirectional_final_states_f32_async"]
+            "arm_scan_selective_scan_bidirectional_final_states_f32_async",
+            "arm_scan_set_kernel_override"]
 
 
 if __name__ == "__main__":  # pragma: no cover

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "../../include/b200scan.h"
+#include "common.cuh"
 #include "m1_scan.h"
 #include "m3_mixer.h"
 #include "m3_angles.h"
@@ -131,7 +132,14 @@ size_t round_up(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Runs `run(device_ptrs, stream)` either directly on device buffers (then
 // synchronizes) or after staging host buffers through device memory.
+int m1_status_code() {
+    return m1_lane_status_and_clear() ? fail(ARM_SCAN_ERR_TIMEOUT, "a Mamba-1 staging wait expired")
+                                      : ARM_SCAN_OK;
+}
+
 int tensor_status_code() {
+    const int m1 = m1_lane_status_and_clear();
+    if (m1) return fail(ARM_SCAN_ERR_TIMEOUT, "a Mamba-1 staging wait expired");
     return m3_tc_status_and_clear()
                ? fail(ARM_SCAN_ERR_TIMEOUT, "a tensor-core MMA completion wait expired")
                : ARM_SCAN_OK;
@@ -372,13 +380,11 @@ int m3_run(const M3Params& m, int backend, cudaStream_t s) {
 namespace b200scan {
 std::atomic<unsigned long long> g_kernel_launches{0};
 void note_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
-bool pdl_enabled() {
-    static const bool on = [] {
-        const char* v = std::getenv("B200SCAN_PDL");
-        return !(v && v[0] == '0');
-    }();
-    return on;
+std::atomic<int> g_override[kKnobCount];
+int kernel_override(int knob) {
+    return knob >= 0 && knob < kKnobCount ? g_override[knob].load(std::memory_order_relaxed) : 0;
 }
+bool pdl_enabled() { return kernel_override(kKnobPdl) == 0; }
 }  // namespace b200scan
 
 extern "C" {
@@ -475,6 +481,11 @@ int m1_host_pipelined(const ArmScanDims* d, const std::vector<Buf>& bufs, int so
         m.h0 = static_cast<const float*>(dptr[8]);
         m.out = static_cast<float*>(dptr[9]);
         m.last_state = static_cast<float*>(dptr[10]);
+        // the whole batch's segment count, so that every row's result is
+        // the one the unpipelined call gives
+        M1Params whole = m;
+        whole.batch = static_cast<int64_t>(nb);
+        m.segments = m1_lane_segments(whole);
         const int rc = m1_run(m, backend, st);
         if (rc != ARM_SCAN_OK) {
             cudaStreamSynchronize(pp.s[0]);
@@ -493,7 +504,7 @@ int m1_host_pipelined(const ArmScanDims* d, const std::vector<Buf>& bufs, int so
     const cudaError_t e1 = cudaStreamSynchronize(pp.s[1]);
     if (e0 != cudaSuccess) return cuda_fail(e0, "kernel");
     if (e1 != cudaSuccess) return cuda_fail(e1, "kernel");
-    return ARM_SCAN_OK;
+    return m1_status_code();
 }
 
 int arm_scan_selective_scan_f32(const ArmScanDims* dims, const float* u, const float* delta,
@@ -520,7 +531,7 @@ int arm_scan_selective_scan_f32(const ArmScanDims* dims, const float* u, const f
         m.out = static_cast<float*>(p[9]);
         m.last_state = static_cast<float*>(p[10]);
         return m1_run(m, backend, s);
-    });
+    }, m1_status_code);
 }
 
 int arm_scan_selective_scan_f32_async(const ArmScanDims* dims, const float* u, const float* delta,
@@ -593,7 +604,7 @@ int arm_scan_selective_scan_bidirectional_f32(const ArmScanDims* dims, const flo
         M1Params m = m1_params(dims, p, delta_softplus, 0);
         return bidir_run(m, static_cast<float*>(p[8]), static_cast<float*>(p[9]),
                          static_cast<float*>(p[10]), static_cast<float*>(p[11]), backend, s);
-    });
+    }, m1_status_code);
 }
 
 int arm_scan_selective_scan_bidirectional_f32_async(
@@ -750,6 +761,14 @@ int arm_scan_selective_state_update_f32_async(const ArmScanDims* dims, float* st
 }
 
 unsigned long long arm_scan_kernel_launches(void) { return b200scan::g_kernel_launches.load(); }
+
+int arm_scan_set_kernel_override(int knob, int value) {
+    if (knob < 0 || knob >= b200scan::kKnobCount)
+        return fail(ARM_SCAN_ERR_BAD_ENUM, "kernel override knob %d out of range", knob);
+    if (value < 0) return fail(ARM_SCAN_ERR_BAD_ENUM, "kernel override value %d is negative", value);
+    b200scan::g_override[knob].store(value, std::memory_order_relaxed);
+    return ARM_SCAN_OK;
+}
 
 int arm_scan_mamba3_mixer_prologue_f32_async(const ArmMamba3MixerDims* dims, const float* proj,
                                              const float* dt_bias, const float* b_norm_weight,

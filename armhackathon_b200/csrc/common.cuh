@@ -153,16 +153,28 @@ __device__ __forceinline__ void griddep_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// B200SCAN_PDL=0 turns the attribute off (plain stream-ordered launches).
+// Kernel-selection overrides for tests and measurements, set through
+// arm_scan_set_kernel_override (process-wide; 0 everywhere means the
+// default dispatch).
+enum KernelKnob {
+    kKnobM1Kernel = 0,    // 0 auto, 1 lane, 2 row-tile, 3 block-chunked, 4 row-tile with time split
+    kKnobM1Segments = 1,  // 0 auto, else the segment count of the lane / time-split kernels
+    kKnobM1BidirShared = 2,  // 0 shared first pass (default), 1 two independent traversals
+    kKnobM3TcSplit = 3,   // 0 fused tensor-core kernel, 1 three-launch form
+    kKnobM3ChunkForm = 4, // 0 auto, 1 sequential, 2 chunk-parallel (fp32 chunk kernels)
+    kKnobPdl = 5,         // 0 programmatic dependent launch on, 1 off
+    kKnobCount = 6,
+};
+int kernel_override(int knob);
 bool pdl_enabled();
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
-                       Args&&... args) {
+cudaError_t launch_pdl_smem(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t stream, Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -170,6 +182,12 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStre
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
+                       Args&&... args) {
+    return launch_pdl_smem(kernel, grid, block, 0, stream, static_cast<Args&&>(args)...);
 }
 
 }  // namespace b200scan

@@ -1,0 +1,709 @@
+// Mamba-1 selective scan, lanes over states, TMA-staged (default kernel for
+// d_state <= 16).
+//
+// Recurrence (reference kernel/arm-scan-core/src/scalar.rs:11-89):
+//   dt = softplus(delta + bias), h_n = exp(dt A_n) h_n + dt u B_n,
+//   y = sum_n C_n h_n + D u, times silu(z); reverse walks the steps from the
+// end (scalar.rs:59).
+//
+// Thread mapping.  Four lanes of a warp own one (batch, channel) row, lane q
+// holding states q, q+4, q+8, q+12 in registers, so a warp covers 8 rows and
+// every lane computes exactly one exp per (step, owned state).  The per-step
+// row work (softplus of delta, dt*u, silu(z), D*u) is spread over the four
+// lanes instead of repeated by each: lane q takes steps 4k+q of every
+// 32-step tile, writes dt and dt*u back into the staged tile, and keeps
+// silu(z) and D*u*silu(z) in registers.  After the recurrence over 4 steps
+// every lane holds 4 partial outputs (its states' share of y at each step);
+// a two-stage butterfly (xor 2, xor 1) reduce-scatters them so that lane q
+// ends with the full y of step 4k+q, the step whose silu(z) it computed.
+//
+// Staging.  A CTA is 32 rows of one (batch, B/C group) and one time segment:
+// four compute warps and one producer warp.  The producer streams 32-step
+// tiles of delta, u, z ([32 rows][32 steps]) and B, C ([N states][32 steps])
+// through a 4-deep shared-memory ring with 2D TMA loads
+// (cp.async.bulk.tensor, 128-byte swizzle so that the rows of a warp's
+// 16-byte loads fall in distinct banks), full/empty mbarriers between the
+// producer and the compute warps.  Outputs are written back from the staged
+// z slot as coalesced 16-byte stores.  Every mbarrier wait is bounded; on
+// expiry the kernel sets a device status flag and stops.
+//
+// Time segments.  When rows are too few to fill the GPU, the sequence is cut
+// into S segments, as in a two-pass segmented scan: pass 1 computes each
+// segment's end state from zero (and the first segment's outputs from h0),
+// a carry kernel chains h_in(s) = exp(A sum dt(prev)) h_in(prev) +
+// h_end(prev), and pass 2 rescans segments 1..S-1 from h_in.  The segment
+// count is chosen from a wave model of the launch (see lane_pick_segments).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "m1_scan.h"
+
+namespace b200scan {
+
+namespace {
+
+constexpr int kLT = 32;        // steps per tile
+constexpr int kLRows = 32;     // rows per CTA
+constexpr int kLStages = 4;    // ring depth
+constexpr int kLWarps = 4;     // compute warps
+constexpr int kLThreads = (kLWarps + 1) * 32;
+constexpr uint32_t kXBytes = kLRows * kLT * 4;  // one [32 rows][32 steps] fp32 tile
+constexpr uint32_t kBCBytes = 16 * kLT * 4;     // one [16 states][32 steps] tile
+constexpr uint32_t kStageBytes = 3 * kXBytes + 2 * kBCBytes;
+constexpr uint32_t kSmemBytes = kLStages * kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+__device__ int g_m1_status;  // 0 ok, 1 a staging wait expired
+
+enum LaneMode {
+    kLaneState = 0,   // from zero: end state + sum of dt
+    kLaneRescan = 1,  // from h_in: y (and last_state on the last segment)
+    kLaneFirst = 2,   // from h0: y, and the true end state into hend
+    kLaneBidir = 3,   // from zero, forward: the end state and the reverse
+                      // traversal's aggregate of the segment (see pass1_bidir)
+};
+
+struct LaneWs {
+    float* hend;   // [S][rows][16]
+    float* hin;    // [S][rows][16]
+    float* dtsum;  // [S][rows]
+};
+
+struct LaneMaps {
+    CUtensorMap delta, u, z, B, C;
+};
+
+// ---- PTX wrappers -----------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mb_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mb_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mb_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// bounded wait for the phase of the given parity; false on expiry
+__device__ __forceinline__ bool mb_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t b = smem_u32(bar);
+    for (uint32_t it = 0; it < kWaitLimit; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done)
+            : "r"(b), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Byte offset of (row r, step m) in a [rows][32] fp32 tile written by TMA
+// with 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8).
+__device__ __forceinline__ uint32_t swz(int r, int m) {
+    return static_cast<uint32_t>(r * 128 + ((((m >> 2) ^ r) & 7) << 4) + (m & 3) * 4);
+}
+__device__ __forceinline__ float4 lds4(const char* base, int r, int chunk) {
+    return *reinterpret_cast<const float4*>(base + r * 128 + (((chunk ^ r) & 7) << 4));
+}
+__device__ __forceinline__ float4 rev4(float4 v) { return make_float4(v.w, v.z, v.y, v.x); }
+__device__ __forceinline__ float f4at(const float4& v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// ---- the sweep --------------------------------------------------------------
+// One CTA: rows [row0, row0 + 32) of one (batch, group), segment s.
+template <int MODE, bool REV>
+__device__ __forceinline__ void lane_sweep(const M1Params& p, const LaneMaps& maps, const LaneWs& ws,
+                                           const LaneWs* wsb, int S, int64_t Ls, int s, char* smem,
+                                           uint64_t* full, uint64_t* empty) {
+    constexpr bool FULL = MODE == kLaneRescan || MODE == kLaneFirst;
+    constexpr bool BID = MODE == kLaneBidir;
+    const int N = static_cast<int>(p.state);
+    const int64_t L = p.len, D = p.dim, G = p.groups, gsz = D / G;
+    const int64_t rows_all = p.batch * D;
+    const int blocks_per_group = static_cast<int>((gsz + kLRows - 1) / kLRows);
+    const int64_t bg = blockIdx.x / blocks_per_group;
+    const int jb = blockIdx.x % blocks_per_group;
+    const int64_t b = bg / G, g = bg % G;
+    const int64_t row0 = b * D + g * gsz + static_cast<int64_t>(jb) * kLRows;
+    const int64_t it0 = static_cast<int64_t>(s) * Ls;
+    const int64_t ie = it0 + Ls < L ? it0 + Ls : L;
+    const int n_tiles = static_cast<int>((ie - it0 + kLT - 1) / kLT);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool has_z = FULL && p.z;
+
+    if (warp == kLWarps) {  // ---- producer warp
+        if (lane == 0) {
+            tma_prefetch_desc(&maps.delta);
+            tma_prefetch_desc(&maps.u);
+            tma_prefetch_desc(&maps.B);
+            if (has_z) tma_prefetch_desc(&maps.z);
+            if (FULL) tma_prefetch_desc(&maps.C);
+            const uint32_t bc = static_cast<uint32_t>(N) * kLT * 4;
+            const uint32_t bytes = 2 * kXBytes + bc + (has_z ? kXBytes : 0) + (FULL ? bc : 0);
+            for (int c = 0; c < n_tiles; ++c) {
+                const int slot = c % kLStages;
+                if (c >= kLStages && !mb_wait(&empty[slot], ((c / kLStages) - 1) & 1)) {
+                    atomicExch(&g_m1_status, 1);
+                    break;
+                }
+                char* st = smem + slot * kStageBytes;
+                const int64_t j0 = it0 + static_cast<int64_t>(c) * kLT;
+                const int x = static_cast<int>(REV ? L - j0 - kLT : j0);
+                const int yr = static_cast<int>(row0);
+                const int yb = static_cast<int>(bg * N);
+                mb_expect_tx(&full[slot], bytes);
+                tma_load_2d(st, &maps.delta, x, yr, &full[slot]);
+                tma_load_2d(st + kXBytes, &maps.u, x, yr, &full[slot]);
+                if (has_z) tma_load_2d(st + 2 * kXBytes, &maps.z, x, yr, &full[slot]);
+                tma_load_2d(st + 3 * kXBytes, &maps.B, x, yb, &full[slot]);
+                if (FULL) tma_load_2d(st + 3 * kXBytes + kBCBytes, &maps.C, x, yb, &full[slot]);
+            }
+        }
+        return;
+    }
+
+    // ---- compute warps: lane (r, q) owns row r (0..31) and states q + 4i
+    const int r = warp * 8 + (lane >> 2), q = lane & 3;
+    const int64_t row = row0 + r;
+    const bool active = static_cast<int64_t>(jb) * kLRows + r < gsz && row < rows_all;
+    const int64_t ch = active ? row % D : 0;
+    float2 a01, a23;  // A * log2(e) for states (q, q+4), (q+8, q+12)
+    {
+        const float* A = p.A + ch * N;
+        auto ld = [&](int n) { return n < N ? A[n] * kLog2e : 0.f; };
+        a01 = make_float2(ld(q), ld(q + 4));
+        a23 = make_float2(ld(q + 8), ld(q + 12));
+    }
+    const float bias = p.delta_bias ? p.delta_bias[ch] : 0.f;
+    const float dsk = (FULL && p.d_skip) ? p.d_skip[ch] : 0.f;
+
+    if (MODE == kLaneRescan) griddep_wait();  // h_in comes from the carry kernel
+    float2 h01 = make_float2(0.f, 0.f), h23 = make_float2(0.f, 0.f);
+    if (active) {
+        const float* hi = MODE == kLaneRescan ? ws.hin + (static_cast<int64_t>(s) * rows_all + row) * 16
+                          : (MODE == kLaneFirst && p.h0) ? p.h0 + row * N
+                                                        : nullptr;
+        if (hi) {
+            auto ld = [&](int n) { return n < N ? hi[n] : 0.f; };
+            h01 = make_float2(ld(q), ld(q + 4));
+            h23 = make_float2(ld(q + 8), ld(q + 12));
+        }
+    }
+    float2 p01 = make_float2(1.f, 1.f), p23 = p01;                  // BID: running decay product
+    float2 hb01 = make_float2(0.f, 0.f), hb23 = hb01;               // BID: reverse aggregate
+    float dtsum = 0.f;
+
+    for (int c = 0; c < n_tiles; ++c) {
+        const int slot = c % kLStages;
+        const bool ok = mb_wait(&full[slot], (c / kLStages) & 1);
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) atomicExch(&g_m1_status, 1);
+            return;
+        }
+        char* st = smem + slot * kStageBytes;
+        char* sd = st;                  // delta -> dt
+        char* su = st + kXBytes;        // u -> dt*u
+        char* sz = st + 2 * kXBytes;    // z -> y
+        const char* sB = st + 3 * kXBytes;
+        const char* sC = sB + kBCBytes;
+        const int64_t j0 = it0 + static_cast<int64_t>(c) * kLT;
+        const int cnt = static_cast<int>(ie - j0 < kLT ? ie - j0 : kLT);
+
+        // phase A: lane q takes traversal steps 4k + q
+        float gk[8], dk[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int j = 4 * k + q;
+            const int m = REV ? kLT - 1 - j : j;
+            const uint32_t off = swz(r, m);
+            float dt = 0.f, dtu = 0.f;
+            const float uu = *reinterpret_cast<const float*>(su + off);
+            if (j < cnt) {
+                dt = *reinterpret_cast<const float*>(sd + off) + bias;
+                if (p.delta_softplus) dt = softplus_fast(dt);
+                dtu = dt * uu;
+            }
+            dtsum += dt;
+            *reinterpret_cast<float*>(sd + off) = dt;
+            *reinterpret_cast<float*>(su + off) = dtu;
+            if (FULL) {
+                const float gz = has_z ? silu_fast(*reinterpret_cast<const float*>(sz + off)) : 1.f;
+                gk[k] = gz;
+                dk[k] = dsk * uu * gz;
+            }
+        }
+        __syncwarp();
+
+        // phase B: the recurrence, 4 steps per block
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int chunk = REV ? 7 - k : k;
+            float4 dt4 = lds4(sd, r, chunk), du4 = lds4(su, r, chunk);
+            float4 b4[4], c4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                b4[i] = lds4(sB, q + 4 * i, chunk);
+                if (FULL) c4[i] = lds4(sC, q + 4 * i, chunk);
+            }
+            if (REV) {
+                dt4 = rev4(dt4);
+                du4 = rev4(du4);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    b4[i] = rev4(b4[i]);
+                    if (FULL) c4[i] = rev4(c4[i]);
+                }
+            }
+            float yp[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float dt = f4at(dt4, t), du = f4at(du4, t);
+                const float2 d2 = make_float2(dt, dt), u2 = make_float2(du, du);
+                const float2 x01 = fmul2(d2, a01), x23 = fmul2(d2, a23);
+                const float2 e01 = make_float2(ex2_approx(x01.x), ex2_approx(x01.y));
+                const float2 e23 = make_float2(ex2_approx(x23.x), ex2_approx(x23.y));
+                const float2 bu01 = fmul2(u2, make_float2(f4at(b4[0], t), f4at(b4[1], t)));
+                const float2 bu23 = fmul2(u2, make_float2(f4at(b4[2], t), f4at(b4[3], t)));
+                h01 = ffma2(e01, h01, bu01);
+                h23 = ffma2(e23, h23, bu23);
+                if (BID) {
+                    hb01 = ffma2(p01, bu01, hb01);
+                    hb23 = ffma2(p23, bu23, hb23);
+                    p01 = fmul2(p01, e01);
+                    p23 = fmul2(p23, e23);
+                }
+                if (FULL) {
+                    float2 y2 = fmul2(make_float2(f4at(c4[0], t), f4at(c4[1], t)), h01);
+                    y2 = ffma2(make_float2(f4at(c4[2], t), f4at(c4[3], t)), h23, y2);
+                    yp[t] = y2.x + y2.y;
+                }
+            }
+            if (FULL) {
+                // reduce-scatter over the row's 4 lanes: lane q gets step 4k + q
+                const bool hi = q & 2, lo = q & 1;
+                const float s0 = hi ? yp[0] : yp[2], s1 = hi ? yp[1] : yp[3];
+                const float k0 = hi ? yp[2] : yp[0], k1 = hi ? yp[3] : yp[1];
+                const float v0 = k0 + __shfl_xor_sync(0xffffffffu, s0, 2);
+                const float v1 = k1 + __shfl_xor_sync(0xffffffffu, s1, 2);
+                const float sl = lo ? v0 : v1, kp = lo ? v1 : v0;
+                const float y = kp + __shfl_xor_sync(0xffffffffu, sl, 1);
+                const int j = 4 * k + q;
+                const int m = REV ? kLT - 1 - j : j;
+                *reinterpret_cast<float*>(sz + swz(r, m)) = fmaf(y, gk[k], dk[k]);
+            }
+        }
+
+        if (FULL) {
+            // phase C: the warp's 8 rows x 32 steps of y, as 16-byte stores
+            __syncwarp();
+            const int64_t ms = REV ? L - j0 - kLT : j0;  // memory step of tile position 0
+#pragma unroll
+            for (int rep = 0; rep < 2; ++rep) {
+                const int idx = rep * 32 + lane;
+                const int rr = warp * 8 + (idx >> 3), cc = idx & 7;
+                const int64_t orow = row0 + rr;
+                const bool valid = REV ? (4 * cc >= kLT - cnt) : (4 * cc < cnt);
+                const bool ract = static_cast<int64_t>(jb) * kLRows + rr < gsz && orow < rows_all;
+                if (valid && ract) {
+                    float4 y4 = lds4(sz, rr, cc);
+                    float4* o4 = reinterpret_cast<float4*>(p.out + orow * L + ms + 4 * cc);
+                    if (p.out_acc) {
+                        const float4 o = __ldcs(o4);
+                        y4 = make_float4(o.x + y4.x, o.y + y4.y, o.z + y4.z, o.w + y4.w);
+                    }
+                    __stcs(o4, y4);
+                }
+            }
+        }
+        // release the slot: the generic-proxy writes above come before the
+        // next TMA writes into it
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mb_arrive(&empty[slot]);
+    }
+
+    // segment summaries
+    dtsum += __shfl_xor_sync(0xffffffffu, dtsum, 1);
+    dtsum += __shfl_xor_sync(0xffffffffu, dtsum, 2);
+    if (!active) return;
+    const float hv[4] = {h01.x, h01.y, h23.x, h23.y};
+    // segment end states for the carry (an unsplit scan with outputs has no
+    // workspace and no carry)
+    if (MODE != kLaneRescan && ws.hend) {
+        float* he = ws.hend + (static_cast<int64_t>(s) * rows_all + row) * 16;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) he[q + 4 * i] = hv[i];
+        if (q == 0) ws.dtsum[static_cast<int64_t>(s) * rows_all + row] = dtsum;
+    }
+    if (BID) {
+        // the reverse traversal visits this segment as its (S - 1 - s)-th
+        const int64_t sr = static_cast<int64_t>(S - 1 - s) * rows_all + row;
+        const float bv[4] = {hb01.x, hb01.y, hb23.x, hb23.y};
+        float* he = wsb->hend + sr * 16;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) he[q + 4 * i] = bv[i];
+        if (q == 0) wsb->dtsum[sr] = dtsum;
+    }
+    if (FULL && s == S - 1 && p.last_state) {
+        float* ls = p.last_state + row * N;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (q + 4 * i < N) ls[q + 4 * i] = hv[i];
+    }
+}
+
+// Shared set-up of every pass: aligned ring, barriers, zeroed B/C rows >= N.
+__device__ __forceinline__ char* lane_setup(uint64_t*& full, uint64_t*& empty, int N) {
+    extern __shared__ unsigned char lane_smem_raw[];
+    char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(lane_smem_raw) + 1023) & ~uintptr_t(1023));
+    full = reinterpret_cast<uint64_t*>(smem + kLStages * kStageBytes);
+    empty = full + kLStages;
+    if (N < 16) {  // TMA writes rows 0..N-1 of the B/C tiles; the rest stay zero
+        for (int i = threadIdx.x; i < kLStages * 2 * (16 - N) * kLT; i += blockDim.x) {
+            const int per = (16 - N) * kLT;
+            const int st = i / (2 * per), rem = i % (2 * per), w = rem / per, e = rem % per;
+            reinterpret_cast<float*>(smem + st * kStageBytes + 3 * kXBytes + w * kBCBytes)[N * kLT + e] = 0.f;
+        }
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kLStages; ++i) {
+            mb_init(&full[i], 1);
+            mb_init(&empty[i], kLWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    return smem;
+}
+
+// Pass 1.  FIRST: segment 0 runs the full scan from h0, segments 1..S-2 the
+// state-only sweep; otherwise every segment is state-only.
+template <bool FIRST, bool REV>
+__global__ void __launch_bounds__(kLThreads, 3)
+    m1_lane_pass1(M1Params p, const __grid_constant__ LaneMaps maps, LaneWs ws, int S, int64_t Ls) {
+    uint64_t *full, *empty;
+    char* smem = lane_setup(full, empty, static_cast<int>(p.state));
+    griddep_launch_dependents();
+    if (FIRST && blockIdx.y == 0)
+        lane_sweep<kLaneFirst, REV>(p, maps, ws, nullptr, S, Ls, 0, smem, full, empty);
+    else
+        lane_sweep<kLaneState, REV>(p, maps, ws, nullptr, S, Ls, blockIdx.y, smem, full, empty);
+}
+
+// Pass 1 of both traversals of the same inputs: one forward walk per segment
+// with every exp computed once gives the forward end state from zero and the
+// reverse traversal's aggregate of the segment from zero,
+// sum_t (prod_{r<t} exp(dt_r A)) dt_t u_t B_t (the running product needs
+// multiplies only), written at the reverse traversal's segment index.
+__global__ void __launch_bounds__(kLThreads, 3)
+    m1_lane_pass1_bidir(M1Params p, const __grid_constant__ LaneMaps maps, LaneWs ws, LaneWs wsb, int S,
+                        int64_t Ls) {
+    uint64_t *full, *empty;
+    char* smem = lane_setup(full, empty, static_cast<int>(p.state));
+    griddep_launch_dependents();
+    lane_sweep<kLaneBidir, false>(p, maps, ws, &wsb, S, Ls, blockIdx.y, smem, full, empty);
+}
+
+// Pass 2: segments s_off .. from their incoming states.
+template <bool REV>
+__global__ void __launch_bounds__(kLThreads, 3)
+    m1_lane_pass2(M1Params p, const __grid_constant__ LaneMaps maps, LaneWs ws, int S, int64_t Ls, int s_off) {
+    uint64_t *full, *empty;
+    char* smem = lane_setup(full, empty, static_cast<int>(p.state));
+    lane_sweep<kLaneRescan, REV>(p, maps, ws, nullptr, S, Ls, blockIdx.y + s_off, smem, full, empty);
+}
+
+// Carry across segments in traversal order.  FIRST: segment 0's hend is its
+// true end state, the carry fills h_in of segments 1..S-1; otherwise every
+// hend is from zero, the carry starts at h0 and ends in last_state.
+template <bool FIRST>
+__global__ void m1_lane_carry(M1Params p, LaneWs ws, int S) {
+    const int64_t rows_all = p.batch * p.dim, N = p.state;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    griddep_launch_dependents();
+    griddep_wait();
+    if (i >= rows_all * N) return;
+    const int64_t row = i / N, n = i % N;
+    const float a = p.A[(row % p.dim) * N + n] * kLog2e;
+    float h = FIRST ? __ldg(ws.hend + row * 16 + n) : (p.h0 ? p.h0[i] : 0.f);
+    const int k_end = FIRST ? S - 1 : S;
+    for (int k0 = FIRST ? 1 : 0; k0 < k_end; k0 += 8) {
+        float ds[8], he[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int64_t sr = static_cast<int64_t>(k0 + u) * rows_all + row;
+            ds[u] = k0 + u < k_end ? __ldg(ws.dtsum + sr) : 0.f;
+            he[u] = k0 + u < k_end ? __ldg(ws.hend + sr * 16 + n) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (k0 + u >= k_end) break;
+            ws.hin[(static_cast<int64_t>(k0 + u) * rows_all + row) * 16 + n] = h;
+            h = fmaf(ex2_approx(a * ds[u]), h, he[u]);
+        }
+    }
+    if (FIRST && S > 1) ws.hin[(static_cast<int64_t>(S - 1) * rows_all + row) * 16 + n] = h;
+    if (!FIRST && p.last_state) p.last_state[i] = h;
+}
+
+// ---- host side --------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// 2D map over a row-major (rows, len) fp32 matrix, box (box_rows, 32 steps).
+cudaError_t make_map(CUtensorMap* m, const float* base, int64_t len, int64_t rows, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(len), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(len) * 4};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kLT), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t make_maps(const M1Params& p, LaneMaps* m) {
+    std::memset(m, 0, sizeof(*m));
+    const int64_t rows = p.batch * p.dim, bcrows = p.batch * p.groups * p.state;
+    cudaError_t e = make_map(&m->delta, p.delta, p.len, rows, kLRows);
+    if (e == cudaSuccess) e = make_map(&m->u, p.u, p.len, rows, kLRows);
+    if (e == cudaSuccess && p.z) e = make_map(&m->z, p.z, p.len, rows, kLRows);
+    if (e == cudaSuccess) e = make_map(&m->B, p.B, p.len, bcrows, static_cast<int>(p.state));
+    if (e == cudaSuccess && p.C) e = make_map(&m->C, p.C, p.len, bcrows, static_cast<int>(p.state));
+    return e;
+}
+
+template <class K>
+cudaError_t allow_smem(K kern) {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+}
+
+// Concurrent CTAs of the lane kernels per device (SMs x resident CTAs per SM).
+int lane_slots() {
+    static int cache[64] = {0};
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+    int sms = 148, per = 3;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (allow_smem(m1_lane_pass2<false>) == cudaSuccess)
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, m1_lane_pass2<false>, kLThreads, kSmemBytes);
+    if (per < 1) per = 1;
+    const int v = sms * per;
+    if (dev >= 0 && dev < 64) cache[dev] = v;
+    return v;
+}
+
+// Segment count: the cheapest S under a wave model.  Each pass costs
+// (steps per segment) x (waves of CTAs it needs); a split scan makes two
+// passes (pass 1 over S-1 segments, pass 2 over S-1), an unsplit one a
+// single pass.  passes_all: the bidirectional (3 passes over all S
+// segments) and final-state-only (1 pass over all S) forms.
+int lane_pick_segments(const M1Params& p, int passes_all) {
+    const int64_t gsz = p.dim / p.groups;
+    const int64_t rb = ((gsz + kLRows - 1) / kLRows) * p.batch * p.groups;
+    const int64_t slots = lane_slots();
+    int best = 1;
+    double best_cost = -1;
+    for (int S = 1; S <= 1024; S *= 2) {
+        if (p.len % S != 0 || (p.len / S) % 4 != 0) break;
+        if (S > 1 && p.len / S < 128) break;
+        const int64_t Ls = p.len / S;
+        const int64_t ctas = passes_all ? rb * S : rb * (S > 1 ? S - 1 : 1);
+        if (ctas > 65535 * 64) break;
+        const int64_t waves = (ctas + slots - 1) / slots;
+        const int passes = passes_all ? passes_all : (S > 1 ? 2 : 1);
+        // a small fixed cost per pass (pipeline fill, launch) breaks ties
+        const double cost = static_cast<double>(passes) * (Ls * waves + 64);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = S;
+        }
+    }
+    return best;
+}
+
+bool lane_applicable(const M1Params& p) {
+    if (p.state > 16 || p.state < 1 || p.len % 4 != 0 || p.len < 4) return false;
+    if (!m1_pointers_aligned16(p)) return false;
+    if (p.len > (int64_t(1) << 30) || p.batch * p.dim > (int64_t(1) << 30)) return false;
+    if (p.batch * p.groups * p.state > (int64_t(1) << 30)) return false;
+    if (p.dim % p.groups != 0) return false;
+    return encode_fn() != nullptr;
+}
+
+struct LaneWsAlloc {
+    void* raw = nullptr;
+    cudaStream_t stream;
+    explicit LaneWsAlloc(cudaStream_t s) : stream(s) {}
+    cudaError_t get(size_t bytes) {
+        cudaMemPool_t pool = nullptr;
+        cudaError_t e = device_workspace_pool(&pool);
+        if (e != cudaSuccess) return e;
+        return cudaMallocFromPoolAsync(&raw, bytes, pool, stream);
+    }
+    cudaError_t release() { return raw ? cudaFreeAsync(raw, stream) : cudaSuccess; }
+};
+
+void carve(float* base, size_t S, size_t rows, LaneWs* ws) {
+    const size_t st = S * rows * 16;
+    ws->hend = base;
+    ws->hin = base + st;
+    ws->dtsum = base + 2 * st;
+}
+
+}  // namespace
+
+// The kKnobM1Segments override, where it divides the sequence into
+// segments of a multiple of 4 steps.
+static int forced_segments(const M1Params& p) {
+    const int s = kernel_override(kKnobM1Segments);
+    return (s >= 1 && p.len % s == 0 && (p.len / s) % 4 == 0) ? s : 0;
+}
+
+int m1_lane_segments(const M1Params& p) {
+    if (!lane_applicable(p)) return 0;
+    if (const int s = forced_segments(p)) return s;
+    if (p.segments > 0 && p.len % p.segments == 0 && (p.len / p.segments) % 4 == 0) return p.segments;
+    return lane_pick_segments(p, p.out ? 0 : 1);
+}
+
+cudaError_t m1_lane_launch(const M1Params& p, int S, cudaStream_t stream) {
+    const int64_t rows = p.batch * p.dim, Ls = p.len / S;
+    LaneMaps maps;
+    cudaError_t e = make_maps(p, &maps);
+    if (e != cudaSuccess) return e;
+    const bool first = p.out != nullptr;  // out == nullptr: final state only
+    auto k1 = first ? (p.reverse ? m1_lane_pass1<true, true> : m1_lane_pass1<true, false>)
+                    : (p.reverse ? m1_lane_pass1<false, true> : m1_lane_pass1<false, false>);
+    auto k2 = p.reverse ? m1_lane_pass2<true> : m1_lane_pass2<false>;
+    if ((e = allow_smem(k1)) != cudaSuccess || (e = allow_smem(k2)) != cudaSuccess) return e;
+    LaneWsAlloc alloc(stream);
+    LaneWs ws = {nullptr, nullptr, nullptr};
+    if (S > 1 || !first) {
+        e = alloc.get((2 * static_cast<size_t>(S) * rows * 16 + static_cast<size_t>(S) * rows) * sizeof(float));
+        if (e != cudaSuccess) return e;
+        carve(static_cast<float*>(alloc.raw), S, rows, &ws);
+    }
+    const int64_t gsz = p.dim / p.groups;
+    const unsigned gx = static_cast<unsigned>(((gsz + kLRows - 1) / kLRows) * p.batch * p.groups);
+    // pass 1 covers segments 0 .. S-2 when the first runs in full (all of
+    // them for S == 1), every segment otherwise
+    const unsigned s1 = first ? static_cast<unsigned>(S > 1 ? S - 1 : 1) : static_cast<unsigned>(S);
+    k1<<<dim3(gx, s1), kLThreads, kSmemBytes, stream>>>(p, maps, ws, S, Ls);
+    note_launch();
+    e = cudaGetLastError();
+    if (e == cudaSuccess && (S > 1 || !first)) {
+        const int64_t n = rows * p.state;
+        const dim3 cg(static_cast<unsigned>((n + 255) / 256));
+        e = first ? launch_pdl(m1_lane_carry<true>, cg, dim3(256), stream, p, ws, S)
+                  : launch_pdl(m1_lane_carry<false>, cg, dim3(256), stream, p, ws, S);
+        note_launch();
+    }
+    if (e == cudaSuccess && first && S > 1) {
+        e = launch_pdl_smem(k2, dim3(gx, static_cast<unsigned>(S - 1)), dim3(kLThreads), kSmemBytes, stream, p, maps,
+                       ws, S, Ls, 1);
+        note_launch();
+    }
+    const cudaError_t ef = alloc.release();
+    return e != cudaSuccess ? e : ef;
+}
+
+// Both traversals of the same inputs: fwd (reverse 0) and bwd (reverse 1)
+// share every input but out / last_state (and out_acc).  One shared pass 1,
+// a carry per direction, a pass 2 per direction over every segment: three
+// exps per (step, state).  bwd.out == fwd.out with bwd.out_acc sums the two
+// outputs in place (bwd's pass 2 runs after fwd's).  fwd.out == nullptr:
+// final states only.  Each direction's carry starts at its own h0.
+int m1_lane_bidir_segments(const M1Params& fwd) {
+    if (!lane_applicable(fwd)) return 0;
+    if (const int s = forced_segments(fwd)) return s;
+    return lane_pick_segments(fwd, fwd.out ? 3 : 1);
+}
+
+cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S, cudaStream_t stream) {
+    const int64_t rows = fwd.batch * fwd.dim, Ls = fwd.len / S;
+    LaneMaps maps;
+    cudaError_t e = make_maps(fwd, &maps);
+    if (e != cudaSuccess) return e;
+    if ((e = allow_smem(m1_lane_pass1_bidir)) != cudaSuccess || (e = allow_smem(m1_lane_pass2<false>)) != cudaSuccess ||
+        (e = allow_smem(m1_lane_pass2<true>)) != cudaSuccess)
+        return e;
+    const size_t per = 2 * static_cast<size_t>(S) * rows * 16 + static_cast<size_t>(S) * rows;
+    LaneWsAlloc alloc(stream);
+    if ((e = alloc.get(2 * per * sizeof(float))) != cudaSuccess) return e;
+    LaneWs wf, wb;
+    carve(static_cast<float*>(alloc.raw), S, rows, &wf);
+    carve(static_cast<float*>(alloc.raw) + per, S, rows, &wb);
+    const int64_t gsz = fwd.dim / fwd.groups;
+    const unsigned gx = static_cast<unsigned>(((gsz + kLRows - 1) / kLRows) * fwd.batch * fwd.groups);
+    const dim3 grid(gx, static_cast<unsigned>(S)), block(kLThreads);
+    m1_lane_pass1_bidir<<<grid, block, kSmemBytes, stream>>>(fwd, maps, wf, wb, S, Ls);
+    note_launch();
+    e = cudaGetLastError();
+    const int64_t n = rows * fwd.state;
+    const dim3 cg(static_cast<unsigned>((n + 255) / 256));
+    // the carries end in last_state; pass 2 leaves it alone
+    M1Params f2 = fwd, b2 = bwd;
+    f2.last_state = nullptr;
+    b2.last_state = nullptr;
+    if (e == cudaSuccess) e = launch_pdl(m1_lane_carry<false>, cg, dim3(256), stream, fwd, wf, S);
+    if (e == cudaSuccess) note_launch();
+    if (e == cudaSuccess) e = launch_pdl(m1_lane_carry<false>, cg, dim3(256), stream, bwd, wb, S);
+    if (e == cudaSuccess) note_launch();
+    if (fwd.out) {
+        LaneMaps mb = maps;  // bwd reads the same inputs
+        if (e == cudaSuccess)
+            e = launch_pdl_smem(m1_lane_pass2<false>, grid, block, kSmemBytes, stream, f2, maps, wf, S, Ls, 0);
+        if (e == cudaSuccess) note_launch();
+        if (e == cudaSuccess)
+            e = launch_pdl_smem(m1_lane_pass2<true>, grid, block, kSmemBytes, stream, b2, mb, wb, S, Ls, 0);
+        if (e == cudaSuccess) note_launch();
+    }
+    const cudaError_t ef = alloc.release();
+    return e != cudaSuccess ? e : ef;
+}
+
+int m1_lane_status_and_clear() {
+    int v = 0, z = 0;
+    cudaMemcpyFromSymbol(&v, g_m1_status, sizeof(int));
+    if (v) cudaMemcpyToSymbol(g_m1_status, &z, sizeof(int));
+    return v;
+}
+
+}  // namespace b200scan

@@ -385,10 +385,9 @@ __global__ void m1_seg_fold_kernel(M1Params p, int64_t S, const float* hend, con
 }  // namespace
 
 int m1_timesplit_segments(const M1Params& p) {
-    if (const char* v = getenv("B200SCAN_M1_TIMESPLIT")) {
-        const int s = atoi(v);
-        if (s <= 1) return 1;
-        return (p.len % s == 0 && (p.len / s) % 4 == 0) ? s : 1;
+    if (kernel_override(kKnobM1Kernel) == 4) {
+        const int s = kernel_override(kKnobM1Segments);
+        if (s > 1 && p.len % s == 0 && (p.len / s) % 4 == 0) return s;
     }
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -455,12 +454,17 @@ cudaError_t m1_final_state_launch(const M1Params& p, cudaStream_t stream) {
     q.out = nullptr;
     q.z = nullptr;
     q.d_skip = nullptr;
-    const int S = m1_seg2_segments(q);
-    if (S > 0) return m1_seg2_launch(q, S, stream);
+    const int S = m1_lane_segments(q);
+    if (S > 0) return m1_lane_launch(q, S, stream);
     const bool tile_ok = q.state <= 16 && q.len <= (INT32_MAX / 4) && q.state * q.len <= INT32_MAX;
     return tile_ok ? m1_tile_launch(q, 1, stream) : cudaErrorNotSupported;
 }
 
+// Dispatch: backend 1 is the sequential cross-check kernel; otherwise the
+// lane kernel where it applies (d_state <= 16, length a multiple of 4,
+// 16-byte aligned tensors), the row-tile kernel (with a time split for long
+// sequences of few rows) for the other lengths with d_state <= 16, and the
+// block-chunked kernel for d_state > 16.
 cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) {
     if (backend == kBackendSequential) {
         const int64_t BD = p.batch * p.dim;
@@ -470,30 +474,15 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
         note_launch();
         return cudaGetLastError();
     }
-    // Otherwise, d_state <= 16: the pipelined row-tile kernel.
-    // B200SCAN_M1_VARIANT overrides for tuning sweeps: 1-4 tile shapes,
-    // 5/6/7 row-sequential with 4/2/1 lanes per row, 0 the block-chunked
-    // kernel (also the path for d_state > 16).
-    int variant = -1;
-    if (const char* v = getenv("B200SCAN_M1_VARIANT")) variant = atoi(v);
-    const int64_t rows = p.batch * p.dim;
-    (void)rows;
-    if (variant == 8 && m1_twopass_applicable(p)) return m1_twopass_launch(p, stream);
-    // default: the fold-free two-pass kernel where it applies (length a
-    // multiple of 64, 16-byte aligned, d_state <= 16); variant 12 forces it
-    if (variant == -1 || variant == 12) {
-        const int S = m1_seg2_segments(p);
-        if (S > 0) return m1_seg2_launch(p, S, stream);
-    }
-    if ((variant == 5 || variant == 6 || variant == 7) && m1_rowseq_applicable(p))
-        return m1_rowseq_launch(p, variant == 6 ? 2 : variant == 7 ? 1 : 4, stream);
+    const int force = kernel_override(kKnobM1Kernel);
+    if (force == 0 || force == 1)
+        if (const int S = m1_lane_segments(p)) return m1_lane_launch(p, S, stream);
     const bool tile_ok = p.state <= 16 && p.len <= (INT32_MAX / 4) && p.state * p.len <= INT32_MAX;
-    if (tile_ok && (variant == -1 || variant == 1)) {
+    if (tile_ok && force != 3) {
         const int S = m1_timesplit_segments(p);
-        if (S > 1) return m1_timesplit_launch(p, S, stream);
+        if (S > 1 && force != 2) return m1_timesplit_launch(p, S, stream);
+        return m1_tile_launch(p, 1, stream);
     }
-    if (tile_ok && variant != 0) return m1_tile_launch(
-        p, (variant >= 1 && variant <= 4) || (variant >= 9 && variant <= 11) ? variant : 1, stream);
     switch (m1_pick_channels_per_cta(p.batch * p.dim)) {
         case 32: return launch_chunked<32, 16>(p, stream);
         case 16: return launch_chunked<16, 16>(p, stream);
@@ -502,21 +491,19 @@ cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream) 
     }
 }
 
-// Whether a bidirectional call takes the shared-pass form of the two-pass
-// kernel (default where that kernel applies; B200SCAN_M1_BIDIR_SHARED=0 runs
-// the two traversals as independent scans).
+// Whether a bidirectional call takes the shared-first-pass form of the lane
+// kernel (wherever that kernel applies and the backend is not the
+// sequential cross-check).
 static int bidir_shared_segments(const M1Params& fwd, int backend) {
-    if (backend == kBackendSequential) return 0;
-    if (const char* v = getenv("B200SCAN_M1_VARIANT"))
-        if (atoi(v) != -1 && atoi(v) != 12) return 0;
-    if (const char* v = getenv("B200SCAN_M1_BIDIR_SHARED"))
-        if (v[0] == '0') return 0;
-    return m1_seg2_segments(fwd);
+    if (backend == kBackendSequential || kernel_override(kKnobM1BidirShared) == 1) return 0;
+    const int force = kernel_override(kKnobM1Kernel);
+    if (force != 0 && force != 1) return 0;
+    return m1_lane_bidir_segments(fwd);
 }
 
 cudaError_t m1_bidir_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                             cudaStream_t stream) {
-    if (const int S = bidir_shared_segments(fwd, backend)) return m1_seg2_bidir_launch(fwd, bwd, S, stream);
+    if (const int S = bidir_shared_segments(fwd, backend)) return m1_lane_bidir_launch(fwd, bwd, S, stream);
     cudaError_t e = m1_scan_launch(fwd, backend, stream);
     if (e != cudaSuccess) return e;
     return m1_scan_launch(bwd, backend, stream);
@@ -528,7 +515,7 @@ cudaError_t m1_bidir_states_launch(const M1Params& fwd, const M1Params& bwd, int
     f.out = r.out = nullptr;
     f.z = r.z = nullptr;
     f.d_skip = r.d_skip = nullptr;
-    if (const int S = bidir_shared_segments(f, backend)) return m1_seg2_bidir_launch(f, r, S, stream);
+    if (const int S = bidir_shared_segments(f, backend)) return m1_lane_bidir_launch(f, r, S, stream);
     const cudaError_t e = m1_final_state_launch(f, stream);
     return e != cudaSuccess ? e : m1_final_state_launch(r, stream);
 }
@@ -548,7 +535,7 @@ cudaError_t m1_bidir_sum_launch(const M1Params& fwd, const M1Params& bwd, int ba
         M1Params r = bwd;
         r.out = fwd.out;
         r.out_acc = 1;
-        return m1_seg2_bidir_launch(fwd, r, S, stream);
+        return m1_lane_bidir_launch(fwd, r, S, stream);
     }
     const int64_t n = fwd.batch * fwd.dim * fwd.len;
     cudaMemPool_t pool = nullptr;

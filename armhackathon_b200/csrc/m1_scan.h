@@ -35,6 +35,8 @@ struct M1Params {
     // Two-pass kernel only: add y to what out already holds (the second
     // traversal of a bidirectional scan summed in place).
     int out_acc = 0;
+    // Lane kernel only: segment count to use (0: chosen from the shape).
+    int segments = 0;
 };
 
 bool m1_pointers_aligned16(const M1Params& p);
@@ -49,21 +51,26 @@ cudaError_t m1_final_state_launch(const M1Params& p, cudaStream_t stream);
 // dt (batch, dim), p.B/p.C (batch, groups, state), p.out (batch, dim);
 // state (batch, dim, state) is read and updated in place.
 cudaError_t m1_decode_launch(const M1Params& p, float* state, cudaStream_t stream);
-// Fold-free two-pass segmented kernel (m1_seg2.cu): segment count (0: not
+// Lanes-over-states kernel (m1_lane.cu), the default for d_state <= 16,
+// length a multiple of 4 and 16-byte aligned tensors: segment count (0: not
 // applicable) and launcher.
-int m1_seg2_segments(const M1Params& p);
-// Both traversals of one bidirectional scan with the two-pass kernel (bwd is
-// fwd with reverse = 1 and its own out / last_state; bwd.out_acc sums into
-// fwd.out).
+int m1_lane_segments(const M1Params& p);
+cudaError_t m1_lane_launch(const M1Params& p, int segments, cudaStream_t stream);
+// Both traversals of one bidirectional scan with the lane kernel: one shared
+// first pass (bwd is fwd with reverse = 1 and its own out / last_state;
+// bwd.out_acc sums into fwd.out; fwd.out == nullptr: final states only).
+int m1_lane_bidir_segments(const M1Params& fwd);
+cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int segments,
+                                 cudaStream_t stream);
+// Device status of the lane kernels (1: a bounded staging wait expired),
+// cleared by the read.
+int m1_lane_status_and_clear();
 // Final states of both traversals (no outputs); each from its own h0.
 cudaError_t m1_bidir_states_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                                    cudaStream_t stream);
 // Bidirectional scan summed into fwd.out (bwd.out unused).
 cudaError_t m1_bidir_sum_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                                 cudaStream_t stream);
-cudaError_t m1_seg2_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S,
-                                 cudaStream_t stream);
-cudaError_t m1_seg2_launch(const M1Params& p, int segments, cudaStream_t stream);
 // Segments of a time-split Mamba-1 scan (1: no split) and its launcher.
 int m1_timesplit_segments(const M1Params& p);
 cudaError_t m1_timesplit_launch(const M1Params& p, int segments, cudaStream_t stream);
@@ -71,12 +78,6 @@ int m1_pick_channels_per_cta(int64_t rows);
 cudaError_t m1_scan_launch(const M1Params& p, int backend, cudaStream_t stream);
 // Pipelined row-tile kernel (m1_tile.cu); requires state <= 16.
 cudaError_t m1_tile_launch(const M1Params& p, int variant, cudaStream_t stream);
-// Row-sequential kernel (m1_rowseq.cu) and its applicability test.
-bool m1_rowseq_applicable(const M1Params& p);
-cudaError_t m1_rowseq_launch(const M1Params& p, int lanes_per_row, cudaStream_t stream);
-// Two-pass kernel (m1_twopass.cu) and its applicability test.
-bool m1_twopass_applicable(const M1Params& p);
-cudaError_t m1_twopass_launch(const M1Params& p, cudaStream_t stream);
 // Forward and reverse scans of the same inputs (fused bidirectional entry).
 cudaError_t m1_bidir_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                             cudaStream_t stream);

@@ -676,9 +676,9 @@ cudaError_t m3_chunk_launch(const M3Params& p, cudaStream_t stream) {
     // measured faster than the sequential form (one CTA per (batch, head)) on
     // every benchmarked shape (config 2 1.81 vs 2.19 ms, config 3 23.2 vs 30.2,
     // config 4a 7.8 vs 17.4); the sequential form remains for single-chunk
-    // sequences.  B200SCAN_M3_CHUNK_SEQ=1 / =0 forces one or the other.
+    // sequences.  The kKnobM3ChunkForm override forces one or the other.
     bool split = p.len > kQR / R;  // more than one chunk of (step, rank) rows
-    if (const char* v = std::getenv("B200SCAN_M3_CHUNK_SEQ")) split = v[0] != '1';
+    if (const int f = kernel_override(kKnobM3ChunkForm)) split = f == 2;
     if (split && (p.dqk * p.dv) % 4 == 0)
         return R == 4 ? m3_chunk_launch_split<4>(p, stream)
              : R == 2 ? m3_chunk_launch_split<2>(p, stream)

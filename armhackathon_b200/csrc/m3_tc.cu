@@ -1767,8 +1767,7 @@ cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
 
 cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
     if (p.angles || p.rank > 1) return m3_tc_launch_fused(p, stream);
-    const char* v = std::getenv("B200SCAN_M3_TC_SPLIT");
-    return (v && v[0] == '1') ? m3_tc_launch_split(p, stream) : m3_tc_launch_fused(p, stream);
+    return kernel_override(kKnobM3TcSplit) == 1 ? m3_tc_launch_split(p, stream) : m3_tc_launch_fused(p, stream);
 }
 
 int m3_tc_status_and_clear() {

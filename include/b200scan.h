@@ -255,10 +255,11 @@ int arm_scan_selective_state_update_f32_async(const ArmScanDims* dims, float* st
                                               const float* dt_bias, int dt_softplus, float* out,
                                               void* stream);
 
-/* Extension (no counterpart in the reference): status of the tensor-core
- * kernels (backend 3).  Their waits on their own MMA completions are
- * bounded; an expired wait abandons the remaining tiles and sets a device
- * flag.  The synchronous entry points check it themselves (code 7); after
+/* Extension (no counterpart in the reference): status of the kernels with
+ * device-side waits: the tensor-core kernels (backend 3), whose waits on
+ * their own MMA completions are bounded, and the Mamba-1 lane kernel, whose
+ * waits on its own TMA staging are bounded; an expired wait abandons the
+ * remaining work and sets a device flag.  The synchronous entry points check it themselves (code 7); after
  * an _async call, synchronize the stream and call this: returns 0, or 7
  * (message in arm_scan_last_error) if a wait expired since the last check,
  * and clears the flag. */
@@ -268,6 +269,18 @@ int arm_scan_tensor_status(void);
  * kernels this library has launched in the process so far (all devices,
  * all threads); the difference around a call is that call's launch count. */
 unsigned long long arm_scan_kernel_launches(void);
+
+/* Extension (tests and measurements, no counterpart in the reference):
+ * process-wide kernel-selection overrides; value 0 everywhere is the
+ * default dispatch.  Knobs: 0 Mamba-1 kernel (0 auto, 1 lane kernel,
+ * 2 row-tile, 3 block-chunked, 4 row-tile with a time split); 1 segment
+ * count of the lane / time-split kernels (0 auto; ignored unless it divides
+ * the length into segments of a multiple of 4 steps); 2 bidirectional form
+ * (0 shared first pass, 1 two independent traversals); 3 Mamba-3 tensor
+ * kernel (0 fused, 1 three-launch form); 4 Mamba-3 fp32 chunk form (0 auto,
+ * 1 sequential, 2 chunk-parallel); 5 programmatic dependent launch (0 on,
+ * 1 off).  Returns 0, or 4 for an unknown knob or a negative value. */
+int arm_scan_set_kernel_override(int knob, int value);
 
 /* Extension: the bidirectional scan merged by sum, as the reference's
  * bidirectional_scan(merge="sum") computes it from the two outputs of

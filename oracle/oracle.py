@@ -225,6 +225,28 @@ def m3_mimo(q, k, v, adt, dt, trap, q_bias, k_bias, cos, sin, psi, zeta, phi,
     return (out, ls) if want_state else out
 
 
+def m3_mimo_x(x, b, c, adt, dt, trap, cos, sin, D=None, reverse=False, dtype=np.float64,
+              nthreads=1, want_state=False):
+    """Mamba-3 MIMO with X given per rank (the h_t / Y_t = h_t C_t form):
+    x (b, l, h, dv, r), b/c (b, l, dqk, r) -> out (b, l, h, dv, r) (and
+    last_state (b, h, dv, dqk) when ``want_state``).  See
+    oracle_m3_mimo_x in scan_oracle_body.h."""
+    d_t = np.dtype(dtype)
+    suffix = "f64" if d_t == np.float64 else "f32"
+    x, b, c = _arr(x, d_t), _arr(b, d_t), _arr(c, d_t)
+    bsz, length, heads, dv, rank = x.shape
+    dqk = b.shape[2]
+    args = [_arr(t, d_t) for t in (adt, dt, trap, cos, sin)]
+    D = _arr(D, d_t)
+    out = np.empty_like(x)
+    ls = np.empty((bsz, heads, dv, dqk), d_t)
+    dims = M3Dims(bsz, heads, dv, dqk, length, rank)
+    _call(f"oracle_m3_mimo_x_{suffix}", ctypes.byref(dims), _p(x), _p(b), _p(c),
+          *[_p(t) for t in args], ctypes.c_size_t(cos.shape[-1]), _p(D),
+          ctypes.c_int(bool(reverse)), _p(out), _p(ls), ctypes.c_int(nthreads))
+    return (out, ls) if want_state else out
+
+
 def bf16_round(x):
     """Round-to-nearest-even to bfloat16, returned as float32."""
     x = np.ascontiguousarray(x, np.float32)

@@ -352,3 +352,93 @@ extern "C" int FN(oracle_m3_mimo)(const oracle_m3_dims* dm, const T* q, const T*
     ROWS_END
     return 0;
 }
+
+/*
+ * Mamba-3 MIMO with the input given per rank (the configuration whose state
+ * recurrence is written out in terms of X, B, C):
+ *   h_t = alpha_t h_{t-1} + beta_t X_{t-1} B_{t-1}^T + gamma_t X_t B_t^T
+ *   Y_t = h_t C_t (+ D X_t)
+ * per (batch, head), h of shape (dv, dqk), X_t of shape (dv, rank),
+ * B_t, C_t of shape (dqk, rank).  The gates are the SISO/MIMO ones of
+ * tests/reference/mamba3_ref.py:27-39 (FN(m3_gates) above):
+ *   alpha_t = exp(adt_t), gamma_t = dt_t sigmoid(trap_t),
+ *   beta_t  = alpha_t dt_t (1 - sigmoid(trap_t))  -- the trapezoid's share
+ * of the previous step, decayed by this step's alpha (mamba3_ref.py:27-39);
+ * "previous" is t-1 forward and t+1 under reverse; the first step of a
+ * traversal has no previous term.  B and C are RoPE-rotated split-halves
+ * over the first `pairs` lanes (mamba3_ref.py:285-298) with the step's
+ * cos/sin, as in the MIMO op.  This is the op of mamba3_ref.py:305-411 with
+ * x_r given directly (replacing the psi projection at :384) and the per-rank
+ * outputs returned without the zeta gate and phi reduction (:405-411).
+ * Layouts: x, out (batch, len, heads, dv, rank); b, c (batch, len, dqk, rank);
+ * adt, dt, trap (batch, heads, len); cos, sin (batch, len, heads, dqk/2);
+ * d_skip (heads) nullable; last_state (batch, heads, dv, dqk) = h after the
+ * last step.
+ */
+extern "C" int FN(oracle_m3_mimo_x)(const oracle_m3_dims* dm, const T* x, const T* bm,
+                       const T* cm, const T* adt, const T* dt, const T* trap,
+                       const T* cosv, const T* sinv, size_t pairs, const T* d_skip,
+                       int reverse, T* out, T* last_state, int nthreads) {
+    if (!dm || !dm->batch || !dm->heads || !dm->dv || !dm->dqk || !dm->len ||
+        !dm->rank || (dm->dqk & 1))
+        return 2;
+    const size_t heads = dm->heads, P = dm->dv, N = dm->dqk, len = dm->len;
+    const size_t R = dm->rank, half = N / 2;
+    if (pairs > half) pairs = half;
+    ROWS_BEGIN(dm->batch * heads)
+        T* h = (T*)malloc(P * N * sizeof(T));
+        T* br = (T*)malloc(N * R * sizeof(T));     /* this step's rotated B [n][r] */
+        T* bp = (T*)malloc(N * R * sizeof(T));     /* previous step's rotated B */
+        T* cr = (T*)malloc(N * R * sizeof(T));
+        T* xp = (T*)malloc(P * R * sizeof(T));     /* previous step's X */
+        for (size_t bh = r0; bh < r1; ++bh) {
+            const size_t bi = bh / heads, hd = bh % heads;
+            const size_t gate_base = (bi * heads + hd) * len;
+            const T dsk = d_skip ? d_skip[hd] : (T)0;
+            for (size_t j = 0; j < P * N; ++j) h[j] = 0;
+            for (size_t i = 0; i < len; ++i) {
+                const size_t t = reverse ? len - 1 - i : i;
+                const size_t g = gate_base + t;
+                const T lam = FN(sigmoid)(trap[g]);
+                const T alpha = EXP(adt[g]);
+                const T gamma = dt[g] * lam;
+                const T beta = alpha * dt[g] * ((T)1 - lam);
+                const size_t bc_off = (bi * len + t) * N * R;
+                const size_t cs_off = ((bi * len + t) * heads + hd) * half;
+                for (size_t n = 0; n < N * R; ++n) { br[n] = bm[bc_off + n]; cr[n] = cm[bc_off + n]; }
+                for (size_t pr = 0; pr < pairs; ++pr) {
+                    const T cs = cosv[cs_off + pr], sn = sinv[cs_off + pr];
+                    for (size_t r = 0; r < R; ++r) {
+                        T a0 = br[pr * R + r], a1 = br[(half + pr) * R + r];
+                        br[pr * R + r] = a0 * cs - a1 * sn; br[(half + pr) * R + r] = a0 * sn + a1 * cs;
+                        a0 = cr[pr * R + r]; a1 = cr[(half + pr) * R + r];
+                        cr[pr * R + r] = a0 * cs - a1 * sn; cr[(half + pr) * R + r] = a0 * sn + a1 * cs;
+                    }
+                }
+                const T* xt = x + ((bi * len + t) * heads + hd) * P * R;
+                for (size_t p = 0; p < P; ++p)
+                    for (size_t n = 0; n < N; ++n) {
+                        T cur = 0, prev = 0;
+                        for (size_t r = 0; r < R; ++r) {
+                            cur = cur + xt[p * R + r] * br[n * R + r];
+                            if (i > 0) prev = prev + xp[p * R + r] * bp[n * R + r];
+                        }
+                        h[p * N + n] = alpha * h[p * N + n] + beta * prev + gamma * cur;
+                    }
+                T* o = out + ((bi * len + t) * heads + hd) * P * R;
+                for (size_t p = 0; p < P; ++p)
+                    for (size_t r = 0; r < R; ++r) {
+                        T s = 0;
+                        for (size_t n = 0; n < N; ++n) s = s + h[p * N + n] * cr[n * R + r];
+                        o[p * R + r] = s + dsk * xt[p * R + r];
+                    }
+                for (size_t j = 0; j < P * R; ++j) xp[j] = xt[j];
+                for (size_t n = 0; n < N * R; ++n) bp[n] = br[n];
+            }
+            if (last_state)
+                for (size_t j = 0; j < P * N; ++j) last_state[bh * P * N + j] = h[j];
+        }
+        free(h); free(br); free(bp); free(cr); free(xp);
+    ROWS_END
+    return 0;
+}

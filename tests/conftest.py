@@ -21,3 +21,20 @@ def pytest_configure(config):
 @pytest.fixture(scope="session")
 def golden_dir():
     return GOLDEN
+
+
+@pytest.fixture
+def knobs():
+    """Set library kernel-selection overrides (``_ffi.KNOBS``) for one test;
+    every knob it set goes back to the default (0) afterwards."""
+    from armhackathon_b200 import _ffi
+    used = []
+
+    def set_knobs(**kw):
+        for k, v in kw.items():
+            _ffi.set_kernel_override(k, v)
+            used.append(k)
+
+    yield set_knobs
+    for k in used:
+        _ffi.set_kernel_override(k, 0)

@@ -30,6 +30,16 @@ What is produced, per family:
   cut to ``MIMO_MAX_L`` tokens the same way, plus ``ref_f64`` from
   ``mamba3_mimo_ref`` (mamba3_ref.py:305).
 
+* ``m3_mimo_x/<case>.npz`` -- the MIMO scan with the input given per rank
+  (BASELINE config 3's formulation: h_t = a_t h_{t-1} + b_t X_{t-1} B_{t-1}^T
+  + g_t X_t B_t^T, Y_t = h_t C_t, per-rank outputs), pinned to the
+  reference's own ``mamba3_mimo_ref``: seeded inputs whose per-rank X is
+  psi_r * v (the form the reference op can express), the reference run once
+  per rank with a one-hot output projection (phi selects rank r, no z), so
+  that its output is rank r's Y (+ D X).  Stored in the per-rank layouts:
+  x (b, l, h, p, r), b/c (b, l, n, r), raw angles (b, l, h, n/4); the
+  reference's B is its K and C its Q; ``ref_f64`` (b, l, h, p, r).
+
 * ``m3_mixer/<case>.npz`` -- the Mamba-3 mixer's prologue (everything between
   ``in_proj`` and the scan call, apps/mamba3_lm/block.py:146-177) run by the
   reference's own ``Mamba3Mixer`` on seeded random weights and inputs: its
@@ -183,6 +193,51 @@ def make_m3(ref):
     return names
 
 
+MIMO_X_CASES = {
+    # name: (batch, len, heads, headdim, d_state, rank, with_D, seed)
+    "r2_small": (1, 24, 2, 8, 16, 2, False, 11),
+    "r4_wide": (2, 20, 3, 16, 32, 4, True, 12),
+    "r4_long": (1, 96, 1, 8, 16, 4, True, 13),
+}
+
+
+def make_mimo_x(ref):
+    import torch
+    sys.path.insert(0, str(ref / "tests"))
+    from reference import mamba3_ref as mod  # noqa: E402
+    names = []
+    for name, (b, l, h, p, n, r, with_d, seed) in MIMO_X_CASES.items():
+        g = torch.Generator().manual_seed(seed)
+        rn = lambda *sh: torch.randn(*sh, generator=g, dtype=torch.float64)  # noqa: E731
+        v = rn(b, l, h, p)
+        psi = rn(h, r, p)
+        Q = rn(b, l, r, 1, n) / np.sqrt(n * r)     # C
+        K = rn(b, l, r, 1, n) / np.sqrt(n * r)     # B
+        dt = torch.nn.functional.softplus(rn(b, h, l) - 2)
+        A = -torch.exp(torch.rand(h, generator=g, dtype=torch.float64) * np.log(16))
+        adt = A.view(1, h, 1) * dt
+        trap = rn(b, h, l)
+        ang = torch.atanh(torch.rand(b, l, h, n // 4, generator=g, dtype=torch.float64) * 0.999)
+        D = 1 + 0.1 * rn(h) if with_d else None
+        zero = torch.zeros(h, r, n, dtype=torch.float64)
+        outs = []
+        for rk in range(r):
+            phi = torch.zeros(h, r, p, dtype=torch.float64)
+            phi[:, rk, :] = 1.0
+            outs.append(mod.mamba3_mimo_ref(Q, K, v, adt, dt, trap, zero, zero, psi,
+                                            torch.ones(h, r, p, dtype=torch.float64), phi,
+                                            ang, D=D, Z=None))
+        x = v.unsqueeze(-1) * psi.permute(1, 0, 2).reshape(1, 1, r, h, p).permute(0, 1, 3, 4, 2)
+        arrays = dict(x=x, b=K[:, :, :, 0, :].permute(0, 1, 3, 2), c=Q[:, :, :, 0, :].permute(0, 1, 3, 2),
+                      adt=adt, dt=dt, trap=trap, angles=ang, ref_f64=torch.stack(outs, -1))
+        if D is not None:
+            arrays["D"] = D
+        _save(HERE / "m3_mimo_x" / f"{name}.npz",
+              **{k: np.ascontiguousarray(t.numpy()) for k, t in arrays.items()})
+        names.append(name)
+    return names
+
+
 MIXER_CASES = {
     # name: (Mamba3Mixer kwargs, batch, len, seed)
     "siso_rope_half": (dict(d_model=64, d_state=16, expand=2, headdim=16, rope_fraction=0.5), 2, 33, 1),
@@ -259,6 +314,7 @@ def main():
     }
     index.update({f"m3_{k}": v for k, v in make_m3(ref).items()})
     index["m3_mixer"] = make_mixer(ref)
+    index["m3_mimo_x"] = make_mimo_x(ref)
     (HERE / "index.json").write_text(json.dumps(index, indent=1) + "\n")
     print(json.dumps({k: (len(v) if isinstance(v, list) else v)
                       for k, v in index.items()}))

@@ -146,7 +146,7 @@ def test_bidirectional_fused_and_merges():
 
 @pytest.mark.parametrize("segments", ["1", "2", "4", "16"])
 @pytest.mark.parametrize("shape", [(2, 70, 1024, 13, 2), (1, 64, 4096, 16, 1)])
-def test_bidirectional_shared_first_pass(segments, shape, monkeypatch):
+def test_bidirectional_shared_first_pass(segments, shape, knobs):
     """The bidirectional entries on lengths the two-pass kernel takes: one
     forward walk per segment gives both traversals' segment aggregates (the
     reverse one from running products of the decays), then a carry and a
@@ -154,7 +154,7 @@ def test_bidirectional_shared_first_pass(segments, shape, monkeypatch):
     Slowly decaying states so the carries matter; grouped B/C, ragged
     channel counts, d_state 13; final states through the C entry."""
     from armhackathon_b200 import _ffi
-    monkeypatch.setenv("B200SCAN_M1_SEG2_S", segments)
+    knobs(m1_segments=int(segments))
     B, D, L, N, G = shape
     x = _slow_decay_case(B, D, L, N, seed=L + N)
     if G > 1:
@@ -187,12 +187,12 @@ def test_bidirectional_shared_first_pass(segments, shape, monkeypatch):
 
 
 @pytest.mark.parametrize("shared", ["1", "0"])
-def test_bidirectional_final_states_and_sum_with_h0(shared, monkeypatch):
+def test_bidirectional_final_states_and_sum_with_h0(shared, knobs):
     """The two calls a sequence split over devices makes: both traversals'
     final states from zero (one shared first pass), then both outputs summed
     from given incoming states (forward one enters at t = 0, reverse one at
     t = L - 1); with and without the shared pass."""
-    monkeypatch.setenv("B200SCAN_M1_BIDIR_SHARED", shared)
+    knobs(m1_bidir_independent=0 if shared == "1" else 1)
     B, D, L, N = 2, 70, 1024, 13
     x = _slow_decay_case(B, D, L, N, seed=11)
     a = arm()
@@ -213,13 +213,13 @@ def test_bidirectional_final_states_and_sum_with_h0(shared, monkeypatch):
     assert rel_err(out.cpu().numpy(), wf + wb) <= REL_TOL
 
 
-def test_bidirectional_sum_without_shared_pass(monkeypatch):
+def test_bidirectional_sum_without_shared_pass(knobs):
     """The sum entry where the traversals run as independent scans (forced,
     and on a length the two-pass kernel does not take): second output in
     workspace, then an add kernel."""
     a = arm()
     for env, L in (("0", 1024), ("1", 777)):
-        monkeypatch.setenv("B200SCAN_M1_BIDIR_SHARED", env)
+        knobs(m1_bidir_independent=0 if env == "1" else 1)
         x = random_case(2, 64, L, 16, seed=9)
         wf, wb, _, _ = oracle.m1_scan_bidir(**x, nthreads=8)
         s = a.bidirectional_scan(**cuda(x), merge="sum")
@@ -289,14 +289,14 @@ def test_mixed_host_device_rejected():
     assert rc == 2
 
 
-@pytest.mark.parametrize("variant", ["0", "1", "2", "3", "4", "5", "6", "7", "8", "9", "10",
-                                     "11", "12"])
+@pytest.mark.parametrize("kernel", ["lane", "tile", "chunked"])
 @pytest.mark.parametrize("reverse", [False, True])
-def test_every_kernel_variant_vs_oracle(variant, reverse, monkeypatch):
-    """Each Mamba-1 kernel shape the library can dispatch to (selected with
-    B200SCAN_M1_VARIANT, read at every launch) against the oracle, on a
-    grouped, h0-seeded case with a ragged row count."""
-    monkeypatch.setenv("B200SCAN_M1_VARIANT", variant)
+def test_every_kernel_vs_oracle(kernel, reverse, knobs):
+    """Each Mamba-1 kernel the library can dispatch to (selected with the
+    kernel override) against the oracle, on a grouped, h0-seeded case with a
+    ragged row count."""
+    from armhackathon_b200 import _ffi
+    knobs(m1_kernel=_ffi.M1_KERNELS[kernel])
     inputs = random_case(3, 40, 1028, 16, 2, seed=7)
     rng = np.random.default_rng(1)
     h0 = rng.standard_normal((3, 40, 16)).astype(np.float32)
@@ -319,10 +319,10 @@ def _slow_decay_case(B, D, L, N, seed):
 
 @pytest.mark.parametrize("segments", ["4", "8"])
 @pytest.mark.parametrize("reverse", [False, True])
-def test_time_split_vs_oracle(segments, reverse, monkeypatch):
+def test_time_split_vs_oracle(segments, reverse, knobs):
     """Few rows, long sequence, split in time (state-only pass, segment-decay
     fold, rescan from the carries): output, h0 resume and last_state."""
-    monkeypatch.setenv("B200SCAN_M1_TIMESPLIT", segments)
+    knobs(m1_kernel=4, m1_segments=int(segments))
     B, D, L, N = 2, 24, 8192, 16
     x = _slow_decay_case(B, D, L, N, seed=int(segments))
     h0 = np.random.default_rng(3).standard_normal((B, D, N)).astype(np.float32)
@@ -367,13 +367,11 @@ def test_host_entry_pipelined_matches_device(shape):
 @pytest.mark.parametrize("shape", [(2, 40, 2048, 16, 2), (3, 130, 1024, 13, 1), (1, 8, 4096, 16, 1)])
 @pytest.mark.parametrize("segments", ["1", "2", "4", "16"])
 @pytest.mark.parametrize("reverse", [False, True])
-def test_fold_free_two_pass_vs_oracle(shape, segments, reverse, monkeypatch):
-    """Variant 12 (fold-free two-pass: segment end states, exact segment-decay
-    carries, rescan) on lengths it covers, with grouped B/C, ragged channel
-    counts, d_state 13, h0 and slowly decaying states that carry across
-    segments."""
-    monkeypatch.setenv("B200SCAN_M1_VARIANT", "12")
-    monkeypatch.setenv("B200SCAN_M1_SEG2_S", segments)
+def test_lane_kernel_segments_vs_oracle(shape, segments, reverse, knobs):
+    """The lane kernel at forced segment counts (segment end states, exact
+    segment-decay carries, rescan), with grouped B/C, ragged channel counts,
+    d_state 13, h0 and slowly decaying states that carry across segments."""
+    knobs(m1_kernel=1, m1_segments=int(segments))
     B, D, L, N, G = shape
     x = _slow_decay_case(B, D, L, N, seed=L + N)
     if G > 1:

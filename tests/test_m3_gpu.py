@@ -323,10 +323,10 @@ def test_tensor_core_fused_matches_cos_sin_entry():
 
 
 @pytest.mark.parametrize("split", ["0", "1"])
-def test_tensor_core_cos_sin_split_and_fused(split, monkeypatch):
+def test_tensor_core_cos_sin_split_and_fused(split, knobs):
     """The reference-layout entry's two tensor-core forms (one persistent
     launch; three launches with B200SCAN_M3_TC_SPLIT=1) against the oracle."""
-    monkeypatch.setenv("B200SCAN_M3_TC_SPLIT", split)
+    knobs(m3_tc_split=int(split))
     x = random_siso(2, 700, 3, 64, 128, 64, seed=5)
     cos, sin = oracle.angles_to_cos_sin(x["angles"].numpy(), x["dt"].numpy(), 64)
     want, wst, _ = oracle.m3_siso(x["q"], x["k"], x["v"], x["adt"], x["dt"], x["trap"],
@@ -407,12 +407,12 @@ def test_chunk_kernel_unaligned_q_k_take_scalar_staging():
 
 @pytest.mark.parametrize("grid", [(6, 9), (17, 23)])
 @pytest.mark.parametrize("seq", ["0", "1"])
-def test_ss2d_mamba3_fused_sum_vs_oracle(grid, seq, monkeypatch):
+def test_ss2d_mamba3_fused_sum_vs_oracle(grid, seq, knobs):
     """merge="sum" / "mean" run all four traversals in one library call that
     reads the grid in place (column-major traversal by index mapping, the
     angle pre-pass per ordering, outputs summed in place), in both chunk-kernel
     forms, on non-square grids whose length is not a multiple of the chunk."""
-    monkeypatch.setenv("B200SCAN_M3_CHUNK_SEQ", seq)
+    knobs(m3_chunk_form=1 if seq == "1" else 2)
     g = torch.Generator().manual_seed(sum(grid))
     b, (H, W), h, dv, dqk, r = 2, grid, 3, 32, 64, 16
     f = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
