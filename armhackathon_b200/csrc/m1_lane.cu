@@ -39,6 +39,8 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "m1_scan.h"
@@ -57,6 +59,12 @@ constexpr uint32_t kBCBytes = 16 * kLT * 4;     // one [16 states][32 steps] til
 constexpr uint32_t kStageBytes = 3 * kXBytes + 2 * kBCBytes;
 constexpr uint32_t kSmemBytes = kLStages * kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
 constexpr uint32_t kWaitLimit = 1u << 24;
+// Owned states (bit i: state q + 4i) whose decays run on the FMA pipe
+// (exp2_poly2) instead of the MUFU unit, to balance the two pipes.
+#ifndef B200SCAN_LANE_POLY_MASK
+#define B200SCAN_LANE_POLY_MASK 0
+#endif
+constexpr int kLanePolyMask = B200SCAN_LANE_POLY_MASK;
 
 __device__ int g_m1_status;  // 0 ok, 1 a staging wait expired
 
@@ -118,17 +126,33 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// Byte offset of (row r, step m) in a [rows][32] fp32 tile written by TMA
-// with 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8).
-__device__ __forceinline__ uint32_t swz(int r, int m) {
-    return static_cast<uint32_t>(r * 128 + ((((m >> 2) ^ r) & 7) << 4) + (m & 3) * 4);
+// Tiles are [rows][32] fp32 written by TMA with 128-byte swizzle: 16-byte
+// chunk c of row r sits at chunk c ^ (r % 8).  With a row's base address
+// (128-byte aligned) and its key (r % 8) << 4, chunk c is at
+// base | ((c << 4) ^ key): one logic op per access for a constant c.
+__device__ __forceinline__ uint32_t chunk_addr(uint32_t base, uint32_t key, int c) {
+    return base | ((static_cast<uint32_t>(c) << 4) ^ key);
 }
-__device__ __forceinline__ float4 lds4(const char* base, int r, int chunk) {
-    return *reinterpret_cast<const float4*>(base + r * 128 + (((chunk ^ r) & 7) << 4));
+// Shared-memory loads are plain (non-volatile) asm so that the compiler may
+// schedule them early; every address is derived from a base passed through
+// order_after(), a volatile no-op with a memory clobber placed after the
+// barrier that makes the data visible, so no load can move above it.
+__device__ __forceinline__ uint32_t order_after(uint32_t base) {
+    asm volatile("mov.b32 %0, %0;" : "+r"(base)::"memory");
+    return base;
 }
-__device__ __forceinline__ float4 rev4(float4 v) { return make_float4(v.w, v.z, v.y, v.x); }
-__device__ __forceinline__ float f4at(const float4& v, int i) {
-    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+__device__ __forceinline__ float4 lds4(uint32_t a) {
+    float4 v;
+    asm("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float lds1(uint32_t a) {
+    float v;
+    asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts1(uint32_t a, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
 
 // ---- the sweep --------------------------------------------------------------
@@ -189,30 +213,31 @@ __device__ __forceinline__ void lane_sweep(const M1Params& p, const LaneMaps& ma
     const int64_t row = row0 + r;
     const bool active = static_cast<int64_t>(jb) * kLRows + r < gsz && row < rows_all;
     const int64_t ch = active ? row % D : 0;
-    float2 a01, a23;  // A * log2(e) for states (q, q+4), (q+8, q+12)
+    float2 a2[4];  // (A_n, A_n) * log2(e) for the owned states n = q + 4i
     {
         const float* A = p.A + ch * N;
-        auto ld = [&](int n) { return n < N ? A[n] * kLog2e : 0.f; };
-        a01 = make_float2(ld(q), ld(q + 4));
-        a23 = make_float2(ld(q + 8), ld(q + 12));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float v = q + 4 * i < N ? A[q + 4 * i] * kLog2e : 0.f;
+            a2[i] = make_float2(v, v);
+        }
     }
     const float bias = p.delta_bias ? p.delta_bias[ch] : 0.f;
     const float dsk = (FULL && p.d_skip) ? p.d_skip[ch] : 0.f;
 
     if (MODE == kLaneRescan) griddep_wait();  // h_in comes from the carry kernel
-    float2 h01 = make_float2(0.f, 0.f), h23 = make_float2(0.f, 0.f);
+    float h[4] = {0.f, 0.f, 0.f, 0.f};
     if (active) {
         const float* hi = MODE == kLaneRescan ? ws.hin + (static_cast<int64_t>(s) * rows_all + row) * 16
                           : (MODE == kLaneFirst && p.h0) ? p.h0 + row * N
                                                         : nullptr;
         if (hi) {
-            auto ld = [&](int n) { return n < N ? hi[n] : 0.f; };
-            h01 = make_float2(ld(q), ld(q + 4));
-            h23 = make_float2(ld(q + 8), ld(q + 12));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) h[i] = q + 4 * i < N ? hi[q + 4 * i] : 0.f;
         }
     }
-    float2 p01 = make_float2(1.f, 1.f), p23 = p01;                  // BID: running decay product
-    float2 hb01 = make_float2(0.f, 0.f), hb23 = hb01;               // BID: reverse aggregate
+    float pr[4] = {1.f, 1.f, 1.f, 1.f};  // BID: running decay product
+    float hb[4] = {0.f, 0.f, 0.f, 0.f};  // BID: reverse aggregate
     float dtsum = 0.f;
 
     for (int c = 0; c < n_tiles; ++c) {
@@ -222,102 +247,104 @@ __device__ __forceinline__ void lane_sweep(const M1Params& p, const LaneMaps& ma
             if (lane == 0) atomicExch(&g_m1_status, 1);
             return;
         }
-        char* st = smem + slot * kStageBytes;
-        char* sd = st;                  // delta -> dt
-        char* su = st + kXBytes;        // u -> dt*u
-        char* sz = st + 2 * kXBytes;    // z -> y
-        const char* sB = st + 3 * kXBytes;
-        const char* sC = sB + kBCBytes;
+        // this lane's row in the delta (-> dt), u, z (-> silu(z) -> y) tiles,
+        // and its states' rows in the B, C tiles
+        const uint32_t st = order_after(smem_u32(smem) + slot * kStageBytes);
+        uint32_t rd = st + r * 128, ru = rd + kXBytes, rz = rd + 2 * kXBytes;
+        const uint32_t rkey = (r & 7) << 4;
+        uint32_t bB = st + 3 * kXBytes + q * 128, bC = bB + kBCBytes;
+        const uint32_t bkey = q << 4;  // states q + 4i: key q (i even), q + 4 (i odd)
         const int64_t j0 = it0 + static_cast<int64_t>(c) * kLT;
         const int cnt = static_cast<int>(ie - j0 < kLT ? ie - j0 : kLT);
 
-        // phase A: lane q takes traversal steps 4k + q
-        float gk[8], dk[8];
+        // phase A: lane q takes the steps at memory positions 4c + q of the
+        // tile (c = 0..7): dt over delta, silu(z) over z; u stays
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int j = 4 * k + q;
-            const int m = REV ? kLT - 1 - j : j;
-            const uint32_t off = swz(r, m);
-            float dt = 0.f, dtu = 0.f;
-            const float uu = *reinterpret_cast<const float*>(su + off);
+        for (int c = 0; c < 8; ++c) {
+            const int m = 4 * c + q;
+            const int j = REV ? kLT - 1 - m : m;  // traversal index within the tile
+            const uint32_t off = chunk_addr(q * 4, rkey, c);  // (c ^ key) * 16 + q * 4
+            float dt = 0.f;
             if (j < cnt) {
-                dt = *reinterpret_cast<const float*>(sd + off) + bias;
+                dt = lds1(rd + off) + bias;
                 if (p.delta_softplus) dt = softplus_fast(dt);
-                dtu = dt * uu;
             }
             dtsum += dt;
-            *reinterpret_cast<float*>(sd + off) = dt;
-            *reinterpret_cast<float*>(su + off) = dtu;
-            if (FULL) {
-                const float gz = has_z ? silu_fast(*reinterpret_cast<const float*>(sz + off)) : 1.f;
-                gk[k] = gz;
-                dk[k] = dsk * uu * gz;
-            }
+            sts1(rd + off, dt);
+            if (has_z) sts1(rz + off, silu_fast(lds1(rz + off)));
         }
         __syncwarp();
+        rd = order_after(rd);
+        ru = order_after(ru);
+        rz = order_after(rz);
 
-        // phase B: the recurrence, 4 steps per block
+        // phase B: the recurrence, one 16-byte chunk (4 steps) at a time;
+        // pairs are formed along time in memory order, (e0, e1), (e2, e3),
+        // so that the packed products read their operands straight from the
+        // 16-byte loads; the state chain walks e0..e3 (e3..e0 in reverse)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            const int chunk = REV ? 7 - k : k;
-            float4 dt4 = lds4(sd, r, chunk), du4 = lds4(su, r, chunk);
-            float4 b4[4], c4[4];
+            const int c = REV ? 7 - k : k;
+            const float4 dt4 = lds4(chunk_addr(rd, rkey, c)), u4 = lds4(chunk_addr(ru, rkey, c));
+            const float2 dtl = make_float2(dt4.x, dt4.y), dth = make_float2(dt4.z, dt4.w);
+            const float2 dul = fmul2(dtl, make_float2(u4.x, u4.y));
+            const float2 duh = fmul2(dth, make_float2(u4.z, u4.w));
+            float2 yl = make_float2(0.f, 0.f), yh = make_float2(0.f, 0.f);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                b4[i] = lds4(sB, q + 4 * i, chunk);
-                if (FULL) c4[i] = lds4(sC, q + 4 * i, chunk);
-            }
-            if (REV) {
-                dt4 = rev4(dt4);
-                du4 = rev4(du4);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    b4[i] = rev4(b4[i]);
-                    if (FULL) c4[i] = rev4(c4[i]);
+                const uint32_t nkey = bkey ^ ((i & 1) << 6), noff = i * 512;
+                const float4 b4 = lds4(chunk_addr(bB + noff, nkey, c));
+                const float2 xl = fmul2(dtl, a2[i]), xh = fmul2(dth, a2[i]);
+                float e[4];
+                if ((kLanePolyMask >> i) & 1) {
+                    const float2 el = exp2_poly2(xl), eh = exp2_poly2(xh);
+                    e[0] = el.x, e[1] = el.y, e[2] = eh.x, e[3] = eh.y;
+                } else {
+                    e[0] = ex2_approx(xl.x), e[1] = ex2_approx(xl.y), e[2] = ex2_approx(xh.x), e[3] = ex2_approx(xh.y);
                 }
-            }
-            float yp[4];
+                const float2 bl = fmul2(dul, make_float2(b4.x, b4.y));
+                const float2 bh = fmul2(duh, make_float2(b4.z, b4.w));
+                const float bu[4] = {bl.x, bl.y, bh.x, bh.y};
+                float hs[4];
+                float hc = h[i];
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const float dt = f4at(dt4, t), du = f4at(du4, t);
-                const float2 d2 = make_float2(dt, dt), u2 = make_float2(du, du);
-                const float2 x01 = fmul2(d2, a01), x23 = fmul2(d2, a23);
-                const float2 e01 = make_float2(ex2_approx(x01.x), ex2_approx(x01.y));
-                const float2 e23 = make_float2(ex2_approx(x23.x), ex2_approx(x23.y));
-                const float2 bu01 = fmul2(u2, make_float2(f4at(b4[0], t), f4at(b4[1], t)));
-                const float2 bu23 = fmul2(u2, make_float2(f4at(b4[2], t), f4at(b4[3], t)));
-                h01 = ffma2(e01, h01, bu01);
-                h23 = ffma2(e23, h23, bu23);
-                if (BID) {
-                    hb01 = ffma2(p01, bu01, hb01);
-                    hb23 = ffma2(p23, bu23, hb23);
-                    p01 = fmul2(p01, e01);
-                    p23 = fmul2(p23, e23);
+                for (int t = 0; t < 4; ++t) {
+                    const int ei = REV ? 3 - t : t;
+                    hc = fmaf(e[ei], hc, bu[ei]);
+                    hs[ei] = hc;
+                    if (BID) {
+                        hb[i] = fmaf(pr[i], bu[ei], hb[i]);
+                        pr[i] *= e[ei];
+                    }
                 }
+                h[i] = hc;
                 if (FULL) {
-                    float2 y2 = fmul2(make_float2(f4at(c4[0], t), f4at(c4[1], t)), h01);
-                    y2 = ffma2(make_float2(f4at(c4[2], t), f4at(c4[3], t)), h23, y2);
-                    yp[t] = y2.x + y2.y;
+                    const float4 c4 = lds4(chunk_addr(bC + noff, nkey, c));
+                    yl = ffma2(make_float2(c4.x, c4.y), make_float2(hs[0], hs[1]), yl);
+                    yh = ffma2(make_float2(c4.z, c4.w), make_float2(hs[2], hs[3]), yh);
                 }
             }
             if (FULL) {
-                // reduce-scatter over the row's 4 lanes: lane q gets step 4k + q
+                // reduce-scatter over the row's 4 lanes: lane q gets memory
+                // element q of the chunk
                 const bool hi = q & 2, lo = q & 1;
-                const float s0 = hi ? yp[0] : yp[2], s1 = hi ? yp[1] : yp[3];
-                const float k0 = hi ? yp[2] : yp[0], k1 = hi ? yp[3] : yp[1];
+                const float s0 = hi ? yl.x : yh.x, s1 = hi ? yl.y : yh.y;
+                const float k0 = hi ? yh.x : yl.x, k1 = hi ? yh.y : yl.y;
                 const float v0 = k0 + __shfl_xor_sync(0xffffffffu, s0, 2);
                 const float v1 = k1 + __shfl_xor_sync(0xffffffffu, s1, 2);
                 const float sl = lo ? v0 : v1, kp = lo ? v1 : v0;
                 const float y = kp + __shfl_xor_sync(0xffffffffu, sl, 1);
-                const int j = 4 * k + q;
-                const int m = REV ? kLT - 1 - j : j;
-                *reinterpret_cast<float*>(sz + swz(r, m)) = fmaf(y, gk[k], dk[k]);
+                const uint32_t off = chunk_addr(q * 4, rkey, c);
+                float yo = fmaf(dsk, lds1(ru + off), y);
+                if (has_z) yo *= lds1(rz + off);
+                sts1(rz + off, yo);
             }
         }
 
         if (FULL) {
             // phase C: the warp's 8 rows x 32 steps of y, as 16-byte stores
             __syncwarp();
+            const uint32_t sy = order_after(st + 2 * kXBytes);
             const int64_t ms = REV ? L - j0 - kLT : j0;  // memory step of tile position 0
 #pragma unroll
             for (int rep = 0; rep < 2; ++rep) {
@@ -327,7 +354,7 @@ __device__ __forceinline__ void lane_sweep(const M1Params& p, const LaneMaps& ma
                 const bool valid = REV ? (4 * cc >= kLT - cnt) : (4 * cc < cnt);
                 const bool ract = static_cast<int64_t>(jb) * kLRows + rr < gsz && orow < rows_all;
                 if (valid && ract) {
-                    float4 y4 = lds4(sz, rr, cc);
+                    float4 y4 = lds4(chunk_addr(sy + rr * 128, (rr & 7) << 4, cc));
                     float4* o4 = reinterpret_cast<float4*>(p.out + orow * L + ms + 4 * cc);
                     if (p.out_acc) {
                         const float4 o = __ldcs(o4);
@@ -348,7 +375,7 @@ __device__ __forceinline__ void lane_sweep(const M1Params& p, const LaneMaps& ma
     dtsum += __shfl_xor_sync(0xffffffffu, dtsum, 1);
     dtsum += __shfl_xor_sync(0xffffffffu, dtsum, 2);
     if (!active) return;
-    const float hv[4] = {h01.x, h01.y, h23.x, h23.y};
+    const float* hv = h;
     // segment end states for the carry (an unsplit scan with outputs has no
     // workspace and no carry)
     if (MODE != kLaneRescan && ws.hend) {
@@ -360,7 +387,7 @@ __device__ __forceinline__ void lane_sweep(const M1Params& p, const LaneMaps& ma
     if (BID) {
         // the reverse traversal visits this segment as its (S - 1 - s)-th
         const int64_t sr = static_cast<int64_t>(S - 1 - s) * rows_all + row;
-        const float bv[4] = {hb01.x, hb01.y, hb23.x, hb23.y};
+        const float* bv = hb;
         float* he = wsb->hend + sr * 16;
 #pragma unroll
         for (int i = 0; i < 4; ++i) he[q + 4 * i] = bv[i];
@@ -398,15 +425,17 @@ __device__ __forceinline__ char* lane_setup(uint64_t*& full, uint64_t*& empty, i
     return smem;
 }
 
-// Pass 1.  FIRST: segment 0 runs the full scan from h0, segments 1..S-2 the
-// state-only sweep; otherwise every segment is state-only.
-template <bool FIRST, bool REV>
+// Pass 1.  FIRST 2: segment 0 runs the full scan from h0, segments 1..S-2
+// the state-only sweep; FIRST 1: the full scan of an unsplit sequence (its
+// own kernel, so that its registers are not those of both sweeps); FIRST 0:
+// every segment state-only.
+template <int FIRST, bool REV>
 __global__ void __launch_bounds__(kLThreads, 3)
     m1_lane_pass1(M1Params p, const __grid_constant__ LaneMaps maps, LaneWs ws, int S, int64_t Ls) {
     uint64_t *full, *empty;
     char* smem = lane_setup(full, empty, static_cast<int>(p.state));
     griddep_launch_dependents();
-    if (FIRST && blockIdx.y == 0)
+    if (FIRST == 1 || (FIRST == 2 && blockIdx.y == 0))
         lane_sweep<kLaneFirst, REV>(p, maps, ws, nullptr, S, Ls, 0, smem, full, empty);
     else
         lane_sweep<kLaneState, REV>(p, maps, ws, nullptr, S, Ls, blockIdx.y, smem, full, empty);
@@ -495,7 +524,7 @@ cudaError_t make_map(CUtensorMap* m, const float* base, int64_t len, int64_t row
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t make_maps(const M1Params& p, LaneMaps* m) {
+cudaError_t encode_maps(const M1Params& p, LaneMaps* m) {
     std::memset(m, 0, sizeof(*m));
     const int64_t rows = p.batch * p.dim, bcrows = p.batch * p.groups * p.state;
     cudaError_t e = make_map(&m->delta, p.delta, p.len, rows, kLRows);
@@ -506,9 +535,66 @@ cudaError_t make_maps(const M1Params& p, LaneMaps* m) {
     return e;
 }
 
+// Tensor maps of the last few distinct calls (per host thread): encoding
+// five maps costs microseconds of host time, which a small op (one batch
+// row) would otherwise spend on every call.
+struct MapKey {
+    const void *u, *delta, *z, *B, *C;
+    int64_t batch, dim, len, state, groups;
+    bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+cudaError_t make_maps(const M1Params& p, LaneMaps* m) {
+    struct Entry {
+        MapKey key;
+        int dev;
+        LaneMaps maps;
+    };
+    thread_local Entry cache[8];
+    thread_local int next = 0, used = 0;
+    MapKey k;
+    std::memset(&k, 0, sizeof(k));
+    k.u = p.u;
+    k.delta = p.delta;
+    k.z = p.z;
+    k.B = p.B;
+    k.C = p.C;
+    k.batch = p.batch;
+    k.dim = p.dim;
+    k.len = p.len;
+    k.state = p.state;
+    k.groups = p.groups;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    for (int i = 0; i < used; ++i)
+        if (cache[i].dev == dev && cache[i].key == k) {
+            *m = cache[i].maps;
+            return cudaSuccess;
+        }
+    const cudaError_t e = encode_maps(p, m);
+    if (e != cudaSuccess) return e;
+    cache[next].key = k;
+    cache[next].dev = dev;
+    cache[next].maps = *m;
+    next = (next + 1) % 8;
+    if (used < 8) ++used;
+    return cudaSuccess;
+}
+
+// Raises the kernel's dynamic shared-memory limit, once per (kernel, device).
 template <class K>
 cudaError_t allow_smem(K kern) {
-    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    static std::mutex mu;
+    static std::vector<std::pair<const void*, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const void* key = reinterpret_cast<const void*>(kern);
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& d : done)
+        if (d.first == key && d.second == dev) return cudaSuccess;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    if (e == cudaSuccess) done.emplace_back(key, dev);
+    return e;
 }
 
 // Concurrent CTAs of the lane kernels per device (SMs x resident CTAs per SM).
@@ -609,8 +695,10 @@ cudaError_t m1_lane_launch(const M1Params& p, int S, cudaStream_t stream) {
     cudaError_t e = make_maps(p, &maps);
     if (e != cudaSuccess) return e;
     const bool first = p.out != nullptr;  // out == nullptr: final state only
-    auto k1 = first ? (p.reverse ? m1_lane_pass1<true, true> : m1_lane_pass1<true, false>)
-                    : (p.reverse ? m1_lane_pass1<false, true> : m1_lane_pass1<false, false>);
+    const int f = first ? (S == 1 ? 1 : 2) : 0;
+    auto k1 = f == 1 ? (p.reverse ? m1_lane_pass1<1, true> : m1_lane_pass1<1, false>)
+            : f == 2 ? (p.reverse ? m1_lane_pass1<2, true> : m1_lane_pass1<2, false>)
+                     : (p.reverse ? m1_lane_pass1<0, true> : m1_lane_pass1<0, false>);
     auto k2 = p.reverse ? m1_lane_pass2<true> : m1_lane_pass2<false>;
     if ((e = allow_smem(k1)) != cudaSuccess || (e = allow_smem(k2)) != cudaSuccess) return e;
     LaneWsAlloc alloc(stream);
