@@ -11,7 +11,6 @@
 //            chunks, then walks its chunk writing cos/sin.
 // Reads of angles are coalesced over pairs (the innermost axis).
 #include <cstdint>
-#include <mutex>
 
 #include "common.cuh"
 #include "m3_angles.h"
@@ -131,15 +130,13 @@ cudaError_t angle_launch(const AngleParams& a, float* ws, cudaStream_t stream) {
 // instead of a caller workspace; every GPU that loads the library holds it
 // (4 MiB) until the process exits.  Host code must not pass the symbol itself
 // to a kernel: on the host it only names a stand-in, so its device address is
-// looked up once per device with cudaGetSymbolAddress (with that device
-// current) and cached.
+// looked up with cudaGetSymbolAddress, with the calling device current, on
+// every call.  The lookup is cheap, and looking it up each time means the
+// address is always the one of the current context (a cached address would
+// go stale after cudaDeviceReset or under another context on the device).
 namespace {
 
 static __device__ __align__(256) float g_angle_scratch[kAngleNoAllocMaxFloats];
-
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-float* g_scratch_ptr[kMaxDevices] = {};
 
 }  // namespace
 
@@ -147,23 +144,11 @@ cudaError_t angle_noalloc_launch(const AngleParams& a, cudaStream_t stream, bool
     const size_t floats = angle_workspace_bytes(a.batch, a.heads, a.len, a.n_angles) / sizeof(float);
     *too_big = floats > static_cast<size_t>(kAngleNoAllocMaxFloats);
     if (*too_big) return cudaSuccess;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_angle_scratch);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    float* ws = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(g_scratch_mu);
-        if (!g_scratch_ptr[dev]) {
-            void* ptr = nullptr;
-            e = cudaGetSymbolAddress(&ptr, g_angle_scratch);
-            if (e != cudaSuccess) return e;
-            g_scratch_ptr[dev] = static_cast<float*>(ptr);
-        }
-        ws = g_scratch_ptr[dev];
-    }
     // Nothing needs clearing: phase 1 writes every chunk sum phase 2 reads.
-    return angle_launch(a, ws, stream);
+    return angle_launch(a, static_cast<float*>(ptr), stream);
 }
 
 }  // namespace b200scan

@@ -173,8 +173,9 @@ int arm_scan_mamba3_angles_f32_async(const ArmMamba3Dims* dims, const float* ang
  * (held by every GPU that loads the library until the process exits), so a
  * problem needing more than 4 MiB of chunk sums
  * (batch*heads*ceil(len/128)*n_angles*4 bytes) is rejected with code 2.
- * The first call on each device looks up the array's device address; make
- * that first call before any stream capture.  All calls share the one array:
+ * Every call looks up the array's device address for the current device
+ * and context (cudaGetSymbolAddress, no allocation), so the entry stays
+ * valid across cudaDeviceReset and context changes.  All calls share the one array:
  * calls whose executions overlap on the GPU (different streams, or different
  * host threads) race on it and must be serialized by the caller.  Arguments
  * and results are those of arm_scan_mamba3_angles_f32_async. */

@@ -196,3 +196,16 @@ def test_bidirectional_sum_and_states_argument_rules():
     assert states_call(backend=2) == 3          # neon backend unavailable
     assert states_call(backend=9) == 4
     assert states_call(d=_ffi.ArmScanDims(1, 6, 64, 4, 4)) == 2  # dim not a multiple of groups
+
+
+def test_no_alloc_angles_reject_problems_beyond_their_scratch():
+    """The allocation-free angle entry checks the problem against its fixed
+    4 MiB scratch before any CUDA call: 64 heads x 1024 chunks x 64 angles x
+    4 B = 16 MiB is refused with code 2 (dummy non-null pointers, no GPU)."""
+    lib = _ffi.load()
+    dims = _ffi.ArmMamba3Dims(1, 64, 0, 128, 128 * 1024, 1)
+    dummy = 16
+    rc = lib.arm_scan_mamba3_angles_f32_noalloc(ctypes.byref(dims), dummy, 64, dummy, dummy,
+                                                dummy, None)
+    assert rc == 2
+    assert b"scratch" in lib.arm_scan_last_error()

@@ -66,15 +66,3 @@ def test_no_alloc_matches_workspace_entry_on_two_calls_in_a_row():
         torch.cuda.synchronize()
         assert torch.allclose(got_c, want_c, atol=TOL, rtol=0)
         assert torch.allclose(got_s, want_s, atol=TOL, rtol=0)
-
-
-def test_no_alloc_rejects_problems_beyond_its_scratch():
-    from armhackathon_b200 import _ffi
-    lib = _ffi.load()
-    # 64 heads x 1024 chunks x 64 angles x 4 B = 16 MiB > 4 MiB
-    dims = _ffi.ArmMamba3Dims(1, 64, 0, 128, 128 * 1024, 1)
-    x = torch.zeros(16, device="cuda")
-    rc = lib.arm_scan_mamba3_angles_f32_noalloc(ctypes.byref(dims), x.data_ptr(), 64,
-                                                x.data_ptr(), x.data_ptr(), x.data_ptr(), None)
-    assert rc == 2
-    assert b"scratch" in lib.arm_scan_last_error()
