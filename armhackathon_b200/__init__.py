@@ -25,7 +25,7 @@ __all__ = [
     "ss2d_noncausal_mamba3", "angles_to_cos_sin", "patch", "unpatch", "stats", "kernel_calls",
     "selective_state_update", "selective_scan_final_state", "mamba3_mixer_prologue",
     "selective_scan_bidirectional_sum", "selective_scan_bidirectional_final_states",
-    "mamba3_mixer_scan",
+    "mamba3_mixer_scan", "mamba3_mimo_x_scan",
 ]
 
 _LAZY = {
@@ -36,6 +36,7 @@ _LAZY = {
     "bidirectional_scan": ".bidirectional",
     "ss2d_scan": ".ss2d", "use_arm_scan": ".ss2d",
     "mamba3_scan": ".mamba3", "mamba3_scan_pair": ".mamba3", "mamba3_mimo_scan": ".mamba3",
+    "mamba3_mimo_x_scan": ".mamba3",
     "angles_to_cos_sin": ".mamba3",
     "ss2d_scan_mamba3": ".ss2d_mamba3",
     "noncausal_scan": ".mamba3_noncausal", "noncausal_scan_dense": ".mamba3_noncausal",

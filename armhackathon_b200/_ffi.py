@@ -129,6 +129,10 @@ def _bind(lib):
     lib.arm_scan_mamba3_mixer_prologue_f32_async.argtypes = [
         ctypes.POINTER(ArmMamba3MixerDims), *([_VP] * 4), ctypes.c_float, ctypes.c_float,
         *([_VP] * 9)]
+    lib.arm_scan_mamba3_mimo_x_tc_async.restype = ctypes.c_int
+    lib.arm_scan_mamba3_mimo_x_tc_async.argtypes = [
+        ctypes.POINTER(ArmMamba3Dims), ctypes.POINTER(ArmMamba3TcOptions), *([_VP] * 8),
+        ctypes.c_int, _VP, _VP, _VP]
     lib.arm_scan_mamba3_siso_tc_async.restype = ctypes.c_int
     lib.arm_scan_mamba3_siso_tc_async.argtypes = [
         ctypes.POINTER(ArmMamba3Dims), ctypes.POINTER(ArmMamba3TcOptions), *([_VP] * 11),
@@ -232,6 +236,17 @@ def mamba3_tc_raw(dims, opts, ptrs, reverse, ptr_out, ptr_last_state, ptr_last_b
     _check(load().arm_scan_mamba3_siso_tc_async(
         ctypes.byref(dims), ctypes.byref(opts), *[_n(p) for p in ptrs], int(reverse), ptr_out,
         _n(ptr_last_state), _n(ptr_last_bx), _n(stream)), "arm_scan_mamba3_siso_tc_async")
+
+
+def mamba3_mimo_x_raw(dims, opts, ptrs, reverse, ptr_out, ptr_last_state, stream):
+    """Per-rank Mamba-3 MIMO on the tensor cores.  ``ptrs``: x, b, c, adt,
+    dt, trap, angles, d_skip (the last two may be 0).  Device pointers,
+    stream-ordered."""
+    if len(ptrs) != 8:
+        raise ValueError(f"expected 8 input pointers, got {len(ptrs)}")
+    _check(load().arm_scan_mamba3_mimo_x_tc_async(
+        ctypes.byref(dims), ctypes.byref(opts), *[_n(p) for p in ptrs], int(reverse), ptr_out,
+        _n(ptr_last_state), _n(stream)), "arm_scan_mamba3_mimo_x_tc_async")
 
 
 def angles_workspace_bytes(dims, n_angles):
@@ -356,7 +371,7 @@ def exported_symbols():
             "arm_scan_mamba3_mixer_prologue_f32_async",
             "arm_scan_selective_scan_bidirectional_sum_f32_async",
             "arm_scan_selective_scan_bidirectional_final_states_f32_async",
-            "arm_scan_set_kernel_override"]
+            "arm_scan_set_kernel_override", "arm_scan_mamba3_mimo_x_tc_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

@@ -867,6 +867,58 @@ int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOp
     return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "mamba3_siso_tc launch");
 }
 
+int arm_scan_mamba3_mimo_x_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOptions* opts,
+                                    const void* x, const void* b, const void* c, const float* adt,
+                                    const float* dt, const float* trap, const float* angles,
+                                    const float* d_skip, int reverse, void* out, float* last_state,
+                                    void* stream) {
+    if (!dims || !opts || !x || !b || !c || !adt || !dt || !trap || !out)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    if (opts->n_angles > 0 && !angles)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "angles is null with n_angles > 0");
+    auto is_dtype = [](int d) { return d == ARM_SCAN_DTYPE_F32 || d == ARM_SCAN_DTYPE_BF16; };
+    if (!is_dtype(opts->in_dtype) || !is_dtype(opts->out_dtype))
+        return fail(ARM_SCAN_ERR_BAD_ENUM, "dtype must be ARM_SCAN_DTYPE_F32 (0) or _BF16 (1)");
+    if (opts->angles_shared != 0 && opts->angles_shared != 1)
+        return fail(ARM_SCAN_ERR_BAD_ENUM, "angles_shared must be 0 or 1, got %d", opts->angles_shared);
+    if (!dims->batch || !dims->heads || !dims->dv || !dims->dqk || !dims->len || !dims->rank)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "a dimension is zero");
+    if (dims->dqk % 2) return fail(ARM_SCAN_ERR_INVALID_DIMS, "dqk must be even");
+    if (opts->n_angles > dims->dqk / 2)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "n_angles (%zu) exceeds dqk/2 (%zu)", opts->n_angles,
+                    dims->dqk / 2);
+    size_t n1 = 0, n2 = 0;
+    if (!mul4(dims->batch, dims->len, dims->heads, dims->dv, &n1) || !mul_ok(n1, dims->rank, &n2) ||
+        n2 > (SIZE_MAX >> 3) / 4)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "element counts overflow");
+    M3Params m{};
+    m.q = static_cast<const float*>(c);
+    m.k = static_cast<const float*>(b);
+    m.v = static_cast<const float*>(x);
+    m.adt = adt;
+    m.dt = dt;
+    m.trap = trap;
+    m.d_skip = d_skip;
+    m.out = static_cast<float*>(out);
+    m.last_state = last_state;
+    m.batch = static_cast<int64_t>(dims->batch);
+    m.heads = static_cast<int64_t>(dims->heads);
+    m.dv = static_cast<int64_t>(dims->dv);
+    m.dqk = static_cast<int64_t>(dims->dqk);
+    m.len = static_cast<int64_t>(dims->len);
+    m.rank = static_cast<int64_t>(dims->rank);
+    m.reverse = reverse ? 1 : 0;
+    m.in_bf16 = opts->in_dtype == ARM_SCAN_DTYPE_BF16;
+    m.out_bf16 = opts->out_dtype == ARM_SCAN_DTYPE_BF16;
+    m.x_per_rank = 1;
+    if (!m3_tc_xr_applicable(m))
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE,
+                    "the per-rank MIMO entry covers rank 2 or 4, dqk 128, dv 64 and batch*heads <= 65535");
+    cudaError_t e = m3_tc_launch_xr(m, angles, static_cast<int64_t>(opts->n_angles), opts->angles_shared,
+                                    static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "mamba3_mimo_x_tc launch");
+}
+
 int arm_scan_mamba3_scan_f32_async(const ArmMamba3Dims* dims, const float* q, const float* k,
                                    const float* v, const float* adt, const float* dt,
                                    const float* trap, const float* q_bias, const float* k_bias,

@@ -41,8 +41,9 @@ __global__ void angle_chunk_sums(AngleParams a, float* ws) {
     const int64_t b = bh / a.heads, h = bh % a.heads;
     const int64_t t0 = static_cast<int64_t>(c) * kAgChunk;
     const int64_t t1 = t0 + kAgChunk < a.len ? t0 + kAgChunk : a.len;
-    const float* ang = a.angles + ((b * a.len) * a.heads + h) * a.n_angles + p;
-    const int64_t ang_step = a.heads * a.n_angles;
+    const float* ang = a.angles_shared ? a.angles + (b * a.len) * a.n_angles + p
+                                       : a.angles + ((b * a.len) * a.heads + h) * a.n_angles + p;
+    const int64_t ang_step = a.angles_shared ? a.n_angles : a.heads * a.n_angles;
     const float* dt = a.dt + (b * a.heads + h) * a.len;
     float s = 0.f;
     for (int64_t t = t0; t < t1; t += kAgUnroll) {
@@ -80,8 +81,9 @@ __global__ void angle_chunk_write(AngleParams a, const float* ws) {
     }
     float theta = 0.f;
     for (int j = 0; j < c; ++j) theta += __ldg(ws + (bh * gridDim.x + j) * a.n_angles + p);
-    const float* ang = a.angles + ((b * a.len) * a.heads + h) * a.n_angles + p;
-    const int64_t ang_step = a.heads * a.n_angles;
+    const float* ang = a.angles_shared ? a.angles + (b * a.len) * a.n_angles + p
+                                       : a.angles + ((b * a.len) * a.heads + h) * a.n_angles + p;
+    const int64_t ang_step = a.angles_shared ? a.n_angles : a.heads * a.n_angles;
     const float* dt = a.dt + (b * a.heads + h) * a.len;
     for (int64_t t = t0; t < t1; t += kAgUnroll) {
         float av[kAgUnroll], dv[kAgUnroll];
@@ -116,10 +118,12 @@ cudaError_t angle_launch(const AngleParams& a, float* ws, cudaStream_t stream) {
     const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(a.batch * a.heads));
     const int t1 = static_cast<int>((a.n_angles + 31) / 32 * 32);
     const int t2 = static_cast<int>((a.half + 31) / 32 * 32);
-    angle_chunk_sums<<<grid, t1, 0, stream>>>(a, ws);
-    note_launch();
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (a.n_angles > 0) {  // no rotated pairs: the write pass alone gives (1, 0)
+        angle_chunk_sums<<<grid, t1, 0, stream>>>(a, ws);
+        note_launch();
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
     angle_chunk_write<<<grid, t2, 0, stream>>>(a, ws);
     note_launch();
     return cudaGetLastError();

@@ -17,6 +17,9 @@ struct AngleParams {
     // written in traversal order
     int64_t grid_w = 0;
     int col_major = 0;
+    // 1: angles are (batch, len, n_angles), one row per step shared by the
+    // heads (theta still differs per head through dt)
+    int angles_shared = 0;
 };
 
 size_t angle_workspace_bytes(int64_t batch, int64_t heads, int64_t len, int64_t n_angles);

@@ -43,6 +43,10 @@ struct M3Params {
     int64_t grid_w;
     int col_major;
     int out_acc;            // out += y (the four SS2D traversals sum in place)
+    // MIMO with the input given per rank (tensor-core kernel only): v is X
+    // (b, l, h, dv, rank), q / k are C / B (b, l, dqk, rank), out is
+    // (b, l, h, dv, rank) per rank; no psi / zeta / phi / z, biases nullable
+    int x_per_rank;
 };
 
 // grid position of traversal step t
@@ -60,7 +64,12 @@ cudaError_t m3_chunk_launch(const M3Params& p, cudaStream_t stream);
 // Tensor-core kernel (m3_tc.cu): bf16 operands, fp32 accumulation; backend 3.
 bool m3_tc_applicable(const M3Params& p);
 cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream);
-int m3_tc_status_and_clear();  // 1 if a bounded wait expired since the last call
+int m3_tc_status_and_clear();
+// Per-rank MIMO on the tensor cores (x_per_rank layouts; q = C, k = B):
+// shape test and launcher (RoPE pre-pass from raw fp32 angles, then the scan).
+bool m3_tc_xr_applicable(const M3Params& p);
+cudaError_t m3_tc_launch_xr(const M3Params& p, const float* angles, int64_t n_angles, int angles_shared,
+                            cudaStream_t stream);  // 1 if a bounded wait expired since the last call
 // true if p (with angles set) is a shape the extension entry covers
 bool m3_tc_angles_applicable(const M3Params& p);
 

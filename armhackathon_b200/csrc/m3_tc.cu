@@ -36,6 +36,7 @@
 
 #include "common.cuh"
 #include "m1_scan.h"
+#include "m3_angles.h"
 #include "m3_scan.h"
 
 namespace b200scan {
@@ -944,6 +945,75 @@ __device__ __forceinline__ void load_x_r(const M3Params& p, int64_t bi, int64_t 
     }
 }
 
+// Per-rank MIMO (p.x_per_rank): X rows of the tile, row j = (step j / R,
+// rank j % R), channels 8pc..8pc+7 of X (b, l, h, dv, R), i.e. stride R.
+template <int R, bool IN16>
+__device__ __forceinline__ void load_x_xr(const M3Params& p, int64_t bi, int64_t h, int64_t s0,
+                                          float (&xv)[kXItems][8]) {
+    const int64_t L = p.len, H = p.heads;
+#pragma unroll
+    for (int q = 0; q < kXItems; ++q) {
+        int j, pc;
+        x_item(q, j, pc);
+        const int64_t it = s0 + j / R;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xv[q][e] = 0.f;
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            const int64_t base = (((bi * L + t) * H + h) * kTcP + pc * 8) * R + j % R;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xv[q][e] = ld1_in<IN16>(p.v, base + e * R);
+        }
+    }
+}
+
+// Per-rank MIMO rotated C (q) and B (k) rows: element (rank rk, dim n) of
+// step t at ((b * L + t) * dqk + n) * R + rk; biases may be absent; same
+// split-halves RoPE and item split as stage_qk_mimo.
+template <int R, bool IN16>
+__device__ __forceinline__ void stage_qk_xr(const M3Params& p, int64_t bi, int64_t h, int64_t s0,
+                                            uint8_t* img_q, uint8_t* img_k, const float* qbs,
+                                            const float* kbs) {
+    const int64_t L = p.len, H = p.heads;
+    constexpr int half = kTcN / 2;
+#pragma unroll
+    for (int m = 0; m < 128 * 8 / kTcThreads2; ++m) {
+        const int item = threadIdx.x + m * kTcThreads2;
+        const int j = (item >> 8) * 32 + (item & 31);
+        const int kc = (item >> 5) & 7;
+        const int rk = j % R;
+        const int64_t it = s0 + j / R;
+        float qlo[8], qhi[8], klo[8], khi[8];
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            const int64_t base = ((bi * L + t) * kTcN + kc * 8) * R + rk;
+            const int bb = rk * kTcN + kc * 8;
+            const int64_t cs = ((bi * L + t) * H + h) * half + kc * 8;
+            float c[8], sn[8];
+            ldg8(p.cos + cs, c);
+            ldg8(p.sin + cs, sn);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                float a0 = ld1_in<IN16>(p.q, base + e * R) + qbs[bb + e];
+                float a1 = ld1_in<IN16>(p.q, base + (half + e) * R) + qbs[bb + half + e];
+                qlo[e] = a0 * c[e] - a1 * sn[e];
+                qhi[e] = a0 * sn[e] + a1 * c[e];
+                a0 = ld1_in<IN16>(p.k, base + e * R) + kbs[bb + e];
+                a1 = ld1_in<IN16>(p.k, base + (half + e) * R) + kbs[bb + half + e];
+                klo[e] = a0 * c[e] - a1 * sn[e];
+                khi[e] = a0 * sn[e] + a1 * c[e];
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qlo[e] = qhi[e] = klo[e] = khi[e] = 0.f;
+        }
+        *reinterpret_cast<uint4*>(img_q + kmaj_off(j, kc * 8, 128)) = pack8(qlo);
+        *reinterpret_cast<uint4*>(img_q + kmaj_off(j, kc * 8 + half, 128)) = pack8(qhi);
+        *reinterpret_cast<uint4*>(img_k + kmaj_off(j, kc * 8, 128)) = pack8(klo);
+        *reinterpret_cast<uint4*>(img_k + kmaj_off(j, kc * 8 + half, 128)) = pack8(khi);
+    }
+}
+
 // MIMO rotated q, k rows from cos/sin, split-halves RoPE: pair m rotates
 // dims (m, m + dqk/2).  One item = row j (step, rank) x low dim chunk kc
 // (dims 8kc..8kc+7) and its partner chunk kc + 8; 1024 items, 4 per thread.
@@ -1153,7 +1223,7 @@ __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_
 
 // Requests every row tile `tile` will read into L2 (one 16-byte-aligned bulk
 // prefetch per row), so that its loads, issued a tile later, hit L2.
-template <bool ANG, bool IN16, int R>
+template <bool ANG, bool IN16, int R, bool XR = false>
 __device__ __forceinline__ void prefetch_tile(const M3Params& p, const float* ta,
                                               const float* theta0, int64_t tile, int n_chunks) {
     const int64_t BH = p.batch * p.heads, H = p.heads, L = p.len;
@@ -1175,7 +1245,10 @@ __device__ __forceinline__ void prefetch_tile(const M3Params& p, const float* ta
             prefetch_l2(q + (bi * L + t) * R * kTcN * es, R * kTcN * es);
             prefetch_l2(k + (bi * L + t) * R * kTcN * es, R * kTcN * es);
         }
-        prefetch_l2(v + row * kTcP * es, kTcP * es);
+        if (XR)
+            prefetch_l2(v + row * kTcP * R * es, kTcP * R * es);
+        else
+            prefetch_l2(v + row * kTcP * es, kTcP * es);
         if (p.z) prefetch_l2(static_cast<const uint8_t*>(static_cast<const void*>(p.z)) + row * kTcP * es,
                              kTcP * es);
         if (ANG) {
@@ -1201,7 +1274,7 @@ __device__ __forceinline__ void prefetch_tile(const M3Params& p, const float* ta
     }
 }
 
-template <bool ANG, bool IN16, bool OUT16, int R>
+template <bool ANG, bool IN16, bool OUT16, int R, bool XR>
 __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainWs cw, int n_chunks,
                                                              const float* ta, const float* theta0) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -1248,7 +1321,7 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
     if (tid == 0) *tile_slot = static_cast<int>(atomicAdd(cw.counter, 1u));
     __syncthreads();
     int64_t tile = *tile_slot;
-    if (tile < n_tiles) prefetch_tile<ANG, IN16, R>(p, ta, theta0, tile, n_chunks);
+    if (tile < n_tiles) prefetch_tile<ANG, IN16, R, XR>(p, ta, theta0, tile, n_chunks);
     __syncthreads();  // every thread has read the first tile
     while (ok && tile < n_tiles) {
         // every thread read the slot (the next tile) before the previous
@@ -1261,7 +1334,9 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
 
         float xv[kXItems][8];
         uint4 xraw[kXItems];  // bf16 inputs: v stays packed until after the gate barrier
-        if (R > 1) {
+        if (XR) {
+            load_x_xr<R, IN16>(p, bi, h, it0, xv);
+        } else if (R > 1) {
             load_x_r<R>(p, bi, h, it0, xv);
         } else if (IN16) {
 #pragma unroll
@@ -1281,17 +1356,17 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         float th[8][4];
         if (ANG) ang_part_a(p, ta, theta0, bi, h, bh, ch, n_chunks, it0, th, qtot, th0s);
         for (int i = tid; i < R * kTcN; i += kTcThreads2) {
-            qbs[i] = __ldg(p.q_bias + h * R * kTcN + i);
-            kbs[i] = __ldg(p.k_bias + h * R * kTcN + i);
+            qbs[i] = (!XR || p.q_bias) ? __ldg(p.q_bias + h * R * kTcN + i) : 0.f;
+            kbs[i] = (!XR || p.k_bias) ? __ldg(p.k_bias + h * R * kTcN + i) : 0.f;
         }
         if (warp == 0) tile_gates_r<R>(p, bh, it0, lcum, scl, gam, wdec, last_decay);
         __syncthreads();
-        if (IN16 && R == 1) {
+        if (IN16 && R == 1 && !XR) {
 #pragma unroll
             for (int q = 0; q < kXItems; ++q) unpack8(xraw[q], xv[q]);
         }
         const int64_t next_tile = *tile_slot;
-        if (next_tile < n_tiles) prefetch_tile<ANG, IN16, R>(p, ta, theta0, next_tile, n_chunks);
+        if (next_tile < n_tiles) prefetch_tile<ANG, IN16, R, XR>(p, ta, theta0, next_tile, n_chunks);
 #pragma unroll
         for (int q = 0; q < kXItems; ++q) {
             int j, pc;
@@ -1307,6 +1382,8 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         if (ANG)
             ang_part_b<IN16>(p, bi, h, bh, it0, th, qtot, th0s, smem + kFQ, smem + kFK, scl, qbs,
                              kbs);
+        else if (XR)
+            stage_qk_xr<R, IN16>(p, bi, h, it0, smem + kFQ, smem + kFK, qbs, kbs);
         else if (R > 1)
             stage_qk_mimo<R>(p, bi, h, it0, smem + kFQ, smem + kFK, qbs, kbs);
         else
@@ -1484,7 +1561,25 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
 #pragma unroll
                 for (int q = 0; q < 32; ++q) y[q] = fmaf(el, zt[q], y[q]);
             }
-            if (R > 1) {
+            if (XR) {
+                // per-rank MIMO: out (b, l, h, dv, R) row (t, rank) = y + D x
+                const int64_t it = it0 + r / R;
+                const int rk = r % R;
+                if (it < L) {
+                    const int64_t t = p.reverse ? L - 1 - it : it;
+                    const float dsk = p.d_skip ? p.d_skip[h] : 0.f;
+                    const int64_t base = (((bi * L + t) * H + h) * kTcP + hc * 32) * R + rk;
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) {
+                        float o = y[q];
+                        if (p.d_skip) o = fmaf(dsk, ld1_in<IN16>(p.v, base + q * R), o);
+                        if (OUT16)
+                            reinterpret_cast<__nv_bfloat16*>(p.out)[base + q * R] = __float2bfloat16_rn(o);
+                        else
+                            p.out[base + q * R] = o;
+                    }
+                }
+            } else if (R > 1) {
                 // MIMO: out_t = sum_r phi_r o g_r o (y_(t,r) + D x_(t,r)),
                 // g_r = silu(z o zeta_r) (1 without z); the R rows of a step
                 // are R adjacent lanes of this warp
@@ -1686,10 +1781,10 @@ cudaError_t m3_tc_launch_split(const M3Params& p, cudaStream_t stream) {
 }
 
 
-template <bool ANG, bool IN16, bool OUT16, int R = 1>
+template <bool ANG, bool IN16, bool OUT16, int R = 1, bool XR = false>
 cudaError_t launch_fused_kernel(const M3Params& p, const ChainWs& cw, int n_chunks, const float* ta,
                                 const float* theta0, cudaStream_t stream) {
-    auto kern = m3_tc_fused<ANG, IN16, OUT16, R>;
+    auto kern = m3_tc_fused<ANG, IN16, OUT16, R, XR>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kFSmem));
     if (e == cudaSuccess)
@@ -1745,7 +1840,15 @@ cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
             e = cudaGetLastError();
         }
     }
-    if (e == cudaSuccess) {
+    if (e == cudaSuccess && p.x_per_rank) {
+#define XR_PICK(RK)                                                                                   \
+    (p.in_bf16 ? (p.out_bf16 ? launch_fused_kernel<false, true, true, RK, true>(p, cw, n_chunks, nullptr, nullptr, stream)   \
+                             : launch_fused_kernel<false, true, false, RK, true>(p, cw, n_chunks, nullptr, nullptr, stream)) \
+               : (p.out_bf16 ? launch_fused_kernel<false, false, true, RK, true>(p, cw, n_chunks, nullptr, nullptr, stream)  \
+                             : launch_fused_kernel<false, false, false, RK, true>(p, cw, n_chunks, nullptr, nullptr, stream)))
+        e = p.rank == 4 ? XR_PICK(4) : XR_PICK(2);
+#undef XR_PICK
+    } else if (e == cudaSuccess) {
         if (p.rank == 4)
             e = launch_fused_kernel<false, false, false, 4>(p, cw, n_chunks, nullptr, nullptr, stream);
         else if (p.rank == 2)
@@ -1768,6 +1871,41 @@ cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
 cudaError_t m3_tc_launch(const M3Params& p, cudaStream_t stream) {
     if (p.angles || p.rank > 1) return m3_tc_launch_fused(p, stream);
     return kernel_override(kKnobM3TcSplit) == 1 ? m3_tc_launch_split(p, stream) : m3_tc_launch_fused(p, stream);
+}
+
+bool m3_tc_xr_applicable(const M3Params& p) {
+    auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    return (p.rank == 2 || p.rank == 4) && p.dqk == kTcN && p.dv == kTcP && p.len > 0 && !p.psi && !p.z &&
+           al(p.q_bias) && al(p.k_bias) && p.batch * p.heads <= 65535;
+}
+
+// Per-rank MIMO: the RoPE pre-pass (raw angles -> cos/sin in a stream-ordered
+// workspace; one angle row per step when angles_shared; no rotated pairs
+// gives cos 1, sin 0), then the fused tensor-core scan.
+cudaError_t m3_tc_launch_xr(const M3Params& p0, const float* angles, int64_t n_angles, int angles_shared,
+                            cudaStream_t stream) {
+    M3Params p = p0;
+    p.x_per_rank = 1;
+    const int64_t half = kTcN / 2;
+    const size_t cs_floats = static_cast<size_t>(p.batch * p.len * p.heads * half);
+    const size_t ws_bytes = n_angles > 0 ? angle_workspace_bytes(p.batch, p.heads, p.len, n_angles) : 0;
+    cudaMemPool_t pool = nullptr;
+    cudaError_t e = device_workspace_pool(&pool);
+    if (e != cudaSuccess) return e;
+    void* raw = nullptr;
+    e = cudaMallocFromPoolAsync(&raw, 2 * cs_floats * 4 + ws_bytes + 256, pool, stream);
+    if (e != cudaSuccess) return e;
+    float* cosv = static_cast<float*>(raw);
+    float* sinv = cosv + cs_floats;
+    float* ws = sinv + cs_floats;
+    AngleParams a{angles, p.dt, cosv, sinv, p.batch, p.heads, p.len, n_angles, half};
+    a.angles_shared = angles_shared;
+    e = angle_launch(a, ws, stream);
+    p.cos = cosv;
+    p.sin = sinv;
+    if (e == cudaSuccess) e = m3_tc_launch_fused(p, stream);
+    const cudaError_t ef = cudaFreeAsync(raw, stream);
+    return e != cudaSuccess ? e : ef;
 }
 
 int m3_tc_status_and_clear() {

@@ -364,3 +364,74 @@ def mamba3_mimo_scan(q, k, v, adt, dt, trap, q_bias, k_bias, psi, zeta, phi,
         _prep(sin, dev), opt(D), opt(z), bool(reverse), _prep(psi, dev), _prep(zeta, dev),
         _prep(phi, dev), backend=_PRECISION[precision])
     return (out, last) if return_last_state else out
+
+
+def mamba3_mimo_x_scan(x, B, C, adt, dt, trap, angles=None, D=None, reverse=False,
+                       return_last_state=False, out_dtype=None):
+    """Mamba-3 MIMO with the input given per rank (tensor cores, bf16 operands,
+    fp32 state).  Per (batch, head), h (dv x dqk):
+
+        h_t = a_t h_{t-1} + b_t X_{t-1} B_{t-1}^T + g_t X_t B_t^T,   Y_t = h_t C_t (+ D X_t)
+
+    with a = exp(adt), g = dt * sigmoid(trap), b = a * dt * (1 - sigmoid(trap))
+    (the gates of ``mamba3_scan``) and B, C RoPE-rotated split-halves by
+    theta = cumsum(tanh(angles) * pi * dt).  This is ``mamba3_mimo_scan`` with
+    x_r given directly instead of psi_r * v, and per-rank outputs instead of
+    the zeta-gated, phi-weighted sum (reference python/arm_scan/mamba3.py:261-334).
+
+    x : (b, l, h, dv, r) fp32 or bf16;  B, C : (b, l, dqk, r), same dtype
+    adt, dt, trap : (b, h, l);  angles : (b, l, a) shared by the heads or
+    (b, l, h, a), a <= dqk/2 (None: no rotation);  D : (h,) or None
+    returns Y (b, l, h, dv, r) in ``out_dtype`` (default x's dtype)
+    [, last_state (b, h, dv, dqk) fp32].  rank 2 or 4, dqk 128, dv 64.
+    """
+    if x.dim() != 5 or B.dim() != 4 or C.dim() != 4:
+        raise ValueError("x must be (b, l, h, dv, r) and B, C (b, l, dqk, r)")
+    b, length, h, dv, rank = x.shape
+    dqk = B.shape[2]
+    if tuple(B.shape) != (b, length, dqk, rank) or tuple(C.shape) != tuple(B.shape):
+        raise ValueError(f"B and C must be {(b, length, dqk, rank)}, got {tuple(B.shape)} and "
+                         f"{tuple(C.shape)}")
+    if x.dtype not in (torch.float32, torch.bfloat16) or B.dtype != x.dtype or C.dtype != x.dtype:
+        raise ValueError("x, B, C must share one dtype, float32 or bfloat16")
+    for name, t in (("adt", adt), ("dt", dt), ("trap", trap)):
+        if tuple(t.shape) != (b, h, length):
+            raise ValueError(f"{name} must be {(b, h, length)}, got {tuple(t.shape)}")
+    shared, n_angles = 1, 0
+    if angles is not None:
+        if angles.dim() == 3 and tuple(angles.shape[:2]) == (b, length):
+            shared = 1
+        elif angles.dim() == 4 and tuple(angles.shape[:3]) == (b, length, h):
+            shared = 0
+        else:
+            raise ValueError(f"angles must be (b, l, a) or (b, l, h, a), got {tuple(angles.shape)}")
+        n_angles = angles.shape[-1]
+        if n_angles > dqk // 2:
+            raise ValueError(f"angles has {n_angles} pairs, head dim allows {dqk // 2}")
+    if D is not None and tuple(D.shape) != (h,):
+        raise ValueError(f"D must be ({h},), got {tuple(D.shape)}")
+    if x.device.type != "cuda":
+        raise ValueError("mamba3_mimo_x_scan runs on CUDA tensors only")
+    out_dtype = x.dtype if out_dtype is None else out_dtype
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("out_dtype must be float32 or bfloat16")
+    f32 = lambda t: t.to(torch.float32).contiguous()  # noqa: E731
+    xs, Bs, Cs = x.contiguous(), B.contiguous(), C.contiguous()
+    adt_, dt_, trap_ = f32(adt), f32(dt), f32(trap)
+    ang = f32(angles) if angles is not None else None
+    Ds = f32(D) if D is not None else None
+    out = torch.empty(b, length, h, dv, rank, dtype=out_dtype, device=x.device)
+    last = torch.empty(b, h, dv, dqk, dtype=torch.float32, device=x.device) \
+        if return_last_state else None
+    dims = _ffi.ArmMamba3Dims(b, h, dv, dqk, length, rank)
+    opts = _ffi.ArmMamba3TcOptions(
+        _ffi.DTYPE_BF16 if x.dtype == torch.bfloat16 else _ffi.DTYPE_F32,
+        _ffi.DTYPE_BF16 if out_dtype == torch.bfloat16 else _ffi.DTYPE_F32, 0, shared, n_angles)
+    ptrs = [xs.data_ptr(), Bs.data_ptr(), Cs.data_ptr(), adt_.data_ptr(), dt_.data_ptr(),
+            trap_.data_ptr(), ang.data_ptr() if ang is not None else 0,
+            Ds.data_ptr() if Ds is not None else 0]
+    with torch.cuda.device(x.device):
+        _ffi.mamba3_mimo_x_raw(dims, opts, ptrs, bool(reverse), out.data_ptr(),
+                               last.data_ptr() if last is not None else 0,
+                               torch.cuda.current_stream(x.device).cuda_stream)
+    return (out, last) if return_last_state else out

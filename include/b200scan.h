@@ -213,6 +213,31 @@ int arm_scan_mamba3_siso_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOp
                                   const void* z, int reverse, void* out, float* last_state,
                                   float* last_bx, void* stream);
 
+/* Extension: Mamba-3 MIMO with the input given per rank, on the tensor
+ * cores.  Per (batch, head), with X_t (dv x rank), B_t and C_t (dqk x rank)
+ * RoPE-rotated split-halves by theta_t = cumsum(tanh(angle) * pi * dt):
+ *   h_t = alpha_t h_{t-1} + beta_t X_{t-1} B_{t-1}^T + gamma_t X_t B_t^T
+ *   Y_t = h_t C_t (+ D X_t)
+ * alpha = exp(adt), gamma = dt sigmoid(trap), beta = alpha dt (1 -
+ * sigmoid(trap)) (the gates of arm_scan_mamba3_scan_f32; "previous" is
+ * t + 1 with reverse).  It is the reference's MIMO op
+ * (python/arm_scan/mamba3.py:261-334, kernel/arm-scan-core/src/mamba3/
+ * mimo.rs:98-284) with x_r given directly instead of psi_r * v and the
+ * per-rank outputs returned instead of the zeta-gated, phi-weighted sum.
+ * Layouts: x, out (batch, len, heads, dv, rank); b, c (batch, len, dqk,
+ * rank); adt, dt, trap (batch, heads, len) fp32; angles fp32, (batch, len,
+ * n_angles) with opts->angles_shared = 1 or (batch, len, heads, n_angles)
+ * (nullable with n_angles 0: no rotation); d_skip (heads) nullable;
+ * last_state (batch, heads, dv, dqk) = h after the last step, nullable.
+ * opts->in_dtype is the dtype of x, b, c; opts->out_dtype that of out;
+ * opts->out_layout is ignored.  rank 2 or 4, dqk 128, dv 64 (else code 3).
+ * Device pointers, stream-ordered; fp32 state, bf16 matrix operands. */
+int arm_scan_mamba3_mimo_x_tc_async(const ArmMamba3Dims* dims, const ArmMamba3TcOptions* opts,
+                                    const void* x, const void* b, const void* c, const float* adt,
+                                    const float* dt, const float* trap, const float* angles,
+                                    const float* d_skip, int reverse, void* out, float* last_state,
+                                    void* stream);
+
 /* Extension (no counterpart in the reference): the four-direction Mamba-3
  * SISO cross-scan of a token grid in one call (the reference composes it in
  * Python, python/arm_scan/ss2d_mamba3.py).  The grid is len / grid_w rows of
