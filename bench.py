@@ -1,25 +1,33 @@
 """Benchmark of the selective-scan hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload prefill_scan|cfg0|cfg2|cfg3|cfg4a|cfg4b]
+                    [--no-configs] [--no-prefill] [--no-e2e] [--no-cpu-baseline]
 
 A step is one Mamba-1 ``selective_scan`` call over one batch of synthetic
-input (fp32, seed 0).  Default workload ``prefill_scan``: the per-layer scan
-of BASELINE config 1 (HF Mamba-1 130M architecture prefill, batch 8 x
-L 2048, d_inner 1536, d_state 16, softplus + delta_bias + D skip + z gate,
-final state returned); 405.5 MB of algorithmic traffic per step, larger than
-the 126 MB L2, so no flush is needed between steps.  ``cfg0`` is BASELINE
-config 0 (batch 1) with an L2 flush between steps.
+input (fp32, seed = rank).  The headline workload ``prefill_scan`` is the
+per-layer scan of BASELINE config 1 (HF Mamba-1 130M architecture prefill,
+batch 8 x L 2048, d_inner 1536, d_state 16, softplus + delta_bias + D skip +
+z gate, final state returned): 405.6 MB of algorithmic traffic per step,
+larger than the 126 MB L2, so no flush is needed between steps.
 
-value      -- algorithmic GB/s of the whole job (all ranks), inputs resident
-              in HBM, CUDA-event timed, max over ranks.
-e2e        -- the same metric through the reference-facing synchronous C
-              entry point with pinned HOST buffers (H2D + kernel + D2H inside
-              the timed region).
-roofline   -- the scan kernel's achieved algorithmic bandwidth against the
-              measured HBM copy bandwidth.
+value        -- algorithmic GB/s of the whole job (all ranks), inputs resident
+                in HBM, CUDA-event timed, max over ranks.
+e2e          -- the same metric through the reference-facing synchronous C
+                entry point with pinned HOST buffers (H2D + kernels + D2H in
+                the timed region).
+roofline     -- the scan kernels' achieved algorithmic bandwidth against the
+                measured HBM copy bandwidth (MEASURED_PEAKS.json).
 cpu_baseline -- the oracle port of the reference's x86 CPU path (scalar
-              recurrence, rows spread over all host threads), rank 0 only.
+                recurrence, rows over all host threads), rank 0 only.
+configs      -- (N = 1) every other BASELINE configuration as a sub-record:
+                config 0, 2 (bf16 tensor path and fp32 path), 3 (per-rank
+                MIMO, bf16), 4a (SS2D Mamba-3), 4b (bidirectional, L 262144)
+                and config 1 (HF prefill tok/s), each with its time,
+                algorithmic bytes and flops, roofline fraction and the CPU
+                port timed on a stated sample (extrapolated linearly in L
+                where the sample is shorter than the configuration).
+                At N > 1: config 4b sequence-parallel over the ranks
+                (strong scaling, one all_gather of segment carries).
 
 Multi-GPU: one process per GPU (torchrun); each rank scans its own batch
 (weak scaling over batch rows, no collective on the data path).
@@ -41,34 +49,21 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "scan GB/s & elems/s vs HBM roofline at 1/2/4/8 B200; Mamba-1 prefill tok/s"
 
-WORKLOADS = {
-    "prefill_scan": dict(batch=8, dim=1536, len=2048, state=16, flush=False,
-                         desc="Mamba-1 selective_scan at the 130M prefill shape (BASELINE "
-                              "config 1's per-layer scan): batch 8 x L 2048, d_inner 1536, "
-                              "d_state 16, fp32"),
-    "cfg0": dict(batch=1, dim=1536, len=2048, state=16, flush=True,
-                 desc="BASELINE config 0: Mamba-1 selective_scan B1 D1536 L2048 N16 fp32"),
-}
+PREFILL = dict(batch=8, dim=1536, len=2048, state=16,
+               desc="Mamba-1 selective_scan at the 130M prefill shape (BASELINE config 1's "
+                    "per-layer scan): batch 8 x L 2048, d_inner 1536, d_state 16, fp32")
+CFG0 = dict(batch=1, dim=1536, len=2048, state=16,
+            desc="BASELINE config 0: Mamba-1 selective_scan B1 D1536 L2048 N16 fp32")
+CFG2 = dict(kind="siso", batch=4, heads=24, dv=64, dqk=128, len=4096, rank=1, pairs=64)
+CFG4A = dict(kind="ss2d", batch=8, heads=6, dv=64, dqk=64, len=128 * 128, rank=1, pairs=32,
+             grid=128)
+CFG3 = dict(batch=8, heads=24, dv=64, dqk=128, len=8192, rank=4, pairs=64)
+CFG4B = dict(batch=1, dim=1536, len=262144, state=16)
 
-
-M3_WORKLOADS = {
-    "cfg2": dict(kind="siso", batch=4, heads=24, dv=64, dqk=128, len=4096, rank=1, pairs=64,
-                 desc="BASELINE config 2: Mamba-3 SISO B4 H24 P64 N128 L4096 (fp32 on the C "
-                      "ABI; the config's bf16 inputs are exactly representable)"),
-    "cfg3": dict(kind="mimo", batch=8, heads=24, dv=64, dqk=128, len=8192, rank=4, pairs=64,
-                 desc="BASELINE config 3 shape: Mamba-3 MIMO r4 B8 H24 P64 N128 L8192 through the "
-                      "reference op formulation (psi/zeta/phi projections)"),
-    "cfg4a": dict(kind="ss2d", batch=8, heads=6, dv=64, dqk=64, len=128 * 128, rank=1, pairs=32,
-                  grid=128, desc="BASELINE config 4a: SS2D Mamba-3 SISO 128x128 grid B8 H6 P64 "
-                                 "N64 fp32, 4 directions summed"),
-    "m3_mixer": dict(kind="mixer", batch=4, heads=24, dv=64, dqk=128, len=4096, rank=1,
-                     pairs=32, desc="Mamba-3 mixer prologue (in_proj output -> scan inputs: "
-                                    "split, softplus/heavy-tail gates, B/C RMSNorm, relayouts) "
-                                    "at config 2's shape with the checkpoint's 3432-wide in_proj "
-                                    "rows (rope_fraction 0.5: 32 angles), fp32"),
-    "cfg4b": dict(kind="bidir", batch=1, dim=1536, len=262144, state=16,
-                  desc="BASELINE config 4b: Mamba-1 bidirectional D1536 N16 L262144 fp32, summed"),
-}
+# algorithmic bytes and flops of the configurations (per call)
+CFG_BYTES = {"cfg0": 50.80e6, "cfg2_bf16": 117.4e6, "cfg2_fp32": None, "cfg3": 1772e6,
+             "cfg4a": 492.8e6, "cfg4b": 6.476e9}
+CFG_FLOPS = {"cfg2_bf16": 22.5e9, "cfg2_fp32": 12.9e9, "cfg3": 824.6e9, "cfg4a": 51.5e9}
 
 
 def m3_inputs(w, device, seed=0):
@@ -158,151 +153,6 @@ def torch_mixer_prologue(proj, nheads, headdim, d_state, n_angles, dt_bias, B_no
             ang.contiguous())
 
 
-def run_m3(args, w):
-    """Time a Mamba-3 or bidirectional workload (recorded for the configs;
-    the headline line is the Mamba-1 prefill scan)."""
-    import torch
-    import armhackathon_b200 as arm
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    if w["kind"] == "bidir":
-        world = int(os.environ.get("WORLD_SIZE", "1"))
-        rank = int(os.environ.get("RANK", "0"))
-        local = int(os.environ.get("LOCAL_RANK", "0"))
-        dev = torch.device("cuda", local)
-        torch.cuda.set_device(dev)
-        seg = w["len"] // world  # strong scaling: one sequence split over the ranks
-        x = make_inputs(dict(batch=1, dim=w["dim"], len=seg, state=w["state"]), dev, seed=rank)
-        if world > 1:
-            import torch.distributed as dist
-            from armhackathon_b200.seqpar import bidirectional_scan_seqpar
-            dist.init_process_group("nccl", device_id=dev)
-            step = lambda: bidirectional_scan_seqpar(  # noqa: E731
-                x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"], z=x["z"],
-                delta_bias=x["delta_bias"], delta_softplus=True)
-        else:
-            step = lambda: arm.bidirectional_scan(  # noqa: E731
-                x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"], z=x["z"],
-                delta_bias=x["delta_bias"], delta_softplus=True, merge="sum")
-        nbytes = 4 * (4 * w["dim"] * w["len"] + 2 * w["state"] * w["len"])
-        for _ in range(args.warmup):
-            step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(args.steps):
-            step()
-        b.record()
-        torch.cuda.synchronize()
-        ms = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
-        if world > 1:
-            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-            dist.destroy_process_group()
-        if rank == 0:
-            print(json.dumps({"metric": METRIC, "workload": args.workload, "desc": w["desc"],
-                              "n_gpus": world, "scaling": "strong",
-                              "ms_per_step": float(ms.item()),
-                              "value": nbytes / (float(ms.item()) * 1e-3) / 1e9, "unit": "GB/s",
-                              "bytes_per_step": nbytes,
-                              "parallelism": f"sequence-parallel over {world} ranks, one "
-                                             "all_gather of segment carries per call"}),
-                  flush=True)
-        return
-    elif w["kind"] == "mixer":
-        return run_mixer(args, w, dev)
-    else:
-        x = m3_inputs(w, dev)
-        nbytes = m3_bytes(w)
-        if w["kind"] == "mimo":
-            prec = "bf16" if args.m3_bf16 else "fp32"
-            step = lambda: arm.mamba3_mimo_scan(**x, precision=prec)  # noqa: E731
-        elif w["kind"] == "siso" and args.m3_bf16:
-            # bf16 model inputs, angles shared by all heads; the tensor-core
-            # entry with the angle pre-pass fused in, output (b, l, h, dv) bf16
-            bf = torch.bfloat16
-            xb = dict(x, q=x["q"].to(bf), k=x["k"].to(bf), v=x["v"].to(bf),
-                      angles=x["angles"][:, :, :1, :].to(bf).contiguous())
-            nbytes = m3_bytes_bf16(w)
-            step = lambda: arm.mamba3_scan(**xb, return_last_state=True,  # noqa: E731
-                                           precision="bf16")
-        elif w["kind"] == "siso":
-            step = lambda: arm.mamba3_scan(**x, return_last_state=True)  # noqa: E731
-        else:
-            B, H, g = w["batch"], w["heads"], w["grid"]
-            grid = lambda t: t.reshape(B, g, g, *t.shape[2:])  # noqa: E731
-            hm = lambda t: t.reshape(B, H, g, g)  # noqa: E731
-            xs = dict(q=grid(x["q"]), k=grid(x["k"]), v=grid(x["v"]), angles=grid(x["angles"]),
-                      adt=hm(x["adt"]), dt=hm(x["dt"]), trap=hm(x["trap"]),
-                      q_bias=x["q_bias"], k_bias=x["k_bias"], D=x["D"])
-            step = lambda: arm.ss2d_scan_mamba3(**xs)  # noqa: E731
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(args.steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / args.steps
-    print(json.dumps({"metric": METRIC, "workload": args.workload, "desc": w["desc"],
-                      "ms_per_step": ms, "value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
-                      "bytes_per_step": nbytes,
-                      "note": "whole op incl. the torch angle pre-pass and output permute"}),
-          flush=True)
-
-
-def run_mixer(args, w, dev):
-    """The fused Mamba-3 mixer prologue: HBM roofline of the one kernel, the
-    same prologue as separate torch ops, and prologue + fp32 scan."""
-    import torch
-    import armhackathon_b200 as arm
-    from armhackathon_b200 import _ffi
-    x = mixer_inputs(w, dev)
-    nbytes = mixer_bytes(w)
-    H, N = w["heads"], w["dqk"]
-    scan_kw = dict(D=torch.ones(H, device=dev), B_bias=torch.zeros(H, 1, N, device=dev),
-                   C_bias=torch.zeros(H, 1, N, device=dev))
-
-    def timed(fn, steps):
-        for _ in range(args.warmup):
-            fn()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(steps):
-            fn()
-        b.record()
-        torch.cuda.synchronize()
-        return a.elapsed_time(b) / steps
-
-    n0 = _ffi.kernel_launches()
-    with ClockSampler(dev.index or 0) as clk:
-        ms = timed(lambda: arm.mamba3_mixer_prologue(**x), args.steps)
-    clocks = clk.summary()
-    per_call = (_ffi.kernel_launches() - n0) / (args.warmup + args.steps)
-    launches = int(round(per_call * args.steps))  # kernels in the timed region
-    torch_ms = timed(lambda: torch_mixer_prologue(**x), args.steps)
-    full_ms = timed(lambda: arm.mamba3_mixer_scan(**x, **scan_kw), max(1, args.steps // 5))
-    bf16_ms = timed(lambda: arm.mamba3_mixer_scan(**x, **scan_kw, precision="bf16"),
-                    max(1, args.steps // 5))
-    peak, peak_kind = peaks()
-    gbs = nbytes / (ms * 1e-3) / 1e9
-    print(json.dumps({
-        "metric": METRIC, "workload": args.workload, "desc": w["desc"], "ms_per_step": ms,
-        "value": gbs, "unit": "GB/s", "bytes_per_step": nbytes, "dtype": "f32",
-        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
-                     "frac": gbs / peak, "peak_source": peak_kind},
-        "gpu_launches": launches, "clocks": clocks,
-        "torch_ops_ms": torch_ms, "prologue_plus_fp32_scan_ms": full_ms,
-        "prologue_plus_bf16_tensor_scan_ms": bf16_ms,
-        "l2": "inputs larger than L2",
-        "note": "the prologue alone (one kernel, CUDA events); torch_ops_ms = the same "
-                "prologue as separate torch ops on this GPU"}), flush=True)
-
-
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -311,45 +161,24 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def profiled_traffic(workload):
-    """DRAM bytes of one scan op (all of its kernels) from the committed ncu
-    summary (profiles/m1_seg2_<workload>.md, line 'traffic_bytes_per_launch:
-    N'), or None when no capture of this workload is committed."""
-    import re
-    f = ROOT / "profiles" / f"m1_seg2_{workload}.md"
-    if not f.exists():
-        return None
-    m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", f.read_text())
-    return int(m.group(1)) if m else None
-
-
-def seg2_segments(w):
-    """Segment count the default Mamba-1 kernel picks for this shape (the rule
-    of m1_seg2_segments in armhackathon_b200/csrc/m1_seg2.cu)."""
-    rows, L, S = w["batch"] * w["dim"], w["len"], 1
-    while rows * S < 148 * 1024 and L % (2 * S) == 0 and L // (2 * S) >= 128 \
-            and (L // (2 * S)) % 64 == 0:
-        S *= 2
-    return S
-
-
-def mufu_roofline(w, k_ms, clocks):
-    """The Mamba-1 scan's binding unit: one exp per (batch, channel, step,
+def mufu_roofline(w, k_ms, clocks, launches_per_call):
+    """The Mamba-1 scan's second roof: one exp per (batch, channel, step,
     state) is the algorithm's minimum (the reference computes exactly that);
-    the MUFU pipe issues 16 of them per clock per SM (nominal), taken at the
-    SM clock sampled during the timed region."""
+    the MUFU unit issues 16 per clock per SM (nominal), at the SM clock
+    sampled during the timed region.  One launch per call means the lane
+    kernel ran unsplit, one exp per (step, state); three mean a time split
+    (pass 1, carry, pass 2), whose rescan adds the exps of segments 1..S-2."""
     import torch
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
     exps = w["batch"] * w["dim"] * w["len"] * w["state"]
-    S = seg2_segments(w)
     achieved = exps / (k_ms * 1e-3) / 1e9
     peak = 16 * sms * mhz * 1e6 / 1e9
     return {"bound": "mufu", "achieved": achieved, "peak": peak, "unit": "Gexp/s",
             "frac": achieved / peak, "peak_source": "nominal 16/clk/SM x sampled SM clock",
-            "executed_per_algorithmic": 2 * (S - 1) / S if S > 1 else 1.0, "segments": S,
-            "note": "the default two-pass kernel computes the exps of segments 1 .. S-2 twice "
-                    "(end states, then outputs), plus the softplus/silu exps per (row, step)"}
+            "launches_per_call": launches_per_call,
+            "executed_per_algorithmic": 1.0 if launches_per_call == 1 else None,
+            "note": "plus the softplus/silu transcendentals, 4 per (row, step)"}
 
 
 def algorithmic_bytes(w):
@@ -477,46 +306,6 @@ def prefill_tok_s(dev, batch, length, steps=3, warmup=2):
             "kernel_engaged": engaged}
 
 
-def run_reference(args, w):
-    """--impl reference: the reference's CPU path (scalar recurrence over rows
-    on all host threads; oracle port, the Rust crate has no toolchain here)."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    nthreads = oracle.hw_threads()
-    rng = np.random.default_rng(0)
-    B, D, L, N = w["batch"], w["dim"], w["len"], w["state"]
-    f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
-    dt = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), D))
-    inp = dict(u=f(B, D, L), delta=f(B, D, L), z=f(B, D, L),
-               A=-np.tile(np.arange(1, N + 1, dtype=np.float32), (D, 1)), B=f(B, N, L),
-               C=f(B, N, L), D=np.ones(D, np.float32),
-               delta_bias=np.log(np.expm1(dt)).astype(np.float32))
-    for _ in range(args.warmup):
-        oracle.m1_scan(**inp, delta_softplus=True, dtype=np.float32, nthreads=nthreads)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        oracle.m1_scan(**inp, delta_softplus=True, dtype=np.float32, nthreads=nthreads)
-        times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    gbs = algorithmic_bytes(w) / t / 1e9
-    line = {"impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": 0,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seed 0, BASELINE config 0 distributions)",
-            "config": {"workload": args.workload, "desc": w["desc"], "batch": B, "dim": D,
-                       "len": L, "state": N},
-            "elems_per_s": B * D * L / t,
-            "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": nthreads, "kind": "port",
-                             "sample": f"the full step workload ({B}x{D}x{L}, N={N}) per step"},
-            "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
-
-
 def cpu_baseline(w):
     """Oracle port of the reference's CPU path on a bounded sample: all host
     threads, batch row 0 only (1/batch of the workload)."""
@@ -545,33 +334,339 @@ def cpu_baseline(w):
             "sample": f"batch row 0 of the workload (1x{D}x{L}, N={N}), {reps} reps"}
 
 
+def sm_peaks(clock_mhz=None):
+    """Compute peaks for the roofline of a sub-record: measured bf16 tensor
+    throughput (MEASURED_PEAKS.json, burst) and the nominal fp32 CUDA-core
+    rate (148 SMs x 128 FMA x 2 at the SM clock)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    bf16 = 1590.0
+    mhz = clock_mhz or 1965.0
+    if p.exists():
+        d = json.loads(p.read_text())
+        bf16 = float(d.get("bf16_tflops", bf16))
+        mhz = clock_mhz or float(d.get("sm_max_mhz", mhz))
+    return bf16, 148 * 128 * 2 * mhz * 1e6 / 1e12
+
+
+def time_call(fn, steps, warmup, graph=True):
+    """Device time per call (ms), CUDA events around `steps` calls.  With
+    graph=True the calls are captured once into a CUDA graph and replayed,
+    so host-side launch overhead does not enter the figure of small ops;
+    falls back to eager launches if capture fails."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    g = None
+    if graph:
+        try:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                fn()
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(steps):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize()
+        except Exception:  # noqa: BLE001 -- eager timing below
+            g = None
+            torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    if g is not None:
+        g.replay()
+    else:
+        for _ in range(steps):
+            fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps, ("cuda graph" if g is not None else "eager")
+
+
+def roof(ms, nbytes, flops, hbm, tc_peak_tflops):
+    """Roofline of one sub-record: the slower of bytes / HBM and flops /
+    compute peak, against the measured time."""
+    t_mem = nbytes / (hbm * 1e9) if nbytes else 0.0
+    t_cmp = flops / (tc_peak_tflops * 1e12) if flops else 0.0
+    bound = "hbm" if t_mem >= t_cmp else "compute"
+    t = max(t_mem, t_cmp)
+    return {"bound": bound, "frac": t / (ms * 1e-3),
+            "achieved_gbs": nbytes / (ms * 1e-3) / 1e9 if nbytes else None,
+            "achieved_tflops": flops / (ms * 1e-3) / 1e12 if flops else None}
+
+
+def cpu_port(kind, nthreads):
+    """The oracle port of the reference's CPU path for one configuration on
+    a bounded sample; returns (ms per full configuration, sample text)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    rng = np.random.default_rng(0)
+    f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+
+    def clock(fn):
+        fn()
+        t0 = time.perf_counter()
+        fn()
+        return time.perf_counter() - t0
+
+    if kind in ("cfg0", "cfg4b"):
+        D, N = 1536, 16
+        L = 2048 if kind == "cfg0" else 16384
+        full_L = 2048 if kind == "cfg0" else 262144
+        dt = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), D))
+        inp = dict(u=f(1, D, L), delta=f(1, D, L), z=f(1, D, L),
+                   A=-np.tile(np.arange(1, N + 1, dtype=np.float32), (D, 1)), B=f(1, N, L),
+                   C=f(1, N, L), D=np.ones(D, np.float32),
+                   delta_bias=np.log(np.expm1(dt)).astype(np.float32))
+        if kind == "cfg0":
+            t = clock(lambda: oracle.m1_scan(**inp, delta_softplus=True, dtype=np.float32,
+                                             nthreads=nthreads))
+        else:
+            t = clock(lambda: oracle.m1_scan_bidir(**inp, delta_softplus=True, dtype=np.float32,
+                                                   nthreads=nthreads))
+        return t * 1e3 * full_L / L, f"1x{D}x{L} (x{full_L // L} extrapolated)"
+    if kind in ("cfg2", "cfg4a"):
+        w = CFG2 if kind == "cfg2" else CFG4A
+        B, H, P, N = w["batch"], w["heads"], w["dv"], w["dqk"]
+        L = 1024
+        full = w["len"] * (4 if kind == "cfg4a" else 1)  # 4a: four traversals
+        dt = np.log1p(np.exp(f(B, H, L) - 4))
+        A = -np.exp(rng.uniform(0, np.log(16), H)).astype(np.float32)
+        cos, sin = oracle.angles_to_cos_sin(f(B, L, H, w["pairs"]), dt, N // 2)
+        args = (f(B, L, 1, N) / np.sqrt(N), f(B, L, 1, N) / np.sqrt(N), f(B, L, H, P),
+                A[None, :, None] * dt, dt, f(B, H, L), np.zeros((H, N), np.float32),
+                np.zeros((H, N), np.float32), cos, sin)
+        t = clock(lambda: oracle.m3_siso(*args, D=np.ones(H, np.float32), dtype=np.float32,
+                                         nthreads=nthreads))
+        return t * 1e3 * full / L, f"{B}x{H} heads, L {L} (x{full / L:g} extrapolated)"
+    if kind == "cfg3":
+        w = CFG3
+        B, H, P, N, R = w["batch"], w["heads"], w["dv"], w["dqk"], w["rank"]
+        B, L = 1, 256
+        dt = np.log1p(np.exp(f(B, H, L) - 4))
+        A = -np.exp(rng.uniform(0, np.log(16), H)).astype(np.float32)
+        cos, sin = oracle.angles_to_cos_sin(f(B, L, H, w["pairs"]), dt, N // 2)
+        t = clock(lambda: oracle.m3_mimo_x(f(B, L, H, P, R), f(B, L, N, R), f(B, L, N, R),
+                                           A[None, :, None] * dt, dt, f(B, H, L), cos, sin,
+                                           dtype=np.float32, nthreads=nthreads))
+        scale = w["batch"] * w["len"] / (B * L)
+        return t * 1e3 * scale, f"1x{H} heads, L {L} (x{scale:g} extrapolated)"
+    raise ValueError(kind)
+
+
+def config_suite(args, dev, hbm, clocks):
+    """Every BASELINE configuration besides the headline, one sub-record each."""
+    import torch
+    import armhackathon_b200 as arm
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    nthreads = oracle.hw_threads()
+    mhz = clocks.get("sm_mhz") if clocks else None
+    bf16_peak, fp32_peak = sm_peaks(mhz)
+    out = {}
+    steps = max(3, min(args.steps, 20))
+
+    def record(name, ms, how, nbytes, flops, peak, desc, cpu_kind):
+        r = {"desc": desc, "ms": ms, "timing": how, "bytes": nbytes, "flops": flops,
+             "roofline": roof(ms, nbytes, flops, hbm, peak)}
+        if cpu_kind and not args.no_cpu_baseline:
+            cms, sample = cpu_port(cpu_kind, nthreads)
+            r["cpu_baseline"] = {"ms": cms, "cores": nthreads, "kind": "port", "sample": sample,
+                                 "speedup": cms / ms}
+        out[name] = r
+
+    # config 0 (L2 flushed between calls is not possible inside the graph:
+    # 50.8 MB fits L2, so the figure is an L2-warm one; the headline is not)
+    x = make_inputs(CFG0, dev)
+    f0 = lambda: arm.selective_scan(x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"],  # noqa: E731
+                                    z=x["z"], delta_bias=x["delta_bias"], delta_softplus=True,
+                                    return_last_state=True)
+    ms, how = time_call(f0, steps, args.warmup)
+    record("cfg0", ms, how, CFG_BYTES["cfg0"], None, bf16_peak, CFG0["desc"] +
+           " (L2-warm: the inputs fit the 126 MB L2)", "cfg0")
+    del x
+
+    # config 2: bf16 inputs on the tensor cores, and the fp32 chunk path
+    x = m3_inputs(CFG2, dev)
+    bf = torch.bfloat16
+    xb = dict(x, q=x["q"].to(bf), k=x["k"].to(bf), v=x["v"].to(bf),
+              angles=x["angles"][:, :, :1, :].to(bf).contiguous())
+    ms, how = time_call(lambda: arm.mamba3_scan(**xb, return_last_state=True, precision="bf16"),
+                        steps, args.warmup)
+    record("cfg2_bf16", ms, how, CFG_BYTES["cfg2_bf16"], CFG_FLOPS["cfg2_bf16"], bf16_peak,
+           "BASELINE config 2: Mamba-3 SISO B4 H24 P64 N128 L4096, bf16 inputs, fp32 state, "
+           "tcgen05 kernel with the angle pre-pass fused", "cfg2")
+    ms, how = time_call(lambda: arm.mamba3_scan(**x, return_last_state=True), steps, args.warmup)
+    record("cfg2_fp32", ms, how, m3_bytes(CFG2), CFG_FLOPS["cfg2_fp32"], fp32_peak,
+           "config 2's shape with fp32 inputs on the fp32 chunk kernels (CUDA cores; "
+           "flops are the sequential form's)", None)
+    del x, xb
+
+    # config 3: per-rank MIMO, bf16
+    w = CFG3
+    g = torch.Generator(device=dev).manual_seed(0)
+    rn = lambda *s: torch.randn(*s, generator=g, device=dev)  # noqa: E731
+    B, L, H, P, N, R = w["batch"], w["len"], w["heads"], w["dv"], w["dqk"], w["rank"]
+    dt = torch.nn.functional.softplus(rn(B, H, L) - 4)
+    A = -torch.exp(torch.rand(H, generator=g, device=dev) * np.log(16))
+    X = rn(B, L, H, P, R).to(bf)
+    Bm = (rn(B, L, N, R) / (N * R) ** 0.5).to(bf)
+    Cm = (rn(B, L, N, R) / (N * R) ** 0.5).to(bf)
+    ang = torch.atanh(torch.rand(B, L, w["pairs"], generator=g, device=dev) * 0.999)
+    trap, adt = rn(B, H, L), A.view(1, H, 1) * dt
+    ms, how = time_call(lambda: arm.mamba3_mimo_x_scan(X, Bm, Cm, adt, dt, trap, angles=ang,
+                                                       return_last_state=True),
+                        max(2, steps // 4), 2)
+    record("cfg3", ms, how, CFG_BYTES["cfg3"], CFG_FLOPS["cfg3"], bf16_peak,
+           "BASELINE config 3: Mamba-3 MIMO r4 with X per rank (B8 H24 P64 N128 L8192), bf16 "
+           "inputs, fp32 state, tcgen05 kernel (32-step tiles of 128 (step, rank) rows)", "cfg3")
+    del X, Bm, Cm
+
+    # config 4a: SS2D Mamba-3, fp32
+    x = m3_inputs(CFG4A, dev)
+    Bq, Hh, gd = CFG4A["batch"], CFG4A["heads"], CFG4A["grid"]
+    grid = lambda t: t.reshape(Bq, gd, gd, *t.shape[2:])  # noqa: E731
+    hm = lambda t: t.reshape(Bq, Hh, gd, gd)  # noqa: E731
+    xs = dict(q=grid(x["q"]), k=grid(x["k"]), v=grid(x["v"]), angles=grid(x["angles"]),
+              adt=hm(x["adt"]), dt=hm(x["dt"]), trap=hm(x["trap"]), q_bias=x["q_bias"],
+              k_bias=x["k_bias"], D=x["D"])
+    ms, how = time_call(lambda: arm.ss2d_scan_mamba3(**xs), max(2, steps // 4), 2)
+    record("cfg4a", ms, how, CFG_BYTES["cfg4a"], CFG_FLOPS["cfg4a"], fp32_peak,
+           "BASELINE config 4a: SS2D Mamba-3 SISO, 128x128 grid, B8 H6 P64 N64 fp32, four "
+           "traversals summed in place", "cfg4a")
+    del x, xs
+
+    # config 4b: bidirectional Mamba-1, one sequence of 262144 steps
+    x = make_inputs(CFG4B, dev)
+    ms, how = time_call(lambda: arm.bidirectional_scan(
+        x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"], z=x["z"],
+        delta_bias=x["delta_bias"], delta_softplus=True, merge="sum"), max(2, steps // 4), 2)
+    record("cfg4b", ms, how, CFG_BYTES["cfg4b"], None, bf16_peak,
+           "BASELINE config 4b: Mamba-1 bidirectional D1536 N16 L262144 fp32, summed, 1 GPU",
+           "cfg4b")
+    del x
+    torch.cuda.empty_cache()
+
+    # Mamba-3 mixer prologue (in_proj output -> scan inputs) at config 2's shape
+    wm = dict(kind="mixer", batch=4, heads=24, dv=64, dqk=128, len=4096, rank=1, pairs=32)
+    xm = mixer_inputs(wm, dev)
+    ms, how = time_call(lambda: arm.mamba3_mixer_prologue(**xm), steps, args.warmup)
+    t_ms, _ = time_call(lambda: torch_mixer_prologue(**xm), steps, args.warmup, graph=False)
+    record("m3_mixer_prologue", ms, how, mixer_bytes(wm), None, bf16_peak,
+           "Mamba-3 mixer prologue (split, softplus / heavy-tail gates, B/C RMSNorm, "
+           "relayouts) at config 2's shape, 3432-wide in_proj rows, fp32, one kernel", None)
+    out["m3_mixer_prologue"]["torch_ops_ms"] = t_ms
+    del xm
+
+    # config 1: HF prefill tokens/s
+    if not args.no_prefill:
+        out["cfg1_prefill"] = {
+            "desc": "BASELINE config 1: random-init Mamba-1 130M architecture, fp32, patched HF "
+                    "MambaForCausalLM full forward (logits included), 1 GPU",
+            "runs": [prefill_tok_s(dev, 8, 2048), prefill_tok_s(dev, 1, 32768)]}
+    return out
+
+
+def run_seqpar_4b(args, dev, rank, world):
+    """Config 4b sequence-parallel over the ranks (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+    from armhackathon_b200.seqpar import bidirectional_scan_seqpar
+    seg = CFG4B["len"] // world
+    x = make_inputs(dict(CFG4B, len=seg), dev, seed=rank)
+    step = lambda: bidirectional_scan_seqpar(  # noqa: E731
+        x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"], z=x["z"],
+        delta_bias=x["delta_bias"], delta_softplus=True)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 5
+    a.record()
+    for _ in range(n):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / n], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"desc": f"BASELINE config 4b over {world} GPUs: one L 262144 sequence split in "
+                    f"{world} segments (strong scaling; one all_gather of segment carries)",
+            "ms": ms, "bytes": CFG_BYTES["cfg4b"], "GB_s": CFG_BYTES["cfg4b"] / (ms * 1e-3) / 1e9,
+            "n_gpus": world}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (scalar recurrence over rows
+    on all host threads; the oracle port, as the Rust crate has no toolchain
+    here) on the headline workload, plus every other configuration as a
+    sub-record on a stated sample.  Rank 0 only."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    nthreads = oracle.hw_threads()
+    rng = np.random.default_rng(0)
+    w = PREFILL
+    B, D, L, N = w["batch"], w["dim"], w["len"], w["state"]
+    f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    dt = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), D))
+    # a step is one batch row of the workload (1/8 of it, bounded CPU time);
+    # the line's value is that row's GB/s
+    inp = dict(u=f(1, D, L), delta=f(1, D, L), z=f(1, D, L),
+               A=-np.tile(np.arange(1, N + 1, dtype=np.float32), (D, 1)), B=f(1, N, L),
+               C=f(1, N, L), D=np.ones(D, np.float32),
+               delta_bias=np.log(np.expm1(dt)).astype(np.float32))
+    for _ in range(args.warmup):
+        oracle.m1_scan(**inp, delta_softplus=True, dtype=np.float32, nthreads=nthreads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.m1_scan(**inp, delta_softplus=True, dtype=np.float32, nthreads=nthreads)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    gbs = algorithmic_bytes(dict(w, batch=1)) / t / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": 0,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3 * B,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seed 0, BASELINE config 0 distributions)",
+            "config": {"workload": "prefill_scan", "desc": w["desc"], "batch": B, "dim": D,
+                       "len": L, "state": N},
+            "elems_per_s": D * L / t,
+            "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": nthreads, "kind": "port",
+                             "sample": f"batch row 0 of the workload (1x{D}x{L}, N={N}) per "
+                                       "step; ms_per_step is scaled to the full batch"},
+            "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    if not args.no_configs:
+        line["configs"] = {}
+        for k in ("cfg0", "cfg2", "cfg3", "cfg4a", "cfg4b"):
+            ms, sample = cpu_port(k, nthreads)
+            line["configs"][k] = {"ms": ms, "cores": nthreads, "kind": "port", "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="prefill_scan",
-                    choices=sorted(WORKLOADS) + sorted(M3_WORKLOADS))
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the sub-records of the other BASELINE configurations")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--m3-bf16", action="store_true",
-                    help="Mamba-3 SISO/MIMO workloads on the tensor-core (bf16 operand) kernels")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the config-1 HF prefill tok/s measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.workload in M3_WORKLOADS:
-        if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "workload": args.workload,
-                              "unavailable": "reference arm is implemented for the Mamba-1 "
-                                             "workloads only"}))
-            return
-        run_m3(args, M3_WORKLOADS[args.workload])
-        return
-    w = WORKLOADS[args.workload]
     if args.impl == "reference":
-        run_reference(args, w)
+        run_reference(args)
         return
 
     import torch
@@ -587,8 +682,8 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
 
+    w = PREFILL
     x = make_inputs(w, dev, seed=rank)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if w["flush"] else None
     stream = torch.cuda.current_stream(dev)
 
     def step():
@@ -606,13 +701,10 @@ def main():
     torch.cuda.synchronize()
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    from armhackathon_b200 import _ffi
     launches_before = _ffi.kernel_launches()
     with ClockSampler(local) as clk:
         t_begin.record(stream)
         for i in range(args.steps):
-            if flush is not None:
-                flush.fill_(i & 0xFF)
             starts[i].record(stream)
             step()
             ends[i].record(stream)
@@ -622,9 +714,7 @@ def main():
     if world > 1:
         dist.barrier()
     kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    step_ms = sum(kernel_ms) / len(kernel_ms) if flush is not None else \
-        t_begin.elapsed_time(t_end) / args.steps
-    t = torch.tensor([step_ms], device=dev)
+    t = torch.tensor([t_begin.elapsed_time(t_end) / args.steps], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms = float(t.item())
@@ -664,41 +754,44 @@ def main():
         d2h = (out_h.numel() + last_h.numel()) * 4
         e2e = {"value": world * nbytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
-               "path": "arm_scan_selective_scan_f32 (synchronous C entry, pinned host buffers)"}
+               "path": "arm_scan_selective_scan_f32 (synchronous C entry, pinned host buffers; "
+                       "host wall clock, max over ranks)"}
+        del host, out_h, last_h
+
+    seqpar = run_seqpar_4b(args, dev, rank, world) if world > 1 and not args.no_configs else None
 
     if rank == 0:
         peak, peak_kind = peaks()
         k_ms = statistics.mean(kernel_ms)
         achieved = nbytes / (k_ms * 1e-3) / 1e9
+        clocks = clk.summary()
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seed = rank, BASELINE config 0 distributions)",
-            "config": {"workload": args.workload, "desc": w["desc"], "batch_per_gpu": w["batch"],
+            "config": {"workload": "prefill_scan", "desc": w["desc"], "batch_per_gpu": w["batch"],
                        "dim": w["dim"], "len": w["len"], "state": w["state"],
                        "parallelism": f"dp{world} (batch rows per rank, no collective)",
-                       "l2": "inputs larger than L2" if not w["flush"] else
-                             "256 MB L2 flush between steps (outside the kernel events)"},
+                       "l2": "inputs larger than L2 (405.6 MB per step), no flush"},
             "elems_per_s": elems / (step_ms * 1e-3),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
-                         "traffic": profiled_traffic(args.workload),
-                         "traffic_source": "ncu dram__bytes_read+write summed over the op's "
-                                           "kernels (profiles/m1_seg2_<workload>.md)",
-                         "bytes_per_launch": nbytes,
-                         "kernel_ms": k_ms},
+                         "traffic": None,
+                         "traffic_note": "not measurable inside the run; the ncu DRAM bytes of "
+                                         "the same workload are in profiles/",
+                         "bytes_per_launch": nbytes, "kernel_ms": k_ms},
+            "mufu": mufu_roofline(w, k_ms, clocks, round(launches / args.steps)),
             "gpu_launches": launches,
             "e2e": e2e,
-            "clocks": clk.summary(),
+            "clocks": clocks,
         }
-        line["mufu"] = mufu_roofline(w, k_ms, line["clocks"])
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w)
-        if not args.no_prefill:
-            line["prefill"] = {
-                "metric": "Mamba-1 prefill tok/s (BASELINE config 1, fp32, patched HF, 1 GPU)",
-                "runs": [prefill_tok_s(dev, 8, 2048), prefill_tok_s(dev, 1, 32768)]}
+        if world == 1 and not args.no_configs:
+            line["configs"] = config_suite(args, dev, peak, clocks)
+        if seqpar:
+            line["configs"] = {"cfg4b_seqpar": seqpar}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
