@@ -125,6 +125,9 @@ def _bind(lib):
     lib.arm_scan_selective_scan_bidirectional_final_states_f32_async.restype = ctypes.c_int
     lib.arm_scan_selective_scan_bidirectional_final_states_f32_async.argtypes = [
         ctypes.POINTER(ArmScanDims), *([_VP] * 6), _I, _I, _VP, _VP, _VP]
+    lib.arm_scan_selective_scan_segment_summary_f32_async.restype = ctypes.c_int
+    lib.arm_scan_selective_scan_segment_summary_f32_async.argtypes = [
+        ctypes.POINTER(ArmScanDims), *([_VP] * 6), _I, _I, _VP, _VP, _VP, _VP]
     lib.arm_scan_mamba3_mixer_prologue_f32_async.restype = ctypes.c_int
     lib.arm_scan_mamba3_mixer_prologue_f32_async.argtypes = [
         ctypes.POINTER(ArmMamba3MixerDims), *([_VP] * 4), ctypes.c_float, ctypes.c_float,
@@ -316,6 +319,15 @@ def bidir_states_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_delta_bias
         "arm_scan_selective_scan_bidirectional_final_states_f32_async")
 
 
+def segment_summary_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_delta_bias,
+                        delta_softplus, backend, ptr_last_fwd, ptr_last_bwd, ptr_dt_sum, stream):
+    """Both final states and the per-row sum of dt of a segment (device pointers)."""
+    _check(load().arm_scan_selective_scan_segment_summary_f32_async(
+        ctypes.byref(dims), ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, _n(ptr_delta_bias),
+        int(bool(delta_softplus)), BACKENDS[backend], ptr_last_fwd, ptr_last_bwd, ptr_dt_sum,
+        _n(stream)), "arm_scan_selective_scan_segment_summary_f32_async")
+
+
 def kernel_launches():
     """GPU kernels the library has launched in this process so far."""
     return int(load().arm_scan_kernel_launches())
@@ -371,7 +383,8 @@ def exported_symbols():
             "arm_scan_mamba3_mixer_prologue_f32_async",
             "arm_scan_selective_scan_bidirectional_sum_f32_async",
             "arm_scan_selective_scan_bidirectional_final_states_f32_async",
-            "arm_scan_set_kernel_override", "arm_scan_mamba3_mimo_x_tc_async"]
+            "arm_scan_set_kernel_override", "arm_scan_mamba3_mimo_x_tc_async",
+            "arm_scan_selective_scan_segment_summary_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

@@ -674,6 +674,30 @@ int arm_scan_selective_scan_bidirectional_final_states_f32_async(
     return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "bidirectional final states launch");
 }
 
+int arm_scan_selective_scan_segment_summary_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
+    const float* c, const float* delta_bias, int delta_softplus, int backend, float* last_fwd,
+    float* last_bwd, float* dt_sum, void* stream) {
+    if (!last_fwd || !last_bwd || !dt_sum)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "last_fwd, last_bwd and dt_sum are required");
+    M1Counts cnt;
+    int rc = bidir_common(dims, u, delta, a, b, c, nullptr, nullptr, delta_bias, backend, 0,
+                          last_fwd, last_bwd, last_fwd, last_bwd, &cnt);
+    if (rc) return rc;
+    std::vector<void*> p = {const_cast<float*>(u), const_cast<float*>(delta),
+                            const_cast<float*>(a), const_cast<float*>(b),
+                            const_cast<float*>(c), nullptr,
+                            nullptr,               const_cast<float*>(delta_bias)};
+    M1Params base = m1_params(dims, p, delta_softplus, 0);
+    M1Params f = base, r = base;
+    f.last_state = last_fwd;
+    f.dt_sum = dt_sum;
+    r.reverse = 1;
+    r.last_state = last_bwd;
+    cudaError_t e = m1_segment_summary_launch(f, r, backend, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "segment summary launch");
+}
+
 int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const float* k,
                              const float* v, const float* adt, const float* dt, const float* trap,
                              const float* q_bias, const float* k_bias, const float* cos,

@@ -477,6 +477,7 @@ __global__ void m1_lane_carry(M1Params p, LaneWs ws, int S) {
     const int64_t row = i / N, n = i % N;
     const float a = p.A[(row % p.dim) * N + n] * kLog2e;
     float h = FIRST ? __ldg(ws.hend + row * 16 + n) : (p.h0 ? p.h0[i] : 0.f);
+    float dts = 0.f;  // the whole sequence's sum of dt (segment summaries)
     const int k_end = FIRST ? S - 1 : S;
     for (int k0 = FIRST ? 1 : 0; k0 < k_end; k0 += 8) {
         float ds[8], he[8];
@@ -491,10 +492,12 @@ __global__ void m1_lane_carry(M1Params p, LaneWs ws, int S) {
             if (k0 + u >= k_end) break;
             ws.hin[(static_cast<int64_t>(k0 + u) * rows_all + row) * 16 + n] = h;
             h = fmaf(ex2_approx(a * ds[u]), h, he[u]);
+            dts += ds[u];
         }
     }
     if (FIRST && S > 1) ws.hin[(static_cast<int64_t>(S - 1) * rows_all + row) * 16 + n] = h;
     if (!FIRST && p.last_state) p.last_state[i] = h;
+    if (!FIRST && p.dt_sum && n == 0) p.dt_sum[row] = dts;
 }
 
 // ---- host side --------------------------------------------------------------

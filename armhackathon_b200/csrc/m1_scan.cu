@@ -521,6 +521,43 @@ cudaError_t m1_bidir_states_launch(const M1Params& fwd, const M1Params& bwd, int
 }
 
 namespace {
+// Sum over the sequence of dt = softplus(delta + bias) per row, one warp per
+// row (the segment-summary fallback where the lane kernel does not apply).
+__global__ void m1_dt_sum_kernel(M1Params p, float* out) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= p.batch * p.dim) return;
+    const float bias = p.delta_bias ? p.delta_bias[row % p.dim] : 0.f;
+    const float* d = p.delta + row * p.len;
+    float s = 0.f;
+    for (int64_t t = lane; t < p.len; t += 32) {
+        float v = d[t] + bias;
+        if (p.delta_softplus) v = softplus_f(v);
+        s += v;
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) out[row] = s;
+}
+}  // namespace
+
+cudaError_t m1_segment_summary_launch(const M1Params& fwd, const M1Params& bwd, int backend,
+                                      cudaStream_t stream) {
+    M1Params f = fwd, r = bwd;
+    f.out = r.out = nullptr;
+    f.z = r.z = nullptr;
+    f.d_skip = r.d_skip = nullptr;
+    r.dt_sum = nullptr;
+    if (const int S = bidir_shared_segments(f, backend)) return m1_lane_bidir_launch(f, r, S, stream);
+    f.dt_sum = nullptr;
+    cudaError_t e = m1_bidir_states_launch(f, r, backend, stream);
+    if (e != cudaSuccess) return e;
+    const int64_t rows = fwd.batch * fwd.dim;
+    m1_dt_sum_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(fwd, fwd.dt_sum);
+    note_launch();
+    return cudaGetLastError();
+}
+
+namespace {
 __global__ void m1_add_kernel(float* __restrict__ out, const float* __restrict__ other, int64_t n) {
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x)

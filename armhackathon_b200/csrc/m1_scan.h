@@ -37,6 +37,9 @@ struct M1Params {
     int out_acc = 0;
     // Lane kernel only: segment count to use (0: chosen from the shape).
     int segments = 0;
+    // Final-state forms only: sum over the sequence of dt per (batch,
+    // channel) row, written when non-null (a segment summary).
+    float* dt_sum = nullptr;
 };
 
 bool m1_pointers_aligned16(const M1Params& p);
@@ -68,6 +71,9 @@ int m1_lane_status_and_clear();
 // Final states of both traversals (no outputs); each from its own h0.
 cudaError_t m1_bidir_states_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                                    cudaStream_t stream);
+// Both final states and the per-row sum of dt (fwd.dt_sum), from zero.
+cudaError_t m1_segment_summary_launch(const M1Params& fwd, const M1Params& bwd, int backend,
+                                      cudaStream_t stream);
 // Bidirectional scan summed into fwd.out (bwd.out unused).
 cudaError_t m1_bidir_sum_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                                 cudaStream_t stream);

@@ -253,6 +253,32 @@ def selective_scan_bidirectional_final_states(u, delta, A, B, C, delta_bias=None
                             bool(delta_softplus))
 
 
+def selective_scan_segment_summary(u, delta, A, B, C, delta_bias=None, delta_softplus=False):
+    """(h_fwd, h_bwd, dt_sum): the states after the forward and the reverse
+    traversal from zero and the per-row sum of dt over the sequence, on CUDA
+    tensors -- what a segment of a sequence split over devices contributes
+    to the others (one shared pass where the lane kernel applies)."""
+    if u.device.type != "cuda":
+        raise ValueError("selective_scan_segment_summary needs CUDA tensors")
+    batch, dim, length = u.shape
+    state = A.shape[1]
+    dev = u.device
+    B = _bc4(B, batch, state, length)
+    C = _bc4(C, batch, state, length)
+    u, delta, A, B, C = (_prep(t, dev) for t in (u, delta, A, B, C))
+    db = None if delta_bias is None else _prep(delta_bias, dev)
+    hf = u.new_empty((batch, dim, state))
+    hb = u.new_empty((batch, dim, state))
+    sdt = u.new_empty((batch, dim))
+    dims = _ffi.ArmScanDims(batch, dim, length, state, B.shape[1] if B.dim() == 4 else 1)
+    with _on_device(u):
+        _ffi.segment_summary_raw(dims, u.data_ptr(), delta.data_ptr(), A.data_ptr(), B.data_ptr(),
+                                 C.data_ptr(), _ptr(db), delta_softplus, "auto", hf.data_ptr(),
+                                 hb.data_ptr(), sdt.data_ptr(), stream=_stream(u))
+    _CALLS["n"] += 1
+    return hf, hb, sdt
+
+
 def selective_scan_bidirectional(u, delta, A, B, C, D=None, z=None,
                                  delta_bias=None, delta_softplus=False):
     """Forward and backward scans of the same inputs in one call.

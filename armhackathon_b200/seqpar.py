@@ -16,8 +16,8 @@ Per call:
      into its incoming states;
   4. rank r scans its segment in both directions from those states.
 With the library's own functions on CUDA tensors and merge "sum", step 1 is
-one call (``selective_scan_bidirectional_final_states``: both directions from a
-shared first pass) and step 4 another (``selective_scan_bidirectional_sum``
+one call (``selective_scan_segment_summary``: both directions' end states and
+the dt sum from one pass over the segment) and step 4 another (``selective_scan_bidirectional_sum``
 with both incoming states).
 The fold is exact algebra, so the result equals the unsplit bidirectional
 scan up to fp32 rounding.  No rank waits on another except inside the
@@ -41,15 +41,39 @@ def _segment_dt_sum(delta, delta_bias, delta_softplus):
 def fold_carries(h_ends, dt_sums, A, rank, reverse):
     """Incoming state of segment ``rank`` from the other segments' summaries.
 
-    h_ends[j] (B, D, N): segment j's state after its traversal from zero;
-    dt_sums[j] (B, D); A (D, N).  Forward folds segments 0..rank-1 in order,
-    reverse folds segments W-1..rank+1."""
-    order = range(rank) if not reverse else range(len(h_ends) - 1, rank, -1)
-    h = torch.zeros_like(h_ends[0])
-    Af = A.float()[None]
-    for j in order:
-        h = torch.exp(Af * dt_sums[j][..., None]) * h + h_ends[j]
-    return h
+    h_ends (W, B, D, N) (or a list of W tensors): each segment's state after its traversal from zero;
+    dt_sums (W, B, D); A (D, N).  Forward: h_in = sum over j < rank of
+    exp(A * sum_{j < k < rank} dt_k) * h_end(j); reverse: the same over
+    j > rank with the segments between j and rank.  Evaluated for all j at
+    once (a handful of tensor ops whatever the number of segments): the
+    decay from segment j to ``rank`` is exp(A * (C_between)), with C the
+    cumulative dt sums over the segments."""
+    if isinstance(h_ends, (list, tuple)):
+        h_ends, dt_sums = torch.stack(list(h_ends)), torch.stack(list(dt_sums))
+    W = h_ends.shape[0]
+    idx = torch.arange(W, device=h_ends.device)
+    cum = torch.cumsum(dt_sums, 0)                    # C_j = sum_{k <= j}
+    if not reverse:
+        upto = cum[rank - 1] if rank > 0 else torch.zeros_like(cum[0])
+        between = upto[None] - cum                    # sum_{j < k < rank}
+        mask = idx < rank
+    else:
+        between = cum[:-1] if W > 1 else cum[:0]      # sum_{rank < k < j} = C_{j-1} - C_rank
+        between = torch.cat([torch.zeros_like(cum[:1]), between], 0) - cum[rank][None]
+        mask = idx > rank
+    w = torch.exp(A.float()[None, None] * between.clamp_min(0)[..., None])
+    w = w * mask.view(W, *([1] * (w.dim() - 1)))
+    return (w * h_ends).sum(0)
+
+
+def segment_summary(u, delta, A, B, C, delta_bias, delta_softplus):
+    """This segment's summary, packed (B, D, 2N + 1): forward end state,
+    backward end state (both from zero) and the sum of dt, from one library
+    call that reads the segment once."""
+    from .op import selective_scan_segment_summary
+    hf, hb, sdt = selective_scan_segment_summary(u, delta, A, B, C, delta_bias=delta_bias,
+                                                 delta_softplus=delta_softplus)
+    return torch.cat([hf, hb, sdt[..., None]], dim=-1).contiguous()
 
 
 def bidirectional_scan_seqpar(u, delta, A, B, C, D=None, z=None, delta_bias=None,
@@ -79,19 +103,17 @@ def bidirectional_scan_seqpar(u, delta, A, B, C, D=None, z=None, delta_bias=None
         scan_fn, "__module__", "") == __package__ + ".op" and getattr(
         state_fn, "__module__", "") == __package__ + ".op"
     if fused:
-        from .op import selective_scan_bidirectional_final_states
-        hf, hb = selective_scan_bidirectional_final_states(u, delta, A, B, C, **skw)
+        packed = segment_summary(u, delta, A, B, C, delta_bias, delta_softplus)
     else:
         hf = state_fn(u, delta, A, B, C, **skw)
         hb = state_fn(u, delta, A, B, C, reverse=True, **skw)
-    sdt = _segment_dt_sum(delta, delta_bias, delta_softplus).to(hf.dtype)
-    packed = torch.cat([hf, hb, sdt[..., None]], dim=-1).contiguous()
+        sdt = _segment_dt_sum(delta, delta_bias, delta_softplus).to(hf.dtype)
+        packed = torch.cat([hf, hb, sdt[..., None]], dim=-1).contiguous()
     parts = [torch.empty_like(packed) for _ in range(world)]
     dist.all_gather(parts, packed, group=group)
-    N = hf.shape[-1]
-    h_f = [p[..., :N] for p in parts]
-    h_b = [p[..., N:2 * N] for p in parts]
-    sums = [p[..., 2 * N] for p in parts]
+    allp = torch.stack(parts)
+    N = (packed.shape[-1] - 1) // 2
+    h_f, h_b, sums = allp[..., :N], allp[..., N:2 * N], allp[..., 2 * N]
     kw = dict(D=D, z=z, **skw)
     h_in_f = fold_carries(h_f, sums, A, rank, False) if rank > 0 else None
     h_in_b = fold_carries(h_b, sums, A, rank, True) if rank < world - 1 else None

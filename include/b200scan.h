@@ -336,6 +336,17 @@ int arm_scan_selective_scan_bidirectional_final_states_f32_async(
     const float* c, const float* delta_bias, int delta_softplus, int backend, float* last_fwd,
     float* last_bwd, void* stream);
 
+/* Extension (no counterpart in the reference): the summary a segment of a
+ * sequence split over devices contributes -- both traversals' final states
+ * from zero (as arm_scan_selective_scan_bidirectional_final_states_f32_async)
+ * and dt_sum (batch, dim), the sum over the segment of dt = softplus(delta +
+ * delta_bias) (or delta + delta_bias), from the same pass over the inputs
+ * where the lane kernel applies.  Device pointers, stream-ordered. */
+int arm_scan_selective_scan_segment_summary_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
+    const float* c, const float* delta_bias, int delta_softplus, int backend, float* last_fwd,
+    float* last_bwd, float* dt_sum, void* stream);
+
 /* Extension: shape of the Mamba-3 mixer whose prologue
  * arm_scan_mamba3_mixer_prologue_f32_async runs (one B/C group; rank 1 for
  * SISO).  The in_proj row is W = 2*heads*headdim + 2*rank*d_state + 3*heads

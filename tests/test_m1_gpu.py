@@ -443,8 +443,8 @@ def test_final_state_entry_equals_scan_last_state(shape, reverse):
 @pytest.mark.parametrize("world", [2, 3])
 def test_seqpar_fused_path_one_device(world, monkeypatch):
     """The sequence-parallel bidirectional scan on the library's own CUDA
-    functions (shared-pass final states, then the sum entry with incoming
-    states), every rank of a ``world``-way split run in this one process: the
+    functions (segment summaries from one pass, then the sum entry with
+    incoming states), every rank of a ``world``-way split run in this one process: the
     all_gather is replaced by the ranks' summaries computed here, so the
     result per segment must equal the unsplit bidirectional sum."""
     import torch.distributed as dist
@@ -456,13 +456,13 @@ def test_seqpar_fused_path_one_device(world, monkeypatch):
     full = a.bidirectional_scan(**t, merge="sum")
     seg = L // world
     sl = lambda v, r: v[..., r * seg:(r + 1) * seg].contiguous()  # noqa: E731
-    summaries = []
+    summaries = [seqpar.segment_summary(sl(t["u"], r), sl(t["delta"], r), t["A"], sl(t["B"], r),
+                                        sl(t["C"], r), t["delta_bias"], True)
+                 for r in range(world)]
+    # the summary's dt sum equals the torch restatement of softplus(delta + bias)
     for r in range(world):
-        hf, hb = a.selective_scan_bidirectional_final_states(
-            sl(t["u"], r), sl(t["delta"], r), t["A"], sl(t["B"], r), sl(t["C"], r),
-            delta_bias=t["delta_bias"], delta_softplus=True)
         sdt = seqpar._segment_dt_sum(sl(t["delta"], r), t["delta_bias"], True)
-        summaries.append(torch.cat([hf, hb, sdt[..., None]], dim=-1))
+        assert torch.allclose(summaries[r][..., -1], sdt, rtol=1e-5, atol=1e-6)
     rank = {"r": 0}
 
     def fake_all_gather(parts, packed, group=None):
