@@ -109,6 +109,12 @@ def _bind(lib):
     lib.arm_scan_mamba3_ss2d_f32_async.argtypes = [
         ctypes.POINTER(ArmMamba3Dims), ctypes.c_size_t, *([_VP] * 9), ctypes.c_size_t,
         _VP, _VP, _VP, _VP]
+    lib.arm_scan_mamba3_noncausal_f32_async.restype = ctypes.c_int
+    lib.arm_scan_mamba3_noncausal_f32_async.argtypes = [
+        ctypes.POINTER(ArmMamba3Dims), ctypes.c_size_t, *([_VP] * 9), ctypes.c_size_t,
+        _VP, _VP, _VP, _VP, _VP, _VP]
+    lib.arm_scan_causal_conv1d_silu_f32_async.restype = ctypes.c_int
+    lib.arm_scan_causal_conv1d_silu_f32_async.argtypes = [ctypes.c_size_t] * 4 + [_VP] * 5
     lib.arm_scan_selective_scan_final_state_f32_async.restype = ctypes.c_int
     lib.arm_scan_selective_scan_final_state_f32_async.argtypes = [
         ctypes.POINTER(ArmScanDims), *([_VP] * 6), ctypes.c_int, ctypes.c_int, _VP, _VP, _VP]
@@ -272,6 +278,24 @@ def ss2d_mamba3_raw(dims, grid_w, ptrs, n_angles, ptr_d_skip, ptr_z, ptr_out, st
         _n(ptr_d_skip), _n(ptr_z), ptr_out, _n(stream)), "arm_scan_mamba3_ss2d_f32_async")
 
 
+def noncausal_raw(dims, grid_w, ptrs, n_angles, ptr_cos, ptr_sin, ptr_d_skip, ptr_z, ptr_out,
+                  stream):
+    """Non-causal Mamba-3 aggregation (1D when grid_w == len, else a grid).
+    ``ptrs``: q, k, v, adt, dt, trap, q_bias, k_bias, angles (angles 0 when
+    cos/sin are given)."""
+    _check(load().arm_scan_mamba3_noncausal_f32_async(
+        ctypes.byref(dims), int(grid_w), *[_n(p) for p in ptrs], int(n_angles), _n(ptr_cos),
+        _n(ptr_sin), _n(ptr_d_skip), _n(ptr_z), ptr_out, _n(stream)),
+        "arm_scan_mamba3_noncausal_f32_async")
+
+
+def conv_silu_raw(batch, dim, length, kernel, ptr_x, ptr_w, ptr_bias, ptr_out, stream):
+    """Causal depthwise conv1d + bias + SiLU (device pointers)."""
+    _check(load().arm_scan_causal_conv1d_silu_f32_async(
+        batch, dim, length, kernel, ptr_x, ptr_w, _n(ptr_bias), ptr_out, _n(stream)),
+        "arm_scan_causal_conv1d_silu_f32_async")
+
+
 def final_state_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_delta_bias, softplus,
                     reverse, ptr_h0, ptr_last, stream):
     """Final state of a Mamba-1 scan without outputs (device pointers)."""
@@ -384,7 +408,8 @@ def exported_symbols():
             "arm_scan_selective_scan_bidirectional_sum_f32_async",
             "arm_scan_selective_scan_bidirectional_final_states_f32_async",
             "arm_scan_set_kernel_override", "arm_scan_mamba3_mimo_x_tc_async",
-            "arm_scan_selective_scan_segment_summary_f32_async"]
+            "arm_scan_selective_scan_segment_summary_f32_async",
+            "arm_scan_mamba3_noncausal_f32_async", "arm_scan_causal_conv1d_silu_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

@@ -14,7 +14,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libb200scan.so"
-SOURCES = ["abi.cu", "m1_scan.cu", "m1_tile.cu", "m1_lane.cu", "m1_decode.cu", "m3_scan.cu", "m3_chunk.cu", "m3_angles.cu", "m3_tc.cu", "m3_mixer.cu"]
+SOURCES = ["abi.cu", "m1_scan.cu", "m1_tile.cu", "m1_lane.cu", "m1_decode.cu", "m3_scan.cu", "m3_chunk.cu", "m3_angles.cu", "m3_tc.cu", "m3_mixer.cu", "m3_noncausal.cu", "m1_conv.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
          "--expt-relaxed-constexpr", "-diag-suppress", "128"]

@@ -698,6 +698,21 @@ int arm_scan_selective_scan_segment_summary_f32_async(
     return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "segment summary launch");
 }
 
+int arm_scan_causal_conv1d_silu_f32_async(size_t batch, size_t dim, size_t len, size_t kernel,
+                                          const float* x, const float* weight, const float* bias,
+                                          float* out, void* stream) {
+    if (!x || !weight || !out) return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    if (!batch || !dim || !len || kernel < 1 || kernel > 8)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "zero dimension or kernel (%zu) outside [1, 8]", kernel);
+    size_t n = 0;
+    if (!mul3(batch, dim, len, &n) || n > (SIZE_MAX >> 3) / 4)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "element counts overflow");
+    cudaError_t e = m1_conv_silu_launch(x, weight, bias, out, static_cast<int64_t>(batch),
+                                        static_cast<int64_t>(dim), static_cast<int64_t>(len),
+                                        static_cast<int>(kernel), static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "causal conv1d launch");
+}
+
 int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const float* k,
                              const float* v, const float* adt, const float* dt, const float* trap,
                              const float* q_bias, const float* k_bias, const float* cos,
@@ -999,23 +1014,36 @@ int arm_scan_mamba3_angles_f32_async(const ArmMamba3Dims* dims, const float* ang
     return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "angle pre-pass launch");
 }
 
-int arm_scan_mamba3_ss2d_f32_async(const ArmMamba3Dims* dims, size_t grid_w, const float* q,
-                                   const float* k, const float* v, const float* adt,
-                                   const float* dt, const float* trap, const float* q_bias,
-                                   const float* k_bias, const float* angles, size_t n_angles,
-                                   const float* d_skip, const float* z, float* out, void* stream) {
-    const void* req[] = {dims, q, k, v, adt, dt, trap, q_bias, k_bias, angles, out};
+// Traversals of a token grid (len / grid_w rows of grid_w tokens, row-major)
+// summed into out (batch, len, heads, dv): the row-major ordering and, with
+// both_orders, the column-major one, each forward and reverse, the angle
+// pre-pass per ordering (reading the grid in place); with noncausal the
+// diagonal term is subtracted once per ordering.  angles (n_angles > 0) or,
+// for a single row-major ordering, cos / sin.
+static int m3_grid_sum(const ArmMamba3Dims* dims, size_t grid_w, bool both_orders, bool noncausal,
+                       const float* q, const float* k, const float* v, const float* adt,
+                       const float* dt, const float* trap, const float* q_bias,
+                       const float* k_bias, const float* angles, size_t n_angles,
+                       const float* cos_in, const float* sin_in, const float* d_skip,
+                       const float* z, float* out, void* stream) {
+    const void* req[] = {dims, q, k, v, adt, dt, trap, q_bias, k_bias, out};
     bool mimo = false;
-    int rc = m3_check_ptrs(req, 11, nullptr, nullptr, nullptr, nullptr, nullptr, &mimo);
+    int rc = m3_check_ptrs(req, 10, nullptr, nullptr, nullptr, nullptr, nullptr, &mimo);
     if (rc) return rc;
     M3Counts cnt;
     if ((rc = m3_validate(dims, false, nullptr, nullptr, &cnt))) return rc;
-    if (dims->rank != 1) return fail(ARM_SCAN_ERR_INVALID_DIMS, "the SS2D entry is SISO (rank 1)");
+    if (dims->rank != 1) return fail(ARM_SCAN_ERR_INVALID_DIMS, "the grid entries are SISO (rank 1)");
     if (!grid_w || dims->len % grid_w)
         return fail(ARM_SCAN_ERR_INVALID_DIMS, "len (%zu) must be a multiple of grid_w (%zu)",
                     dims->len, grid_w);
-    if (!n_angles || n_angles > dims->dqk / 2)
-        return fail(ARM_SCAN_ERR_INVALID_DIMS, "n_angles (%zu) must be in [1, dqk/2]", n_angles);
+    const bool trig_given = cos_in && sin_in;
+    if (!trig_given) {
+        if (!angles) return fail(ARM_SCAN_ERR_NULL_POINTER, "angles (or cos and sin) are required");
+        if (!n_angles || n_angles > dims->dqk / 2)
+            return fail(ARM_SCAN_ERR_INVALID_DIMS, "n_angles (%zu) must be in [1, dqk/2]", n_angles);
+    } else if (both_orders) {
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "cos/sin serve one ordering; pass raw angles for 2D");
+    }
     if (dims->batch * dims->heads > 65535)
         return fail(ARM_SCAN_ERR_INVALID_DIMS, "batch*heads above 65535");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1034,26 +1062,34 @@ int arm_scan_mamba3_ss2d_f32_async(const ArmMamba3Dims* dims, size_t grid_w, con
     base.out_acc = 1;
     if (!m3_chunk_applicable(base))
         return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE,
-                    "the SS2D entry covers dv <= 128, dqk <= 128 with 16-byte aligned v, z, out");
+                    "the grid entries cover dv <= 128, dqk <= 128 with 16-byte aligned v, z, out");
+    const int orders = both_orders ? 2 : 1;
     const size_t cs = cnt.blhr;  // floats of one cos (or sin) array
-    const size_t ws_angle = arm_scan_mamba3_angles_workspace_bytes(dims, n_angles);
+    const size_t ws_angle = trig_given ? 0 : arm_scan_mamba3_angles_workspace_bytes(dims, n_angles);
     cudaMemPool_t pool = nullptr;
     cudaError_t e = device_workspace_pool(&pool);
     if (e != cudaSuccess) return cuda_fail(e, "workspace pool");
     void* raw = nullptr;
-    e = cudaMallocFromPoolAsync(&raw, 4 * cs * sizeof(float) + ws_angle + 256, pool, s);
+    const size_t trig_floats = trig_given ? 0 : 2 * orders * cs;
+    e = cudaMallocFromPoolAsync(&raw, trig_floats * sizeof(float) + ws_angle + 256, pool, s);
     if (e != cudaSuccess) return cuda_fail(e, "workspace");
     float* trig = static_cast<float*>(raw);  // [ordering][cos, sin]
-    float* angle_ws = trig + 4 * cs;
+    float* angle_ws = trig + trig_floats;
     e = cudaMemsetAsync(out, 0, cnt.blhv * sizeof(float), s);
-    for (int col = 0; col < 2 && e == cudaSuccess; ++col) {
-        float* cosv = trig + (2 * col) * cs;
-        float* sinv = cosv + cs;
-        AngleParams a{angles, dt, cosv, sinv, static_cast<int64_t>(dims->batch),
-                      static_cast<int64_t>(dims->heads), static_cast<int64_t>(dims->len),
-                      static_cast<int64_t>(n_angles), static_cast<int64_t>(dims->dqk / 2),
-                      static_cast<int64_t>(grid_w), col};
-        e = angle_launch(a, angle_ws, s);
+    for (int col = 0; col < orders && e == cudaSuccess; ++col) {
+        const float* cosv = cos_in;
+        const float* sinv = sin_in;
+        if (!trig_given) {
+            float* c = trig + (2 * col) * cs;
+            float* sn = c + cs;
+            AngleParams a{angles, dt, c, sn, static_cast<int64_t>(dims->batch),
+                          static_cast<int64_t>(dims->heads), static_cast<int64_t>(dims->len),
+                          static_cast<int64_t>(n_angles), static_cast<int64_t>(dims->dqk / 2),
+                          static_cast<int64_t>(grid_w), col};
+            e = angle_launch(a, angle_ws, s);
+            cosv = c;
+            sinv = sn;
+        }
         for (int rev = 0; rev < 2 && e == cudaSuccess; ++rev) {
             M3Params m = base;
             m.cos = cosv;
@@ -1063,9 +1099,34 @@ int arm_scan_mamba3_ss2d_f32_async(const ArmMamba3Dims* dims, size_t grid_w, con
             e = m3_chunk_launch(m, s);
         }
     }
+    if (e == cudaSuccess && noncausal) e = m3_diag_sub_launch(base, orders, s);
     const cudaError_t ef = cudaFreeAsync(raw, s);
     if (e == cudaSuccess) e = ef;
-    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "mamba3 ss2d launch");
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "mamba3 grid traversals launch");
+}
+
+int arm_scan_mamba3_ss2d_f32_async(const ArmMamba3Dims* dims, size_t grid_w, const float* q,
+                                   const float* k, const float* v, const float* adt,
+                                   const float* dt, const float* trap, const float* q_bias,
+                                   const float* k_bias, const float* angles, size_t n_angles,
+                                   const float* d_skip, const float* z, float* out, void* stream) {
+    if (!angles) return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    return m3_grid_sum(dims, grid_w, true, false, q, k, v, adt, dt, trap, q_bias, k_bias, angles,
+                       n_angles, nullptr, nullptr, d_skip, z, out, stream);
+}
+
+int arm_scan_mamba3_noncausal_f32_async(const ArmMamba3Dims* dims, size_t grid_w, const float* q,
+                                        const float* k, const float* v, const float* adt,
+                                        const float* dt, const float* trap, const float* q_bias,
+                                        const float* k_bias, const float* angles, size_t n_angles,
+                                        const float* cos, const float* sin, const float* d_skip,
+                                        const float* z, float* out, void* stream) {
+    if ((cos == nullptr) != (sin == nullptr))
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "cos and sin must be given together");
+    const bool two_d = dims && grid_w != 0 && grid_w != dims->len;
+    return m3_grid_sum(dims, grid_w ? grid_w : (dims ? dims->len : 0), two_d, true, q, k, v, adt, dt,
+                       trap, q_bias, k_bias, cos ? nullptr : angles, n_angles, cos, sin, d_skip, z,
+                       out, stream);
 }
 
 int arm_scan_mamba3_angles_f32_noalloc(const ArmMamba3Dims* dims, const float* angles,

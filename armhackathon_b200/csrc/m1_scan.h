@@ -77,6 +77,10 @@ cudaError_t m1_segment_summary_launch(const M1Params& fwd, const M1Params& bwd, 
 // Bidirectional scan summed into fwd.out (bwd.out unused).
 cudaError_t m1_bidir_sum_launch(const M1Params& fwd, const M1Params& bwd, int backend,
                                 cudaStream_t stream);
+// Causal depthwise conv1d (kernel K, zero history) + bias + SiLU over
+// (batch, dim, len) rows, weights (dim, K) (m1_conv.cu).
+cudaError_t m1_conv_silu_launch(const float* x, const float* w, const float* bias, float* out,
+                                int64_t batch, int64_t dim, int64_t len, int K, cudaStream_t stream);
 // Segments of a time-split Mamba-1 scan (1: no split) and its launcher.
 int m1_timesplit_segments(const M1Params& p);
 cudaError_t m1_timesplit_launch(const M1Params& p, int segments, cudaStream_t stream);

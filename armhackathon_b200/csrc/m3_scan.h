@@ -68,6 +68,10 @@ int m3_tc_status_and_clear();
 // Per-rank MIMO on the tensor cores (x_per_rank layouts; q = C, k = B):
 // shape test and launcher (RoPE pre-pass from raw fp32 angles, then the scan).
 bool m3_tc_xr_applicable(const M3Params& p);
+// out -= count * (D + gamma_t (q_t . k_t)) v_t [* silu(z_t)] per (b, t, h):
+// the diagonal correction of the non-causal aggregation (m3_noncausal.cu);
+// q, k (b, len, dqk) unrotated, out / v / z (b, len, h, dv).
+cudaError_t m3_diag_sub_launch(const M3Params& p, int count, cudaStream_t stream);
 cudaError_t m3_tc_launch_xr(const M3Params& p, const float* angles, int64_t n_angles, int angles_shared,
                             cudaStream_t stream);  // 1 if a bounded wait expired since the last call
 // true if p (with angles set) is a shape the extension entry covers

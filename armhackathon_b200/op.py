@@ -24,6 +24,7 @@ from typing import Optional, Tuple
 import torch
 
 from . import _ffi
+from .layout import m1_layout
 
 _CALLS = {"n": 0}
 
@@ -113,11 +114,13 @@ def selective_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None,
     it equals flipping u/delta/B/C/z in time, scanning forward and flipping
     the result; ``last_state`` is then the state after consuming t = 0.
     """
-    batch, dim, length = u.shape
-    state = A.shape[1]
+    lay = m1_layout(u.shape, delta.shape, A.shape, B.shape, C.shape,
+                    None if D is None else D.shape, None if z is None else z.shape,
+                    None if delta_bias is None else delta_bias.shape,
+                    None if initial_state is None else initial_state.shape)
     dev = u.device
-    B = _bc4(B, batch, state, length)
-    C = _bc4(C, batch, state, length)
+    B = B.reshape(lay.bc_shape)
+    C = C.reshape(lay.bc_shape)
     opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
     out, last_state = _selective_scan_op(
         _prep(u, dev), _prep(delta, dev), _prep(A, dev), _prep(B, dev), _prep(C, dev),
@@ -277,6 +280,24 @@ def selective_scan_segment_summary(u, delta, A, B, C, delta_bias=None, delta_sof
                                  hb.data_ptr(), sdt.data_ptr(), stream=_stream(u))
     _CALLS["n"] += 1
     return hf, hb, sdt
+
+
+def causal_conv1d_silu(x, weight, bias=None):
+    """silu(causal depthwise conv1d(x) + bias) over (batch, dim, len) CUDA
+    rows; weight (dim, kernel) or (dim, 1, kernel) as nn.Conv1d stores it.
+    One kernel pass (the Mamba-1 mixer's input prologue)."""
+    if x.device.type != "cuda" or x.dim() != 3:
+        raise ValueError("causal_conv1d_silu takes a (batch, dim, len) CUDA tensor")
+    batch, dim, length = x.shape
+    w = weight.reshape(dim, -1)
+    dev = x.device
+    xs, ws = _prep(x, dev), _prep(w, dev)
+    bs = None if bias is None else _prep(bias, dev)
+    out = torch.empty_like(xs)
+    with _on_device(xs):
+        _ffi.conv_silu_raw(batch, dim, length, ws.shape[1], xs.data_ptr(), ws.data_ptr(),
+                           _ptr(bs), out.data_ptr(), _stream(xs))
+    return out
 
 
 def selective_scan_bidirectional(u, delta, A, B, C, D=None, z=None,

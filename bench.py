@@ -669,6 +669,12 @@ def main():
         run_reference(args)
         return
 
+    # libraries may print banners to stdout (NCCL's version line); keep
+    # stdout for the one JSON line: everything else goes to stderr until then
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+
     import torch
     import torch.distributed as dist
     import armhackathon_b200 as arm
@@ -792,7 +798,8 @@ def main():
             line["configs"] = config_suite(args, dev, peak, clocks)
         if seqpar:
             line["configs"] = {"cfg4b_seqpar": seqpar}
-        print(json.dumps(line), flush=True)
+        sys.stdout.flush()
+        os.write(json_fd, (json.dumps(line) + "\n").encode())
     if world > 1:
         dist.destroy_process_group()
 

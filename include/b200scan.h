@@ -254,6 +254,22 @@ int arm_scan_mamba3_ss2d_f32_async(const ArmMamba3Dims* dims, size_t grid_w, con
                                    const float* k_bias, const float* angles, size_t n_angles,
                                    const float* d_skip, const float* z, float* out, void* stream);
 
+/* Extension: the non-causal Mamba-3 aggregation (every token sees every
+ * other), forward + reverse - diagonal, in one call (the reference composes
+ * it in Python, python/arm_scan/mamba3_noncausal.py:89-98 for 1D and
+ * :178-218 for a grid).  grid_w == 0 or len: one sequence (1D), with raw
+ * angles or with precomputed cos / sin (batch, len, heads, dqk/2); otherwise
+ * a token grid of len / grid_w rows, row-major and column-major orderings
+ * summed, raw angles only.  Layouts as arm_scan_mamba3_ss2d_f32_async; out
+ * (batch, len, heads, dv).  The scans sum into out in place and one kernel
+ * subtracts the doubly counted diagonal term.  fp32 chunk kernels. */
+int arm_scan_mamba3_noncausal_f32_async(const ArmMamba3Dims* dims, size_t grid_w, const float* q,
+                                        const float* k, const float* v, const float* adt,
+                                        const float* dt, const float* trap, const float* q_bias,
+                                        const float* k_bias, const float* angles, size_t n_angles,
+                                        const float* cos, const float* sin, const float* d_skip,
+                                        const float* z, float* out, void* stream);
+
 /* Extension (no counterpart in the reference): the final state of
  * arm_scan_selective_scan_f32_async's recurrence without computing the
  * outputs (D, z and out play no part): the first step of a sequence-parallel
@@ -346,6 +362,16 @@ int arm_scan_selective_scan_segment_summary_f32_async(
     const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
     const float* c, const float* delta_bias, int delta_softplus, int backend, float* last_fwd,
     float* last_bwd, float* dt_sum, void* stream);
+
+/* Extension (no counterpart in the reference, whose HF patch leaves it to
+ * torch, python/arm_scan/patch.py:57-116): the Mamba-1 mixer's input
+ * prologue, causal depthwise conv1d + bias + SiLU, in one pass:
+ *   out[b, d, t] = silu(bias[d] + sum_{j < kernel} weight[d, j] x[b, d, t - kernel + 1 + j])
+ * with zeros before t = 0.  x, out (batch, dim, len); weight (dim, kernel);
+ * bias (dim) nullable; kernel in [1, 8].  Device pointers, stream-ordered. */
+int arm_scan_causal_conv1d_silu_f32_async(size_t batch, size_t dim, size_t len, size_t kernel,
+                                          const float* x, const float* weight, const float* bias,
+                                          float* out, void* stream);
 
 /* Extension: shape of the Mamba-3 mixer whose prologue
  * arm_scan_mamba3_mixer_prologue_f32_async runs (one B/C group; rank 1 for

@@ -131,6 +131,29 @@ def test_ss2d_mamba3_directions_vs_oracle():
         assert rel_err(got.cpu().numpy(), want.numpy()) <= REL_TOL
     nc_rows, nc_cols = a.ss2d_noncausal_mamba3(**{k: v.cuda() for k, v in x.items()}, merge="none")
     assert nc_rows.shape == (b, H, W, h, dv) and nc_cols.shape == (b, H, W, h, dv)
+    # the one-call grid form (both orderings summed in place, diagonal
+    # subtracted per ordering) against the per-ordering calls
+    nc_sum = a.ss2d_noncausal_mamba3(**{k: v.cuda() for k, v in x.items()}, merge="sum")
+    assert rel_err(nc_sum.cpu().numpy(), (nc_rows + nc_cols).cpu().numpy()) <= REL_TOL
+    # and the row ordering against the dense mask on the row-major sequence
+    rv = {k: grid_to_views_time_major(x[k])[:b] for k in ("q", "k", "v", "angles", "z")}
+    rv.update({k: grid_to_views(x[k])[:b] for k in ("adt", "dt", "trap")})
+    dense = a.noncausal_scan_dense(**{k: v.double() for k, v in rv.items()}, q_bias=x["q_bias"].double(),
+                                   k_bias=x["k_bias"].double(), D=x["D"].double())
+    assert rel_err(nc_rows.reshape(dense.shape).cpu().numpy(), dense.numpy()) <= REL_TOL
+
+
+def test_noncausal_with_cos_sin():
+    """The 1D non-causal call given precomputed cos / sin equals the one
+    given raw angles."""
+    x = {k: v.cuda() for k, v in random_siso(2, 130, 3, 32, 64, 16, seed=12).items()}
+    a = arm()
+    cos, sin = a.angles_to_cos_sin(x["angles"], x["dt"], 32)
+    y1 = a.noncausal_scan(**x)
+    xc = dict(x)
+    xc.pop("angles")
+    y2 = a.noncausal_scan(**xc, cos=cos, sin=sin)
+    assert rel_err(y2.cpu().numpy(), y1.cpu().numpy()) <= REL_TOL
 
 
 def test_mimo_random_state_and_reverse():
