@@ -25,13 +25,15 @@ __all__ = [
     "ss2d_noncausal_mamba3", "angles_to_cos_sin", "patch", "unpatch", "stats", "kernel_calls",
     "selective_state_update", "selective_scan_final_state", "mamba3_mixer_prologue",
     "selective_scan_bidirectional_sum", "selective_scan_bidirectional_final_states",
-    "mamba3_mixer_scan", "mamba3_mimo_x_scan",
+    "mamba3_mixer_scan", "mamba3_mimo_x_scan", "selective_scan_segment_summary",
+    "causal_conv1d_silu",
 ]
 
 _LAZY = {
     "selective_scan": ".op", "selective_scan_bidirectional": ".op", "kernel_calls": ".op",
     "selective_state_update": ".op", "selective_scan_final_state": ".op",
     "selective_scan_bidirectional_sum": ".op",
+    "selective_scan_segment_summary": ".op", "causal_conv1d_silu": ".op",
     "selective_scan_bidirectional_final_states": ".op",
     "bidirectional_scan": ".bidirectional",
     "ss2d_scan": ".ss2d", "use_arm_scan": ".ss2d",

@@ -1,220 +1,252 @@
-"""Route Hugging Face transformers' Mamba-1 mixer through the GPU scan.
+"""Run Hugging Face transformers' Mamba-1 mixer on this library's kernels.
 
-Same surface and behaviour as the reference's python/arm_scan/patch.py:
-``patch()`` swaps ``MambaMixer.slow_forward`` (the path HF takes whenever the
-``mamba_ssm`` CUDA kernels are not installed, on CPU and on GPU alike) for a
-transcription of it whose recurrence runs through ``selective_scan`` with
-softplus fused into the kernel; ``unpatch()`` restores the original;
-``stats()`` reports engagement.  Projections, conv, gating, weights and cache
-seeding are left exactly as upstream does them.
+The public surface is the reference's (python/arm_scan/patch.py): ``patch()``,
+``unpatch()``, ``stats()``.  The design is this module's own:
 
-slow_forward's signature changed across transformers releases, so the API is
-detected at patch time from the original's parameters:
-  "cache_position":     slow_forward(self, x, cache_params, cache_position,
-                        attention_mask); prefill iff cache_position spans the
-                        conv kernel; caches via update_conv_state(layer, state,
-                        cache_position) and ssm_states[layer].copy_()
-  "has_previous_state": slow_forward(self, x, cache_params, attention_mask);
-                        prefill iff not cache_params.has_previous_state(layer);
-                        caches via update_conv_state(state, layer) and
-                        update_recurrent_state(state, layer)
-For releases without slow_forward but with a module-level
-``mamba_selective_scan`` that function is wrapped instead.
+* One ``_Router`` object owns the installation: it records every attribute it
+  replaces (owner, name, original) so that ``unpatch()`` restores exactly
+  those, and counts what each call did.
+* The replaced ``MambaMixer.slow_forward`` (HF's path whenever the
+  ``mamba_ssm`` CUDA kernels are not installed) sorts each call into one of
+  three routes -- ``prefill`` (no cache, or the cached prefill of
+  ``generate()``), ``decode`` (one token with a warm cache, "has_previous_state"
+  cache API) or ``original`` (training, autograd, CPU decode, unknown API) --
+  and runs the first two on the GPU.
+* The prefill route runs the mixer's middle section on library kernels:
+  causal depthwise conv1d + bias + SiLU in one kernel
+  (``causal_conv1d_silu``), then the scan with ``dt_proj``'s bias and the
+  softplus applied inside the scan kernel (``delta_bias``,
+  ``delta_softplus``), so the dt_proj output is never biased or activated in
+  torch.  in_proj, x_proj, dt_proj's matmul and out_proj stay torch GEMMs.
+* The decode route is one ``selective_state_update`` per layer and token.
 
-The kernel handles cache-less forwards and the cached prefill of
-``generate()`` (zero initial state).  With the "has_previous_state" API the
-decode steps of ``generate()`` also run on the GPU (one
-``selective_state_update`` per layer and token; an extension: the reference
-falls back for them).  Other decode steps, mamba.py training mode and any
-call that needs autograd (the op has no backward) fall back to the original.
+Two cache APIs of transformers are recognised from slow_forward's signature:
+"cache_position" (prefill iff cache_position spans the conv kernel; caches
+through update_conv_state(layer, state, cache_position) and
+ssm_states[layer]) and "has_previous_state" (prefill iff the cache has no
+state for the layer; update_conv_state(state, layer) and
+update_recurrent_state(state, layer)).  Releases without slow_forward but
+with a module-level ``mamba_selective_scan`` get that function replaced.
 """
 
 import inspect
+from dataclasses import dataclass
 
 import torch
 import torch.nn.functional as F
 
-from .op import kernel_calls, selective_scan, selective_state_update
-
-_STATE = {"orig": None, "api": None, "arg_names": (), "target": None,
-          "fast_calls": 0, "fallback_calls": 0, "decode_calls": 0}
+from .op import causal_conv1d_silu, kernel_calls, selective_scan, selective_state_update
 
 
-def _detect_api(orig):
-    names = list(inspect.signature(orig).parameters)
-    if "cache_position" in names:
+@dataclass
+class _Counters:
+    fast_calls: int = 0       # prefill route (and the scan-function replacement)
+    decode_calls: int = 0     # decode route
+    fallback_calls: int = 0   # original implementation
+
+
+class _Router:
+    def __init__(self):
+        self.saved = []        # (owner, name, original)
+        self.api = None
+        self.counters = _Counters()
+
+    @property
+    def active(self):
+        return bool(self.saved)
+
+    def replace(self, owner, name, new):
+        self.saved.append((owner, name, getattr(owner, name)))
+        setattr(owner, name, new)
+
+    def restore(self):
+        for owner, name, orig in reversed(self.saved):
+            setattr(owner, name, orig)
+        self.saved.clear()
+        self.api = None
+
+
+_ROUTER = _Router()
+
+
+def _cache_api(fn):
+    params = inspect.signature(fn).parameters
+    if "cache_position" in params:
         return "cache_position"
-    if "cache_params" in names:
+    if "cache_params" in params:
         return "has_previous_state"
     return None
 
 
-def _needs_grad(module, x):
-    return torch.is_grad_enabled() and (
-        x.requires_grad or any(p.requires_grad for p in module.parameters()))
+def _grad_needed(module, x):
+    if not torch.is_grad_enabled():
+        return False
+    return x.requires_grad or any(p.requires_grad for p in module.parameters())
 
 
-def _mixer_scan_forward(self, input_states, cache_params, cache_position, attention_mask, api):
-    """MambaMixer.slow_forward's no-cache / cached-prefill branch with the
-    recurrence on the GPU kernel."""
-    seq_len = input_states.shape[1]
-    dtype = input_states.dtype
-    projected_states = self.in_proj(input_states).transpose(1, 2)
-    hidden_states, gate = projected_states.chunk(2, dim=1)
+def _route(mixer, x, cache_params, cache_position, api):
+    if mixer.training or _grad_needed(mixer, x):
+        return "original"
+    if cache_params is None:
+        return "prefill" if x.is_cuda else "original"
+    if api == "cache_position":
+        warm = cache_position is None or cache_position.shape[0] != mixer.conv_kernel_size
+    else:
+        warm = cache_params.has_previous_state(mixer.layer_idx)
+    if not warm:
+        return "prefill" if x.is_cuda else "original"
+    if api == "has_previous_state" and x.shape[1] == 1 and x.is_cuda:
+        return "decode"
+    return "original"
+
+
+def _conv_silu(mixer, hidden):
+    """The mixer's conv1d + activation: one library kernel when the
+    activation is SiLU (Mamba's), else torch."""
+    if isinstance(mixer.act, torch.nn.SiLU) or getattr(mixer, "activation", None) == "silu":
+        return causal_conv1d_silu(hidden, mixer.conv1d.weight,
+                                  mixer.conv1d.bias if mixer.use_conv_bias else None)
+    return mixer.act(mixer.conv1d(hidden)[..., :hidden.shape[-1]])
+
+
+def _prefill(mixer, x, cache_params, cache_position, attention_mask, api):
+    seq_len = x.shape[1]
+    out_dtype = x.dtype
+    hidden, gate = mixer.in_proj(x).transpose(1, 2).chunk(2, dim=1)
     if attention_mask is not None:
-        hidden_states = hidden_states * attention_mask.unsqueeze(1)
+        hidden = hidden * attention_mask.unsqueeze(1)
     if cache_params is not None:
-        conv_state = F.pad(hidden_states, (self.conv_kernel_size - hidden_states.shape[-1], 0))
+        # the conv cache holds the last kernel_size inputs (zero-padded on the left)
+        window = F.pad(hidden, (mixer.conv_kernel_size - seq_len, 0))
         if api == "cache_position":
-            cache_params.update_conv_state(self.layer_idx, conv_state, cache_position)
+            cache_params.update_conv_state(mixer.layer_idx, window, cache_position)
         else:
-            cache_params.update_conv_state(conv_state, self.layer_idx)
-    hidden_states = self.act(self.conv1d(hidden_states)[..., :seq_len])
+            cache_params.update_conv_state(window, mixer.layer_idx)
+    u = _conv_silu(mixer, hidden.contiguous())
     if attention_mask is not None:
-        hidden_states = hidden_states * attention_mask.unsqueeze(1)
-    ssm_parameters = self.x_proj(hidden_states.transpose(1, 2))
-    time_step, B, C = torch.split(
-        ssm_parameters, [self.time_step_rank, self.ssm_state_size, self.ssm_state_size], dim=-1)
-    # raw dt_proj output; softplus runs inside the kernel
-    discrete_time_step = self.dt_proj(time_step).transpose(1, 2)
-    A = -torch.exp(self.A_log.float())
-    scan_output, last_state = selective_scan(
-        hidden_states, discrete_time_step, A, B.transpose(1, 2), C.transpose(1, 2),
-        D=self.D, z=gate, delta_softplus=True, return_last_state=True)
+        u = u * attention_mask.unsqueeze(1)
+    proj = mixer.x_proj(u.transpose(1, 2))
+    ts, Bm, Cm = torch.split(proj, [mixer.time_step_rank, mixer.ssm_state_size,
+                                    mixer.ssm_state_size], dim=-1)
+    # dt_proj without its bias: the scan adds it and applies the softplus
+    dt_raw = F.linear(ts, mixer.dt_proj.weight).transpose(1, 2)
+    y, h_last = selective_scan(u, dt_raw, -torch.exp(mixer.A_log.float()), Bm.transpose(1, 2),
+                               Cm.transpose(1, 2), D=mixer.D, z=gate,
+                               delta_bias=mixer.dt_proj.bias, delta_softplus=True,
+                               return_last_state=True)
     if cache_params is not None:
         if api == "cache_position":
-            cache_params.ssm_states[self.layer_idx].copy_(last_state)
+            cache_params.ssm_states[mixer.layer_idx].copy_(h_last)
         else:
-            cache_params.update_recurrent_state(last_state.to(dtype), self.layer_idx)
-    return self.out_proj(scan_output.transpose(1, 2).to(dtype))
+            cache_params.update_recurrent_state(h_last.to(out_dtype), mixer.layer_idx)
+    return mixer.out_proj(y.transpose(1, 2).to(out_dtype))
 
 
-def _mixer_decode_forward(self, input_states, cache_params, attention_mask):
-    """MambaMixer.slow_forward's decode branch ("has_previous_state" API, one
-    token) with the state update on the GPU kernel."""
-    # shapes and mask handling exactly as the original's decode branch
-    dtype = input_states.dtype
-    projected_states = self.in_proj(input_states).transpose(1, 2)
-    hidden_states, gate = projected_states.chunk(2, dim=1)
+def _decode(mixer, x, cache_params, attention_mask):
+    """One token with a warm cache ("has_previous_state" API)."""
+    out_dtype = x.dtype
+    hidden, gate = mixer.in_proj(x).transpose(1, 2).chunk(2, dim=1)
     if attention_mask is not None:
-        hidden_states = hidden_states * attention_mask.unsqueeze(1)
-    state = cache_params.layers[self.layer_idx].recurrent_states.to(torch.float32).contiguous()
-    conv_state = cache_params.update_conv_state(hidden_states, self.layer_idx)
-    conv_state = conv_state.to(self.conv1d.weight.device)
-    hidden_states = torch.sum(conv_state * self.conv1d.weight[:, 0, :], dim=-1)
-    if self.use_conv_bias:
-        hidden_states = hidden_states + self.conv1d.bias
-    hidden_states = self.act(hidden_states).to(dtype).unsqueeze(-1)  # [batch, intermediate_size, 1]
+        hidden = hidden * attention_mask.unsqueeze(1)
+    layer = mixer.layer_idx
+    h = cache_params.layers[layer].recurrent_states.to(torch.float32).contiguous()
+    window = cache_params.update_conv_state(hidden, layer).to(mixer.conv1d.weight.device)
+    conv = (window * mixer.conv1d.weight[:, 0, :]).sum(-1)
+    if mixer.use_conv_bias:
+        conv = conv + mixer.conv1d.bias
+    u = mixer.act(conv).to(out_dtype)
     if attention_mask is not None:
-        hidden_states = hidden_states * attention_mask.unsqueeze(1)
-    hidden_states = hidden_states[:, :, -1]
-    ssm_parameters = self.x_proj(hidden_states)
-    time_step, B, C = torch.split(
-        ssm_parameters, [self.time_step_rank, self.ssm_state_size, self.ssm_state_size], dim=-1)
-    A = -torch.exp(self.A_log.float())
-    y = selective_state_update(state, hidden_states, self.dt_proj(time_step), A, B, C, D=self.D,
-                               z=gate[:, :, -1], dt_softplus=True)
-    cache_params.update_recurrent_state(state.to(dtype), self.layer_idx)
-    return self.out_proj(y.unsqueeze(1).to(dtype))
+        u = u * attention_mask[:, -1:]
+    ts, Bm, Cm = torch.split(mixer.x_proj(u), [mixer.time_step_rank, mixer.ssm_state_size,
+                                                mixer.ssm_state_size], dim=-1)
+    y = selective_state_update(h, u, mixer.dt_proj(ts), -torch.exp(mixer.A_log.float()), Bm, Cm,
+                               D=mixer.D, z=gate[:, :, -1], dt_softplus=True)
+    cache_params.update_recurrent_state(h.to(out_dtype), layer)
+    return mixer.out_proj(y.unsqueeze(1).to(out_dtype))
 
 
-def _patch_scan_fn(modeling_mamba):
-    """Releases exposing a module-level ``mamba_selective_scan`` (same
-    argument list as ``selective_scan``): wrap it, falling back to the
-    original for calls that need autograd."""
+def _install_mixer(modeling_mamba):
+    orig = modeling_mamba.MambaMixer.slow_forward
+    api = _cache_api(orig)
+    if api is None:
+        return None
+    names = tuple(inspect.signature(orig).parameters)[2:]
+    counters = _ROUTER.counters
+
+    def slow_forward(self, input_states, *args, **kwargs):
+        kw = dict(zip(names, args), **kwargs)
+        cache_params = kw.get("cache_params")
+        cache_position = kw.get("cache_position")
+        route = _route(self, input_states, cache_params, cache_position, api)
+        if route == "prefill":
+            counters.fast_calls += 1
+            return _prefill(self, input_states, cache_params, cache_position,
+                            kw.get("attention_mask"), api)
+        if route == "decode":
+            counters.decode_calls += 1
+            return _decode(self, input_states, cache_params, kw.get("attention_mask"))
+        counters.fallback_calls += 1
+        return orig(self, input_states, *args, **kwargs)
+
+    _ROUTER.replace(modeling_mamba.MambaMixer, "slow_forward", slow_forward)
+    _ROUTER.api = api
+    return f"transformers MambaMixer.slow_forward ({api} API)"
+
+
+def _install_scan_fn(modeling_mamba):
+    """Releases with a module-level ``mamba_selective_scan`` (the argument
+    list of ``selective_scan``): calls that need no autograd run here."""
     orig = modeling_mamba.mamba_selective_scan
+    counters = _ROUTER.counters
 
     def mamba_selective_scan(hidden_states, dt, A, B, C, D=None, z=None, delta_bias=None,
-                             delta_softplus=False, return_last_state=False, use_mambapy=False,
-                             use_associative_scan=False, **kwargs):
-        tensors = (hidden_states, dt, A, B, C)
-        needs_grad = torch.is_grad_enabled() and any(
-            t.requires_grad for t in (*tensors, D, z, delta_bias) if t is not None)
-        if needs_grad:
-            _STATE["fallback_calls"] += 1
+                             delta_softplus=False, return_last_state=False, **kwargs):
+        args = (hidden_states, dt, A, B, C, D, z, delta_bias)
+        if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in args):
+            counters.fallback_calls += 1
             return orig(hidden_states, dt, A, B, C, D=D, z=z, delta_bias=delta_bias,
                         delta_softplus=delta_softplus, return_last_state=return_last_state,
-                        use_mambapy=use_mambapy, use_associative_scan=use_associative_scan,
                         **kwargs)
-        _STATE["fast_calls"] += 1
+        counters.fast_calls += 1
         return selective_scan(hidden_states, dt, A, B, C, D=D, z=z, delta_bias=delta_bias,
-                              delta_softplus=delta_softplus,
-                              return_last_state=return_last_state)
+                              delta_softplus=delta_softplus, return_last_state=return_last_state)
 
-    modeling_mamba.mamba_selective_scan = mamba_selective_scan
-    _STATE.update(orig=orig, api="selective_scan_fn", target="mamba_selective_scan")
-    return ["transformers mamba_selective_scan (selective_scan_fn API)"]
+    _ROUTER.replace(modeling_mamba, "mamba_selective_scan", mamba_selective_scan)
+    _ROUTER.api = "selective_scan_fn"
+    return "transformers mamba_selective_scan (selective_scan_fn API)"
 
 
 def patch():
-    """Route HF Mamba's slow path through the GPU kernel.  Returns the list of
-    patched targets ([] if this transformers release is not recognised).
-    Idempotent."""
-    if _STATE["orig"] is not None:
-        return ["transformers MambaMixer.slow_forward (already patched)"]
+    """Send HF Mamba-1's slow path through the library.  Returns the list of
+    replaced targets ([] when this transformers release is not recognised);
+    calling it again while patched changes nothing."""
+    if _ROUTER.active:
+        return [f"already patched ({_ROUTER.api} API)"]
     from transformers.models.mamba import modeling_mamba
-    if not hasattr(modeling_mamba.MambaMixer, "slow_forward"):
-        if hasattr(modeling_mamba, "mamba_selective_scan"):
-            return _patch_scan_fn(modeling_mamba)
+    target = None
+    if hasattr(modeling_mamba.MambaMixer, "slow_forward"):
+        target = _install_mixer(modeling_mamba)
+    elif hasattr(modeling_mamba, "mamba_selective_scan"):
+        target = _install_scan_fn(modeling_mamba)
+    if target is None:
         import warnings
-        warnings.warn("patch(): this transformers release has neither MambaMixer.slow_forward "
-                      "nor mamba_selective_scan; leaving it unpatched")
+        warnings.warn("patch(): no recognised Mamba mixer entry in this transformers release; "
+                      "nothing patched")
         return []
-    orig = modeling_mamba.MambaMixer.slow_forward
-    api = _detect_api(orig)
-    if api is None:
-        import warnings
-        warnings.warn("patch(): unrecognised MambaMixer.slow_forward signature; "
-                      "leaving it unpatched")
-        return []
-    arg_names = tuple(inspect.signature(orig).parameters)[2:]
-
-    def slow_forward(self, input_states, *args, **kwargs):
-        bound = dict(zip(arg_names, args))
-        bound.update(kwargs)
-        cache_params = bound.get("cache_params")
-        cache_position = bound.get("cache_position")
-        attention_mask = bound.get("attention_mask")
-        use_mambapy = getattr(self, "use_mambapy", False)
-        if api == "cache_position":
-            is_prefill = cache_params is None or (
-                cache_position is not None and cache_position.shape[0] == self.conv_kernel_size)
-        else:
-            is_prefill = cache_params is None or not cache_params.has_previous_state(
-                self.layer_idx)
-        if (not is_prefill and api == "has_previous_state" and input_states.shape[1] == 1
-                and input_states.device.type == "cuda" and not self.training
-                and not _needs_grad(self, input_states)):
-            _STATE["decode_calls"] += 1
-            return _mixer_decode_forward(self, input_states, cache_params, attention_mask)
-        if (use_mambapy and self.training) or not is_prefill or _needs_grad(self, input_states):
-            _STATE["fallback_calls"] += 1
-            return orig(self, input_states, *args, **kwargs)
-        _STATE["fast_calls"] += 1
-        return _mixer_scan_forward(self, input_states, cache_params, cache_position,
-                                   attention_mask, api)
-
-    modeling_mamba.MambaMixer.slow_forward = slow_forward
-    _STATE.update(orig=orig, api=api, arg_names=arg_names, target="slow_forward")
-    return [f"transformers MambaMixer.slow_forward ({api} API)"]
+    return [target]
 
 
 def unpatch():
-    """Restore the original implementation.  Returns False if not patched."""
-    if _STATE["orig"] is None:
+    """Put back everything ``patch()`` replaced.  False if nothing was patched."""
+    if not _ROUTER.active:
         return False
-    from transformers.models.mamba import modeling_mamba
-    if _STATE.get("target") == "mamba_selective_scan":
-        modeling_mamba.mamba_selective_scan = _STATE["orig"]
-    else:
-        modeling_mamba.MambaMixer.slow_forward = _STATE["orig"]
-    _STATE.update(orig=None, api=None, target=None)
+    _ROUTER.restore()
     return True
 
 
 def stats():
-    """Engagement counters."""
-    return {"fast_calls": _STATE["fast_calls"], "fallback_calls": _STATE["fallback_calls"],
-            "decode_calls": _STATE["decode_calls"],
-            "kernel_calls": kernel_calls(), "patched": _STATE["orig"] is not None,
-            "api": _STATE["api"]}
+    """How calls were routed since import, and the library's kernel-call count."""
+    c = _ROUTER.counters
+    return {"fast_calls": c.fast_calls, "fallback_calls": c.fallback_calls,
+            "decode_calls": c.decode_calls, "kernel_calls": kernel_calls(),
+            "patched": _ROUTER.active, "api": _ROUTER.api}

@@ -479,3 +479,19 @@ def test_seqpar_fused_path_one_device(world, monkeypatch):
             sl(t["u"], r), sl(t["delta"], r), t["A"], sl(t["B"], r), sl(t["C"], r), D=t["D"],
             z=sl(t["z"], r), delta_bias=t["delta_bias"], delta_softplus=True)
         assert rel_err(y.cpu().numpy(), sl(full, r).cpu().numpy()) <= REL_TOL
+
+
+@pytest.mark.parametrize("shape", [(2, 48, 64, 4), (1, 7, 33, 4), (2, 16, 40, 3), (1, 5, 9, 6)])
+def test_causal_conv1d_silu_matches_torch(shape):
+    """The mixer prologue kernel (causal depthwise conv1d + bias + SiLU)
+    against torch's conv1d with padding kernel-1 sliced to the sequence:
+    vectorised (len multiple of 4, kernel <= 4) and general shapes."""
+    import torch.nn.functional as F
+    B, D, L, K = shape
+    g = torch.Generator().manual_seed(L)
+    x = torch.randn(B, D, L, generator=g).cuda()
+    w = torch.randn(D, 1, K, generator=g).cuda()
+    b = torch.randn(D, generator=g).cuda()
+    want = F.silu(F.conv1d(x, w, b, padding=K - 1, groups=D)[..., :L])
+    got = arm().causal_conv1d_silu(x, w, b)
+    assert rel_err(got.cpu().numpy(), want.cpu().numpy()) <= 1e-5
