@@ -20,7 +20,7 @@ import os
 import sys
 from pathlib import Path
 
-ABI_VERSION = 11
+ABI_VERSION = 12
 
 _LIB_NAMES = ["libb200scan.so"]
 
@@ -123,6 +123,8 @@ def _bind(lib):
         ctypes.POINTER(ArmScanDims), *([_VP] * 9), ctypes.c_int, _VP, _VP]
     lib.arm_scan_kernel_launches.restype = ctypes.c_ulonglong
     lib.arm_scan_kernel_launches.argtypes = []
+    lib.arm_scan_set_device.restype = ctypes.c_int
+    lib.arm_scan_set_device.argtypes = [_I]
     lib.arm_scan_set_kernel_override.restype = ctypes.c_int
     lib.arm_scan_set_kernel_override.argtypes = [_I, _I]
     lib.arm_scan_selective_scan_bidirectional_sum_f32_async.restype = ctypes.c_int
@@ -352,6 +354,12 @@ def segment_summary_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_delta_b
         _n(stream)), "arm_scan_selective_scan_segment_summary_f32_async")
 
 
+def set_device(ordinal):
+    """Device the synchronous host-buffer calls of this thread run on (-1:
+    the current CUDA device)."""
+    _check(load().arm_scan_set_device(int(ordinal)), "arm_scan_set_device")
+
+
 def kernel_launches():
     """GPU kernels the library has launched in this process so far."""
     return int(load().arm_scan_kernel_launches())
@@ -409,7 +417,8 @@ def exported_symbols():
             "arm_scan_selective_scan_bidirectional_final_states_f32_async",
             "arm_scan_set_kernel_override", "arm_scan_mamba3_mimo_x_tc_async",
             "arm_scan_selective_scan_segment_summary_f32_async",
-            "arm_scan_mamba3_noncausal_f32_async", "arm_scan_causal_conv1d_silu_f32_async"]
+            "arm_scan_mamba3_noncausal_f32_async", "arm_scan_causal_conv1d_silu_f32_async",
+            "arm_scan_set_device"]
 
 
 if __name__ == "__main__":  # pragma: no cover

@@ -147,6 +147,10 @@ int tensor_status_code() {
 
 // post (optional) runs after a successful synchronization and may turn the
 // result into an error (device-side status flags).
+// Device the synchronous entries stage host buffers through, per calling
+// thread (arm_scan_set_device); -1: the thread's current CUDA device.
+thread_local int g_host_device = -1;
+
 template <class Run>
 int run_sync(std::vector<Buf>& bufs, Run&& run, int (*post)() = nullptr) {
     int dev = -1;
@@ -164,6 +168,7 @@ int run_sync(std::vector<Buf>& bufs, Run&& run, int (*post)() = nullptr) {
         if (e != cudaSuccess) return cuda_fail(e, "kernel");
         return post ? post() : ARM_SCAN_OK;
     }
+    DeviceGuard pick(g_host_device);
     int cur = 0;
     cudaError_t e = cudaGetDevice(&cur);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -418,6 +423,7 @@ int m1_host_pipelined(const ArmScanDims* d, const std::vector<Buf>& bufs, int so
     constexpr int kSliced[] = {0, 1, 3, 4, 6, 8, 9, 10};
     constexpr int kShared[] = {2, 5, 7};
     const size_t nb = d->batch;
+    DeviceGuard pick(g_host_device);
     int cur = 0;
     cudaError_t e = cudaGetDevice(&cur);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -800,6 +806,15 @@ int arm_scan_selective_state_update_f32_async(const ArmScanDims* dims, float* st
 }
 
 unsigned long long arm_scan_kernel_launches(void) { return b200scan::g_kernel_launches.load(); }
+
+int arm_scan_set_device(int ordinal) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) n = 0;
+    if (ordinal < -1 || (ordinal >= 0 && ordinal >= n))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "device ordinal %d outside [-1, %d)", ordinal, n);
+    g_host_device = ordinal;
+    return ARM_SCAN_OK;
+}
 
 int arm_scan_set_kernel_override(int knob, int value) {
     if (knob < 0 || knob >= b200scan::kKnobCount)

@@ -5,15 +5,22 @@
  * kernel/arm-scan-ffi/src/lib.rs (ABI v7).  Entry points, structs, enum values
  * and return codes 0-5 keep the reference's names, argument order and meaning
  * so an existing ctypes/cgo binding only changes the library path and the
- * expected version number (v8).  v8 adds:
+ * expected version number (now 12; it was 7).  Added since v7:
  *   - device-pointer, stream-ordered variants (suffix _async) that take a
  *     cudaStream_t as `void* stream` and never synchronize;
  *   - a final-state output for the Mamba-3 SISO and MIMO scans;
  *   - return codes 6 (CUDA error) and 7 (timeout of a bounded wait);
- *   - arm_scan_last_error(), a per-thread message for the last failure.
+ *   - arm_scan_last_error(), a per-thread message for the last failure;
+ *   - arm_scan_set_device(), the device ordinal the synchronous entries use;
+ *   - extension entry points for the tensor-core Mamba-3 paths, the
+ *     per-rank MIMO form, the fused bidirectional forms, non-causal and 2D
+ *     compositions, segment summaries for sequence parallelism, decode, the
+ *     mixers' prologues and an allocation-free angle pre-pass (each
+ *     declared below with its contract).
  *
  * Memory.  The synchronous v7-shaped entry points accept either HOST pointers
- * (every buffer in host memory: inputs are copied to the current CUDA device,
+ * (every buffer in host memory: inputs are copied to the CUDA device chosen by
+ * arm_scan_set_device, by default the calling thread's current device,
  * the scan runs, outputs are copied back, and the call returns when the
  * results are in the caller's buffers -- the reference's blocking contract) or
  * DEVICE pointers (every buffer on the current device: the scan runs on the
@@ -43,7 +50,7 @@
 extern "C" {
 #endif
 
-#define ARM_SCAN_ABI_VERSION 11u
+#define ARM_SCAN_ABI_VERSION 12u
 
 /* Return codes (0-5: reference arm-scan-ffi/src/lib.rs:53-58). */
 #define ARM_SCAN_OK 0
@@ -84,7 +91,8 @@ typedef struct ArmMamba3Dims {
     size_t rank;
 } ArmMamba3Dims;
 
-/* Replaces arm_scan_abi_version, arm-scan-ffi/src/lib.rs:37-40. Returns 9. */
+/* Replaces arm_scan_abi_version, arm-scan-ffi/src/lib.rs:37-40.  Returns
+ * ARM_SCAN_ABI_VERSION (12). */
 uint32_t arm_scan_abi_version(void);
 
 /* Message describing the calling thread's most recent non-zero return. */
@@ -323,6 +331,14 @@ unsigned long long arm_scan_kernel_launches(void);
  * 1 sequential, 2 chunk-parallel); 5 programmatic dependent launch (0 on,
  * 1 off).  Returns 0, or 4 for an unknown knob or a negative value. */
 int arm_scan_set_kernel_override(int knob, int value);
+
+/* Extension: the device ordinal the synchronous entry points stage HOST
+ * buffers through, for the calling thread (the reference runs on the host
+ * and has no device argument; this is the boundary's device_ordinal).  -1
+ * (the default) means the thread's current CUDA device.  Device-pointer
+ * calls always run on the device that owns the buffers.  Returns 0, or 2
+ * for an ordinal outside [-1, device count). */
+int arm_scan_set_device(int ordinal);
 
 /* Extension: the bidirectional scan merged by sum, as the reference's
  * bidirectional_scan(merge="sum") computes it from the two outputs of

@@ -1,4 +1,4 @@
-"""C-ABI library checks that need no GPU: it loads, reports ABI v8, exports
+"""C-ABI library checks that need no GPU: it loads, reports ABI v12, exports
 every entry point include/b200scan.h declares, and rejects bad arguments with
 the reference's codes before touching a device (reference
 kernel/arm-scan-ffi/src/lib.rs:53-58 and its FFI unit tests)."""
@@ -21,9 +21,9 @@ def declared_functions():
     return sorted(set(re.findall(r"\b(arm_scan_[a-z0-9_]+)\s*\(", text)))
 
 
-def test_library_loads_with_abi_v11():
+def test_library_loads_with_abi_v12():
     lib = _ffi.load()
-    assert lib.arm_scan_abi_version() == 11
+    assert lib.arm_scan_abi_version() == 12
     assert _ffi.lib_path().name == "libb200scan.so"
 
 
@@ -209,3 +209,13 @@ def test_no_alloc_angles_reject_problems_beyond_their_scratch():
                                                 dummy, None)
     assert rc == 2
     assert b"scratch" in lib.arm_scan_last_error()
+
+
+def test_set_device_rejects_ordinals_outside_the_machine():
+    """arm_scan_set_device accepts -1 (the current device) and rejects an
+    ordinal beyond the device count with code 2 (no GPU here: every ordinal
+    >= 0 is outside)."""
+    lib = _ffi.load()
+    assert lib.arm_scan_set_device(-1) == 0
+    assert lib.arm_scan_set_device(64) == 2
+    assert lib.arm_scan_set_device(-2) == 2
