@@ -282,39 +282,54 @@ __device__ __forceinline__ void lane_sweep(const M1Params& p, const LaneMaps& ma
         // pairs are formed along time in memory order, (e0, e1), (e2, e3),
         // so that the packed products read their operands straight from the
         // 16-byte loads; the state chain walks e0..e3 (e3..e0 in reverse)
+        // The decays of chunk k + 1 are computed while chunk k's chains run:
+        // the exps do not depend on the state, so issuing them one chunk
+        // ahead keeps MUFU work ready whenever a chain waits.
+        struct Chunk {
+            float e[4][4];   // decays [state][memory element]
+            float2 dul, duh; // dt * u, (e0, e1) and (e2, e3)
+        };
+        auto decays = [&](int c, Chunk& ck) {
+            const float4 dt4 = lds4(chunk_addr(rd, rkey, c)), u4 = lds4(chunk_addr(ru, rkey, c));
+            const float2 dtl = make_float2(dt4.x, dt4.y), dth = make_float2(dt4.z, dt4.w);
+            ck.dul = fmul2(dtl, make_float2(u4.x, u4.y));
+            ck.duh = fmul2(dth, make_float2(u4.z, u4.w));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 xl = fmul2(dtl, a2[i]), xh = fmul2(dth, a2[i]);
+                if ((kLanePolyMask >> i) & 1) {
+                    const float2 el = exp2_poly2(xl), eh = exp2_poly2(xh);
+                    ck.e[i][0] = el.x, ck.e[i][1] = el.y, ck.e[i][2] = eh.x, ck.e[i][3] = eh.y;
+                } else {
+                    ck.e[i][0] = ex2_approx(xl.x), ck.e[i][1] = ex2_approx(xl.y);
+                    ck.e[i][2] = ex2_approx(xh.x), ck.e[i][3] = ex2_approx(xh.y);
+                }
+            }
+        };
+        Chunk cur, nxt;
+        decays(REV ? 7 : 0, cur);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             const int c = REV ? 7 - k : k;
-            const float4 dt4 = lds4(chunk_addr(rd, rkey, c)), u4 = lds4(chunk_addr(ru, rkey, c));
-            const float2 dtl = make_float2(dt4.x, dt4.y), dth = make_float2(dt4.z, dt4.w);
-            const float2 dul = fmul2(dtl, make_float2(u4.x, u4.y));
-            const float2 duh = fmul2(dth, make_float2(u4.z, u4.w));
+            if (k + 1 < 8) decays(REV ? 6 - k : k + 1, nxt);
             float2 yl = make_float2(0.f, 0.f), yh = make_float2(0.f, 0.f);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const uint32_t nkey = bkey ^ ((i & 1) << 6), noff = i * 512;
                 const float4 b4 = lds4(chunk_addr(bB + noff, nkey, c));
-                const float2 xl = fmul2(dtl, a2[i]), xh = fmul2(dth, a2[i]);
-                float e[4];
-                if ((kLanePolyMask >> i) & 1) {
-                    const float2 el = exp2_poly2(xl), eh = exp2_poly2(xh);
-                    e[0] = el.x, e[1] = el.y, e[2] = eh.x, e[3] = eh.y;
-                } else {
-                    e[0] = ex2_approx(xl.x), e[1] = ex2_approx(xl.y), e[2] = ex2_approx(xh.x), e[3] = ex2_approx(xh.y);
-                }
-                const float2 bl = fmul2(dul, make_float2(b4.x, b4.y));
-                const float2 bh = fmul2(duh, make_float2(b4.z, b4.w));
+                const float2 bl = fmul2(cur.dul, make_float2(b4.x, b4.y));
+                const float2 bh = fmul2(cur.duh, make_float2(b4.z, b4.w));
                 const float bu[4] = {bl.x, bl.y, bh.x, bh.y};
                 float hs[4];
                 float hc = h[i];
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
                     const int ei = REV ? 3 - t : t;
-                    hc = fmaf(e[ei], hc, bu[ei]);
+                    hc = fmaf(cur.e[i][ei], hc, bu[ei]);
                     hs[ei] = hc;
                     if (BID) {
                         hb[i] = fmaf(pr[i], bu[ei], hb[i]);
-                        pr[i] *= e[ei];
+                        pr[i] *= cur.e[i][ei];
                     }
                 }
                 h[i] = hc;
@@ -324,6 +339,7 @@ __device__ __forceinline__ void lane_sweep(const M1Params& p, const LaneMaps& ma
                     yh = ffma2(make_float2(c4.z, c4.w), make_float2(hs[2], hs[3]), yh);
                 }
             }
+            if (k + 1 < 8) cur = nxt;
             if (FULL) {
                 // reduce-scatter over the row's 4 lanes: lane q gets memory
                 // element q of the chunk
