@@ -653,8 +653,10 @@ int lane_pick_segments(const M1Params& p, int passes_all) {
         if (ctas > 65535 * 64) break;
         const int64_t waves = (ctas + slots - 1) / slots;
         const int passes = passes_all ? passes_all : (S > 1 ? 2 : 1);
-        // a small fixed cost per pass (pipeline fill, launch) breaks ties
-        const double cost = static_cast<double>(passes) * (Ls * waves + 64);
+        // a small fixed cost per pass (pipeline fill, launch) breaks ties;
+        // the carries walk the segments serially (about two steps' time
+        // each, measured), so many short segments cost their own
+        const double cost = static_cast<double>(passes) * (Ls * waves + 64) + (S > 1 ? 2.0 * S : 0.0);
         if (best_cost < 0 || cost < best_cost) {
             best_cost = cost;
             best = S;
