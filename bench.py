@@ -651,6 +651,42 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def profile_case(case):
+    """Three calls of one case, for ncu captures (-s 2 -c 1 takes the third):
+    prefill -- the headline scan; bidir_slice -- config 4b's bidirectional
+    sum on 256 of its 1536 channels (1.3 GB on the device); cfg3_eighth --
+    config 3's per-rank MIMO on B2 x L4096 (1/8 of it)."""
+    import torch
+    import armhackathon_b200 as arm
+    dev = torch.device("cuda", 0)
+    if case == "prefill":
+        x = make_inputs(PREFILL, dev)
+        f = lambda: arm.selective_scan(x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"],  # noqa: E731
+                                       z=x["z"], delta_bias=x["delta_bias"], delta_softplus=True,
+                                       return_last_state=True)
+    elif case == "bidir_slice":
+        x = make_inputs(dict(CFG4B, dim=256), dev)
+        f = lambda: arm.bidirectional_scan(x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"],  # noqa: E731
+                                           z=x["z"], delta_bias=x["delta_bias"],
+                                           delta_softplus=True, merge="sum")
+    else:
+        g = torch.Generator(device=dev).manual_seed(0)
+        rn = lambda *s: torch.randn(*s, generator=g, device=dev)  # noqa: E731
+        B, L, H, P, N, R = 2, 4096, 24, 64, 128, 4
+        dt = torch.nn.functional.softplus(rn(B, H, L) - 4)
+        X = rn(B, L, H, P, R).bfloat16()
+        Bm = (rn(B, L, N, R) / (N * R) ** 0.5).bfloat16()
+        Cm = (rn(B, L, N, R) / (N * R) ** 0.5).bfloat16()
+        ang = torch.atanh(torch.rand(B, L, 64, generator=g, device=dev) * 0.999)
+        trap = rn(B, H, L)
+        f = lambda: arm.mamba3_mimo_x_scan(X, Bm, Cm, -dt, dt, trap, angles=ang,  # noqa: E731
+                                           return_last_state=True)
+    for _ in range(3):
+        f()
+    torch.cuda.synchronize()
+    print(f"profile case {case}: 3 calls done", file=sys.stderr)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -663,8 +699,14 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the config-1 HF prefill tok/s measurement")
+    ap.add_argument("--profile-case", choices=["prefill", "bidir_slice", "cfg3_eighth"],
+                    help="run three calls of one small case and exit (the program the ncu "
+                         "captures in profiles/ run)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
