@@ -967,6 +967,125 @@ __device__ __forceinline__ void load_x_xr(const M3Params& p, int64_t bi, int64_t
     }
 }
 
+// bf16 per-rank MIMO, 16-byte loads: a tile's X is TS = 128 / R steps of
+// dv x R contiguous elements; item (step s, 16-byte chunk i) holds channels
+// i*8/R .. +8/R-1 of every rank.  4 items per thread (1024 chunks).
+template <int R>
+__device__ __forceinline__ void load_x_xr16_raw(const M3Params& p, int64_t bi, int64_t h, int64_t s0,
+                                                uint4 (&raw)[4]) {
+    const int64_t L = p.len, H = p.heads;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int item = threadIdx.x + m * kTcThreads2;
+        const int st = item / (8 * R), ci = item % (8 * R);
+        const int64_t it = s0 + st;
+        raw[m] = make_uint4(0u, 0u, 0u, 0u);
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            raw[m] = ld8_raw16(p.v, ((bi * L + t) * H + h) * kTcP * R + ci * 8);
+        }
+    }
+}
+// The X and w o X operand images (MN-major, m = channel, k = row (step, rank))
+// from those chunks: each rank's 8/R adjacent channels go in one store.
+template <int R>
+__device__ __forceinline__ void store_x_xr16(const uint4 (&raw)[4], const float* wdec, uint8_t* img_x,
+                                             uint8_t* img_xw) {
+    constexpr int CPI = 8 / R;  // channels per item
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int item = threadIdx.x + m * kTcThreads2;
+        const int st = item / (8 * R), ci = item % (8 * R);
+        float v[8];
+        unpack8(raw[m], v);
+#pragma unroll
+        for (int rk = 0; rk < R; ++rk) {
+            const int j = st * R + rk;
+            const float w = wdec[j];
+            const uint32_t o = mnmaj_off(ci * CPI, j, kTcP);
+            if (CPI == 2) {
+                *reinterpret_cast<uint32_t*>(img_x + o) = pack_bf16x2(v[rk], v[R + rk]);
+                *reinterpret_cast<uint32_t*>(img_xw + o) = pack_bf16x2(w * v[rk], w * v[R + rk]);
+            } else {
+                *reinterpret_cast<uint2*>(img_x + o) =
+                    make_uint2(pack_bf16x2(v[rk], v[R + rk]), pack_bf16x2(v[2 * R + rk], v[3 * R + rk]));
+                *reinterpret_cast<uint2*>(img_xw + o) = make_uint2(
+                    pack_bf16x2(w * v[rk], w * v[R + rk]), pack_bf16x2(w * v[2 * R + rk], w * v[3 * R + rk]));
+            }
+        }
+    }
+}
+
+// bf16 per-rank MIMO C (q) and B (k) with 16-byte loads: item (step s, low
+// chunk i) covers dims i*8/R .. +8/R-1 of every rank and their split-halves
+// partners 64 dims up; rotated, bias-added, stored 8/R dims per row at once.
+template <int R>
+__device__ __forceinline__ void stage_qk_xr16(const M3Params& p, int64_t bi, int64_t h, int64_t s0,
+                                              uint8_t* img_q, uint8_t* img_k, const float* qbs,
+                                              const float* kbs) {
+    const int64_t L = p.len, H = p.heads;
+    constexpr int half = kTcN / 2, CPI = 8 / R;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int item = threadIdx.x + m * kTcThreads2;
+        const int st = item / (8 * R), ci = item % (8 * R);
+        const int n0 = ci * CPI;
+        const int64_t it = s0 + st;
+        float ql[8], qh[8], kl[8], kh[8], c[CPI], sn[CPI];
+        if (it < L) {
+            const int64_t t = p.reverse ? L - 1 - it : it;
+            const int64_t base = (bi * L + t) * kTcN * R + ci * 8;
+            unpack8(ld8_raw16(p.q, base), ql);
+            unpack8(ld8_raw16(p.q, base + half * R), qh);
+            unpack8(ld8_raw16(p.k, base), kl);
+            unpack8(ld8_raw16(p.k, base + half * R), kh);
+            const int64_t cs = ((bi * L + t) * H + h) * half + n0;
+#pragma unroll
+            for (int e = 0; e < CPI; ++e) {
+                c[e] = __ldg(p.cos + cs + e);
+                sn[e] = __ldg(p.sin + cs + e);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ql[e] = qh[e] = kl[e] = kh[e] = 0.f;
+#pragma unroll
+            for (int e = 0; e < CPI; ++e) c[e] = 1.f, sn[e] = 0.f;
+        }
+#pragma unroll
+        for (int rk = 0; rk < R; ++rk) {
+            const int j = st * R + rk;
+            float qlo[CPI], qhi[CPI], klo[CPI], khi[CPI];
+#pragma unroll
+            for (int e = 0; e < CPI; ++e) {
+                const int bb = rk * kTcN + n0 + e;
+                float a0 = ql[e * R + rk] + qbs[bb], a1 = qh[e * R + rk] + qbs[bb + half];
+                qlo[e] = a0 * c[e] - a1 * sn[e];
+                qhi[e] = a0 * sn[e] + a1 * c[e];
+                a0 = kl[e * R + rk] + kbs[bb];
+                a1 = kh[e * R + rk] + kbs[bb + half];
+                klo[e] = a0 * c[e] - a1 * sn[e];
+                khi[e] = a0 * sn[e] + a1 * c[e];
+            }
+            const uint32_t ol = kmaj_off(j, n0, 128), oh = kmaj_off(j, n0 + half, 128);
+            if (CPI == 2) {
+                *reinterpret_cast<uint32_t*>(img_q + ol) = pack_bf16x2(qlo[0], qlo[CPI - 1]);
+                *reinterpret_cast<uint32_t*>(img_q + oh) = pack_bf16x2(qhi[0], qhi[CPI - 1]);
+                *reinterpret_cast<uint32_t*>(img_k + ol) = pack_bf16x2(klo[0], klo[CPI - 1]);
+                *reinterpret_cast<uint32_t*>(img_k + oh) = pack_bf16x2(khi[0], khi[CPI - 1]);
+            } else {
+                *reinterpret_cast<uint2*>(img_q + ol) =
+                    make_uint2(pack_bf16x2(qlo[0], qlo[1 % CPI]), pack_bf16x2(qlo[2 % CPI], qlo[3 % CPI]));
+                *reinterpret_cast<uint2*>(img_q + oh) =
+                    make_uint2(pack_bf16x2(qhi[0], qhi[1 % CPI]), pack_bf16x2(qhi[2 % CPI], qhi[3 % CPI]));
+                *reinterpret_cast<uint2*>(img_k + ol) =
+                    make_uint2(pack_bf16x2(klo[0], klo[1 % CPI]), pack_bf16x2(klo[2 % CPI], klo[3 % CPI]));
+                *reinterpret_cast<uint2*>(img_k + oh) =
+                    make_uint2(pack_bf16x2(khi[0], khi[1 % CPI]), pack_bf16x2(khi[2 % CPI], khi[3 % CPI]));
+            }
+        }
+    }
+}
+
 // Per-rank MIMO rotated C (q) and B (k) rows: element (rank rk, dim n) of
 // step t at ((b * L + t) * dqk + n) * R + rk; biases may be absent; same
 // split-halves RoPE and item split as stage_qk_mimo.
@@ -1334,7 +1453,10 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
 
         float xv[kXItems][8];
         uint4 xraw[kXItems];  // bf16 inputs: v stays packed until after the gate barrier
-        if (XR) {
+        uint4 xr16[4];  // bf16 per-rank X: raw 16-byte chunks until the gate barrier
+        if (XR && IN16) {
+            load_x_xr16_raw<R>(p, bi, h, it0, xr16);
+        } else if (XR) {
             load_x_xr<R, IN16>(p, bi, h, it0, xv);
         } else if (R > 1) {
             load_x_r<R>(p, bi, h, it0, xv);
@@ -1367,21 +1489,27 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         }
         const int64_t next_tile = *tile_slot;
         if (next_tile < n_tiles) prefetch_tile<ANG, IN16, R, XR>(p, ta, theta0, next_tile, n_chunks);
+        if (XR && IN16) {
+            store_x_xr16<R>(xr16, wdec, smem + kFX, smem + kFXw);
+        } else {
 #pragma unroll
-        for (int q = 0; q < kXItems; ++q) {
-            int j, pc;
-            x_item(q, j, pc);
-            const float w = wdec[j];
-            float xw[8];
+            for (int q = 0; q < kXItems; ++q) {
+                int j, pc;
+                x_item(q, j, pc);
+                const float w = wdec[j];
+                float xw[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) xw[e] = w * xv[q][e];
-            const uint32_t o = mnmaj_off(pc * 8, j, kTcP);
-            *reinterpret_cast<uint4*>(smem + kFX + o) = pack8(xv[q]);
-            *reinterpret_cast<uint4*>(smem + kFXw + o) = pack8(xw);
+                for (int e = 0; e < 8; ++e) xw[e] = w * xv[q][e];
+                const uint32_t o = mnmaj_off(pc * 8, j, kTcP);
+                *reinterpret_cast<uint4*>(smem + kFX + o) = pack8(xv[q]);
+                *reinterpret_cast<uint4*>(smem + kFXw + o) = pack8(xw);
+            }
         }
         if (ANG)
             ang_part_b<IN16>(p, bi, h, bh, it0, th, qtot, th0s, smem + kFQ, smem + kFK, scl, qbs,
                              kbs);
+        else if (XR && IN16)
+            stage_qk_xr16<R>(p, bi, h, it0, smem + kFQ, smem + kFK, qbs, kbs);
         else if (XR)
             stage_qk_xr<R, IN16>(p, bi, h, it0, smem + kFQ, smem + kFK, qbs, kbs);
         else if (R > 1)
