@@ -1017,6 +1017,8 @@ int arm_scan_mamba3_angles_f32_async(const ArmMamba3Dims* dims, const float* ang
                     dims->dqk);
     if (dims->batch * dims->heads > 65535)
         return fail(ARM_SCAN_ERR_INVALID_DIMS, "batch*heads above 65535");
+    if ((dims->len + 127) / 128 > static_cast<size_t>(INT32_MAX))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "len %zu: more 128-step chunks than a grid holds", dims->len);
     const size_t need = arm_scan_mamba3_angles_workspace_bytes(dims, n_angles);
     if (workspace_bytes < need)
         return fail(ARM_SCAN_ERR_INVALID_DIMS, "workspace of %zu bytes, %zu needed",
@@ -1061,6 +1063,8 @@ static int m3_grid_sum(const ArmMamba3Dims* dims, size_t grid_w, bool both_order
     }
     if (dims->batch * dims->heads > 65535)
         return fail(ARM_SCAN_ERR_INVALID_DIMS, "batch*heads above 65535");
+    if ((dims->len + 127) / 128 > static_cast<size_t>(INT32_MAX))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "len %zu: more 128-step chunks than a grid holds", dims->len);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     std::vector<void*> p = {const_cast<float*>(q),      const_cast<float*>(k),
                             const_cast<float*>(v),      const_cast<float*>(adt),
@@ -1157,6 +1161,8 @@ int arm_scan_mamba3_angles_f32_noalloc(const ArmMamba3Dims* dims, const float* a
                     dims->dqk);
     if (dims->batch * dims->heads > 65535)
         return fail(ARM_SCAN_ERR_INVALID_DIMS, "batch*heads above 65535");
+    if ((dims->len + 127) / 128 > static_cast<size_t>(INT32_MAX))
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "len %zu: more 128-step chunks than a grid holds", dims->len);
     AngleParams a{angles, dt, cos, sin, static_cast<int64_t>(dims->batch),
                   static_cast<int64_t>(dims->heads), static_cast<int64_t>(dims->len),
                   static_cast<int64_t>(n_angles), static_cast<int64_t>(dims->dqk / 2)};

@@ -10,6 +10,7 @@
 //   phase 2: each (batch*head, chunk, pair) adds the sums of the earlier
 //            chunks, then walks its chunk writing cos/sin.
 // Reads of angles are coalesced over pairs (the innermost axis).
+#include <climits>
 #include <cstdint>
 
 #include "common.cuh"
@@ -115,6 +116,7 @@ size_t angle_workspace_bytes(int64_t batch, int64_t heads, int64_t len, int64_t 
 
 cudaError_t angle_launch(const AngleParams& a, float* ws, cudaStream_t stream) {
     const int64_t chunks = (a.len + kAgChunk - 1) / kAgChunk;
+    if (chunks > INT32_MAX || a.batch * a.heads > 65535) return cudaErrorInvalidValue;
     const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(a.batch * a.heads));
     const int t1 = static_cast<int>((a.n_angles + 31) / 32 * 32);
     const int t2 = static_cast<int>((a.half + 31) / 32 * 32);

@@ -219,3 +219,15 @@ def test_set_device_rejects_ordinals_outside_the_machine():
     assert lib.arm_scan_set_device(-1) == 0
     assert lib.arm_scan_set_device(64) == 2
     assert lib.arm_scan_set_device(-2) == 2
+
+
+def test_angle_entries_reject_lengths_beyond_the_grid():
+    """The angle pre-pass launches one CTA per 128-step chunk: a length whose
+    chunk count does not fit the grid is refused (code 2) before any CUDA call."""
+    lib = _ffi.load()
+    dims = _ffi.ArmMamba3Dims(1, 1, 0, 128, (1 << 31) * 128 + 1, 1)
+    dummy = 16
+    rc = lib.arm_scan_mamba3_angles_f32_async(ctypes.byref(dims), dummy, 64, dummy, dummy, dummy,
+                                              dummy, 1 << 40, None)
+    assert rc == 2
+    assert b"chunks" in lib.arm_scan_last_error()
