@@ -51,13 +51,18 @@ namespace {
 
 constexpr int kLT = 32;        // steps per tile
 constexpr int kLRows = 32;     // rows per CTA
-constexpr int kLStages = 4;    // ring depth
+// Ring depth: 4 stages (3 CTAs per SM, 128 registers) for the unsplit sweep,
+// whose row count caps the CTAs anyway; 3 stages (4 CTAs per SM) for the
+// split and bidirectional passes, which have CTAs to spare and gain from the
+// extra warps.
+constexpr int kLStagesWide = 4, kLStagesDense = 3;
 constexpr int kLWarps = 4;     // compute warps
 constexpr int kLThreads = (kLWarps + 1) * 32;
 constexpr uint32_t kXBytes = kLRows * kLT * 4;  // one [32 rows][32 steps] fp32 tile
 constexpr uint32_t kBCBytes = 16 * kLT * 4;     // one [16 states][32 steps] tile
 constexpr uint32_t kStageBytes = 3 * kXBytes + 2 * kBCBytes;
-constexpr uint32_t kSmemBytes = kLStages * kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
+constexpr uint32_t smem_bytes(int stages) { return stages * kStageBytes + 1024 /* alignment */ + 256 /* barriers */; }
+constexpr int min_blocks(int stages) { return stages == kLStagesWide ? 3 : 4; }
 constexpr uint32_t kWaitLimit = 1u << 24;
 // Owned states (bit i: state q + 4i) whose decays run on the FMA pipe
 // (exp2_poly2) instead of the MUFU unit, to balance the two pipes.
@@ -157,7 +162,7 @@ __device__ __forceinline__ void sts1(uint32_t a, float v) {
 
 // ---- the sweep --------------------------------------------------------------
 // One CTA: rows [row0, row0 + 32) of one (batch, group), segment s.
-template <int MODE, bool REV>
+template <int MODE, bool REV, int kLStages>
 __device__ __forceinline__ void lane_sweep(const M1Params& p, const LaneMaps& maps, const LaneWs& ws,
                                            const LaneWs* wsb, int S, int64_t Ls, int s, char* smem,
                                            uint64_t* full, uint64_t* empty) {
@@ -418,6 +423,7 @@ __device__ __forceinline__ void lane_sweep(const M1Params& p, const LaneMaps& ma
 }
 
 // Shared set-up of every pass: aligned ring, barriers, zeroed B/C rows >= N.
+template <int kLStages>
 __device__ __forceinline__ char* lane_setup(uint64_t*& full, uint64_t*& empty, int N) {
     extern __shared__ unsigned char lane_smem_raw[];
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(lane_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -445,16 +451,16 @@ __device__ __forceinline__ char* lane_setup(uint64_t*& full, uint64_t*& empty, i
 // the state-only sweep; FIRST 1: the full scan of an unsplit sequence (its
 // own kernel, so that its registers are not those of both sweeps); FIRST 0:
 // every segment state-only.
-template <int FIRST, bool REV>
-__global__ void __launch_bounds__(kLThreads, 3)
+template <int FIRST, bool REV, int ST>
+__global__ void __launch_bounds__(kLThreads, min_blocks(ST))
     m1_lane_pass1(M1Params p, const __grid_constant__ LaneMaps maps, LaneWs ws, int S, int64_t Ls) {
     uint64_t *full, *empty;
-    char* smem = lane_setup(full, empty, static_cast<int>(p.state));
+    char* smem = lane_setup<ST>(full, empty, static_cast<int>(p.state));
     griddep_launch_dependents();
     if (FIRST == 1 || (FIRST == 2 && blockIdx.y == 0))
-        lane_sweep<kLaneFirst, REV>(p, maps, ws, nullptr, S, Ls, 0, smem, full, empty);
+        lane_sweep<kLaneFirst, REV, ST>(p, maps, ws, nullptr, S, Ls, 0, smem, full, empty);
     else
-        lane_sweep<kLaneState, REV>(p, maps, ws, nullptr, S, Ls, blockIdx.y, smem, full, empty);
+        lane_sweep<kLaneState, REV, ST>(p, maps, ws, nullptr, S, Ls, blockIdx.y, smem, full, empty);
 }
 
 // Pass 1 of both traversals of the same inputs: one forward walk per segment
@@ -462,22 +468,23 @@ __global__ void __launch_bounds__(kLThreads, 3)
 // reverse traversal's aggregate of the segment from zero,
 // sum_t (prod_{r<t} exp(dt_r A)) dt_t u_t B_t (the running product needs
 // multiplies only), written at the reverse traversal's segment index.
-__global__ void __launch_bounds__(kLThreads, 3)
+template <int ST>
+__global__ void __launch_bounds__(kLThreads, min_blocks(ST))
     m1_lane_pass1_bidir(M1Params p, const __grid_constant__ LaneMaps maps, LaneWs ws, LaneWs wsb, int S,
                         int64_t Ls) {
     uint64_t *full, *empty;
-    char* smem = lane_setup(full, empty, static_cast<int>(p.state));
+    char* smem = lane_setup<ST>(full, empty, static_cast<int>(p.state));
     griddep_launch_dependents();
-    lane_sweep<kLaneBidir, false>(p, maps, ws, &wsb, S, Ls, blockIdx.y, smem, full, empty);
+    lane_sweep<kLaneBidir, false, ST>(p, maps, ws, &wsb, S, Ls, blockIdx.y, smem, full, empty);
 }
 
 // Pass 2: segments s_off .. from their incoming states.
-template <bool REV>
-__global__ void __launch_bounds__(kLThreads, 3)
+template <bool REV, int ST>
+__global__ void __launch_bounds__(kLThreads, min_blocks(ST))
     m1_lane_pass2(M1Params p, const __grid_constant__ LaneMaps maps, LaneWs ws, int S, int64_t Ls, int s_off) {
     uint64_t *full, *empty;
-    char* smem = lane_setup(full, empty, static_cast<int>(p.state));
-    lane_sweep<kLaneRescan, REV>(p, maps, ws, nullptr, S, Ls, blockIdx.y + s_off, smem, full, empty);
+    char* smem = lane_setup<ST>(full, empty, static_cast<int>(p.state));
+    lane_sweep<kLaneRescan, REV, ST>(p, maps, ws, nullptr, S, Ls, blockIdx.y + s_off, smem, full, empty);
 }
 
 // Carry across segments in traversal order.  FIRST: segment 0's hend is its
@@ -601,7 +608,7 @@ cudaError_t make_maps(const M1Params& p, LaneMaps* m) {
 
 // Raises the kernel's dynamic shared-memory limit, once per (kernel, device).
 template <class K>
-cudaError_t allow_smem(K kern) {
+cudaError_t allow_smem(K kern, uint32_t bytes) {
     static std::mutex mu;
     static std::vector<std::pair<const void*, int>> done;
     int dev = 0;
@@ -611,26 +618,35 @@ cudaError_t allow_smem(K kern) {
     for (const auto& d : done)
         if (d.first == key && d.second == dev) return cudaSuccess;
     const cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
     if (e == cudaSuccess) done.emplace_back(key, dev);
     return e;
 }
 
 // Concurrent CTAs of the lane kernels per device (SMs x resident CTAs per SM).
-int lane_slots() {
-    static int cache[64] = {0};
+// Concurrent CTAs per device (SMs x resident CTAs per SM) of the wide
+// (unsplit sweep) or the dense (split / bidirectional) configuration.
+int lane_slots(bool dense) {
+    static int cache[64][2] = {{0}};
     static std::mutex mu;
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
-    if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
-    int sms = 148, per = 3;
+    if (dev >= 0 && dev < 64 && cache[dev][dense]) return cache[dev][dense];
+    int sms = 148, per = dense ? 4 : 3;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (allow_smem(m1_lane_pass2<false>) == cudaSuccess)
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, m1_lane_pass2<false>, kLThreads, kSmemBytes);
+    if (dense) {
+        auto k = m1_lane_pass2<false, kLStagesDense>;
+        if (allow_smem(k, smem_bytes(kLStagesDense)) == cudaSuccess)
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, kLThreads, smem_bytes(kLStagesDense));
+    } else {
+        auto k = m1_lane_pass1<1, false, kLStagesWide>;
+        if (allow_smem(k, smem_bytes(kLStagesWide)) == cudaSuccess)
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, kLThreads, smem_bytes(kLStagesWide));
+    }
     if (per < 1) per = 1;
     const int v = sms * per;
-    if (dev >= 0 && dev < 64) cache[dev] = v;
+    if (dev >= 0 && dev < 64) cache[dev][dense] = v;
     return v;
 }
 
@@ -642,7 +658,6 @@ int lane_slots() {
 int lane_pick_segments(const M1Params& p, int passes_all) {
     const int64_t gsz = p.dim / p.groups;
     const int64_t rb = ((gsz + kLRows - 1) / kLRows) * p.batch * p.groups;
-    const int64_t slots = lane_slots();
     int best = 1;
     double best_cost = -1;
     for (int S = 1; S <= 1024; S *= 2) {
@@ -651,6 +666,7 @@ int lane_pick_segments(const M1Params& p, int passes_all) {
         const int64_t Ls = p.len / S;
         const int64_t ctas = passes_all ? rb * S : rb * (S > 1 ? S - 1 : 1);
         if (ctas > 65535 * 64) break;
+        const int64_t slots = lane_slots(ctas > lane_slots(false));
         const int64_t waves = (ctas + slots - 1) / slots;
         const int passes = passes_all ? passes_all : (S > 1 ? 2 : 1);
         // a small fixed cost per pass (pipeline fill, launch) breaks ties;
@@ -717,11 +733,22 @@ cudaError_t m1_lane_launch(const M1Params& p, int S, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     const bool first = p.out != nullptr;  // out == nullptr: final state only
     const int f = first ? (S == 1 ? 1 : 2) : 0;
-    auto k1 = f == 1 ? (p.reverse ? m1_lane_pass1<1, true> : m1_lane_pass1<1, false>)
-            : f == 2 ? (p.reverse ? m1_lane_pass1<2, true> : m1_lane_pass1<2, false>)
-                     : (p.reverse ? m1_lane_pass1<0, true> : m1_lane_pass1<0, false>);
-    auto k2 = p.reverse ? m1_lane_pass2<true> : m1_lane_pass2<false>;
-    if ((e = allow_smem(k1)) != cudaSuccess || (e = allow_smem(k2)) != cudaSuccess) return e;
+    constexpr int W = kLStagesWide, Dn = kLStagesDense;
+    const int64_t gsz = p.dim / p.groups;
+    const unsigned gx = static_cast<unsigned>(((gsz + kLRows - 1) / kLRows) * p.batch * p.groups);
+    // pass 1 covers segments 0 .. S-2 when the first runs in full (all of
+    // them for S == 1), every segment otherwise
+    const unsigned s1 = first ? static_cast<unsigned>(S > 1 ? S - 1 : 1) : static_cast<unsigned>(S);
+    // the dense configuration where a pass has more CTAs than the wide one holds
+    const bool dense = static_cast<int64_t>(gx) * s1 > lane_slots(false);
+#define LANE_P1(F) (dense ? (p.reverse ? m1_lane_pass1<F, true, Dn> : m1_lane_pass1<F, false, Dn>) \
+                          : (p.reverse ? m1_lane_pass1<F, true, W> : m1_lane_pass1<F, false, W>))
+    auto k1 = f == 1 ? LANE_P1(1) : f == 2 ? LANE_P1(2) : LANE_P1(0);
+#undef LANE_P1
+    auto k2 = dense ? (p.reverse ? m1_lane_pass2<true, Dn> : m1_lane_pass2<false, Dn>)
+                    : (p.reverse ? m1_lane_pass2<true, W> : m1_lane_pass2<false, W>);
+    const uint32_t smem1 = smem_bytes(dense ? Dn : W), smem2 = smem1;
+    if ((e = allow_smem(k1, smem1)) != cudaSuccess || (e = allow_smem(k2, smem2)) != cudaSuccess) return e;
     LaneWsAlloc alloc(stream);
     LaneWs ws = {nullptr, nullptr, nullptr};
     if (S > 1 || !first) {
@@ -729,12 +756,7 @@ cudaError_t m1_lane_launch(const M1Params& p, int S, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         carve(static_cast<float*>(alloc.raw), S, rows, &ws);
     }
-    const int64_t gsz = p.dim / p.groups;
-    const unsigned gx = static_cast<unsigned>(((gsz + kLRows - 1) / kLRows) * p.batch * p.groups);
-    // pass 1 covers segments 0 .. S-2 when the first runs in full (all of
-    // them for S == 1), every segment otherwise
-    const unsigned s1 = first ? static_cast<unsigned>(S > 1 ? S - 1 : 1) : static_cast<unsigned>(S);
-    k1<<<dim3(gx, s1), kLThreads, kSmemBytes, stream>>>(p, maps, ws, S, Ls);
+    k1<<<dim3(gx, s1), kLThreads, smem1, stream>>>(p, maps, ws, S, Ls);
     note_launch();
     e = cudaGetLastError();
     if (e == cudaSuccess && (S > 1 || !first)) {
@@ -745,7 +767,7 @@ cudaError_t m1_lane_launch(const M1Params& p, int S, cudaStream_t stream) {
         note_launch();
     }
     if (e == cudaSuccess && first && S > 1) {
-        e = launch_pdl_smem(k2, dim3(gx, static_cast<unsigned>(S - 1)), dim3(kLThreads), kSmemBytes, stream, p, maps,
+        e = launch_pdl_smem(k2, dim3(gx, static_cast<unsigned>(S - 1)), dim3(kLThreads), smem2, stream, p, maps,
                        ws, S, Ls, 1);
         note_launch();
     }
@@ -770,8 +792,16 @@ cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S
     LaneMaps maps;
     cudaError_t e = make_maps(fwd, &maps);
     if (e != cudaSuccess) return e;
-    if ((e = allow_smem(m1_lane_pass1_bidir)) != cudaSuccess || (e = allow_smem(m1_lane_pass2<false>)) != cudaSuccess ||
-        (e = allow_smem(m1_lane_pass2<true>)) != cudaSuccess)
+    const int64_t gsz0 = fwd.dim / fwd.groups;
+    const int64_t ctas = ((gsz0 + kLRows - 1) / kLRows) * fwd.batch * fwd.groups * S;
+    const bool dense = ctas > lane_slots(false);
+    constexpr int W = kLStagesWide, Dn = kLStagesDense;
+    auto kb = dense ? m1_lane_pass1_bidir<Dn> : m1_lane_pass1_bidir<W>;
+    auto kf = dense ? m1_lane_pass2<false, Dn> : m1_lane_pass2<false, W>;
+    auto kr = dense ? m1_lane_pass2<true, Dn> : m1_lane_pass2<true, W>;
+    const uint32_t smem = smem_bytes(dense ? Dn : W);
+    if ((e = allow_smem(kb, smem)) != cudaSuccess || (e = allow_smem(kf, smem)) != cudaSuccess ||
+        (e = allow_smem(kr, smem)) != cudaSuccess)
         return e;
     const size_t per = 2 * static_cast<size_t>(S) * rows * 16 + static_cast<size_t>(S) * rows;
     LaneWsAlloc alloc(stream);
@@ -782,7 +812,7 @@ cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S
     const int64_t gsz = fwd.dim / fwd.groups;
     const unsigned gx = static_cast<unsigned>(((gsz + kLRows - 1) / kLRows) * fwd.batch * fwd.groups);
     const dim3 grid(gx, static_cast<unsigned>(S)), block(kLThreads);
-    m1_lane_pass1_bidir<<<grid, block, kSmemBytes, stream>>>(fwd, maps, wf, wb, S, Ls);
+    kb<<<grid, block, smem, stream>>>(fwd, maps, wf, wb, S, Ls);
     note_launch();
     e = cudaGetLastError();
     const int64_t n = rows * fwd.state;
@@ -798,10 +828,10 @@ cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S
     if (fwd.out) {
         LaneMaps mb = maps;  // bwd reads the same inputs
         if (e == cudaSuccess)
-            e = launch_pdl_smem(m1_lane_pass2<false>, grid, block, kSmemBytes, stream, f2, maps, wf, S, Ls, 0);
+            e = launch_pdl_smem(kf, grid, block, smem, stream, f2, maps, wf, S, Ls, 0);
         if (e == cudaSuccess) note_launch();
         if (e == cudaSuccess)
-            e = launch_pdl_smem(m1_lane_pass2<true>, grid, block, kSmemBytes, stream, b2, mb, wb, S, Ls, 0);
+            e = launch_pdl_smem(kr, grid, block, smem, stream, b2, mb, wb, S, Ls, 0);
         if (e == cudaSuccess) note_launch();
     }
     const cudaError_t ef = alloc.release();
