@@ -652,10 +652,13 @@ def run_reference(args):
 
 
 def profile_case(case):
-    """Three calls of one case, for ncu captures (-s 2 -c 1 takes the third):
-    prefill -- the headline scan; bidir_slice -- config 4b's bidirectional
-    sum on 256 of its 1536 channels (1.3 GB on the device); cfg3_eighth --
-    config 3's per-rank MIMO on B2 x L4096 (1/8 of it)."""
+    """Three calls of one case, for ncu captures: prefill -- the headline
+    scan; bidir_slice -- config 4b's bidirectional sum on 256 of its 1536
+    channels (1.3 GB on the device); cfg3_eighth -- config 3's per-rank MIMO
+    on B2 x L4096 (1/8 of it); cfg2_bf16 / cfg2_fp32 -- config 2 on the
+    tensor-core and the fp32 chunk path; cfg4a -- config 4a's SS2D; mixer --
+    the Mamba-3 mixer prologue at config 2's shape; tile_prefill -- the
+    headline scan on the row-tile fallback kernel."""
     import torch
     import armhackathon_b200 as arm
     dev = torch.device("cuda", 0)
@@ -669,6 +672,35 @@ def profile_case(case):
         f = lambda: arm.bidirectional_scan(x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"],  # noqa: E731
                                            z=x["z"], delta_bias=x["delta_bias"],
                                            delta_softplus=True, merge="sum")
+    elif case in ("cfg2_bf16", "cfg2_fp32"):
+        x = m3_inputs(CFG2, dev)
+        if case == "cfg2_bf16":
+            bf = torch.bfloat16
+            x = dict(x, q=x["q"].to(bf), k=x["k"].to(bf), v=x["v"].to(bf),
+                     angles=x["angles"][:, :, :1, :].to(bf).contiguous())
+            f = lambda: arm.mamba3_scan(**x, return_last_state=True, precision="bf16")  # noqa: E731
+        else:
+            f = lambda: arm.mamba3_scan(**x, return_last_state=True)  # noqa: E731
+    elif case == "cfg4a":
+        x = m3_inputs(CFG4A, dev)
+        Bq, Hh, gd = CFG4A["batch"], CFG4A["heads"], CFG4A["grid"]
+        grid = lambda t: t.reshape(Bq, gd, gd, *t.shape[2:])  # noqa: E731
+        hm = lambda t: t.reshape(Bq, Hh, gd, gd)  # noqa: E731
+        xs = dict(q=grid(x["q"]), k=grid(x["k"]), v=grid(x["v"]), angles=grid(x["angles"]),
+                  adt=hm(x["adt"]), dt=hm(x["dt"]), trap=hm(x["trap"]), q_bias=x["q_bias"],
+                  k_bias=x["k_bias"], D=x["D"])
+        f = lambda: arm.ss2d_scan_mamba3(**xs)  # noqa: E731
+    elif case == "mixer":
+        wm = dict(kind="mixer", batch=4, heads=24, dv=64, dqk=128, len=4096, rank=1, pairs=32)
+        xm = mixer_inputs(wm, dev)
+        f = lambda: arm.mamba3_mixer_prologue(**xm)  # noqa: E731
+    elif case == "tile_prefill":
+        from armhackathon_b200 import _ffi
+        _ffi.set_kernel_override("m1_kernel", _ffi.M1_KERNELS["tile"])
+        x = make_inputs(PREFILL, dev)
+        f = lambda: arm.selective_scan(x["u"], x["delta"], x["A"], x["B"], x["C"], D=x["D"],  # noqa: E731
+                                       z=x["z"], delta_bias=x["delta_bias"], delta_softplus=True,
+                                       return_last_state=True)
     else:
         g = torch.Generator(device=dev).manual_seed(0)
         rn = lambda *s: torch.randn(*s, generator=g, device=dev)  # noqa: E731
@@ -699,7 +731,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the config-1 HF prefill tok/s measurement")
-    ap.add_argument("--profile-case", choices=["prefill", "bidir_slice", "cfg3_eighth"],
+    ap.add_argument("--profile-case", choices=["prefill", "bidir_slice", "cfg3_eighth", "cfg2_bf16",
+                                               "cfg2_fp32", "cfg4a", "mixer", "tile_prefill"],
                     help="run three calls of one small case and exit (the program the ncu "
                          "captures in profiles/ run)")
     args = ap.parse_args()
