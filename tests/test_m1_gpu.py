@@ -495,3 +495,23 @@ def test_causal_conv1d_silu_matches_torch(shape):
     want = F.silu(F.conv1d(x, w, b, padding=K - 1, groups=D)[..., :L])
     got = arm().causal_conv1d_silu(x, w, b)
     assert rel_err(got.cpu().numpy(), want.cpu().numpy()) <= 1e-5
+
+
+@pytest.mark.parametrize("L", [1024, 1027])
+def test_segment_summary_end_states_and_dt_sums(L):
+    """The segment-summary entry (sequence parallelism): both traversals' end
+    states from zero and the per-row sum of dt, on the lane kernel (length a
+    multiple of 4: one shared pass) and on the fallback (1027: the row-tile
+    scans plus a dt-sum kernel), against the oracle and a float64 sum."""
+    B, D, N = 2, 40, 16
+    x = _slow_decay_case(B, D, L, N, seed=L)
+    t = cuda(x)
+    hf, hb, sdt = arm().selective_scan_segment_summary(
+        t["u"], t["delta"], t["A"], t["B"], t["C"], delta_bias=t["delta_bias"],
+        delta_softplus=True)
+    _, wlf = oracle.m1_scan(**x, nthreads=8)
+    _, wlb = oracle.m1_scan(**x, reverse=True, nthreads=8)
+    assert rel_err(hf.cpu().numpy(), wlf) <= REL_TOL
+    assert rel_err(hb.cpu().numpy(), wlb) <= REL_TOL
+    dt = np.logaddexp(0.0, x["delta"].astype(np.float64) + x["delta_bias"][None, :, None])
+    assert rel_err(sdt.cpu().numpy(), dt.sum(-1)) <= REL_TOL
