@@ -20,7 +20,7 @@ import os
 import sys
 from pathlib import Path
 
-ABI_VERSION = 12
+ABI_VERSION = 13
 
 _LIB_NAMES = ["libb200scan.so"]
 
@@ -136,6 +136,14 @@ def _bind(lib):
     lib.arm_scan_selective_scan_segment_summary_f32_async.restype = ctypes.c_int
     lib.arm_scan_selective_scan_segment_summary_f32_async.argtypes = [
         ctypes.POINTER(ArmScanDims), *([_VP] * 6), _I, _I, _VP, _VP, _VP, _VP]
+    lib.arm_scan_selective_scan_bidirectional_workspace_bytes.restype = ctypes.c_size_t
+    lib.arm_scan_selective_scan_bidirectional_workspace_bytes.argtypes = [ctypes.POINTER(ArmScanDims)]
+    lib.arm_scan_selective_scan_bidirectional_summary_f32_async.restype = ctypes.c_int
+    lib.arm_scan_selective_scan_bidirectional_summary_f32_async.argtypes = [
+        ctypes.POINTER(ArmScanDims), *([_VP] * 6), _I, _VP, ctypes.c_size_t, _VP, _VP, _VP, _VP]
+    lib.arm_scan_selective_scan_bidirectional_finish_f32_async.restype = ctypes.c_int
+    lib.arm_scan_selective_scan_bidirectional_finish_f32_async.argtypes = [
+        ctypes.POINTER(ArmScanDims), *([_VP] * 8), _I, _VP, ctypes.c_size_t, _VP, _VP, _VP, _VP]
     lib.arm_scan_mamba3_mixer_prologue_f32_async.restype = ctypes.c_int
     lib.arm_scan_mamba3_mixer_prologue_f32_async.argtypes = [
         ctypes.POINTER(ArmMamba3MixerDims), *([_VP] * 4), ctypes.c_float, ctypes.c_float,
@@ -354,6 +362,32 @@ def segment_summary_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_delta_b
         _n(stream)), "arm_scan_selective_scan_segment_summary_f32_async")
 
 
+def bidirectional_workspace_bytes(dims):
+    """Workspace of the two-phase bidirectional form (0: shape not covered)."""
+    return int(load().arm_scan_selective_scan_bidirectional_workspace_bytes(ctypes.byref(dims)))
+
+
+def bidirectional_summary_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_delta_bias,
+                              delta_softplus, ptr_ws, ws_bytes, ptr_last_fwd, ptr_last_bwd,
+                              ptr_dt_sum, stream):
+    """Phase 1 of the two-phase bidirectional form (device pointers)."""
+    _check(load().arm_scan_selective_scan_bidirectional_summary_f32_async(
+        ctypes.byref(dims), ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, _n(ptr_delta_bias),
+        int(bool(delta_softplus)), ptr_ws, int(ws_bytes), ptr_last_fwd, ptr_last_bwd, ptr_dt_sum,
+        _n(stream)), "arm_scan_selective_scan_bidirectional_summary_f32_async")
+
+
+def bidirectional_finish_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_d, ptr_z,
+                             ptr_delta_bias, delta_softplus, ptr_ws, ws_bytes, ptr_h0_fwd,
+                             ptr_h0_bwd, ptr_out, stream):
+    """Phase 2 of the two-phase bidirectional form (device pointers)."""
+    _check(load().arm_scan_selective_scan_bidirectional_finish_f32_async(
+        ctypes.byref(dims), ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, _n(ptr_d), _n(ptr_z),
+        _n(ptr_delta_bias), int(bool(delta_softplus)), ptr_ws, int(ws_bytes), _n(ptr_h0_fwd),
+        _n(ptr_h0_bwd), ptr_out, _n(stream)),
+        "arm_scan_selective_scan_bidirectional_finish_f32_async")
+
+
 def set_device(ordinal):
     """Device the synchronous host-buffer calls of this thread run on (-1:
     the current CUDA device)."""
@@ -418,7 +452,9 @@ def exported_symbols():
             "arm_scan_set_kernel_override", "arm_scan_mamba3_mimo_x_tc_async",
             "arm_scan_selective_scan_segment_summary_f32_async",
             "arm_scan_mamba3_noncausal_f32_async", "arm_scan_causal_conv1d_silu_f32_async",
-            "arm_scan_set_device"]
+            "arm_scan_set_device", "arm_scan_selective_scan_bidirectional_workspace_bytes",
+            "arm_scan_selective_scan_bidirectional_summary_f32_async",
+            "arm_scan_selective_scan_bidirectional_finish_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

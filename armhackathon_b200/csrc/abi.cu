@@ -719,6 +719,77 @@ int arm_scan_causal_conv1d_silu_f32_async(size_t batch, size_t dim, size_t len, 
     return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "causal conv1d launch");
 }
 
+size_t arm_scan_selective_scan_bidirectional_workspace_bytes(const ArmScanDims* dims) {
+    M1Counts cnt;
+    if (!dims || m1_validate(dims, &cnt) != ARM_SCAN_OK) return 0;
+    std::vector<void*> p(8, nullptr);
+    M1Params m = m1_params(dims, p, 1, 0);
+    size_t bytes = 0;
+    m1_lane_bidir_plan(m, &bytes);
+    return bytes;
+}
+
+static int bidir_phase_common(const ArmScanDims* dims, const float* u, const float* delta,
+                              const float* a, const float* b, const float* c, const float* d_skip,
+                              const float* z, const float* delta_bias, int delta_softplus,
+                              void* workspace, size_t ws_bytes, float* out, float* last_fwd,
+                              float* last_bwd, float* dt_sum, const float* h0_fwd,
+                              const float* h0_bwd, bool summary, void* stream) {
+    if (!dims || !u || !delta || !a || !b || !c || !workspace)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    if (summary ? (!last_fwd || !last_bwd || !dt_sum) : !out)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required output pointer is null");
+    M1Counts cnt;
+    int rc = m1_validate(dims, &cnt);
+    if (rc) return rc;
+    std::vector<void*> p = {const_cast<float*>(u), const_cast<float*>(delta),
+                            const_cast<float*>(a), const_cast<float*>(b),
+                            const_cast<float*>(c), const_cast<float*>(d_skip),
+                            const_cast<float*>(z), const_cast<float*>(delta_bias)};
+    M1Params base = m1_params(dims, p, delta_softplus, 0);
+    M1Params f = base, r = base;
+    r.reverse = 1;
+    if (summary) {
+        f.z = r.z = nullptr;
+        f.d_skip = r.d_skip = nullptr;
+        f.last_state = last_fwd;
+        f.dt_sum = dt_sum;
+        r.last_state = last_bwd;
+    } else {
+        f.out = out;
+        r.out = out;
+        r.out_acc = 1;
+        f.h0 = h0_fwd;
+        r.h0 = h0_bwd;
+    }
+    size_t need = 0;
+    if (!m1_lane_bidir_plan(f, &need))
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE, "the two-phase form needs d_state <= 16 and len a multiple of 4");
+    if (ws_bytes < need) return fail(ARM_SCAN_ERR_INVALID_DIMS, "workspace of %zu bytes, %zu needed", ws_bytes, need);
+    cudaError_t e = m1_lane_bidir_phase(f, r, workspace, ws_bytes, summary, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorNotSupported)
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE, "the two-phase form needs 16-byte aligned tensors");
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "bidirectional phase launch");
+}
+
+int arm_scan_selective_scan_bidirectional_summary_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
+    const float* c, const float* delta_bias, int delta_softplus, void* workspace, size_t ws_bytes,
+    float* last_fwd, float* last_bwd, float* dt_sum, void* stream) {
+    return bidir_phase_common(dims, u, delta, a, b, c, nullptr, nullptr, delta_bias, delta_softplus,
+                              workspace, ws_bytes, nullptr, last_fwd, last_bwd, dt_sum, nullptr, nullptr,
+                              true, stream);
+}
+
+int arm_scan_selective_scan_bidirectional_finish_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
+    const float* c, const float* d_skip, const float* z, const float* delta_bias, int delta_softplus,
+    void* workspace, size_t ws_bytes, const float* h0_fwd, const float* h0_bwd, float* out,
+    void* stream) {
+    return bidir_phase_common(dims, u, delta, a, b, c, d_skip, z, delta_bias, delta_softplus, workspace,
+                              ws_bytes, out, nullptr, nullptr, nullptr, h0_fwd, h0_bwd, false, stream);
+}
+
 int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const float* k,
                              const float* v, const float* adt, const float* dt, const float* trap,
                              const float* q_bias, const float* k_bias, const float* cos,

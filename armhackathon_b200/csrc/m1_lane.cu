@@ -787,14 +787,22 @@ int m1_lane_bidir_segments(const M1Params& fwd) {
     return lane_pick_segments(fwd, fwd.out ? 3 : 1);
 }
 
-cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S, cudaStream_t stream) {
+// The bidirectional passes over a given workspace (both directions' segment
+// aggregates, see lane_bidir_ws_floats).  first: the shared pass 1; then
+// the carries (each direction from its own h0, ending in its last_state and,
+// forward, dt_sum); finish: the two rescans (fwd.out != nullptr).  A
+// sequence split over devices runs first + carries from zero (its summary),
+// exchanges summaries, and later finish with the carries from the folded
+// incoming states, reusing pass 1's aggregates from the same workspace.
+static cudaError_t lane_bidir_run(const M1Params& fwd, const M1Params& bwd, int S, float* raw, bool first,
+                                  bool finish, cudaStream_t stream) {
     const int64_t rows = fwd.batch * fwd.dim, Ls = fwd.len / S;
     LaneMaps maps;
     cudaError_t e = make_maps(fwd, &maps);
     if (e != cudaSuccess) return e;
-    const int64_t gsz0 = fwd.dim / fwd.groups;
-    const int64_t ctas = ((gsz0 + kLRows - 1) / kLRows) * fwd.batch * fwd.groups * S;
-    const bool dense = ctas > lane_slots(false);
+    const int64_t gsz = fwd.dim / fwd.groups;
+    const unsigned gx = static_cast<unsigned>(((gsz + kLRows - 1) / kLRows) * fwd.batch * fwd.groups);
+    const bool dense = static_cast<int64_t>(gx) * S > lane_slots(false);
     constexpr int W = kLStagesWide, Dn = kLStagesDense;
     auto kb = dense ? m1_lane_pass1_bidir<Dn> : m1_lane_pass1_bidir<W>;
     auto kf = dense ? m1_lane_pass2<false, Dn> : m1_lane_pass2<false, W>;
@@ -804,17 +812,15 @@ cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S
         (e = allow_smem(kr, smem)) != cudaSuccess)
         return e;
     const size_t per = 2 * static_cast<size_t>(S) * rows * 16 + static_cast<size_t>(S) * rows;
-    LaneWsAlloc alloc(stream);
-    if ((e = alloc.get(2 * per * sizeof(float))) != cudaSuccess) return e;
     LaneWs wf, wb;
-    carve(static_cast<float*>(alloc.raw), S, rows, &wf);
-    carve(static_cast<float*>(alloc.raw) + per, S, rows, &wb);
-    const int64_t gsz = fwd.dim / fwd.groups;
-    const unsigned gx = static_cast<unsigned>(((gsz + kLRows - 1) / kLRows) * fwd.batch * fwd.groups);
+    carve(raw, S, rows, &wf);
+    carve(raw + per, S, rows, &wb);
     const dim3 grid(gx, static_cast<unsigned>(S)), block(kLThreads);
-    kb<<<grid, block, smem, stream>>>(fwd, maps, wf, wb, S, Ls);
-    note_launch();
-    e = cudaGetLastError();
+    if (first) {
+        kb<<<grid, block, smem, stream>>>(fwd, maps, wf, wb, S, Ls);
+        note_launch();
+        e = cudaGetLastError();
+    }
     const int64_t n = rows * fwd.state;
     const dim3 cg(static_cast<unsigned>((n + 255) / 256));
     // the carries end in last_state; pass 2 leaves it alone
@@ -825,17 +831,51 @@ cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S
     if (e == cudaSuccess) note_launch();
     if (e == cudaSuccess) e = launch_pdl(m1_lane_carry<false>, cg, dim3(256), stream, bwd, wb, S);
     if (e == cudaSuccess) note_launch();
-    if (fwd.out) {
-        LaneMaps mb = maps;  // bwd reads the same inputs
-        if (e == cudaSuccess)
-            e = launch_pdl_smem(kf, grid, block, smem, stream, f2, maps, wf, S, Ls, 0);
+    if (finish && fwd.out) {
+        if (e == cudaSuccess) e = launch_pdl_smem(kf, grid, block, smem, stream, f2, maps, wf, S, Ls, 0);
         if (e == cudaSuccess) note_launch();
-        if (e == cudaSuccess)
-            e = launch_pdl_smem(kr, grid, block, smem, stream, b2, mb, wb, S, Ls, 0);
+        if (e == cudaSuccess) e = launch_pdl_smem(kr, grid, block, smem, stream, b2, maps, wb, S, Ls, 0);
         if (e == cudaSuccess) note_launch();
     }
+    return e;
+}
+
+static size_t lane_bidir_ws_floats(int64_t rows, int S) {
+    return 2 * (2 * static_cast<size_t>(S) * rows * 16 + static_cast<size_t>(S) * rows);
+}
+
+cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int S, cudaStream_t stream) {
+    LaneWsAlloc alloc(stream);
+    cudaError_t e = alloc.get(lane_bidir_ws_floats(fwd.batch * fwd.dim, S) * sizeof(float));
+    if (e != cudaSuccess) return e;
+    e = lane_bidir_run(fwd, bwd, S, static_cast<float*>(alloc.raw), true, true, stream);
     const cudaError_t ef = alloc.release();
     return e != cudaSuccess ? e : ef;
+}
+
+// Two-phase form for sequence parallelism (caller's workspace).  The segment
+// count depends on the shape and the device only, so both phases agree.
+int m1_lane_bidir_plan(const M1Params& shape, size_t* ws_bytes) {
+    M1Params q = shape;
+    q.out = reinterpret_cast<float*>(uintptr_t(256));  // the plan of a call with outputs
+    const bool ok = q.state <= 16 && q.state >= 1 && q.len % 4 == 0 && q.len >= 4 && q.dim % q.groups == 0 &&
+                    q.len <= (int64_t(1) << 30) && q.batch * q.dim <= (int64_t(1) << 30) && encode_fn() != nullptr;
+    if (!ok) {
+        *ws_bytes = 0;
+        return 0;
+    }
+    const int S = forced_segments(q) ? forced_segments(q) : lane_pick_segments(q, 3);
+    *ws_bytes = lane_bidir_ws_floats(q.batch * q.dim, S) * sizeof(float);
+    return S;
+}
+
+cudaError_t m1_lane_bidir_phase(const M1Params& fwd, const M1Params& bwd, void* workspace, size_t ws_bytes,
+                                bool summary, cudaStream_t stream) {
+    size_t need = 0;
+    const int S = m1_lane_bidir_plan(fwd, &need);
+    if (!S || !lane_applicable(fwd)) return cudaErrorNotSupported;
+    if (ws_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u)) return cudaErrorInvalidValue;
+    return lane_bidir_run(fwd, bwd, S, static_cast<float*>(workspace), summary, !summary, stream);
 }
 
 int m1_lane_status_and_clear() {

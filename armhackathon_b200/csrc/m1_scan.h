@@ -65,6 +65,15 @@ cudaError_t m1_lane_launch(const M1Params& p, int segments, cudaStream_t stream)
 int m1_lane_bidir_segments(const M1Params& fwd);
 cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int segments,
                                  cudaStream_t stream);
+// Two-phase bidirectional form over a caller's workspace (sequence
+// parallelism): the plan (segment count, 0 when the lane kernel cannot take
+// the shape; *ws_bytes its workspace) and a phase: summary (shared pass 1,
+// carries from fwd.h0 / bwd.h0 into last_state and fwd.dt_sum) or finish
+// (carries from the incoming states, both rescans; pass 1's aggregates are
+// read from the workspace, which must be unchanged since the summary call).
+int m1_lane_bidir_plan(const M1Params& shape, size_t* ws_bytes);
+cudaError_t m1_lane_bidir_phase(const M1Params& fwd, const M1Params& bwd, void* workspace, size_t ws_bytes,
+                                bool summary, cudaStream_t stream);
 // Device status of the lane kernels (1: a bounded staging wait expired),
 // cleared by the read.
 int m1_lane_status_and_clear();

@@ -282,6 +282,87 @@ def selective_scan_segment_summary(u, delta, A, B, C, delta_bias=None, delta_sof
     return hf, hb, sdt
 
 
+class BidirectionalSegment:
+    """The bidirectional sum of one segment of a sequence split over devices,
+    in two phases around the exchange of segment summaries (CUDA tensors,
+    the layouts of ``selective_scan``).
+
+    ``summary()`` returns (h_fwd, h_bwd, dt_sum) as
+    ``selective_scan_segment_summary`` does, from one shared pass that also
+    leaves its per-segment aggregates in a workspace this object holds;
+    ``finish(h0_fwd, h0_bwd)`` returns out_fwd + out_bwd from those incoming
+    states as ``selective_scan_bidirectional_sum`` does, reusing the
+    aggregates instead of re-reading the inputs for them.  The input tensors
+    must not change between the two calls.  Where the two-phase kernels do
+    not cover the shape (state > 16, length not a multiple of 4, unaligned
+    tensors) both phases run the one-call functions instead."""
+
+    def __init__(self, u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False):
+        if u.device.type != "cuda":
+            raise ValueError("BidirectionalSegment needs CUDA tensors")
+        batch, dim, length = u.shape
+        state = A.shape[1]
+        dev = u.device
+        B = _bc4(B, batch, state, length)
+        C = _bc4(C, batch, state, length)
+        opt = lambda t: None if t is None else _prep(t, dev)  # noqa: E731
+        self.u, self.delta, self.A, self.B, self.C = (_prep(t, dev) for t in (u, delta, A, B, C))
+        self.D, self.z, self.delta_bias = opt(D), opt(z), opt(delta_bias)
+        self.delta_softplus = bool(delta_softplus)
+        self.shape = (batch, dim, state)
+        self.dims = _ffi.ArmScanDims(batch, dim, length, state, self.B.shape[1] if self.B.dim() == 4 else 1)
+        self.ws_bytes = _ffi.bidirectional_workspace_bytes(self.dims)
+        aligned = all(t is None or t.data_ptr() % 16 == 0
+                      for t in (self.u, self.delta, self.A, self.B, self.C, self.D, self.z,
+                                self.delta_bias))
+        if not aligned:
+            self.ws_bytes = 0
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev) if self.ws_bytes else None
+        self._summarised = False
+
+    def summary(self):
+        if self.ws is None:
+            self._summarised = True
+            return selective_scan_segment_summary(self.u, self.delta, self.A, self.B, self.C,
+                                                  delta_bias=self.delta_bias,
+                                                  delta_softplus=self.delta_softplus)
+        hf = self.u.new_empty(self.shape)
+        hb = self.u.new_empty(self.shape)
+        sdt = self.u.new_empty(self.shape[:2])
+        with _on_device(self.u):
+            _ffi.bidirectional_summary_raw(
+                self.dims, self.u.data_ptr(), self.delta.data_ptr(), self.A.data_ptr(),
+                self.B.data_ptr(), self.C.data_ptr(), _ptr(self.delta_bias), self.delta_softplus,
+                self.ws.data_ptr(), self.ws_bytes, hf.data_ptr(), hb.data_ptr(), sdt.data_ptr(),
+                _stream(self.u))
+        _CALLS["n"] += 1
+        self._summarised = True
+        return hf, hb, sdt
+
+    def finish(self, h0_fwd=None, h0_bwd=None):
+        if not self._summarised:
+            raise RuntimeError("BidirectionalSegment.finish() before summary()")
+        dev = self.u.device
+        h0 = [None if t is None else _prep(t, dev) for t in (h0_fwd, h0_bwd)]
+        for t in h0:
+            if t is not None and tuple(t.shape) != self.shape:
+                raise ValueError(f"initial states must be {self.shape}, got {tuple(t.shape)}")
+        if self.ws is None:
+            return selective_scan_bidirectional_sum(self.u, self.delta, self.A, self.B, self.C,
+                                                    D=self.D, z=self.z, delta_bias=self.delta_bias,
+                                                    delta_softplus=self.delta_softplus,
+                                                    initial_states=tuple(h0))
+        out = torch.empty_like(self.u)
+        with _on_device(self.u):
+            _ffi.bidirectional_finish_raw(
+                self.dims, self.u.data_ptr(), self.delta.data_ptr(), self.A.data_ptr(),
+                self.B.data_ptr(), self.C.data_ptr(), _ptr(self.D), _ptr(self.z),
+                _ptr(self.delta_bias), self.delta_softplus, self.ws.data_ptr(), self.ws_bytes,
+                _ptr(h0[0]), _ptr(h0[1]), out.data_ptr(), _stream(self.u))
+        _CALLS["n"] += 1
+        return out
+
+
 def causal_conv1d_silu(x, weight, bias=None):
     """silu(causal depthwise conv1d(x) + bias) over (batch, dim, len) CUDA
     rows; weight (dim, kernel) or (dim, 1, kernel) as nn.Conv1d stores it.

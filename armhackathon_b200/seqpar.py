@@ -15,10 +15,11 @@ Per call:
   3. rank r folds the summaries of ranks < r (forward) and > r (backward)
      into its incoming states;
   4. rank r scans its segment in both directions from those states.
-With the library's own functions on CUDA tensors and merge "sum", step 1 is
-one call (``selective_scan_segment_summary``: both directions' end states and
-the dt sum from one pass over the segment) and step 4 another (``selective_scan_bidirectional_sum``
-with both incoming states).
+With the library's own functions on CUDA tensors and merge "sum", steps 1
+and 4 are the two phases of one ``BidirectionalSegment``: step 1 reads the
+segment once for both directions' end states and the dt sum, keeping that
+pass's per-chunk aggregates on the device, and step 4 rescans both
+directions from the incoming states without a second pass to rebuild them.
 The fold is exact algebra, so the result equals the unsplit bidirectional
 scan up to fp32 rounding.  No rank waits on another except inside the
 all_gather, whose timeout is the process group's.
@@ -103,7 +104,10 @@ def bidirectional_scan_seqpar(u, delta, A, B, C, D=None, z=None, delta_bias=None
         scan_fn, "__module__", "") == __package__ + ".op" and getattr(
         state_fn, "__module__", "") == __package__ + ".op"
     if fused:
-        packed = segment_summary(u, delta, A, B, C, delta_bias, delta_softplus)
+        from .op import BidirectionalSegment
+        seg = BidirectionalSegment(u, delta, A, B, C, D=D, z=z, **skw)
+        hf, hb, sdt = seg.summary()
+        packed = torch.cat([hf, hb, sdt[..., None]], dim=-1).contiguous()
     else:
         hf = state_fn(u, delta, A, B, C, **skw)
         hb = state_fn(u, delta, A, B, C, reverse=True, **skw)
@@ -118,9 +122,7 @@ def bidirectional_scan_seqpar(u, delta, A, B, C, D=None, z=None, delta_bias=None
     h_in_f = fold_carries(h_f, sums, A, rank, False) if rank > 0 else None
     h_in_b = fold_carries(h_b, sums, A, rank, True) if rank < world - 1 else None
     if fused:
-        from .op import selective_scan_bidirectional_sum
-        return selective_scan_bidirectional_sum(u, delta, A, B, C, initial_states=(h_in_f, h_in_b),
-                                                **kw)
+        return seg.finish(h_in_f, h_in_b)
     yf = scan_fn(u, delta, A, B, C, initial_state=h_in_f, **kw)
     yb = scan_fn(u, delta, A, B, C, reverse=True, initial_state=h_in_b, **kw)
     return yf + yb if merge == "sum" else (yf, yb)

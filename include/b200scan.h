@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define ARM_SCAN_ABI_VERSION 12u
+#define ARM_SCAN_ABI_VERSION 13u
 
 /* Return codes (0-5: reference arm-scan-ffi/src/lib.rs:53-58). */
 #define ARM_SCAN_OK 0
@@ -92,7 +92,7 @@ typedef struct ArmMamba3Dims {
 } ArmMamba3Dims;
 
 /* Replaces arm_scan_abi_version, arm-scan-ffi/src/lib.rs:37-40.  Returns
- * ARM_SCAN_ABI_VERSION (12). */
+ * ARM_SCAN_ABI_VERSION (13). */
 uint32_t arm_scan_abi_version(void);
 
 /* Message describing the calling thread's most recent non-zero return. */
@@ -388,6 +388,31 @@ int arm_scan_selective_scan_segment_summary_f32_async(
 int arm_scan_causal_conv1d_silu_f32_async(size_t batch, size_t dim, size_t len, size_t kernel,
                                           const float* x, const float* weight, const float* bias,
                                           float* out, void* stream);
+
+/* Extension (no counterpart in the reference): the bidirectional sum in two
+ * phases around an exchange, for a sequence split over devices.  The
+ * summary phase makes one shared pass over this segment and returns its
+ * summary (both traversals' end states from zero, the per-row sum of dt) --
+ * as arm_scan_selective_scan_segment_summary_f32_async does -- and keeps
+ * the pass's per-segment aggregates in the caller's workspace; the finish
+ * phase, given the incoming states folded from the other segments'
+ * summaries, writes out = forward + reverse outputs (as the sum entry with
+ * h0_fwd / h0_bwd) without a second pass over the inputs to rebuild those
+ * aggregates.  The workspace (16-byte aligned, the size reported by
+ * ..._bidirectional_workspace_bytes for the same dims, 0 when the shape is
+ * not covered: d_state > 16 or len not a multiple of 4) must not change
+ * between the two calls.  Device pointers, stream-ordered; code 3 if the
+ * tensors are not 16-byte aligned. */
+size_t arm_scan_selective_scan_bidirectional_workspace_bytes(const ArmScanDims* dims);
+int arm_scan_selective_scan_bidirectional_summary_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
+    const float* c, const float* delta_bias, int delta_softplus, void* workspace, size_t ws_bytes,
+    float* last_fwd, float* last_bwd, float* dt_sum, void* stream);
+int arm_scan_selective_scan_bidirectional_finish_f32_async(
+    const ArmScanDims* dims, const float* u, const float* delta, const float* a, const float* b,
+    const float* c, const float* d_skip, const float* z, const float* delta_bias, int delta_softplus,
+    void* workspace, size_t ws_bytes, const float* h0_fwd, const float* h0_bwd, float* out,
+    void* stream);
 
 /* Extension: shape of the Mamba-3 mixer whose prologue
  * arm_scan_mamba3_mixer_prologue_f32_async runs (one B/C group; rank 1 for

@@ -23,7 +23,7 @@ def declared_functions():
 
 def test_library_loads_with_abi_v12():
     lib = _ffi.load()
-    assert lib.arm_scan_abi_version() == 12
+    assert lib.arm_scan_abi_version() == 13
     assert _ffi.lib_path().name == "libb200scan.so"
 
 
@@ -231,3 +231,17 @@ def test_angle_entries_reject_lengths_beyond_the_grid():
                                               dummy, 1 << 40, None)
     assert rc == 2
     assert b"chunks" in lib.arm_scan_last_error()
+
+
+def test_bidirectional_workspace_bytes_host_only():
+    """The two-phase form's workspace size is a host computation that needs
+    no device for the shapes it does not cover (state > 16, length not a
+    multiple of 4, no dims): 0.  (Covered shapes need the device's SM count
+    for their segment plan; the GPU tests check those.)"""
+    from armhackathon_b200 import _ffi
+    lib = _ffi.load()
+    f = lambda *d: _ffi.bidirectional_workspace_bytes(_ffi.ArmScanDims(*d))  # noqa: E731
+    assert f(1, 64, 1027, 16, 1) == 0
+    assert f(1, 64, 1024, 32, 1) == 0
+    assert f(1, 64, 0, 16, 1) == 0
+    assert lib.arm_scan_selective_scan_bidirectional_workspace_bytes(None) == 0

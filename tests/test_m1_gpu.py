@@ -515,3 +515,41 @@ def test_segment_summary_end_states_and_dt_sums(L):
     assert rel_err(hb.cpu().numpy(), wlb) <= REL_TOL
     dt = np.logaddexp(0.0, x["delta"].astype(np.float64) + x["delta_bias"][None, :, None])
     assert rel_err(sdt.cpu().numpy(), dt.sum(-1)) <= REL_TOL
+
+
+@pytest.mark.parametrize("segments,shape", [("auto", (2, 40, 1024, 16)), ("4", (2, 40, 1024, 16)),
+                                            ("1", (1, 24, 512, 8)), ("auto", (1, 24, 1027, 16))])
+def test_bidirectional_segment_two_phases(segments, shape, knobs):
+    """The two-phase bidirectional form (summary, then finish from incoming
+    states over the same workspace) equals the one-call functions it
+    splits: the summary is bit-identical to the segment-summary entry and
+    the finish to the sum entry with the same incoming states -- on the
+    lane kernel with the automatic and forced segment counts, and on the
+    one-call fallback (length not a multiple of 4)."""
+    if segments != "auto":
+        knobs(m1_segments=int(segments))
+    B, D, L, N = shape
+    x = _slow_decay_case(B, D, L, N, seed=L + N)
+    t = cuda(x)
+    a = arm()
+    seg = a.BidirectionalSegment(t["u"], t["delta"], t["A"], t["B"], t["C"], D=t["D"], z=t["z"],
+                                 delta_bias=t["delta_bias"], delta_softplus=True)
+    assert (seg.ws_bytes > 0) == (L % 4 == 0)
+    with pytest.raises(RuntimeError):
+        seg.finish()
+    got = seg.summary()
+    want = a.selective_scan_segment_summary(t["u"], t["delta"], t["A"], t["B"], t["C"],
+                                            delta_bias=t["delta_bias"], delta_softplus=True)
+    for g, w in zip(got, want):
+        assert torch.equal(g, w)
+    g = torch.Generator().manual_seed(5)
+    h0f = torch.randn(B, D, N, generator=g).cuda()
+    h0b = torch.randn(B, D, N, generator=g).cuda()
+    for init in [(h0f, h0b), (None, h0b), (h0f, None), (None, None)]:
+        y = seg.finish(*init)
+        ref = a.selective_scan_bidirectional_sum(**t, initial_states=init)
+        assert torch.equal(y, ref)
+    # and against the oracle: forward from h0f plus reverse from h0b
+    yf, _ = oracle.m1_scan(**x, h0=h0f.cpu().numpy(), nthreads=8)
+    yb, _ = oracle.m1_scan(**x, h0=h0b.cpu().numpy(), reverse=True, nthreads=8)
+    assert rel_err(seg.finish(h0f, h0b).cpu().numpy(), yf + yb) <= REL_TOL
