@@ -26,7 +26,7 @@ __all__ = [
     "selective_state_update", "selective_scan_final_state", "mamba3_mixer_prologue",
     "selective_scan_bidirectional_sum", "selective_scan_bidirectional_final_states",
     "mamba3_mixer_scan", "mamba3_mimo_x_scan", "selective_scan_segment_summary",
-    "causal_conv1d_silu", "BidirectionalSegment",
+    "causal_conv1d_silu", "BidirectionalSegment", "selective_scan_ss2d",
 ]
 
 _LAZY = {
@@ -34,7 +34,7 @@ _LAZY = {
     "selective_state_update": ".op", "selective_scan_final_state": ".op",
     "selective_scan_bidirectional_sum": ".op",
     "selective_scan_segment_summary": ".op", "causal_conv1d_silu": ".op",
-    "BidirectionalSegment": ".op",
+    "BidirectionalSegment": ".op", "selective_scan_ss2d": ".op",
     "selective_scan_bidirectional_final_states": ".op",
     "bidirectional_scan": ".bidirectional",
     "ss2d_scan": ".ss2d", "use_arm_scan": ".ss2d",

@@ -144,6 +144,9 @@ def _bind(lib):
     lib.arm_scan_selective_scan_bidirectional_finish_f32_async.restype = ctypes.c_int
     lib.arm_scan_selective_scan_bidirectional_finish_f32_async.argtypes = [
         ctypes.POINTER(ArmScanDims), *([_VP] * 8), _I, _VP, ctypes.c_size_t, _VP, _VP, _VP, _VP]
+    lib.arm_scan_selective_scan_ss2d_f32_async.restype = ctypes.c_int
+    lib.arm_scan_selective_scan_ss2d_f32_async.argtypes = [
+        ctypes.POINTER(ArmScanDims), ctypes.c_size_t, ctypes.c_size_t, *([_VP] * 7), _I, _I, _VP, _VP]
     lib.arm_scan_mamba3_mixer_prologue_f32_async.restype = ctypes.c_int
     lib.arm_scan_mamba3_mixer_prologue_f32_async.argtypes = [
         ctypes.POINTER(ArmMamba3MixerDims), *([_VP] * 4), ctypes.c_float, ctypes.c_float,
@@ -388,6 +391,15 @@ def bidirectional_finish_raw(dims, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_d,
         "arm_scan_selective_scan_bidirectional_finish_f32_async")
 
 
+def ss2d_raw(dims, h, w, ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, ptr_d, ptr_delta_bias,
+             delta_softplus, merge_mean, ptr_out, stream):
+    """Mamba-1 SS2D cross-scan of grids read in place (device pointers)."""
+    _check(load().arm_scan_selective_scan_ss2d_f32_async(
+        ctypes.byref(dims), int(h), int(w), ptr_u, ptr_delta, ptr_a, ptr_b, ptr_c, _n(ptr_d),
+        _n(ptr_delta_bias), int(bool(delta_softplus)), int(bool(merge_mean)), ptr_out, _n(stream)),
+        "arm_scan_selective_scan_ss2d_f32_async")
+
+
 def set_device(ordinal):
     """Device the synchronous host-buffer calls of this thread run on (-1:
     the current CUDA device)."""
@@ -454,7 +466,8 @@ def exported_symbols():
             "arm_scan_mamba3_noncausal_f32_async", "arm_scan_causal_conv1d_silu_f32_async",
             "arm_scan_set_device", "arm_scan_selective_scan_bidirectional_workspace_bytes",
             "arm_scan_selective_scan_bidirectional_summary_f32_async",
-            "arm_scan_selective_scan_bidirectional_finish_f32_async"]
+            "arm_scan_selective_scan_bidirectional_finish_f32_async",
+            "arm_scan_selective_scan_ss2d_f32_async"]
 
 
 if __name__ == "__main__":  # pragma: no cover

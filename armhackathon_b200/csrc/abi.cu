@@ -790,6 +790,42 @@ int arm_scan_selective_scan_bidirectional_finish_f32_async(
                               ws_bytes, out, nullptr, nullptr, nullptr, h0_fwd, h0_bwd, false, stream);
 }
 
+int arm_scan_selective_scan_ss2d_f32_async(
+    const ArmScanDims* dims, size_t h, size_t w, const float* u, const float* delta,
+    const float* a, const float* b, const float* c, const float* d_skip, const float* delta_bias,
+    int delta_softplus, int merge_mean, float* out, void* stream) {
+    if (!dims || !u || !delta || !a || !b || !c || !out)
+        return fail(ARM_SCAN_ERR_NULL_POINTER, "a required pointer is null");
+    M1Counts cnt;
+    int rc = m1_validate(dims, &cnt);
+    if (rc) return rc;
+    if (h == 0 || w == 0 || h * w != dims->len || dims->len / h != w)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "len %zu is not h %zu x w %zu", dims->len, h, w);
+    if (dims->state > 16)
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE, "the SS2D entry covers d_state <= 16");
+    if (dims->groups > 1 && (dims->dim / dims->groups) % 8 != 0)
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE,
+                    "the SS2D entry needs channels per B/C group to be a multiple of 8");
+    if (w > 0x7fffffffu || dims->batch > 65535 || dims->dim > 65535u * 8)
+        return fail(ARM_SCAN_ERR_INVALID_DIMS, "grid too large for the SS2D entry");
+    std::vector<void*> p = {const_cast<float*>(u), const_cast<float*>(delta),
+                            const_cast<float*>(a), const_cast<float*>(b),
+                            const_cast<float*>(c), const_cast<float*>(d_skip),
+                            nullptr, const_cast<float*>(delta_bias)};
+    M1Params base = m1_params(dims, p, delta_softplus, 0);
+    M1Params f = base, r = base;
+    f.out = out;
+    r.reverse = 1;
+    r.out = nullptr;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = m1_bidir_sum_launch(f, r, 0, s);
+    if (e != cudaSuccess) return cuda_fail(e, "SS2D row-major traversals");
+    e = m1_ss2d_cols_launch(f, static_cast<int64_t>(h), static_cast<int64_t>(w), merge_mean ? 0.25f : 1.f, s);
+    if (e == cudaErrorNotSupported)
+        return fail(ARM_SCAN_ERR_BACKEND_UNAVAILABLE, "the SS2D column kernels do not cover this shape");
+    return e == cudaSuccess ? ARM_SCAN_OK : cuda_fail(e, "SS2D column-major traversals");
+}
+
 int arm_scan_mamba3_scan_f32(const ArmMamba3Dims* dims, const float* q, const float* k,
                              const float* v, const float* adt, const float* dt, const float* trap,
                              const float* q_bias, const float* k_bias, const float* cos,

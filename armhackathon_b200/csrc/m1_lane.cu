@@ -878,6 +878,306 @@ cudaError_t m1_lane_bidir_phase(const M1Params& fwd, const M1Params& bwd, void* 
     return lane_bidir_run(fwd, bwd, S, static_cast<float*>(workspace), summary, !summary, stream);
 }
 
+// ---- SS2D: the column-major traversals of an (h, w) grid, in place ---------
+// The column-major ordering visits t = c*h + r, so its natural segments of h
+// steps are the grid's columns.  A CTA owns 32 adjacent columns of 8
+// channels of one batch entry (one thread per (channel, column), all of its
+// states in registers) and sweeps the columns' steps in blocks of kColRB
+// rows of the grid, staged by cp.async into double-buffered shared memory:
+// each staged row of u, delta, B_n, C_n is 128 contiguous bytes of the grid,
+// and B/C are staged once for the CTA's 8 channels.  The grid is read in
+// place, with no transposed copy.  Three launches per ordering:
+//  1. m1_col_pass1: per column, from zero, the forward end state, the
+//     reverse end state (sum over r of prod_{r'<r} a_{r'} * b_r, from the
+//     same sweep: one exp per (step, state)) and the sum of dt -- written as
+//     the aggregates of forward segment c and of reverse segment w-1-c;
+//  2. m1_lane_carry per direction (segments in traversal order);
+//  3. m1_col_pass2: per column, the forward rescan from its incoming state
+//     and then the reverse one, both adding y + D u into the output, the
+//     second also applying the merge scale.
+struct ColGrid {
+    int64_t h, w;
+    float scale;  // applied to the finished sum (1 for "sum", 0.25 for "mean")
+};
+
+constexpr int kColWarps = 8;
+constexpr int kColRB = 8;  // grid rows per staged block
+// one stage: B, C [kColRB][16][32], u, delta [kColWarps][kColRB][32] (floats)
+constexpr int kColBC = kColRB * 16 * 32;
+constexpr int kColX = kColWarps * kColRB * 32;
+constexpr int kColStage = 2 * kColBC + 2 * kColX;
+constexpr size_t kColSmem = 2 * kColStage * sizeof(float);
+
+struct ColCta {
+    int64_t bi, grp, c0, d0, c, d, row;
+    bool live;  // this thread's (channel, column) exists
+};
+
+__device__ __forceinline__ ColCta col_cta(const M1Params& p, const ColGrid& g) {
+    ColCta t;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    t.c0 = static_cast<int64_t>(blockIdx.x) * 32;
+    t.d0 = static_cast<int64_t>(blockIdx.y) * kColWarps;
+    t.bi = blockIdx.z;
+    t.c = t.c0 + lane;
+    t.d = t.d0 + warp;
+    t.live = t.c < g.w && t.d < p.dim;
+    t.row = t.bi * p.dim + (t.d < p.dim ? t.d : p.dim - 1);
+    // a CTA's channels share one B/C group (channel blocks never straddle
+    // a group: the launcher checks dim/groups % kColWarps == 0 or groups 1)
+    t.grp = t.d0 / (p.dim / p.groups);
+    return t;
+}
+
+__device__ __forceinline__ void cp_async_f(float* dst, const float* src, bool pred, int bytes) {
+    const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+    if (bytes == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(src), "r"(pred ? 16 : 0));
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(src), "r"(pred ? 4 : 0));
+}
+
+// Stage grid rows [r0, r0 + kColRB) of this CTA's columns: B (and C when
+// WITH_C), u and delta.  VEC: 16-byte copies (w % 4 == 0, aligned tensors).
+template <bool VEC, bool WITH_C>
+__device__ __forceinline__ void col_stage(const M1Params& p, const ColGrid& g, const ColCta& t, int64_t r0,
+                                          float* st) {
+    constexpr int U = VEC ? 4 : 1;     // floats per copy
+    constexpr int PER = 32 / U;        // copies per staged row
+    const int64_t L = p.len, N = p.state;
+    const float* Bg = p.B + (t.bi * p.groups + t.grp) * N * L + t.c0;
+    const float* Cg = p.C + (t.bi * p.groups + t.grp) * N * L + t.c0;
+    const int nbc = kColRB * static_cast<int>(N) * PER;
+    for (int i = threadIdx.x; i < nbc; i += kColWarps * 32) {
+        const int r = i / (static_cast<int>(N) * PER), n = (i / PER) % static_cast<int>(N), j = (i % PER) * U;
+        const bool ok = r0 + r < g.h && t.c0 + j < g.w;
+        const int64_t o = ok ? n * L + (r0 + r) * g.w + j : 0;
+        cp_async_f(st + (r * 16 + n) * 32 + j, Bg + o, ok, U * 4);
+        if (WITH_C) cp_async_f(st + kColBC + (r * 16 + n) * 32 + j, Cg + o, ok, U * 4);
+    }
+    constexpr int nx = kColWarps * kColRB * PER;
+    for (int i = threadIdx.x; i < nx; i += kColWarps * 32) {
+        const int wv = i / (kColRB * PER), r = (i / PER) % kColRB, j = (i % PER) * U;
+        const bool ok = r0 + r < g.h && t.c0 + j < g.w && t.d0 + wv < p.dim;
+        const int64_t o = ok ? ((t.bi * p.dim + t.d0 + wv) * L + (r0 + r) * g.w + t.c0 + j) : 0;
+        const int so = (wv * kColRB + r) * 32 + j;
+        cp_async_f(st + 2 * kColBC + so, p.u + o, ok, U * 4);
+        cp_async_f(st + 2 * kColBC + kColX + so, p.delta + o, ok, U * 4);
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+}
+
+__device__ __forceinline__ void col_params(const M1Params& p, const ColCta& t, float (&a2)[16], float& bias,
+                                           float& dsk) {
+    const int64_t N = p.state, d = t.d < p.dim ? t.d : p.dim - 1;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) a2[n] = n < N ? __ldg(p.A + d * N + n) * kLog2e : 0.f;
+    bias = p.delta_bias ? __ldg(p.delta_bias + d) : 0.f;
+    dsk = p.d_skip ? __ldg(p.d_skip + d) : 0.f;
+}
+
+// Sweep the CTA's columns over the grid rows, forward (REV false) or
+// backward, calling blk(r0, rows, stage) for every staged block of rows.
+template <bool VEC, bool WITH_C, bool REV, typename Blk>
+__device__ __forceinline__ void col_sweep(const M1Params& p, const ColGrid& g, const ColCta& t, float* sm,
+                                          Blk blk) {
+    const int64_t nb = (g.h + kColRB - 1) / kColRB;
+    auto block_r0 = [&](int64_t k) { return (REV ? nb - 1 - k : k) * kColRB; };
+    col_stage<VEC, WITH_C>(p, g, t, block_r0(0), sm);
+    for (int64_t k = 0; k < nb; ++k) {
+        float* st = sm + (k & 1) * kColStage;
+        if (k + 1 < nb) {
+            col_stage<VEC, WITH_C>(p, g, t, block_r0(k + 1), sm + ((k + 1) & 1) * kColStage);
+            asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        }
+        __syncthreads();
+        const int64_t r0 = block_r0(k);
+        const int rows = static_cast<int>(g.h - r0 < kColRB ? g.h - r0 : kColRB);
+        blk(r0, rows, st);
+        __syncthreads();  // the stage is refilled two blocks later
+    }
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kColWarps * 32, 2) m1_col_pass1(M1Params p, ColGrid g, LaneWs wf, LaneWs wb) {
+    extern __shared__ __align__(16) float csm[];
+    const ColCta t = col_cta(p, g);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t N = p.state, rows = p.batch * p.dim;
+    float a2[16], bias, dsk;
+    col_params(p, t, a2, bias, dsk);
+    // states in pairs (n, n+1) for the packed fp32x2 instructions; a
+    // missing odd partner keeps b = 0, so its state stays 0
+    float2 hf[8], hr[8], pr[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        hf[k] = make_float2(0.f, 0.f);
+        hr[k] = make_float2(0.f, 0.f);
+        pr[k] = make_float2(1.f, 1.f);
+    }
+    float dts = 0.f;
+    auto step = [&](int q, const float* st) {
+        const int xo = (warp * kColRB + q) * 32 + lane;
+        float dt = st[2 * kColBC + kColX + xo] + bias;
+        if (p.delta_softplus) dt = softplus_fast(dt);
+        const float du = dt * st[2 * kColBC + xo];
+        dts += dt;
+        const float2 dt2 = make_float2(dt, dt), du2 = make_float2(du, du);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if (2 * k < N) {
+                const float2 x = fmul2(dt2, make_float2(a2[2 * k], a2[2 * k + 1]));
+                const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                const float* bp = st + (q * 16 + 2 * k) * 32 + lane;
+                const float2 bu = fmul2(du2, make_float2(bp[0], 2 * k + 1 < N ? bp[32] : 0.f));
+                hf[k] = ffma2(e, hf[k], bu);
+                hr[k] = ffma2(pr[k], bu, hr[k]);
+                pr[k] = fmul2(pr[k], e);
+            }
+        }
+    };
+    col_sweep<VEC, false, false>(p, g, t, csm, [&](int64_t, int rows, const float* st) {
+        if (rows == kColRB) {
+#pragma unroll
+            for (int q = 0; q < kColRB; ++q) step(q, st);
+        } else {
+            for (int q = 0; q < rows; ++q) step(q, st);
+        }
+    });
+    if (!t.live) return;
+    const int64_t sf = t.c, sb = g.w - 1 - t.c;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        if (2 * k < N) {
+            wf.hend[(sf * rows + t.row) * 16 + 2 * k] = hf[k].x;
+            wb.hend[(sb * rows + t.row) * 16 + 2 * k] = hr[k].x;
+        }
+        if (2 * k + 1 < N) {
+            wf.hend[(sf * rows + t.row) * 16 + 2 * k + 1] = hf[k].y;
+            wb.hend[(sb * rows + t.row) * 16 + 2 * k + 1] = hr[k].y;
+        }
+    }
+    wf.dtsum[sf * rows + t.row] = dts;
+    wb.dtsum[sb * rows + t.row] = dts;
+}
+
+template <bool VEC, bool REV>
+__device__ __forceinline__ void col_rescan(const M1Params& p, const ColGrid& g, const ColCta& t, float* sm,
+                                           const float (&a2)[16], float bias, float dsk, const float* hin,
+                                           float scale) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t L = p.len, N = p.state;
+    // states in pairs (n, n+1) for the packed fp32x2 instructions; a
+    // missing odd partner has h = b = c = 0
+    float2 h[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+        h[k] = make_float2((t.live && 2 * k < N) ? hin[2 * k] : 0.f, (t.live && 2 * k + 1 < N) ? hin[2 * k + 1] : 0.f);
+    float* out = p.out + t.row * L + t.c;
+    auto step = [&](int q, const float* st) {
+        const int xo = (warp * kColRB + q) * 32 + lane;
+        float dt = st[2 * kColBC + kColX + xo] + bias;
+        if (p.delta_softplus) dt = softplus_fast(dt);
+        const float uu = st[2 * kColBC + xo];
+        const float du = dt * uu;
+        const float2 dt2 = make_float2(dt, dt), du2 = make_float2(du, du);
+        float2 y = make_float2(dsk * uu, 0.f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if (2 * k < N) {
+                const bool odd = 2 * k + 1 < N;
+                const float2 x = fmul2(dt2, make_float2(a2[2 * k], a2[2 * k + 1]));
+                const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                const float* bp = st + (q * 16 + 2 * k) * 32 + lane;
+                const float2 bu = fmul2(du2, make_float2(bp[0], odd ? bp[32] : 0.f));
+                h[k] = ffma2(e, h[k], bu);
+                y = ffma2(make_float2(bp[kColBC], odd ? bp[kColBC + 32] : 0.f), h[k], y);
+            }
+        }
+        return y.x + y.y;
+    };
+    col_sweep<VEC, true, REV>(p, g, t, sm, [&](int64_t r0, int rows, const float* st) {
+        if (rows == kColRB) {
+            // the block's output values are requested before its steps run
+            float ov[kColRB];
+#pragma unroll
+            for (int i = 0; i < kColRB; ++i) ov[i] = t.live ? out[(r0 + i) * g.w] : 0.f;
+#pragma unroll
+            for (int i = 0; i < kColRB; ++i) {
+                const int q = REV ? kColRB - 1 - i : i;
+                const float y = step(q, st);
+                if (t.live) out[(r0 + q) * g.w] = (ov[q] + y) * scale;
+            }
+        } else {
+            for (int i = 0; i < rows; ++i) {
+                const int q = REV ? rows - 1 - i : i;
+                const float y = step(q, st);
+                if (t.live) {
+                    float* o = out + (r0 + q) * g.w;
+                    *o = (*o + y) * scale;
+                }
+            }
+        }
+    });
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kColWarps * 32, 2) m1_col_pass2(M1Params p, ColGrid g, LaneWs wf, LaneWs wb) {
+    extern __shared__ __align__(16) float csm[];
+    const ColCta t = col_cta(p, g);
+    const int64_t rows = p.batch * p.dim;
+    float a2[16], bias, dsk;
+    col_params(p, t, a2, bias, dsk);
+    const int64_t cc = t.c < g.w ? t.c : g.w - 1;
+    col_rescan<VEC, false>(p, g, t, csm, a2, bias, dsk, wf.hin + (cc * rows + t.row) * 16, 1.f);
+    col_rescan<VEC, true>(p, g, t, csm, a2, bias, dsk, wb.hin + ((g.w - 1 - cc) * rows + t.row) * 16, g.scale);
+}
+
+cudaError_t m1_ss2d_cols_launch(const M1Params& p, int64_t h, int64_t w, float scale, cudaStream_t stream) {
+    if (p.state > 16 || p.state < 1 || h < 1 || w < 1 || h * w != p.len || p.dim % p.groups != 0 ||
+        p.batch > 65535 || (p.dim + kColWarps - 1) / kColWarps > 65535 || w > 0x7fffffff)
+        return cudaErrorNotSupported;
+    // a CTA's 8 channels must share one B/C group
+    if (p.groups > 1 && (p.dim / p.groups) % kColWarps != 0) return cudaErrorNotSupported;
+    const int64_t rows = p.batch * p.dim;
+    const int S = static_cast<int>(w);
+    const size_t per = 2 * static_cast<size_t>(S) * rows * 16 + static_cast<size_t>(S) * rows;
+    const bool vec = w % 4 == 0 && m1_pointers_aligned16(p);
+    auto k1 = vec ? m1_col_pass1<true> : m1_col_pass1<false>;
+    auto k2 = vec ? m1_col_pass2<true> : m1_col_pass2<false>;
+    cudaError_t e;
+    if ((e = allow_smem(k1, kColSmem)) != cudaSuccess || (e = allow_smem(k2, kColSmem)) != cudaSuccess) return e;
+    LaneWsAlloc alloc(stream);
+    if ((e = alloc.get(2 * per * sizeof(float))) != cudaSuccess) return e;
+    LaneWs wf, wb;
+    carve(static_cast<float*>(alloc.raw), S, rows, &wf);
+    carve(static_cast<float*>(alloc.raw) + per, S, rows, &wb);
+    const ColGrid g{h, w, scale};
+    const dim3 grid(static_cast<unsigned>((w + 31) / 32), static_cast<unsigned>((p.dim + kColWarps - 1) / kColWarps),
+                    static_cast<unsigned>(p.batch));
+    M1Params q = p;
+    q.h0 = nullptr;
+    q.last_state = nullptr;
+    q.dt_sum = nullptr;
+    k1<<<grid, kColWarps * 32, kColSmem, stream>>>(q, g, wf, wb);
+    note_launch();
+    e = cudaGetLastError();
+    const dim3 cg(static_cast<unsigned>((rows * q.state + 255) / 256));
+    if (e == cudaSuccess) e = launch_pdl(m1_lane_carry<false>, cg, dim3(256), stream, q, wf, S);
+    if (e == cudaSuccess) note_launch();
+    if (e == cudaSuccess) e = launch_pdl(m1_lane_carry<false>, cg, dim3(256), stream, q, wb, S);
+    if (e == cudaSuccess) note_launch();
+    if (e == cudaSuccess) {
+        k2<<<grid, kColWarps * 32, kColSmem, stream>>>(q, g, wf, wb);
+        note_launch();
+        e = cudaGetLastError();
+    }
+    const cudaError_t ef = alloc.release();
+    return e != cudaSuccess ? e : ef;
+}
+
 int m1_lane_status_and_clear() {
     int v = 0, z = 0;
     cudaMemcpyFromSymbol(&v, g_m1_status, sizeof(int));

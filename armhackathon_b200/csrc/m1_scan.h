@@ -74,6 +74,11 @@ cudaError_t m1_lane_bidir_launch(const M1Params& fwd, const M1Params& bwd, int s
 int m1_lane_bidir_plan(const M1Params& shape, size_t* ws_bytes);
 cudaError_t m1_lane_bidir_phase(const M1Params& fwd, const M1Params& bwd, void* workspace, size_t ws_bytes,
                                 bool summary, cudaStream_t stream);
+// SS2D column-major traversals (forward and reverse) of (batch, dim, h, w)
+// grids read in place, added into p.out (which holds the row-major
+// traversals' sum); the finished sum is multiplied by scale.
+// cudaErrorNotSupported when d_state > 16 or the dims do not fit.
+cudaError_t m1_ss2d_cols_launch(const M1Params& p, int64_t h, int64_t w, float scale, cudaStream_t stream);
 // Device status of the lane kernels (1: a bounded staging wait expired),
 // cleared by the read.
 int m1_lane_status_and_clear();

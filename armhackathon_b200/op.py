@@ -363,6 +363,36 @@ class BidirectionalSegment:
         return out
 
 
+def selective_scan_ss2d(u, delta, A, B, C, D=None, delta_bias=None, delta_softplus=True,
+                        merge="sum"):
+    """The Mamba-1 SS2D cross-scan, merged "sum" or "mean", in one library call
+    over CUDA grids read in place: u, delta (b, d, h, w); B, C (b, n, h, w)
+    or (b, groups, n, h, w); A (d, n); D, delta_bias (d,).  The row-major
+    traversals run as a bidirectional sum over the grid's natural order, the
+    column-major ones as per-column segments (no transposed copies)."""
+    if u.device.type != "cuda" or u.dim() != 4:
+        raise ValueError("selective_scan_ss2d takes (b, d, h, w) CUDA grids")
+    if merge not in ("sum", "mean"):
+        raise ValueError(f"merge must be 'sum' or 'mean', got {merge!r}")
+    b, d, h, w = u.shape
+    state = A.shape[1]
+    dev = u.device
+    G = 1 if B.dim() == 4 else B.shape[1]
+    bc = lambda t: _prep(t, dev).reshape(b, G, state, h * w)  # noqa: E731
+    us, ds = _prep(u, dev), _prep(delta, dev)
+    As, Bs, Cs = _prep(A, dev), bc(B), bc(C)
+    Ds = None if D is None else _prep(D, dev)
+    db = None if delta_bias is None else _prep(delta_bias, dev)
+    out = torch.empty_like(us)
+    dims = _ffi.ArmScanDims(b, d, h * w, state, G)
+    with _on_device(us):
+        _ffi.ss2d_raw(dims, h, w, us.data_ptr(), ds.data_ptr(), As.data_ptr(), Bs.data_ptr(),
+                      Cs.data_ptr(), _ptr(Ds), _ptr(db), delta_softplus, merge == "mean",
+                      out.data_ptr(), _stream(us))
+    _CALLS["n"] += 1
+    return out
+
+
 def causal_conv1d_silu(x, weight, bias=None):
     """silu(causal depthwise conv1d(x) + bias) over (batch, dim, len) CUDA
     rows; weight (dim, kernel) or (dim, 1, kernel) as nn.Conv1d stores it.

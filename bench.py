@@ -59,6 +59,28 @@ CFG4A = dict(kind="ss2d", batch=8, heads=6, dv=64, dqk=64, len=128 * 128, rank=1
              grid=128)
 CFG3 = dict(batch=8, heads=24, dv=64, dqk=128, len=8192, rank=4, pairs=64)
 CFG4B = dict(batch=1, dim=1536, len=262144, state=16)
+# the reference's SS2D workload (bench/bench_ss2d.py): level-1 grid, seed batch 4
+M1SS2D = dict(batch=4, dim=96, h=384, w=320, state=16)
+
+
+def m1_ss2d_inputs(dev):
+    """Seeded grids of the SS2D workload: u, delta, A, B, C, D, delta_bias."""
+    import torch
+    w = M1SS2D
+    g = torch.Generator(device=dev).manual_seed(0)
+    rn = lambda *s: torch.randn(*s, generator=g, device=dev)  # noqa: E731
+    gs = (w["batch"], w["dim"], w["h"], w["w"])
+    u, delta = rn(*gs), rn(*gs) * 0.5
+    Bm, Cm = rn(w["batch"], w["state"], w["h"], w["w"]), rn(w["batch"], w["state"], w["h"], w["w"])
+    A = -torch.exp(torch.rand(w["dim"], w["state"], generator=g, device=dev) * 2)
+    return (u, delta, A, Bm, Cm, torch.ones(w["dim"], device=dev),
+            torch.full((w["dim"],), -2.0, device=dev))
+
+
+def m1_ss2d_bytes(w):
+    """u, delta and out (batch, dim, h, w) plus B, C (batch, state, h, w), fp32."""
+    L = w["h"] * w["w"]
+    return 4.0 * L * w["batch"] * (3 * w["dim"] + 2 * w["state"])
 
 # algorithmic bytes and flops of the configurations (per call)
 CFG_BYTES = {"cfg0": 50.80e6, "cfg2_bf16": 117.4e6, "cfg2_fp32": None, "cfg3": 1772e6,
@@ -455,6 +477,18 @@ def cpu_port(kind, nthreads):
                                            dtype=np.float32, nthreads=nthreads))
         scale = w["batch"] * w["len"] / (B * L)
         return t * 1e3 * scale, f"1x{H} heads, L {L} (x{scale:g} extrapolated)"
+    if kind == "m1_ss2d":
+        w = M1SS2D
+        d, n, L = 16, w["state"], w["h"] * w["w"]
+        inp = dict(u=f(1, d, L), delta=f(1, d, L), A=-np.tile(np.arange(1, n + 1, dtype=np.float32),
+                                                              (d, 1)),
+                   B=f(1, n, L), C=f(1, n, L), D=np.ones(d, np.float32),
+                   delta_bias=np.full(d, -2.0, np.float32))
+        # two orderings, each a fused bidirectional pair (the reference's composition)
+        t = 2 * clock(lambda: oracle.m1_scan_bidir(**inp, delta_softplus=True, dtype=np.float32,
+                                                   nthreads=nthreads))
+        scale = w["batch"] * w["dim"] / d
+        return t * 1e3 * scale, f"1x{d} channels of the grid (x{scale:g} extrapolated)"
     raise ValueError(kind)
 
 
@@ -550,6 +584,25 @@ def config_suite(args, dev, hbm, clocks):
            "cfg4b")
     del x
     torch.cuda.empty_cache()
+
+    # Mamba-1 SS2D at the reference's level-1 diffusion grid, one call
+    w = M1SS2D
+    u, delta, A, Bm, Cm, Dk, bias = m1_ss2d_inputs(dev)
+    ms, how = time_call(lambda: arm.ss2d_scan(u, delta, A, Bm, Cm, D=Dk, delta_bias=bias),
+                        steps, args.warmup)
+    record("m1_ss2d", ms, how, m1_ss2d_bytes(w), None, bf16_peak,
+           "Mamba-1 SS2D, four traversals summed, B4 D96 N16 on the reference's level-1 "
+           "384x320 diffusion grid, fp32, grids read in place", "m1_ss2d")
+    from armhackathon_b200.ss2d import grid_to_views, views_to_grid
+
+    def views_path():
+        both = arm.selective_scan_bidirectional_sum(
+            grid_to_views(u), grid_to_views(delta), A, grid_to_views(Bm), grid_to_views(Cm), D=Dk,
+            delta_bias=bias, delta_softplus=True)
+        rs, cs = views_to_grid(both[:w["batch"]], both[w["batch"]:], w["h"], w["w"])
+        return rs + cs
+    out["m1_ss2d"]["views_path_ms"], _ = time_call(views_path, steps, args.warmup, graph=False)
+    del u, delta, Bm, Cm
 
     # Mamba-3 mixer prologue (in_proj output -> scan inputs) at config 2's shape
     wm = dict(kind="mixer", batch=4, heads=24, dv=64, dqk=128, len=4096, rank=1, pairs=32)
@@ -658,7 +711,8 @@ def profile_case(case):
     on B2 x L4096 (1/8 of it); cfg2_bf16 / cfg2_fp32 -- config 2 on the
     tensor-core and the fp32 chunk path; cfg4a -- config 4a's SS2D; mixer --
     the Mamba-3 mixer prologue at config 2's shape; tile_prefill -- the
-    headline scan on the row-tile fallback kernel."""
+    headline scan on the row-tile fallback kernel; m1_ss2d -- the Mamba-1
+    SS2D workload (level-1 diffusion grid)."""
     import torch
     import armhackathon_b200 as arm
     dev = torch.device("cuda", 0)
@@ -694,6 +748,9 @@ def profile_case(case):
         wm = dict(kind="mixer", batch=4, heads=24, dv=64, dqk=128, len=4096, rank=1, pairs=32)
         xm = mixer_inputs(wm, dev)
         f = lambda: arm.mamba3_mixer_prologue(**xm)  # noqa: E731
+    elif case == "m1_ss2d":
+        u, delta, A, Bm, Cm, Dk, bias = m1_ss2d_inputs(dev)
+        f = lambda: arm.ss2d_scan(u, delta, A, Bm, Cm, D=Dk, delta_bias=bias)  # noqa: E731
     elif case == "tile_prefill":
         from armhackathon_b200 import _ffi
         _ffi.set_kernel_override("m1_kernel", _ffi.M1_KERNELS["tile"])
@@ -732,7 +789,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the config-1 HF prefill tok/s measurement")
     ap.add_argument("--profile-case", choices=["prefill", "bidir_slice", "cfg3_eighth", "cfg2_bf16",
-                                               "cfg2_fp32", "cfg4a", "mixer", "tile_prefill"],
+                                               "cfg2_fp32", "cfg4a", "mixer", "tile_prefill",
+                                               "m1_ss2d"],
                     help="run three calls of one small case and exit (the program the ncu "
                          "captures in profiles/ run)")
     args = ap.parse_args()

@@ -414,6 +414,19 @@ int arm_scan_selective_scan_bidirectional_finish_f32_async(
     void* workspace, size_t ws_bytes, const float* h0_fwd, const float* h0_bwd, float* out,
     void* stream);
 
+/* Extension: the Mamba-1 SS2D cross-scan (reference python/arm_scan/ss2d.py
+ * :102-167, merges "sum" and "mean") as one call over grids read in place:
+ * u, delta (batch, dim, h, w), B, C (batch, groups, state, h, w), A (dim,
+ * state), d_skip, delta_bias (dim) nullable; no z.  out (batch, dim, h, w)
+ * = row-major forward + backward + column-major forward + backward, each
+ * with its own D u (times 0.25 when merge_mean).  dims->len must be h * w;
+ * d_state <= 16 and, with groups > 1, dim / groups a multiple of 8 (code 3
+ * otherwise).  Device pointers, stream-ordered. */
+int arm_scan_selective_scan_ss2d_f32_async(
+    const ArmScanDims* dims, size_t h, size_t w, const float* u, const float* delta,
+    const float* a, const float* b, const float* c, const float* d_skip, const float* delta_bias,
+    int delta_softplus, int merge_mean, float* out, void* stream);
+
 /* Extension: shape of the Mamba-3 mixer whose prologue
  * arm_scan_mamba3_mixer_prologue_f32_async runs (one B/C group; rank 1 for
  * SISO).  The in_proj row is W = 2*heads*headdim + 2*rank*d_state + 3*heads

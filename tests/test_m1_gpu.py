@@ -238,10 +238,11 @@ def test_ss2d_golden_planes():
             assert err < 1e-4, (name, key, err)
         want = sum(d[k] for k in ("out_row_fwd", "out_row_bwd", "out_col_fwd", "out_col_bwd"))
         for merge, scale in (("sum", 1.0), ("mean", 0.25)):
-            got = a.ss2d_scan(t("u"), t("delta"), t("A"), t("B"), t("C"), D=t("D"),
-                              delta_bias=t("delta_bias"), merge=merge)
-            err = np.abs(got.cpu().numpy().astype(np.float64) - scale * want).max()
-            assert err < 4e-4, (name, merge, err)
+            for fn in (a.ss2d_scan, a.selective_scan_ss2d):  # views / in place
+                got = fn(t("u"), t("delta"), t("A"), t("B"), t("C"), D=t("D"),
+                         delta_bias=t("delta_bias"), merge=merge)
+                err = np.abs(got.cpu().numpy().astype(np.float64) - scale * want).max()
+                assert err < 4e-4, (name, merge, fn.__name__, err)
 
 
 def test_config0_full_size_properties():
@@ -553,3 +554,75 @@ def test_bidirectional_segment_two_phases(segments, shape, knobs):
     yf, _ = oracle.m1_scan(**x, h0=h0f.cpu().numpy(), nthreads=8)
     yb, _ = oracle.m1_scan(**x, h0=h0b.cpu().numpy(), reverse=True, nthreads=8)
     assert rel_err(seg.finish(h0f, h0b).cpu().numpy(), yf + yb) <= REL_TOL
+
+
+def _grid_views(x, h, w):
+    """(b, c, h, w) numpy grid -> its row-major and column-major sequences."""
+    b, c = x.shape[:2]
+    return x.reshape(b, c, h * w), np.ascontiguousarray(x.transpose(0, 1, 3, 2)).reshape(b, c, w * h)
+
+
+@pytest.mark.parametrize("shape", [(2, 32, 48, 40, 16, 2), (1, 12, 17, 33, 8, 1), (1, 8, 5, 64, 16, 1),
+                                   (1, 24, 16, 20, 16, 2)])
+def test_ss2d_in_place_vs_oracle(shape):
+    """The one-call Mamba-1 SS2D (row-major traversals over the grid's own
+    order, column-major ones per column, all summed into one output) against
+    the f64 oracle run on the four traversal sequences: with groups, with
+    d_state 8, with a grid whose length is not a multiple of 4 (the row
+    traversals then take the fallback kernels), with columns longer than
+    rows, and with groups of 12 channels, which the in-place call rejects
+    (code 3) and ``ss2d_scan`` runs through stacked views.  ``ss2d_scan``
+    itself takes the in-place call only for grids that fill the GPU."""
+    B, D, H, W, N, G = shape
+    rng = np.random.default_rng(H * W)
+    f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    u, delta = f(B, D, H, W), (f(B, D, H, W) * 0.5).astype(np.float32)
+    Bm, Cm = f(B, G, N, H, W), f(B, G, N, H, W)
+    A = (-rng.uniform(0.1, 2.0, (D, N))).astype(np.float32)
+    Dk, bias = f(D), (rng.uniform(-3, -1, D)).astype(np.float32)
+    want = np.zeros((B, D, H, W))
+    for order in ("row", "col"):
+        pick = 0 if order == "row" else 1
+        us, ds = _grid_views(u, H, W)[pick], _grid_views(delta, H, W)[pick]
+        bs = _grid_views(Bm.reshape(B, G * N, H, W), H, W)[pick].reshape(B, G, N, H * W)
+        cs = _grid_views(Cm.reshape(B, G * N, H, W), H, W)[pick].reshape(B, G, N, H * W)
+        for rev in (False, True):
+            y, _ = oracle.m1_scan(us, ds, A, bs, cs, D=Dk, delta_bias=bias, delta_softplus=True,
+                                  reverse=rev, nthreads=8)
+            y = y.reshape(B, D, H, W) if order == "row" else y.reshape(B, D, W, H).transpose(0, 1, 3, 2)
+            want += y
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    args = (t(u), t(delta), t(A), t(Bm), t(Cm))
+    kw = dict(D=t(Dk), delta_bias=t(bias))
+    for merge, scale in (("sum", 1.0), ("mean", 0.25)):
+        got = arm().ss2d_scan(*args, **kw, merge=merge)
+        assert rel_err(got.cpu().numpy(), scale * want) <= REL_TOL
+        if G > 1 and (D // G) % 8:
+            with pytest.raises(RuntimeError, match="code 3"):
+                arm().selective_scan_ss2d(*args, **kw, merge=merge)
+        else:
+            got = arm().selective_scan_ss2d(*args, **kw, merge=merge)
+            assert rel_err(got.cpu().numpy(), scale * want) <= REL_TOL
+
+
+def test_ss2d_production_shape_matches_planes():
+    """The reference's SS2D workload shape (level-2 grid 192 x 160, inner
+    dim 192, d_state 16): the in-place call's sum equals the sum of the four
+    planes of merge="none" (transposed views through the bidirectional
+    kernels), at batch 1 (called directly: ``ss2d_scan`` takes views there)
+    and at batch 4 (through ``ss2d_scan``)."""
+    g = torch.Generator(device="cuda").manual_seed(7)
+    d, h, w, n = 192, 192, 160, 16
+    r = lambda *s: torch.randn(*s, generator=g, device="cuda")  # noqa: E731
+    a = arm()
+    for b, fn in ((1, a.selective_scan_ss2d), (4, a.ss2d_scan)):
+        u, delta = r(b, d, h, w), r(b, d, h, w) * 0.5
+        Bm, Cm = r(b, n, h, w), r(b, n, h, w)
+        A = -torch.rand(d, n, generator=g, device="cuda") * 2 - 0.1
+        Dk, bias = r(d), torch.rand(d, generator=g, device="cuda") * 2 - 3
+        planes = a.ss2d_scan(u, delta, A, Bm, Cm, D=Dk, delta_bias=bias, merge="none")
+        calls = a.kernel_calls()
+        got = fn(u, delta, A, Bm, Cm, D=Dk, delta_bias=bias, merge="sum")
+        assert a.kernel_calls() == calls + 1  # one library call
+        want = sum(p.double() for p in planes)
+        assert rel_err(got.cpu().numpy(), want.cpu().numpy()) <= REL_TOL
