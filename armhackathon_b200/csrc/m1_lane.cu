@@ -898,6 +898,8 @@ cudaError_t m1_lane_bidir_phase(const M1Params& fwd, const M1Params& bwd, void* 
 struct ColGrid {
     int64_t h, w;
     float scale;  // applied to the finished sum (1 for "sum", 0.25 for "mean")
+    int64_t hs;   // grid rows per sub-segment (a multiple of kColRB)
+    int k;        // sub-segments per column (1: a column is one segment)
 };
 
 constexpr int kColWarps = 8;
@@ -910,13 +912,18 @@ constexpr size_t kColSmem = 2 * kColStage * sizeof(float);
 
 struct ColCta {
     int64_t bi, grp, c0, d0, c, d, row;
-    bool live;  // this thread's (channel, column) exists
+    int64_t r_lo, r_hi;  // grid rows of this CTA's sub-segment
+    int j;               // its index within the column
+    bool live;           // this thread's (channel, column) exists
 };
 
 __device__ __forceinline__ ColCta col_cta(const M1Params& p, const ColGrid& g) {
     ColCta t;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    t.c0 = static_cast<int64_t>(blockIdx.x) * 32;
+    t.c0 = static_cast<int64_t>(blockIdx.x / g.k) * 32;
+    t.j = static_cast<int>(blockIdx.x % g.k);
+    t.r_lo = t.j * g.hs;
+    t.r_hi = t.r_lo + g.hs < g.h ? t.r_lo + g.hs : g.h;
     t.d0 = static_cast<int64_t>(blockIdx.y) * kColWarps;
     t.bi = blockIdx.z;
     t.c = t.c0 + lane;
@@ -950,7 +957,7 @@ __device__ __forceinline__ void col_stage(const M1Params& p, const ColGrid& g, c
     const int nbc = kColRB * static_cast<int>(N) * PER;
     for (int i = threadIdx.x; i < nbc; i += kColWarps * 32) {
         const int r = i / (static_cast<int>(N) * PER), n = (i / PER) % static_cast<int>(N), j = (i % PER) * U;
-        const bool ok = r0 + r < g.h && t.c0 + j < g.w;
+        const bool ok = r0 + r < t.r_hi && t.c0 + j < g.w;
         const int64_t o = ok ? n * L + (r0 + r) * g.w + j : 0;
         cp_async_f(st + (r * 16 + n) * 32 + j, Bg + o, ok, U * 4);
         if (WITH_C) cp_async_f(st + kColBC + (r * 16 + n) * 32 + j, Cg + o, ok, U * 4);
@@ -958,7 +965,7 @@ __device__ __forceinline__ void col_stage(const M1Params& p, const ColGrid& g, c
     constexpr int nx = kColWarps * kColRB * PER;
     for (int i = threadIdx.x; i < nx; i += kColWarps * 32) {
         const int wv = i / (kColRB * PER), r = (i / PER) % kColRB, j = (i % PER) * U;
-        const bool ok = r0 + r < g.h && t.c0 + j < g.w && t.d0 + wv < p.dim;
+        const bool ok = r0 + r < t.r_hi && t.c0 + j < g.w && t.d0 + wv < p.dim;
         const int64_t o = ok ? ((t.bi * p.dim + t.d0 + wv) * L + (r0 + r) * g.w + t.c0 + j) : 0;
         const int so = (wv * kColRB + r) * 32 + j;
         cp_async_f(st + 2 * kColBC + so, p.u + o, ok, U * 4);
@@ -981,8 +988,8 @@ __device__ __forceinline__ void col_params(const M1Params& p, const ColCta& t, f
 template <bool VEC, bool WITH_C, bool REV, typename Blk>
 __device__ __forceinline__ void col_sweep(const M1Params& p, const ColGrid& g, const ColCta& t, float* sm,
                                           Blk blk) {
-    const int64_t nb = (g.h + kColRB - 1) / kColRB;
-    auto block_r0 = [&](int64_t k) { return (REV ? nb - 1 - k : k) * kColRB; };
+    const int64_t nb = (t.r_hi - t.r_lo + kColRB - 1) / kColRB;
+    auto block_r0 = [&](int64_t k) { return t.r_lo + (REV ? nb - 1 - k : k) * kColRB; };
     col_stage<VEC, WITH_C>(p, g, t, block_r0(0), sm);
     for (int64_t k = 0; k < nb; ++k) {
         float* st = sm + (k & 1) * kColStage;
@@ -994,7 +1001,7 @@ __device__ __forceinline__ void col_sweep(const M1Params& p, const ColGrid& g, c
         }
         __syncthreads();
         const int64_t r0 = block_r0(k);
-        const int rows = static_cast<int>(g.h - r0 < kColRB ? g.h - r0 : kColRB);
+        const int rows = static_cast<int>(t.r_hi - r0 < kColRB ? t.r_hi - r0 : kColRB);
         blk(r0, rows, st);
         __syncthreads();  // the stage is refilled two blocks later
     }
@@ -1047,7 +1054,10 @@ __global__ void __launch_bounds__(kColWarps * 32, 2) m1_col_pass1(M1Params p, Co
         }
     });
     if (!t.live) return;
-    const int64_t sf = t.c, sb = g.w - 1 - t.c;
+    // one segment per column: the carries' segment order (forward c,
+    // reverse w-1-c); sub-segments: (column, sub-segment) for m1_col_fold
+    const int64_t sf = g.k == 1 ? t.c : t.c * g.k + t.j;
+    const int64_t sb = g.k == 1 ? g.w - 1 - t.c : sf;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         if (2 * k < N) {
@@ -1065,8 +1075,8 @@ __global__ void __launch_bounds__(kColWarps * 32, 2) m1_col_pass1(M1Params p, Co
 
 template <bool VEC, bool REV>
 __device__ __forceinline__ void col_rescan(const M1Params& p, const ColGrid& g, const ColCta& t, float* sm,
-                                           const float (&a2)[16], float bias, float dsk, const float* hin,
-                                           float scale) {
+                                           const float (&a2)[16], float bias, float dsk,
+                                           const float (&hin)[16], float scale) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t L = p.len, N = p.state;
     // states in pairs (n, n+1) for the packed fp32x2 instructions; a
@@ -1074,7 +1084,7 @@ __device__ __forceinline__ void col_rescan(const M1Params& p, const ColGrid& g, 
     float2 h[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-        h[k] = make_float2((t.live && 2 * k < N) ? hin[2 * k] : 0.f, (t.live && 2 * k + 1 < N) ? hin[2 * k + 1] : 0.f);
+        h[k] = make_float2(hin[2 * k], hin[2 * k + 1]);
     float* out = p.out + t.row * L + t.c;
     auto step = [&](int q, const float* st) {
         const int xo = (warp * kColRB + q) * 32 + lane;
@@ -1123,16 +1133,73 @@ __device__ __forceinline__ void col_rescan(const M1Params& p, const ColGrid& g, 
     });
 }
 
+// Incoming state of this thread's sub-segment in one direction: the
+// column's incoming state (from the carries) advanced over the sub-segments
+// the traversal visits before this one (forward: j' < j; reverse: j' > j).
+template <bool REV>
+__device__ __forceinline__ void col_sub_hin(const M1Params& p, const ColGrid& g, const ColCta& t,
+                                            const float (&a2)[16], const float* col_hin, const LaneWs& sub,
+                                            float (&h)[16]) {
+    const int64_t N = p.state, rows = p.batch * p.dim;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) h[n] = (t.live && n < N) ? col_hin[n] : 0.f;
+    if (g.k == 1 || !t.live) return;
+    const int first = REV ? g.k - 1 : 0;
+    for (int jj = first; jj != t.j; jj += REV ? -1 : 1) {
+        const int64_t si = (t.c * g.k + jj) * rows + t.row;
+        const float ds = sub.dtsum[si];
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+            if (n < N) h[n] = fmaf(ex2_approx(a2[n] * ds), h[n], sub.hend[si * 16 + n]);
+    }
+}
+
 template <bool VEC>
-__global__ void __launch_bounds__(kColWarps * 32, 2) m1_col_pass2(M1Params p, ColGrid g, LaneWs wf, LaneWs wb) {
+__global__ void __launch_bounds__(kColWarps * 32, 2) m1_col_pass2(M1Params p, ColGrid g, LaneWs wf, LaneWs wb,
+                                                                  LaneWs subf, LaneWs subr) {
     extern __shared__ __align__(16) float csm[];
     const ColCta t = col_cta(p, g);
     const int64_t rows = p.batch * p.dim;
     float a2[16], bias, dsk;
     col_params(p, t, a2, bias, dsk);
     const int64_t cc = t.c < g.w ? t.c : g.w - 1;
-    col_rescan<VEC, false>(p, g, t, csm, a2, bias, dsk, wf.hin + (cc * rows + t.row) * 16, 1.f);
-    col_rescan<VEC, true>(p, g, t, csm, a2, bias, dsk, wb.hin + ((g.w - 1 - cc) * rows + t.row) * 16, g.scale);
+    float h0[16];
+    col_sub_hin<false>(p, g, t, a2, wf.hin + (cc * rows + t.row) * 16, subf, h0);
+    col_rescan<VEC, false>(p, g, t, csm, a2, bias, dsk, h0, 1.f);
+    col_sub_hin<true>(p, g, t, a2, wb.hin + ((g.w - 1 - cc) * rows + t.row) * 16, subr, h0);
+    col_rescan<VEC, true>(p, g, t, csm, a2, bias, dsk, h0, g.scale);
+}
+
+// Sub-segments -> column aggregates (time-split columns only): per (column,
+// row, state) the forward fold over j = 0..k-1 and the reverse one over
+// j = k-1..0 of the sub-segments' end states from zero, and the column's
+// sum of dt, in the carries' segment order (forward c, reverse w-1-c).
+__global__ void m1_col_fold(M1Params p, ColGrid g, LaneWs subf, LaneWs subr, LaneWs wf, LaneWs wb) {
+    const int64_t rows = p.batch * p.dim, N = p.state;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= g.w * rows * N) return;
+    const int64_t n = i % N, row = (i / N) % rows, c = i / (N * rows);
+    const float a = __ldg(p.A + (row % p.dim) * N + n) * kLog2e;
+    float hf = 0.f, hr = 0.f, dts = 0.f;
+    for (int jj = 0; jj < g.k; ++jj) {
+        const int64_t sf = (c * g.k + jj) * rows + row, sr = (c * g.k + (g.k - 1 - jj)) * rows + row;
+        hf = fmaf(ex2_approx(a * subf.dtsum[sf]), hf, subf.hend[sf * 16 + n]);
+        hr = fmaf(ex2_approx(a * subr.dtsum[sr]), hr, subr.hend[sr * 16 + n]);
+        dts += subf.dtsum[sf];
+    }
+    wf.hend[(c * rows + row) * 16 + n] = hf;
+    wb.hend[((g.w - 1 - c) * rows + row) * 16 + n] = hr;
+    if (n == 0) {
+        wf.dtsum[c * rows + row] = dts;
+        wb.dtsum[(g.w - 1 - c) * rows + row] = dts;
+    }
+}
+
+static int64_t sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
+    return sms;
 }
 
 cudaError_t m1_ss2d_cols_launch(const M1Params& p, int64_t h, int64_t w, float scale, cudaStream_t stream) {
@@ -1143,34 +1210,65 @@ cudaError_t m1_ss2d_cols_launch(const M1Params& p, int64_t h, int64_t w, float s
     if (p.groups > 1 && (p.dim / p.groups) % kColWarps != 0) return cudaErrorNotSupported;
     const int64_t rows = p.batch * p.dim;
     const int S = static_cast<int>(w);
+    // Split the columns in time when (columns / 32) x (channels / 8) x batch
+    // CTAs would not give every SM two: about four CTAs per SM after the split.
+    const int64_t base = ((w + 31) / 32) * ((p.dim + kColWarps - 1) / kColWarps) * p.batch;
+    const int64_t sms = sm_count();
+    int64_t k = 1;
+    if (base < 2 * sms) {
+        k = (4 * sms + base - 1) / base;
+        const int64_t max_k = (h + kColRB - 1) / kColRB;
+        k = k < max_k ? k : max_k;
+    }
+    const int64_t hs = ((((h + k - 1) / k) + kColRB - 1) / kColRB) * kColRB;
+    k = (h + hs - 1) / hs;
+    if (((w + 31) / 32) * k > 0x7fffffff) return cudaErrorNotSupported;
     const size_t per = 2 * static_cast<size_t>(S) * rows * 16 + static_cast<size_t>(S) * rows;
+    // sub-segment aggregates: forward and reverse end states, one dt sum
+    const size_t sub_n = static_cast<size_t>(S) * k * rows;
+    const size_t sub = k > 1 ? 2 * sub_n * 16 + sub_n : 0;
     const bool vec = w % 4 == 0 && m1_pointers_aligned16(p);
     auto k1 = vec ? m1_col_pass1<true> : m1_col_pass1<false>;
     auto k2 = vec ? m1_col_pass2<true> : m1_col_pass2<false>;
     cudaError_t e;
     if ((e = allow_smem(k1, kColSmem)) != cudaSuccess || (e = allow_smem(k2, kColSmem)) != cudaSuccess) return e;
     LaneWsAlloc alloc(stream);
-    if ((e = alloc.get(2 * per * sizeof(float))) != cudaSuccess) return e;
-    LaneWs wf, wb;
-    carve(static_cast<float*>(alloc.raw), S, rows, &wf);
-    carve(static_cast<float*>(alloc.raw) + per, S, rows, &wb);
-    const ColGrid g{h, w, scale};
-    const dim3 grid(static_cast<unsigned>((w + 31) / 32), static_cast<unsigned>((p.dim + kColWarps - 1) / kColWarps),
-                    static_cast<unsigned>(p.batch));
+    if ((e = alloc.get((2 * per + sub) * sizeof(float))) != cudaSuccess) return e;
+    float* raw = static_cast<float*>(alloc.raw);
+    LaneWs wf, wb, subf{}, subr{};
+    carve(raw, S, rows, &wf);
+    carve(raw + per, S, rows, &wb);
+    if (k > 1) {
+        subf.hend = raw + 2 * per;
+        subr.hend = subf.hend + sub_n * 16;
+        subf.dtsum = subr.dtsum = subr.hend + sub_n * 16;
+    }
+    const ColGrid g{h, w, scale, hs, static_cast<int>(k)};
+    const dim3 grid(static_cast<unsigned>(((w + 31) / 32) * k),
+                    static_cast<unsigned>((p.dim + kColWarps - 1) / kColWarps), static_cast<unsigned>(p.batch));
     M1Params q = p;
     q.h0 = nullptr;
     q.last_state = nullptr;
     q.dt_sum = nullptr;
-    k1<<<grid, kColWarps * 32, kColSmem, stream>>>(q, g, wf, wb);
+    if (k > 1)
+        k1<<<grid, kColWarps * 32, kColSmem, stream>>>(q, g, subf, subr);
+    else
+        k1<<<grid, kColWarps * 32, kColSmem, stream>>>(q, g, wf, wb);
     note_launch();
     e = cudaGetLastError();
+    if (e == cudaSuccess && k > 1) {
+        const int64_t nf = w * rows * q.state;
+        m1_col_fold<<<static_cast<unsigned>((nf + 255) / 256), 256, 0, stream>>>(q, g, subf, subr, wf, wb);
+        note_launch();
+        e = cudaGetLastError();
+    }
     const dim3 cg(static_cast<unsigned>((rows * q.state + 255) / 256));
     if (e == cudaSuccess) e = launch_pdl(m1_lane_carry<false>, cg, dim3(256), stream, q, wf, S);
     if (e == cudaSuccess) note_launch();
     if (e == cudaSuccess) e = launch_pdl(m1_lane_carry<false>, cg, dim3(256), stream, q, wb, S);
     if (e == cudaSuccess) note_launch();
     if (e == cudaSuccess) {
-        k2<<<grid, kColWarps * 32, kColSmem, stream>>>(q, g, wf, wb);
+        k2<<<grid, kColWarps * 32, kColSmem, stream>>>(q, g, wf, wb, subf, subr);
         note_launch();
         e = cudaGetLastError();
     }

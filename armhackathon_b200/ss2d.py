@@ -3,13 +3,13 @@
 
 The four directions are two traversal pairs over two token orderings:
 row-major (h, w) and column-major (w, h), each scanned forward and backward.
-Merged ("sum" / "mean") on CUDA grids with enough columns x channels to
-fill the GPU, all four are one library call that reads the grids in place
-(``selective_scan_ss2d``: the row-major pair as a bidirectional sum over
-the grid's own order, the column-major pair as per-column segments).
-Otherwise (small grids, merge "none", a custom scan pair) both orderings are
-stacked on the batch axis as views, so one bidirectional call covers all
-four directions.  Time-varying inputs arrive grid-shaped.
+Merged ("sum" / "mean") on CUDA grids, all four are one library call that
+reads the grids in place (``selective_scan_ss2d``: the row-major pair as a
+bidirectional sum over the grid's own order, the column-major pair as
+per-column segments, split in time when the columns are too few to fill
+the GPU).  Otherwise (merge "none", a custom scan pair, d_state > 16) both
+orderings are stacked on the batch axis as views, so one bidirectional call
+covers all four directions.  Time-varying inputs arrive grid-shaped.
 """
 
 import torch
@@ -47,20 +47,12 @@ def scan_fn_arm(u, delta, A, B, C, D=None, delta_bias=None, delta_softplus=True)
                           delta_softplus=delta_softplus)
 
 
-# CTAs (32 columns x 8 channels each) per SM below which the per-column
-# sweeps leave the GPU underfilled and the stacked-views form is faster
-# (measured: batch 1 at 384 x 320, dim 96 -- 120 CTAs -- 1.03 ms in place
-# against 0.84 ms through views; batch 4 -- 480 CTAs -- 2.75 against 3.09).
-_MIN_COLUMN_CTAS = 2 * 148
-
-
 def _in_place_fits(u, A, B):
-    """Whether the one-call in-place SS2D covers (and suits) this shape."""
-    b, d, _, w = u.shape
+    """Whether the one-call in-place SS2D covers this shape: d_state <= 16
+    and, with B/C groups, a multiple of 8 channels per group."""
+    d = u.shape[1]
     groups = B.shape[1] if B.dim() == 5 else 1
-    if A.shape[1] > 16 or (groups > 1 and (d // groups) % 8 != 0):
-        return False
-    return ((w + 31) // 32) * ((d + 7) // 8) * b >= _MIN_COLUMN_CTAS
+    return A.shape[1] <= 16 and (groups == 1 or (d // groups) % 8 == 0)
 
 
 def ss2d_scan(u, delta, A, B, C, D=None, delta_bias=None, delta_softplus=True,

@@ -238,7 +238,7 @@ def test_ss2d_golden_planes():
             assert err < 1e-4, (name, key, err)
         want = sum(d[k] for k in ("out_row_fwd", "out_row_bwd", "out_col_fwd", "out_col_bwd"))
         for merge, scale in (("sum", 1.0), ("mean", 0.25)):
-            for fn in (a.ss2d_scan, a.selective_scan_ss2d):  # views / in place
+            for fn in (a.ss2d_scan, a.selective_scan_ss2d):
                 got = fn(t("u"), t("delta"), t("A"), t("B"), t("C"), D=t("D"),
                          delta_bias=t("delta_bias"), merge=merge)
                 err = np.abs(got.cpu().numpy().astype(np.float64) - scale * want).max()
@@ -571,8 +571,9 @@ def test_ss2d_in_place_vs_oracle(shape):
     d_state 8, with a grid whose length is not a multiple of 4 (the row
     traversals then take the fallback kernels), with columns longer than
     rows, and with groups of 12 channels, which the in-place call rejects
-    (code 3) and ``ss2d_scan`` runs through stacked views.  ``ss2d_scan``
-    itself takes the in-place call only for grids that fill the GPU."""
+    (code 3) and ``ss2d_scan`` runs through stacked views.  These grids are
+    too small to fill the GPU, so their columns are split in time (the
+    sub-segment fold); the production-shape test covers unsplit columns."""
     B, D, H, W, N, G = shape
     rng = np.random.default_rng(H * W)
     f = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
@@ -609,20 +610,20 @@ def test_ss2d_production_shape_matches_planes():
     """The reference's SS2D workload shape (level-2 grid 192 x 160, inner
     dim 192, d_state 16): the in-place call's sum equals the sum of the four
     planes of merge="none" (transposed views through the bidirectional
-    kernels), at batch 1 (called directly: ``ss2d_scan`` takes views there)
-    and at batch 4 (through ``ss2d_scan``)."""
+    kernels), at batch 1 (columns split in time) and at batch 4 (one segment
+    per column)."""
     g = torch.Generator(device="cuda").manual_seed(7)
     d, h, w, n = 192, 192, 160, 16
     r = lambda *s: torch.randn(*s, generator=g, device="cuda")  # noqa: E731
     a = arm()
-    for b, fn in ((1, a.selective_scan_ss2d), (4, a.ss2d_scan)):
+    for b in (1, 4):
         u, delta = r(b, d, h, w), r(b, d, h, w) * 0.5
         Bm, Cm = r(b, n, h, w), r(b, n, h, w)
         A = -torch.rand(d, n, generator=g, device="cuda") * 2 - 0.1
         Dk, bias = r(d), torch.rand(d, generator=g, device="cuda") * 2 - 3
         planes = a.ss2d_scan(u, delta, A, Bm, Cm, D=Dk, delta_bias=bias, merge="none")
         calls = a.kernel_calls()
-        got = fn(u, delta, A, Bm, Cm, D=Dk, delta_bias=bias, merge="sum")
+        got = a.ss2d_scan(u, delta, A, Bm, Cm, D=Dk, delta_bias=bias, merge="sum")
         assert a.kernel_calls() == calls + 1  # one library call
         want = sum(p.double() for p in planes)
         assert rel_err(got.cpu().numpy(), want.cpu().numpy()) <= REL_TOL
