@@ -698,7 +698,7 @@ def run_reference(args):
                     "d2h_bytes_per_step": 0}}
     if not args.no_configs:
         line["configs"] = {}
-        for k in ("cfg0", "cfg2", "cfg3", "cfg4a", "cfg4b"):
+        for k in ("cfg0", "cfg2", "cfg3", "cfg4a", "cfg4b", "m1_ss2d"):
             ms, sample = cpu_port(k, nthreads)
             line["configs"][k] = {"ms": ms, "cores": nthreads, "kind": "port", "sample": sample}
     print(json.dumps(line), flush=True)
