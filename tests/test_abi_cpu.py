@@ -1,4 +1,4 @@
-"""C-ABI library checks that need no GPU: it loads, reports ABI v12, exports
+"""C-ABI library checks that need no GPU: it loads, reports ABI v13, exports
 every entry point include/b200scan.h declares, and rejects bad arguments with
 the reference's codes before touching a device (reference
 kernel/arm-scan-ffi/src/lib.rs:53-58 and its FFI unit tests)."""
@@ -21,7 +21,7 @@ def declared_functions():
     return sorted(set(re.findall(r"\b(arm_scan_[a-z0-9_]+)\s*\(", text)))
 
 
-def test_library_loads_with_abi_v12():
+def test_library_loads_with_abi_v13():
     lib = _ffi.load()
     assert lib.arm_scan_abi_version() == 13
     assert _ffi.lib_path().name == "libb200scan.so"
@@ -245,3 +245,42 @@ def test_bidirectional_workspace_bytes_host_only():
     assert f(1, 64, 1024, 32, 1) == 0
     assert f(1, 64, 0, 16, 1) == 0
     assert lib.arm_scan_selective_scan_bidirectional_workspace_bytes(None) == 0
+
+
+def test_ss2d_entry_rejects_before_device_work():
+    """The one-call Mamba-1 SS2D entry: null pointers (code 1), a length that
+    is not h x w (code 2), d_state > 16 and groups whose channel count is
+    not a multiple of 8 (code 3) -- all host checks, no device touched."""
+    lib = _ffi.load()
+    buf = (ctypes.c_float * 8)()
+    p = ctypes.cast(buf, ctypes.c_void_p).value
+
+    def call(dims, h, w, out=p):
+        return lib.arm_scan_selective_scan_ss2d_f32_async(
+            ctypes.byref(dims), h, w, p, p, p, p, p, None, None, 1, 0, out, None)
+
+    assert call(_ffi.ArmScanDims(1, 8, 12, 16, 1), 3, 4, out=None) == 1
+    assert call(_ffi.ArmScanDims(1, 8, 12, 16, 1), 3, 5) == 2
+    assert call(_ffi.ArmScanDims(1, 8, 12, 16, 1), 0, 12) == 2
+    assert call(_ffi.ArmScanDims(1, 8, 12, 32, 1), 3, 4) == 3
+    assert call(_ffi.ArmScanDims(1, 24, 12, 16, 2), 3, 4) == 3
+    assert "multiple of 8" in lib.arm_scan_last_error().decode()
+
+
+def test_bidirectional_phases_reject_before_device_work():
+    """The two-phase bidirectional entries: null workspace or outputs (code
+    1) and shapes the two-phase kernels do not cover (code 3), checked on
+    the host."""
+    lib = _ffi.load()
+    buf = (ctypes.c_float * 8)()
+    p = ctypes.cast(buf, ctypes.c_void_p).value
+    dims = _ffi.ArmScanDims(1, 8, 64, 16, 1)
+    s = lib.arm_scan_selective_scan_bidirectional_summary_f32_async
+    f = lib.arm_scan_selective_scan_bidirectional_finish_f32_async
+    assert s(ctypes.byref(dims), p, p, p, p, p, None, 1, None, 0, p, p, p, None) == 1
+    assert s(ctypes.byref(dims), p, p, p, p, p, None, 1, p, 64, p, None, p, None) == 1
+    assert f(ctypes.byref(dims), p, p, p, p, p, None, None, None, 1, p, 64, None, None, None,
+             None) == 1
+    odd = _ffi.ArmScanDims(1, 8, 63, 16, 1)
+    assert f(ctypes.byref(odd), p, p, p, p, p, None, None, None, 1, p, 64, None, None, p,
+             None) == 3
