@@ -41,7 +41,18 @@
 
 namespace b200scan {
 
-__device__ int g_tc_status;  // 0 ok, 1 an mbarrier wait timed out
+__device__ int g_tc_status;
+#ifdef M3TC_PHASE_PROF
+__device__ unsigned long long g_tc_phase[64];
+#define W_MARK(slot) do { if ((threadIdx.x & 31) == 0) { long long _n = clock64(); atomicAdd(&g_tc_phase[(slot)], (unsigned long long)(_n - w_t)); } } while (0)
+#define W_SET() w_t = clock64()
+#define PH_MARK(i) do { if (threadIdx.x == 0) { long long _n = clock64(); if ((i) >= 0) atomicAdd(&g_tc_phase[(i)], (unsigned long long)(_n - ph_t)); ph_t = _n; } } while (0)
+#else
+#define PH_MARK(i) do {} while (0)
+#define W_MARK(slot) do {} while (0)
+#define W_SET() do {} while (0)
+#endif
+  // 0 ok, 1 an mbarrier wait timed out
 
 namespace {
 
@@ -174,6 +185,29 @@ __device__ __forceinline__ void ldg8(const float* g, float (&f)[8]) {
 // bulk prefetch of [g, g + bytes) into L2 (16-byte aligned, multiple of 16)
 __device__ __forceinline__ void prefetch_l2(const void* g, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(g), "r"(bytes) : "memory");
+}
+
+// bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)
+// from this GPU's global memory into shared memory, completing on `bar`
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+        "l"(src), "r"(bytes), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+        : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(bar))),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// line prefetches into L2 (the load/store unit, not the bulk-copy engine)
+// for short rows: one per 128 bytes of [g, g + bytes)
+__device__ __forceinline__ void prefetch_lines(const void* g, uint32_t bytes) {
+    const char* c = static_cast<const char*>(g);
+    for (uint32_t o = 0; o < bytes; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(c + o));
 }
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
@@ -726,9 +760,9 @@ __device__ __forceinline__ void st_release(unsigned int* p, unsigned int v) {
 
 // bounded wait until *flag >= want; false on expiry (about a second)
 __device__ __forceinline__ bool wait_flag(const unsigned int* flag, unsigned int want) {
-    for (uint32_t it = 0; it < (1u << 22); ++it) {
+    for (uint32_t it = 0; it < (1u << 25); ++it) {
         if (ld_acquire(flag) >= want) return true;
-        __nanosleep(256);
+        __nanosleep(32);
     }
     return false;
 }
@@ -918,6 +952,58 @@ __device__ __forceinline__ void tile_gates_r(const M3Params& p, int64_t bh, int6
         }
     }
     if (decay && lane == 0) *decay = ex2_approx(last);
+}
+
+// SISO gates over four warps (angles mode): thread j = tid < 128 takes step
+// j of the tile.  Part 1 (before the stage barrier): trapezoid scale,
+// gamma, and the warp-local inclusive prefix of the log2 decay into lcum,
+// the warp's total into wtot.  Part 2 (after it, same threads): add the
+// totals of the warps before, then the state weight and the chunk's decay.
+__device__ __forceinline__ void gates_split_1(const M3Params& p, int64_t bh, int64_t it0, float* lcum,
+                                              float* scl, float* gam, float* wtot) {
+    constexpr float kLog2eF = 1.4426950408889634f;
+    const int j = threadIdx.x, lane = j & 31;
+    const int64_t L = p.len, gate_base = bh * L;
+    const int64_t it = it0 + j;
+    float lv = 0.f, sc = 0.f, gm = 0.f;
+    if (it < L) {
+        const int64_t t = p.reverse ? L - 1 - it : it;
+        const int64_t g = gate_base + t;
+        const bool more = it + 1 < L;
+        const int64_t nx = more ? (p.reverse ? g - 1 : g + 1) : g;
+        const float dtg = __ldg(p.dt + g), trg = __ldg(p.trap + g);
+        const float dtn = __ldg(p.dt + nx), trn = __ldg(p.trap + nx);
+        const float adt = __ldg(p.adt + g);
+        const float gamma = dtg * sigmoid_f(trg);
+        const float shifted = more ? dtn * (1.f - sigmoid_f(trn)) : 0.f;
+        lv = adt * kLog2eF;
+        sc = gamma + shifted;
+        gm = gamma;
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(0xffffffffu, lv, o);
+        if (lane >= o) lv += v;
+    }
+    lcum[j] = lv;
+    scl[j] = sc;
+    gam[j] = gm;
+    if (lane == 31) wtot[j >> 5] = lv;
+}
+__device__ __forceinline__ void gates_split_2(float* lcum, const float* scl, float* wdec,
+                                              const float* wtot, float* decay) {
+    const int j = threadIdx.x, w = j >> 5;
+    float before = 0.f, last = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float v = wtot[q];
+        before += q < w ? v : 0.f;
+        last += v;
+    }
+    const float l = lcum[j] + before;
+    lcum[j] = l;
+    wdec[j] = ex2_approx(last - l) * scl[j];
+    if (j == 0) *decay = ex2_approx(last);
 }
 
 // X rows (fp32 inputs): SISO x = v; MIMO x_r = psi_r o v.
@@ -1188,108 +1274,92 @@ __device__ __forceinline__ void stage_qk_mimo(const M3Params& p, int64_t bi, int
 }
 
 // Rotated q, k rows of one chunk from raw angles, in two parts around the
-// gate pass's barrier.  Lane = step within the warp's quadrant
-// (j = 32 * (warp & 3) + lane); the warp pair (w, w + 4) splits the 16 dim
-// chunks (kc = 2 i + (warp >> 2)).  theta(step, pair) = theta0(chunk) +
-// prefix over the chunk's steps, in natural time order, of ta * dt: a warp
-// scan over lanes plus the totals of the quadrants before.
+// gate pass's barrier.  theta(step, pair) = theta0(chunk) + prefix over the
+// chunk's steps, in natural time order, of ta * dt.
 //
-// Part A (before the barrier): increments, warp scans, quadrant totals and
-// the chunk's theta0 row into shared memory.
+// Part A (before the barrier): thread = (pair pr = tid % 64, quarter qd =
+// tid / 64 of the tile's 128 rows); it walks its 32 rows in natural time
+// order, accumulating ta * dt (lanes = consecutive pairs, so every load is
+// one coalesced row segment and dt a broadcast), and writes the running sum
+// into a [128 rows][64 pairs] fp32 table in shared memory (16-byte chunk c
+// of row j stored at chunk c ^ (j % 16), so that both the row-wise writes
+// here and the per-row 16-byte reads of part B are free of bank conflicts).
+// The quarter's total goes to qtot, the chunk's theta0 row to th0s.
+template <bool SWZ>
+__device__ __forceinline__ uint32_t ang_tab_idx(int j, int pr) {
+    return SWZ ? static_cast<uint32_t>(j * 64 + ((((pr >> 2) ^ (j & 15)) << 2) | (pr & 3)))
+               : static_cast<uint32_t>(j * 64 + pr);
+}
+template <bool SWZ>
 __device__ __forceinline__ void ang_part_a(const M3Params& p, const float* ta, const float* theta0,
                                            int64_t bi, int64_t h, int64_t bh, int ch,
-                                           int n_chunks, int64_t it0, float (&th)[8][4],
-                                           float* qtot, float* th0s) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int qd = warp & 3, sub = warp >> 2;
+                                           int n_chunks, float* tab, float* qtot, float* th0s) {
+    const int tid = threadIdx.x, pr = tid & 63, qd = tid >> 6;
     const int64_t L = p.len, H = p.heads, NA = p.n_angles;
-    const int j = qd * 32 + lane;
-    const int64_t it = it0 + j;
-    const bool live = it < L;
     const bool rev = p.reverse != 0;
-    const int64_t t = live ? (rev ? L - 1 - it : it) : 0;
-    if (tid < NA) th0s[tid] = __ldg(theta0 + (bh * n_chunks + ch) * 64 + tid);
-    const float dtv = live ? __ldg(p.dt + bh * L + t) : 0.f;
-    const int64_t arow = p.angles_shared ? (bi * L + t) : ((bi * L + t) * H + h);
-    const float* tr = ta + arow * NA;
-    if ((NA & 3) == 0) {
+    int64_t lo, hi;
+    chunk_range(L, ch, p.reverse, lo, hi);
+    const int n = static_cast<int>(hi - lo);  // valid rows of the tile
+    if (tid < 64) th0s[tid] = tid < NA ? __ldg(theta0 + (bh * n_chunks + ch) * 64 + tid) : 0.f;
+    // rows of this quarter in natural time order: forward j = 32 qd + u,
+    // reverse j = 32 qd + 31 - u; natural time t(j) = lo + j / hi - 1 - j
+    const int jbase = rev ? qd * 32 + 31 : qd * 32;
+    const int jstep = rev ? -1 : 1;
+    const int64_t t0 = rev ? hi - 1 - jbase : lo + jbase;  // natural time of u = 0
+    const int64_t astep = p.angles_shared ? NA : H * NA;
+    const bool act = pr < NA;
+    const float* tp = ta + (p.angles_shared ? (bi * L + t0) * NA : ((bi * L + t0) * H + h) * NA) + pr;
+    // dt of the quarter's rows: lane u holds row u's, shuffled to the pairs
+    const int lane = tid & 31;
+    const float dtl = (jbase + jstep * lane < n) ? __ldg(p.dt + bh * L + t0 + lane) : 0.f;
+    float a[32];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int kc = 2 * i + sub;
-            float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (live && 4 * kc < NA) v4 = __ldg(reinterpret_cast<const float4*>(tr) + kc);
-            th[i][0] = v4.x * dtv;
-            th[i][1] = v4.y * dtv;
-            th[i][2] = v4.z * dtv;
-            th[i][3] = v4.w * dtv;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int pr = 4 * (2 * i + sub) + e;
-                th[i][e] = (live && pr < NA) ? __ldg(tr + pr) * dtv : 0.f;
-            }
+    for (int u = 0; u < 32; ++u) {
+        const bool in = jbase + jstep * u < n;
+        a[u] = (in && act) ? __ldg(tp + u * astep) : 0.f;
     }
+    float acc = 0.f;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float v = rev ? __shfl_down_sync(0xffffffffu, th[i][e], o)
-                                    : __shfl_up_sync(0xffffffffu, th[i][e], o);
-                if (rev ? lane + o < 32 : lane >= o) th[i][e] += v;
-            }
+    for (int u = 0; u < 32; ++u) {
+        acc = fmaf(a[u], __shfl_sync(0xffffffffu, dtl, u), acc);
+        tab[ang_tab_idx<SWZ>(jbase + jstep * u, pr)] = acc;
     }
-    if (lane == (rev ? 0 : 31)) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) qtot[qd * 64 + 4 * (2 * i + sub) + e] = th[i][e];
-    }
+    qtot[qd * 64 + pr] = acc;
 }
 
-// Part B (after the barrier): quadrant offsets, then q, k loads (two items
-// per round trip), rotation, bf16 operand images, and the fp32 carry k.
+// Part B (after the barrier): the tile's 128 rows x 16 dim chunks (8 dims,
+// 4 rotation pairs each) as 8 items per thread: row j = 32 (warp & 3) +
+// lane, chunk kc = 2 m + (warp >> 2) for item m (the warp pair (w, w + 4)
+// shares every 32-byte sector of a row).  (A mapping with 8 rows x 4 chunks
+// per warp load, fewer sectors per request, measured 13% slower.)  Per
+// item: theta from the table plus theta0 and the totals of the quarters
+// before, q, k loads (all eight items in flight at once for bf16 inputs),
+// rotation, bf16 operand images, and the fp32 carry k.
 template <bool IN16>
 __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_t h, int64_t bh,
-                                           int64_t it0, float (&th)[8][4], const float* qtot,
+                                           int64_t it0, const float* tab, const float* qtot,
                                            const float* th0s, uint8_t* img_q, uint8_t* img_k,
                                            const float* scl, const float* qb, const float* kb) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int qd = warp & 3, sub = warp >> 2;
     const int64_t L = p.len, NA = p.n_angles;
-    const int j = qd * 32 + lane;
-    const int64_t it = it0 + j;
-    const bool live = it < L;
     const bool rev = p.reverse != 0;
-    const int64_t t = live ? (rev ? L - 1 - it : it) : 0;
+    auto item = [&](int m, int& j, int& kc) {
+        j = (warp & 3) * 32 + lane;
+        kc = 2 * m + (warp >> 2);
+    };
+    constexpr int kPer = IN16 ? 8 : 2;  // items per round trip
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int pr = 4 * (2 * i + sub) + e;
-            if (pr >= NA) continue;
-            float off = th0s[pr];
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                if (rev ? q > qd : q < qd) off += qtot[q * 64 + pr];
-            th[i][e] += off;
-        }
-    const bool want_bx = p.last_bx && live && it == L - 1;
-    const int64_t qrow = (bi * L + t) * kTcN;
-    // two rounds of four items: every q, k load of a round is in flight
-    // before any of them is used (bf16 rows stay packed until then)
-    constexpr int kPer = 4;
-#pragma unroll
-    for (int m = 0; m < 8 / kPer; ++m) {
+    for (int m0 = 0; m0 < 8; m0 += kPer) {
         uint4 qraw[kPer], kraw[kPer];
         float qa[kPer][8], ka[kPer][8];
 #pragma unroll
         for (int u = 0; u < kPer; ++u) {
-            const int kc = 2 * (kPer * m + u) + sub;
+            int j, kc;
+            item(m0 + u, j, kc);
+            const int64_t it = it0 + j;
+            const bool live = it < L;
+            const int64_t t = live ? (rev ? L - 1 - it : it) : 0;
+            const int64_t qrow = (bi * L + t) * kTcN;
             if (IN16) {
                 qraw[u] = live ? ld8_raw16(p.q, qrow + kc * 8) : make_uint4(0u, 0u, 0u, 0u);
                 kraw[u] = live ? ld8_raw16(p.k, qrow + kc * 8) : make_uint4(0u, 0u, 0u, 0u);
@@ -1307,15 +1377,30 @@ __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_
                 unpack8(qraw[u], qa[u]);
                 unpack8(kraw[u], ka[u]);
             }
-            const int i = kPer * m + u;
-            const int kc = 2 * i + sub;
+            int j, kc;
+            item(m0 + u, j, kc);
+            const int64_t it = it0 + j;
+            const bool live = it < L;
+            const int qd = j >> 5;  // quarter of the row (uniform over the warp)
+            float4 t4 = *reinterpret_cast<const float4*>(th0s + 4 * kc);
+            for (int q = 0; q < 4; ++q) {
+                if (rev ? q > qd : q < qd) {
+                    const float4 v = *reinterpret_cast<const float4*>(qtot + q * 64 + 4 * kc);
+                    t4.x += v.x; t4.y += v.y; t4.z += v.z; t4.w += v.w;
+                }
+            }
+            {
+                const float4 v = *reinterpret_cast<const float4*>(tab + ang_tab_idx<true>(j, 4 * kc));
+                t4.x += v.x; t4.y += v.y; t4.z += v.z; t4.w += v.w;
+            }
+            const float th[4] = {t4.x, t4.y, t4.z, t4.w};
             float qbb[8], kbb[8], qr[8], kr[8];
             ld8(qb + kc * 8, qbb);
             ld8(kb + kc * 8, kbb);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 float sn = 0.f, cs = 1.f;
-                if (4 * kc + e < NA) __sincosf(th[i][e], &sn, &cs);
+                if (4 * kc + e < NA) __sincosf(th[e], &sn, &cs);
                 float a0 = qa[u][2 * e] + qbb[2 * e], a1 = qa[u][2 * e + 1] + qbb[2 * e + 1];
                 qr[2 * e] = a0 * cs - a1 * sn;
                 qr[2 * e + 1] = a0 * sn + a1 * cs;
@@ -1328,7 +1413,7 @@ __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_
 #pragma unroll
                 for (int e = 0; e < 8; ++e) qr[e] = kr[e] = 0.f;
             }
-            if (want_bx) {
+            if (p.last_bx && live && it == L - 1) {
                 // scale_T * k_T for the carry: rotated k of the final step, fp32
 #pragma unroll
                 for (int e = 0; e < 8; ++e) p.last_bx[bh * kTcN + kc * 8 + e] = scl[j] * kr[e];
@@ -1340,56 +1425,149 @@ __device__ __forceinline__ void ang_part_b(const M3Params& p, int64_t bi, int64_
     }
 }
 
+// Part B for bf16 inputs, from raw q, k rows staged in shared memory.  The
+// tile's q and k rows ([n rows][dqk] bf16, natural time order, 256 bytes a
+// row) arrive by two bulk copies issued at the start of the tile into the
+// Q and K operand regions (still free then).  Item mapping: a thread keeps
+// one dim chunk kc (8 dims, 4 rotation pairs; its q, k biases stay in
+// registers) and takes 8 rows j = 8 (2 m + s) + (lane & 7); with
+// kc = 8 hh + ((lane + c) & 7), the 8 lanes of a shared-memory phase see 8
+// different row residues and chunk residues, so the raw-row and theta-table
+// reads and the K-major image stores (bank group = j mod 8) are free of
+// conflicts.  Rotated rows stay packed in registers until every thread has
+// read its raw rows (the caller's barrier); store_qk_img then writes the
+// operand images over them.  qoff holds each quarter's theta offset (theta0
+// plus the quarters before it in natural time).
+__device__ __forceinline__ void qk16_item(int m, int& j, int& kc) {
+    const int lane = threadIdx.x & 31, idx = (threadIdx.x >> 5) * 4 + (lane >> 3);
+    const int hh = idx & 1, c = (idx >> 1) & 7, sg = idx >> 4;
+    j = 8 * (2 * m + sg) + (lane & 7);
+    kc = 8 * hh + ((lane + c) & 7);
+}
+__device__ __forceinline__ void ang_part_b16(const M3Params& p, int64_t bh, int64_t it0, int n,
+                                             const float* tab, const float* qoff,
+                                             const uint8_t* raw_q, const uint8_t* raw_k,
+                                             const float* scl, const float* qb, const float* kb,
+                                             uint4 (&qi)[8], uint4 (&ki)[8]) {
+    const int64_t L = p.len, NA = p.n_angles;
+    const bool rev = p.reverse != 0;
+    int j0, kc;
+    qk16_item(0, j0, kc);
+    float qbb[8], kbb[8];
+    ld8(qb + kc * 8, qbb);
+    ld8(kb + kc * 8, kbb);
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        const int j = j0 + 16 * m;
+        const int64_t it = it0 + j;
+        const bool live = it < L;
+        const int rr = live ? (rev ? n - 1 - j : j) : 0;  // raw row (natural time) of row j
+        float qa[8], ka[8];
+        unpack8(*reinterpret_cast<const uint4*>(raw_q + rr * 256 + kc * 16), qa);
+        unpack8(*reinterpret_cast<const uint4*>(raw_k + rr * 256 + kc * 16), ka);
+        float4 t4 = *reinterpret_cast<const float4*>(qoff + (j >> 5) * 64 + 4 * kc);
+        {
+            const float4 v = *reinterpret_cast<const float4*>(tab + ang_tab_idx<false>(j, 4 * kc));
+            t4.x += v.x; t4.y += v.y; t4.z += v.z; t4.w += v.w;
+        }
+        const float th[4] = {t4.x, t4.y, t4.z, t4.w};
+        float qr[8], kr[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float sn = 0.f, cs = 1.f;
+            if (4 * kc + e < NA) __sincosf(th[e], &sn, &cs);
+            float a0 = qa[2 * e] + qbb[2 * e], a1 = qa[2 * e + 1] + qbb[2 * e + 1];
+            qr[2 * e] = a0 * cs - a1 * sn;
+            qr[2 * e + 1] = a0 * sn + a1 * cs;
+            a0 = ka[2 * e] + kbb[2 * e];
+            a1 = ka[2 * e + 1] + kbb[2 * e + 1];
+            kr[2 * e] = a0 * cs - a1 * sn;
+            kr[2 * e + 1] = a0 * sn + a1 * cs;
+        }
+        if (!live) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qr[e] = kr[e] = 0.f;
+        }
+        if (p.last_bx && live && it == L - 1) {
+            // scale_T * k_T for the carry: rotated k of the final step, fp32
+#pragma unroll
+            for (int e = 0; e < 8; ++e) p.last_bx[bh * kTcN + kc * 8 + e] = scl[j] * kr[e];
+        }
+        qi[m] = pack8(qr);
+        ki[m] = pack8(kr);
+    }
+}
+__device__ __forceinline__ void store_qk_img(const uint4 (&qi)[8], const uint4 (&ki)[8], uint8_t* img_q,
+                                             uint8_t* img_k) {
+    int j0, kc;
+    qk16_item(0, j0, kc);
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        const uint32_t o = kmaj_off(j0 + 16 * m, kc * 8, 128);
+        *reinterpret_cast<uint4*>(img_q + o) = qi[m];
+        *reinterpret_cast<uint4*>(img_k + o) = ki[m];
+    }
+}
+
 // Requests every row tile `tile` will read into L2 (one 16-byte-aligned bulk
 // prefetch per row), so that its loads, issued a tile later, hit L2.
 template <bool ANG, bool IN16, int R, bool XR = false>
 __device__ __forceinline__ void prefetch_tile(const M3Params& p, const float* ta,
-                                              const float* theta0, int64_t tile, int n_chunks) {
+                                              const float* theta0, int64_t tile, int n_chunks,
+                                              int tid) {
     const int64_t BH = p.batch * p.heads, H = p.heads, L = p.len;
     const int64_t bh = tile % BH, bi = bh / H, h = bh % H;
     const int ch = static_cast<int>(tile / BH);
     constexpr int TS = kTcQ / R;
     const int64_t s0 = static_cast<int64_t>(ch) * TS;
-    const int tid = threadIdx.x;
     const uint32_t es = IN16 ? 2 : 4;  // bytes per element of q, k, v, z
-    if (tid < TS) {
-        const int64_t it = s0 + tid;
-        if (it >= L) return;
+    // per-row work: v rows on threads [0, TS), z rows on [TS, 2 TS) (wrapping),
+    // plus per-head ta or cos/sin rows; the contiguous blocks (q, k and shared
+    // ta rows of the tile's natural-time range), the gate spans and theta0 on
+    // threads 0..6 as a second task
+    const int ri = tid % TS;
+    const int64_t it = s0 + ri;
+    if (it < L) {
         const int64_t t = p.reverse ? L - 1 - it : it;
         const int64_t row = (bi * L + t) * H + h;
-        const uint8_t* q = static_cast<const uint8_t*>(static_cast<const void*>(p.q));
-        const uint8_t* k = static_cast<const uint8_t*>(static_cast<const void*>(p.k));
-        const uint8_t* v = static_cast<const uint8_t*>(static_cast<const void*>(p.v));
-        if (h == 0) {  // q, k rows are shared by all heads
-            prefetch_l2(q + (bi * L + t) * R * kTcN * es, R * kTcN * es);
-            prefetch_l2(k + (bi * L + t) * R * kTcN * es, R * kTcN * es);
+        if (tid < TS) {
+            const uint8_t* v = static_cast<const uint8_t*>(static_cast<const void*>(p.v));
+            prefetch_lines(v + row * kTcP * R * es, kTcP * R * es);
+            if (ANG) {
+                if (!p.angles_shared && (p.n_angles & 3) == 0 && p.n_angles > 0)
+                    prefetch_lines(ta + row * p.n_angles, static_cast<uint32_t>(p.n_angles * 4));
+            } else {
+                prefetch_lines(p.cos + row * (kTcN / 2), kTcN * 2);
+                prefetch_lines(p.sin + row * (kTcN / 2), kTcN * 2);
+            }
+        } else if (tid < 2 * TS && p.z) {
+            prefetch_lines(static_cast<const uint8_t*>(static_cast<const void*>(p.z)) + row * kTcP * es, kTcP * es);
         }
-        if (XR)
-            prefetch_l2(v + row * kTcP * R * es, kTcP * R * es);
-        else
-            prefetch_l2(v + row * kTcP * es, kTcP * es);
-        if (p.z) prefetch_l2(static_cast<const uint8_t*>(static_cast<const void*>(p.z)) + row * kTcP * es,
-                             kTcP * es);
-        if (ANG) {
-            const int64_t arow = p.angles_shared ? (bi * L + t) : row;
-            if ((p.n_angles & 3) == 0 && p.n_angles > 0 && (!p.angles_shared || h == 0))
-                prefetch_l2(ta + arow * p.n_angles, static_cast<uint32_t>(p.n_angles * 4));
-        } else {
-            prefetch_l2(p.cos + row * (kTcN / 2), kTcN * 2);
-            prefetch_l2(p.sin + row * (kTcN / 2), kTcN * 2);
-        }
-    } else if (tid < TS + 3) {
-        // gate rows: TS steps (+1 for the trapezoid's next step), 16-byte aligned span
-        const float* g = tid == TS ? p.dt : tid == TS + 1 ? p.trap : p.adt;
-        if (reinterpret_cast<uintptr_t>(g) & 15u) return;  // bulk prefetch needs 16-byte alignment
-        int64_t lo = p.reverse ? L - (s0 + TS) - 1 : s0;
-        int64_t hi = p.reverse ? L - s0 : s0 + TS + 1;
+    }
+    if (tid < 7) {
+        int64_t lo = p.reverse ? L - (s0 + TS) : s0;
+        int64_t hi = p.reverse ? L - s0 : s0 + TS;
         lo = lo < 0 ? 0 : lo;
         hi = hi > L ? L : hi;
-        const int64_t a = (bh * L + lo) & ~int64_t(3), b = ((bh * L + hi) + 3) & ~int64_t(3);
-        if (b > a) prefetch_l2(g + a, static_cast<uint32_t>((b - a) * 4));
-    } else if (ANG && tid == TS + 3 && p.n_angles > 0) {
-        prefetch_l2(theta0 + (bh * n_chunks + ch) * 64, 256);
+        if (hi <= lo) return;
+        const int64_t n = hi - lo;
+        if (tid < 2) {
+            if (h != 0) return;  // q, k rows are shared by all heads
+            const uint8_t* b = static_cast<const uint8_t*>(static_cast<const void*>(tid == 0 ? p.q : p.k));
+            prefetch_l2(b + (bi * L + lo) * R * kTcN * es, static_cast<uint32_t>(n * R * kTcN * es));
+        } else if (tid == 2) {
+            if (ANG && p.angles_shared && h == 0 && (p.n_angles & 3) == 0 && p.n_angles > 0)
+                prefetch_l2(ta + (bi * L + lo) * p.n_angles, static_cast<uint32_t>(n * p.n_angles * 4));
+        } else if (tid < 6) {
+            // gate rows (+1 step for the trapezoid's next step), 16-byte aligned span
+            const float* g = tid == 3 ? p.dt : tid == 4 ? p.trap : p.adt;
+            if (reinterpret_cast<uintptr_t>(g) & 15u) return;  // bulk prefetch needs 16-byte alignment
+            const int64_t glo = lo > 0 ? lo - 1 : 0, ghi = hi < L ? hi + 1 : L;
+            const int64_t a = (bh * L + glo) & ~int64_t(3), b = ((bh * L + ghi) + 3) & ~int64_t(3);
+            if (b > a) prefetch_l2(g + a, static_cast<uint32_t>((b - a) * 4));
+        } else if (ANG && p.n_angles > 0) {
+            prefetch_l2(theta0 + (bh * n_chunks + ch) * 64, 256);
+        }
     }
 }
 
@@ -1402,10 +1580,12 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
     float* gam = scl + kTcQ;
     float* wdec = gam + kTcQ;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kFMisc);
+    uint64_t* bar_ld = reinterpret_cast<uint64_t*>(smem + kFMisc + 8);  // raw q, k staging
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kFMisc + 16);
     int* tile_slot = reinterpret_cast<int*>(smem + kFMisc + 24);  // the next tile
 
     float* last_decay = reinterpret_cast<float*>(smem + kFMisc + 28);
+    float* gwtot = reinterpret_cast<float*>(smem + kFMisc + 32);  // angles mode: gate warp totals
     float* qtot = reinterpret_cast<float*>(smem + kFQtot);  // angles mode: quadrant totals
     float* th0s = qtot + 4 * 64;                            // angles mode: chunk's theta0
     float* qbs = reinterpret_cast<float*>(smem + kFBias);   // [R][dqk]
@@ -1420,12 +1600,18 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
     if (warp == 0) tmem_alloc(tmem_slot, 256);
     if (tid == 0) {
         mbar_init(bar, 1);
+        mbar_init(bar_ld, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // bf16 angles mode: the tile's raw q, k rows are bulk-copied into the Q
+    // and K operand regions at the start of the tile
+    constexpr bool kStageQK = ANG && IN16 && R == 1 && !XR;
+    uint32_t ld_phase = 0;
+    bool ld_pending = false;
     const uint32_t t_lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int hc = warp >> 2;                 // column half of this warp
     const int r = (warp & 3) * 32 + lane;     // TMEM lane: row i (G, Y, Z) / state row n (dS)
@@ -1440,27 +1626,41 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
     if (tid == 0) *tile_slot = static_cast<int>(atomicAdd(cw.counter, 1u));
     __syncthreads();
     int64_t tile = *tile_slot;
-    if (tile < n_tiles) prefetch_tile<ANG, IN16, R, XR>(p, ta, theta0, tile, n_chunks);
+    if (tile < n_tiles) prefetch_tile<ANG, IN16, R, XR>(p, ta, theta0, tile, n_chunks, tid);
     __syncthreads();  // every thread has read the first tile
+#ifdef M3TC_PHASE_PROF
+    long long ph_t = clock64();
+    long long w_t = 0;
+#endif
     while (ok && tile < n_tiles) {
+PH_MARK(-1);
+        W_SET();
         // every thread read the slot (the next tile) before the previous
         // tile's closing barrier, so thread 0 may refill it now
-        if (tid == 0) *tile_slot = static_cast<int>(atomicAdd(cw.counter, 1u));
+        if (tid == kTcThreads2 - 32) *tile_slot = static_cast<int>(atomicAdd(cw.counter, 1u));
         const int64_t bh = tile % BH;
         const int ch = static_cast<int>(tile / BH);
         const int64_t bi = bh / H, h = bh % H;
         const int64_t it0 = static_cast<int64_t>(ch) * (kTcQ / R);  // first step of the tile
+        int n_rows = 0;  // kStageQK: rows of the tile
+        if (kStageQK) {
+            int64_t lo, hi;
+            chunk_range(L, ch, p.reverse, lo, hi);
+            n_rows = static_cast<int>(hi - lo);
+            if (tid == 32) {
+                const uint32_t bytes = static_cast<uint32_t>(n_rows) * kTcN * 2;
+                const uint16_t* q16 = static_cast<const uint16_t*>(static_cast<const void*>(p.q));
+                const uint16_t* k16 = static_cast<const uint16_t*>(static_cast<const void*>(p.k));
+                mbar_expect_tx(bar_ld, 2 * bytes);
+                bulk_g2s(smem + kFQ, q16 + (bi * L + lo) * kTcN, bytes, bar_ld);
+                bulk_g2s(smem + kFK, k16 + (bi * L + lo) * kTcN, bytes, bar_ld);
+            }
+            ld_pending = true;
+        }
 
         float xv[kXItems][8];
         uint4 xraw[kXItems];  // bf16 inputs: v stays packed until after the gate barrier
-        uint4 xr16[4];  // bf16 per-rank X: raw 16-byte chunks until the gate barrier
-        if (XR && IN16) {
-            load_x_xr16_raw<R>(p, bi, h, it0, xr16);
-        } else if (XR) {
-            load_x_xr<R, IN16>(p, bi, h, it0, xv);
-        } else if (R > 1) {
-            load_x_r<R>(p, bi, h, it0, xv);
-        } else if (IN16) {
+        auto load_xraw = [&]() {
 #pragma unroll
             for (int q = 0; q < kXItems; ++q) {
                 int j, pc;
@@ -1472,43 +1672,110 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
                     xraw[q] = ld8_raw16(p.v, ((bi * L + t) * H + h) * kTcP + pc * 8);
                 }
             }
+        };
+        uint4 xr16[4];  // bf16 per-rank X: raw 16-byte chunks until the gate barrier
+        if (XR && IN16) {
+            load_x_xr16_raw<R>(p, bi, h, it0, xr16);
+        } else if (XR) {
+            load_x_xr<R, IN16>(p, bi, h, it0, xv);
+        } else if (R > 1) {
+            load_x_r<R>(p, bi, h, it0, xv);
+        } else if (IN16) {
+            if (!kStageQK) load_xraw();  // staged mode: after the rotation (registers)
         } else {
-            load_x_t<false>(p, bi, h, it0, xv);
+            if (!ANG) load_x_t<false>(p, bi, h, it0, xv);  // angles mode: after the rotation
         }
-        float th[8][4];
-        if (ANG) ang_part_a(p, ta, theta0, bi, h, bh, ch, n_chunks, it0, th, qtot, th0s);
+        if (ANG)
+            ang_part_a<!IN16>(p, ta, theta0, bi, h, bh, ch, n_chunks, reinterpret_cast<float*>(smem + kFX),
+                       qtot, th0s);
+        W_MARK(32 + warp);
         for (int i = tid; i < R * kTcN; i += kTcThreads2) {
             qbs[i] = (!XR || p.q_bias) ? __ldg(p.q_bias + h * R * kTcN + i) : 0.f;
             kbs[i] = (!XR || p.k_bias) ? __ldg(p.k_bias + h * R * kTcN + i) : 0.f;
         }
-        if (warp == 0) tile_gates_r<R>(p, bh, it0, lcum, scl, gam, wdec, last_decay);
+        W_MARK(40 + warp);
+        if (ANG) {
+            if (warp < 4) gates_split_1(p, bh, it0, lcum, scl, gam, gwtot);
+        } else if (warp == 0) {
+            tile_gates_r<R>(p, bh, it0, lcum, scl, gam, wdec, last_decay);
+        }
+        W_MARK(16 + warp);
         __syncthreads();
-        if (IN16 && R == 1 && !XR) {
-#pragma unroll
-            for (int q = 0; q < kXItems; ++q) unpack8(xraw[q], xv[q]);
-        }
+PH_MARK(0);
+        W_SET();
         const int64_t next_tile = *tile_slot;
-        if (next_tile < n_tiles) prefetch_tile<ANG, IN16, R, XR>(p, ta, theta0, next_tile, n_chunks);
-        if (XR && IN16) {
-            store_x_xr16<R>(xr16, wdec, smem + kFX, smem + kFXw);
-        } else {
+        if (next_tile < n_tiles) prefetch_tile<ANG, IN16, R, XR>(p, ta, theta0, next_tile, n_chunks,
+                                                             (tid + kTcThreads2 / 2) % kTcThreads2);
+        // X and w o X operand images (in angles mode after the rotation,
+        // whose theta table shares their shared memory)
+        auto store_x = [&]() {
+            if (ANG && !IN16) load_x_t<false>(p, bi, h, it0, xv);
+            if (kStageQK) load_xraw();
+            if (IN16 && R == 1 && !XR) {
 #pragma unroll
-            for (int q = 0; q < kXItems; ++q) {
-                int j, pc;
-                x_item(q, j, pc);
-                const float w = wdec[j];
-                float xw[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) xw[e] = w * xv[q][e];
-                const uint32_t o = mnmaj_off(pc * 8, j, kTcP);
-                *reinterpret_cast<uint4*>(smem + kFX + o) = pack8(xv[q]);
-                *reinterpret_cast<uint4*>(smem + kFXw + o) = pack8(xw);
+                for (int q = 0; q < kXItems; ++q) unpack8(xraw[q], xv[q]);
             }
-        }
-        if (ANG)
-            ang_part_b<IN16>(p, bi, h, bh, it0, th, qtot, th0s, smem + kFQ, smem + kFK, scl, qbs,
-                             kbs);
-        else if (XR && IN16)
+            if (XR && IN16) {
+                store_x_xr16<R>(xr16, wdec, smem + kFX, smem + kFXw);
+            } else {
+#pragma unroll
+                for (int q = 0; q < kXItems; ++q) {
+                    int j, pc;
+                    x_item(q, j, pc);
+                    const float w = wdec[j];
+                    float xw[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) xw[e] = w * xv[q][e];
+                    const uint32_t o = mnmaj_off(pc * 8, j, kTcP);
+                    *reinterpret_cast<uint4*>(smem + kFX + o) = pack8(xv[q]);
+                    *reinterpret_cast<uint4*>(smem + kFXw + o) = pack8(xw);
+                }
+            }
+        };
+        if (!ANG) store_x();
+        if (kStageQK) {
+            if (tid < kTcQ) {
+                gates_split_2(lcum, scl, wdec, gwtot, last_decay);
+            } else if (tid < kTcQ + 64) {
+                // theta offset of each quarter (theta0 + the quarters before it
+                // in natural time), in place over the quarter totals
+                const int pr = tid - kTcQ;
+                float v[4], acc = th0s[pr];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) v[q] = qtot[q * 64 + pr];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int qq = p.reverse ? 3 - q : q;
+                    qtot[qq * 64 + pr] = acc;
+                    acc += v[qq];
+                }
+            }
+            __syncthreads();
+            const bool got = mbar_wait(bar_ld, ld_phase);
+            ld_phase ^= 1;
+            ld_pending = !got;
+            W_MARK(24 + warp);
+            uint4 qi[8], ki[8];
+            ang_part_b16(p, bh, it0, n_rows, reinterpret_cast<const float*>(smem + kFX), qtot,
+                         smem + kFQ, smem + kFK, scl, qbs, kbs, qi, ki);
+            W_MARK(48 + warp);
+            // every read of the raw rows and of the theta table precedes the
+            // operand-image and X stores over them
+            if (__syncthreads_or(!got)) {
+                if (tid == 0) atomicExch(&g_tc_status, 1);
+                ok = false;
+                break;
+            }
+            store_qk_img(qi, ki, smem + kFQ, smem + kFK);
+            store_x();
+            W_MARK(56 + warp);
+        } else if (ANG) {
+            if (tid < kTcQ) gates_split_2(lcum, scl, wdec, gwtot, last_decay);
+            ang_part_b<IN16>(p, bi, h, bh, it0, reinterpret_cast<const float*>(smem + kFX), qtot, th0s,
+                             smem + kFQ, smem + kFK, scl, qbs, kbs);
+            __syncthreads();  // every read of the theta table precedes the X stores
+            store_x();
+        } else if (XR && IN16)
             stage_qk_xr16<R>(p, bi, h, it0, smem + kFQ, smem + kFK, qbs, kbs);
         else if (XR)
             stage_qk_xr<R, IN16>(p, bi, h, it0, smem + kFQ, smem + kFK, qbs, kbs);
@@ -1531,6 +1798,7 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
+PH_MARK(1);
         tc_fence_after();
         // ---- group 1: G = Qr Kr^T; dS^T = Kr^T (w o X)
         if (tid == 0) {
@@ -1550,9 +1818,69 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
             umma_commit(bar);
         }
         ok = cta_wait(bar, phase);
+PH_MARK(2);
         phase ^= 1;
         if (!ok) break;
         tc_fence_after();
+        // ---- chain first (it gates the successor chunk's tile): S_in from
+        // the predecessor chunk, S_out published
+        {
+            bool got = true;
+            if (tid == 0 && ch > 0) got = wait_flag(cw.flags + bh, static_cast<unsigned>(ch));
+PH_MARK(4);
+            if (__syncthreads_or(!got)) {
+                if (tid == 0) atomicExch(&g_tc_status, 1);
+                ok = false;
+                break;
+            }
+            float sin_[32], ds[32];
+            // slot layout: float4 q of thread (r, hc) at [hc * 8 + q][r], so
+            // that a warp's accesses are 512 contiguous bytes
+            const float4* slot_in = reinterpret_cast<const float4*>(cw.slots + (bh * 2 + ((ch + 1) & 1)) * kSt) +
+                                    hc * 8 * kTcN + r;
+            float4* slot_out = reinterpret_cast<float4*>(cw.slots + (bh * 2 + (ch & 1)) * kSt) + hc * 8 * kTcN + r;
+            if (ch > 0) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 v4 = __ldcg(slot_in + q * kTcN);
+                    sin_[4 * q] = v4.x; sin_[4 * q + 1] = v4.y; sin_[4 * q + 2] = v4.z; sin_[4 * q + 3] = v4.w;
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 32; ++q) sin_[q] = 0.f;
+            }
+            tmem_ld32(tS + t_lane + hc * 32, ds);
+            const float dec = *last_decay;
+            float so[32];
+#pragma unroll
+            for (int q = 0; q < 32; ++q) so[q] = fmaf(dec, sin_[q], ds[q]);
+            if (ch + 1 < n_chunks) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    __stcg(slot_out + q * kTcN,
+                           make_float4(so[4 * q], so[4 * q + 1], so[4 * q + 2], so[4 * q + 3]));
+            } else if (p.last_state) {
+                // final state, (p, n) layout
+#pragma unroll
+                for (int q = 0; q < 32; ++q) p.last_state[(bh * kTcP + hc * 32 + q) * kTcN + r] = so[q];
+            }
+            // S_in^T operand image (m = p, k = n): 4 chunks of 8 p at state row r
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = sin_[c8 * 8 + e];
+                *reinterpret_cast<uint4*>(smem + kFS + mnmaj_off(hc * 32 + c8 * 8, r, kTcP)) = pack8(f);
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();  // every thread's S_out stores precede the release below
+PH_MARK(5);
+            tc_fence_after();
+            // the barrier orders every thread's S_out stores before this
+            // release (cumulative at gpu scope)
+            if (tid == 0 && ch + 1 < n_chunks) st_release(cw.flags + bh, static_cast<unsigned>(ch + 1));
+        }
         {
             // W = mask o G (row i = r, this warp's column half) over Kr
             const float li = lcum[r], gi = gam[r];
@@ -1584,6 +1912,7 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
+PH_MARK(3);
         tc_fence_after();
         if (tid == 0) {
             const uint32_t id_Y = instr_desc(128, kTcP, false, true);
@@ -1592,65 +1921,6 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
                 const uint64_t b = smem_desc(sbase + kFX + kb * 2 * 8 * 128, 8 * 128, 128);
                 umma(tY, a, b, id_Y, kb > 0);
             }
-            // no commit yet: Z joins this group after the chain step
-        }
-        // ---- chain: S_in from the predecessor chunk, S_out published
-        {
-            bool got = true;
-            if (tid == 0 && ch > 0) got = wait_flag(cw.flags + bh, static_cast<unsigned>(ch));
-            if (__syncthreads_or(!got)) {
-                if (tid == 0) atomicExch(&g_tc_status, 1);
-                ok = false;
-                if (tid == 0) umma_commit(bar);  // drain the issued Y before leaving
-                mbar_wait(bar, phase);
-                break;
-            }
-            float sin_[32], ds[32];
-            float* slot_in = cw.slots + (bh * 2 + ((ch + 1) & 1)) * kSt + r * kTcP + hc * 32;
-            float* slot_out = cw.slots + (bh * 2 + (ch & 1)) * kSt + r * kTcP + hc * 32;
-            if (ch > 0) {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float4 v4 = __ldcg(reinterpret_cast<const float4*>(slot_in) + q);
-                    sin_[4 * q] = v4.x; sin_[4 * q + 1] = v4.y; sin_[4 * q + 2] = v4.z; sin_[4 * q + 3] = v4.w;
-                }
-            } else {
-#pragma unroll
-                for (int q = 0; q < 32; ++q) sin_[q] = 0.f;
-            }
-            tmem_ld32(tS + t_lane + hc * 32, ds);
-            const float dec = *last_decay;
-            float so[32];
-#pragma unroll
-            for (int q = 0; q < 32; ++q) so[q] = fmaf(dec, sin_[q], ds[q]);
-            if (ch + 1 < n_chunks) {
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    __stcg(reinterpret_cast<float4*>(slot_out) + q,
-                           make_float4(so[4 * q], so[4 * q + 1], so[4 * q + 2], so[4 * q + 3]));
-            } else if (p.last_state) {
-                // final state, (p, n) layout
-#pragma unroll
-                for (int q = 0; q < 32; ++q) p.last_state[(bh * kTcP + hc * 32 + q) * kTcN + r] = so[q];
-            }
-            // S_in^T operand image (m = p, k = n): 4 chunks of 8 p at state row r
-#pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
-                float f[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = sin_[c8 * 8 + e];
-                *reinterpret_cast<uint4*>(smem + kFS + mnmaj_off(hc * 32 + c8 * 8, r, kTcP)) = pack8(f);
-            }
-            fence_async_smem();
-            tc_fence_before();
-            __syncthreads();  // every thread's S_out stores precede the release below
-            tc_fence_after();
-            if (tid == 0 && ch + 1 < n_chunks) {
-                __threadfence();
-                st_release(cw.flags + bh, static_cast<unsigned>(ch + 1));
-            }
-        }
-        if (tid == 0) {
             if (ch > 0) {
                 const uint32_t id_Z = instr_desc(128, kTcP, false, true);
 #pragma unroll
@@ -1676,6 +1946,7 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
             }
         }
         ok = cta_wait(bar, phase);
+PH_MARK(6);
         phase ^= 1;
         if (!ok) break;
         tc_fence_after();
@@ -1786,10 +2057,12 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
         // the next tile overwrites shared memory and tensor memory
         tc_fence_before();
         __syncthreads();
+PH_MARK(7);
         tc_fence_after();
         tile = next_tile;
     }
     if (!ok) mbar_wait(bar, phase ^ 1);  // MMAs still in flight: bounded second wait
+    if (ld_pending) mbar_wait(bar_ld, ld_phase);  // a staging copy in flight: bounded wait
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -2044,3 +2317,11 @@ int m3_tc_status_and_clear() {
 }
 
 }  // namespace b200scan
+
+#ifdef M3TC_PHASE_PROF
+extern "C" int arm_scan_debug_tc_phases(unsigned long long* out, int reset) {
+    cudaMemcpyFromSymbol(out, b200scan::g_tc_phase, sizeof(unsigned long long) * 64);
+    if (reset) { unsigned long long z[64] = {0}; cudaMemcpyToSymbol(b200scan::g_tc_phase, z, sizeof(z)); }
+    return 0;
+}
+#endif
