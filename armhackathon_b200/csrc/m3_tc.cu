@@ -882,18 +882,70 @@ __global__ void __launch_bounds__(256) m3_tc_angle_sums(M3Params p, float* ta, f
         theta0[(bh * n_chunks + c) * 64 + pr] = ((part[0][pr] + part[1][pr]) + part[2][pr]) + part[3][pr];
 }
 
-// Exclusive prefix of the chunk sums in natural-time order, in place.
-__global__ void m3_tc_angle_prefix(M3Params p, float* theta0, int n_chunks) {
-    const int64_t bh = blockIdx.x;
-    const int pr = threadIdx.x;
-    if (pr >= p.n_angles) return;
-    float acc = 0.f;
-    for (int i = 0; i < n_chunks; ++i) {
-        const int c = p.reverse ? n_chunks - 1 - i : i;
-        float* cell = theta0 + (bh * n_chunks + c) * 64 + pr;
-        const float v = *cell;
-        *cell = acc;
-        acc += v;
+// Shared angles (one row per (batch, step) for every head): one CTA per
+// (traversal chunk, batch) computes the chunk's ta rows once (tanh, written
+// to the table) and every head's chunk sums theta0[bh][c][pair] =
+// sum over the chunk's steps of ta * dt_h, from shared memory: ta as
+// [128 steps][64 pairs], dt as [heads][128 steps].
+template <bool IN16>
+__global__ void __launch_bounds__(256) m3_tc_angle_sums_shared(M3Params p, float* ta, float* theta0,
+                                                              int n_chunks) {
+    extern __shared__ float ang_sm[];
+    float* tas = ang_sm;             // [128][64]
+    float* dts = ang_sm + kTcQ * 64;  // [heads][128]
+    constexpr float kPiF = 3.14159265358979323846f;
+    const int c = blockIdx.x;
+    const int64_t bi = blockIdx.y;
+    const int64_t H = p.heads, L = p.len, NA = p.n_angles;
+    int64_t lo, hi;
+    chunk_range(L, c, p.reverse, lo, hi);
+    const int n = static_cast<int>(hi - lo);
+    for (int i = threadIdx.x; i < kTcQ * 64; i += blockDim.x) {
+        const int st = i >> 6, pr = i & 63;
+        float tv = 0.f;
+        if (st < n && pr < NA) {
+            const int64_t e = (bi * L + lo + st) * NA + pr;
+            // tanh x = 1 - 2 / (1 + e^{2x}): absolute error <= ~2.5e-7
+            tv = (1.f - __fdividef(2.f, 1.f + __expf(2.f * ld1_in<IN16>(p.angles, e)))) * kPiF;
+            ta[e] = tv;
+        }
+        tas[i] = tv;
+    }
+    for (int i = threadIdx.x; i < H * kTcQ; i += blockDim.x) {
+        const int64_t hh = i / kTcQ;
+        const int st = i % kTcQ;
+        dts[i] = st < n ? __ldg(p.dt + (bi * H + hh) * L + lo + st) : 0.f;
+    }
+    __syncthreads();
+    const int pr = threadIdx.x & 63, hg = threadIdx.x >> 6;
+    constexpr int kHk = 6;  // heads per thread and pass: hg + 4 k
+    for (int64_t h0 = hg; h0 < H; h0 += 4 * kHk) {
+        // per quarter of 32 steps, then ((q0 + q1) + q2) + q3: the order of
+        // m3_tc_angle_sums, so shared and per-head angles agree bit for bit
+        float acc[kHk];
+#pragma unroll
+        for (int k = 0; k < kHk; ++k) acc[k] = 0.f;
+        for (int qr = 0; qr < 4; ++qr) {
+            float part[kHk];
+#pragma unroll
+            for (int k = 0; k < kHk; ++k) part[k] = 0.f;
+            const int se = 32 * qr + 32 < n ? 32 * qr + 32 : n;
+            for (int st = 32 * qr; st < se; ++st) {
+                const float tv = tas[st * 64 + pr];
+#pragma unroll
+                for (int k = 0; k < kHk; ++k) {
+                    const int64_t hh = h0 + 4 * k;
+                    if (hh < H) part[k] = fmaf(tv, dts[hh * kTcQ + st], part[k]);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kHk; ++k) acc[k] = qr == 0 ? part[k] : acc[k] + part[k];
+        }
+#pragma unroll
+        for (int k = 0; k < kHk; ++k) {
+            const int64_t hh = h0 + 4 * k;
+            if (hh < H && pr < NA) theta0[((bi * H + hh) * n_chunks + c) * 64 + pr] = acc[k];
+        }
     }
 }
 
@@ -1300,7 +1352,28 @@ __device__ __forceinline__ void ang_part_a(const M3Params& p, const float* ta, c
     int64_t lo, hi;
     chunk_range(L, ch, p.reverse, lo, hi);
     const int n = static_cast<int>(hi - lo);  // valid rows of the tile
-    if (tid < 64) th0s[tid] = tid < NA ? __ldg(theta0 + (bh * n_chunks + ch) * 64 + tid) : 0.f;
+    if (tid >= 128 && tid < 192) {  // warps 4, 5: no gate work in this stage
+        const int pt = tid - 128;
+        // theta0 of the chunk: the chunk sums of the chunks before it in
+        // natural time (traversal chunks 0..ch-1, or ch+1..n_chunks-1 in
+        // reverse), summed in natural time order
+        float acc = 0.f;
+        if (pt < NA) {
+            const float* col = theta0 + bh * n_chunks * 64 + pt;
+            const int cnt = rev ? n_chunks - 1 - ch : ch;
+            for (int i0 = 0; i0 < cnt; i0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int i = i0 + u;
+                    v[u] = i < cnt ? __ldg(col + (rev ? n_chunks - 1 - i : i) * 64) : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc += v[u];
+            }
+        }
+        th0s[pt] = acc;
+    }
     // rows of this quarter in natural time order: forward j = 32 qd + u,
     // reverse j = 32 qd + 31 - u; natural time t(j) = lo + j / hi - 1 - j
     const int jbase = rev ? qd * 32 + 31 : qd * 32;
@@ -2226,17 +2299,25 @@ cudaError_t m3_tc_launch_fused(const M3Params& p, cudaStream_t stream) {
     float* ta = theta0 + th_floats;
     e = cudaMemsetAsync(cw.flags, 0, flag_bytes, stream);
     if (e == cudaSuccess && ang && p.n_angles > 0) {
-        const dim3 g(static_cast<unsigned>(n_chunks), static_cast<unsigned>(bh));
-        if (p.in_bf16) {
-            m3_tc_angle_sums<true><<<g, 256, 0, stream>>>(p, ta, theta0, n_chunks);
-            note_launch();
+        // chunk sums of ta * dt per (bh, chunk, pair); each tile of the main
+        // kernel sums the ones before it into its theta0
+        const size_t sh_bytes = static_cast<size_t>(kTcQ) * (64 + p.heads) * 4;
+        if (p.angles_shared && sh_bytes <= 200 * 1024) {
+            auto kern = p.in_bf16 ? m3_tc_angle_sums_shared<true> : m3_tc_angle_sums_shared<false>;
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(sh_bytes));
+            if (e == cudaSuccess) {
+                kern<<<dim3(static_cast<unsigned>(n_chunks), static_cast<unsigned>(p.batch)), 256, sh_bytes,
+                       stream>>>(p, ta, theta0, n_chunks);
+                note_launch();
+                e = cudaGetLastError();
+            }
         } else {
-            m3_tc_angle_sums<false><<<g, 256, 0, stream>>>(p, ta, theta0, n_chunks);
-            note_launch();
-        }
-        e = cudaGetLastError();
-        if (e == cudaSuccess) {
-            m3_tc_angle_prefix<<<static_cast<unsigned>(bh), 64, 0, stream>>>(p, theta0, n_chunks);
+            const dim3 g(static_cast<unsigned>(n_chunks), static_cast<unsigned>(bh));
+            if (p.in_bf16)
+                m3_tc_angle_sums<true><<<g, 256, 0, stream>>>(p, ta, theta0, n_chunks);
+            else
+                m3_tc_angle_sums<false><<<g, 256, 0, stream>>>(p, ta, theta0, n_chunks);
             note_launch();
             e = cudaGetLastError();
         }
