@@ -2033,7 +2033,68 @@ PH_MARK(6);
 #pragma unroll
                 for (int q = 0; q < 32; ++q) y[q] = fmaf(el, zt[q], y[q]);
             }
-            if (XR) {
+            if (XR && R == 4) {
+                // per-rank MIMO, rank 4: out (b, l, h, dv, R) row (t, rank) =
+                // y + D x.  The 4 lanes of a step (adjacent lanes, one rank
+                // each) exchange 8-channel blocks in two butterfly stages so
+                // that lane k ends with channels 8k..8k+7 of every rank: 32
+                // contiguous output elements, written as 16-byte stores.
+                const int64_t it = it0 + r / R;
+                const int rk = r % R;
+                const bool hi = rk & 2, lo = rk & 1;
+                float A0[8], A1[8], B0[8], B1[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    // stage 1 (lanes k, k ^ 2): keep blocks 2 hi, 2 hi + 1
+                    const float s0 = hi ? y[i] : y[16 + i], s1 = hi ? y[8 + i] : y[24 + i];
+                    A0[i] = hi ? y[16 + i] : y[i];
+                    A1[i] = hi ? y[24 + i] : y[8 + i];
+                    B0[i] = __shfl_xor_sync(0xffffffffu, s0, 2);
+                    B1[i] = __shfl_xor_sync(0xffffffffu, s1, 2);
+                }
+                float vk[8], vk2[8], vk1[8], vk3[8];  // ranks k, k^2, k^1, k^3; block k
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    // stage 2 (lanes k, k ^ 1): keep block 2 hi + lo
+                    vk[i] = lo ? A1[i] : A0[i];
+                    vk2[i] = lo ? B1[i] : B0[i];
+                    vk1[i] = __shfl_xor_sync(0xffffffffu, lo ? A0[i] : A1[i], 1);
+                    vk3[i] = __shfl_xor_sync(0xffffffffu, lo ? B0[i] : B1[i], 1);
+                }
+                if (it < L) {
+                    const int64_t t = p.reverse ? L - 1 - it : it;
+                    const int64_t o0 = (((bi * L + t) * H + h) * kTcP + hc * 32 + 8 * rk) * R;
+                    float o[32];  // o[4 i + rank]: channel 8k + i
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            o[4 * i + q] = q == rk ? vk[i] : q == (rk ^ 2) ? vk2[i] : q == (rk ^ 1) ? vk1[i] : vk3[i];
+                    if (p.d_skip) {
+                        const float dsk = p.d_skip[h];
+#pragma unroll
+                        for (int c8 = 0; c8 < 4; ++c8) {
+                            float xv8[8];
+                            ld8_in<IN16>(p.v, o0 + 8 * c8, xv8);
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) o[8 * c8 + e] = fmaf(dsk, xv8[e], o[8 * c8 + e]);
+                        }
+                    }
+#pragma unroll
+                    for (int c8 = 0; c8 < 4; ++c8) {
+                        float f8[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f8[e] = o[8 * c8 + e];
+                        if (OUT16) {
+                            *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + o0 + 8 * c8) = pack8(f8);
+                        } else {
+                            float4* o4 = reinterpret_cast<float4*>(p.out + o0 + 8 * c8);
+                            o4[0] = make_float4(f8[0], f8[1], f8[2], f8[3]);
+                            o4[1] = make_float4(f8[4], f8[5], f8[6], f8[7]);
+                        }
+                    }
+                }
+            } else if (XR) {
                 // per-rank MIMO: out (b, l, h, dv, R) row (t, rank) = y + D x
                 const int64_t it = it0 + r / R;
                 const int rk = r % R;
