@@ -42,16 +42,6 @@
 namespace b200scan {
 
 __device__ int g_tc_status;
-#ifdef M3TC_PHASE_PROF
-__device__ unsigned long long g_tc_phase[64];
-#define W_MARK(slot) do { if ((threadIdx.x & 31) == 0) { long long _n = clock64(); atomicAdd(&g_tc_phase[(slot)], (unsigned long long)(_n - w_t)); } } while (0)
-#define W_SET() w_t = clock64()
-#define PH_MARK(i) do { if (threadIdx.x == 0) { long long _n = clock64(); if ((i) >= 0) atomicAdd(&g_tc_phase[(i)], (unsigned long long)(_n - ph_t)); ph_t = _n; } } while (0)
-#else
-#define PH_MARK(i) do {} while (0)
-#define W_MARK(slot) do {} while (0)
-#define W_SET() do {} while (0)
-#endif
   // 0 ok, 1 an mbarrier wait timed out
 
 namespace {
@@ -720,14 +710,20 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_out(M3Params p, TcWs ws,
 // atomic counter in chunk-major order (tile = chunk * batch*heads + bh), so a
 // tile's predecessor chunk (same bh) was always taken earlier by a running
 // CTA.  Per tile:
+//   0. (bf16 inputs, raw angles) the tile's q, k rows are bulk-copied into
+//      the Q, K regions; the theta scan (thread per pair and quarter, into a
+//      table over the X region) and the gates (four warps) run meanwhile;
+//      the rotation reads both from shared memory;
 //   1. G = Qr Kr^T and dS^T = Kr^T (w o X) in one MMA group;
-//   2. W = mask o G over Kr (free once group 1 completed), Y = W X issued;
-//   3. the chain: wait for the predecessor's outgoing state (flag per bh,
-//      acquire), S_out = 2^{l2_last} S_in + dS in fp32, publish it (release)
-//      to the bh's other slot, then build the bf16 S_in^T operand;
-//   4. Z = Qr S_in^T;  y = (Y + 2^{l2_i} Z + D x) * silu(z).
+//   2. the chain, first because the successor chunk's tile waits for it:
+//      wait for the predecessor's outgoing state (flag per bh, acquire),
+//      S_out = 2^{l2_last} S_in + dS in fp32, publish it (release) to the
+//      bh's other slot, then build the bf16 S_in^T operand;
+//   3. W = mask o G over Kr (free once group 1 completed);
+//   4. Y = W X and Z = Qr S_in^T in one group;  y = (Y + 2^{l2_i} Z + D x) * silu(z).
 // The outgoing states live in two fp32 slots per bh (chunk c reads slot
-// (c+1)&1, writes slot c&1): 64 KB per bh, resident in L2.
+// (c+1)&1, writes slot c&1): 64 KB per bh, resident in L2, laid out so that a
+// warp's accesses are contiguous.
 // The wait for a predecessor is bounded (with nanosleep backoff); on expiry
 // the tile sets the status flag, and the CTA stops after its MMAs drain.
 constexpr uint32_t kFQ = 0;                        // Qr K-major (A of G, Z)
@@ -1701,13 +1697,7 @@ __global__ void __launch_bounds__(kTcThreads2, 2) m3_tc_fused(M3Params p, ChainW
     int64_t tile = *tile_slot;
     if (tile < n_tiles) prefetch_tile<ANG, IN16, R, XR>(p, ta, theta0, tile, n_chunks, tid);
     __syncthreads();  // every thread has read the first tile
-#ifdef M3TC_PHASE_PROF
-    long long ph_t = clock64();
-    long long w_t = 0;
-#endif
     while (ok && tile < n_tiles) {
-PH_MARK(-1);
-        W_SET();
         // every thread read the slot (the next tile) before the previous
         // tile's closing barrier, so thread 0 may refill it now
         if (tid == kTcThreads2 - 32) *tile_slot = static_cast<int>(atomicAdd(cw.counter, 1u));
@@ -1761,21 +1751,16 @@ PH_MARK(-1);
         if (ANG)
             ang_part_a<!IN16>(p, ta, theta0, bi, h, bh, ch, n_chunks, reinterpret_cast<float*>(smem + kFX),
                        qtot, th0s);
-        W_MARK(32 + warp);
         for (int i = tid; i < R * kTcN; i += kTcThreads2) {
             qbs[i] = (!XR || p.q_bias) ? __ldg(p.q_bias + h * R * kTcN + i) : 0.f;
             kbs[i] = (!XR || p.k_bias) ? __ldg(p.k_bias + h * R * kTcN + i) : 0.f;
         }
-        W_MARK(40 + warp);
         if (ANG) {
             if (warp < 4) gates_split_1(p, bh, it0, lcum, scl, gam, gwtot);
         } else if (warp == 0) {
             tile_gates_r<R>(p, bh, it0, lcum, scl, gam, wdec, last_decay);
         }
-        W_MARK(16 + warp);
         __syncthreads();
-PH_MARK(0);
-        W_SET();
         const int64_t next_tile = *tile_slot;
         if (next_tile < n_tiles) prefetch_tile<ANG, IN16, R, XR>(p, ta, theta0, next_tile, n_chunks,
                                                              (tid + kTcThreads2 / 2) % kTcThreads2);
@@ -1827,11 +1812,9 @@ PH_MARK(0);
             const bool got = mbar_wait(bar_ld, ld_phase);
             ld_phase ^= 1;
             ld_pending = !got;
-            W_MARK(24 + warp);
             uint4 qi[8], ki[8];
             ang_part_b16(p, bh, it0, n_rows, reinterpret_cast<const float*>(smem + kFX), qtot,
                          smem + kFQ, smem + kFK, scl, qbs, kbs, qi, ki);
-            W_MARK(48 + warp);
             // every read of the raw rows and of the theta table precedes the
             // operand-image and X stores over them
             if (__syncthreads_or(!got)) {
@@ -1841,7 +1824,6 @@ PH_MARK(0);
             }
             store_qk_img(qi, ki, smem + kFQ, smem + kFK);
             store_x();
-            W_MARK(56 + warp);
         } else if (ANG) {
             if (tid < kTcQ) gates_split_2(lcum, scl, wdec, gwtot, last_decay);
             ang_part_b<IN16>(p, bi, h, bh, it0, reinterpret_cast<const float*>(smem + kFX), qtot, th0s,
@@ -1871,7 +1853,6 @@ PH_MARK(0);
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-PH_MARK(1);
         tc_fence_after();
         // ---- group 1: G = Qr Kr^T; dS^T = Kr^T (w o X)
         if (tid == 0) {
@@ -1891,7 +1872,6 @@ PH_MARK(1);
             umma_commit(bar);
         }
         ok = cta_wait(bar, phase);
-PH_MARK(2);
         phase ^= 1;
         if (!ok) break;
         tc_fence_after();
@@ -1900,7 +1880,6 @@ PH_MARK(2);
         {
             bool got = true;
             if (tid == 0 && ch > 0) got = wait_flag(cw.flags + bh, static_cast<unsigned>(ch));
-PH_MARK(4);
             if (__syncthreads_or(!got)) {
                 if (tid == 0) atomicExch(&g_tc_status, 1);
                 ok = false;
@@ -1948,7 +1927,6 @@ PH_MARK(4);
             fence_async_smem();
             tc_fence_before();
             __syncthreads();  // every thread's S_out stores precede the release below
-PH_MARK(5);
             tc_fence_after();
             // the barrier orders every thread's S_out stores before this
             // release (cumulative at gpu scope)
@@ -1985,7 +1963,6 @@ PH_MARK(5);
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-PH_MARK(3);
         tc_fence_after();
         if (tid == 0) {
             const uint32_t id_Y = instr_desc(128, kTcP, false, true);
@@ -2019,7 +1996,6 @@ PH_MARK(3);
             }
         }
         ok = cta_wait(bar, phase);
-PH_MARK(6);
         phase ^= 1;
         if (!ok) break;
         tc_fence_after();
@@ -2191,7 +2167,6 @@ PH_MARK(6);
         // the next tile overwrites shared memory and tensor memory
         tc_fence_before();
         __syncthreads();
-PH_MARK(7);
         tc_fence_after();
         tile = next_tile;
     }
@@ -2268,7 +2243,8 @@ cudaError_t device_workspace_pool(cudaMemPool_t* out) {
 }
 
 
-// Three-launch form (kernels A, B, C): selected with B200SCAN_M3_TC_SPLIT=1.
+// Three-launch form (kernels A, B, C): selected with the kernel override
+// kKnobM3TcSplit = 1 (arm_scan_set_kernel_override).
 cudaError_t m3_tc_launch_split(const M3Params& p, cudaStream_t stream) {
     const int64_t bh = p.batch * p.heads;
     const int n_chunks = static_cast<int>((p.len + kTcQ - 1) / kTcQ);
@@ -2460,10 +2436,3 @@ int m3_tc_status_and_clear() {
 
 }  // namespace b200scan
 
-#ifdef M3TC_PHASE_PROF
-extern "C" int arm_scan_debug_tc_phases(unsigned long long* out, int reset) {
-    cudaMemcpyFromSymbol(out, b200scan::g_tc_phase, sizeof(unsigned long long) * 64);
-    if (reset) { unsigned long long z[64] = {0}; cudaMemcpyToSymbol(b200scan::g_tc_phase, z, sizeof(z)); }
-    return 0;
-}
-#endif
