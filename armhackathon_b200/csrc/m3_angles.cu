@@ -34,75 +34,101 @@ __device__ __forceinline__ int64_t angle_phys(const AngleParams& a, int64_t t) {
     return (t % rows) * a.grid_w + t / rows;
 }
 
+// HG heads per thread (HG > 1 only for head-shared angles): the angle row
+// and its tanh are loaded and computed once for HG heads, whose chains run
+// side by side; per head the arithmetic and its order are those of HG = 1.
+template <int HG>
 __global__ void angle_chunk_sums(AngleParams a, float* ws) {
-    const int64_t bh = blockIdx.y;
+    const int64_t bh0 = static_cast<int64_t>(blockIdx.y) * HG;
     const int c = blockIdx.x;
     const int p = threadIdx.x;
     if (p >= a.n_angles) return;
-    const int64_t b = bh / a.heads, h = bh % a.heads;
+    const int64_t b = bh0 / a.heads, h0 = bh0 % a.heads;
     const int64_t t0 = static_cast<int64_t>(c) * kAgChunk;
     const int64_t t1 = t0 + kAgChunk < a.len ? t0 + kAgChunk : a.len;
     const float* ang = a.angles_shared ? a.angles + (b * a.len) * a.n_angles + p
-                                       : a.angles + ((b * a.len) * a.heads + h) * a.n_angles + p;
+                                       : a.angles + ((b * a.len) * a.heads + h0) * a.n_angles + p;
     const int64_t ang_step = a.angles_shared ? a.n_angles : a.heads * a.n_angles;
-    const float* dt = a.dt + (b * a.heads + h) * a.len;
-    float s = 0.f;
+    const float* dt = a.dt + (b * a.heads + h0) * a.len;
+    float s[HG];
+#pragma unroll
+    for (int k = 0; k < HG; ++k) s[k] = 0.f;
     for (int64_t t = t0; t < t1; t += kAgUnroll) {
-        float av[kAgUnroll], dv[kAgUnroll];
+        float av[kAgUnroll], dv[HG][kAgUnroll];
 #pragma unroll
         for (int u = 0; u < kAgUnroll; ++u) {
             const bool in = t + u < t1;
             const int64_t pt = in ? angle_phys(a, t + u) : 0;
             av[u] = in ? __ldg(ang + pt * ang_step) : 0.f;
-            dv[u] = in ? __ldg(dt + pt) : 0.f;
+#pragma unroll
+            for (int k = 0; k < HG; ++k) dv[k][u] = in ? __ldg(dt + k * a.len + pt) : 0.f;
         }
 #pragma unroll
-        for (int u = 0; u < kAgUnroll; ++u) s = fmaf(tanhf(av[u]) * kPi, dv[u], s);
+        for (int u = 0; u < kAgUnroll; ++u) {
+            const float tv = tanhf(av[u]) * kPi;
+#pragma unroll
+            for (int k = 0; k < HG; ++k) s[k] = fmaf(tv, dv[k][u], s[k]);
+        }
     }
-    ws[(bh * gridDim.x + c) * a.n_angles + p] = s;
+    const int nc = gridDim.x;
+#pragma unroll
+    for (int k = 0; k < HG; ++k) ws[((bh0 + k) * nc + c) * a.n_angles + p] = s[k];
 }
 
+template <int HG>
 __global__ void angle_chunk_write(AngleParams a, const float* ws) {
-    const int64_t bh = blockIdx.y;
+    const int64_t bh0 = static_cast<int64_t>(blockIdx.y) * HG;
     const int c = blockIdx.x;
     const int p = threadIdx.x;
     if (p >= a.half) return;
-    const int64_t b = bh / a.heads, h = bh % a.heads;
+    const int64_t b = bh0 / a.heads, h0 = bh0 % a.heads;
     const int64_t t0 = static_cast<int64_t>(c) * kAgChunk;
     const int64_t t1 = t0 + kAgChunk < a.len ? t0 + kAgChunk : a.len;
     const int64_t out_step = a.heads * a.half;
-    float* cs_out = a.cos + ((b * a.len) * a.heads + h) * a.half + p;
-    float* sn_out = a.sin + ((b * a.len) * a.heads + h) * a.half + p;
+    float* cs_out = a.cos + ((b * a.len) * a.heads + h0) * a.half + p;
+    float* sn_out = a.sin + ((b * a.len) * a.heads + h0) * a.half + p;
     if (p >= a.n_angles) {
-        for (int64_t t = t0; t < t1; ++t) {
-            cs_out[t * out_step] = 1.f;
-            sn_out[t * out_step] = 0.f;
-        }
+        for (int64_t t = t0; t < t1; ++t)
+#pragma unroll
+            for (int k = 0; k < HG; ++k) {
+                cs_out[t * out_step + k * a.half] = 1.f;
+                sn_out[t * out_step + k * a.half] = 0.f;
+            }
         return;
     }
-    float theta = 0.f;
-    for (int j = 0; j < c; ++j) theta += __ldg(ws + (bh * gridDim.x + j) * a.n_angles + p);
+    const int nc = gridDim.x;
+    float theta[HG];
+#pragma unroll
+    for (int k = 0; k < HG; ++k) {
+        theta[k] = 0.f;
+        for (int j = 0; j < c; ++j) theta[k] += __ldg(ws + ((bh0 + k) * nc + j) * a.n_angles + p);
+    }
     const float* ang = a.angles_shared ? a.angles + (b * a.len) * a.n_angles + p
-                                       : a.angles + ((b * a.len) * a.heads + h) * a.n_angles + p;
+                                       : a.angles + ((b * a.len) * a.heads + h0) * a.n_angles + p;
     const int64_t ang_step = a.angles_shared ? a.n_angles : a.heads * a.n_angles;
-    const float* dt = a.dt + (b * a.heads + h) * a.len;
+    const float* dt = a.dt + (b * a.heads + h0) * a.len;
     for (int64_t t = t0; t < t1; t += kAgUnroll) {
-        float av[kAgUnroll], dv[kAgUnroll];
+        float av[kAgUnroll], dv[HG][kAgUnroll];
 #pragma unroll
         for (int u = 0; u < kAgUnroll; ++u) {
             const bool in = t + u < t1;
             const int64_t pt = in ? angle_phys(a, t + u) : 0;
             av[u] = in ? __ldg(ang + pt * ang_step) : 0.f;
-            dv[u] = in ? __ldg(dt + pt) : 0.f;
+#pragma unroll
+            for (int k = 0; k < HG; ++k) dv[k][u] = in ? __ldg(dt + k * a.len + pt) : 0.f;
         }
 #pragma unroll
         for (int u = 0; u < kAgUnroll; ++u) {
             if (t + u >= t1) break;
-            theta = fmaf(tanhf(av[u]) * kPi, dv[u], theta);
-            float sn, cs;
-            sincosf(theta, &sn, &cs);
-            cs_out[(t + u) * out_step] = cs;
-            sn_out[(t + u) * out_step] = sn;
+            const float tv = tanhf(av[u]) * kPi;
+#pragma unroll
+            for (int k = 0; k < HG; ++k) {
+                theta[k] = fmaf(tv, dv[k][u], theta[k]);
+                float sn, cs;
+                sincosf(theta[k], &sn, &cs);
+                cs_out[(t + u) * out_step + k * a.half] = cs;
+                sn_out[(t + u) * out_step + k * a.half] = sn;
+            }
         }
     }
 }
@@ -117,16 +143,25 @@ size_t angle_workspace_bytes(int64_t batch, int64_t heads, int64_t len, int64_t 
 cudaError_t angle_launch(const AngleParams& a, float* ws, cudaStream_t stream) {
     const int64_t chunks = (a.len + kAgChunk - 1) / kAgChunk;
     if (chunks > INT32_MAX || a.batch * a.heads > 65535) return cudaErrorInvalidValue;
-    const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(a.batch * a.heads));
+    // head-shared angles: 4 heads per thread when the head count allows
+    const bool g4 = a.angles_shared && a.heads % 4 == 0;
+    const int hg = g4 ? 4 : 1;
+    const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(a.batch * a.heads / hg));
     const int t1 = static_cast<int>((a.n_angles + 31) / 32 * 32);
     const int t2 = static_cast<int>((a.half + 31) / 32 * 32);
     if (a.n_angles > 0) {  // no rotated pairs: the write pass alone gives (1, 0)
-        angle_chunk_sums<<<grid, t1, 0, stream>>>(a, ws);
+        if (g4)
+            angle_chunk_sums<4><<<grid, t1, 0, stream>>>(a, ws);
+        else
+            angle_chunk_sums<1><<<grid, t1, 0, stream>>>(a, ws);
         note_launch();
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    angle_chunk_write<<<grid, t2, 0, stream>>>(a, ws);
+    if (g4)
+        angle_chunk_write<4><<<grid, t2, 0, stream>>>(a, ws);
+    else
+        angle_chunk_write<1><<<grid, t2, 0, stream>>>(a, ws);
     note_launch();
     return cudaGetLastError();
 }
