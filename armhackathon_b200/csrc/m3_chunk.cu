@@ -39,7 +39,7 @@ constexpr int kCkThreads = 256;
 constexpr int kQR = 64;  // rows (step, rank) per chunk
 
 // kCkFull: every array (sequential form); kCkDs: w*k, x and gates (state
-// contributions); kCkOut: everything but w*k (outputs).
+// contributions); kCkOut: everything but w*k (outputs; W^T over k^T).
 enum CkMode { kCkFull = 0, kCkDs = 1, kCkOut = 2 };
 
 struct CkLayout {
@@ -57,8 +57,14 @@ struct CkLayout {
         kT = qT + (q ? N * QP4 : 0);
         kw = kT + (q ? N * QP4 : 0);
         x = kw + (k ? kQR * NP4 : 0);
-        WT = x + kQR * PP4;
-        ST = WT + (q ? kQR * QP4 : 0);
+        // outputs-only mode: W^T over k^T (N >= kQR rows), written once
+        // every thread has read k^T, where that lets more CTAs fit an SM
+        // (227 KB each): 64 x 64 heads go from 2 to 3
+        const int plain = (N * QP4 * 2 + kQR * PP4 + kQR * QP4 + N * PP4 + 4 * kQR + 8) * 4;
+        const int aliased = plain - kQR * QP4 * 4;
+        const bool alias = mode == kCkOut && N >= kQR && (227 * 1024) / aliased > (227 * 1024) / plain;
+        WT = alias ? kT : x + kQR * PP4;
+        ST = alias ? x + kQR * PP4 : WT + (q ? kQR * QP4 : 0);
         gate = ST + (q ? N * PP4 : 0);
         total = gate + 4 * kQR + 8;  // lcum, scale, gamma, w  + eQ
     }
@@ -327,6 +333,7 @@ __device__ __forceinline__ void ck_w(const CkLayout& ly, const CkSmem& s) {
                 for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(av[u], bv[v], acc[u][v]);
         }
     }
+    if (ly.WT == ly.kT) __syncthreads();  // W^T replaces k^T: every read of k^T first
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
         float out[4];
