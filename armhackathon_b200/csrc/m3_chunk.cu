@@ -525,7 +525,7 @@ struct CkWs {
 };
 
 template <int R>
-__global__ void __launch_bounds__(kCkThreads) m3_chunk_ds_kernel(M3Params p, CkWs ws, int n_chunks) {
+__global__ void __launch_bounds__(kCkThreads, 4) m3_chunk_ds_kernel(M3Params p, CkWs ws, int n_chunks) {
     const bool vec = ck_vec_ok(p);
     constexpr int QS = kQR / R;
     extern __shared__ float4 smem4[];
