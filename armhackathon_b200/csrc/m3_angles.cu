@@ -39,7 +39,9 @@ __device__ __forceinline__ int64_t angle_phys(const AngleParams& a, int64_t t) {
 // side by side; per head the arithmetic and its order are those of HG = 1.
 template <int HG>
 __global__ void angle_chunk_sums(AngleParams a, float* ws) {
-    const int64_t bh0 = static_cast<int64_t>(blockIdx.y) * HG;
+    // threadIdx.y: one of blockDim.y (batch*head) groups sharing the CTA
+    const int64_t bh0 = (static_cast<int64_t>(blockIdx.y) * blockDim.y + threadIdx.y) * HG;
+    if (bh0 >= a.batch * a.heads) return;
     const int c = blockIdx.x;
     const int p = threadIdx.x;
     if (p >= a.n_angles) return;
@@ -77,7 +79,9 @@ __global__ void angle_chunk_sums(AngleParams a, float* ws) {
 
 template <int HG>
 __global__ void angle_chunk_write(AngleParams a, const float* ws) {
-    const int64_t bh0 = static_cast<int64_t>(blockIdx.y) * HG;
+    // threadIdx.y: one of blockDim.y (batch*head) groups sharing the CTA
+    const int64_t bh0 = (static_cast<int64_t>(blockIdx.y) * blockDim.y + threadIdx.y) * HG;
+    if (bh0 >= a.batch * a.heads) return;
     const int c = blockIdx.x;
     const int p = threadIdx.x;
     if (p >= a.half) return;
@@ -146,22 +150,26 @@ cudaError_t angle_launch(const AngleParams& a, float* ws, cudaStream_t stream) {
     // head-shared angles: 4 heads per thread when the head count allows
     const bool g4 = a.angles_shared && a.heads % 4 == 0;
     const int hg = g4 ? 4 : 1;
-    const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(a.batch * a.heads / hg));
     const int t1 = static_cast<int>((a.n_angles + 31) / 32 * 32);
     const int t2 = static_cast<int>((a.half + 31) / 32 * 32);
+    // at least 2 warps per CTA (one warp per CTA would cap an SM at its CTA
+    // slots, half its warps)
+    const int by = t2 < 64 ? 64 / t2 : 1;
+    const int64_t groups = a.batch * a.heads / hg;
+    const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>((groups + by - 1) / by));
     if (a.n_angles > 0) {  // no rotated pairs: the write pass alone gives (1, 0)
         if (g4)
-            angle_chunk_sums<4><<<grid, t1, 0, stream>>>(a, ws);
+            angle_chunk_sums<4><<<grid, dim3(t1, by), 0, stream>>>(a, ws);
         else
-            angle_chunk_sums<1><<<grid, t1, 0, stream>>>(a, ws);
+            angle_chunk_sums<1><<<grid, dim3(t1, by), 0, stream>>>(a, ws);
         note_launch();
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     if (g4)
-        angle_chunk_write<4><<<grid, t2, 0, stream>>>(a, ws);
+        angle_chunk_write<4><<<grid, dim3(t2, by), 0, stream>>>(a, ws);
     else
-        angle_chunk_write<1><<<grid, t2, 0, stream>>>(a, ws);
+        angle_chunk_write<1><<<grid, dim3(t2, by), 0, stream>>>(a, ws);
     note_launch();
     return cudaGetLastError();
 }
